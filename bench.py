@@ -1,0 +1,527 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 quantized matvec path.
+
+Headline workload (one "step" = one sampler token): the Q6_K vocabulary
+output projection 152064 x 3584 of a seeded synthetic hidden state, followed
+by greedy argmax.  Rows are sharded over the ranks: rank r owns rows
+[r*ceil(N/W), min(N, (r+1)*ceil(N/W))), runs the fused projection+argmax
+kernel on its slice, and one NCCL all-gather joins every rank's logit slice
+together with its 8-byte argmax key; the token is the maximum key.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Metric: algorithmic GB/s (packed weight bytes + f32 x + f32 logits per step,
+whole job) over the timed steps, max over ranks of CUDA-event time.  Extra
+keys: tokens/s, the kernel roofline, an end-to-end figure through the C ABI
+with host buffers, the reference's CPU path on the host cores, and (N=1) the
+other benchmark configurations.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import importlib.util
+import io
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "my-inference-engine_b200")
+Q5_0, Q8_0, Q4_K, Q6_K = 6, 8, 12, 14
+VOCAB_ROWS, HIDDEN = 152064, 3584
+METRIC = "Q4_K/Q6_K/Q8_0 GEMV weight GB/s vs HBM peak; decode tokens/s at 1/2/4/8 GPU"
+
+
+def _load(name, path):
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def load_qmv():
+    build = _load("qmv_build", os.path.join(PKG, "build.py"))
+    if not os.path.exists(build.LIB_PATH):
+        build.build_library()
+    mod = _load("my_inference_engine_b200", os.path.join(PKG, "__init__.py"))
+    mod.load_library()
+    return mod
+
+
+def workloads():
+    return _load("qmv_workloads", os.path.join(PKG, "workloads.py"))
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            d = json.load(fh)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(name):
+    """dram bytes per launch from a committed ncu summary (profiles/<name>.txt,
+    line 'dram_bytes_per_launch: <int>'), scaled by the caller; None if absent."""
+    path = os.path.join(REPO, "profiles", name + ".txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_uuid: str | None):
+        self.uuid = device_uuid
+        self.proc = None
+        self.out = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu=timestamp,{self.FIELDS}", "--format=csv,noheader,nounits",
+               "-lms", "100"]
+        if self.uuid:
+            cmd[1:1] = ["-i", self.uuid]
+        try:
+            self.out = open("/tmp/qmv_clocks_%d.csv" % os.getpid(), "w+")
+            self.proc = subprocess.Popen(cmd, stdout=self.out, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+
+    def mark(self, which):
+        setattr(self, which, datetime.datetime.now())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.seek(0)
+        rows = list(csv.reader(io.StringIO(self.out.read())))
+        self.out.close()
+        try:
+            os.unlink(self.out.name)
+        except OSError:
+            pass
+        samples, nearest = [], []
+        for r in rows:
+            if len(r) < 10:
+                continue
+            try:
+                ts = datetime.datetime.strptime(r[0].strip(), "%Y/%m/%d %H:%M:%S.%f")
+            except ValueError:
+                continue
+            rec = {"ts": ts, "sm": float(r[2]), "max": float(r[3]), "power": r[4].strip(),
+                   "hw_slowdown": r[6].strip(), "hw_thermal": r[7].strip(), "sw_thermal": r[8].strip(),
+                   "sw_power_cap": r[9].strip()}
+            nearest.append(rec)
+            if self.t0 and self.t1 and self.t0 <= ts <= self.t1:
+                samples.append(rec)
+        used = samples
+        note = None
+        if not used and nearest and self.t0 and self.t1:
+            mid = self.t0 + (self.t1 - self.t0) / 2
+            used = sorted(nearest, key=lambda r: abs((r["ts"] - mid).total_seconds()))[:2]
+            note = "timed region shorter than the sampling period: nearest samples used"
+        if not used:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        reasons = []
+        for key, label in (("hw_slowdown", "hw_slowdown"), ("hw_thermal", "hw_thermal_slowdown"),
+                           ("sw_thermal", "sw_thermal_slowdown"), ("sw_power_cap", "sw_power_cap")):
+            if any(r[key] == "Active" for r in used):
+                reasons.append(label)
+        out = {"sm_mhz": statistics.median(r["sm"] for r in used), "sm_max_mhz": used[0]["max"],
+               "reasons": reasons, "samples": len(used)}
+        if note:
+            out["note"] = note
+        return out
+
+
+# ------------------------------------------------------------ CPU reference
+
+def cpu_reference_lib():
+    """(Reference, kind): the reference's own OpenMP build (oracle/_ref) when
+    present, else the scalar C restatement of it (a single-thread port)."""
+    binding = _load("qmv_oracle_binding", os.path.join(REPO, "oracle", "binding.py"))
+    if not os.path.exists(binding.REF_AVX2_SO) and os.path.isdir(os.path.join(binding.REFERENCE_SRC, "src")):
+        binding.build(reference=True)
+    if os.path.exists(binding.REF_AVX2_SO):
+        return binding.Reference(binding.REF_AVX2_SO), "reference"
+    if not os.path.exists(binding.ORACLE_SO):
+        binding.build(reference=False)
+    return binding.Oracle(), "port"
+
+
+def cpu_vocab_step(lib, kind, blocks, x, threads):
+    if kind == "reference":
+        y = lib.matvec(Q6_K, blocks, VOCAB_ROWS, HIDDEN, x)
+        ok, tok, _ = lib.greedy(y)
+    else:
+        y = lib.matvec(Q6_K, blocks, VOCAB_ROWS, HIDDEN, x, threads=threads)
+        ok, tok = lib.argmax(y)
+    return tok
+
+
+def time_cpu_reference(blocks, x, min_seconds, max_steps=None):
+    lib, kind = cpu_reference_lib()
+    cores = os.cpu_count() or 1
+    if kind == "reference":
+        lib.set_threads(cores)
+    cpu_vocab_step(lib, kind, blocks, x, cores)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu_vocab_step(lib, kind, blocks, x, cores)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds or (max_steps and n >= max_steps):
+            break
+    return n, el, kind, cores
+
+
+# --------------------------------------------------------------- helpers
+
+def vocab_bytes(rows):
+    return rows * (HIDDEN // 256) * 210
+
+
+def shard(rank, world):
+    per = -(-VOCAB_ROWS // world)
+    b = min(VOCAB_ROWS, rank * per)
+    e = min(VOCAB_ROWS, (rank + 1) * per)
+    return b, e, per
+
+
+def copies_for(slice_bytes, l2_bytes):
+    """Distinct weight copies so the rotating set is >= 2.5x L2 (no L2 reuse
+    between consecutive launches)."""
+    return max(1, math.ceil(2.5 * l2_bytes / max(1, slice_bytes)))
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    wl = workloads()
+    blocks = wl.make_blocks(Q6_K, VOCAB_ROWS, HIDDEN, seed=0)
+    x = wl.make_activations(HIDDEN, seed=0)
+    lib, kind = cpu_reference_lib()
+    cores = os.cpu_count() or 1
+    if kind == "reference":
+        lib.set_threads(cores)
+    for _ in range(args.warmup):
+        cpu_vocab_step(lib, kind, blocks, x, cores)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_vocab_step(lib, kind, blocks, x, cores)
+    el = time.perf_counter() - t0
+    step_bytes = vocab_bytes(VOCAB_ROWS) + 4 * HIDDEN + 4 * VOCAB_ROWS
+    value = args.steps * step_bytes / el / 1e9
+    sample = f"full {VOCAB_ROWS}x{HIDDEN} Q6_K projection + greedy argmax per step"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * el / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "tokens_per_s": round(args.steps / el, 3),
+        "config": {"workload": "cfg2_q6_k_vocab_projection_argmax", "rows": VOCAB_ROWS, "cols": HIDDEN,
+                   "ggml_type": "Q6_K", "parallelism": "host OpenMP"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------- b200 arm
+
+def run_b200(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    qmv = load_qmv()
+    qmv.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    props = torch.cuda.get_device_properties(local_rank)
+    l2 = getattr(props, "L2_cache_size", 126 * 1024 * 1024) or 126 * 1024 * 1024
+    wl = workloads()
+
+    b, e, per = shard(rank, world)
+    rows = e - b
+    per_pad = (per + 3) // 4 * 4
+    blocks = wl.make_blocks(Q6_K, VOCAB_ROWS, HIDDEN, seed=0, row_begin=b, row_end=e)
+    copies = copies_for(vocab_bytes(rows), l2)
+    weights = [qmv.Weight(Q6_K, blocks, e - b, HIDDEN) for _ in range(copies)]
+    x_host = wl.make_activations(HIDDEN, seed=0)
+    x_dev = torch.from_numpy(x_host).to(dev)
+    stride = per_pad + 2  # logits slice + 8-byte key, one all-gather
+    sendbuf = torch.zeros(stride, dtype=torch.float32, device=dev)
+    gathered = torch.zeros(world * stride, dtype=torch.float32, device=dev)
+    keyview = sendbuf[per_pad:per_pad + 2].view(torch.int64)
+    ws = torch.zeros(qmv.argmax_workspace_bytes(), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    SIGN = torch.tensor(-(1 << 63), dtype=torch.int64, device=dev)
+
+    def combine():
+        keys = gathered.view(world, stride)[:, per_pad:per_pad + 2].contiguous().view(torch.int64).view(-1)
+        return torch.bitwise_xor(torch.bitwise_xor(keys, SIGN).max(), SIGN)
+
+    kstart = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    kend = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+
+    def step(i, timed):
+        w = weights[i % copies]
+        if timed:
+            kstart[i].record(stream)
+        w.matvec_argmax(x_dev.data_ptr(), sendbuf.data_ptr(), keyview.data_ptr(), ws.data_ptr(), sptr)
+        if timed:
+            kend[i].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, sendbuf)
+
+    # correctness gate before timing: the fused kernel's token on this input
+    step(0, False)
+    if world > 1:
+        tok_key = int(combine().item()) & 0xFFFFFFFFFFFFFFFF
+    else:
+        tok_key = int(keyview.item()) & 0xFFFFFFFFFFFFFFFF
+    token = qmv.key_to_token(tok_key)
+
+    for i in range(args.warmup):
+        step(i, False)
+    uuid = None
+    try:
+        uuid = "GPU-" + str(props.uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    if clocks:
+        clocks.mark("t0")
+    t_start.record(stream)
+    for i in range(args.steps):
+        step(i, True)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.mark("t1")
+    if world > 1:
+        dist.barrier()
+    ms = t_start.elapsed_time(t_end)
+    kms = sum(kstart[i].elapsed_time(kend[i]) for i in range(args.steps)) / args.steps
+    t = torch.tensor([ms, kms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, kms_max = float(t[0]), float(t[1])
+    clock_info = clocks.stop() if clocks else None
+
+    # ---- end to end through the C ABI with host buffers (pinned)
+    x_pin = torch.from_numpy(x_host).pin_memory()
+    out_pin = torch.empty(world * stride, dtype=torch.float32).pin_memory()
+    e2e_steps = max(3, min(args.steps, 200))
+    def e2e_step(i):
+        x_dev.copy_(x_pin, non_blocking=True)
+        w = weights[i % copies]
+        w.matvec_argmax(x_dev.data_ptr(), sendbuf.data_ptr(), keyview.data_ptr(), ws.data_ptr(), sptr)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, sendbuf)
+            if rank == 0:
+                out_pin.copy_(gathered, non_blocking=True)
+        else:
+            out_pin[:stride].copy_(sendbuf, non_blocking=True)
+        stream.synchronize()
+        if rank == 0:
+            keys = out_pin.numpy().reshape(world, stride)[:, per_pad:per_pad + 2].copy().view(np.uint64)
+            return qmv.key_to_token(int(keys.max()))
+        return None
+    for i in range(2):
+        e2e_step(i)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    e2e_tok = None
+    for i in range(e2e_steps):
+        e2e_tok = e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms[0])
+
+    step_bytes = vocab_bytes(VOCAB_ROWS) + world * 4 * HIDDEN + 4 * VOCAB_ROWS
+    value = args.steps * step_bytes / (ms * 1e-3) / 1e9
+    e2e_value = e2e_steps * step_bytes / (e2e_ms * 1e-3) / 1e9
+
+    result = None
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        launch_bytes = vocab_bytes(rows) + 4 * HIDDEN + 4 * rows
+        achieved = launch_bytes / (kms_max * 1e-3) / 1e9
+        traffic = profile_traffic("gemv_q6_k_cfg2")
+        if traffic is not None:
+            traffic = traffic * rows / VOCAB_ROWS
+        result = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8-dp4a/f32",
+            "data": "synthetic (seeded splitmix64; Q6_K blocks per the configuration)",
+            "tokens_per_s": round(args.steps / (ms * 1e-3), 1),
+            "token": token,
+            "config": {"workload": "cfg2_q6_k_vocab_projection_argmax", "rows": VOCAB_ROWS, "cols": HIDDEN,
+                       "ggml_type": "Q6_K", "parallelism": f"row-shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                       "rows_per_rank": per, "l2_defeat": f"{copies} rotating weight copies per rank (>= 2.5x L2)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": "gemv_kernel<Q6_K> fused argmax", "kernel_ms": round(kms_max, 5),
+                         "peak_source": peak_kind},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * HIDDEN,
+                    "d2h_bytes_per_step": 4 * world * stride, "steps": e2e_steps,
+                    "tokens_per_s": round(e2e_steps / (e2e_ms * 1e-3), 1), "token": e2e_tok},
+            "gpu_launches": args.steps,
+            "clocks": clock_info,
+        }
+    for wobj in weights:
+        wobj.free()
+    del weights
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def extras_single_gpu(qmv, steps):
+    """Secondary configurations on one GPU (GB/s or TFLOP/s per call)."""
+    import torch
+    wl = workloads()
+    props = torch.cuda.get_device_properties(torch.cuda.current_device())
+    l2 = getattr(props, "L2_cache_size", 126 * 1024 * 1024) or 126 * 1024 * 1024
+    peak, _ = measured_peaks()
+    out = {}
+    for name, batch in (("cfg0_q8_0_4864x896", 0), ("cfg1a_q4_k_18944x3584", 0),
+                        ("cfg1b_q4_k_3584x18944", 0), ("cfg3_q5_0_4864x896", 8),
+                        ("cfg3_q5_0_4864x896", 512)):
+        gtype, rows, cols = wl.CONFIGS[name]
+        blocks = wl.make_blocks(gtype, rows, cols, seed=0)
+        wbytes = blocks.nbytes
+        copies = copies_for(wbytes, l2)
+        ws = [qmv.Weight(gtype, blocks, rows, cols) for _ in range(copies)]
+        P = max(1, batch)
+        X = torch.from_numpy(np.stack([wl.make_activations(cols, seed=p) for p in range(P)])).cuda()
+        Y = torch.empty((P, rows), dtype=torch.float32, device="cuda")
+        n = max(steps, 3 * copies)
+
+        def call(i):
+            if batch:
+                ws[i % copies].matmul(X.data_ptr(), P, Y.data_ptr())
+            else:
+                ws[i % copies].matvec(X.data_ptr(), Y.data_ptr())
+        for i in range(3 * copies):
+            call(i)
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(n):
+            call(i)
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / n
+        alg = wl.algorithmic_bytes(gtype, rows, cols, P)
+        key = name if not batch else f"{name}_P{batch}"
+        rec = {"us_per_call": round(ms * 1e3, 2), "GB_s": round(alg / (ms * 1e-3) / 1e9, 1),
+               "frac_hbm": round(alg / (ms * 1e-3) / 1e9 / peak, 3), "copies": copies}
+        if batch:
+            rec["TFLOP_s"] = round(2.0 * P * rows * cols / (ms * 1e-3) / 1e12, 2)
+        out[key] = rec
+        for w in ws:
+            w.free()
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and world == 1 and args.gpus > 1:
+        print(json.dumps({"error": "run N>1 under torchrun (one process per GPU)"}), flush=True)
+        return 2
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+
+    result = run_b200(args, rank, world, local_rank)
+    if rank != 0:
+        return 0
+    if world == 1 and not args.no_extras:
+        qmv = load_qmv()
+        result["configs"] = extras_single_gpu(qmv, steps=200)
+    if world == 1 and not args.no_cpu_baseline:
+        wl = workloads()
+        blocks = wl.make_blocks(Q6_K, VOCAB_ROWS, HIDDEN, seed=0)
+        x = wl.make_activations(HIDDEN, seed=0)
+        n, el, kind, cores = time_cpu_reference(blocks, x, args.cpu_seconds)
+        step_bytes = vocab_bytes(VOCAB_ROWS) + 4 * HIDDEN + 4 * VOCAB_ROWS
+        result["cpu_baseline"] = {
+            "value": round(n * step_bytes / el / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+            "sample": f"{n} full {VOCAB_ROWS}x{HIDDEN} Q6_K projections + greedy argmax "
+                      f"({el:.1f} s, {'reference OpenMP AVX2 build' if kind == 'reference' else 'scalar C port'})"}
+    print(json.dumps(result), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,147 @@
+/*
+ * qmv_b200 — C ABI of the B200 (sm_100a) quantized matrix-vector library.
+ *
+ * Plain C types only: pointers, sizes, ints.  CUDA streams are passed as
+ * `void *` (a cudaStream_t / CUstream; NULL = the legacy default stream).
+ * Every function returns 1 on success and 0 on failure; on failure
+ * qmv_last_error() (per calling thread) holds a one-line message.  No
+ * function aborts the process.
+ *
+ * Citations name the reference engine's interface each entry point replaces
+ * or backs (paths inside trungnguyen21/my-inference-engine).
+ */
+#ifndef QMV_B200_H
+#define QMV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "gguf_quantized_view.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Device-resident packed tensor (opaque). */
+typedef struct QmvWeight QmvWeight;
+
+/* ---- errors, devices ---------------------------------------------------- */
+
+/* Last error of the calling thread ("" if none).  Replaces the reference's
+ * set_error/error-buffer convention (src/sampler.cpp:7-12,
+ * src/qwen2_architecture.cpp:62-67) for the device path. */
+const char *qmv_last_error(void);
+
+/* Copy the last error into buf (always NUL-terminated when capacity > 0). */
+int qmv_copy_last_error(char *buf, int capacity);
+
+/* Library ABI version (increments on any signature change). */
+int qmv_abi_version(void);
+
+/* Number of visible CUDA devices. */
+int qmv_device_count(int *count);
+
+/* Make `device` current for the calling thread (all later calls of this
+ * thread allocate and launch there). */
+int qmv_set_device(int device);
+
+/* ---- residency of packed tensors ----------------------------------------
+ * Backs the packed-weight source of the reference: the borrowed mmap views
+ * returned by gguf_get_quantized_tensor_view (src/gguf_reader.cpp:573-637,
+ * struct src/gguf_reader.h:31-40).  Validation follows
+ * src/quantized_matvec.cpp:94-149. */
+
+/* Upload rows [row_begin, row_end) of `view` to the current device, repacked
+ * into 16-byte-aligned rows.  row_begin = 0, row_end = rows uploads the whole
+ * tensor; a sub-range is one rank's shard of a row-partitioned projection. */
+int qmv_weight_upload(const GgufQuantizedTensorView *view, int row_begin, int row_end,
+                      QmvWeight **out);
+
+/* Free a weight from qmv_weight_upload (not one owned by the registry). */
+int qmv_weight_free(QmvWeight *weight);
+
+/* Shape of a resident weight.  Any output pointer may be NULL. */
+int qmv_weight_info(const QmvWeight *weight, uint32_t *ggml_type, int *rows, int *cols,
+                    int *row_begin, uint64_t *device_bytes);
+
+/* Registry lookup-or-upload keyed by (view->data, type, shape) on the current
+ * device; thread-safe, uploads once.  The registry owns the weight. */
+int qmv_resident_weight(const GgufQuantizedTensorView *view, QmvWeight **out);
+
+/* Free every registry-owned weight (no call may be using them). */
+int qmv_resident_release_all(void);
+
+/* ---- compute on device buffers ----------------------------------------- */
+
+/* y = W x.  x: x_count floats (== columns), y: y_count floats (== rows of
+ * this weight).  Device pointers.  Device form of quantized_tensor_matvec_f32
+ * (src/quantized_matvec.h:32-38, src/quantized_matvec.cpp:86-162). */
+int qmv_matvec(const QmvWeight *weight, const float *x, int x_count, float *y, int y_count,
+               void *stream);
+
+/* Y[p, :] = W X[p, :] for p < batch.  X: [batch, x_count], Y: [batch, y_count],
+ * token-major, device pointers.  Device form of quantized_tensor_matmul_f32
+ * (src/quantized_matvec.h:42-50, src/quantized_matvec.cpp:164-224). */
+int qmv_matmul(const QmvWeight *weight, const float *X, int x_count, int batch, float *Y,
+               int y_count, void *stream);
+
+/* Bit-exact dequantisation of a resident weight into out[rows * cols]
+ * (row-major).  Same bits as the reference's *_dequantize_block
+ * (src/quantization.cpp:54-67, 161-184, 380-409, 588-615). */
+int qmv_dequantize(const QmvWeight *weight, float *out, uint64_t out_count, void *stream);
+
+/* Bit-exact dequantisation of block_count raw GGUF blocks already in device
+ * memory (any byte alignment) into out[block_count * block_elements].
+ * Used for single rows such as an embedding lookup
+ * (src/qwen2_architecture.cpp:375-475). */
+int qmv_dequantize_raw(uint32_t ggml_type, const void *blocks, uint64_t block_count,
+                       float *out, void *stream);
+
+/* ---- greedy argmax -------------------------------------------------------
+ * Argmax results are 64-bit keys: the high word orders the float value, the
+ * low word is 0xFFFFFFFF - index, so the maximum key is the largest logit with
+ * the lowest index on ties (src/sampler.cpp:29-31).  Any NaN/Inf makes the key
+ * QMV_KEY_NONFINITE.  Keys combine across shards with an unsigned 64-bit max
+ * (one NCCL all-reduce). */
+#define QMV_KEY_NONFINITE 0xFFFFFFFFFFFFFFFFull
+
+/* Bytes of device workspace the argmax entry points need (zero it once
+ * before first use; the kernels leave it zeroed). */
+size_t qmv_argmax_workspace_bytes(void);
+
+/* *key (device) = argmax key of logits[0..n) with indices offset by
+ * index_base.  Device form of sampler_greedy_sample (src/sampler.cpp:14-36). */
+int qmv_argmax(const float *logits, int n, int index_base, uint64_t *key, void *workspace,
+               void *stream);
+
+/* Fused vocab projection + greedy argmax: logits = W x (device, y_count ==
+ * rows of this weight) and *key (device) = argmax key over those rows with
+ * indices offset by the weight's row_begin.  Output projection
+ * (src/qwen2_architecture.cpp:1504-1523) followed by the sampler. */
+int qmv_matvec_argmax(const QmvWeight *weight, const float *x, int x_count, float *logits,
+                      int y_count, uint64_t *key, void *workspace, void *stream);
+
+/* Host: decode a key into a token id.  Returns 0 (id = -1) for
+ * QMV_KEY_NONFINITE or a key with no valid index. */
+int qmv_key_to_token(uint64_t key, int *token_id);
+
+/* Host-facing greedy sampler over DEVICE logits with the reference's contract
+ * (src/sampler.h:4-13): synchronises `stream`, writes the id, and on failure
+ * returns 0, sets *token_id = -1 when writable and fills `error`. */
+int qmv_greedy_sample(const float *logits, int vocab_size, int *token_id, char *error,
+                      int error_capacity, void *stream);
+
+/* ---- drop-in entry points with C linkage ---------------------------------
+ * Same arguments and results as the C++ functions in quantized_matvec.h
+ * (host input/output; see there), for C/cgo/ctypes callers. */
+int qmv_quantized_tensor_matvec_f32(const GgufQuantizedTensorView *matrix, const float *input,
+                                    int input_count, float *output, int output_count);
+int qmv_quantized_tensor_matmul_f32(const GgufQuantizedTensorView *matrix, const float *inputs,
+                                    int input_count, int batch_count, float *outputs,
+                                    int output_count);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,288 @@
+"""Python host mirror of the B200 quantized matvec library.
+
+The product is the C-ABI shared library ``libqmv_b200.so`` (built from
+``csrc/`` by ``build.py``; declarations in ``include/qmv_b200.h``).  This module
+binds it with ctypes and mirrors the reference engine's interface for the
+path, so tests read like the reference's own tests:
+
+* ``GgufQuantizedTensorView`` - the reference's view struct
+  (src/gguf_reader.h:31-40), field for field.
+* ``quantized_tensor_matvec_f32`` / ``quantized_tensor_matmul_f32`` - the
+  reference's entry points (src/quantized_matvec.h:32-50): host arrays in,
+  host arrays out, 1 on success and 0 on failure.
+* ``sampler_greedy_sample`` - the reference's greedy sampler contract
+  (src/sampler.h:4-13) over device logits.
+* ``Weight`` - a device-resident packed tensor with device-pointer
+  ``matvec`` / ``matmul`` / ``matvec_argmax`` / ``dequantize``.
+
+Device buffers are passed as raw pointers (``int``), e.g. ``tensor.data_ptr()``
+of a CUDA torch tensor; streams as raw ``cudaStream_t`` values.  There is no
+CPU fallback: without the built library, or without a GPU, compute calls fail.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libqmv_b200.so")
+
+ENGINE_GGML_TYPE_Q5_0 = 6
+ENGINE_GGML_TYPE_Q8_0 = 8
+ENGINE_GGML_TYPE_Q4_K = 12
+ENGINE_GGML_TYPE_Q6_K = 14
+BLOCK_ELEMENTS = {6: 32, 8: 32, 12: 256, 14: 256}
+BLOCK_BYTES = {6: 22, 8: 34, 12: 144, 14: 210}
+KEY_NONFINITE = 0xFFFFFFFFFFFFFFFF
+
+# Every symbol include/qmv_b200.h declares, plus the C++ drop-in pair from
+# include/quantized_matvec.h (mangled, C++ linkage).
+C_SYMBOLS = [
+    "qmv_last_error", "qmv_copy_last_error", "qmv_abi_version", "qmv_device_count",
+    "qmv_set_device", "qmv_weight_upload", "qmv_weight_free", "qmv_weight_info",
+    "qmv_resident_weight", "qmv_resident_release_all", "qmv_matvec", "qmv_matmul",
+    "qmv_dequantize", "qmv_dequantize_raw", "qmv_argmax_workspace_bytes", "qmv_argmax",
+    "qmv_matvec_argmax", "qmv_key_to_token", "qmv_greedy_sample",
+    "qmv_quantized_tensor_matvec_f32", "qmv_quantized_tensor_matmul_f32",
+]
+CXX_DROPIN_SYMBOLS = {
+    "quantized_tensor_matvec_f32": "_Z27quantized_tensor_matvec_f32PK23GgufQuantizedTensorViewPKfiPfi",
+    "quantized_tensor_matmul_f32": "_Z27quantized_tensor_matmul_f32PK23GgufQuantizedTensorViewPKfiiPfi",
+}
+
+
+class GgufQuantizedTensorView(ctypes.Structure):
+    """Same fields, order and types as src/gguf_reader.h:31-40."""
+
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("ggml_type", ctypes.c_uint32),
+        ("dimension_count", ctypes.c_uint32),
+        ("dimensions", ctypes.c_uint64 * 4),
+        ("element_count", ctypes.c_uint64),
+        ("block_elements", ctypes.c_uint64),
+        ("block_bytes", ctypes.c_uint64),
+        ("block_count", ctypes.c_uint64),
+    ]
+
+
+def make_view(ggml_type: int, data, rows: int, cols: int) -> GgufQuantizedTensorView:
+    """A well-formed 2-D view over ``data`` (numpy uint8 array or address)."""
+    v = GgufQuantizedTensorView()
+    v.data = data.ctypes.data if isinstance(data, np.ndarray) else data
+    v.ggml_type = ggml_type
+    v.dimension_count = 2
+    v.dimensions[0] = cols
+    v.dimensions[1] = rows
+    v.element_count = cols * rows
+    be = BLOCK_ELEMENTS.get(ggml_type, 32)
+    v.block_elements = be
+    v.block_bytes = BLOCK_BYTES.get(ggml_type, 0)
+    v.block_count = (cols * rows) // be
+    return v
+
+
+_lib = None
+
+
+def library_loaded() -> bool:
+    return _lib is not None
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load libqmv_b200.so (raises if it is missing; no fallback exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} is missing: build it with my-inference-engine_b200/build.py")
+    lib = ctypes.CDLL(path)
+    P, I, U32, U64, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_size_t
+    IP = ctypes.POINTER(ctypes.c_int)
+    VP = ctypes.POINTER(GgufQuantizedTensorView)
+    sigs = {
+        "qmv_last_error": (ctypes.c_char_p, []),
+        "qmv_copy_last_error": (I, [ctypes.c_char_p, I]),
+        "qmv_abi_version": (I, []),
+        "qmv_device_count": (I, [IP]),
+        "qmv_set_device": (I, [I]),
+        "qmv_weight_upload": (I, [VP, I, I, ctypes.POINTER(P)]),
+        "qmv_weight_free": (I, [P]),
+        "qmv_weight_info": (I, [P, ctypes.POINTER(U32), IP, IP, IP, ctypes.POINTER(U64)]),
+        "qmv_resident_weight": (I, [VP, ctypes.POINTER(P)]),
+        "qmv_resident_release_all": (I, []),
+        "qmv_matvec": (I, [P, P, I, P, I, P]),
+        "qmv_matmul": (I, [P, P, I, I, P, I, P]),
+        "qmv_dequantize": (I, [P, P, U64, P]),
+        "qmv_dequantize_raw": (I, [U32, P, U64, P, P]),
+        "qmv_argmax_workspace_bytes": (SZ, []),
+        "qmv_argmax": (I, [P, I, I, P, P, P]),
+        "qmv_matvec_argmax": (I, [P, P, I, P, I, P, P, P]),
+        "qmv_key_to_token": (I, [U64, IP]),
+        "qmv_greedy_sample": (I, [P, I, IP, ctypes.c_char_p, I, P]),
+        "qmv_quantized_tensor_matvec_f32": (I, [VP, P, I, P, I]),
+        "qmv_quantized_tensor_matmul_f32": (I, [VP, P, I, I, P, I]),
+    }
+    for name, (res, args) in sigs.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    for mangled in CXX_DROPIN_SYMBOLS.values():
+        fn = getattr(lib, mangled)
+        fn.restype = I
+    getattr(lib, CXX_DROPIN_SYMBOLS["quantized_tensor_matvec_f32"]).argtypes = [VP, P, I, P, I]
+    getattr(lib, CXX_DROPIN_SYMBOLS["quantized_tensor_matmul_f32"]).argtypes = [VP, P, I, I, P, I]
+    _lib = lib
+    return lib
+
+
+def lib() -> ctypes.CDLL:
+    return load_library()
+
+
+def last_error() -> str:
+    return lib().qmv_last_error().decode()
+
+
+class QmvError(RuntimeError):
+    pass
+
+
+def _check(ok: int, what: str):
+    if not ok:
+        raise QmvError(f"{what}: {last_error()}")
+
+
+def _ptr(a) -> int | None:
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return a
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    raise TypeError(f"cannot take the address of {type(a)}")
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+# ------------------------------------------------ reference-shaped entry points
+
+def quantized_tensor_matvec_f32(matrix: GgufQuantizedTensorView, input, input_count: int,
+                                output, output_count: int, cxx_symbol: bool = False) -> int:
+    """src/quantized_matvec.h:32-38 over host numpy buffers (returns 1/0)."""
+    fn = getattr(lib(), CXX_DROPIN_SYMBOLS["quantized_tensor_matvec_f32"]) if cxx_symbol \
+        else lib().qmv_quantized_tensor_matvec_f32
+    return fn(ctypes.byref(matrix) if matrix is not None else None, _ptr(input), input_count,
+              _ptr(output), output_count)
+
+
+def quantized_tensor_matmul_f32(matrix: GgufQuantizedTensorView, inputs, input_count: int,
+                                batch_count: int, outputs, output_count: int,
+                                cxx_symbol: bool = False) -> int:
+    """src/quantized_matvec.h:42-50 over host numpy buffers (returns 1/0)."""
+    fn = getattr(lib(), CXX_DROPIN_SYMBOLS["quantized_tensor_matmul_f32"]) if cxx_symbol \
+        else lib().qmv_quantized_tensor_matmul_f32
+    return fn(ctypes.byref(matrix) if matrix is not None else None, _ptr(inputs), input_count,
+              batch_count, _ptr(outputs), output_count)
+
+
+def sampler_greedy_sample(logits_dev, vocab_size: int, stream=None):
+    """(ok, token_id, error) for device logits, src/sampler.h:4-13 contract."""
+    tok = ctypes.c_int(99)
+    err = ctypes.create_string_buffer(128)
+    ok = lib().qmv_greedy_sample(_ptr(logits_dev), vocab_size, ctypes.byref(tok), err, 128,
+                                 _ptr(stream))
+    return ok, tok.value, err.value.decode()
+
+
+def key_to_token(key: int) -> int:
+    tok = ctypes.c_int(0)
+    if not lib().qmv_key_to_token(ctypes.c_uint64(key), ctypes.byref(tok)):
+        return -1
+    return tok.value
+
+
+def argmax_workspace_bytes() -> int:
+    return lib().qmv_argmax_workspace_bytes()
+
+
+def argmax(logits_dev, n: int, key_dev, workspace_dev, index_base: int = 0, stream=None):
+    _check(lib().qmv_argmax(_ptr(logits_dev), n, index_base, _ptr(key_dev), _ptr(workspace_dev),
+                            _ptr(stream)), "qmv_argmax")
+
+
+def dequantize_raw(ggml_type: int, blocks_dev, block_count: int, out_dev, stream=None):
+    _check(lib().qmv_dequantize_raw(ggml_type, _ptr(blocks_dev), block_count, _ptr(out_dev),
+                                    _ptr(stream)), "qmv_dequantize_raw")
+
+
+def set_device(device: int):
+    _check(lib().qmv_set_device(device), "qmv_set_device")
+
+
+def device_count() -> int:
+    n = ctypes.c_int(0)
+    _check(lib().qmv_device_count(ctypes.byref(n)), "qmv_device_count")
+    return n.value
+
+
+class Weight:
+    """A packed tensor resident on the current CUDA device."""
+
+    def __init__(self, ggml_type: int, blocks: np.ndarray, rows: int, cols: int,
+                 row_begin: int = 0, row_end: int | None = None):
+        self._blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+        self.view = make_view(ggml_type, self._blocks, rows, cols)
+        self.ggml_type = ggml_type
+        self.cols = cols
+        self.row_begin = row_begin
+        self.row_end = rows if row_end is None else row_end
+        self.rows = self.row_end - self.row_begin
+        h = ctypes.c_void_p()
+        _check(lib().qmv_weight_upload(ctypes.byref(self.view), row_begin, self.row_end,
+                                       ctypes.byref(h)), "qmv_weight_upload")
+        self.handle = h
+        self._blocks = None  # the device copy is independent of the host bytes
+
+    def free(self):
+        if self.handle:
+            _check(lib().qmv_weight_free(self.handle), "qmv_weight_free")
+            self.handle = None
+
+    def __del__(self):
+        try:
+            if self.handle and _lib is not None:
+                _lib.qmv_weight_free(self.handle)
+        except Exception:
+            pass
+
+    def info(self):
+        t, r, c, rb = ctypes.c_uint32(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        nbytes = ctypes.c_uint64()
+        _check(lib().qmv_weight_info(self.handle, ctypes.byref(t), ctypes.byref(r), ctypes.byref(c),
+                                     ctypes.byref(rb), ctypes.byref(nbytes)), "qmv_weight_info")
+        return {"type": t.value, "rows": r.value, "cols": c.value, "row_begin": rb.value,
+                "device_bytes": nbytes.value}
+
+    def matvec(self, x_dev, y_dev, stream=None):
+        _check(lib().qmv_matvec(self.handle, _ptr(x_dev), self.cols, _ptr(y_dev), self.rows,
+                                _ptr(stream)), "qmv_matvec")
+
+    def matmul(self, X_dev, batch: int, Y_dev, stream=None):
+        _check(lib().qmv_matmul(self.handle, _ptr(X_dev), self.cols, batch, _ptr(Y_dev), self.rows,
+                                _ptr(stream)), "qmv_matmul")
+
+    def matvec_argmax(self, x_dev, logits_dev, key_dev, workspace_dev, stream=None):
+        _check(lib().qmv_matvec_argmax(self.handle, _ptr(x_dev), self.cols, _ptr(logits_dev),
+                                       self.rows, _ptr(key_dev), _ptr(workspace_dev),
+                                       _ptr(stream)), "qmv_matvec_argmax")
+
+    def dequantize(self, out_dev, stream=None):
+        _check(lib().qmv_dequantize(self.handle, _ptr(out_dev), self.rows * self.cols,
+                                    _ptr(stream)), "qmv_dequantize")

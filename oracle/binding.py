@@ -1,0 +1,202 @@
+"""ctypes binding of the CPU oracle — TEST INFRASTRUCTURE ONLY.
+
+``Oracle`` wraps oracle/libqmv_oracle.so (our C restatement of the reference's
+scalar path, oracle/qmv_oracle.c).  ``Reference`` wraps oracle/_ref/*.so, the
+reference engine's own sources compiled by oracle/Makefile.  Only tests/,
+__graft_entry__.smoke() and bench.py's CPU-baseline leg use this module; the
+product library never does.
+"""
+from __future__ import annotations
+
+import concurrent.futures as cf
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "libqmv_oracle.so")
+REF_SCALAR_SO = os.path.join(HERE, "_ref", "libqmvref_scalar.so")
+REF_AVX2_SO = os.path.join(HERE, "_ref", "libqmvref_avx2.so")
+REFERENCE_SRC = "/root/reference"
+
+_P = ctypes.c_void_p
+
+
+def build(reference: bool | None = None) -> None:
+    """Compile the oracle (and oracle/_ref when the reference sources exist)."""
+    subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
+    if reference is None:
+        reference = os.path.isdir(os.path.join(REFERENCE_SRC, "src"))
+    if reference:
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={REFERENCE_SRC}"], check=True)
+
+
+def _addr(a):
+    return a.ctypes.data if isinstance(a, np.ndarray) else a
+
+
+class Oracle:
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            build(reference=False)
+        L = ctypes.CDLL(path)
+        L.or_f16_to_f32.restype = ctypes.c_float
+        L.or_f16_to_f32.argtypes = [ctypes.c_uint16]
+        for n in ("or_q8_0_dot", "or_q5_0_dot", "or_q4_k_dot", "or_q6_k_dot"):
+            getattr(L, n).restype = ctypes.c_float
+            getattr(L, n).argtypes = [_P, _P]
+        for n in ("or_q8_0_dequant", "or_q5_0_dequant", "or_q4_k_dequant", "or_q6_k_dequant"):
+            getattr(L, n).restype = None
+            getattr(L, n).argtypes = [_P, _P]
+        L.or_q4_k_scale_min.argtypes = [_P, ctypes.c_int, _P, _P]
+        L.or_q6_k_value.argtypes = [_P, ctypes.c_int, _P, _P]
+        L.or_dequant_blocks.argtypes = [ctypes.c_uint32, _P, ctypes.c_uint64, _P]
+        L.or_matvec_rows.argtypes = [ctypes.c_uint32, _P, ctypes.c_int, ctypes.c_int, _P, _P,
+                                     ctypes.c_int, ctypes.c_int]
+        L.or_matmul.argtypes = [ctypes.c_uint32, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P]
+        L.or_row_abs_dot.argtypes = [ctypes.c_uint32, _P, ctypes.c_int, ctypes.c_int, _P, _P]
+        L.or_argmax.argtypes = [_P, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+        self.lib = L
+
+    def f16(self, bits: int) -> float:
+        return self.lib.or_f16_to_f32(bits)
+
+    def f16_all(self) -> np.ndarray:
+        """float32 decode of all 65536 encodings (bit patterns preserved)."""
+        out = np.empty(65536, dtype=np.float32)
+        f = self.lib.or_f16_to_f32
+        for h in range(65536):
+            out[h] = f(h)
+        return out
+
+    def dequant(self, gtype: int, blocks: np.ndarray, nblocks: int) -> np.ndarray:
+        be = 32 if gtype in (6, 8) else 256
+        out = np.empty(nblocks * be, dtype=np.float32)
+        assert self.lib.or_dequant_blocks(gtype, _addr(blocks), nblocks, out.ctypes.data)
+        return out
+
+    def block_dot(self, gtype: int, blk, x: np.ndarray) -> float:
+        fn = {8: self.lib.or_q8_0_dot, 6: self.lib.or_q5_0_dot, 12: self.lib.or_q4_k_dot,
+              14: self.lib.or_q6_k_dot}[gtype]
+        return fn(_addr(blk), x.ctypes.data)
+
+    def matvec(self, gtype: int, blocks: np.ndarray, rows: int, cols: int, x: np.ndarray,
+               row_begin: int = 0, row_end: int | None = None, threads: int = 1) -> np.ndarray:
+        """y[row_begin:row_end] (full-length array; other rows left at 0)."""
+        row_end = rows if row_end is None else row_end
+        y = np.zeros(rows, dtype=np.float32)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        blocks = np.ascontiguousarray(blocks)
+        if threads <= 1:
+            assert self.lib.or_matvec_rows(gtype, blocks.ctypes.data, rows, cols, x.ctypes.data,
+                                           y.ctypes.data, row_begin, row_end)
+            return y
+        edges = np.linspace(row_begin, row_end, threads + 1).astype(int)
+
+        def part(i):
+            return self.lib.or_matvec_rows(gtype, blocks.ctypes.data, rows, cols, x.ctypes.data,
+                                           y.ctypes.data, int(edges[i]), int(edges[i + 1]))
+
+        with cf.ThreadPoolExecutor(threads) as ex:
+            assert all(ex.map(part, range(threads)))
+        return y
+
+    def matmul(self, gtype: int, blocks: np.ndarray, rows: int, cols: int, X: np.ndarray,
+               batch: int) -> np.ndarray:
+        Y = np.empty((batch, rows), dtype=np.float32)
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        assert self.lib.or_matmul(gtype, _addr(blocks), rows, cols, X.ctypes.data, batch, Y.ctypes.data)
+        return Y
+
+    def row_abs_dot(self, gtype: int, blocks: np.ndarray, rows: int, cols: int,
+                    x: np.ndarray) -> np.ndarray:
+        s = np.empty(rows, dtype=np.float64)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        assert self.lib.or_row_abs_dot(gtype, _addr(blocks), rows, cols, x.ctypes.data, s.ctypes.data)
+        return s
+
+    def argmax(self, logits: np.ndarray):
+        tok = ctypes.c_int(99)
+        logits = np.ascontiguousarray(logits, dtype=np.float32)
+        ok = self.lib.or_argmax(logits.ctypes.data, logits.size, ctypes.byref(tok))
+        return ok, tok.value
+
+
+class ViewC(ctypes.Structure):
+    """src/gguf_reader.h:31-40 (for handing views to the reference)."""
+
+    _fields_ = [("data", ctypes.c_void_p), ("ggml_type", ctypes.c_uint32),
+                ("dimension_count", ctypes.c_uint32), ("dimensions", ctypes.c_uint64 * 4),
+                ("element_count", ctypes.c_uint64), ("block_elements", ctypes.c_uint64),
+                ("block_bytes", ctypes.c_uint64), ("block_count", ctypes.c_uint64)]
+
+
+class Reference:
+    """The reference engine's own hot-path code (oracle/_ref)."""
+
+    def __init__(self, path: str = REF_SCALAR_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        L = ctypes.CDLL(path)
+        L.ref_f16_to_f32.argtypes = [ctypes.c_uint16, _P]
+        L.ref_dequant_blocks.argtypes = [ctypes.c_uint32, _P, ctypes.c_uint64, _P]
+        L.ref_block_dot.argtypes = [ctypes.c_uint32, _P, _P, _P]
+        L.ref_q4_k_unpack_scale_min.argtypes = [_P, ctypes.c_int, _P, _P]
+        L.ref_q6_k_unpack_value.argtypes = [_P, ctypes.c_int, _P, _P]
+        L.ref_matvec_view.argtypes = [_P, _P, ctypes.c_int, _P, ctypes.c_int]
+        L.ref_matmul_view.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int]
+        L.ref_matvec.argtypes = [ctypes.c_uint32, _P, ctypes.c_int, ctypes.c_int, _P, _P]
+        L.ref_matmul.argtypes = [ctypes.c_uint32, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P]
+        L.ref_greedy.argtypes = [_P, ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_char_p, ctypes.c_int]
+        L.ref_set_threads.argtypes = [ctypes.c_int]
+        self.lib = L
+        assert L.ref_view_size() == ctypes.sizeof(ViewC)
+
+    def set_threads(self, n: int) -> int:
+        return self.lib.ref_set_threads(n)
+
+    def f16(self, bits: int) -> float:
+        out = ctypes.c_float()
+        assert self.lib.ref_f16_to_f32(bits, ctypes.byref(out))
+        return out.value
+
+    def dequant(self, gtype: int, blocks: np.ndarray, nblocks: int) -> np.ndarray:
+        be = 32 if gtype in (6, 8) else 256
+        out = np.empty(nblocks * be, dtype=np.float32)
+        assert self.lib.ref_dequant_blocks(gtype, _addr(blocks), nblocks, out.ctypes.data)
+        return out
+
+    def block_dot(self, gtype: int, blk, x: np.ndarray) -> float:
+        out = ctypes.c_float()
+        assert self.lib.ref_block_dot(gtype, _addr(blk), x.ctypes.data, ctypes.byref(out))
+        return out.value
+
+    def matvec(self, gtype: int, blocks: np.ndarray, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
+        y = np.empty(rows, dtype=np.float32)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        assert self.lib.ref_matvec(gtype, _addr(blocks), rows, cols, x.ctypes.data, y.ctypes.data)
+        return y
+
+    def matmul(self, gtype: int, blocks: np.ndarray, rows: int, cols: int, X: np.ndarray,
+               batch: int) -> np.ndarray:
+        Y = np.empty((batch, rows), dtype=np.float32)
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        assert self.lib.ref_matmul(gtype, _addr(blocks), rows, cols, X.ctypes.data, batch, Y.ctypes.data)
+        return Y
+
+    def matvec_view(self, view, x, xn, y, yn) -> int:
+        return self.lib.ref_matvec_view(ctypes.byref(view) if view is not None else None,
+                                        _addr(x), xn, _addr(y), yn)
+
+    def matmul_view(self, view, X, xn, batch, Y, yn) -> int:
+        return self.lib.ref_matmul_view(ctypes.byref(view) if view is not None else None,
+                                        _addr(X), xn, batch, _addr(Y), yn)
+
+    def greedy(self, logits: np.ndarray):
+        tok = ctypes.c_int(99)
+        err = ctypes.create_string_buffer(128)
+        logits = np.ascontiguousarray(logits, dtype=np.float32)
+        ok = self.lib.ref_greedy(logits.ctypes.data, logits.size, ctypes.byref(tok), err, 128)
+        return ok, tok.value, err.value.decode()

@@ -1,0 +1,336 @@
+/*
+ * CPU ORACLE — TEST INFRASTRUCTURE ONLY.
+ *
+ * This file restates, in plain C, the scalar (non-SIMD) arithmetic of the
+ * reference engine's quantized matrix-vector path so that tests can check the
+ * CUDA path against it.  Only tests/, __graft_entry__.smoke() and bench.py's
+ * cpu_baseline leg may load it; the product library never links or calls it.
+ *
+ * Parity pin: every function here is compared bit-for-bit with the reference's
+ * own sources compiled from /root/reference by oracle/Makefile (the `_ref`
+ * libraries), and with the known-answer blocks of the reference's tests
+ * (tests/q8_0_reference_test.cpp, q5_0_..., q4_k_..., q6_k_...,
+ * quantized_matvec_reference_test.cpp, sampler_greedy_test.cpp), see
+ * tests/test_oracle.py.
+ *
+ * Packed blocks are passed as raw bytes (GGUF little-endian layout); the
+ * reference's struct layouts are restated as byte offsets.
+ *
+ * Build: cc -O2 -ffp-contract=off -fPIC -shared (no FMA contraction, so every
+ * product and sum rounds exactly as the reference's scalar build does).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+/* GGML type ids: src/gguf_reader.h:7-11. */
+#define OR_Q5_0 6u
+#define OR_Q8_0 8u
+#define OR_Q4_K 12u
+#define OR_Q6_K 14u
+
+static uint16_t rd16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+/* IEEE binary16 -> binary32 by bit expansion.
+ * Follows src/quantization.cpp:11-52 (portable branch :23-49): subnormals are
+ * renormalised, Inf keeps its sign, NaN payloads are shifted up and quieted. */
+float or_f16_to_f32(uint16_t h)
+{
+    uint32_t sign = ((uint32_t)h & 0x8000u) << 16;
+    uint32_t e = (h >> 10) & 0x1fu;
+    uint32_t m = h & 0x3ffu;
+    uint32_t bits;
+    if (e == 0u) {
+        if (m == 0u) {
+            bits = sign;
+        } else {
+            /* value = m * 2^-24; find the leading one and renormalise */
+            int exp32 = 127 - 15 + 1;
+            while ((m & 0x400u) == 0u) { m <<= 1; exp32--; }
+            bits = sign | ((uint32_t)exp32 << 23) | ((m & 0x3ffu) << 13);
+        }
+    } else if (e == 31u) {
+        bits = sign | 0x7f800000u | (m << 13) | (m ? 0x00400000u : 0u);
+    } else {
+        bits = sign | ((e + (127u - 15u)) << 23) | (m << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+/* ---------------- Q8_0: 2 B fp16 d + 32 x int8 (quantization.h:33-36) ---- */
+
+/* quantization.cpp:54-67: out[i] = d * q[i] */
+void or_q8_0_dequant(const uint8_t *blk, float *out)
+{
+    float d = or_f16_to_f32(rd16(blk));
+    const int8_t *q = (const int8_t *)(blk + 2);
+    for (int i = 0; i < 32; i++) out[i] = d * (float)q[i];
+}
+
+/* quantization.cpp:150-156 (scalar branch): acc += (d * q[i]) * x[i] */
+float or_q8_0_dot(const uint8_t *blk, const float *x)
+{
+    float d = or_f16_to_f32(rd16(blk));
+    const int8_t *q = (const int8_t *)(blk + 2);
+    float acc = 0.0f;
+    for (int i = 0; i < 32; i++) acc += d * (float)q[i] * x[i];
+    return acc;
+}
+
+/* ---------------- Q5_0: d (2) + qh (4) + qs (16) (quantization.h:93-97) --- */
+
+static int q5_0_value(const uint8_t *blk, int i)
+{
+    const uint8_t *qh = blk + 2;
+    const uint8_t *qs = blk + 6;
+    int nib = (i < 16) ? (qs[i] & 0x0f) : (qs[i - 16] >> 4);
+    int hi = (qh[i >> 3] >> (i & 7)) & 1;
+    return (nib | (hi << 4)) - 16;
+}
+
+/* quantization.cpp:161-184: out[i] = d * (v - 16) */
+void or_q5_0_dequant(const uint8_t *blk, float *out)
+{
+    float d = or_f16_to_f32(rd16(blk));
+    for (int i = 0; i < 32; i++) out[i] = d * (float)q5_0_value(blk, i);
+}
+
+/* quantization.cpp:332-346 (scalar branch): acc += (d * v) * x[i] */
+float or_q5_0_dot(const uint8_t *blk, const float *x)
+{
+    float d = or_f16_to_f32(rd16(blk));
+    float acc = 0.0f;
+    for (int i = 0; i < 32; i++) acc += d * (float)q5_0_value(blk, i) * x[i];
+    return acc;
+}
+
+/* ---------------- Q4_K: d, dmin, 12 B scales, 128 B nibbles (h:152-157) --- */
+
+/* 6-bit scale/min of sub-block j from the 12-byte field.
+ * quantization.cpp:351-378 (layout described at quantization.h:169-179). */
+void or_q4_k_scale_min(const uint8_t *sm, int j, uint8_t *sc, uint8_t *mn)
+{
+    if (j < 4) {
+        *sc = sm[j] & 63;
+        *mn = sm[j + 4] & 63;
+    } else {
+        *sc = (uint8_t)((sm[j + 4] & 0x0f) | ((sm[j - 4] >> 6) << 4));
+        *mn = (uint8_t)((sm[j + 4] >> 4) | ((sm[j] >> 6) << 4));
+    }
+}
+
+/* quantization.cpp:380-409: out = (d*sc) * nib - (dmin*m), two roundings
+ * for the products and one for the difference (no fused multiply-add). */
+void or_q4_k_dequant(const uint8_t *blk, float *out)
+{
+    float d = or_f16_to_f32(rd16(blk));
+    float dmin = or_f16_to_f32(rd16(blk + 2));
+    const uint8_t *sm = blk + 4;
+    const uint8_t *qs = blk + 16;
+    for (int j = 0; j < 8; j++) {
+        uint8_t sc, mn;
+        or_q4_k_scale_min(sm, j, &sc, &mn);
+        float scale = d * (float)sc;
+        float minimum = dmin * (float)mn;
+        const uint8_t *p = qs + 32 * (j >> 1);
+        int shift = (j & 1) * 4;
+        for (int o = 0; o < 32; o++) {
+            float t = scale * (float)((p[o] >> shift) & 0x0f);
+            out[32 * j + o] = t - minimum;
+        }
+    }
+}
+
+/* quantization.cpp:536-554 (scalar branch): sub-block order, then offset. */
+float or_q4_k_dot(const uint8_t *blk, const float *x)
+{
+    float d = or_f16_to_f32(rd16(blk));
+    float dmin = or_f16_to_f32(rd16(blk + 2));
+    const uint8_t *sm = blk + 4;
+    const uint8_t *qs = blk + 16;
+    float acc = 0.0f;
+    for (int j = 0; j < 8; j++) {
+        uint8_t sc, mn;
+        or_q4_k_scale_min(sm, j, &sc, &mn);
+        float scale = d * (float)sc;
+        float minimum = dmin * (float)mn;
+        const uint8_t *p = qs + 32 * (j >> 1);
+        int shift = (j & 1) * 4;
+        for (int o = 0; o < 32; o++) {
+            float w = scale * (float)((p[o] >> shift) & 0x0f) - minimum;
+            acc += w * x[32 * j + o];
+        }
+    }
+    return acc;
+}
+
+/* ---------------- Q6_K: ql 128, qh 64, sc 16 x int8, d (h:236-241) ------- */
+
+/* Weight index i -> signed 6-bit value and int8 scale multiplier.
+ * quantization.cpp:559-586 (layout quantization.h:220-234, 254-258). */
+void or_q6_k_value(const uint8_t *blk, int i, int *q, int *sc)
+{
+    const uint8_t *ql = blk;
+    const uint8_t *qh = blk + 128;
+    const int8_t *scales = (const int8_t *)(blk + 192);
+    int g = i >> 7, local = i & 127, r = local >> 5, o = local & 31;
+    int lo = (ql[64 * g + 32 * (r & 1) + o] >> (4 * (r >> 1))) & 0x0f;
+    int hi = (qh[32 * g + o] >> (2 * r)) & 0x03;
+    *q = (lo | (hi << 4)) - 32;
+    *sc = scales[8 * g + 2 * r + (o >> 4)];
+}
+
+/* quantization.cpp:588-615: out = (d * sc) * q, evaluated left to right. */
+void or_q6_k_dequant(const uint8_t *blk, float *out)
+{
+    float d = or_f16_to_f32(rd16(blk + 208));
+    for (int i = 0; i < 256; i++) {
+        int q, sc;
+        or_q6_k_value(blk, i, &q, &sc);
+        out[i] = d * (float)sc * (float)q;
+    }
+}
+
+/* quantization.cpp:734-753 (scalar branch); index order = natural order. */
+float or_q6_k_dot(const uint8_t *blk, const float *x)
+{
+    float d = or_f16_to_f32(rd16(blk + 208));
+    float acc = 0.0f;
+    for (int i = 0; i < 256; i++) {
+        int q, sc;
+        or_q6_k_value(blk, i, &q, &sc);
+        acc += (d * (float)sc * (float)q) * x[i];
+    }
+    return acc;
+}
+
+/* ---------------- tensor-level helpers ----------------------------------- */
+
+int or_block_elements(uint32_t type)
+{
+    switch (type) {
+    case OR_Q5_0: case OR_Q8_0: return 32;
+    case OR_Q4_K: case OR_Q6_K: return 256;
+    default: return 0;
+    }
+}
+
+int or_block_bytes(uint32_t type)
+{
+    switch (type) {
+    case OR_Q5_0: return 22;
+    case OR_Q8_0: return 34;
+    case OR_Q4_K: return 144;
+    case OR_Q6_K: return 210;
+    default: return 0;
+    }
+}
+
+static float block_dot(uint32_t type, const uint8_t *blk, const float *x)
+{
+    switch (type) {
+    case OR_Q5_0: return or_q5_0_dot(blk, x);
+    case OR_Q8_0: return or_q8_0_dot(blk, x);
+    case OR_Q4_K: return or_q4_k_dot(blk, x);
+    default: return or_q6_k_dot(blk, x);
+    }
+}
+
+static void block_dequant(uint32_t type, const uint8_t *blk, float *out)
+{
+    switch (type) {
+    case OR_Q5_0: or_q5_0_dequant(blk, out); break;
+    case OR_Q8_0: or_q8_0_dequant(blk, out); break;
+    case OR_Q4_K: or_q4_k_dequant(blk, out); break;
+    default: or_q6_k_dequant(blk, out); break;
+    }
+}
+
+/* Dequantize nblocks consecutive blocks. Returns 0 for an unknown type. */
+int or_dequant_blocks(uint32_t type, const uint8_t *data, uint64_t nblocks, float *out)
+{
+    int be = or_block_elements(type), bb = or_block_bytes(type);
+    if (be == 0) return 0;
+    for (uint64_t b = 0; b < nblocks; b++) block_dequant(type, data + b * bb, out + b * be);
+    return 1;
+}
+
+/* Rows [row_begin, row_end) of y = W x.  Per row, block dots are summed in
+ * block order starting from 0.0f: quantized_matvec.cpp:10-84 (accumulation
+ * :36,49,62,75), driven row by row as in :151-160. */
+int or_matvec_rows(uint32_t type, const uint8_t *data, int rows, int cols,
+                   const float *x, float *y, int row_begin, int row_end)
+{
+    int be = or_block_elements(type), bb = or_block_bytes(type);
+    if (be == 0 || cols % be != 0 || row_begin < 0 || row_end > rows) return 0;
+    int nb = cols / be;
+    for (int r = row_begin; r < row_end; r++) {
+        float acc = 0.0f;
+        const uint8_t *row = data + (uint64_t)r * nb * bb;
+        for (int b = 0; b < nb; b++) acc += block_dot(type, row + (uint64_t)b * bb, x + b * be);
+        y[r] = acc;
+    }
+    return 1;
+}
+
+int or_matvec(uint32_t type, const uint8_t *data, int rows, int cols,
+              const float *x, float *y)
+{
+    return or_matvec_rows(type, data, rows, cols, x, y, 0, rows);
+}
+
+/* Y[p, r] for p < batch: quantized_matvec.cpp:164-224.  Y starts at 0.0f and
+ * each block's dot for position p is added in block order (:197-211). */
+int or_matmul(uint32_t type, const uint8_t *data, int rows, int cols,
+              const float *X, int batch, float *Y)
+{
+    int be = or_block_elements(type), bb = or_block_bytes(type);
+    if (be == 0 || cols % be != 0) return 0;
+    int nb = cols / be;
+    for (int r = 0; r < rows; r++) {
+        for (int p = 0; p < batch; p++) Y[(uint64_t)p * rows + r] = 0.0f;
+        for (int b = 0; b < nb; b++) {
+            const uint8_t *blk = data + ((uint64_t)r * nb + b) * bb;
+            for (int p = 0; p < batch; p++)
+                Y[(uint64_t)p * rows + r] += block_dot(type, blk, X + (uint64_t)p * cols + b * be);
+        }
+    }
+    return 1;
+}
+
+/* Per-row tolerance scale S[r] = sum_k |w_rk * x_k| with w the reference's
+ * dequantized weight, accumulated in double (tolerance = 1e-4 * S[r]). */
+int or_row_abs_dot(uint32_t type, const uint8_t *data, int rows, int cols,
+                   const float *x, double *s)
+{
+    int be = or_block_elements(type), bb = or_block_bytes(type);
+    if (be == 0 || cols % be != 0) return 0;
+    int nb = cols / be;
+    float w[256];
+    for (int r = 0; r < rows; r++) {
+        double acc = 0.0;
+        for (int b = 0; b < nb; b++) {
+            block_dequant(type, data + ((uint64_t)r * nb + b) * bb, w);
+            for (int i = 0; i < be; i++) acc += fabs((double)w[i] * (double)x[b * be + i]);
+        }
+        s[r] = acc;
+    }
+    return 1;
+}
+
+/* Greedy argmax: src/sampler.cpp:14-36.  Strict '>' keeps the lowest id on
+ * ties; any NaN/Inf anywhere fails (returns 0, *id = -1). */
+int or_argmax(const float *logits, int n, int *id)
+{
+    if (id) *id = -1;
+    if (logits == 0 || n <= 0 || id == 0) return 0;
+    int best = 0;
+    for (int i = 0; i < n; i++) {
+        if (!isfinite(logits[i])) return 0;
+        if (logits[i] > logits[best]) best = i;
+    }
+    *id = best;
+    return 1;
+}

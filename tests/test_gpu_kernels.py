@@ -1,0 +1,279 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle (calls go through
+the C ABI; device buffers come from torch).
+
+Bars (from the north star):
+  * dequantisation: bit-exact with the reference's *_dequantize_block;
+  * matvec/matmul: |y - y_ref| <= 1e-4 * sum_k |w_k x_k| per row, with w the
+    reference's dequantised weight;
+  * greedy argmax: the same token id as sampler_greedy_sample.
+"""
+import numpy as np
+import pytest
+
+from conftest import tolerance_ok
+from test_oracle import (q4_k_block, q5_0_block, q6_k_block, q8_0_block, q4_k_reference_block,
+                         q5_0_reference_block, q6_k_reference_block, fixture_block)
+
+pytestmark = pytest.mark.gpu
+
+Q5_0, Q8_0, Q4_K, Q6_K = 6, 8, 12, 14
+BE = {6: 32, 8: 32, 12: 256, 14: 256}
+BB = {6: 22, 8: 34, 12: 144, 14: 210}
+REL_TOL = 1e-4  # |y - y_ref| <= 1e-4 * sum|w x| (north-star parity bound)
+
+
+def f32_bits(a):
+    return np.asarray(a, dtype=np.float32).view(np.uint32)
+
+
+def to_dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def check_matvec(torch, qmv, oracle, gtype, blocks, rows, cols, x, rows_to_check=None):
+    w = qmv.Weight(gtype, blocks, rows, cols)
+    xd = to_dev(torch, x)
+    yd = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+    w.matvec(xd.data_ptr(), yd.data_ptr())
+    torch.cuda.synchronize()
+    y = yd.cpu().numpy()
+    if rows_to_check is None:
+        y_ref = oracle.matvec(gtype, blocks, rows, cols, x, threads=8)
+        s = oracle.row_abs_dot(gtype, blocks, rows, cols, x)
+        bad, err, bound = tolerance_ok(y, y_ref, s, REL_TOL)
+    else:
+        sel = np.asarray(rows_to_check)
+        sub = np.ascontiguousarray(blocks.reshape(rows, -1)[sel])
+        y_ref = oracle.matvec(gtype, sub, sel.size, cols, x)
+        s = oracle.row_abs_dot(gtype, sub, sel.size, cols, x)
+        bad, err, bound = tolerance_ok(y[sel], y_ref, s, REL_TOL)
+    assert bad.size == 0, f"{bad.size} rows out of tolerance, worst ratio {np.max(err / np.maximum(bound, 1e-30))}"
+    w.free()
+    return y
+
+
+# -------------------------------------------------------------- dequant
+
+@pytest.mark.parametrize("gtype,rows,cols", [(Q8_0, 67, 160), (Q5_0, 67, 160), (Q4_K, 23, 768),
+                                             (Q6_K, 23, 768), (Q8_0, 4864, 896), (Q5_0, 4864, 896)])
+def test_dequant_resident_bitexact(cuda, qmv, oracle, workloads, gtype, rows, cols):
+    torch = cuda
+    blocks = workloads.make_blocks(gtype, rows, cols, seed=21)
+    w = qmv.Weight(gtype, blocks, rows, cols)
+    out = torch.empty(rows * cols, dtype=torch.float32, device="cuda")
+    w.dequantize(out.data_ptr())
+    torch.cuda.synchronize()
+    want = oracle.dequant(gtype, blocks, rows * cols // BE[gtype])
+    assert np.array_equal(f32_bits(out.cpu().numpy()), f32_bits(want))
+
+
+@pytest.mark.parametrize("gtype", [Q8_0, Q5_0, Q4_K, Q6_K])
+def test_dequant_raw_unaligned_and_special_scales(cuda, qmv, oracle, gtype):
+    """Raw blocks at an odd device address; fp16 scales cover subnormals, both
+    zeros, Inf and NaN (payload bits must match the reference too)."""
+    torch = cuda
+    rng = np.random.default_rng(gtype)
+    specials = [0x0001, 0x03FF, 0x8001, 0x0000, 0x8000, 0x7C00, 0xFC00, 0x7E01, 0x7C01, 0xFDFF, 0x3800, 0x1234]
+    n = 64
+    blocks = rng.integers(0, 256, size=(n, BB[gtype]), dtype=np.uint8)
+    for i in range(n):
+        d = specials[i % len(specials)]
+        off = 208 if gtype == Q6_K else 0
+        blocks[i, off:off + 2] = [d & 0xFF, d >> 8]
+        if gtype == Q4_K:
+            m = specials[(i + 3) % len(specials)]
+            blocks[i, 2:4] = [m & 0xFF, m >> 8]
+    raw = np.zeros(blocks.size + 1, np.uint8)
+    raw[1:] = blocks.reshape(-1)
+    draw = to_dev(torch, raw)
+    out = torch.empty(n * BE[gtype], dtype=torch.float32, device="cuda")
+    qmv.dequantize_raw(gtype, draw.data_ptr() + 1, n, out.data_ptr())
+    torch.cuda.synchronize()
+    want = oracle.dequant(gtype, blocks, n)
+    assert np.array_equal(f32_bits(out.cpu().numpy()), f32_bits(want))
+
+
+def test_dequant_reference_known_blocks(cuda, qmv, oracle):
+    torch = cuda
+    for gtype, blk in ((Q8_0, q8_0_block(0x3800, [-4, 0, 6])), (Q5_0, q5_0_reference_block()),
+                       (Q4_K, q4_k_reference_block()), (Q6_K, q6_k_reference_block())):
+        d = to_dev(torch, blk)
+        out = torch.empty(BE[gtype], dtype=torch.float32, device="cuda")
+        qmv.dequantize_raw(gtype, d.data_ptr(), 1, out.data_ptr())
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy(), oracle.dequant(gtype, blk, 1))
+
+
+# -------------------------------------------------------------- matvec
+
+@pytest.mark.parametrize("gtype,rows,cols", [
+    (Q8_0, 1, 32), (Q8_0, 17, 96), (Q8_0, 300, 896), (Q8_0, 129, 4096),
+    (Q5_0, 1, 32), (Q5_0, 17, 96), (Q5_0, 300, 896), (Q5_0, 77, 3584),
+    (Q4_K, 1, 256), (Q4_K, 17, 768), (Q4_K, 301, 3584), (Q4_K, 64, 18944),
+    (Q6_K, 1, 256), (Q6_K, 17, 768), (Q6_K, 301, 3584), (Q6_K, 33, 18944),
+    (Q8_0, 5, 65536),
+])
+def test_matvec_shapes(cuda, qmv, oracle, workloads, gtype, rows, cols):
+    blocks = workloads.make_blocks(gtype, rows, cols, seed=rows + cols)
+    x = workloads.make_activations(cols, seed=rows)
+    check_matvec(cuda, qmv, oracle, gtype, blocks, rows, cols, x)
+
+
+@pytest.mark.parametrize("name", ["cfg0_q8_0_4864x896", "cfg1a_q4_k_18944x3584",
+                                  "cfg1b_q4_k_3584x18944", "cfg3_q5_0_4864x896"])
+def test_matvec_benchmark_configs(cuda, qmv, oracle, workloads, name):
+    gtype, rows, cols = workloads.CONFIGS[name]
+    blocks = workloads.make_blocks(gtype, rows, cols, seed=0)
+    x = workloads.make_activations(cols, seed=0)
+    check_matvec(cuda, qmv, oracle, gtype, blocks, rows, cols, x)
+
+
+def test_matvec_known_answers(cuda, qmv):
+    """quantized_matvec_reference_test.cpp:44-154 on the device."""
+    torch = cuda
+    cases = []
+    blocks = np.concatenate([q8_0_block(0x3800, [2, -4]), q8_0_block(0x3800, [6, 2])])
+    x = np.zeros(32, np.float32)
+    x[:2] = [1, 2]
+    cases.append((Q8_0, blocks, 2, 32, x, [-3.0, 5.0]))
+    x1 = np.zeros(32, np.float32)
+    x1[0] = 1
+    cases.append((Q5_0, q5_0_block(0x3800, [0] * 4, [0] * 16), 1, 32, x1, [-8.0]))
+    x2 = np.zeros(256, np.float32)
+    x2[0] = 1
+    sm = [0] * 12
+    sm[0] = sm[4] = 1
+    cases.append((Q4_K, q4_k_block(0x3800, 0x3400, sm, [0] * 128), 1, 256, x2, [-0.25]))
+    sc = [0] * 16
+    sc[0] = 1
+    cases.append((Q6_K, q6_k_block([0] * 128, [0] * 64, sc, 0x3800), 1, 256, x2, [-16.0]))
+    for gtype, blk, rows, cols, xv, want in cases:
+        w = qmv.Weight(gtype, blk, rows, cols)
+        xd = to_dev(torch, xv)
+        yd = torch.empty(rows, dtype=torch.float32, device="cuda")
+        w.matvec(xd.data_ptr(), yd.data_ptr())
+        torch.cuda.synchronize()
+        assert np.allclose(yd.cpu().numpy(), want, atol=1e-5, rtol=0), gtype
+
+
+@pytest.mark.parametrize("gtype", [Q5_0, Q8_0, Q4_K, Q6_K])
+@pytest.mark.parametrize("cxx", [False, True])
+def test_dropin_host_entry_unaligned(cuda, qmv, oracle, gtype, cxx):
+    """The reference-signature entry points (C and mangled C++ symbols) on
+    host storage at an odd address: 17 rows x 3 constant blocks
+    (quantized_matvec_reference_test.cpp:156-202), then seeded blocks."""
+    be, bb = BE[gtype], BB[gtype]
+    rows, nbr = 17, 3
+    cols = nbr * be
+    storage = np.zeros(1 + rows * nbr * bb, np.uint8)
+    x = np.array([(c % 13 - 6) / 8.0 for c in range(cols)], np.float32)
+    expected = np.zeros(rows)
+    for r in range(rows):
+        for b in range(nbr):
+            blk, wv = fixture_block(gtype, r * nbr + b)
+            storage[1 + (r * nbr + b) * bb: 1 + (r * nbr + b + 1) * bb] = blk
+            expected[r] += wv * x[b * be:(b + 1) * be].astype(np.float64).sum()
+    view = qmv.make_view(gtype, storage.ctypes.data + 1, rows, cols)
+    out = np.full(rows + 2, -999.0, np.float32)
+    assert qmv.quantized_tensor_matvec_f32(view, x, cols, out.ctypes.data + 4, rows, cxx_symbol=cxx) == 1, qmv.last_error()
+    assert out[0] == -999.0 and out[-1] == -999.0  # sentinels untouched
+    assert np.allclose(out[1:-1], expected, atol=1e-5, rtol=0)
+    # batched == repeated matvec (quantized_matvec_reference_test.cpp:204-221)
+    X = np.stack([x, x[::-1].copy(), -x])
+    Y = np.zeros((3, rows), np.float32)
+    assert qmv.quantized_tensor_matmul_f32(view, X, cols, 3, Y, rows, cxx_symbol=cxx) == 1, qmv.last_error()
+    for p in range(3):
+        yp = np.zeros(rows, np.float32)
+        assert qmv.quantized_tensor_matvec_f32(view, X[p], cols, yp, rows, cxx_symbol=cxx) == 1
+        s = oracle.row_abs_dot(gtype, storage[1:], rows, cols, X[p])
+        assert tolerance_ok(Y[p], yp, 2 * s)[0].size == 0
+
+
+# -------------------------------------------------------------- matmul
+
+@pytest.mark.parametrize("gtype,rows,cols", [(Q5_0, 4864, 896), (Q8_0, 300, 896), (Q4_K, 129, 3584),
+                                             (Q6_K, 129, 3584), (Q4_K, 40, 18944)])
+@pytest.mark.parametrize("batch", [1, 3, 8, 13])
+def test_matmul_parity(cuda, qmv, oracle, workloads, gtype, rows, cols, batch):
+    torch = cuda
+    blocks = workloads.make_blocks(gtype, rows, cols, seed=3)
+    X = np.stack([workloads.make_activations(cols, seed=50 + p) for p in range(batch)])
+    w = qmv.Weight(gtype, blocks, rows, cols)
+    Xd = to_dev(torch, X)
+    Yd = torch.full((batch, rows), float("nan"), dtype=torch.float32, device="cuda")
+    w.matmul(Xd.data_ptr(), batch, Yd.data_ptr())
+    torch.cuda.synchronize()
+    Y = Yd.cpu().numpy()
+    Y_ref = oracle.matmul(gtype, blocks, rows, cols, X, batch)
+    for p in range(batch):
+        s = oracle.row_abs_dot(gtype, blocks, rows, cols, X[p])
+        bad, err, bound = tolerance_ok(Y[p], Y_ref[p], s, REL_TOL)
+        assert bad.size == 0, (p, bad[:5])
+
+
+# -------------------------------------------------------------- argmax
+
+def test_argmax_known_answers(cuda, qmv):
+    """tests/sampler_greedy_test.cpp:52-83 on device logits."""
+    torch = cuda
+    fmax = float(np.finfo(np.float32).max)
+    cases = [([-3.0, 0.5, 7.0, 2.0], 2), ([-10.0, -2.0, -5.0], 1), ([4.0, 4.0, -1.0, 4.0], 0),
+             ([-1.0, 9.0, 9.0], 1), ([-fmax], 0), ([-fmax, fmax, 0.0], 1), ([-0.0, 0.0], 0)]
+    for logits, want in cases:
+        d = to_dev(torch, np.array(logits, np.float32))
+        ok, tok, err = qmv.sampler_greedy_sample(d.data_ptr(), len(logits))
+        assert (ok, tok, err) == (1, want, "")
+    for bad in (np.nan, np.inf, -np.inf):
+        for at in range(3):
+            a = np.array([3.0, 2.0, 1.0], np.float32)
+            a[at] = bad
+            d = to_dev(torch, a)
+            ok, tok, err = qmv.sampler_greedy_sample(d.data_ptr(), 3)
+            assert (ok, tok) == (0, -1) and err == "Greedy sampler received a non-finite logit."
+
+
+def test_argmax_large_random_and_ties(cuda, qmv, oracle):
+    torch = cuda
+    rng = np.random.default_rng(7)
+    ws = torch.zeros(qmv.argmax_workspace_bytes(), dtype=torch.uint8, device="cuda")
+    key = torch.zeros(1, dtype=torch.int64, device="cuda")
+    for n in (1, 31, 1000, 152064, 1 << 22):
+        a = rng.standard_normal(n).astype(np.float32)
+        if n > 10:
+            a[n // 3] = a[n - 2] = a.max() + 1.0  # tie: the lower index must win
+        d = to_dev(torch, a)
+        for _ in range(2):  # the workspace counter must re-arm itself
+            qmv.argmax(d.data_ptr(), n, key.data_ptr(), ws.data_ptr())
+            torch.cuda.synchronize()
+            k = int(key.cpu().numpy().view(np.uint64)[0])
+            assert qmv.key_to_token(k) == oracle.argmax(a)[1]
+    assert int(ws.sum().item()) == 0
+
+
+def test_matvec_argmax_fused_and_sharded(cuda, qmv, oracle, workloads):
+    """Fused projection + argmax on a 6000-row Q6_K matrix, whole and as
+    2/3/8 row shards combined by a key max (the cross-rank combine)."""
+    torch = cuda
+    rows, cols = 6000, 3584
+    blocks = workloads.make_blocks(Q6_K, rows, cols, seed=9)
+    x = workloads.make_activations(cols, seed=9)
+    y_ref = oracle.matvec(Q6_K, blocks, rows, cols, x, threads=8)
+    ok, want = oracle.argmax(y_ref)
+    assert ok
+    xd = to_dev(torch, x)
+    ws = torch.zeros(qmv.argmax_workspace_bytes(), dtype=torch.uint8, device="cuda")
+    for shards in (1, 2, 3, 8):
+        per = -(-rows // shards)
+        keys = []
+        logits = torch.empty(rows, dtype=torch.float32, device="cuda")
+        for r in range(shards):
+            b, e = r * per, min(rows, (r + 1) * per)
+            w = qmv.Weight(Q6_K, blocks, rows, cols, row_begin=b, row_end=e)
+            key = torch.zeros(1, dtype=torch.int64, device="cuda")
+            w.matvec_argmax(xd.data_ptr(), logits[b:e].data_ptr(), key.data_ptr(), ws.data_ptr())
+            torch.cuda.synchronize()
+            keys.append(int(key.cpu().numpy().view(np.uint64)[0]))
+            w.free()
+        assert qmv.key_to_token(max(keys)) == want
+        s = oracle.row_abs_dot(Q6_K, blocks, rows, cols, x)
+        assert tolerance_ok(logits.cpu().numpy(), y_ref, s, REL_TOL)[0].size == 0
