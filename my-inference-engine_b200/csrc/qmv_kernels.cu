@@ -12,11 +12,14 @@
 //                (src/sampler.cpp:14-36).
 //
 // Integer inner loop.  Each 32-element block j of x is quantized on the fly
-// into 16-bit integers xq = rint(x * 32639 / amax_j) held as two int8 planes
-// (hi = (xq + 128) >> 8, lo = xq - 256 hi), with s_j = amax_j / 32639.  A
-// block dot is then s_j * (256 * dp4a(w, hi) + dp4a(w, lo)) with exact 32-bit
-// integer sums; the relative quantisation error of x is 2^-16 of the block
-// maximum, far inside the parity bound |y - y_ref| <= 1e-4 * sum|w x|.
+// into 16-bit integers xq = rint(x / s_j) held as two int8 planes
+// (hi = (xq + 128) >> 8, lo = xq - 256 hi), where s_j is the power of two
+// that puts max|xq| in (16320, 32639].  A block dot is then
+// s_j * (256 * dp4a(w, hi) + dp4a(w, lo)) with exact 32-bit integer sums; the
+// quantisation error of x is at most 2^-15 of the block maximum (none at all
+// for dyadic inputs), far inside the parity bound
+// |y - y_ref| <= 1e-4 * sum|w x|.  Blocks whose maximum is below 2^-100 share
+// the scale 2^-114, so magnitudes under 2^-115 quantize to zero.
 // Offsets of Q5_0 (-16) and Q6_K (-32) are folded in with per-16-element sums
 // of xq; the Q4_K minimum uses the same sums.
 #include <cuda_fp16.h>
@@ -31,7 +34,6 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr unsigned kFull = 0xffffffffu;
-constexpr int kXQMax = 32639;  // 127 * 256 + 127: keeps hi and lo in int8
 
 __host__ __device__ constexpr uint32_t pad16(uint32_t v) { return (v + 15u) & ~15u; }
 
@@ -215,9 +217,17 @@ __device__ void quantize_x(const float *__restrict__ x, int cols, uint8_t *base)
             a = max(a, __shfl_xor_sync(kFull, a, 1));
             a = max(a, __shfl_xor_sync(kFull, a, 2));
             a = max(a, __shfl_xor_sync(kFull, a, 4));
+            // Power-of-two scale s = 2^e with |x| / s <= 32639: x * 2^-e is
+            // exact, so dyadic inputs (small integers, k/2^n) stay exact.
             const bool bad = a >= 0x7f800000u;
-            const float amax = __uint_as_float(a);
-            const float inv = (a == 0u || bad) ? 0.f : (float)kXQMax / amax;
+            const int ea = max((int)(a >> 23), 27);  // blocks below 2^-100 share 2^-114
+            int e = ea - 127 - 14;
+            float inv = __uint_as_float((uint32_t)(127 - e) << 23);
+            if (__uint_as_float(a) * inv >= 32639.5f) {
+                e += 1;
+                inv *= 0.5f;
+            }
+            if (bad) inv = 0.f;
             int q0 = __float2int_rn(v[u].x * inv), q1 = __float2int_rn(v[u].y * inv);
             int q2 = __float2int_rn(v[u].z * inv), q3 = __float2int_rn(v[u].w * inv);
             int h0 = (q0 + 128) >> 8, h1 = (q1 + 128) >> 8, h2 = (q2 + 128) >> 8, h3 = (q3 + 128) >> 8;
@@ -233,7 +243,8 @@ __device__ void quantize_x(const float *__restrict__ x, int cols, uint8_t *base)
                 xh[f] = hh;
                 xl[f] = ll;
                 if ((lane & 3) == 0) xsum[f >> 2] = s4;
-                if ((lane & 7) == 0) xs[f >> 3] = bad ? __uint_as_float(0x7fc00000u) : amax / (float)kXQMax;
+                if ((lane & 7) == 0)
+                    xs[f >> 3] = bad ? __uint_as_float(0x7fc00000u) : __uint_as_float((uint32_t)(127 + e) << 23);
             }
         }
     }
@@ -630,16 +641,40 @@ struct BlockRef {
     const uint8_t *qh;   // Q5_0 high bits
 };
 
+// The reference's scalar build runs on x86 SSE, where a NaN result carries
+// the payload of the first NaN operand (quieted) and an invalid operation on
+// non-NaN operands (Inf * 0, Inf - Inf) yields the default NaN 0xFFC00000.
+// GPU arithmetic returns a canonical NaN instead, so the dequantiser restores
+// the x86 bits to stay bit-exact for every encoding.
+__device__ __forceinline__ float x86_nan(float a, float b)
+{
+    if (isnan(a)) return __uint_as_float(__float_as_uint(a) | 0x00400000u);
+    if (isnan(b)) return __uint_as_float(__float_as_uint(b) | 0x00400000u);
+    return __uint_as_float(0xffc00000u);
+}
+
+__device__ __forceinline__ float mul_ref(float a, float b)
+{
+    const float r = __fmul_rn(a, b);
+    return isnan(r) ? x86_nan(a, b) : r;
+}
+
+__device__ __forceinline__ float sub_ref(float a, float b)
+{
+    const float r = __fsub_rn(a, b);
+    return isnan(r) ? x86_nan(a, b) : r;
+}
+
 // Value i of a block, with the reference's rounding sequence (no FMA).
 template <uint32_t FMT>
 __device__ __forceinline__ float dequant_value(const BlockRef &b, int i)
 {
     if constexpr (FMT == kQ8_0) {
-        return __fmul_rn(f16_exact(b.d16), (float)(int8_t)b.p[i]);
+        return mul_ref(f16_exact(b.d16), (float)(int8_t)b.p[i]);
     } else if constexpr (FMT == kQ5_0) {
         const int nib = i < 16 ? (b.p[i] & 0x0f) : (b.p[i - 16] >> 4);
         const int hi = (b.qh[i >> 3] >> (i & 7)) & 1;
-        return __fmul_rn(f16_exact(b.d16), (float)((nib | (hi << 4)) - 16));
+        return mul_ref(f16_exact(b.d16), (float)((nib | (hi << 4)) - 16));
     } else if constexpr (FMT == kQ4_K) {
         const uint8_t *sm = b.p + 4;
         const int j = i >> 5, o = i & 31;
@@ -653,17 +688,17 @@ __device__ __forceinline__ float dequant_value(const BlockRef &b, int i)
         }
         const float d = f16_exact((uint32_t)b.p[0] | ((uint32_t)b.p[1] << 8));
         const float dmin = f16_exact((uint32_t)b.p[2] | ((uint32_t)b.p[3] << 8));
-        const float scale = __fmul_rn(d, (float)sc);
-        const float minimum = __fmul_rn(dmin, (float)mn);
+        const float scale = mul_ref(d, (float)sc);
+        const float minimum = mul_ref(dmin, (float)mn);
         const int nib = (b.p[16 + 32 * (j >> 1) + o] >> (4 * (j & 1))) & 0x0f;
-        return __fsub_rn(__fmul_rn(scale, (float)nib), minimum);
+        return sub_ref(mul_ref(scale, (float)nib), minimum);
     } else {
         const int g = i >> 7, loc = i & 127, r = loc >> 5, o = loc & 31;
         const int lo = (b.p[64 * g + 32 * (r & 1) + o] >> (4 * (r >> 1))) & 0x0f;
         const int hi = (b.p[128 + 32 * g + o] >> (2 * r)) & 0x03;
         const int q = (lo | (hi << 4)) - 32;
         const int sc = (int8_t)b.p[192 + 8 * g + 2 * r + (o >> 4)];
-        return __fmul_rn(__fmul_rn(f16_exact(b.d16), (float)sc), (float)q);
+        return mul_ref(mul_ref(f16_exact(b.d16), (float)sc), (float)q);
     }
 }
 

@@ -239,6 +239,36 @@ def test_seeded_workload_bitexact_vs_reference(oracle, ref, workloads, gtype, ro
                           f32_bits(ref.matmul(gtype, blocks, rows, cols, X, 3)))
 
 
+SPECIAL_F16 = [0x0001, 0x03FF, 0x8001, 0x0000, 0x8000, 0x7C00, 0xFC00, 0x7E01, 0x7C01, 0xFDFF,
+               0x3800, 0x1234]
+
+
+def special_scale_blocks(gtype, n=64, seed=None):
+    """Random payloads whose fp16 scales cycle through subnormals, signed
+    zeros, infinities and NaN payloads (shared with the GPU dequant test)."""
+    rng = np.random.default_rng(gtype if seed is None else seed)
+    bb = {6: 22, 8: 34, 12: 144, 14: 210}[gtype]
+    blocks = rng.integers(0, 256, size=(n, bb), dtype=np.uint8)
+    for i in range(n):
+        d = SPECIAL_F16[i % len(SPECIAL_F16)]
+        off = 208 if gtype == Q6_K else 0
+        blocks[i, off:off + 2] = [d & 0xFF, d >> 8]
+        if gtype == Q4_K:
+            m = SPECIAL_F16[(i + 3) % len(SPECIAL_F16)]
+            blocks[i, 2:4] = [m & 0xFF, m >> 8]
+    return blocks
+
+
+@pytest.mark.parametrize("gtype", [Q8_0, Q5_0, Q4_K, Q6_K])
+def test_special_scales_bitexact_vs_reference(oracle, ref, gtype):
+    """NaN payloads, Inf*0 and Inf-Inf results must carry the same bits as the
+    reference's x86 build (the GPU dequantiser reproduces these rules)."""
+    blocks = special_scale_blocks(gtype)
+    want = ref.dequant(gtype, blocks, 64)
+    assert np.array_equal(f32_bits(oracle.dequant(gtype, blocks, 64)), f32_bits(want))
+    assert np.isnan(want).any() and np.isinf(want).any()
+
+
 # ------------------------------------------------------ matvec / argmax KATs
 
 def fixture_block(gtype, index):
