@@ -122,16 +122,9 @@ int upload(const GgufQuantizedTensorView *view, int row_begin, int row_end, QmvW
     uint8_t *tmp = nullptr;
     cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&w->dev, bytes);
-    if (e == cudaSuccess) {
-        if (L.type == qmv::kQ4_K) {
-            // raw 144-byte blocks are already the resident layout
-            e = cudaMemcpyAsync(w->dev, src, raw_bytes, cudaMemcpyHostToDevice, s);
-        } else {
-            e = cudaMalloc(&tmp, raw_bytes);
-            if (e == cudaSuccess) e = cudaMemcpyAsync(tmp, src, raw_bytes, cudaMemcpyHostToDevice, s);
-            if (e == cudaSuccess) e = qmv::launch_repack(L, tmp, w->dev, s);
-        }
-    }
+    if (e == cudaSuccess) e = cudaMalloc(&tmp, raw_bytes);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(tmp, src, raw_bytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = qmv::launch_repack(L, tmp, w->dev, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (tmp) cudaFree(tmp);
     if (s) cudaStreamDestroy(s);

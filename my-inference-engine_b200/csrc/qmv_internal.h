@@ -12,29 +12,39 @@ namespace qmv {
 enum : uint32_t { kQ5_0 = 6u, kQ8_0 = 8u, kQ4_K = 12u, kQ6_K = 14u };
 
 // Largest column count the kernels stage in shared memory (x is quantized to
-// 2.375 B/column per position): 65536 columns = 152 KiB for one position.
+// 2.5 B/column per position): 65536 columns = 160 KiB for one position.
 constexpr int kMaxCols = 65536;
 // Upper bound on CTAs of one argmax-producing launch (size of the workspace
 // key array).
 constexpr int kMaxArgmaxCtas = 2048;
 constexpr size_t kArgmaxWorkspaceBytes = 16 + 8 * (size_t)kMaxArgmaxCtas;
 
-// Device layout of one resident tensor.  Rows are contiguous and every row
-// starts on a 16-byte boundary; the odd-sized fp16 block scales of Q8_0, Q5_0
-// and Q6_K are moved to the end of their row so the quant payload can be read
-// with 128-bit loads:
-//   Q8_0 row: qs[32*nb] | d[nb] (fp16, padded to 16 B)
-//   Q5_0 row: qs[16*nb] | qh[4*nb] (padded) | d[nb] (padded)
-//   Q4_K row: raw 144-byte blocks (already 9 x 16 B)
-//   Q6_K row: {ql[128] qh[64] sc[16]}[nb] (208 B each) | d[nb] (padded)
+// Device layout of one resident tensor ("chunk-major").  Rows are contiguous
+// and start on 16-byte boundaries.  A row is cut into C chunks, the unit one
+// GEMV lane handles (a 32-weight block for Q8_0/Q5_0, 64 weights for
+// Q4_K/Q6_K), and each chunk's 16-byte pieces are stored piece-major:
+// piece j of chunk c sits at (j * C + c) * 16, so the 32 lanes of a warp
+// reading piece j of chunks c..c+31 read one contiguous 512-byte run.
+// Per-row segments (bytes, C = chunks per row, nb = blocks per row):
+//   Q8_0 (C = nb):    q[0..15] pieces | q[16..31] pieces | d[C] fp16      (32 C + pad)
+//   Q5_0 (C = nb):    qs pieces | qh[C] u32 (off_a) | d[C] fp16 (off_b)    (22 nb + pad)
+//   Q4_K (C = 4 nb):  qs bytes 0-15 of group g | bytes 16-31 | raw 16-byte
+//                     headers {d, dmin, 12 scale bytes}[nb] (off_a)        (144 nb, no pad)
+//   Q6_K (C = 4 nb):  chunk (sb, g, h) = 4 sb + 2 g + h holds weights
+//                     {128 g + 32 r + 16 h + o}: ql[64g+16h..] | ql[64g+32+16h..]
+//                     | qh[32g+16h..] pieces | sc[8g+2r+h] r=0..3 as 4 bytes (off_a)
+//                     | d[nb] fp16 (off_b)                                 (208 nb + pad)
+// Every byte of the GGUF blocks is kept; only the Q8_0/Q5_0/Q6_K padding to
+// 16 bytes per row is added.
 struct Layout {
     uint32_t type;
     int rows;
     int cols;
     int nb;               // blocks per row
+    int C;                // chunks per row
     uint64_t row_stride;  // bytes, multiple of 16
-    uint32_t off_qh;      // Q5_0 qh segment
-    uint32_t off_d;       // Q8_0/Q5_0/Q6_K fp16 scale segment
+    uint32_t off_a;       // Q8_0 d, Q5_0 qh, Q4_K headers, Q6_K scales
+    uint32_t off_b;       // Q5_0 d, Q6_K d
 };
 
 int block_elements(uint32_t type);

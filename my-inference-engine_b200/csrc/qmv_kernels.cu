@@ -1,27 +1,31 @@
 // sm_100a kernels for the GGUF quantized matrix-vector path.
 //
-//  * repack      raw GGUF blocks -> 16-byte-aligned resident rows (once).
+//  * repack      raw GGUF blocks -> chunk-major resident rows (once per upload).
 //  * dequant     bit-exact block decoding (same float bits as the reference's
 //                *_dequantize_block, src/quantization.cpp:54-67, 161-184,
-//                380-409, 588-615).
-//  * gemv        y = W x, in-register dequantisation with dp4a integer dots.
-//  * matmul      Y = W X for a batch of positions, each weight block loaded
+//                380-409, 588-615, including x86 NaN payload rules).
+//  * gemv        y = W x with in-register dequantisation and dp4a integer dots.
+//  * matmul      Y = W X for a batch of positions; each weight chunk is loaded
 //                once and applied to every position
 //                (src/quantized_matvec.cpp:164-224).
-//  * argmax      greedy selection fused into the gemv epilogue, or alone
+//  * argmax      greedy selection fused into the gemv epilogue, or standalone
 //                (src/sampler.cpp:14-36).
 //
-// Integer inner loop.  Each 32-element block j of x is quantized on the fly
-// into 16-bit integers xq = rint(x / s_j) held as two int8 planes
-// (hi = (xq + 128) >> 8, lo = xq - 256 hi), where s_j is the power of two
-// that puts max|xq| in (16320, 32639].  A block dot is then
-// s_j * (256 * dp4a(w, hi) + dp4a(w, lo)) with exact 32-bit integer sums; the
-// quantisation error of x is at most 2^-15 of the block maximum (none at all
-// for dyadic inputs), far inside the parity bound
-// |y - y_ref| <= 1e-4 * sum|w x|.  Blocks whose maximum is below 2^-100 share
-// the scale 2^-114, so magnitudes under 2^-115 quantize to zero.
-// Offsets of Q5_0 (-16) and Q6_K (-32) are folded in with per-16-element sums
-// of xq; the Q4_K minimum uses the same sums.
+// Integer inner loop.  Each 32-element block of x is quantized on the fly
+// into 16-bit integers xq = rint(x / s) held as two int8 planes
+// (hi = (xq + 128) >> 8, lo = xq - 256 hi), where s is the power of two that
+// puts max|xq| in (16320, 32639].  A block dot is then
+// s * (256 * dp4a(w, hi) + dp4a(w, lo)) with exact 32-bit integer sums; the
+// quantisation error of x is at most 2^-15 of the block maximum (zero for
+// dyadic inputs), far inside the parity bound |y - y_ref| <= 1e-4 * sum|w x|.
+// Blocks whose maximum is below 2^-100 share the scale 2^-114, so magnitudes
+// under 2^-115 quantize to zero.  The Q5_0 (-16) and Q6_K (-32) offsets and
+// the Q4_K minimum use per-16-element sums of xq.
+//
+// Shared-memory x layout mirrors the weight layout: the 16-element slice j
+// of chunk c is stored at (j * C + c) * 16 in each plane, with one record
+// {scale bits, sum of xq} per slice, so lanes reading consecutive chunks hit
+// consecutive banks.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -79,21 +83,18 @@ __device__ __forceinline__ uint4 ld_stream(const uint8_t *p)
     return v;
 }
 
-__device__ __forceinline__ uint2 ld_stream8(const uint8_t *p)
+__device__ __forceinline__ uint32_t ld_stream32(const uint8_t *p)
 {
-    uint2 v;
-    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    uint32_t v;
+    asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
     return v;
 }
 
-__device__ __forceinline__ uint32_t ld_u32(const uint8_t *p)
+__device__ __forceinline__ uint32_t ld_stream16(const uint8_t *p)
 {
-    return __ldg(reinterpret_cast<const unsigned int *>(p));
-}
-
-__device__ __forceinline__ uint32_t ld_u16(const uint8_t *p)
-{
-    return __ldg(reinterpret_cast<const unsigned short *>(p));
+    unsigned short v;
+    asm("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
 }
 
 __device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c)
@@ -136,7 +137,7 @@ __device__ unsigned long long block_max_key(unsigned long long k, unsigned long 
 }
 
 // Publish this CTA's key; the last CTA to arrive folds all of them into
-// *out and re-arms the counter.  No CTA waits on another.
+// *am.key and re-arms the counter.  No CTA waits on another.
 __device__ void finish_argmax(unsigned long long cta_key, const ArgmaxOut &am,
                               unsigned long long *scratch)
 {
@@ -165,40 +166,70 @@ __device__ void finish_argmax(unsigned long long cta_key, const ArgmaxOut &am,
 
 // ------------------------------------------------------- x quantisation
 
-struct XS {
-    const int8_t *xh;   // [cols]
-    const int8_t *xl;   // [cols]
-    const float *xs;    // [cols/32] block scale (NaN if the block is non-finite)
-    const int *xsum;    // [cols/16] sum of xq over 16 elements
+// Slices of 16 x values per chunk and the chunk-major index of the slice
+// that starts at position p (a multiple of 16).
+template <uint32_t FMT> struct Slices;
+template <> struct Slices<kQ8_0> {
+    static constexpr int kPerChunk = 2;
+    static __device__ __forceinline__ int index(int p, int C) { return ((p >> 4) & 1) * C + (p >> 5); }
+};
+template <> struct Slices<kQ5_0> {
+    static constexpr int kPerChunk = 2;
+    static __device__ __forceinline__ int index(int p, int C) { return ((p >> 4) & 1) * C + (p >> 5); }
+};
+template <> struct Slices<kQ4_K> {
+    static constexpr int kPerChunk = 4;
+    static __device__ __forceinline__ int index(int p, int C) { return ((p >> 4) & 3) * C + (p >> 6); }
+};
+template <> struct Slices<kQ6_K> {
+    static constexpr int kPerChunk = 4;
+    static __device__ __forceinline__ int index(int p, int C)
+    {
+        return ((p >> 5) & 3) * C + 2 * (p >> 7) + ((p >> 4) & 1);
+    }
 };
 
-// Bytes of one quantized position, rounded up to 16 so that consecutive
-// positions keep the 16-byte alignment of their 128-bit shared loads.
+// Quantized x of one position in shared memory.
+struct XS {
+    const uint8_t *hi;   // [cols] int8, chunk-major slices
+    const uint8_t *lo;   // [cols]
+    const int2 *rec;     // [cols/16] {scale bits (NaN if non-finite), sum of xq}
+    __device__ __forceinline__ uint4 h(int j, int C, int c) const
+    {
+        return *reinterpret_cast<const uint4 *>(hi + ((j * C + c) << 4));
+    }
+    __device__ __forceinline__ uint4 l(int j, int C, int c) const
+    {
+        return *reinterpret_cast<const uint4 *>(lo + ((j * C + c) << 4));
+    }
+    __device__ __forceinline__ int2 r(int j, int C, int c) const { return rec[j * C + c]; }
+};
+
+// Bytes of one quantized position, rounded up to 16 so consecutive positions
+// keep the 16-byte alignment of their 128-bit shared loads.
 __host__ __device__ constexpr size_t xs_bytes(int cols)
 {
-    return (2 * (size_t)cols + (size_t)cols / 8 + (size_t)cols / 4 + 15) & ~(size_t)15;
+    return (2 * (size_t)cols + (size_t)cols / 2 + 15) & ~(size_t)15;
 }
 
-__device__ __forceinline__ XS xs_view(uint8_t *base, int cols)
+__device__ __forceinline__ XS xs_view(const uint8_t *base, int cols)
 {
     XS s;
-    s.xh = reinterpret_cast<const int8_t *>(base);
-    s.xl = reinterpret_cast<const int8_t *>(base + cols);
-    s.xs = reinterpret_cast<const float *>(base + 2 * cols);
-    s.xsum = reinterpret_cast<const int *>(base + 2 * cols + cols / 8);
+    s.hi = base;
+    s.lo = base + cols;
+    s.rec = reinterpret_cast<const int2 *>(base + 2 * cols);
     return s;
 }
 
-// Quantize x[0..cols) into shared memory (all threads of the CTA take part;
-// 8 consecutive lanes own one 32-element block).
-__device__ void quantize_x(const float *__restrict__ x, int cols, uint8_t *base)
+// Quantize x[0..cols) into shared memory (every thread of the CTA takes part;
+// 8 consecutive lanes own one 32-element block, 4 lanes one 16-element slice).
+template <uint32_t FMT>
+__device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t *base)
 {
-    uint32_t *xh = reinterpret_cast<uint32_t *>(base);
-    uint32_t *xl = reinterpret_cast<uint32_t *>(base + cols);
-    float *xs = reinterpret_cast<float *>(base + 2 * cols);
-    int *xsum = reinterpret_cast<int *>(base + 2 * cols + cols / 8);
+    uint8_t *hi = base;
+    uint8_t *lo = base + cols;
+    int2 *rec = reinterpret_cast<int2 *>(base + 2 * cols);
     const int n4 = cols >> 2;
-    const int lane = threadIdx.x & 31;
     constexpr int U = 8;
     for (int it0 = 0; it0 * kThreads < n4; it0 += U) {
         float4 v[U];
@@ -228,23 +259,27 @@ __device__ void quantize_x(const float *__restrict__ x, int cols, uint8_t *base)
                 inv *= 0.5f;
             }
             if (bad) inv = 0.f;
-            int q0 = __float2int_rn(v[u].x * inv), q1 = __float2int_rn(v[u].y * inv);
-            int q2 = __float2int_rn(v[u].z * inv), q3 = __float2int_rn(v[u].w * inv);
-            int h0 = (q0 + 128) >> 8, h1 = (q1 + 128) >> 8, h2 = (q2 + 128) >> 8, h3 = (q3 + 128) >> 8;
-            int l0 = q0 - (h0 << 8), l1 = q1 - (h1 << 8), l2 = q2 - (h2 << 8), l3 = q3 - (h3 << 8);
-            uint32_t hh = (uint32_t)(h0 & 0xff) | ((uint32_t)(h1 & 0xff) << 8) |
-                          ((uint32_t)(h2 & 0xff) << 16) | ((uint32_t)(h3 & 0xff) << 24);
-            uint32_t ll = (uint32_t)(l0 & 0xff) | ((uint32_t)(l1 & 0xff) << 8) |
-                          ((uint32_t)(l2 & 0xff) << 16) | ((uint32_t)(l3 & 0xff) << 24);
+            const int q0 = __float2int_rn(v[u].x * inv), q1 = __float2int_rn(v[u].y * inv);
+            const int q2 = __float2int_rn(v[u].z * inv), q3 = __float2int_rn(v[u].w * inv);
+            const int h0 = (q0 + 128) >> 8, h1 = (q1 + 128) >> 8, h2 = (q2 + 128) >> 8, h3 = (q3 + 128) >> 8;
+            const int l0 = q0 - (h0 << 8), l1 = q1 - (h1 << 8), l2 = q2 - (h2 << 8), l3 = q3 - (h3 << 8);
+            const uint32_t hh = (uint32_t)(h0 & 0xff) | ((uint32_t)(h1 & 0xff) << 8) |
+                                ((uint32_t)(h2 & 0xff) << 16) | ((uint32_t)(h3 & 0xff) << 24);
+            const uint32_t ll = (uint32_t)(l0 & 0xff) | ((uint32_t)(l1 & 0xff) << 8) |
+                                ((uint32_t)(l2 & 0xff) << 16) | ((uint32_t)(l3 & 0xff) << 24);
             int s4 = q0 + q1 + q2 + q3;
             s4 += __shfl_xor_sync(kFull, s4, 1);
             s4 += __shfl_xor_sync(kFull, s4, 2);
             if (f < n4) {
-                xh[f] = hh;
-                xl[f] = ll;
-                if ((lane & 3) == 0) xsum[f >> 2] = s4;
-                if ((lane & 7) == 0)
-                    xs[f >> 3] = bad ? __uint_as_float(0x7fc00000u) : __uint_as_float((uint32_t)(127 + e) << 23);
+                const int p = (4 * f) & ~15;
+                const int si = Slices<FMT>::index(p, C);
+                const int off = (si << 4) + ((4 * f) & 15);
+                *reinterpret_cast<uint32_t *>(hi + off) = hh;
+                *reinterpret_cast<uint32_t *>(lo + off) = ll;
+                if ((f & 3) == 0) {
+                    const float sc = bad ? __uint_as_float(0x7fc00000u) : __uint_as_float((uint32_t)(127 + e) << 23);
+                    rec[si] = make_int2((int)__float_as_uint(sc), s4);
+                }
             }
         }
     }
@@ -252,35 +287,33 @@ __device__ void quantize_x(const float *__restrict__ x, int cols, uint8_t *base)
 
 // ------------------------------------------------- per-format chunk code
 //
-// A "chunk" is the unit one thread handles per row: a whole 32-weight block
-// for Q8_0/Q5_0, 64 weights (two sub-blocks / four 16-element scale groups)
-// for Q4_K/Q6_K.  W<FMT> holds one row's chunk in registers; load() issues the
-// global loads, dot() consumes x from shared memory.
+// W<FMT> holds one row's chunk in registers: load() issues the global loads
+// (each a contiguous run across the lanes of a warp), dot() consumes the
+// matching x slices from shared memory.
 
-template <uint32_t FMT> struct Chunk;
+template <uint32_t FMT> struct W;
 
-template <> struct Chunk<kQ8_0> {
+template <> struct W<kQ8_0> {
     uint4 a, b;
     uint32_t d;
-    static __host__ __device__ int per_row(int cols) { return cols / 32; }
-    __device__ void load(const uint8_t *row, const Layout &L, int c)
+    __device__ __forceinline__ void zero() { a = b = make_uint4(0, 0, 0, 0); d = 0; }
+    __device__ __forceinline__ void load(const uint8_t *row, const Layout &L, int c)
     {
-        a = ld_stream(row + 32 * c);
-        b = ld_stream(row + 32 * c + 16);
-        d = ld_u16(row + L.off_d + 2 * c);
+        a = ld_stream(row + (c << 4));
+        b = ld_stream(row + ((L.C + c) << 4));
+        d = ld_stream16(row + L.off_a + 2 * c);
     }
-    __device__ float dot(const XS &s, int c) const
+    __device__ __forceinline__ float dot(const XS &s, int C, int c) const
     {
-        const uint4 *h = reinterpret_cast<const uint4 *>(s.xh + 32 * c);
-        const uint4 *l = reinterpret_cast<const uint4 *>(s.xl + 32 * c);
-        uint4 h0 = h[0], h1 = h[1], l0 = l[0], l1 = l[1];
+        const uint4 h0 = s.h(0, C, c), h1 = s.h(1, C, c), l0 = s.l(0, C, c), l1 = s.l(1, C, c);
         int ah = dp4a(a.x, h0.x, 0);
         ah = dp4a(a.y, h0.y, ah); ah = dp4a(a.z, h0.z, ah); ah = dp4a(a.w, h0.w, ah);
         ah = dp4a(b.x, h1.x, ah); ah = dp4a(b.y, h1.y, ah); ah = dp4a(b.z, h1.z, ah); ah = dp4a(b.w, h1.w, ah);
         int al = dp4a(a.x, l0.x, 0);
         al = dp4a(a.y, l0.y, al); al = dp4a(a.z, l0.z, al); al = dp4a(a.w, l0.w, al);
         al = dp4a(b.x, l1.x, al); al = dp4a(b.y, l1.y, al); al = dp4a(b.z, l1.z, al); al = dp4a(b.w, l1.w, al);
-        return (f16_fast(d) * s.xs[c]) * (float)(ah * 256 + al);
+        const float sx = __int_as_float(s.r(0, C, c).x);
+        return (f16_fast(d) * sx) * (float)(ah * 256 + al);
     }
 };
 
@@ -290,75 +323,71 @@ __device__ __forceinline__ uint32_t spread4(uint32_t v)
     return ((v & 0xfu) * 0x02040810u) & 0x10101010u;
 }
 
-template <> struct Chunk<kQ5_0> {
+template <> struct W<kQ5_0> {
     uint4 q;
     uint32_t qh, d;
-    static __host__ __device__ int per_row(int cols) { return cols / 32; }
-    __device__ void load(const uint8_t *row, const Layout &L, int c)
+    __device__ __forceinline__ void zero() { q = make_uint4(0, 0, 0, 0); qh = d = 0; }
+    __device__ __forceinline__ void load(const uint8_t *row, const Layout &L, int c)
     {
-        q = ld_stream(row + 16 * c);
-        qh = ld_u32(row + L.off_qh + 4 * c);
-        d = ld_u16(row + L.off_d + 2 * c);
+        q = ld_stream(row + (c << 4));
+        qh = ld_stream32(row + L.off_a + 4 * c);
+        d = ld_stream16(row + L.off_b + 2 * c);
     }
-    __device__ float dot(const XS &s, int c) const
+    __device__ __forceinline__ float dot(const XS &s, int C, int c) const
     {
-        const uint4 *h = reinterpret_cast<const uint4 *>(s.xh + 32 * c);
-        const uint4 *l = reinterpret_cast<const uint4 *>(s.xl + 32 * c);
-        uint4 h0 = h[0], h1 = h[1], l0 = l[0], l1 = l[1];
+        const uint4 h0 = s.h(0, C, c), h1 = s.h(1, C, c), l0 = s.l(0, C, c), l1 = s.l(1, C, c);
         const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-        const uint32_t xh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-        const uint32_t xl[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+        const uint32_t xh0[4] = {h0.x, h0.y, h0.z, h0.w}, xh1[4] = {h1.x, h1.y, h1.z, h1.w};
+        const uint32_t xl0[4] = {l0.x, l0.y, l0.z, l0.w}, xl1[4] = {l1.x, l1.y, l1.z, l1.w};
         int ah = 0, al = 0;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            // weights 4k..4k+3: low nibbles; weights 16+4k..: high nibbles
-            uint32_t lo = (w[k] & 0x0f0f0f0fu) | spread4(qh >> (4 * k));
-            uint32_t hi = ((w[k] >> 4) & 0x0f0f0f0fu) | spread4(qh >> (16 + 4 * k));
-            ah = dp4a(lo, xh[k], ah);
-            al = dp4a(lo, xl[k], al);
-            ah = dp4a(hi, xh[4 + k], ah);
-            al = dp4a(hi, xl[4 + k], al);
+            // weights 4k..4k+3 from low nibbles, 16+4k.. from high nibbles;
+            // the fifth bit of weight i is bit i of qh
+            const uint32_t lw = (w[k] & 0x0f0f0f0fu) | spread4(qh >> (4 * k));
+            const uint32_t hw = ((w[k] >> 4) & 0x0f0f0f0fu) | spread4(qh >> (16 + 4 * k));
+            ah = dp4a(lw, xh0[k], ah);
+            al = dp4a(lw, xl0[k], al);
+            ah = dp4a(hw, xh1[k], ah);
+            al = dp4a(hw, xl1[k], al);
         }
-        const int sx = s.xsum[2 * c] + s.xsum[2 * c + 1];
-        return (f16_fast(d) * s.xs[c]) * (float)(ah * 256 + al - 16 * sx);
+        const int2 r0 = s.r(0, C, c), r1 = s.r(1, C, c);
+        return (f16_fast(d) * __int_as_float(r0.x)) * (float)(ah * 256 + al - 16 * (r0.y + r1.y));
     }
 };
 
-template <> struct Chunk<kQ4_K> {
-    uint4 hdr, a, b;
-    static __host__ __device__ int per_row(int cols) { return cols / 64; }
-    __device__ void load(const uint8_t *row, const Layout &, int c)
+template <> struct W<kQ4_K> {
+    uint4 a, b, hdr;
+    __device__ __forceinline__ void zero() { a = b = hdr = make_uint4(0, 0, 0, 0); }
+    __device__ __forceinline__ void load(const uint8_t *row, const Layout &L, int c)
     {
-        const uint8_t *blk = row + 144 * (c >> 2);
-        hdr = ld_stream(blk);
-        a = ld_stream(blk + 16 + 32 * (c & 3));
-        b = ld_stream(blk + 32 + 32 * (c & 3));
+        a = ld_stream(row + (c << 4));
+        b = ld_stream(row + ((L.C + c) << 4));
+        hdr = ld_stream(row + L.off_a + ((c >> 2) << 4));
     }
-    __device__ float dot(const XS &s, int c) const
+    __device__ __forceinline__ float dot(const XS &s, int C, int c) const
     {
-        const int g = c & 3;
-        const uint4 *h = reinterpret_cast<const uint4 *>(s.xh + 64 * c);
-        const uint4 *l = reinterpret_cast<const uint4 *>(s.xl + 64 * c);
-        const uint32_t q[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        // slice 0/1: low nibbles of pieces a/b (sub-block 2g);
+        // slice 2/3: high nibbles (sub-block 2g+1)
+        const uint4 x0 = s.h(0, C, c), x1 = s.h(1, C, c), x2 = s.h(2, C, c), x3 = s.h(3, C, c);
+        const uint4 y0 = s.l(0, C, c), y1 = s.l(1, C, c), y2 = s.l(2, C, c), y3 = s.l(3, C, c);
+        const uint32_t pa[4] = {a.x, a.y, a.z, a.w}, pb[4] = {b.x, b.y, b.z, b.w};
+        const uint32_t h0[4] = {x0.x, x0.y, x0.z, x0.w}, h1[4] = {x1.x, x1.y, x1.z, x1.w};
+        const uint32_t h2[4] = {x2.x, x2.y, x2.z, x2.w}, h3[4] = {x3.x, x3.y, x3.z, x3.w};
+        const uint32_t l0[4] = {y0.x, y0.y, y0.z, y0.w}, l1[4] = {y1.x, y1.y, y1.z, y1.w};
+        const uint32_t l2[4] = {y2.x, y2.y, y2.z, y2.w}, l3[4] = {y3.x, y3.y, y3.z, y3.w};
         int ah0 = 0, al0 = 0, ah1 = 0, al1 = 0;
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            uint4 xh0 = h[k], xl0 = l[k], xh1 = h[2 + k], xl1 = l[2 + k];
-            const uint32_t xa[4] = {xh0.x, xh0.y, xh0.z, xh0.w};
-            const uint32_t xb[4] = {xl0.x, xl0.y, xl0.z, xl0.w};
-            const uint32_t xc[4] = {xh1.x, xh1.y, xh1.z, xh1.w};
-            const uint32_t xd[4] = {xl1.x, xl1.y, xl1.z, xl1.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                uint32_t lo = q[4 * k + j] & 0x0f0f0f0fu;         // sub-block 2g
-                uint32_t hi = (q[4 * k + j] >> 4) & 0x0f0f0f0fu;  // sub-block 2g+1
-                ah0 = dp4a(lo, xa[j], ah0);
-                al0 = dp4a(lo, xb[j], al0);
-                ah1 = dp4a(hi, xc[j], ah1);
-                al1 = dp4a(hi, xd[j], al1);
-            }
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t la = pa[k] & 0x0f0f0f0fu, lb = pb[k] & 0x0f0f0f0fu;
+            const uint32_t ua = (pa[k] >> 4) & 0x0f0f0f0fu, ub = (pb[k] >> 4) & 0x0f0f0f0fu;
+            ah0 = dp4a(la, h0[k], ah0); al0 = dp4a(la, l0[k], al0);
+            ah0 = dp4a(lb, h1[k], ah0); al0 = dp4a(lb, l1[k], al0);
+            ah1 = dp4a(ua, h2[k], ah1); al1 = dp4a(ua, l2[k], al1);
+            ah1 = dp4a(ub, h3[k], ah1); al1 = dp4a(ub, l3[k], al1);
         }
         // 6-bit scale / min of sub-blocks 2g and 2g+1 (src/quantization.cpp:351-378)
+        const int g = c & 3;
         const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
         uint32_t sc0, m0, sc1, m1;
         if (g < 2) {
@@ -367,68 +396,55 @@ template <> struct Chunk<kQ4_K> {
             sc1 = (s0 >> t1) & 63u; m1 = (s1 >> t1) & 63u;
         } else {
             const int t0 = 16 * (g - 2), t1 = t0 + 8;
-            sc0 = ((s2 >> t0) & 15u) | (((s0 >> t0) >> 6 & 3u) << 4);
-            m0 = ((s2 >> t0) >> 4 & 15u) | (((s1 >> t0) >> 6 & 3u) << 4);
-            sc1 = ((s2 >> t1) & 15u) | (((s0 >> t1) >> 6 & 3u) << 4);
-            m1 = ((s2 >> t1) >> 4 & 15u) | (((s1 >> t1) >> 6 & 3u) << 4);
+            sc0 = ((s2 >> t0) & 15u) | ((((s0 >> t0) >> 6) & 3u) << 4);
+            m0 = (((s2 >> t0) >> 4) & 15u) | ((((s1 >> t0) >> 6) & 3u) << 4);
+            sc1 = ((s2 >> t1) & 15u) | ((((s0 >> t1) >> 6) & 3u) << 4);
+            m1 = (((s2 >> t1) >> 4) & 15u) | ((((s1 >> t1) >> 6) & 3u) << 4);
         }
         const float d = f16_fast(hdr.x), dmin = f16_fast(hdr.x >> 16);
-        const int j0 = 2 * c;  // 32-element x block of sub-block 2g
-        const int S0 = s.xsum[2 * j0] + s.xsum[2 * j0 + 1];
-        const int S1 = s.xsum[2 * j0 + 2] + s.xsum[2 * j0 + 3];
-        const float v0 = (d * (float)sc0) * (float)(ah0 * 256 + al0) - (dmin * (float)m0) * (float)S0;
-        const float v1 = (d * (float)sc1) * (float)(ah1 * 256 + al1) - (dmin * (float)m1) * (float)S1;
-        return s.xs[j0] * v0 + s.xs[j0 + 1] * v1;
+        const int2 r0 = s.r(0, C, c), r1 = s.r(1, C, c), r2 = s.r(2, C, c), r3 = s.r(3, C, c);
+        const float v0 = (d * (float)sc0) * (float)(ah0 * 256 + al0) - (dmin * (float)m0) * (float)(r0.y + r1.y);
+        const float v1 = (d * (float)sc1) * (float)(ah1 * 256 + al1) - (dmin * (float)m1) * (float)(r2.y + r3.y);
+        return __int_as_float(r0.x) * v0 + __int_as_float(r2.x) * v1;
     }
 };
 
-template <> struct Chunk<kQ6_K> {
-    uint4 l0, l1, qh;
-    uint2 sc;
-    uint32_t d;
-    static __host__ __device__ int per_row(int cols) { return cols / 64; }
-    __device__ void load(const uint8_t *row, const Layout &L, int c)
+template <> struct W<kQ6_K> {
+    uint4 a, b, u;
+    uint32_t sc, d;
+    __device__ __forceinline__ void zero() { a = b = u = make_uint4(0, 0, 0, 0); sc = d = 0; }
+    __device__ __forceinline__ void load(const uint8_t *row, const Layout &L, int c)
     {
-        const int sb = c >> 2, g = (c >> 1) & 1, h = c & 1;
-        const uint8_t *blk = row + 208 * sb;
-        l0 = ld_stream(blk + 64 * g + 16 * h);
-        l1 = ld_stream(blk + 64 * g + 32 + 16 * h);
-        qh = ld_stream(blk + 128 + 32 * g + 16 * h);
-        sc = ld_stream8(blk + 192 + 8 * g);
-        d = ld_u16(row + L.off_d + 2 * sb);
+        a = ld_stream(row + (c << 4));
+        b = ld_stream(row + ((L.C + c) << 4));
+        u = ld_stream(row + ((2 * L.C + c) << 4));
+        sc = ld_stream32(row + L.off_a + 4 * c);
+        d = ld_stream16(row + L.off_b + 2 * (c >> 2));
     }
-    __device__ float dot(const XS &s, int c) const
+    __device__ __forceinline__ float dot(const XS &s, int C, int c) const
     {
-        // positions of region r: 128*(c>>1) + 16*(c&1) + 32*r
-        const int base = 128 * (c >> 1) + 16 * (c & 1);
-        const int h = c & 1;
-        const uint32_t a[4] = {l0.x, l0.y, l0.z, l0.w};
-        const uint32_t b[4] = {l1.x, l1.y, l1.z, l1.w};
-        const uint32_t u[4] = {qh.x, qh.y, qh.z, qh.w};
+        const uint32_t pa[4] = {a.x, a.y, a.z, a.w}, pb[4] = {b.x, b.y, b.z, b.w};
+        const uint32_t pu[4] = {u.x, u.y, u.z, u.w};
         float acc = 0.f;
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-            const uint4 xh4 = *reinterpret_cast<const uint4 *>(s.xh + base + 32 * r);
-            const uint4 xl4 = *reinterpret_cast<const uint4 *>(s.xl + base + 32 * r);
-            const uint32_t xa[4] = {xh4.x, xh4.y, xh4.z, xh4.w};
-            const uint32_t xb[4] = {xl4.x, xl4.y, xl4.z, xl4.w};
+            const uint4 xh4 = s.h(r, C, c), xl4 = s.l(r, C, c);
+            const uint32_t xh[4] = {xh4.x, xh4.y, xh4.z, xh4.w};
+            const uint32_t xl[4] = {xl4.x, xl4.y, xl4.z, xl4.w};
             int ah = 0, al = 0;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                uint32_t lowbits, highbits;
-                if (r == 0) { lowbits = a[k] & 0x0f0f0f0fu; highbits = (u[k] << 4) & 0x30303030u; }
-                else if (r == 1) { lowbits = b[k] & 0x0f0f0f0fu; highbits = (u[k] << 2) & 0x30303030u; }
-                else if (r == 2) { lowbits = (a[k] >> 4) & 0x0f0f0f0fu; highbits = u[k] & 0x30303030u; }
-                else { lowbits = (b[k] >> 4) & 0x0f0f0f0fu; highbits = (u[k] >> 2) & 0x30303030u; }
-                const uint32_t w = lowbits | highbits;  // 6-bit values 0..63
-                ah = dp4a(w, xa[k], ah);
-                al = dp4a(w, xb[k], al);
+                uint32_t w;  // 6-bit values 0..63 (src/quantization.cpp:559-586)
+                if (r == 0) w = (pa[k] & 0x0f0f0f0fu) | ((pu[k] << 4) & 0x30303030u);
+                else if (r == 1) w = (pb[k] & 0x0f0f0f0fu) | ((pu[k] << 2) & 0x30303030u);
+                else if (r == 2) w = ((pa[k] >> 4) & 0x0f0f0f0fu) | (pu[k] & 0x30303030u);
+                else w = ((pb[k] >> 4) & 0x0f0f0f0fu) | ((pu[k] >> 2) & 0x30303030u);
+                ah = dp4a(w, xh[k], ah);
+                al = dp4a(w, xl[k], al);
             }
-            const int S = s.xsum[(base >> 4) + 2 * r];
-            // int8 scale sc[8g + 2r + h]: byte (2r + h) of the loaded 8 bytes
-            const uint32_t sw = (r < 2) ? sc.x : sc.y;
-            const int scale = (int)(int8_t)((sw >> (8 * ((2 * r + h) & 3))) & 0xffu);
-            acc += ((float)scale * s.xs[(base >> 5) + r]) * (float)(ah * 256 + al - 32 * S);
+            const int2 rr = s.r(r, C, c);
+            const int scale = (int)(int8_t)((sc >> (8 * r)) & 0xffu);
+            acc += ((float)scale * __int_as_float(rr.x)) * (float)(ah * 256 + al - 32 * rr.y);
         }
         return f16_fast(d) * acc;
     }
@@ -436,13 +452,14 @@ template <> struct Chunk<kQ6_K> {
 
 // ---------------------------------------------------------------- GEMV
 //
-// Persistent CTAs, each owning a contiguous range of rows [r0, r1).  Inside
-// a CTA, groups of TPT threads each take R consecutive rows per pass; the
-// TPT threads of a group stride over the row's chunks, so the x chunk in
-// registers serves R rows.  Reductions are shuffle trees in a fixed order,
-// so results are deterministic.
-
-template <int R> struct RowAcc { float v[R]; };
+// Persistent grid.  A warp owns whole row tiles: TPT lanes (16 or 32) per
+// group, 32/TPT groups per warp, R rows per group, so a warp tile is
+// (32/TPT)*R consecutive rows.  Warp tiles are dealt round-robin over every
+// warp of the grid.  Within a tile the group's lanes stride over the chunks
+// of its rows; one x slice set from shared memory serves R rows.  The next
+// item's weights are loaded before the current item is computed (one-deep
+// register prefetch), and the only synchronisation is a shuffle reduction in
+// a fixed order, so results are deterministic.
 
 template <uint32_t FMT, int TPT, int R>
 __global__ void __launch_bounds__(kThreads)
@@ -450,67 +467,74 @@ gemv_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x
             float *__restrict__ y, ArgmaxOut am, int want_argmax)
 {
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ float red[kThreads / 32][R];
     __shared__ unsigned long long kscratch[kThreads / 32];
 
-    const int cols = L.cols;
-    quantize_x(x, cols, smem);
+    const int C = L.C;
+    quantize_x<FMT>(x, L.cols, C, smem);
     __syncthreads();
-    const XS s = xs_view(smem, cols);
+    const XS s = xs_view(smem, L.cols);
 
-    const int r0 = (int)((long long)L.rows * blockIdx.x / gridDim.x);
-    const int r1 = (int)((long long)L.rows * (blockIdx.x + 1) / gridDim.x);
-    constexpr int NG = kThreads / TPT;
-    const int group = threadIdx.x / TPT, gl = threadIdx.x % TPT;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int C = Chunk<FMT>::per_row(cols);
-    const int passes = (r1 - r0 + NG * R - 1) / (NG * R);
+    constexpr int GPW = 32 / TPT;
+    constexpr int WR = GPW * R;
+    const int lane = threadIdx.x & 31;
+    const int grp = lane / TPT, gl = lane % TPT;
+    const int wg = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+    const int wtot = gridDim.x * (kThreads / 32);
+    const int NI = (C + TPT - 1) / TPT;
+    const int tiles = (L.rows + WR - 1) / WR;
+    const int my_tiles = wg < tiles ? (tiles - 1 - wg) / wtot + 1 : 0;
+    const int n_items = my_tiles * NI;
+
     unsigned long long best = 0ull;
+    W<FMT> cur[R], nxt[R];
+    float acc[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) acc[i] = 0.f;
 
-    for (int ps = 0; ps < passes; ++ps) {
-        const int row0 = r0 + (ps * NG + group) * R;
-        float acc[R];
-#pragma unroll
-        for (int i = 0; i < R; ++i) acc[i] = 0.f;
-        for (int c = gl; c < C; c += TPT) {
-            Chunk<FMT> ch[R];
-#pragma unroll
-            for (int i = 0; i < R; ++i)
-                if (row0 + i < r1) ch[i].load(w + (uint64_t)(row0 + i) * L.row_stride, L, c);
-#pragma unroll
-            for (int i = 0; i < R; ++i)
-                if (row0 + i < r1) acc[i] += ch[i].dot(s, c);
-        }
-        constexpr int WL = TPT < 32 ? TPT : 32;
+    auto load_item = [&](int k, W<FMT> (&dst)[R]) {
+        const int t = wg + (k / NI) * wtot;
+        const int c = (k % NI) * TPT + gl;
+        const int row0 = t * WR + grp * R;
 #pragma unroll
         for (int i = 0; i < R; ++i) {
-#pragma unroll
-            for (int o = WL / 2; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(kFull, acc[i], o);
+            if (c < C && row0 + i < L.rows)
+                dst[i].load(w + (uint64_t)(row0 + i) * L.row_stride, L, c);
+            else
+                dst[i].zero();
         }
-        float out = 0.f;
-        if constexpr (TPT > 32) {
-            if (lane == 0) {
+    };
+
+    if (n_items > 0) load_item(0, cur);
+    for (int k = 0; k < n_items; ++k) {
+        if (k + 1 < n_items) load_item(k + 1, nxt);
+        const int it = k % NI;
+        const int t = wg + (k / NI) * wtot;
+        const int c = it * TPT + gl;
+        const int row0 = t * WR + grp * R;
+        if (c < C) {
 #pragma unroll
-                for (int i = 0; i < R; ++i) red[warp][i] = acc[i];
+            for (int i = 0; i < R; ++i)
+                if (row0 + i < L.rows) acc[i] += cur[i].dot(s, C, c);
+        }
+        if (it == NI - 1) {
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+#pragma unroll
+                for (int o = TPT / 2; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(kFull, acc[i], o);
             }
-            __syncthreads();
-            if (gl < R) {
-                constexpr int WPG = TPT / 32;
-                for (int k = 0; k < WPG; ++k) out += red[group * WPG + k][gl];
-            }
-            __syncthreads();
-        } else {
+            float out = 0.f;
 #pragma unroll
             for (int i = 0; i < R; ++i)
                 if (gl == i) out = acc[i];
-        }
-        if (gl < R) {
-            const int row = row0 + gl;
-            if (row < r1) {
-                y[row] = out;
-                if (want_argmax) best = max_ull(best, make_key(out, am.index_base + row));
+            if (gl < R && row0 + gl < L.rows) {
+                y[row0 + gl] = out;
+                if (want_argmax) best = max_ull(best, make_key(out, am.index_base + row0 + gl));
             }
+#pragma unroll
+            for (int i = 0; i < R; ++i) acc[i] = 0.f;
         }
+#pragma unroll
+        for (int i = 0; i < R; ++i) cur[i] = nxt[i];
     }
     if (want_argmax) {
         best = block_max_key(best, kscratch);
@@ -520,8 +544,9 @@ gemv_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x
 
 // ------------------------------------------------------------- matmul
 //
-// Batched form: NP <= 8 positions share every weight chunk load.  x of all
-// positions is quantized into shared memory first.
+// Batched form for up to NP positions per launch: x of every position is
+// quantized into shared memory first, then each group of TPT lanes takes one
+// row at a time and applies every loaded weight chunk to all positions.
 
 template <uint32_t FMT, int TPT, int NP>
 __global__ void __launch_bounds__(kThreads)
@@ -529,59 +554,43 @@ matmul_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__
               float *__restrict__ Y)
 {
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ float red[kThreads / 32][NP];
-    const int cols = L.cols;
-    const size_t xb = xs_bytes(cols);
-    for (int p = 0; p < np; ++p) quantize_x(X + (size_t)p * cols, cols, smem + p * xb);
+    const int C = L.C;
+    const size_t xb = xs_bytes(L.cols);
+    for (int p = 0; p < np; ++p) quantize_x<FMT>(X + (size_t)p * L.cols, L.cols, C, smem + p * xb);
     __syncthreads();
 
-    const int r0 = (int)((long long)L.rows * blockIdx.x / gridDim.x);
-    const int r1 = (int)((long long)L.rows * (blockIdx.x + 1) / gridDim.x);
-    constexpr int NG = kThreads / TPT;
-    const int group = threadIdx.x / TPT, gl = threadIdx.x % TPT;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int C = Chunk<FMT>::per_row(cols);
-    const int passes = (r1 - r0 + NG - 1) / NG;
+    constexpr int GPW = 32 / TPT;
+    const int lane = threadIdx.x & 31;
+    const int grp = lane / TPT, gl = lane % TPT;
+    const int wg = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+    const int wtot = gridDim.x * (kThreads / 32);
+    const int tiles = (L.rows + GPW - 1) / GPW;
 
-    for (int ps = 0; ps < passes; ++ps) {
-        const int row = r0 + ps * NG + group;
+    for (int t = wg; t < tiles; t += wtot) {
+        const int row = t * GPW + grp;
         float acc[NP];
 #pragma unroll
         for (int p = 0; p < NP; ++p) acc[p] = 0.f;
-        if (row < r1) {
+        if (row < L.rows) {
             const uint8_t *rp = w + (uint64_t)row * L.row_stride;
             for (int c = gl; c < C; c += TPT) {
-                Chunk<FMT> ch;
+                W<FMT> ch;
                 ch.load(rp, L, c);
 #pragma unroll
                 for (int p = 0; p < NP; ++p)
-                    if (p < np) acc[p] += ch.dot(xs_view(smem + p * xb, cols), c);
+                    if (p < np) acc[p] += ch.dot(xs_view(smem + p * xb, L.cols), C, c);
             }
         }
-        constexpr int WL = TPT < 32 ? TPT : 32;
 #pragma unroll
         for (int p = 0; p < NP; ++p) {
 #pragma unroll
-            for (int o = WL / 2; o > 0; o >>= 1) acc[p] += __shfl_xor_sync(kFull, acc[p], o);
+            for (int o = TPT / 2; o > 0; o >>= 1) acc[p] += __shfl_xor_sync(kFull, acc[p], o);
         }
         float out = 0.f;
-        if constexpr (TPT > 32) {
-            if (lane == 0) {
 #pragma unroll
-                for (int p = 0; p < NP; ++p) red[warp][p] = acc[p];
-            }
-            __syncthreads();
-            if (gl < np) {
-                constexpr int WPG = TPT / 32;
-                for (int k = 0; k < WPG; ++k) out += red[group * WPG + k][gl];
-            }
-            __syncthreads();
-        } else {
-#pragma unroll
-            for (int p = 0; p < NP; ++p)
-                if (gl == p) out = acc[p];
-        }
-        if (gl < np && row < r1) Y[(size_t)gl * L.rows + row] = out;
+        for (int p = 0; p < NP; ++p)
+            if (gl == p) out = acc[p];
+        if (gl < np && row < L.rows) Y[(size_t)gl * L.rows + row] = out;
     }
 }
 
@@ -600,46 +609,105 @@ argmax_kernel(const float *__restrict__ logits, int n, ArgmaxOut am)
 
 // ----------------------------------------------------- repack / dequant
 
+__device__ __forceinline__ void copy16(uint8_t *dst, const uint8_t *src)
+{
+    for (int k = 0; k < 16; ++k) dst[k] = src[k];
+}
+
+// One thread per (row, chunk): move the chunk's bytes from its raw GGUF
+// block(s) to their chunk-major places.
 __global__ void repack_kernel(Layout L, const uint8_t *__restrict__ raw, uint8_t *__restrict__ dst)
 {
-    const uint64_t nblocks = (uint64_t)L.rows * L.nb;
+    const uint64_t total = (uint64_t)L.rows * L.C;
     const int bb = (L.type == kQ8_0) ? 34 : (L.type == kQ5_0) ? 22 : (L.type == kQ4_K) ? 144 : 210;
-    for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nblocks;
-         b += (uint64_t)gridDim.x * blockDim.x) {
-        const uint64_t row = b / L.nb;
-        const int j = (int)(b % L.nb);
-        const uint8_t *src = raw + b * bb;
+    const int C = L.C;
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
+         e += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t row = e / C;
+        const int c = (int)(e % C);
+        const uint8_t *src = raw + row * (uint64_t)L.nb * bb;
         uint8_t *r = dst + row * L.row_stride;
         switch (L.type) {
-        case kQ8_0:
-            r[L.off_d + 2 * j] = src[0];
-            r[L.off_d + 2 * j + 1] = src[1];
-            for (int k = 0; k < 32; ++k) r[32 * j + k] = src[2 + k];
+        case kQ8_0: {
+            const uint8_t *blk = src + (uint64_t)c * 34;
+            copy16(r + (c << 4), blk + 2);
+            copy16(r + ((C + c) << 4), blk + 18);
+            r[L.off_a + 2 * c] = blk[0];
+            r[L.off_a + 2 * c + 1] = blk[1];
             break;
-        case kQ5_0:
-            r[L.off_d + 2 * j] = src[0];
-            r[L.off_d + 2 * j + 1] = src[1];
-            for (int k = 0; k < 4; ++k) r[L.off_qh + 4 * j + k] = src[2 + k];
-            for (int k = 0; k < 16; ++k) r[16 * j + k] = src[6 + k];
+        }
+        case kQ5_0: {
+            const uint8_t *blk = src + (uint64_t)c * 22;
+            copy16(r + (c << 4), blk + 6);
+            for (int k = 0; k < 4; ++k) r[L.off_a + 4 * c + k] = blk[2 + k];
+            r[L.off_b + 2 * c] = blk[0];
+            r[L.off_b + 2 * c + 1] = blk[1];
             break;
-        case kQ4_K:
-            for (int k = 0; k < 144; ++k) r[144 * j + k] = src[k];
+        }
+        case kQ4_K: {
+            const int sb = c >> 2, g = c & 3;
+            const uint8_t *blk = src + (uint64_t)sb * 144;
+            copy16(r + (c << 4), blk + 16 + 32 * g);
+            copy16(r + ((C + c) << 4), blk + 32 + 32 * g);
+            if (g == 0) copy16(r + L.off_a + (sb << 4), blk);
             break;
-        default:
-            for (int k = 0; k < 208; ++k) r[208 * j + k] = src[k];
-            r[L.off_d + 2 * j] = src[208];
-            r[L.off_d + 2 * j + 1] = src[209];
+        }
+        default: {
+            const int sb = c >> 2, g = (c >> 1) & 1, h = c & 1;
+            const uint8_t *blk = src + (uint64_t)sb * 210;
+            copy16(r + (c << 4), blk + 64 * g + 16 * h);
+            copy16(r + ((C + c) << 4), blk + 64 * g + 32 + 16 * h);
+            copy16(r + ((2 * C + c) << 4), blk + 128 + 32 * g + 16 * h);
+            for (int q = 0; q < 4; ++q) r[L.off_a + 4 * c + q] = blk[192 + 8 * g + 2 * q + h];
+            if ((c & 3) == 0) {
+                r[L.off_b + 2 * sb] = blk[208];
+                r[L.off_b + 2 * sb + 1] = blk[209];
+            }
             break;
+        }
         }
     }
 }
 
-// Pointers to the fields of one block, wherever they live.
-struct BlockRef {
-    uint32_t d16;        // Q8_0/Q5_0/Q6_K scale bits
-    const uint8_t *p;    // Q8_0 qs / Q5_0 qs / Q4_K whole block / Q6_K payload
-    const uint8_t *qh;   // Q5_0 high bits
-};
+// Rebuild the raw GGUF bytes of block b of a resident row (inverse of repack).
+__device__ void gather_raw_block(const Layout &L, const uint8_t *r, int b, uint8_t *out)
+{
+    const int C = L.C;
+    switch (L.type) {
+    case kQ8_0:
+        out[0] = r[L.off_a + 2 * b];
+        out[1] = r[L.off_a + 2 * b + 1];
+        copy16(out + 2, r + (b << 4));
+        copy16(out + 18, r + ((C + b) << 4));
+        break;
+    case kQ5_0:
+        out[0] = r[L.off_b + 2 * b];
+        out[1] = r[L.off_b + 2 * b + 1];
+        for (int k = 0; k < 4; ++k) out[2 + k] = r[L.off_a + 4 * b + k];
+        copy16(out + 6, r + (b << 4));
+        break;
+    case kQ4_K:
+        copy16(out, r + L.off_a + (b << 4));
+        for (int g = 0; g < 4; ++g) {
+            copy16(out + 16 + 32 * g, r + ((4 * b + g) << 4));
+            copy16(out + 32 + 32 * g, r + ((C + 4 * b + g) << 4));
+        }
+        break;
+    default:
+        for (int g = 0; g < 2; ++g) {
+            for (int h = 0; h < 2; ++h) {
+                const int c = 4 * b + 2 * g + h;
+                copy16(out + 64 * g + 16 * h, r + (c << 4));
+                copy16(out + 64 * g + 32 + 16 * h, r + ((C + c) << 4));
+                copy16(out + 128 + 32 * g + 16 * h, r + ((2 * C + c) << 4));
+                for (int q = 0; q < 4; ++q) out[192 + 8 * g + 2 * q + h] = r[L.off_a + 4 * c + q];
+            }
+        }
+        out[208] = r[L.off_b + 2 * b];
+        out[209] = r[L.off_b + 2 * b + 1];
+        break;
+    }
+}
 
 // The reference's scalar build runs on x86 SSE, where a NaN result carries
 // the payload of the first NaN operand (quieted) and an invalid operation on
@@ -665,18 +733,21 @@ __device__ __forceinline__ float sub_ref(float a, float b)
     return isnan(r) ? x86_nan(a, b) : r;
 }
 
-// Value i of a block, with the reference's rounding sequence (no FMA).
+__device__ __forceinline__ uint32_t rd16(const uint8_t *p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8); }
+
+// Value i of a raw GGUF block, with the reference's rounding sequence.
 template <uint32_t FMT>
-__device__ __forceinline__ float dequant_value(const BlockRef &b, int i)
+__device__ __forceinline__ float dequant_value(const uint8_t *blk, int i)
 {
     if constexpr (FMT == kQ8_0) {
-        return mul_ref(f16_exact(b.d16), (float)(int8_t)b.p[i]);
+        return mul_ref(f16_exact(rd16(blk)), (float)(int8_t)blk[2 + i]);
     } else if constexpr (FMT == kQ5_0) {
-        const int nib = i < 16 ? (b.p[i] & 0x0f) : (b.p[i - 16] >> 4);
-        const int hi = (b.qh[i >> 3] >> (i & 7)) & 1;
-        return mul_ref(f16_exact(b.d16), (float)((nib | (hi << 4)) - 16));
+        const uint8_t *qh = blk + 2, *qs = blk + 6;
+        const int nib = i < 16 ? (qs[i] & 0x0f) : (qs[i - 16] >> 4);
+        const int hi = (qh[i >> 3] >> (i & 7)) & 1;
+        return mul_ref(f16_exact(rd16(blk)), (float)((nib | (hi << 4)) - 16));
     } else if constexpr (FMT == kQ4_K) {
-        const uint8_t *sm = b.p + 4;
+        const uint8_t *sm = blk + 4;
         const int j = i >> 5, o = i & 31;
         int sc, mn;
         if (j < 4) {
@@ -686,92 +757,51 @@ __device__ __forceinline__ float dequant_value(const BlockRef &b, int i)
             sc = (sm[j + 4] & 0x0f) | ((sm[j - 4] >> 6) << 4);
             mn = (sm[j + 4] >> 4) | ((sm[j] >> 6) << 4);
         }
-        const float d = f16_exact((uint32_t)b.p[0] | ((uint32_t)b.p[1] << 8));
-        const float dmin = f16_exact((uint32_t)b.p[2] | ((uint32_t)b.p[3] << 8));
-        const float scale = mul_ref(d, (float)sc);
-        const float minimum = mul_ref(dmin, (float)mn);
-        const int nib = (b.p[16 + 32 * (j >> 1) + o] >> (4 * (j & 1))) & 0x0f;
+        const float scale = mul_ref(f16_exact(rd16(blk)), (float)sc);
+        const float minimum = mul_ref(f16_exact(rd16(blk + 2)), (float)mn);
+        const int nib = (blk[16 + 32 * (j >> 1) + o] >> (4 * (j & 1))) & 0x0f;
         return sub_ref(mul_ref(scale, (float)nib), minimum);
     } else {
         const int g = i >> 7, loc = i & 127, r = loc >> 5, o = loc & 31;
-        const int lo = (b.p[64 * g + 32 * (r & 1) + o] >> (4 * (r >> 1))) & 0x0f;
-        const int hi = (b.p[128 + 32 * g + o] >> (2 * r)) & 0x03;
+        const int lo = (blk[64 * g + 32 * (r & 1) + o] >> (4 * (r >> 1))) & 0x0f;
+        const int hi = (blk[128 + 32 * g + o] >> (2 * r)) & 0x03;
         const int q = (lo | (hi << 4)) - 32;
-        const int sc = (int8_t)b.p[192 + 8 * g + 2 * r + (o >> 4)];
-        return mul_ref(mul_ref(f16_exact(b.d16), (float)sc), (float)q);
+        const int sc = (int8_t)blk[192 + 8 * g + 2 * r + (o >> 4)];
+        return mul_ref(mul_ref(f16_exact(rd16(blk + 208)), (float)sc), (float)q);
     }
 }
 
-template <uint32_t FMT>
-__device__ __forceinline__ BlockRef ref_layout(const Layout &L, const uint8_t *w, uint64_t row, int j)
-{
-    const uint8_t *r = w + row * L.row_stride;
-    BlockRef b;
-    b.qh = nullptr;
-    b.d16 = 0;
-    if constexpr (FMT == kQ8_0) {
-        b.p = r + 32 * j;
-        b.d16 = (uint32_t)r[L.off_d + 2 * j] | ((uint32_t)r[L.off_d + 2 * j + 1] << 8);
-    } else if constexpr (FMT == kQ5_0) {
-        b.p = r + 16 * j;
-        b.qh = r + L.off_qh + 4 * j;
-        b.d16 = (uint32_t)r[L.off_d + 2 * j] | ((uint32_t)r[L.off_d + 2 * j + 1] << 8);
-    } else if constexpr (FMT == kQ4_K) {
-        b.p = r + 144 * j;
-    } else {
-        b.p = r + 208 * j;
-        b.d16 = (uint32_t)r[L.off_d + 2 * j] | ((uint32_t)r[L.off_d + 2 * j + 1] << 8);
-    }
-    return b;
-}
+template <uint32_t FMT> struct BlockShape;
+template <> struct BlockShape<kQ8_0> { static constexpr int E = 32, B = 34; };
+template <> struct BlockShape<kQ5_0> { static constexpr int E = 32, B = 22; };
+template <> struct BlockShape<kQ4_K> { static constexpr int E = 256, B = 144; };
+template <> struct BlockShape<kQ6_K> { static constexpr int E = 256, B = 210; };
 
-template <uint32_t FMT>
-__device__ __forceinline__ BlockRef ref_raw(const uint8_t *blk)
-{
-    BlockRef b;
-    b.qh = nullptr;
-    b.d16 = 0;
-    if constexpr (FMT == kQ8_0) {
-        b.d16 = (uint32_t)blk[0] | ((uint32_t)blk[1] << 8);
-        b.p = blk + 2;
-    } else if constexpr (FMT == kQ5_0) {
-        b.d16 = (uint32_t)blk[0] | ((uint32_t)blk[1] << 8);
-        b.qh = blk + 2;
-        b.p = blk + 6;
-    } else if constexpr (FMT == kQ4_K) {
-        b.p = blk;
-    } else {
-        b.p = blk;
-        b.d16 = (uint32_t)blk[208] | ((uint32_t)blk[209] << 8);
-    }
-    return b;
-}
-
+// One thread per block: gather its raw bytes, then decode every value.
 template <uint32_t FMT>
 __global__ void dequant_layout_kernel(Layout L, const uint8_t *__restrict__ w, float *__restrict__ out)
 {
-    constexpr int BE = (FMT == kQ8_0 || FMT == kQ5_0) ? 32 : 256;
-    const uint64_t total = (uint64_t)L.rows * L.cols;
+    constexpr int BE = BlockShape<FMT>::E;
+    const uint64_t total = (uint64_t)L.rows * L.nb;
+    uint8_t raw[BlockShape<FMT>::B];
     for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
          e += (uint64_t)gridDim.x * blockDim.x) {
-        const uint64_t row = e / (uint64_t)L.cols;
-        const int col = (int)(e % (uint64_t)L.cols);
-        const BlockRef b = ref_layout<FMT>(L, w, row, col / BE);
-        out[e] = dequant_value<FMT>(b, col % BE);
+        const uint64_t row = e / L.nb;
+        const int b = (int)(e % L.nb);
+        gather_raw_block(L, w + row * L.row_stride, b, raw);
+        float *o = out + e * BE;
+        for (int i = 0; i < BE; ++i) o[i] = dequant_value<FMT>(raw, i);
     }
 }
 
 template <uint32_t FMT>
 __global__ void dequant_raw_kernel(const uint8_t *__restrict__ raw, uint64_t nblocks, float *__restrict__ out)
 {
-    constexpr int BE = (FMT == kQ8_0 || FMT == kQ5_0) ? 32 : 256;
-    constexpr int BB = (FMT == kQ8_0) ? 34 : (FMT == kQ5_0) ? 22 : (FMT == kQ4_K) ? 144 : 210;
+    constexpr int BE = BlockShape<FMT>::E, BB = BlockShape<FMT>::B;
     const uint64_t total = nblocks * BE;
     for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total;
-         e += (uint64_t)gridDim.x * blockDim.x) {
-        const BlockRef b = ref_raw<FMT>(raw + (e / BE) * BB);
-        out[e] = dequant_value<FMT>(b, (int)(e % BE));
-    }
+         e += (uint64_t)gridDim.x * blockDim.x)
+        out[e] = dequant_value<FMT>(raw + (e / BE) * BB, (int)(e % BE));
 }
 
 // ------------------------------------------------------ launch helpers
@@ -780,10 +810,10 @@ int sm_count()
 {
     static int count = 0;
     if (count == 0) {
-        int dev = 0;
+        int dev = 0, n = 0;
         cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
-        if (count <= 0) count = 148;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        count = n > 0 ? n : 148;
     }
     return count;
 }
@@ -797,14 +827,33 @@ unsigned grid_for(uint64_t work, int threads)
     return (unsigned)g;
 }
 
+// Per-thread cache of (device, kernel, shared bytes) -> resident CTAs per SM.
 template <typename K>
 cudaError_t prepare(K kernel, size_t smem, int *blocks_per_sm)
 {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    struct Entry {
+        const void *fn;
+        int dev;
+        size_t smem;
+        int occ;
+    };
+    static thread_local Entry cache[64];
+    static thread_local int used = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    for (int i = 0; i < used; ++i) {
+        if (cache[i].fn == (const void *)kernel && cache[i].dev == dev && cache[i].smem == smem) {
+            *blocks_per_sm = cache[i].occ;
+            return cudaSuccess;
+        }
+    }
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, kernel, kThreads, smem);
     if (e != cudaSuccess) return e;
     if (*blocks_per_sm < 1) return cudaErrorInvalidConfiguration;
+    if (used < 64) cache[used++] = Entry{(const void *)kernel, dev, smem, *blocks_per_sm};
     return cudaSuccess;
 }
 
@@ -817,9 +866,10 @@ cudaError_t gemv_go(const Layout &L, const uint8_t *w, const float *x, float *y,
     int occ = 0;
     cudaError_t e = prepare(kernel, smem, &occ);
     if (e != cudaSuccess) return e;
-    constexpr int rows_per_pass = (kThreads / TPT) * R;
+    constexpr int WR = (32 / TPT) * R;
+    const long long warp_tiles = ((long long)L.rows + WR - 1) / WR;
     long long grid = (long long)sm_count() * occ;
-    long long useful = ((long long)L.rows + rows_per_pass - 1) / rows_per_pass;
+    const long long useful = (warp_tiles + (kThreads / 32) - 1) / (kThreads / 32);
     if (grid > useful) grid = useful;
     if (am && grid > kMaxArgmaxCtas) grid = kMaxArgmaxCtas;
     if (grid < 1) grid = 1;
@@ -828,29 +878,14 @@ cudaError_t gemv_go(const Layout &L, const uint8_t *w, const float *x, float *y,
     return cudaGetLastError();
 }
 
-template <uint32_t FMT, int R>
-cudaError_t gemv_pick_tpt(const Layout &L, const uint8_t *w, const float *x, float *y,
-                          const ArgmaxOut *am, cudaStream_t s)
-{
-    const int C = Chunk<FMT>::per_row(L.cols);
-    if (C <= 16) return gemv_go<FMT, 16, R>(L, w, x, y, am, s);
-    if (C <= 32) return gemv_go<FMT, 32, R>(L, w, x, y, am, s);
-    if (C <= 64) return gemv_go<FMT, 64, R>(L, w, x, y, am, s);
-    if (C <= 128) return gemv_go<FMT, 128, R>(L, w, x, y, am, s);
-    return gemv_go<FMT, 256, R>(L, w, x, y, am, s);
-}
-
 template <uint32_t FMT>
 cudaError_t gemv_fmt(const Layout &L, const uint8_t *w, const float *x, float *y, const ArgmaxOut *am,
                      cudaStream_t s)
 {
-    // Few rows per CTA -> smaller row tiles keep every group busy.
-    const long long rows_per_cta = (long long)L.rows / (2LL * sm_count());
-    const int C = Chunk<FMT>::per_row(L.cols);
-    const int tpt = C <= 16 ? 16 : C <= 32 ? 32 : C <= 64 ? 64 : C <= 128 ? 128 : 256;
-    const int groups = kThreads / tpt;
-    if (rows_per_cta < 4LL * groups) return gemv_pick_tpt<FMT, 2>(L, w, x, y, am, s);
-    return gemv_pick_tpt<FMT, 4>(L, w, x, y, am, s);
+    // 16-lane groups for short rows, whole warps otherwise; two rows per group
+    // share each x slice load.
+    if (L.C <= 16) return gemv_go<FMT, 16, 2>(L, w, x, y, am, s);
+    return gemv_go<FMT, 32, 2>(L, w, x, y, am, s);
 }
 
 template <uint32_t FMT, int TPT>
@@ -867,9 +902,10 @@ cudaError_t matmul_go(const Layout &L, const uint8_t *w, const float *X, int bat
     int occ = 0;
     cudaError_t e = prepare(kernel, xb * np_max, &occ);
     if (e != cudaSuccess) return e;
-    constexpr int rows_per_pass = kThreads / TPT;
+    constexpr int GPW = 32 / TPT;
+    const long long tiles = ((long long)L.rows + GPW - 1) / GPW;
     long long grid = (long long)sm_count() * occ;
-    long long useful = ((long long)L.rows + rows_per_pass - 1) / rows_per_pass;
+    const long long useful = (tiles + (kThreads / 32) - 1) / (kThreads / 32);
     if (grid > useful) grid = useful;
     if (grid < 1) grid = 1;
     for (int p0 = 0; p0 < batch; p0 += np_max) {
@@ -886,10 +922,8 @@ template <uint32_t FMT>
 cudaError_t matmul_fmt(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
                        cudaStream_t s)
 {
-    const int C = Chunk<FMT>::per_row(L.cols);
-    if (C <= 16) return matmul_go<FMT, 16>(L, w, X, batch, Y, s);
-    if (C <= 32) return matmul_go<FMT, 32>(L, w, X, batch, Y, s);
-    return matmul_go<FMT, 64>(L, w, X, batch, Y, s);
+    if (L.C <= 16) return matmul_go<FMT, 16>(L, w, X, batch, Y, s);
+    return matmul_go<FMT, 32>(L, w, X, batch, Y, s);
 }
 
 }  // namespace
@@ -928,20 +962,26 @@ bool make_layout(uint32_t type, int rows, int cols, Layout *out)
     const uint32_t nb = (uint32_t)L.nb;
     switch (type) {
     case kQ8_0:
-        L.off_d = 32 * nb;
-        L.row_stride = L.off_d + pad16(2 * nb);
+        L.C = L.nb;
+        L.off_a = 32 * nb;
+        L.row_stride = L.off_a + pad16(2 * nb);
         break;
     case kQ5_0:
-        L.off_qh = 16 * nb;
-        L.off_d = L.off_qh + pad16(4 * nb);
-        L.row_stride = L.off_d + pad16(2 * nb);
+        L.C = L.nb;
+        L.off_a = 16 * nb;
+        L.off_b = L.off_a + pad16(4 * nb);
+        L.row_stride = L.off_b + pad16(2 * nb);
         break;
     case kQ4_K:
+        L.C = 4 * L.nb;
+        L.off_a = 128 * nb;
         L.row_stride = 144ull * nb;
         break;
     default:
-        L.off_d = 208 * nb;
-        L.row_stride = L.off_d + pad16(2 * nb);
+        L.C = 4 * L.nb;
+        L.off_a = 192 * nb;
+        L.off_b = 208 * nb;
+        L.row_stride = L.off_b + pad16(2 * nb);
         break;
     }
     *out = L;
@@ -952,14 +992,14 @@ cudaError_t launch_repack(const Layout &L, const uint8_t *raw, uint8_t *dst, cud
 {
     cudaError_t e = cudaMemsetAsync(dst, 0, (size_t)L.rows * L.row_stride, s);
     if (e != cudaSuccess) return e;
-    const uint64_t nblocks = (uint64_t)L.rows * L.nb;
-    repack_kernel<<<grid_for(nblocks, kThreads), kThreads, 0, s>>>(L, raw, dst);
+    const uint64_t n = (uint64_t)L.rows * L.C;
+    repack_kernel<<<grid_for(n, kThreads), kThreads, 0, s>>>(L, raw, dst);
     return cudaGetLastError();
 }
 
 cudaError_t launch_dequant_layout(const Layout &L, const uint8_t *w, float *out, cudaStream_t s)
 {
-    const unsigned g = grid_for((uint64_t)L.rows * L.cols, kThreads);
+    const unsigned g = grid_for((uint64_t)L.rows * L.nb, kThreads);
     switch (L.type) {
     case kQ8_0: dequant_layout_kernel<kQ8_0><<<g, kThreads, 0, s>>>(L, w, out); break;
     case kQ5_0: dequant_layout_kernel<kQ5_0><<<g, kThreads, 0, s>>>(L, w, out); break;
