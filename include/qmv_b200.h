@@ -45,6 +45,18 @@ int qmv_device_count(int *count);
  * thread allocate and launch there). */
 int qmv_set_device(int device);
 
+/* Device status of the current device: bit 0 = a consumer's pipeline wait
+ * expired, bit 1 = a producer's wait expired, bit 2 = draining in-flight
+ * copies timed out.  0 means every bounded wait completed.  clear != 0 resets
+ * the word.  No counterpart in the reference (its kernels never wait). */
+int qmv_device_status(uint32_t *flags, int clear);
+
+/* GEMV kernel selection for the calling process: 0 = automatic (TMA bulk-copy
+ * pipeline when its shared-memory stages fit, direct loads otherwise),
+ * 1 = direct loads, 2 = TMA pipeline only (shapes it cannot stage fail).
+ * No counterpart in the reference; both paths compute the same function. */
+int qmv_set_gemv_path(int path);
+
 /* ---- residency of packed tensors ----------------------------------------
  * Backs the packed-weight source of the reference: the borrowed mmap views
  * returned by gguf_get_quantized_tensor_view (src/gguf_reader.cpp:573-637,

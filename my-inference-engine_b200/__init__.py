@@ -41,7 +41,7 @@ KEY_NONFINITE = 0xFFFFFFFFFFFFFFFF
 # include/quantized_matvec.h (mangled, C++ linkage).
 C_SYMBOLS = [
     "qmv_last_error", "qmv_copy_last_error", "qmv_abi_version", "qmv_device_count",
-    "qmv_set_device", "qmv_weight_upload", "qmv_weight_free", "qmv_weight_info",
+    "qmv_set_device", "qmv_device_status", "qmv_set_gemv_path", "qmv_weight_upload", "qmv_weight_free", "qmv_weight_info",
     "qmv_resident_weight", "qmv_resident_release_all", "qmv_matvec", "qmv_matmul",
     "qmv_dequantize", "qmv_dequantize_raw", "qmv_argmax_workspace_bytes", "qmv_argmax",
     "qmv_matvec_argmax", "qmv_key_to_token", "qmv_greedy_sample",
@@ -108,6 +108,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "qmv_abi_version": (I, []),
         "qmv_device_count": (I, [IP]),
         "qmv_set_device": (I, [I]),
+        "qmv_device_status": (I, [ctypes.POINTER(U32), I]),
+        "qmv_set_gemv_path": (I, [I]),
         "qmv_weight_upload": (I, [VP, I, I, ctypes.POINTER(P)]),
         "qmv_weight_free": (I, [P]),
         "qmv_weight_info": (I, [P, ctypes.POINTER(U32), IP, IP, IP, ctypes.POINTER(U64)]),
@@ -220,6 +222,21 @@ def argmax(logits_dev, n: int, key_dev, workspace_dev, index_base: int = 0, stre
 def dequantize_raw(ggml_type: int, blocks_dev, block_count: int, out_dev, stream=None):
     _check(lib().qmv_dequantize_raw(ggml_type, _ptr(blocks_dev), block_count, _ptr(out_dev),
                                     _ptr(stream)), "qmv_dequantize_raw")
+
+
+def device_status(clear: bool = False) -> int:
+    """Bits set by bounded device waits that expired (0 = healthy)."""
+    v = ctypes.c_uint32(0)
+    _check(lib().qmv_device_status(ctypes.byref(v), 1 if clear else 0), "qmv_device_status")
+    return v.value
+
+
+GEMV_AUTO, GEMV_LOADS, GEMV_TMA = 0, 1, 2
+
+
+def set_gemv_path(path: int):
+    """0 automatic, 1 direct-load kernel, 2 TMA pipeline kernel."""
+    _check(lib().qmv_set_gemv_path(path), "qmv_set_gemv_path")
 
 
 def set_device(device: int):

@@ -241,6 +241,22 @@ QMV_EXPORT int qmv_set_device(int device)
     return 1;
 }
 
+QMV_EXPORT int qmv_device_status(uint32_t *flags, int clear)
+{
+    if (flags == nullptr) return fail("flags pointer is null");
+    unsigned int v = 0;
+    QMV_CUDA(qmv::read_status(&v, clear != 0), "read device status");
+    *flags = v;
+    return 1;
+}
+
+QMV_EXPORT int qmv_set_gemv_path(int path)
+{
+    if (path < 0 || path > 2) return fail("gemv path must be 0, 1 or 2");
+    qmv::set_gemv_path(path);
+    return 1;
+}
+
 QMV_EXPORT int qmv_weight_upload(const GgufQuantizedTensorView *view, int row_begin, int row_end,
                                  QmvWeight **out)
 {

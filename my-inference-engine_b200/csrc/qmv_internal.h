@@ -72,6 +72,11 @@ cudaError_t launch_gemv(const Layout &L, const uint8_t *w, const float *x, float
 // Y[p] = W X[p], p < batch.
 cudaError_t launch_matmul(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
                           cudaStream_t s);
+// GEMV kernel selection: 0 automatic (TMA pipeline when its stages fit in
+// shared memory, direct loads otherwise), 1 direct loads, 2 TMA pipeline only.
+void set_gemv_path(int path);
+// Device status bits set by bounded waits that expired (0 = healthy).
+cudaError_t read_status(unsigned int *out, bool clear);
 // Argmax key of logits[0..n).
 cudaError_t launch_argmax(const float *logits, int n, const ArgmaxOut &am, cudaStream_t s);
 

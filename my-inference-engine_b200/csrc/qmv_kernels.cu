@@ -24,7 +24,7 @@
 //
 // Shared-memory x layout mirrors the weight layout: the 16-element slice j
 // of chunk c is stored at (j * C + c) * 16 in each plane, with one record
-// {scale bits, sum of xq} per slice, so lanes reading consecutive chunks hit
+// {s, s * sum of xq} per slice, so lanes reading consecutive chunks hit
 // consecutive banks.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -193,7 +193,7 @@ template <> struct Slices<kQ6_K> {
 struct XS {
     const uint8_t *hi;   // [cols] int8, chunk-major slices
     const uint8_t *lo;   // [cols]
-    const int2 *rec;     // [cols/16] {scale bits (NaN if non-finite), sum of xq}
+    const float2 *rec;   // [cols/16] {s, s * sum of xq}; s is NaN for a non-finite block
     __device__ __forceinline__ uint4 h(int j, int C, int c) const
     {
         return *reinterpret_cast<const uint4 *>(hi + ((j * C + c) << 4));
@@ -202,7 +202,7 @@ struct XS {
     {
         return *reinterpret_cast<const uint4 *>(lo + ((j * C + c) << 4));
     }
-    __device__ __forceinline__ int2 r(int j, int C, int c) const { return rec[j * C + c]; }
+    __device__ __forceinline__ float2 r(int j, int C, int c) const { return rec[j * C + c]; }
 };
 
 // Bytes of one quantized position, rounded up to 16 so consecutive positions
@@ -217,7 +217,7 @@ __device__ __forceinline__ XS xs_view(const uint8_t *base, int cols)
     XS s;
     s.hi = base;
     s.lo = base + cols;
-    s.rec = reinterpret_cast<const int2 *>(base + 2 * cols);
+    s.rec = reinterpret_cast<const float2 *>(base + 2 * cols);
     return s;
 }
 
@@ -228,7 +228,7 @@ __device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t
 {
     uint8_t *hi = base;
     uint8_t *lo = base + cols;
-    int2 *rec = reinterpret_cast<int2 *>(base + 2 * cols);
+    float2 *rec = reinterpret_cast<float2 *>(base + 2 * cols);
     const int n4 = cols >> 2;
     constexpr int U = 8;
     for (int it0 = 0; it0 * kThreads < n4; it0 += U) {
@@ -277,8 +277,9 @@ __device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t
                 *reinterpret_cast<uint32_t *>(hi + off) = hh;
                 *reinterpret_cast<uint32_t *>(lo + off) = ll;
                 if ((f & 3) == 0) {
+                    // s * sum is exact: s is a power of two, |sum| < 2^20
                     const float sc = bad ? __uint_as_float(0x7fc00000u) : __uint_as_float((uint32_t)(127 + e) << 23);
-                    rec[si] = make_int2((int)__float_as_uint(sc), s4);
+                    rec[si] = make_float2(sc, sc * (float)s4);
                 }
             }
         }
@@ -287,13 +288,63 @@ __device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t
 
 // ------------------------------------------------- per-format chunk code
 //
-// W<FMT> holds one row's chunk in registers: load() issues the global loads
-// (each a contiguous run across the lanes of a warp), dot() consumes the
-// matching x slices from shared memory.
+// XR<N> holds the N x slices of one chunk in registers (loaded once, reused by
+// every row the lane handles).  W<FMT> holds one row's chunk of weights:
+// load() reads global memory (each piece a contiguous run across the warp),
+// load_smem() reads a row staged in shared memory by the TMA pipeline, and
+// dot() combines them.
+
+template <int N> struct XR {
+    uint4 h[N], l[N];
+    float2 r[N];
+};
+
+template <int N>
+__device__ __forceinline__ XR<N> load_xr(const XS &s, int C, int c)
+{
+    XR<N> x;
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+        x.h[j] = s.h(j, C, c);
+        x.l[j] = s.l(j, C, c);
+        x.r[j] = s.r(j, C, c);
+    }
+    return x;
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t a)
+{
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t a)
+{
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t lds16(uint32_t a)
+{
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
 
 template <uint32_t FMT> struct W;
 
+__device__ __forceinline__ int dot4(const uint4 &w, const uint4 &x, int acc)
+{
+    acc = dp4a(w.x, x.x, acc);
+    acc = dp4a(w.y, x.y, acc);
+    acc = dp4a(w.z, x.z, acc);
+    return dp4a(w.w, x.w, acc);
+}
+
 template <> struct W<kQ8_0> {
+    static constexpr int kSlices = 2;
     uint4 a, b;
     uint32_t d;
     __device__ __forceinline__ void zero() { a = b = make_uint4(0, 0, 0, 0); d = 0; }
@@ -303,17 +354,17 @@ template <> struct W<kQ8_0> {
         b = ld_stream(row + ((L.C + c) << 4));
         d = ld_stream16(row + L.off_a + 2 * c);
     }
-    __device__ __forceinline__ float dot(const XS &s, int C, int c) const
+    __device__ __forceinline__ void load_smem(uint32_t row, const Layout &L, int c)
     {
-        const uint4 h0 = s.h(0, C, c), h1 = s.h(1, C, c), l0 = s.l(0, C, c), l1 = s.l(1, C, c);
-        int ah = dp4a(a.x, h0.x, 0);
-        ah = dp4a(a.y, h0.y, ah); ah = dp4a(a.z, h0.z, ah); ah = dp4a(a.w, h0.w, ah);
-        ah = dp4a(b.x, h1.x, ah); ah = dp4a(b.y, h1.y, ah); ah = dp4a(b.z, h1.z, ah); ah = dp4a(b.w, h1.w, ah);
-        int al = dp4a(a.x, l0.x, 0);
-        al = dp4a(a.y, l0.y, al); al = dp4a(a.z, l0.z, al); al = dp4a(a.w, l0.w, al);
-        al = dp4a(b.x, l1.x, al); al = dp4a(b.y, l1.y, al); al = dp4a(b.z, l1.z, al); al = dp4a(b.w, l1.w, al);
-        const float sx = __int_as_float(s.r(0, C, c).x);
-        return (f16_fast(d) * sx) * (float)(ah * 256 + al);
+        a = lds128(row + (c << 4));
+        b = lds128(row + ((L.C + c) << 4));
+        d = lds16(row + L.off_a + 2 * c);
+    }
+    __device__ __forceinline__ float dot(const XR<2> &x) const
+    {
+        const int ah = dot4(b, x.h[1], dot4(a, x.h[0], 0));
+        const int al = dot4(b, x.l[1], dot4(a, x.l[0], 0));
+        return (f16_fast(d) * x.r[0].x) * (float)(ah * 256 + al);
     }
 };
 
@@ -324,6 +375,7 @@ __device__ __forceinline__ uint32_t spread4(uint32_t v)
 }
 
 template <> struct W<kQ5_0> {
+    static constexpr int kSlices = 2;
     uint4 q;
     uint32_t qh, d;
     __device__ __forceinline__ void zero() { q = make_uint4(0, 0, 0, 0); qh = d = 0; }
@@ -333,61 +385,62 @@ template <> struct W<kQ5_0> {
         qh = ld_stream32(row + L.off_a + 4 * c);
         d = ld_stream16(row + L.off_b + 2 * c);
     }
-    __device__ __forceinline__ float dot(const XS &s, int C, int c) const
+    __device__ __forceinline__ void load_smem(uint32_t row, const Layout &L, int c)
     {
-        const uint4 h0 = s.h(0, C, c), h1 = s.h(1, C, c), l0 = s.l(0, C, c), l1 = s.l(1, C, c);
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-        const uint32_t xh0[4] = {h0.x, h0.y, h0.z, h0.w}, xh1[4] = {h1.x, h1.y, h1.z, h1.w};
-        const uint32_t xl0[4] = {l0.x, l0.y, l0.z, l0.w}, xl1[4] = {l1.x, l1.y, l1.z, l1.w};
-        int ah = 0, al = 0;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            // weights 4k..4k+3 from low nibbles, 16+4k.. from high nibbles;
-            // the fifth bit of weight i is bit i of qh
-            const uint32_t lw = (w[k] & 0x0f0f0f0fu) | spread4(qh >> (4 * k));
-            const uint32_t hw = ((w[k] >> 4) & 0x0f0f0f0fu) | spread4(qh >> (16 + 4 * k));
-            ah = dp4a(lw, xh0[k], ah);
-            al = dp4a(lw, xl0[k], al);
-            ah = dp4a(hw, xh1[k], ah);
-            al = dp4a(hw, xl1[k], al);
-        }
-        const int2 r0 = s.r(0, C, c), r1 = s.r(1, C, c);
-        return (f16_fast(d) * __int_as_float(r0.x)) * (float)(ah * 256 + al - 16 * (r0.y + r1.y));
+        q = lds128(row + (c << 4));
+        qh = lds32(row + L.off_a + 4 * c);
+        d = lds16(row + L.off_b + 2 * c);
+    }
+    __device__ __forceinline__ float dot(const XR<2> &x) const
+    {
+        // weights 4k..4k+3 from low nibbles, 16+4k.. from high nibbles; the
+        // fifth bit of weight i is bit i of qh
+        const uint4 lw = make_uint4((q.x & 0x0f0f0f0fu) | spread4(qh), (q.y & 0x0f0f0f0fu) | spread4(qh >> 4),
+                                    (q.z & 0x0f0f0f0fu) | spread4(qh >> 8), (q.w & 0x0f0f0f0fu) | spread4(qh >> 12));
+        const uint4 hw = make_uint4(((q.x >> 4) & 0x0f0f0f0fu) | spread4(qh >> 16),
+                                    ((q.y >> 4) & 0x0f0f0f0fu) | spread4(qh >> 20),
+                                    ((q.z >> 4) & 0x0f0f0f0fu) | spread4(qh >> 24),
+                                    ((q.w >> 4) & 0x0f0f0f0fu) | spread4(qh >> 28));
+        const int ah = dot4(hw, x.h[1], dot4(lw, x.h[0], 0));
+        const int al = dot4(hw, x.l[1], dot4(lw, x.l[0], 0));
+        return f16_fast(d) * (x.r[0].x * (float)(ah * 256 + al) - 16.f * (x.r[0].y + x.r[1].y));
     }
 };
 
 template <> struct W<kQ4_K> {
+    static constexpr int kSlices = 4;
     uint4 a, b, hdr;
-    __device__ __forceinline__ void zero() { a = b = hdr = make_uint4(0, 0, 0, 0); }
+    int g;
+    __device__ __forceinline__ void zero() { a = b = hdr = make_uint4(0, 0, 0, 0); g = 0; }
     __device__ __forceinline__ void load(const uint8_t *row, const Layout &L, int c)
     {
         a = ld_stream(row + (c << 4));
         b = ld_stream(row + ((L.C + c) << 4));
         hdr = ld_stream(row + L.off_a + ((c >> 2) << 4));
+        g = c & 3;
     }
-    __device__ __forceinline__ float dot(const XS &s, int C, int c) const
+    __device__ __forceinline__ void load_smem(uint32_t row, const Layout &L, int c)
     {
-        // slice 0/1: low nibbles of pieces a/b (sub-block 2g);
-        // slice 2/3: high nibbles (sub-block 2g+1)
-        const uint4 x0 = s.h(0, C, c), x1 = s.h(1, C, c), x2 = s.h(2, C, c), x3 = s.h(3, C, c);
-        const uint4 y0 = s.l(0, C, c), y1 = s.l(1, C, c), y2 = s.l(2, C, c), y3 = s.l(3, C, c);
-        const uint32_t pa[4] = {a.x, a.y, a.z, a.w}, pb[4] = {b.x, b.y, b.z, b.w};
-        const uint32_t h0[4] = {x0.x, x0.y, x0.z, x0.w}, h1[4] = {x1.x, x1.y, x1.z, x1.w};
-        const uint32_t h2[4] = {x2.x, x2.y, x2.z, x2.w}, h3[4] = {x3.x, x3.y, x3.z, x3.w};
-        const uint32_t l0[4] = {y0.x, y0.y, y0.z, y0.w}, l1[4] = {y1.x, y1.y, y1.z, y1.w};
-        const uint32_t l2[4] = {y2.x, y2.y, y2.z, y2.w}, l3[4] = {y3.x, y3.y, y3.z, y3.w};
-        int ah0 = 0, al0 = 0, ah1 = 0, al1 = 0;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const uint32_t la = pa[k] & 0x0f0f0f0fu, lb = pb[k] & 0x0f0f0f0fu;
-            const uint32_t ua = (pa[k] >> 4) & 0x0f0f0f0fu, ub = (pb[k] >> 4) & 0x0f0f0f0fu;
-            ah0 = dp4a(la, h0[k], ah0); al0 = dp4a(la, l0[k], al0);
-            ah0 = dp4a(lb, h1[k], ah0); al0 = dp4a(lb, l1[k], al0);
-            ah1 = dp4a(ua, h2[k], ah1); al1 = dp4a(ua, l2[k], al1);
-            ah1 = dp4a(ub, h3[k], ah1); al1 = dp4a(ub, l3[k], al1);
-        }
+        a = lds128(row + (c << 4));
+        b = lds128(row + ((L.C + c) << 4));
+        hdr = lds128(row + L.off_a + ((c >> 2) << 4));
+        g = c & 3;
+    }
+    __device__ __forceinline__ float dot(const XR<4> &x) const
+    {
+        // slices 0/1: low nibbles of pieces a/b (sub-block 2g);
+        // slices 2/3: high nibbles (sub-block 2g+1)
+        const uint4 la = make_uint4(a.x & 0x0f0f0f0fu, a.y & 0x0f0f0f0fu, a.z & 0x0f0f0f0fu, a.w & 0x0f0f0f0fu);
+        const uint4 lb = make_uint4(b.x & 0x0f0f0f0fu, b.y & 0x0f0f0f0fu, b.z & 0x0f0f0f0fu, b.w & 0x0f0f0f0fu);
+        const uint4 ua = make_uint4((a.x >> 4) & 0x0f0f0f0fu, (a.y >> 4) & 0x0f0f0f0fu,
+                                    (a.z >> 4) & 0x0f0f0f0fu, (a.w >> 4) & 0x0f0f0f0fu);
+        const uint4 ub = make_uint4((b.x >> 4) & 0x0f0f0f0fu, (b.y >> 4) & 0x0f0f0f0fu,
+                                    (b.z >> 4) & 0x0f0f0f0fu, (b.w >> 4) & 0x0f0f0f0fu);
+        const int ah0 = dot4(lb, x.h[1], dot4(la, x.h[0], 0));
+        const int al0 = dot4(lb, x.l[1], dot4(la, x.l[0], 0));
+        const int ah1 = dot4(ub, x.h[3], dot4(ua, x.h[2], 0));
+        const int al1 = dot4(ub, x.l[3], dot4(ua, x.l[2], 0));
         // 6-bit scale / min of sub-blocks 2g and 2g+1 (src/quantization.cpp:351-378)
-        const int g = c & 3;
         const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
         uint32_t sc0, m0, sc1, m1;
         if (g < 2) {
@@ -402,14 +455,14 @@ template <> struct W<kQ4_K> {
             m1 = (((s2 >> t1) >> 4) & 15u) | ((((s1 >> t1) >> 6) & 3u) << 4);
         }
         const float d = f16_fast(hdr.x), dmin = f16_fast(hdr.x >> 16);
-        const int2 r0 = s.r(0, C, c), r1 = s.r(1, C, c), r2 = s.r(2, C, c), r3 = s.r(3, C, c);
-        const float v0 = (d * (float)sc0) * (float)(ah0 * 256 + al0) - (dmin * (float)m0) * (float)(r0.y + r1.y);
-        const float v1 = (d * (float)sc1) * (float)(ah1 * 256 + al1) - (dmin * (float)m1) * (float)(r2.y + r3.y);
-        return __int_as_float(r0.x) * v0 + __int_as_float(r2.x) * v1;
+        const float v0 = (d * (float)sc0) * (x.r[0].x * (float)(ah0 * 256 + al0)) - (dmin * (float)m0) * (x.r[0].y + x.r[1].y);
+        const float v1 = (d * (float)sc1) * (x.r[2].x * (float)(ah1 * 256 + al1)) - (dmin * (float)m1) * (x.r[2].y + x.r[3].y);
+        return v0 + v1;
     }
 };
 
 template <> struct W<kQ6_K> {
+    static constexpr int kSlices = 4;
     uint4 a, b, u;
     uint32_t sc, d;
     __device__ __forceinline__ void zero() { a = b = u = make_uint4(0, 0, 0, 0); sc = d = 0; }
@@ -421,45 +474,58 @@ template <> struct W<kQ6_K> {
         sc = ld_stream32(row + L.off_a + 4 * c);
         d = ld_stream16(row + L.off_b + 2 * (c >> 2));
     }
-    __device__ __forceinline__ float dot(const XS &s, int C, int c) const
+    __device__ __forceinline__ void load_smem(uint32_t row, const Layout &L, int c)
     {
-        const uint32_t pa[4] = {a.x, a.y, a.z, a.w}, pb[4] = {b.x, b.y, b.z, b.w};
-        const uint32_t pu[4] = {u.x, u.y, u.z, u.w};
-        float acc = 0.f;
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const uint4 xh4 = s.h(r, C, c), xl4 = s.l(r, C, c);
-            const uint32_t xh[4] = {xh4.x, xh4.y, xh4.z, xh4.w};
-            const uint32_t xl[4] = {xl4.x, xl4.y, xl4.z, xl4.w};
-            int ah = 0, al = 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                uint32_t w;  // 6-bit values 0..63 (src/quantization.cpp:559-586)
-                if (r == 0) w = (pa[k] & 0x0f0f0f0fu) | ((pu[k] << 4) & 0x30303030u);
-                else if (r == 1) w = (pb[k] & 0x0f0f0f0fu) | ((pu[k] << 2) & 0x30303030u);
-                else if (r == 2) w = ((pa[k] >> 4) & 0x0f0f0f0fu) | (pu[k] & 0x30303030u);
-                else w = ((pb[k] >> 4) & 0x0f0f0f0fu) | ((pu[k] >> 2) & 0x30303030u);
-                ah = dp4a(w, xh[k], ah);
-                al = dp4a(w, xl[k], al);
-            }
-            const int2 rr = s.r(r, C, c);
-            const int scale = (int)(int8_t)((sc >> (8 * r)) & 0xffu);
-            acc += ((float)scale * __int_as_float(rr.x)) * (float)(ah * 256 + al - 32 * rr.y);
-        }
+        a = lds128(row + (c << 4));
+        b = lds128(row + ((L.C + c) << 4));
+        u = lds128(row + ((2 * L.C + c) << 4));
+        sc = lds32(row + L.off_a + 4 * c);
+        d = lds16(row + L.off_b + 2 * (c >> 2));
+    }
+    __device__ __forceinline__ float dot(const XR<4> &x) const
+    {
+        // 6-bit values 0..63 per region (src/quantization.cpp:559-586)
+        const uint4 w0 = make_uint4((a.x & 0x0f0f0f0fu) | ((u.x << 4) & 0x30303030u),
+                                    (a.y & 0x0f0f0f0fu) | ((u.y << 4) & 0x30303030u),
+                                    (a.z & 0x0f0f0f0fu) | ((u.z << 4) & 0x30303030u),
+                                    (a.w & 0x0f0f0f0fu) | ((u.w << 4) & 0x30303030u));
+        const uint4 w1 = make_uint4((b.x & 0x0f0f0f0fu) | ((u.x << 2) & 0x30303030u),
+                                    (b.y & 0x0f0f0f0fu) | ((u.y << 2) & 0x30303030u),
+                                    (b.z & 0x0f0f0f0fu) | ((u.z << 2) & 0x30303030u),
+                                    (b.w & 0x0f0f0f0fu) | ((u.w << 2) & 0x30303030u));
+        const uint4 w2 = make_uint4(((a.x >> 4) & 0x0f0f0f0fu) | (u.x & 0x30303030u),
+                                    ((a.y >> 4) & 0x0f0f0f0fu) | (u.y & 0x30303030u),
+                                    ((a.z >> 4) & 0x0f0f0f0fu) | (u.z & 0x30303030u),
+                                    ((a.w >> 4) & 0x0f0f0f0fu) | (u.w & 0x30303030u));
+        const uint4 w3 = make_uint4(((b.x >> 4) & 0x0f0f0f0fu) | ((u.x >> 2) & 0x30303030u),
+                                    ((b.y >> 4) & 0x0f0f0f0fu) | ((u.y >> 2) & 0x30303030u),
+                                    ((b.z >> 4) & 0x0f0f0f0fu) | ((u.z >> 2) & 0x30303030u),
+                                    ((b.w >> 4) & 0x0f0f0f0fu) | ((u.w >> 2) & 0x30303030u));
+        const int A0 = dot4(w0, x.h[0], 0) * 256 + dot4(w0, x.l[0], 0);
+        const int A1 = dot4(w1, x.h[1], 0) * 256 + dot4(w1, x.l[1], 0);
+        const int A2 = dot4(w2, x.h[2], 0) * 256 + dot4(w2, x.l[2], 0);
+        const int A3 = dot4(w3, x.h[3], 0) * 256 + dot4(w3, x.l[3], 0);
+        const float s0 = (float)(int)(int8_t)(sc & 0xffu), s1 = (float)(int)(int8_t)((sc >> 8) & 0xffu);
+        const float s2 = (float)(int)(int8_t)((sc >> 16) & 0xffu), s3 = (float)(int)(int8_t)(sc >> 24);
+        float acc = s0 * (x.r[0].x * (float)A0 - 32.f * x.r[0].y);
+        acc += s1 * (x.r[1].x * (float)A1 - 32.f * x.r[1].y);
+        acc += s2 * (x.r[2].x * (float)A2 - 32.f * x.r[2].y);
+        acc += s3 * (x.r[3].x * (float)A3 - 32.f * x.r[3].y);
         return f16_fast(d) * acc;
     }
 };
 
-// ---------------------------------------------------------------- GEMV
+// ------------------------------------------------------- GEMV (loads)
 //
-// Persistent grid.  A warp owns whole row tiles: TPT lanes (16 or 32) per
-// group, 32/TPT groups per warp, R rows per group, so a warp tile is
-// (32/TPT)*R consecutive rows.  Warp tiles are dealt round-robin over every
+// Direct-load form (used when the TMA stages below do not fit, e.g. very
+// long rows).  Persistent grid.  A warp owns whole row tiles: TPT lanes (16
+// or 32) per group, 32/TPT groups per warp, R rows per group, so a warp tile
+// is (32/TPT)*R consecutive rows.  Warp tiles are dealt round-robin over every
 // warp of the grid.  Within a tile the group's lanes stride over the chunks
-// of its rows; one x slice set from shared memory serves R rows.  The next
-// item's weights are loaded before the current item is computed (one-deep
-// register prefetch), and the only synchronisation is a shuffle reduction in
-// a fixed order, so results are deterministic.
+// of its rows; one x slice set serves R rows.  The next item's weights are
+// loaded before the current item is computed (one-deep register prefetch),
+// and the only synchronisation is a shuffle reduction in a fixed order, so
+// results are deterministic.
 
 template <uint32_t FMT, int TPT, int R>
 __global__ void __launch_bounds__(kThreads)
@@ -468,6 +534,7 @@ gemv_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x
 {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ unsigned long long kscratch[kThreads / 32];
+    constexpr int NSL = W<FMT>::kSlices;
 
     const int C = L.C;
     quantize_x<FMT>(x, L.cols, C, smem);
@@ -486,14 +553,14 @@ gemv_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x
     const int n_items = my_tiles * NI;
 
     unsigned long long best = 0ull;
-    W<FMT> cur[R], nxt[R];
+    W<FMT> bufa[R], bufb[R];
     float acc[R];
 #pragma unroll
     for (int i = 0; i < R; ++i) acc[i] = 0.f;
 
-    auto load_item = [&](int k, W<FMT> (&dst)[R]) {
-        const int t = wg + (k / NI) * wtot;
-        const int c = (k % NI) * TPT + gl;
+    // Item k = (tile t, chunk iteration it); both advance incrementally.
+    auto load_item = [&](int t, int it, W<FMT> (&dst)[R]) {
+        const int c = it * TPT + gl;
         const int row0 = t * WR + grp * R;
 #pragma unroll
         for (int i = 0; i < R; ++i) {
@@ -503,18 +570,20 @@ gemv_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x
                 dst[i].zero();
         }
     };
-
-    if (n_items > 0) load_item(0, cur);
-    for (int k = 0; k < n_items; ++k) {
-        if (k + 1 < n_items) load_item(k + 1, nxt);
-        const int it = k % NI;
-        const int t = wg + (k / NI) * wtot;
+    // Compute item (t, it) from `use` while `pre` receives item k+1.
+    auto step = [&](int k, int &t, int &it, W<FMT> (&use)[R], W<FMT> (&pre)[R]) {
+        int nt = t, nit = it + 1;
+        if (nit == NI) {
+            nit = 0;
+            nt += wtot;
+        }
+        if (k + 1 < n_items) load_item(nt, nit, pre);
         const int c = it * TPT + gl;
         const int row0 = t * WR + grp * R;
         if (c < C) {
+            const XR<NSL> xr = load_xr<NSL>(s, C, c);
 #pragma unroll
-            for (int i = 0; i < R; ++i)
-                if (row0 + i < L.rows) acc[i] += cur[i].dot(s, C, c);
+            for (int i = 0; i < R; ++i) acc[i] += use[i].dot(xr);
         }
         if (it == NI - 1) {
 #pragma unroll
@@ -533,8 +602,225 @@ gemv_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x
 #pragma unroll
             for (int i = 0; i < R; ++i) acc[i] = 0.f;
         }
+        t = nt;
+        it = nit;
+    };
+
+    int t = wg, it = 0;
+    if (n_items > 0) load_item(t, it, bufa);
+    for (int k = 0; k < n_items; k += 2) {
+        step(k, t, it, bufa, bufb);
+        if (k + 1 < n_items) step(k + 1, t, it, bufb, bufa);
+    }
+    if (want_argmax) {
+        best = block_max_key(best, kscratch);
+        finish_argmax(best, am, kscratch);
+    }
+}
+
+// --------------------------------------------------- GEMV (TMA pipeline)
+//
+// One CTA per SM owns a contiguous range of rows, which is one contiguous
+// byte range of the resident tensor.  A producer warp streams it into a ring
+// of NS shared-memory stages with cp.async.bulk (1-D TMA, no multicast),
+// each stage holding kConsumerWarps * R rows and completing on an mbarrier
+// with its byte count.  Consumer warps each take R rows of a stage; their
+// lanes stride over the chunks, loading the x slices of a chunk once for the
+// R rows, then release the stage through an "empty" mbarrier.  Weights are
+// read from shared memory with conflict-free 128-bit loads (chunk-major rows).
+//
+// Every mbarrier wait is bounded by a globaltimer deadline: on expiry the
+// waiting thread sets a bit in g_status, stops issuing work, and the producer
+// still waits (again bounded) for the copies it has in flight before the CTA
+// exits.
+
+constexpr int kConsumerWarps = 8;
+constexpr int kTmaThreads = (kConsumerWarps + 1) * 32;
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+__device__ unsigned int g_status;
+enum : unsigned int { kStatusConsumerTimeout = 1u, kStatusProducerTimeout = 2u, kStatusDrainTimeout = 4u };
+
+__device__ __forceinline__ unsigned long long globaltimer()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity)
+{
+    if (mbar_try(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t n = 1;; ++n) {
+        if (mbar_try(bar, parity)) return true;
+        if ((n & 63u) == 0u && globaltimer() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar)
+{
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// 1-D bulk copy global -> shared, completing on `bar` (no multicast).
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+struct TmaPlan {
+    uint32_t x_bytes;      // quantized x, rounded to 128
+    uint32_t stage_bytes;  // rows_per_stage * row_stride, rounded to 128
+    int rows_per_stage;    // kConsumerWarps * R
+    int stages;            // NS
+};
+
+template <uint32_t FMT, int R>
+__global__ void __launch_bounds__(kTmaThreads, 1)
+gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x,
+                float *__restrict__ y, ArgmaxOut am, int want_argmax, TmaPlan P)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) unsigned long long bars[2 * 8];
+    __shared__ unsigned long long kscratch[kTmaThreads / 32];
+    constexpr int NSL = W<FMT>::kSlices;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int C = L.C;
+    const int NS = P.stages;
+    const uint32_t stage0 = (uint32_t)__cvta_generic_to_shared(smem + P.x_bytes);
+    const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(&bars[0]);
+    const uint32_t empty0 = full0 + 8u * 8u;
+
+    const int r0 = (int)((long long)L.rows * blockIdx.x / gridDim.x);
+    const int r1 = (int)((long long)L.rows * (blockIdx.x + 1) / gridDim.x);
+    const int SR = P.rows_per_stage;
+    const int n_stages = (r1 - r0 + SR - 1) / SR;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(full0 + 8u * i, 1u);
+            mbar_init(empty0 + 8u * i, (uint32_t)kConsumerWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    unsigned long long best = 0ull;
+    if (warp == kConsumerWarps) {
+        // ---------------- producer
+        if (lane == 0) {
+            int issued = 0;
+            bool ok = true;
+            for (int k = 0; k < n_stages; ++k) {
+                const int sidx = k % NS;
+                if (k >= NS && !mbar_wait(empty0 + 8u * sidx, (uint32_t)((k / NS - 1) & 1))) {
+                    atomicOr(&g_status, kStatusProducerTimeout);
+                    ok = false;
+                    break;
+                }
+                const int rows_k = min(SR, r1 - (r0 + k * SR));
+                const uint32_t bytes = (uint32_t)rows_k * (uint32_t)L.row_stride;
+                const uint32_t bar = full0 + 8u * sidx;
+                mbar_expect_tx(bar, bytes);
+                const uint8_t *src = w + (uint64_t)(r0 + k * SR) * L.row_stride;
+                const uint32_t dst = stage0 + (uint32_t)sidx * P.stage_bytes;
+                for (uint32_t off = 0; off < bytes; off += 32768u) {
+                    const uint32_t n = min(32768u, bytes - off);
+                    bulk_g2s(dst + off, src + off, n, bar);
+                }
+                ++issued;
+            }
+            if (!ok) {
+                // drain: every issued copy must land before the CTA exits
+                for (int k = max(0, issued - NS); k < issued; ++k) {
+                    if (!mbar_wait(full0 + 8u * (k % NS), (uint32_t)((k / NS) & 1))) {
+                        atomicOr(&g_status, kStatusDrainTimeout);
+                        break;
+                    }
+                }
+            }
+        }
+    } else {
+        // ---------------- consumers
+        quantize_x<FMT>(x, L.cols, C, smem);
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+        const XS s = xs_view(smem, L.cols);
+        const int NI = (C + 31) >> 5;
+        for (int k = 0; k < n_stages; ++k) {
+            const int sidx = k % NS;
+            if (!mbar_wait(full0 + 8u * sidx, (uint32_t)((k / NS) & 1))) {
+                atomicOr(&g_status, kStatusConsumerTimeout);
+                break;
+            }
+            const int base_row = r0 + k * SR;
+            const int rows_k = min(SR, r1 - base_row);
+            const uint32_t sbase = stage0 + (uint32_t)sidx * P.stage_bytes;
+            float acc[R];
 #pragma unroll
-        for (int i = 0; i < R; ++i) cur[i] = nxt[i];
+            for (int i = 0; i < R; ++i) acc[i] = 0.f;
+            const int lr0 = warp * R;
+            if (lr0 < rows_k) {
+                for (int it = 0; it < NI; ++it) {
+                    const int c = it * 32 + lane;
+                    if (c < C) {
+                        const XR<NSL> xr = load_xr<NSL>(s, C, c);
+#pragma unroll
+                        for (int i = 0; i < R; ++i) {
+                            if (lr0 + i < rows_k) {
+                                W<FMT> wv;
+                                wv.load_smem(sbase + (uint32_t)(lr0 + i) * (uint32_t)L.row_stride, L, c);
+                                acc[i] += wv.dot(xr);
+                            }
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty0 + 8u * sidx);
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(kFull, acc[i], o);
+            }
+            float out = 0.f;
+#pragma unroll
+            for (int i = 0; i < R; ++i)
+                if (lane == i) out = acc[i];
+            if (lane < R && lr0 + lane < rows_k) {
+                const int row = base_row + lr0 + lane;
+                y[row] = out;
+                if (want_argmax) best = max_ull(best, make_key(out, am.index_base + row));
+            }
+        }
     }
     if (want_argmax) {
         best = block_max_key(best, kscratch);
@@ -578,7 +864,8 @@ matmul_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__
                 ch.load(rp, L, c);
 #pragma unroll
                 for (int p = 0; p < NP; ++p)
-                    if (p < np) acc[p] += ch.dot(xs_view(smem + p * xb, L.cols), C, c);
+                    if (p < np)
+                        acc[p] += ch.dot(load_xr<W<FMT>::kSlices>(xs_view(smem + p * xb, L.cols), C, c));
             }
         }
 #pragma unroll
@@ -827,6 +1114,31 @@ unsigned grid_for(uint64_t work, int threads)
     return (unsigned)g;
 }
 
+// The dynamic shared-memory limit is per-function state: raise it once per
+// (kernel, device) to the opt-in maximum, so a later launch with less shared
+// memory never lowers it below what another shape needs.
+cudaError_t allow_max_smem(const void *fn, int dev)
+{
+    struct Entry {
+        const void *fn;
+        int dev;
+    };
+    static thread_local Entry done[64];
+    static thread_local int used = 0;
+    for (int i = 0; i < used; ++i)
+        if (done[i].fn == fn && done[i].dev == dev) return cudaSuccess;
+    int optin = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    cudaFuncAttributes attr;
+    e = cudaFuncGetAttributes(&attr, fn);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)attr.sharedSizeBytes);
+    if (e != cudaSuccess) return e;
+    if (used < 64) done[used++] = Entry{fn, dev};
+    return cudaSuccess;
+}
+
 // Per-thread cache of (device, kernel, shared bytes) -> resident CTAs per SM.
 template <typename K>
 cudaError_t prepare(K kernel, size_t smem, int *blocks_per_sm)
@@ -848,7 +1160,7 @@ cudaError_t prepare(K kernel, size_t smem, int *blocks_per_sm)
             return cudaSuccess;
         }
     }
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    e = allow_max_smem((const void *)kernel, dev);
     if (e != cudaSuccess) return e;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, kernel, kThreads, smem);
     if (e != cudaSuccess) return e;
@@ -878,10 +1190,59 @@ cudaError_t gemv_go(const Layout &L, const uint8_t *w, const float *x, float *y,
     return cudaGetLastError();
 }
 
+int g_gemv_path = 0;  // 0 auto, 1 direct loads, 2 TMA pipeline
+
+// Shared-memory plan of the TMA kernel; false when fewer than two stages fit.
+bool tma_plan(const Layout &L, TmaPlan *P)
+{
+    constexpr uint32_t kBudget = 227u * 1024u - 1024u;  // dynamic bytes, leaving static room
+    constexpr uint32_t kStageTarget = 48u * 1024u;
+    const uint32_t xb = (uint32_t)((xs_bytes(L.cols) + 127) & ~(size_t)127);
+    if (xb >= kBudget) return false;
+    int R = 2;
+    uint64_t sb = (uint64_t)kConsumerWarps * R * L.row_stride;
+    if (sb > kStageTarget) {
+        R = 1;
+        sb = (uint64_t)kConsumerWarps * L.row_stride;
+    }
+    sb = (sb + 127) & ~127ull;
+    const uint64_t ns = (kBudget - xb) / sb;
+    if (ns < 2) return false;
+    P->x_bytes = xb;
+    P->stage_bytes = (uint32_t)sb;
+    P->rows_per_stage = kConsumerWarps * R;
+    P->stages = (int)(ns > 8 ? 8 : ns);
+    return true;
+}
+
+template <uint32_t FMT, int R>
+cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, const float *x, float *y,
+                        const ArgmaxOut *am, cudaStream_t s)
+{
+    auto kernel = gemv_tma_kernel<FMT, R>;
+    const size_t smem = (size_t)P.x_bytes + (size_t)P.stages * P.stage_bytes;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    e = allow_max_smem((const void *)kernel, dev);
+    if (e != cudaSuccess) return e;
+    long long grid = sm_count();
+    if (grid > L.rows) grid = L.rows;
+    ArgmaxOut a = am ? *am : ArgmaxOut{nullptr, nullptr, 0};
+    kernel<<<(unsigned)grid, kTmaThreads, smem, s>>>(L, w, x, y, a, am ? 1 : 0, P);
+    return cudaGetLastError();
+}
+
 template <uint32_t FMT>
 cudaError_t gemv_fmt(const Layout &L, const uint8_t *w, const float *x, float *y, const ArgmaxOut *am,
                      cudaStream_t s)
 {
+    TmaPlan P;
+    if (g_gemv_path != 1 && tma_plan(L, &P)) {
+        if (P.rows_per_stage == 2 * kConsumerWarps) return gemv_tma_go<FMT, 2>(L, P, w, x, y, am, s);
+        return gemv_tma_go<FMT, 1>(L, P, w, x, y, am, s);
+    }
+    if (g_gemv_path == 2) return cudaErrorInvalidConfiguration;
     // 16-lane groups for short rows, whole warps otherwise; two rows per group
     // share each x slice load.
     if (L.C <= 16) return gemv_go<FMT, 16, 2>(L, w, x, y, am, s);
@@ -1046,6 +1407,18 @@ cudaError_t launch_matmul(const Layout &L, const uint8_t *w, const float *X, int
     case kQ6_K: return matmul_fmt<kQ6_K>(L, w, X, batch, Y, s);
     default: return cudaErrorInvalidValue;
     }
+}
+
+void set_gemv_path(int path) { g_gemv_path = path; }
+
+cudaError_t read_status(unsigned int *out, bool clear)
+{
+    cudaError_t e = cudaMemcpyFromSymbol(out, g_status, sizeof(unsigned int));
+    if (e == cudaSuccess && clear) {
+        const unsigned int zero = 0u;
+        e = cudaMemcpyToSymbol(g_status, &zero, sizeof(unsigned int));
+    }
+    return e;
 }
 
 cudaError_t launch_argmax(const float *logits, int n, const ArgmaxOut &am, cudaStream_t s)

@@ -31,6 +31,15 @@ def to_dev(torch, a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
+@pytest.fixture(params=[0, 1], ids=["auto", "loads"])
+def gemv_path(request, qmv):
+    """Run a test with the automatic kernel choice (TMA pipeline where its
+    stages fit) and with the direct-load kernel forced."""
+    qmv.set_gemv_path(request.param)
+    yield request.param
+    qmv.set_gemv_path(0)
+
+
 def check_matvec(torch, qmv, oracle, gtype, blocks, rows, cols, x, rows_to_check=None):
     w = qmv.Weight(gtype, blocks, rows, cols)
     xd = to_dev(torch, x)
@@ -105,7 +114,7 @@ def test_dequant_reference_known_blocks(cuda, qmv, oracle):
     (Q6_K, 1, 256), (Q6_K, 17, 768), (Q6_K, 301, 3584), (Q6_K, 33, 18944),
     (Q8_0, 5, 65536),
 ])
-def test_matvec_shapes(cuda, qmv, oracle, workloads, gtype, rows, cols):
+def test_matvec_shapes(cuda, qmv, oracle, workloads, gemv_path, gtype, rows, cols):
     blocks = workloads.make_blocks(gtype, rows, cols, seed=rows + cols)
     x = workloads.make_activations(cols, seed=rows)
     check_matvec(cuda, qmv, oracle, gtype, blocks, rows, cols, x)
@@ -113,14 +122,14 @@ def test_matvec_shapes(cuda, qmv, oracle, workloads, gtype, rows, cols):
 
 @pytest.mark.parametrize("name", ["cfg0_q8_0_4864x896", "cfg1a_q4_k_18944x3584",
                                   "cfg1b_q4_k_3584x18944", "cfg3_q5_0_4864x896"])
-def test_matvec_benchmark_configs(cuda, qmv, oracle, workloads, name):
+def test_matvec_benchmark_configs(cuda, qmv, oracle, workloads, gemv_path, name):
     gtype, rows, cols = workloads.CONFIGS[name]
     blocks = workloads.make_blocks(gtype, rows, cols, seed=0)
     x = workloads.make_activations(cols, seed=0)
     check_matvec(cuda, qmv, oracle, gtype, blocks, rows, cols, x)
 
 
-def test_matvec_known_answers(cuda, qmv):
+def test_matvec_known_answers(cuda, qmv, gemv_path):
     """quantized_matvec_reference_test.cpp:44-154 on the device."""
     torch = cuda
     cases = []
@@ -243,7 +252,7 @@ def test_argmax_large_random_and_ties(cuda, qmv, oracle):
     assert int(ws[:4].view(torch.int32).item()) == 0
 
 
-def test_matvec_argmax_fused_and_sharded(cuda, qmv, oracle, workloads):
+def test_matvec_argmax_fused_and_sharded(cuda, qmv, oracle, workloads, gemv_path):
     """Fused projection + argmax on a 6000-row Q6_K matrix, whole and as
     2/3/8 row shards combined by a key max (the cross-rank combine)."""
     torch = cuda
@@ -270,3 +279,28 @@ def test_matvec_argmax_fused_and_sharded(cuda, qmv, oracle, workloads):
         assert qmv.key_to_token(max(keys)) == want
         s = oracle.row_abs_dot(Q6_K, blocks, rows, cols, x)
         assert tolerance_ok(logits.cpu().numpy(), y_ref, s, REL_TOL)[0].size == 0
+
+
+def test_tma_path_covers_benchmark_shapes(cuda, qmv, workloads):
+    """The TMA pipeline must accept every benchmark shape (path 2 fails
+    instead of falling back)."""
+    torch = cuda
+    qmv.set_gemv_path(2)
+    try:
+        for name, (gtype, rows, cols) in workloads.CONFIGS.items():
+            blocks = workloads.make_blocks(gtype, 64, cols, seed=1)
+            w = qmv.Weight(gtype, blocks, 64, cols)
+            xd = torch.zeros(cols, dtype=torch.float32, device="cuda")
+            yd = torch.empty(64, dtype=torch.float32, device="cuda")
+            w.matvec(xd.data_ptr(), yd.data_ptr())
+            torch.cuda.synchronize()
+            assert not yd.abs().sum().item(), name
+            w.free()
+    finally:
+        qmv.set_gemv_path(0)
+
+
+def test_zz_device_status_clean(cuda, qmv):
+    """No bounded pipeline wait expired during the GPU tests."""
+    cuda.cuda.synchronize()
+    assert qmv.device_status() == 0
