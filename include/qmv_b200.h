@@ -133,6 +133,20 @@ int qmv_argmax(const float *logits, int n, int index_base, uint64_t *key, void *
 int qmv_matvec_argmax(const QmvWeight *weight, const float *x, int x_count, float *logits,
                       int y_count, uint64_t *key, void *workspace, void *stream);
 
+/* Greedy argmax that allocates nothing and needs no workspace: same result
+ * as qmv_argmax, for callers that cannot call cudaMalloc -- for example a host
+ * that owns every device allocation through its own pool and gives a plugin
+ * only the logits and the key buffer.  No counterpart in the reference (its
+ * sampler runs on the host).  The scratch is a static device array of
+ * 16 + 8 * 2048 bytes, held on every GPU that loads this library until the
+ * process exits, so n is limited to QMV_ARGMAX_NOALLOC_MAX_LOGITS; larger n
+ * is rejected with an error.  The first call on a device looks up the array's
+ * device address; make that first call before any stream capture.  All calls
+ * on a device share the array: each call clears its counter first, and calls
+ * that overlap on the GPU (e.g. on concurrent streams) race. */
+#define QMV_ARGMAX_NOALLOC_MAX_LOGITS (2048 * 4096)
+int qmv_argmax_noalloc(const float *logits, int n, int index_base, uint64_t *key, void *stream);
+
 /* Host: decode a key into a token id.  Returns 0 (id = -1) for
  * QMV_KEY_NONFINITE or a key with no valid index. */
 int qmv_key_to_token(uint64_t key, int *token_id);

@@ -44,7 +44,7 @@ C_SYMBOLS = [
     "qmv_set_device", "qmv_device_status", "qmv_set_gemv_path", "qmv_weight_upload", "qmv_weight_free", "qmv_weight_info",
     "qmv_resident_weight", "qmv_resident_release_all", "qmv_matvec", "qmv_matmul",
     "qmv_dequantize", "qmv_dequantize_raw", "qmv_argmax_workspace_bytes", "qmv_argmax",
-    "qmv_matvec_argmax", "qmv_key_to_token", "qmv_greedy_sample",
+    "qmv_matvec_argmax", "qmv_argmax_noalloc", "qmv_key_to_token", "qmv_greedy_sample",
     "qmv_quantized_tensor_matvec_f32", "qmv_quantized_tensor_matmul_f32",
 ]
 CXX_DROPIN_SYMBOLS = {
@@ -122,6 +122,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "qmv_argmax_workspace_bytes": (SZ, []),
         "qmv_argmax": (I, [P, I, I, P, P, P]),
         "qmv_matvec_argmax": (I, [P, P, I, P, I, P, P, P]),
+        "qmv_argmax_noalloc": (I, [P, I, I, P, P]),
         "qmv_key_to_token": (I, [U64, IP]),
         "qmv_greedy_sample": (I, [P, I, IP, ctypes.c_char_p, I, P]),
         "qmv_quantized_tensor_matvec_f32": (I, [VP, P, I, P, I]),
@@ -217,6 +218,16 @@ def argmax_workspace_bytes() -> int:
 def argmax(logits_dev, n: int, key_dev, workspace_dev, index_base: int = 0, stream=None):
     _check(lib().qmv_argmax(_ptr(logits_dev), n, index_base, _ptr(key_dev), _ptr(workspace_dev),
                             _ptr(stream)), "qmv_argmax")
+
+
+ARGMAX_NOALLOC_MAX_LOGITS = 2048 * 4096
+
+
+def argmax_noalloc(logits_dev, n: int, key_dev, index_base: int = 0, stream=None):
+    """Greedy argmax whose scratch is a static device array (no workspace, no
+    allocation); n <= ARGMAX_NOALLOC_MAX_LOGITS."""
+    _check(lib().qmv_argmax_noalloc(_ptr(logits_dev), n, index_base, _ptr(key_dev), _ptr(stream)),
+           "qmv_argmax_noalloc")
 
 
 def dequantize_raw(ggml_type: int, blocks_dev, block_count: int, out_dev, stream=None):

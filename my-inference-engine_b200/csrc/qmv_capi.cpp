@@ -399,6 +399,20 @@ QMV_EXPORT int qmv_matvec_argmax(const QmvWeight *w, const float *x, int x_count
     return 1;
 }
 
+QMV_EXPORT int qmv_argmax_noalloc(const float *logits, int n, int index_base, uint64_t *key, void *stream)
+{
+    if (logits == nullptr || key == nullptr) return fail("logits or key is null");
+    if (n <= 0) return fail("vocabulary size must be positive");
+    if (n > qmv::noalloc_max_logits())
+        return fail("qmv_argmax_noalloc takes at most %d logits (its static scratch holds one key per "
+                    "%d logits); use qmv_argmax with a workspace for %d",
+                    qmv::noalloc_max_logits(), qmv::noalloc_max_logits() / 2048, n);
+    if (index_base < 0 || (long long)index_base + n > (long long)INT_MAX) return fail("index range overflows int");
+    QMV_CUDA(qmv::launch_argmax_noalloc(logits, n, index_base, (unsigned long long *)key, (cudaStream_t)stream),
+             "argmax (no allocation) launch");
+    return 1;
+}
+
 QMV_EXPORT int qmv_key_to_token(uint64_t key, int *token_id)
 {
     if (token_id == nullptr) return fail("token_id is null");

@@ -79,5 +79,10 @@ void set_gemv_path(int path);
 cudaError_t read_status(unsigned int *out, bool clear);
 // Argmax key of logits[0..n).
 cudaError_t launch_argmax(const float *logits, int n, const ArgmaxOut &am, cudaStream_t s);
+// Same, with the scratch in a static device array (no allocation, no caller
+// workspace); n <= noalloc_max_logits().
+int noalloc_max_logits();
+cudaError_t launch_argmax_noalloc(const float *logits, int n, int index_base, unsigned long long *key,
+                                  cudaStream_t s);
 
 }  // namespace qmv

@@ -30,6 +30,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "qmv_internal.h"
 
 namespace qmv {
@@ -1426,6 +1428,63 @@ cudaError_t launch_argmax(const float *logits, int n, const ArgmaxOut &am, cudaS
     unsigned g = grid_for((uint64_t)n, kThreads * 4);
     if (g > (unsigned)kMaxArgmaxCtas) g = kMaxArgmaxCtas;
     argmax_kernel<<<g, kThreads, 0, s>>>(logits, n, am);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------- argmax without allocation
+//
+// For callers that cannot call cudaMalloc (a host that owns every device
+// allocation through its own pool and hands a plugin only input and output
+// buffers): the argmax scratch -- the arrival counter and one key slot per CTA
+// -- lives in this file-scope device array instead of a caller workspace.
+// One CTA covers kNoAllocLogitsPerCta logits, so the array bounds a call at
+// kNoAllocMaxLogits logits.  Every GPU that loads the library holds the array
+// until the process exits.  All calls on a device share it and it keeps the
+// last call's contents: each call clears the counter first, and calls that
+// overlap on the GPU (concurrent streams) race on it.
+
+namespace {
+constexpr int kNoAllocMaxCtas = 2048;
+constexpr int kNoAllocLogitsPerCta = 4096;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[16 + 8 * kNoAllocMaxCtas];
+
+std::mutex g_noalloc_mutex;
+void *g_noalloc_ptr[256];  // device address of g_noalloc_scratch per device
+}  // namespace
+
+int noalloc_max_logits() { return kNoAllocMaxCtas * kNoAllocLogitsPerCta; }
+
+// Device address of the scratch array on the current device.  Host code only
+// knows a host-side stand-in for the symbol, so the address is looked up once
+// per device (with that device current) and cached.
+static cudaError_t noalloc_scratch(void **out)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 256) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return cudaSuccess;
+}
+
+cudaError_t launch_argmax_noalloc(const float *logits, int n, int index_base, unsigned long long *key,
+                                  cudaStream_t s)
+{
+    if (n <= 0 || n > noalloc_max_logits()) return cudaErrorInvalidValue;
+    void *scratch = nullptr;
+    cudaError_t e = noalloc_scratch(&scratch);
+    if (e != cudaSuccess) return e;
+    e = cudaMemsetAsync(scratch, 0, 16, s);  // arrival counter starts at zero
+    if (e != cudaSuccess) return e;
+    const unsigned g = (unsigned)((n + kNoAllocLogitsPerCta - 1) / kNoAllocLogitsPerCta);
+    argmax_kernel<<<g, kThreads, 0, s>>>(logits, n, ArgmaxOut{key, scratch, index_base});
     return cudaGetLastError();
 }
 
