@@ -172,19 +172,15 @@ __device__ void finish_argmax(unsigned long long cta_key, const ArgmaxOut &am,
 // that starts at position p (a multiple of 16).
 template <uint32_t FMT> struct Slices;
 template <> struct Slices<kQ8_0> {
-    static constexpr int kPerChunk = 2;
     static __device__ __forceinline__ int index(int p, int C) { return ((p >> 4) & 1) * C + (p >> 5); }
 };
 template <> struct Slices<kQ5_0> {
-    static constexpr int kPerChunk = 2;
     static __device__ __forceinline__ int index(int p, int C) { return ((p >> 4) & 1) * C + (p >> 5); }
 };
 template <> struct Slices<kQ4_K> {
-    static constexpr int kPerChunk = 4;
     static __device__ __forceinline__ int index(int p, int C) { return ((p >> 4) & 3) * C + (p >> 6); }
 };
 template <> struct Slices<kQ6_K> {
-    static constexpr int kPerChunk = 4;
     static __device__ __forceinline__ int index(int p, int C)
     {
         return ((p >> 5) & 3) * C + 2 * (p >> 7) + ((p >> 4) & 1);
@@ -225,7 +221,7 @@ __device__ __forceinline__ XS xs_view(const uint8_t *base, int cols)
 
 // Quantize x[0..cols) into shared memory (every thread of the CTA takes part;
 // 8 consecutive lanes own one 32-element block, 4 lanes one 16-element slice).
-template <uint32_t FMT>
+template <uint32_t FMT, int NT = kThreads>
 __device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t *base)
 {
     uint8_t *hi = base;
@@ -233,18 +229,18 @@ __device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t
     float2 *rec = reinterpret_cast<float2 *>(base + 2 * cols);
     const int n4 = cols >> 2;
     constexpr int U = 8;
-    for (int it0 = 0; it0 * kThreads < n4; it0 += U) {
+    for (int it0 = 0; it0 * NT < n4; it0 += U) {
         float4 v[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            int f = (it0 + u) * kThreads + threadIdx.x;
+            int f = (it0 + u) * NT + threadIdx.x;
             v[u] = f < n4 ? __ldg(reinterpret_cast<const float4 *>(x) + f)
                           : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            if ((it0 + u) * kThreads >= n4) break;  // uniform across the CTA
-            const int f = (it0 + u) * kThreads + threadIdx.x;
+            if ((it0 + u) * NT >= n4) break;  // uniform across the CTA
+            const int f = (it0 + u) * NT + threadIdx.x;
             uint32_t a = max(max(__float_as_uint(fabsf(v[u].x)), __float_as_uint(fabsf(v[u].y))),
                              max(__float_as_uint(fabsf(v[u].z)), __float_as_uint(fabsf(v[u].w))));
             a = max(a, __shfl_xor_sync(kFull, a, 1));
@@ -442,26 +438,36 @@ template <> struct W<kQ4_K> {
         const int al0 = dot4(lb, x.l[1], dot4(la, x.l[0], 0));
         const int ah1 = dot4(ub, x.h[3], dot4(ua, x.h[2], 0));
         const int al1 = dot4(ub, x.l[3], dot4(ua, x.l[2], 0));
-        // 6-bit scale / min of sub-blocks 2g and 2g+1 (src/quantization.cpp:351-378)
+        // 6-bit scale / min of sub-blocks 2g and 2g+1 (src/quantization.cpp:351-378),
+        // computed without a branch: lanes of one warp hold different g.
+        // Sub-block j < 4: sc = b[j] & 63, m = b[j+4] & 63.  j >= 4:
+        // sc = (b[j+4] & 15) | (b[j-4] >> 6) << 4, m = (b[j+4] >> 4) | (b[j] >> 6) << 4.
         const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
-        uint32_t sc0, m0, sc1, m1;
-        if (g < 2) {
-            const int t0 = 16 * g, t1 = 16 * g + 8;
-            sc0 = (s0 >> t0) & 63u; m0 = (s1 >> t0) & 63u;
-            sc1 = (s0 >> t1) & 63u; m1 = (s1 >> t1) & 63u;
-        } else {
-            const int t0 = 16 * (g - 2), t1 = t0 + 8;
-            sc0 = ((s2 >> t0) & 15u) | ((((s0 >> t0) >> 6) & 3u) << 4);
-            m0 = (((s2 >> t0) >> 4) & 15u) | ((((s1 >> t0) >> 6) & 3u) << 4);
-            sc1 = ((s2 >> t1) & 15u) | ((((s0 >> t1) >> 6) & 3u) << 4);
-            m1 = (((s2 >> t1) >> 4) & 15u) | ((((s1 >> t1) >> 6) & 3u) << 4);
-        }
+        const int t0 = 16 * (g & 1), t1 = t0 + 8;  // byte offset of j and j+1 within a word
+        const uint32_t lo_s = g < 2 ? s0 : s2;     // word holding the low bits of sc
+        const uint32_t lo_m = g < 2 ? s1 : (s2 >> 4);
+        const uint32_t lmask = g < 2 ? 63u : 15u;
+        const uint32_t hs = g < 2 ? 0u : s0, hm = g < 2 ? 0u : s1;  // top-2-bit sources
+        const uint32_t sc0 = ((lo_s >> t0) & lmask) | ((((hs >> t0) >> 6) & 3u) << 4);
+        const uint32_t m0 = ((lo_m >> t0) & lmask) | ((((hm >> t0) >> 6) & 3u) << 4);
+        const uint32_t sc1 = ((lo_s >> t1) & lmask) | ((((hs >> t1) >> 6) & 3u) << 4);
+        const uint32_t m1 = ((lo_m >> t1) & lmask) | ((((hm >> t1) >> 6) & 3u) << 4);
         const float d = f16_fast(hdr.x), dmin = f16_fast(hdr.x >> 16);
         const float v0 = (d * (float)sc0) * (x.r[0].x * (float)(ah0 * 256 + al0)) - (dmin * (float)m0) * (x.r[0].y + x.r[1].y);
         const float v1 = (d * (float)sc1) * (x.r[2].x * (float)(ah1 * 256 + al1)) - (dmin * (float)m1) * (x.r[2].y + x.r[3].y);
         return v0 + v1;
     }
 };
+
+// Signed byte B of v as an int, in one byte-permute (sign-replicating
+// selector nibbles).
+template <int B>
+__device__ __forceinline__ int sbyte(uint32_t v)
+{
+    int r;
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(v), "n"(((8 | B) << 12) | ((8 | B) << 8) | ((8 | B) << 4) | B));
+    return r;
+}
 
 template <> struct W<kQ6_K> {
     static constexpr int kSlices = 4;
@@ -507,8 +513,8 @@ template <> struct W<kQ6_K> {
         const int A1 = dot4(w1, x.h[1], 0) * 256 + dot4(w1, x.l[1], 0);
         const int A2 = dot4(w2, x.h[2], 0) * 256 + dot4(w2, x.l[2], 0);
         const int A3 = dot4(w3, x.h[3], 0) * 256 + dot4(w3, x.l[3], 0);
-        const float s0 = (float)(int)(int8_t)(sc & 0xffu), s1 = (float)(int)(int8_t)((sc >> 8) & 0xffu);
-        const float s2 = (float)(int)(int8_t)((sc >> 16) & 0xffu), s3 = (float)(int)(int8_t)(sc >> 24);
+        const float s0 = (float)sbyte<0>(sc), s1 = (float)sbyte<1>(sc);
+        const float s2 = (float)sbyte<2>(sc), s3 = (float)sbyte<3>(sc);
         float acc = s0 * (x.r[0].x * (float)A0 - 32.f * x.r[0].y);
         acc += s1 * (x.r[1].x * (float)A1 - 32.f * x.r[1].y);
         acc += s2 * (x.r[2].x * (float)A2 - 32.f * x.r[2].y);
@@ -534,7 +540,7 @@ __global__ void __launch_bounds__(kThreads)
 gemv_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x,
             float *__restrict__ y, ArgmaxOut am, int want_argmax)
 {
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem[];
     __shared__ unsigned long long kscratch[kThreads / 32];
     constexpr int NSL = W<FMT>::kSlices;
 
@@ -636,8 +642,7 @@ gemv_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x
 // still waits (again bounded) for the copies it has in flight before the CTA
 // exits.
 
-constexpr int kConsumerWarps = 8;
-constexpr int kTmaThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMaxConsumerWarps = 16;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ unsigned int g_status;
@@ -702,18 +707,21 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
 struct TmaPlan {
     uint32_t x_bytes;      // quantized x, rounded to 128
     uint32_t stage_bytes;  // rows_per_stage * row_stride, rounded to 128
-    int rows_per_stage;    // kConsumerWarps * R
+    int rows_per_stage;    // CW * R
     int stages;            // NS
+    int consumer_warps;    // CW
+    int rows_per_warp;     // R
 };
 
-template <uint32_t FMT, int R>
-__global__ void __launch_bounds__(kTmaThreads, 1)
+template <uint32_t FMT, int CW, int R>
+__global__ void __launch_bounds__((CW + 1) * 32, 1)
 gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x,
                 float *__restrict__ y, ArgmaxOut am, int want_argmax, TmaPlan P)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) unsigned long long bars[2 * 8];
-    __shared__ unsigned long long kscratch[kTmaThreads / 32];
+    __shared__ unsigned long long kscratch[kMaxConsumerWarps + 1];
+    constexpr int kConsumerWarps = CW;
     constexpr int NSL = W<FMT>::kSlices;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int C = L.C;
@@ -773,7 +781,7 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
         }
     } else {
         // ---------------- consumers
-        quantize_x<FMT>(x, L.cols, C, smem);
+        quantize_x<FMT, CW * 32>(x, L.cols, C, smem);
         asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
         const XS s = xs_view(smem, L.cols);
         const int NI = (C + 31) >> 5;
@@ -794,15 +802,16 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
                 for (int it = 0; it < NI; ++it) {
                     const int c = it * 32 + lane;
                     if (c < C) {
+                        // All R rows are loaded without a row guard: the stage
+                        // buffer holds CW * R rows, so rows past rows_k read
+                        // in-bounds (stale) bytes whose sums are never written.
+                        W<FMT> wv[R];
+#pragma unroll
+                        for (int i = 0; i < R; ++i)
+                            wv[i].load_smem(sbase + (uint32_t)(lr0 + i) * (uint32_t)L.row_stride, L, c);
                         const XR<NSL> xr = load_xr<NSL>(s, C, c);
 #pragma unroll
-                        for (int i = 0; i < R; ++i) {
-                            if (lr0 + i < rows_k) {
-                                W<FMT> wv;
-                                wv.load_smem(sbase + (uint32_t)(lr0 + i) * (uint32_t)L.row_stride, L, c);
-                                acc[i] += wv.dot(xr);
-                            }
-                        }
+                        for (int i = 0; i < R; ++i) acc[i] += wv[i].dot(xr);
                     }
                 }
             }
@@ -841,7 +850,7 @@ __global__ void __launch_bounds__(kThreads)
 matmul_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ X, int np,
               float *__restrict__ Y)
 {
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem[];
     const int C = L.C;
     const size_t xb = xs_bytes(L.cols);
     for (int p = 0; p < np; ++p) quantize_x<FMT>(X + (size_t)p * L.cols, L.cols, C, smem + p * xb);
@@ -1194,34 +1203,37 @@ cudaError_t gemv_go(const Layout &L, const uint8_t *w, const float *x, float *y,
 
 int g_gemv_path = 0;  // 0 auto, 1 direct loads, 2 TMA pipeline
 
-// Shared-memory plan of the TMA kernel; false when fewer than two stages fit.
+// Shared-memory plan of the TMA kernel: the first of these (consumer warps,
+// rows per warp, minimum stages) whose stages fit.  Two rows per warp share
+// each x slice load, so they come first; 16 warps hide shared-memory latency
+// better than 8.  false when none fits (the direct-load kernel runs).
 bool tma_plan(const Layout &L, TmaPlan *P)
 {
     constexpr uint32_t kBudget = 227u * 1024u - 1024u;  // dynamic bytes, leaving static room
-    constexpr uint32_t kStageTarget = 48u * 1024u;
+    static const int kCandidates[][3] = {{16, 2, 2}, {8, 2, 3}, {16, 1, 3}, {8, 2, 2}, {16, 1, 2}, {8, 1, 2}};
     const uint32_t xb = (uint32_t)((xs_bytes(L.cols) + 127) & ~(size_t)127);
     if (xb >= kBudget) return false;
-    int R = 2;
-    uint64_t sb = (uint64_t)kConsumerWarps * R * L.row_stride;
-    if (sb > kStageTarget) {
-        R = 1;
-        sb = (uint64_t)kConsumerWarps * L.row_stride;
+    for (const auto &cand : kCandidates) {
+        const int cw = cand[0], r = cand[1], min_stages = cand[2];
+        const uint64_t sb = ((uint64_t)cw * r * L.row_stride + 127) & ~127ull;
+        const uint64_t ns = (kBudget - xb) / sb;
+        if ((int)ns < min_stages) continue;
+        P->x_bytes = xb;
+        P->stage_bytes = (uint32_t)sb;
+        P->rows_per_stage = cw * r;
+        P->stages = (int)(ns > 8 ? 8 : ns);
+        P->consumer_warps = cw;
+        P->rows_per_warp = r;
+        return true;
     }
-    sb = (sb + 127) & ~127ull;
-    const uint64_t ns = (kBudget - xb) / sb;
-    if (ns < 2) return false;
-    P->x_bytes = xb;
-    P->stage_bytes = (uint32_t)sb;
-    P->rows_per_stage = kConsumerWarps * R;
-    P->stages = (int)(ns > 8 ? 8 : ns);
-    return true;
+    return false;
 }
 
-template <uint32_t FMT, int R>
+template <uint32_t FMT, int CW, int R>
 cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, const float *x, float *y,
                         const ArgmaxOut *am, cudaStream_t s)
 {
-    auto kernel = gemv_tma_kernel<FMT, R>;
+    auto kernel = gemv_tma_kernel<FMT, CW, R>;
     const size_t smem = (size_t)P.x_bytes + (size_t)P.stages * P.stage_bytes;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -1231,7 +1243,7 @@ cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, con
     long long grid = sm_count();
     if (grid > L.rows) grid = L.rows;
     ArgmaxOut a = am ? *am : ArgmaxOut{nullptr, nullptr, 0};
-    kernel<<<(unsigned)grid, kTmaThreads, smem, s>>>(L, w, x, y, a, am ? 1 : 0, P);
+    kernel<<<(unsigned)grid, (CW + 1) * 32, smem, s>>>(L, w, x, y, a, am ? 1 : 0, P);
     return cudaGetLastError();
 }
 
@@ -1241,8 +1253,12 @@ cudaError_t gemv_fmt(const Layout &L, const uint8_t *w, const float *x, float *y
 {
     TmaPlan P;
     if (g_gemv_path != 1 && tma_plan(L, &P)) {
-        if (P.rows_per_stage == 2 * kConsumerWarps) return gemv_tma_go<FMT, 2>(L, P, w, x, y, am, s);
-        return gemv_tma_go<FMT, 1>(L, P, w, x, y, am, s);
+        if (P.consumer_warps == 16) {
+            if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 16, 2>(L, P, w, x, y, am, s);
+            return gemv_tma_go<FMT, 16, 1>(L, P, w, x, y, am, s);
+        }
+        if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 8, 2>(L, P, w, x, y, am, s);
+        return gemv_tma_go<FMT, 8, 1>(L, P, w, x, y, am, s);
     }
     if (g_gemv_path == 2) return cudaErrorInvalidConfiguration;
     // 16-lane groups for short rows, whole warps otherwise; two rows per group
