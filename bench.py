@@ -272,33 +272,44 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     qmv = load_qmv()
     qmv.set_device(local_rank)
+    sh = _load("qmv_sharding", os.path.join(PKG, "sharding.py"))
     dev = torch.device("cuda", local_rank)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     props = torch.cuda.get_device_properties(local_rank)
     l2 = getattr(props, "L2_cache_size", 126 * 1024 * 1024) or 126 * 1024 * 1024
     wl = workloads()
+    p2p = world > 1 and args.exchange == "p2p"
 
-    b, e, per = shard(rank, world)
+    b, e, per = sh.shard_rows(VOCAB_ROWS, world, rank)
     rows = e - b
-    per_pad = (per + 3) // 4 * 4
     blocks = wl.make_blocks(Q6_K, VOCAB_ROWS, HIDDEN, seed=0, row_begin=b, row_end=e)
     copies = copies_for(vocab_bytes(rows), l2)
-    weights = [qmv.Weight(Q6_K, blocks, e - b, HIDDEN) for _ in range(copies)]
+    weights = [qmv.Weight.from_row_slice(Q6_K, blocks, VOCAB_ROWS, HIDDEN, b) for _ in range(copies)]
+    del blocks
     x_host = wl.make_activations(HIDDEN, seed=0)
     x_dev = torch.from_numpy(x_host).to(dev)
-    stride = per_pad + 2  # logits slice + 8-byte key, one all-gather
-    sendbuf = torch.zeros(stride, dtype=torch.float32, device=dev)
-    gathered = torch.zeros(world * stride, dtype=torch.float32, device=dev)
-    keyview = sendbuf[per_pad:per_pad + 2].view(torch.int64)
     ws = torch.zeros(qmv.argmax_workspace_bytes(), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
+    # NCCL mode: one all-gather of {logit slice, 8-byte key} per rank
+    per_pad = (per + 3) // 4 * 4
+    stride = per_pad + 2
+    sendbuf = torch.zeros(stride, dtype=torch.float32, device=dev)
+    gathered = torch.zeros(world * stride, dtype=torch.float32, device=dev)
+    keyview = sendbuf[per_pad:per_pad + 2].view(torch.int64)
     SIGN = torch.tensor(-(1 << 63), dtype=torch.int64, device=dev)
+    # p2p mode: fused kernel, exchange over peer memory
+    group = sh.ExchangeGroup(qmv, rank, world, per) if p2p else None
+    gkey = torch.zeros(1, dtype=torch.int64, device=dev)
 
-    def combine():
-        keys = gathered.view(world, stride)[:, per_pad:per_pad + 2].contiguous().view(torch.int64).view(-1)
-        return torch.bitwise_xor(torch.bitwise_xor(keys, SIGN).max(), SIGN)
+    def global_key():
+        if p2p:
+            return int(gkey.item()) & 0xFFFFFFFFFFFFFFFF
+        if world > 1:
+            keys = gathered.view(world, stride)[:, per_pad:per_pad + 2].contiguous().view(torch.int64).view(-1)
+            return int(torch.bitwise_xor(torch.bitwise_xor(keys, SIGN).max(), SIGN).item()) & 0xFFFFFFFFFFFFFFFF
+        return int(keyview.item()) & 0xFFFFFFFFFFFFFFFF
 
     kstart = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     kend = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -307,19 +318,19 @@ def run_b200(args, rank, world, local_rank):
         w = weights[i % copies]
         if timed:
             kstart[i].record(stream)
-        w.matvec_argmax(x_dev.data_ptr(), sendbuf.data_ptr(), keyview.data_ptr(), ws.data_ptr(), sptr)
+        if p2p:
+            w.matvec_argmax_exchange(x_dev.data_ptr(), rank, world, group.buffers, per, group.next_epoch(),
+                                     gkey.data_ptr(), ws.data_ptr(), sptr)
+        else:
+            w.matvec_argmax(x_dev.data_ptr(), sendbuf.data_ptr(), keyview.data_ptr(), ws.data_ptr(), sptr)
         if timed:
             kend[i].record(stream)
-        if world > 1:
+        if world > 1 and not p2p:
             dist.all_gather_into_tensor(gathered, sendbuf)
 
-    # correctness gate before timing: the fused kernel's token on this input
+    # correctness gate before timing: the token of this input
     step(0, False)
-    if world > 1:
-        tok_key = int(combine().item()) & 0xFFFFFFFFFFFFFFFF
-    else:
-        tok_key = int(keyview.item()) & 0xFFFFFFFFFFFFFFFF
-    token = qmv.key_to_token(tok_key)
+    token = qmv.key_to_token(global_key())
 
     for i in range(args.warmup):
         step(i, False)
@@ -357,23 +368,32 @@ def run_b200(args, rank, world, local_rank):
 
     # ---- end to end through the C ABI with host buffers (pinned)
     x_pin = torch.from_numpy(x_host).pin_memory()
-    out_pin = torch.empty(world * stride, dtype=torch.float32).pin_memory()
+    out_floats = world * per if p2p else world * stride
+    out_pin = torch.empty(out_floats, dtype=torch.float32).pin_memory()
+    key_pin = torch.empty(1, dtype=torch.int64).pin_memory()
     e2e_steps = max(3, min(args.steps, 200))
+
     def e2e_step(i):
         x_dev.copy_(x_pin, non_blocking=True)
-        w = weights[i % copies]
-        w.matvec_argmax(x_dev.data_ptr(), sendbuf.data_ptr(), keyview.data_ptr(), ws.data_ptr(), sptr)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, sendbuf)
-            if rank == 0:
+        step(i, False)
+        if rank == 0:
+            if p2p:
+                key_pin.copy_(gkey, non_blocking=True)
+                # gathered logits, out of the library-owned exchange buffer (same stream)
+                qmv.memcpy(out_pin.data_ptr(), qmv.exchange_logits(group.own, world, per, group.epoch),
+                           4 * out_floats, sptr)
+            elif world > 1:
                 out_pin.copy_(gathered, non_blocking=True)
-        else:
-            out_pin[:stride].copy_(sendbuf, non_blocking=True)
+            else:
+                out_pin[:stride].copy_(sendbuf, non_blocking=True)
         stream.synchronize()
         if rank == 0:
+            if p2p:
+                return qmv.key_to_token(int(key_pin.numpy().view(np.uint64)[0]))
             keys = out_pin.numpy().reshape(world, stride)[:, per_pad:per_pad + 2].copy().view(np.uint64)
             return qmv.key_to_token(int(keys.max()))
         return None
+
     for i in range(2):
         e2e_step(i)
     if world > 1:
@@ -391,6 +411,7 @@ def run_b200(args, rank, world, local_rank):
     if world > 1:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_ms = float(e2e_ms[0])
+    status = qmv.device_status()
 
     step_bytes = vocab_bytes(VOCAB_ROWS) + world * 4 * HIDDEN + 4 * VOCAB_ROWS
     value = args.steps * step_bytes / (ms * 1e-3) / 1e9
@@ -404,6 +425,12 @@ def run_b200(args, rank, world, local_rank):
         traffic = profile_traffic("gemv_q6_k_cfg2")
         if traffic is not None:
             traffic = traffic * rows / VOCAB_ROWS
+        if world == 1:
+            par = "row-shard x1"
+        elif p2p:
+            par = f"row-shard x{world}, fused exchange over peer memory (NVLink)"
+        else:
+            par = f"row-shard x{world} + NCCL all-gather"
         result = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
@@ -412,23 +439,26 @@ def run_b200(args, rank, world, local_rank):
             "tokens_per_s": round(args.steps / (ms * 1e-3), 1),
             "token": token,
             "config": {"workload": "cfg2_q6_k_vocab_projection_argmax", "rows": VOCAB_ROWS, "cols": HIDDEN,
-                       "ggml_type": "Q6_K", "parallelism": f"row-shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
-                       "rows_per_rank": per, "l2_defeat": f"{copies} rotating weight copies per rank (>= 2.5x L2)"},
+                       "ggml_type": "Q6_K", "parallelism": par, "rows_per_rank": per,
+                       "l2_defeat": f"{copies} rotating weight copies per rank (>= 2.5x L2)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": "gemv_kernel<Q6_K> fused argmax", "kernel_ms": round(kms_max, 5),
-                         "peak_source": peak_kind},
+                         "kernel": "gemv_tma_kernel<Q6_K> fused argmax" + (" + exchange" if p2p else ""),
+                         "kernel_ms": round(kms_max, 5), "peak_source": peak_kind},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * HIDDEN,
-                    "d2h_bytes_per_step": 4 * world * stride, "steps": e2e_steps,
+                    "d2h_bytes_per_step": 4 * out_floats + (8 if p2p else 0), "steps": e2e_steps,
                     "tokens_per_s": round(e2e_steps / (e2e_ms * 1e-3), 1), "token": e2e_tok},
             "gpu_launches": args.steps,
             "clocks": clock_info,
+            "device_status": status,
         }
     for wobj in weights:
         wobj.free()
     del weights
     if world > 1:
         dist.barrier()
+        if group is not None:
+            group.close()
         dist.destroy_process_group()
     return result
 
@@ -509,6 +539,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1: fused peer-memory exchange (default) or a separate NCCL all-gather")
     ap.add_argument("--only", default=None,
                     help="run one secondary configuration only (e.g. cfg1a_q4_k_18944x3584, "
                          "cfg3_q5_0_4864x896_P512) for --steps calls; used for profiling")

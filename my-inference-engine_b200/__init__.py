@@ -44,7 +44,9 @@ C_SYMBOLS = [
     "qmv_set_device", "qmv_device_status", "qmv_set_gemv_path", "qmv_weight_upload", "qmv_weight_free", "qmv_weight_info",
     "qmv_resident_weight", "qmv_resident_release_all", "qmv_matvec", "qmv_matmul",
     "qmv_dequantize", "qmv_dequantize_raw", "qmv_argmax_workspace_bytes", "qmv_argmax",
-    "qmv_matvec_argmax", "qmv_argmax_noalloc", "qmv_key_to_token", "qmv_greedy_sample",
+    "qmv_matvec_argmax", "qmv_exchange_bytes", "qmv_ipc_alloc", "qmv_ipc_open", "qmv_ipc_close",
+    "qmv_ipc_free", "qmv_memcpy", "qmv_exchange_logits", "qmv_matvec_argmax_exchange",
+    "qmv_argmax_noalloc", "qmv_key_to_token", "qmv_greedy_sample",
     "qmv_quantized_tensor_matvec_f32", "qmv_quantized_tensor_matmul_f32",
 ]
 CXX_DROPIN_SYMBOLS = {
@@ -123,6 +125,14 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "qmv_argmax": (I, [P, I, I, P, P, P]),
         "qmv_matvec_argmax": (I, [P, P, I, P, I, P, P, P]),
         "qmv_argmax_noalloc": (I, [P, I, I, P, P]),
+        "qmv_exchange_bytes": (I, [I, I, ctypes.POINTER(SZ)]),
+        "qmv_ipc_alloc": (I, [SZ, ctypes.POINTER(P), P]),
+        "qmv_ipc_open": (I, [P, ctypes.POINTER(P)]),
+        "qmv_ipc_close": (I, [P]),
+        "qmv_ipc_free": (I, [P]),
+        "qmv_exchange_logits": (I, [P, I, I, U32, ctypes.POINTER(P)]),
+        "qmv_memcpy": (I, [P, P, SZ, P]),
+        "qmv_matvec_argmax_exchange": (I, [P, P, I, I, I, ctypes.POINTER(P), I, U32, P, P, P]),
         "qmv_key_to_token": (I, [U64, IP]),
         "qmv_greedy_sample": (I, [P, I, IP, ctypes.c_char_p, I, P]),
         "qmv_quantized_tensor_matvec_f32": (I, [VP, P, I, P, I]),
@@ -250,6 +260,46 @@ def set_gemv_path(path: int):
     _check(lib().qmv_set_gemv_path(path), "qmv_set_gemv_path")
 
 
+def exchange_bytes(world: int, slot_rows: int) -> int:
+    n = ctypes.c_size_t(0)
+    _check(lib().qmv_exchange_bytes(world, slot_rows, ctypes.byref(n)), "qmv_exchange_bytes")
+    return n.value
+
+
+def ipc_alloc(nbytes: int):
+    """(device pointer, 64-byte IPC handle) of a zeroed exchange buffer."""
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(64)
+    _check(lib().qmv_ipc_alloc(nbytes, ctypes.byref(ptr), handle), "qmv_ipc_alloc")
+    return ptr.value, handle.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    ptr = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(handle, 64)
+    _check(lib().qmv_ipc_open(buf, ctypes.byref(ptr)), "qmv_ipc_open")
+    return ptr.value
+
+
+def ipc_close(ptr: int):
+    _check(lib().qmv_ipc_close(ptr), "qmv_ipc_close")
+
+
+def ipc_free(ptr: int):
+    _check(lib().qmv_ipc_free(ptr), "qmv_ipc_free")
+
+
+def memcpy(dst, src, nbytes: int, stream=None):
+    """Synchronous copy between any host/device addresses (unified addressing)."""
+    _check(lib().qmv_memcpy(_ptr(dst), _ptr(src), nbytes, _ptr(stream)), "qmv_memcpy")
+
+
+def exchange_logits(buffer: int, world: int, slot_rows: int, epoch: int) -> int:
+    out = ctypes.c_void_p()
+    _check(lib().qmv_exchange_logits(buffer, world, slot_rows, epoch, ctypes.byref(out)), "qmv_exchange_logits")
+    return out.value
+
+
 def set_device(device: int):
     _check(lib().qmv_set_device(device), "qmv_set_device")
 
@@ -277,6 +327,29 @@ class Weight:
                                        ctypes.byref(h)), "qmv_weight_upload")
         self.handle = h
         self._blocks = None  # the device copy is independent of the host bytes
+
+    @classmethod
+    def from_row_slice(cls, ggml_type: int, slice_blocks: np.ndarray, rows_total: int, cols: int,
+                       row_begin: int) -> "Weight":
+        """Upload rows [row_begin, row_begin + len) of a rows_total x cols matrix
+        when only those rows' packed bytes are in memory (a rank's shard).  The
+        weight keeps global row indices (argmax keys, exchange slots)."""
+        blocks = np.ascontiguousarray(slice_blocks, dtype=np.uint8)
+        row_bytes = (cols // BLOCK_ELEMENTS[ggml_type]) * BLOCK_BYTES[ggml_type]
+        n = blocks.size // row_bytes
+        self = cls.__new__(cls)
+        self._blocks = blocks
+        # the view's base is placed so that row `row_begin` is the slice's first
+        # byte; only rows [row_begin, row_begin + n) are ever read
+        self.view = make_view(ggml_type, blocks.ctypes.data - row_begin * row_bytes, rows_total, cols)
+        self.ggml_type, self.cols = ggml_type, cols
+        self.row_begin, self.row_end, self.rows = row_begin, row_begin + n, n
+        h = ctypes.c_void_p()
+        _check(lib().qmv_weight_upload(ctypes.byref(self.view), row_begin, row_begin + n, ctypes.byref(h)),
+               "qmv_weight_upload")
+        self.handle = h
+        self._blocks = None
+        return self
 
     def free(self):
         if self.handle:
@@ -310,6 +383,16 @@ class Weight:
         _check(lib().qmv_matvec_argmax(self.handle, _ptr(x_dev), self.cols, _ptr(logits_dev),
                                        self.rows, _ptr(key_dev), _ptr(workspace_dev),
                                        _ptr(stream)), "qmv_matvec_argmax")
+
+    def matvec_argmax_exchange(self, x_dev, rank: int, world: int, buffers, slot_rows: int, epoch: int,
+                               key_dev, workspace_dev, stream=None):
+        """Fused row-shard projection + argmax + exchange over peer memory
+        (qmv_matvec_argmax_exchange); `buffers` lists every rank's exchange
+        buffer pointer as seen from this process."""
+        arr = (ctypes.c_void_p * world)(*buffers)
+        _check(lib().qmv_matvec_argmax_exchange(self.handle, _ptr(x_dev), self.cols, rank, world, arr,
+                                                slot_rows, epoch, _ptr(key_dev), _ptr(workspace_dev),
+                                                _ptr(stream)), "qmv_matvec_argmax_exchange")
 
     def dequantize(self, out_dev, stream=None):
         _check(lib().qmv_dequantize(self.handle, _ptr(out_dev), self.rows * self.cols,

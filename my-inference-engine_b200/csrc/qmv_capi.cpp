@@ -413,6 +413,107 @@ QMV_EXPORT int qmv_argmax_noalloc(const float *logits, int n, int index_base, ui
     return 1;
 }
 
+QMV_EXPORT int qmv_exchange_bytes(int world, int slot_rows, size_t *bytes)
+{
+    if (bytes == nullptr) return fail("bytes pointer is null");
+    if (world < 2 || world > qmv::kMaxPeers) return fail("world must be 2..%d", qmv::kMaxPeers);
+    if (slot_rows <= 0) return fail("slot_rows must be positive");
+    *bytes = 2 * qmv::exchange_parity_bytes(world, slot_rows);
+    return 1;
+}
+
+QMV_EXPORT int qmv_ipc_alloc(size_t bytes, void **dev_ptr, void *handle)
+{
+    if (dev_ptr == nullptr || handle == nullptr || bytes == 0) return fail("bad arguments");
+    *dev_ptr = nullptr;
+    void *p = nullptr;
+    QMV_CUDA(cudaMalloc(&p, bytes), "cudaMalloc(exchange buffer)");
+    cudaError_t e = cudaMemset(p, 0, bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail("exchange buffer", e);
+    }
+    memcpy(handle, &h, sizeof h);
+    *dev_ptr = p;
+    return 1;
+}
+
+QMV_EXPORT int qmv_ipc_open(const void *handle, void **dev_ptr)
+{
+    if (dev_ptr == nullptr || handle == nullptr) return fail("bad arguments");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    QMV_CUDA(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    return 1;
+}
+
+QMV_EXPORT int qmv_ipc_close(void *dev_ptr)
+{
+    QMV_CUDA(cudaIpcCloseMemHandle(dev_ptr), "cudaIpcCloseMemHandle");
+    return 1;
+}
+
+QMV_EXPORT int qmv_ipc_free(void *dev_ptr)
+{
+    QMV_CUDA(cudaFree(dev_ptr), "cudaFree(exchange buffer)");
+    return 1;
+}
+
+QMV_EXPORT int qmv_memcpy(void *dst, const void *src, size_t bytes, void *stream)
+{
+    if ((dst == nullptr || src == nullptr) && bytes) return fail("dst or src is null");
+    QMV_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, (cudaStream_t)stream), "cudaMemcpyAsync");
+    QMV_CUDA(cudaStreamSynchronize((cudaStream_t)stream), "cudaStreamSynchronize");
+    return 1;
+}
+
+QMV_EXPORT int qmv_exchange_logits(void *buffer, int world, int slot_rows, uint32_t epoch, float **logits)
+{
+    if (buffer == nullptr || logits == nullptr) return fail("bad arguments");
+    if (world < 2 || world > qmv::kMaxPeers || slot_rows <= 0) return fail("bad world or slot_rows");
+    *logits = (float *)((uint8_t *)buffer + (epoch & 1u) * qmv::exchange_parity_bytes(world, slot_rows));
+    return 1;
+}
+
+QMV_EXPORT int qmv_matvec_argmax_exchange(const QmvWeight *w, const float *x, int x_count, int rank, int world,
+                                          void *const *buffers, int slot_rows, uint32_t epoch, uint64_t *key,
+                                          void *workspace, void *stream)
+{
+    if (!check_weight(w)) return 0;
+    if (x == nullptr || key == nullptr || workspace == nullptr || buffers == nullptr)
+        return fail("x, key, workspace or buffers is null");
+    if (world < 2 || world > qmv::kMaxPeers) return fail("world must be 2..%d", qmv::kMaxPeers);
+    if (rank < 0 || rank >= world) return fail("rank %d outside 0..%d", rank, world - 1);
+    if (x_count != w->L.cols) return fail("x_count %d does not match %d columns", x_count, w->L.cols);
+    if (slot_rows < w->L.rows || w->row_begin != rank * slot_rows)
+        return fail("weight rows [%d, %d) are not rank %d's slot of %d rows", w->row_begin,
+                    w->row_begin + w->L.rows, rank, slot_rows);
+    if (epoch == 0) return fail("epoch must be positive");
+    if (!aligned16(x)) return fail("x must be 16-byte aligned");
+    const size_t pb = qmv::exchange_parity_bytes(world, slot_rows);
+    const size_t keys_off = ((size_t)world * slot_rows * 4 + 255) & ~(size_t)255;
+    const size_t flags_off = keys_off + (((size_t)world * 8 + 255) & ~(size_t)255);
+    qmv::Exchange ex{};
+    ex.world = world;
+    ex.rank = rank;
+    ex.epoch = epoch;
+    ex.slot_rows = slot_rows;
+    for (int p = 0; p < world; ++p) {
+        if (buffers[p] == nullptr) return fail("buffer of rank %d is null", p);
+        uint8_t *base = (uint8_t *)buffers[p] + (epoch & 1u) * pb;
+        ex.logits[p] = (float *)base;
+        ex.keys[p] = (unsigned long long *)(base + keys_off);
+        ex.flags[p] = (unsigned int *)(base + flags_off);
+    }
+    float *y = ex.logits[rank] + (size_t)rank * slot_rows;
+    qmv::ArgmaxOut am{(unsigned long long *)key, workspace, w->row_begin};
+    QMV_CUDA(qmv::launch_gemv_exchange(w->L, w->dev, x, y, am, ex, (cudaStream_t)stream),
+             "gemv+argmax+exchange launch");
+    return 1;
+}
+
 QMV_EXPORT int qmv_key_to_token(uint64_t key, int *token_id)
 {
     if (token_id == nullptr) return fail("token_id is null");

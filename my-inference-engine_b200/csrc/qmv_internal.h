@@ -66,9 +66,31 @@ struct ArgmaxOut {
     int index_base;           // global index of row 0
 };
 
+// Row-sharded exchange over peer memory (one node, up to kMaxPeers GPUs).
+// Each rank's exchange buffer holds two parity regions (selected by the
+// step's epoch): logits[world * slot_rows] f32 | keys[world] u64 | flags[world]
+// u32.  The pointers below are already resolved to this step's parity region
+// of every rank's buffer (own + IPC-opened peers).
+constexpr int kMaxPeers = 8;
+struct Exchange {
+    int world;  // <= 1: no exchange
+    int rank;
+    unsigned int epoch;  // > 0, increases every step
+    int slot_rows;
+    float *logits[kMaxPeers];
+    unsigned long long *keys[kMaxPeers];
+    unsigned int *flags[kMaxPeers];
+};
+size_t exchange_parity_bytes(int world, int slot_rows);
+
 // y = W x (and optionally the argmax key of y).
 cudaError_t launch_gemv(const Layout &L, const uint8_t *w, const float *x, float *y,
                         const ArgmaxOut *am, cudaStream_t s);
+// Fused projection + argmax + exchange: y is this rank's slot in its own
+// buffer; needs the TMA pipeline (cudaErrorNotSupported when its stages do
+// not fit).
+cudaError_t launch_gemv_exchange(const Layout &L, const uint8_t *w, const float *x, float *y,
+                                 const ArgmaxOut &am, const Exchange &ex, cudaStream_t s);
 // Y[p] = W X[p], p < batch.
 cudaError_t launch_matmul(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
                           cudaStream_t s);

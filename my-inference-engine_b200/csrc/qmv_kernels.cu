@@ -140,8 +140,10 @@ __device__ unsigned long long block_max_key(unsigned long long k, unsigned long 
 
 // Publish this CTA's key; the last CTA to arrive folds all of them into
 // *am.key and re-arms the counter.  No CTA waits on another.
+__device__ void exchange_finish(const Exchange &ex, unsigned long long rank_key, unsigned long long *out_key);
+
 __device__ void finish_argmax(unsigned long long cta_key, const ArgmaxOut &am,
-                              unsigned long long *scratch)
+                              unsigned long long *scratch, const Exchange *ex = nullptr)
 {
     unsigned int *counter = reinterpret_cast<unsigned int *>(am.workspace);
     unsigned long long *keys =
@@ -160,9 +162,97 @@ __device__ void finish_argmax(unsigned long long cta_key, const ArgmaxOut &am,
     for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x)
         k = max_ull(k, __ldcg(keys + i));
     k = block_max_key(k, scratch);
+    if (ex != nullptr && ex->world > 1) {
+        __shared__ unsigned long long rank_key;
+        if (threadIdx.x == 0) {
+            rank_key = k;
+            *counter = 0u;
+        }
+        __syncthreads();
+        exchange_finish(*ex, rank_key, am.key);
+        return;
+    }
     if (threadIdx.x == 0) {
         *am.key = k;
         *counter = 0u;
+    }
+}
+
+// ------------------------------------------------------ peer exchange
+//
+// Row-sharded projection across the GPUs of one node.  Every CTA copies the
+// logits of its own contiguous rows into each peer's slot for this rank
+// (coalesced NVLink stores) and fences at system scope before it counts
+// itself done.  The last CTA of the rank then stores the rank's argmax key
+// into every peer, publishes the step's epoch in every peer's flag for this
+// rank with a release store, waits (bounded) until all peers' flags for this
+// rank carry the epoch, and folds the keys.  After the kernel every rank holds
+// all logits and the same global key.
+
+__device__ unsigned int g_peer_status;
+
+__device__ __forceinline__ void st_release_sys(unsigned int *p, unsigned int v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int *p)
+{
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long globaltimer_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Copy rows [r0, r1) of this rank's slot to every peer (all threads of the CTA).
+__device__ void exchange_rows(const Exchange &ex, const float *y_local, int r0, int r1)
+{
+    for (int p = 0; p < ex.world; ++p) {
+        if (p == ex.rank) continue;
+        float *dst = ex.logits[p] + (size_t)ex.rank * ex.slot_rows;
+        for (int i = r0 + (int)threadIdx.x; i < r1; i += blockDim.x) dst[i] = y_local[i];
+    }
+    __threadfence_system();
+}
+
+// Last CTA of the rank: publish key + flag, wait for all peers, fold keys.
+__device__ void exchange_finish(const Exchange &ex, unsigned long long rank_key, unsigned long long *out_key)
+{
+    __shared__ int ok;
+    if (threadIdx.x == 0) ok = 1;
+    __syncthreads();
+    const int p = threadIdx.x;
+    if (p < ex.world) ex.keys[p][ex.rank] = rank_key;
+    __threadfence_system();
+    __syncthreads();
+    if (p < ex.world) st_release_sys(ex.flags[p] + ex.rank, ex.epoch);
+    if (p < ex.world) {
+        const unsigned int *flag = ex.flags[ex.rank] + p;
+        if (ld_acquire_sys(flag) != ex.epoch) {
+            const unsigned long long t0 = globaltimer_ns();
+            for (uint32_t n = 1;; ++n) {
+                if (ld_acquire_sys(flag) == ex.epoch) break;
+                if ((n & 63u) == 0u && globaltimer_ns() - t0 > 2000000000ull) {
+                    atomicOr(&g_peer_status, 1u);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long k = 0ull;
+        if (ok) {
+            for (int q = 0; q < ex.world; ++q) k = max_ull(k, ((volatile unsigned long long *)ex.keys[ex.rank])[q]);
+        }
+        *out_key = k;  // 0 decodes as "no token" when a peer never arrived
     }
 }
 
@@ -716,7 +806,7 @@ struct TmaPlan {
 template <uint32_t FMT, int CW, int R>
 __global__ void __launch_bounds__((CW + 1) * 32, 1)
 gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x,
-                float *__restrict__ y, ArgmaxOut am, int want_argmax, TmaPlan P)
+                float *__restrict__ y, ArgmaxOut am, int want_argmax, TmaPlan P, Exchange ex)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) unsigned long long bars[2 * 8];
@@ -833,9 +923,13 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
             }
         }
     }
+    if (ex.world > 1) {
+        __syncthreads();  // this CTA's rows of y are written
+        exchange_rows(ex, y, r0, r1);
+    }
     if (want_argmax) {
         best = block_max_key(best, kscratch);
-        finish_argmax(best, am, kscratch);
+        finish_argmax(best, am, kscratch, &ex);
     }
 }
 
@@ -1231,7 +1325,7 @@ bool tma_plan(const Layout &L, TmaPlan *P)
 
 template <uint32_t FMT, int CW, int R>
 cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, const float *x, float *y,
-                        const ArgmaxOut *am, cudaStream_t s)
+                        const ArgmaxOut *am, cudaStream_t s, const Exchange &ex = Exchange{})
 {
     auto kernel = gemv_tma_kernel<FMT, CW, R>;
     const size_t smem = (size_t)P.x_bytes + (size_t)P.stages * P.stage_bytes;
@@ -1243,8 +1337,22 @@ cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, con
     long long grid = sm_count();
     if (grid > L.rows) grid = L.rows;
     ArgmaxOut a = am ? *am : ArgmaxOut{nullptr, nullptr, 0};
-    kernel<<<(unsigned)grid, (CW + 1) * 32, smem, s>>>(L, w, x, y, a, am ? 1 : 0, P);
+    kernel<<<(unsigned)grid, (CW + 1) * 32, smem, s>>>(L, w, x, y, a, am ? 1 : 0, P, ex);
     return cudaGetLastError();
+}
+
+template <uint32_t FMT>
+cudaError_t gemv_exchange_fmt(const Layout &L, const uint8_t *w, const float *x, float *y, const ArgmaxOut &am,
+                              const Exchange &ex, cudaStream_t s)
+{
+    TmaPlan P;
+    if (!tma_plan(L, &P)) return cudaErrorNotSupported;
+    if (P.consumer_warps == 16) {
+        if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 16, 2>(L, P, w, x, y, &am, s, ex);
+        return gemv_tma_go<FMT, 16, 1>(L, P, w, x, y, &am, s, ex);
+    }
+    if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 8, 2>(L, P, w, x, y, &am, s, ex);
+    return gemv_tma_go<FMT, 8, 1>(L, P, w, x, y, &am, s, ex);
 }
 
 template <uint32_t FMT>
@@ -1429,12 +1537,36 @@ cudaError_t launch_matmul(const Layout &L, const uint8_t *w, const float *X, int
 
 void set_gemv_path(int path) { g_gemv_path = path; }
 
+size_t exchange_parity_bytes(int world, int slot_rows)
+{
+    const size_t logits = ((size_t)world * slot_rows * 4 + 255) & ~(size_t)255;
+    const size_t keys = ((size_t)world * 8 + 255) & ~(size_t)255;
+    const size_t flags = ((size_t)world * 4 + 255) & ~(size_t)255;
+    return logits + keys + flags;
+}
+
+cudaError_t launch_gemv_exchange(const Layout &L, const uint8_t *w, const float *x, float *y,
+                                 const ArgmaxOut &am, const Exchange &ex, cudaStream_t s)
+{
+    switch (L.type) {
+    case kQ8_0: return gemv_exchange_fmt<kQ8_0>(L, w, x, y, am, ex, s);
+    case kQ5_0: return gemv_exchange_fmt<kQ5_0>(L, w, x, y, am, ex, s);
+    case kQ4_K: return gemv_exchange_fmt<kQ4_K>(L, w, x, y, am, ex, s);
+    case kQ6_K: return gemv_exchange_fmt<kQ6_K>(L, w, x, y, am, ex, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
 cudaError_t read_status(unsigned int *out, bool clear)
 {
+    unsigned int peer = 0u;
     cudaError_t e = cudaMemcpyFromSymbol(out, g_status, sizeof(unsigned int));
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&peer, g_peer_status, sizeof(unsigned int));
+    if (e == cudaSuccess && peer) *out |= 8u;
     if (e == cudaSuccess && clear) {
         const unsigned int zero = 0u;
         e = cudaMemcpyToSymbol(g_status, &zero, sizeof(unsigned int));
+        if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_peer_status, &zero, sizeof(unsigned int));
     }
     return e;
 }
