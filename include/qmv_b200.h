@@ -136,11 +136,12 @@ int qmv_matvec_argmax(const QmvWeight *weight, const float *x, int x_count, floa
 
 /* ---- row-sharded projection over peer memory (one node, 2..8 GPUs) -------
  * The vocabulary projection split by rows across ranks, one process per GPU
- * (SURVEY row e; the reference runs it on one CPU, src/qwen2_architecture.cpp
- * :1504-1523 + src/sampler.cpp:14-36).  Each rank owns an exchange buffer of
- * qmv_exchange_bytes() (two parity regions: logits[world * slot_rows] f32 |
- * keys[world] u64 | flags[world] u32) allocated with qmv_ipc_alloc, shares its
- * IPC handle, and opens every peer's handle with qmv_ipc_open. */
+ * (the reference runs it on one CPU: src/qwen2_architecture.cpp:1504-1523 +
+ * src/sampler.cpp:14-36).  Each rank owns an exchange buffer of
+ * qmv_exchange_bytes() allocated with qmv_ipc_alloc: a 256-byte control block
+ * (the rank's device-side step counter) and two parity regions
+ * (logits[world * slot_rows] f32 | keys[world] u64 | flags[world] u32).  The
+ * ranks share their IPC handles and open each other's with qmv_ipc_open. */
 
 /* Bytes of one rank's exchange buffer. */
 int qmv_exchange_bytes(int world, int slot_rows, size_t *bytes);
@@ -158,22 +159,23 @@ int qmv_ipc_free(void *dev_ptr);
  * raw device pointers owned by this library. */
 int qmv_memcpy(void *dst, const void *src, size_t bytes, void *stream);
 
-/* Gathered logits of step `epoch` inside a rank's own buffer:
- * logits[world * slot_rows], rank r's rows at r * slot_rows. */
+/* Gathered logits of the `epoch`-th call (1, 2, ...) inside a rank's own
+ * buffer: logits[world * slot_rows], rank r's rows at r * slot_rows. */
 int qmv_exchange_logits(void *buffer, int world, int slot_rows, uint32_t epoch, float **logits);
 
 /* One kernel per rank: this rank's rows of W x (the weight must hold rows
  * [rank * slot_rows, ...)), its argmax key, stores of its logits and key into
  * every rank's buffer over NVLink, and a bounded wait for every peer's flag of
- * this epoch.  On completion *key (device) is the global argmax key on every
- * rank and every rank's buffer holds all logits.  `buffers` is a host array
- * of world device pointers (own + opened peers).  epoch starts at 1 and
- * increases by one per step; read the gathered logits on the same stream
- * before the next call.  A peer that never arrives within 2 s leaves key 0
- * (no token) and sets bit 3 of qmv_device_status. */
+ * this step.  The step counter lives in the buffer (device side), so the
+ * call can be captured in a CUDA graph and replayed.  On completion *key
+ * (device) is the global argmax key on every rank and every rank's buffer
+ * holds all logits of the step.  `buffers` is a host array of world device
+ * pointers (own + opened peers).  Read a step's gathered logits on the same
+ * stream before the call after next.  A peer that never arrives within 2 s
+ * leaves key 0 (no token) and sets bit 3 of qmv_device_status. */
 int qmv_matvec_argmax_exchange(const QmvWeight *weight, const float *x, int x_count, int rank, int world,
-                               void *const *buffers, int slot_rows, uint32_t epoch, uint64_t *key,
-                               void *workspace, void *stream);
+                               void *const *buffers, int slot_rows, uint64_t *key, void *workspace,
+                               void *stream);
 
 /* Greedy argmax that allocates nothing and needs no workspace: same result
  * as qmv_argmax, for callers that cannot call cudaMalloc -- for example a host

@@ -132,7 +132,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "qmv_ipc_free": (I, [P]),
         "qmv_exchange_logits": (I, [P, I, I, U32, ctypes.POINTER(P)]),
         "qmv_memcpy": (I, [P, P, SZ, P]),
-        "qmv_matvec_argmax_exchange": (I, [P, P, I, I, I, ctypes.POINTER(P), I, U32, P, P, P]),
+        "qmv_matvec_argmax_exchange": (I, [P, P, I, I, I, ctypes.POINTER(P), I, P, P, P]),
         "qmv_key_to_token": (I, [U64, IP]),
         "qmv_greedy_sample": (I, [P, I, IP, ctypes.c_char_p, I, P]),
         "qmv_quantized_tensor_matvec_f32": (I, [VP, P, I, P, I]),
@@ -384,14 +384,14 @@ class Weight:
                                        self.rows, _ptr(key_dev), _ptr(workspace_dev),
                                        _ptr(stream)), "qmv_matvec_argmax")
 
-    def matvec_argmax_exchange(self, x_dev, rank: int, world: int, buffers, slot_rows: int, epoch: int,
-                               key_dev, workspace_dev, stream=None):
+    def matvec_argmax_exchange(self, x_dev, rank: int, world: int, buffers, slot_rows: int, key_dev,
+                               workspace_dev, stream=None):
         """Fused row-shard projection + argmax + exchange over peer memory
         (qmv_matvec_argmax_exchange); `buffers` lists every rank's exchange
         buffer pointer as seen from this process."""
         arr = (ctypes.c_void_p * world)(*buffers)
         _check(lib().qmv_matvec_argmax_exchange(self.handle, _ptr(x_dev), self.cols, rank, world, arr,
-                                                slot_rows, epoch, _ptr(key_dev), _ptr(workspace_dev),
+                                                slot_rows, _ptr(key_dev), _ptr(workspace_dev),
                                                 _ptr(stream)), "qmv_matvec_argmax_exchange")
 
     def dequantize(self, out_dev, stream=None):

@@ -418,7 +418,7 @@ QMV_EXPORT int qmv_exchange_bytes(int world, int slot_rows, size_t *bytes)
     if (bytes == nullptr) return fail("bytes pointer is null");
     if (world < 2 || world > qmv::kMaxPeers) return fail("world must be 2..%d", qmv::kMaxPeers);
     if (slot_rows <= 0) return fail("slot_rows must be positive");
-    *bytes = 2 * qmv::exchange_parity_bytes(world, slot_rows);
+    *bytes = qmv::kExchangeHeader + 2 * qmv::exchange_parity_bytes(world, slot_rows);
     return 1;
 }
 
@@ -473,13 +473,14 @@ QMV_EXPORT int qmv_exchange_logits(void *buffer, int world, int slot_rows, uint3
 {
     if (buffer == nullptr || logits == nullptr) return fail("bad arguments");
     if (world < 2 || world > qmv::kMaxPeers || slot_rows <= 0) return fail("bad world or slot_rows");
-    *logits = (float *)((uint8_t *)buffer + (epoch & 1u) * qmv::exchange_parity_bytes(world, slot_rows));
+    *logits = (float *)((uint8_t *)buffer + qmv::kExchangeHeader +
+                        (epoch & 1u) * qmv::exchange_parity_bytes(world, slot_rows));
     return 1;
 }
 
 QMV_EXPORT int qmv_matvec_argmax_exchange(const QmvWeight *w, const float *x, int x_count, int rank, int world,
-                                          void *const *buffers, int slot_rows, uint32_t epoch, uint64_t *key,
-                                          void *workspace, void *stream)
+                                          void *const *buffers, int slot_rows, uint64_t *key, void *workspace,
+                                          void *stream)
 {
     if (!check_weight(w)) return 0;
     if (x == nullptr || key == nullptr || workspace == nullptr || buffers == nullptr)
@@ -490,7 +491,6 @@ QMV_EXPORT int qmv_matvec_argmax_exchange(const QmvWeight *w, const float *x, in
     if (slot_rows < w->L.rows || w->row_begin != rank * slot_rows)
         return fail("weight rows [%d, %d) are not rank %d's slot of %d rows", w->row_begin,
                     w->row_begin + w->L.rows, rank, slot_rows);
-    if (epoch == 0) return fail("epoch must be positive");
     if (!aligned16(x)) return fail("x must be 16-byte aligned");
     const size_t pb = qmv::exchange_parity_bytes(world, slot_rows);
     const size_t keys_off = ((size_t)world * slot_rows * 4 + 255) & ~(size_t)255;
@@ -498,18 +498,20 @@ QMV_EXPORT int qmv_matvec_argmax_exchange(const QmvWeight *w, const float *x, in
     qmv::Exchange ex{};
     ex.world = world;
     ex.rank = rank;
-    ex.epoch = epoch;
     ex.slot_rows = slot_rows;
+    if (buffers[rank] == nullptr) return fail("buffer of rank %d is null", rank);
+    ex.epoch = (unsigned int *)buffers[rank];
     for (int p = 0; p < world; ++p) {
         if (buffers[p] == nullptr) return fail("buffer of rank %d is null", p);
-        uint8_t *base = (uint8_t *)buffers[p] + (epoch & 1u) * pb;
-        ex.logits[p] = (float *)base;
-        ex.keys[p] = (unsigned long long *)(base + keys_off);
-        ex.flags[p] = (unsigned int *)(base + flags_off);
+        for (int par = 0; par < 2; ++par) {
+            uint8_t *base = (uint8_t *)buffers[p] + qmv::kExchangeHeader + par * pb;
+            ex.logits[par][p] = (float *)base;
+            ex.keys[par][p] = (unsigned long long *)(base + keys_off);
+            ex.flags[par][p] = (unsigned int *)(base + flags_off);
+        }
     }
-    float *y = ex.logits[rank] + (size_t)rank * slot_rows;
     qmv::ArgmaxOut am{(unsigned long long *)key, workspace, w->row_begin};
-    QMV_CUDA(qmv::launch_gemv_exchange(w->L, w->dev, x, y, am, ex, (cudaStream_t)stream),
+    QMV_CUDA(qmv::launch_gemv_exchange(w->L, w->dev, x, nullptr, am, ex, (cudaStream_t)stream),
              "gemv+argmax+exchange launch");
     return 1;
 }

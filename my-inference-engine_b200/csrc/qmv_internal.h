@@ -67,19 +67,22 @@ struct ArgmaxOut {
 };
 
 // Row-sharded exchange over peer memory (one node, up to kMaxPeers GPUs).
-// Each rank's exchange buffer holds two parity regions (selected by the
-// step's epoch): logits[world * slot_rows] f32 | keys[world] u64 | flags[world]
-// u32.  The pointers below are already resolved to this step's parity region
-// of every rank's buffer (own + IPC-opened peers).
+// Each rank's exchange buffer starts with a 256-byte control block whose
+// first word is the rank's step counter (epoch, device-side), followed by two
+// parity regions: logits[world * slot_rows] f32 | keys[world] u64 |
+// flags[world] u32.  A kernel runs epoch = counter + 1, uses parity region
+// epoch & 1 and stores the counter back when its exchange completed, so
+// repeated launches (including CUDA-graph replays) need no host epoch.
 constexpr int kMaxPeers = 8;
+constexpr size_t kExchangeHeader = 256;
 struct Exchange {
     int world;  // <= 1: no exchange
     int rank;
-    unsigned int epoch;  // > 0, increases every step
     int slot_rows;
-    float *logits[kMaxPeers];
-    unsigned long long *keys[kMaxPeers];
-    unsigned int *flags[kMaxPeers];
+    unsigned int *epoch;  // this rank's counter
+    float *logits[2][kMaxPeers];
+    unsigned long long *keys[2][kMaxPeers];
+    unsigned int *flags[2][kMaxPeers];
 };
 size_t exchange_parity_bytes(int world, int slot_rows);
 

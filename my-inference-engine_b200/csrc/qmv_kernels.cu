@@ -210,34 +210,48 @@ __device__ __forceinline__ unsigned long long globaltimer_ns()
     return t;
 }
 
+// This launch's epoch (the counter is only stored back by the last CTA after
+// every CTA has read it).
+__device__ __forceinline__ unsigned int exchange_epoch(const Exchange &ex)
+{
+    return *((volatile unsigned int *)ex.epoch) + 1u;
+}
+
 // Copy rows [r0, r1) of this rank's slot to every peer (all threads of the CTA).
-__device__ void exchange_rows(const Exchange &ex, const float *y_local, int r0, int r1)
+__device__ void exchange_rows(const Exchange &ex, int par, const float *y_local, int r0, int r1)
 {
     for (int p = 0; p < ex.world; ++p) {
         if (p == ex.rank) continue;
-        float *dst = ex.logits[p] + (size_t)ex.rank * ex.slot_rows;
+        float *dst = ex.logits[par][p] + (size_t)ex.rank * ex.slot_rows;
         for (int i = r0 + (int)threadIdx.x; i < r1; i += blockDim.x) dst[i] = y_local[i];
     }
-    __threadfence_system();
+    // One system-scope fence per CTA: the barrier orders every thread's peer
+    // stores before thread 0's fence, which orders them before the CTA's
+    // arrival on the counter (and so before the rank's release flag).
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
 }
 
-// Last CTA of the rank: publish key + flag, wait for all peers, fold keys.
+// Last CTA of the rank: publish key + flag, wait for all peers, fold keys,
+// advance the rank's epoch counter.
 __device__ void exchange_finish(const Exchange &ex, unsigned long long rank_key, unsigned long long *out_key)
 {
     __shared__ int ok;
+    const unsigned int epoch = exchange_epoch(ex);
+    const int par = (int)(epoch & 1u);
     if (threadIdx.x == 0) ok = 1;
     __syncthreads();
     const int p = threadIdx.x;
-    if (p < ex.world) ex.keys[p][ex.rank] = rank_key;
+    if (p < ex.world) ex.keys[par][p][ex.rank] = rank_key;
     __threadfence_system();
     __syncthreads();
-    if (p < ex.world) st_release_sys(ex.flags[p] + ex.rank, ex.epoch);
+    if (p < ex.world) st_release_sys(ex.flags[par][p] + ex.rank, epoch);
     if (p < ex.world) {
-        const unsigned int *flag = ex.flags[ex.rank] + p;
-        if (ld_acquire_sys(flag) != ex.epoch) {
+        const unsigned int *flag = ex.flags[par][ex.rank] + p;
+        if (ld_acquire_sys(flag) != epoch) {
             const unsigned long long t0 = globaltimer_ns();
             for (uint32_t n = 1;; ++n) {
-                if (ld_acquire_sys(flag) == ex.epoch) break;
+                if (ld_acquire_sys(flag) == epoch) break;
                 if ((n & 63u) == 0u && globaltimer_ns() - t0 > 2000000000ull) {
                     atomicOr(&g_peer_status, 1u);
                     ok = 0;
@@ -250,9 +264,11 @@ __device__ void exchange_finish(const Exchange &ex, unsigned long long rank_key,
     if (threadIdx.x == 0) {
         unsigned long long k = 0ull;
         if (ok) {
-            for (int q = 0; q < ex.world; ++q) k = max_ull(k, ((volatile unsigned long long *)ex.keys[ex.rank])[q]);
+            for (int q = 0; q < ex.world; ++q)
+                k = max_ull(k, ((volatile unsigned long long *)ex.keys[par][ex.rank])[q]);
         }
         *out_key = k;  // 0 decodes as "no token" when a peer never arrived
+        *ex.epoch = epoch;
     }
 }
 
@@ -824,6 +840,9 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
     const int r1 = (int)((long long)L.rows * (blockIdx.x + 1) / gridDim.x);
     const int SR = P.rows_per_stage;
     const int n_stages = (r1 - r0 + SR - 1) / SR;
+    // with an exchange, y is this rank's slot in this epoch's parity region
+    const int par = ex.world > 1 ? (int)(exchange_epoch(ex) & 1u) : 0;
+    if (ex.world > 1) y = ex.logits[par][ex.rank] + (size_t)ex.rank * ex.slot_rows;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NS; ++i) {
@@ -925,7 +944,7 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
     }
     if (ex.world > 1) {
         __syncthreads();  // this CTA's rows of y are written
-        exchange_rows(ex, y, r0, r1);
+        exchange_rows(ex, par, y, r0, r1);
     }
     if (want_argmax) {
         best = block_max_key(best, kscratch);

@@ -76,8 +76,11 @@ class ExchangeGroup:
                 self.buffers.append(ptr)
         self.epoch = 0
 
-    def next_epoch(self) -> int:
-        self.epoch += 1
+    def next_epoch(self, steps: int = 1) -> int:
+        """Advance the host's count of exchange calls (the device keeps its own
+        counter); returns the epoch of the latest call, which locates its
+        gathered logits (qmv_exchange_logits)."""
+        self.epoch += steps
         return self.epoch
 
     def close(self):

@@ -40,7 +40,7 @@ def main():
         x = wl.make_activations(cols, seed=10 + step)
         xd = torch.from_numpy(x).cuda()
         epoch = group.next_epoch()
-        w.matvec_argmax_exchange(xd.data_ptr(), rank, world, group.buffers, slot, epoch, key.data_ptr(),
+        w.matvec_argmax_exchange(xd.data_ptr(), rank, world, group.buffers, slot, key.data_ptr(),
                                  ws.data_ptr())
         torch.cuda.synchronize()
         qmv.memcpy(host, qmv.exchange_logits(group.own, world, slot, epoch), host.nbytes)
