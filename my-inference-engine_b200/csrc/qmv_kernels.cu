@@ -840,9 +840,11 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
     const int r1 = (int)((long long)L.rows * (blockIdx.x + 1) / gridDim.x);
     const int SR = P.rows_per_stage;
     const int n_stages = (r1 - r0 + SR - 1) / SR;
-    // with an exchange, y is this rank's slot in this epoch's parity region
-    const int par = ex.world > 1 ? (int)(exchange_epoch(ex) & 1u) : 0;
-    if (ex.world > 1) y = ex.logits[par][ex.rank] + (size_t)ex.rank * ex.slot_rows;
+    // Programmatic dependent launch: the next launch in the stream may start
+    // now; it only streams weights until its griddepcontrol.wait, and this
+    // grid touches x, y, the workspace and the exchange buffers only after its
+    // own wait (i.e. after the previous grid has completed).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NS; ++i) {
@@ -888,8 +890,13 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
                 }
             }
         }
+        __syncwarp();
+        asm volatile("griddepcontrol.wait;" ::: "memory");
     } else {
         // ---------------- consumers
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (ex.world > 1)  // this rank's slot in this epoch's parity region
+            y = ex.logits[exchange_epoch(ex) & 1u][ex.rank] + (size_t)ex.rank * ex.slot_rows;
         quantize_x<FMT, CW * 32>(x, L.cols, C, smem);
         asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
         const XS s = xs_view(smem, L.cols);
@@ -944,7 +951,8 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
     }
     if (ex.world > 1) {
         __syncthreads();  // this CTA's rows of y are written
-        exchange_rows(ex, par, y, r0, r1);
+        const int par = (int)(exchange_epoch(ex) & 1u);
+        exchange_rows(ex, par, ex.logits[par][ex.rank] + (size_t)ex.rank * ex.slot_rows, r0, r1);
     }
     if (want_argmax) {
         best = block_max_key(best, kscratch);
@@ -1356,7 +1364,19 @@ cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, con
     long long grid = sm_count();
     if (grid > L.rows) grid = L.rows;
     ArgmaxOut a = am ? *am : ArgmaxOut{nullptr, nullptr, 0};
-    kernel<<<(unsigned)grid, (CW + 1) * 32, smem, s>>>(L, w, x, y, a, am ? 1 : 0, P, ex);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((CW + 1) * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const int want = am ? 1 : 0;
+    e = cudaLaunchKernelEx(&cfg, kernel, L, w, x, y, a, want, P, ex);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
