@@ -73,6 +73,17 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def measured_tensor_peak():
+    """Dense bf16 TFLOP/s of this pool's B200s (burst, cuBLAS) and its source."""
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            d = json.load(fh)
+        if "bf16_tflops" in d:
+            return float(d["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
 def profile_traffic(name):
     """dram bytes per launch from a committed ncu summary (profiles/<name>.txt,
     line 'dram_bytes_per_launch: <int>'), scaled by the caller; None if absent."""
@@ -556,7 +567,15 @@ def extras_single_gpu(qmv, steps, only=None):
                "frac_hbm": round(alg / (ms * 1e-3) / 1e9 / peak, 3), "copies": copies, "calls": n,
                "timing": "CUDA graph replay"}
         if batch:
-            rec["TFLOP_s"] = round(2.0 * P * rows * cols / (ms * 1e-3) / 1e12, 2)
+            tflops = 2.0 * P * rows * cols / (ms * 1e-3) / 1e12
+            rec["TFLOP_s"] = round(tflops, 2)
+            if P >= 32:
+                # tensor-core kernel: three bf16 MMAs per product (wh*xh + wl*xh + wh*xl)
+                tpeak, tkind = measured_tensor_peak()
+                rec["kernel"] = "matmul_tc_kernel (tcgen05.mma kind::f16, bf16 hi/lo splits)"
+                rec["tensor_TFLOP_s_issued"] = round(3 * tflops, 2)
+                rec["frac_tensor"] = round(3 * tflops / tpeak, 3)
+                rec["tensor_peak_source"] = tkind
         out[key] = rec
         del graph
         for w in ws:

@@ -47,9 +47,9 @@ int qmv_set_device(int device);
 
 /* Device status of the current device: bit 0 = a consumer's pipeline wait
  * expired, bit 1 = a producer's wait expired, bit 2 = draining in-flight
- * copies timed out, bit 3 = a peer's exchange flag never arrived.  0 means
- * every bounded wait completed.  clear != 0 resets
- * the word.  No counterpart in the reference (its kernels never wait). */
+ * copies timed out, bit 3 = a peer's exchange flag never arrived, bit 4 = a
+ * tensor-core matmul's wait for its MMAs expired.  0 means every bounded
+ * wait completed.  clear != 0 resets the word.  No counterpart in the reference (its kernels never wait). */
 int qmv_device_status(uint32_t *flags, int clear);
 
 /* GEMV kernel selection for the calling process: 0 = automatic (TMA bulk-copy
@@ -57,6 +57,14 @@ int qmv_device_status(uint32_t *flags, int clear);
  * 1 = direct loads, 2 = TMA pipeline only (shapes it cannot stage fail).
  * No counterpart in the reference; both paths compute the same function. */
 int qmv_set_gemv_path(int path);
+
+/* Batched-matmul kernel selection for the calling process: 0 = automatic
+ * (tensor cores, tcgen05 with bf16 hi/lo operand splits and fp32
+ * accumulation, from 32 positions when X is 16-byte aligned; CUDA-core dp4a
+ * kernel otherwise), 1 = CUDA cores only, 2 = tensor cores only (a misaligned
+ * X then fails).  No counterpart in the reference; both paths compute the
+ * same function within the parity bound. */
+int qmv_set_matmul_path(int path);
 
 /* ---- residency of packed tensors ----------------------------------------
  * Backs the packed-weight source of the reference: the borrowed mmap views

@@ -41,7 +41,7 @@ KEY_NONFINITE = 0xFFFFFFFFFFFFFFFF
 # include/quantized_matvec.h (mangled, C++ linkage).
 C_SYMBOLS = [
     "qmv_last_error", "qmv_copy_last_error", "qmv_abi_version", "qmv_device_count",
-    "qmv_set_device", "qmv_device_status", "qmv_set_gemv_path", "qmv_weight_upload", "qmv_weight_free", "qmv_weight_info",
+    "qmv_set_device", "qmv_device_status", "qmv_set_gemv_path", "qmv_set_matmul_path", "qmv_weight_upload", "qmv_weight_free", "qmv_weight_info",
     "qmv_resident_weight", "qmv_resident_release_all", "qmv_matvec", "qmv_matmul",
     "qmv_dequantize", "qmv_dequantize_raw", "qmv_argmax_workspace_bytes", "qmv_argmax",
     "qmv_matvec_argmax", "qmv_exchange_bytes", "qmv_ipc_alloc", "qmv_ipc_open", "qmv_ipc_close",
@@ -112,6 +112,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "qmv_set_device": (I, [I]),
         "qmv_device_status": (I, [ctypes.POINTER(U32), I]),
         "qmv_set_gemv_path": (I, [I]),
+        "qmv_set_matmul_path": (I, [I]),
         "qmv_weight_upload": (I, [VP, I, I, ctypes.POINTER(P)]),
         "qmv_weight_free": (I, [P]),
         "qmv_weight_info": (I, [P, ctypes.POINTER(U32), IP, IP, IP, ctypes.POINTER(U64)]),
@@ -258,6 +259,14 @@ GEMV_AUTO, GEMV_LOADS, GEMV_TMA = 0, 1, 2
 def set_gemv_path(path: int):
     """0 automatic, 1 direct-load kernel, 2 TMA pipeline kernel."""
     _check(lib().qmv_set_gemv_path(path), "qmv_set_gemv_path")
+
+
+MATMUL_AUTO, MATMUL_CUDA_CORES, MATMUL_TENSOR_CORES = 0, 1, 2
+
+
+def set_matmul_path(path: int):
+    """0 automatic, 1 CUDA-core (dp4a) kernel, 2 tensor-core (tcgen05) kernel."""
+    _check(lib().qmv_set_matmul_path(path), "qmv_set_matmul_path")
 
 
 def exchange_bytes(world: int, slot_rows: int) -> int:

@@ -257,6 +257,13 @@ QMV_EXPORT int qmv_set_gemv_path(int path)
     return 1;
 }
 
+QMV_EXPORT int qmv_set_matmul_path(int path)
+{
+    if (path < 0 || path > 2) return fail("matmul path must be 0, 1 or 2");
+    qmv::set_matmul_path(path);
+    return 1;
+}
+
 QMV_EXPORT int qmv_weight_upload(const GgufQuantizedTensorView *view, int row_begin, int row_end,
                                  QmvWeight **out)
 {

@@ -100,6 +100,9 @@ cudaError_t launch_matmul(const Layout &L, const uint8_t *w, const float *X, int
 // GEMV kernel selection: 0 automatic (TMA pipeline when its stages fit in
 // shared memory, direct loads otherwise), 1 direct loads, 2 TMA pipeline only.
 void set_gemv_path(int path);
+// Matmul kernel selection: 0 automatic (tensor cores from 32 positions when X
+// is 16-byte aligned), 1 CUDA cores (dp4a), 2 tensor cores only.
+void set_matmul_path(int path);
 // Device status bits set by bounded waits that expired (0 = healthy).
 cudaError_t read_status(unsigned int *out, bool clear);
 // Argmax key of logits[0..n).

@@ -26,6 +26,7 @@
 // of chunk c is stored at (j * C + c) * 16 in each plane, with one record
 // {s, s * sum of xq} per slice, so lanes reading consecutive chunks hit
 // consecutive banks.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -1013,6 +1014,441 @@ matmul_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__
     }
 }
 
+// ---------------------------------------------- matmul (tensor cores)
+//
+// Batched projection of many positions on the 5th-generation tensor cores
+// (src/quantized_matvec.cpp:164-224 computes the same Y[p] = W X[p]).
+// A CTA owns a tile of 128 rows x TN positions and walks K in stages of 64.
+// All 512 threads stage one step: weights are decoded from the resident
+// layout to the reference's fp32 values and split into two bf16 planes
+// w = wh + wl, the positions' x likewise x = xh + xl, and both are written to
+// shared memory in the canonical K-major no-swizzle layout (8-row x 16-byte
+// core matrices; 16-byte unit u of a plane sits at u * 16).  Thread 0 then
+// issues, per 16-wide K slice, wh*xh + wl*xh + wh*xl as tcgen05.mma
+// (kind::f16, bf16 inputs, fp32 accumulator of 128 lanes x TN columns in
+// tensor memory) and commits the stage's MMAs to the mbarrier that frees the
+// stage.  wl and xl carry the next 8 bits, so every product is exact to
+// about 2^-16 of |w x| -- far inside the parity bound 1e-4 * sum|w x|.  Raw
+// bytes of the next stage are loaded into registers before the current one
+// is converted.  The epilogue reads the accumulator with tcgen05.ld (warp w
+// reads lanes 32 (w % 4) .. + 31, a quarter of the columns) and writes
+// Y[p][row], one 128-byte run per warp store.
+//
+// A tile that holds a non-finite weight scale, or an x whose bf16 rounding
+// is not finite, is recomputed on the CUDA cores in fp32 so that Inf and NaN
+// propagate as in the reference's loop; the split planes could otherwise
+// turn Inf * 0 into NaN.
+
+constexpr int kTcM = 128;         // rows per tile = accumulator lanes
+constexpr int kTcK = 64;          // K per stage
+constexpr int kTcThreads = 512;
+constexpr int kTcStages = 3;
+constexpr unsigned int kStatusMmaTimeout = 16u;
+
+__host__ __device__ constexpr uint32_t tc_stage_bytes(int tn)
+{
+    return 2u * kTcM * kTcK * 2u + 2u * (uint32_t)tn * kTcK * 2u;
+}
+
+__device__ __forceinline__ uint32_t ldg16(const uint8_t *p) { return __ldg((const unsigned short *)p); }
+
+// Raw bytes of 8 consecutive weights (k0 .. k0 + 7, k0 a multiple of 8) of
+// one resident row, and their decoding to fp32 with the reference's
+// arithmetic (src/quantization.cpp:54-67, 161-184, 380-409, 588-615).
+template <uint32_t FMT> struct Raw8;
+
+template <> struct Raw8<kQ8_0> {
+    uint2 q;
+    uint32_t d;
+    __device__ __forceinline__ void load(const uint8_t *row, const Layout &L, int k0)
+    {
+        const int b = k0 >> 5, i0 = k0 & 31;
+        q = __ldg((const uint2 *)(row + (((i0 < 16) ? b : L.C + b) << 4) + (i0 & 8)));
+        d = ldg16(row + L.off_a + 2 * b);
+    }
+    __device__ __forceinline__ bool decode(int, float v[8]) const
+    {
+        const float s = f16_fast(d);
+        v[0] = s * (float)sbyte<0>(q.x); v[1] = s * (float)sbyte<1>(q.x);
+        v[2] = s * (float)sbyte<2>(q.x); v[3] = s * (float)sbyte<3>(q.x);
+        v[4] = s * (float)sbyte<0>(q.y); v[5] = s * (float)sbyte<1>(q.y);
+        v[6] = s * (float)sbyte<2>(q.y); v[7] = s * (float)sbyte<3>(q.y);
+        return (d & 0x7c00u) != 0x7c00u;
+    }
+};
+
+template <> struct Raw8<kQ5_0> {
+    uint2 q;
+    uint32_t qh, d;
+    __device__ __forceinline__ void load(const uint8_t *row, const Layout &L, int k0)
+    {
+        const int b = k0 >> 5, i0 = k0 & 31;
+        q = __ldg((const uint2 *)(row + (b << 4) + (i0 & 8)));
+        qh = __ldg((const uint32_t *)(row + L.off_a + 4 * b)) >> i0;
+        d = ldg16(row + L.off_b + 2 * b);
+    }
+    __device__ __forceinline__ bool decode(int k0, float v[8]) const
+    {
+        // weight i of the block: low nibble of byte i (i < 16) or high nibble
+        // of byte i - 16, fifth bit = bit i of qh
+        const int sh = (k0 & 16) ? 4 : 0;
+        const float s = f16_fast(d);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t byte = ((i < 4 ? q.x : q.y) >> (8 * (i & 3))) & 0xffu;
+            const int n = (int)(((byte >> sh) & 15u) | (((qh >> i) & 1u) << 4));
+            v[i] = s * (float)(n - 16);
+        }
+        return (d & 0x7c00u) != 0x7c00u;
+    }
+};
+
+template <> struct Raw8<kQ4_K> {
+    uint2 q;
+    uint4 hdr;
+    __device__ __forceinline__ void load(const uint8_t *row, const Layout &L, int k0)
+    {
+        const int sb = k0 >> 8, j = (k0 >> 5) & 7, o0 = k0 & 31;
+        const int c = 4 * sb + (j >> 1);
+        q = __ldg((const uint2 *)(row + (((o0 < 16) ? c : L.C + c) << 4) + (o0 & 8)));
+        hdr = __ldg((const uint4 *)(row + L.off_a + (sb << 4)));
+    }
+    __device__ __forceinline__ bool decode(int k0, float v[8]) const
+    {
+        // 6-bit scale and minimum of sub-block j (src/quantization.cpp:351-378);
+        // header bytes 4..15 are the 12 packed scale bytes
+        const int j = (k0 >> 5) & 7, t = 8 * (j & 3);
+        uint32_t sc, mn;
+        if (j < 4) {
+            sc = (hdr.y >> t) & 63u;
+            mn = (hdr.z >> t) & 63u;
+        } else {
+            sc = ((hdr.w >> t) & 15u) | (((hdr.y >> t) >> 6 & 3u) << 4);
+            mn = ((hdr.w >> t) >> 4 & 15u) | (((hdr.z >> t) >> 6 & 3u) << 4);
+        }
+        const float scale = __fmul_rn(f16_fast(hdr.x & 0xffffu), (float)sc);
+        const float minimum = __fmul_rn(f16_fast(hdr.x >> 16), (float)mn);
+        const int sh = 4 * (j & 1);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t byte = ((i < 4 ? q.x : q.y) >> (8 * (i & 3))) & 0xffu;
+            v[i] = __fsub_rn(__fmul_rn(scale, (float)((byte >> sh) & 15u)), minimum);
+        }
+        return (hdr.x & 0x7c00u) != 0x7c00u && (hdr.x & 0x7c000000u) != 0x7c000000u;
+    }
+};
+
+template <> struct Raw8<kQ6_K> {
+    uint2 ql, qh;
+    uint32_t sc, d;
+    __device__ __forceinline__ void load(const uint8_t *row, const Layout &L, int k0)
+    {
+        // weight 128 g + 32 r + o of the super-block lives in chunk
+        // 4 sb + 2 g + (o >> 4)
+        const int sb = k0 >> 8, g = (k0 >> 7) & 1, r = (k0 >> 5) & 3, o0 = k0 & 31;
+        const int c = 4 * sb + 2 * g + (o0 >> 4);
+        ql = __ldg((const uint2 *)(row + ((((r & 1) ? L.C : 0) + c) << 4) + (o0 & 8)));
+        qh = __ldg((const uint2 *)(row + ((2 * L.C + c) << 4) + (o0 & 8)));
+        sc = __ldg((const uint32_t *)(row + L.off_a + 4 * c));
+        d = ldg16(row + L.off_b + 2 * sb);
+    }
+    __device__ __forceinline__ bool decode(int k0, float v[8]) const
+    {
+        const int r = (k0 >> 5) & 3;
+        const int s = (int)(int8_t)((sc >> (8 * r)) & 0xffu);
+        const float ds = __fmul_rn(f16_fast(d), (float)s);
+        const int shl = 4 * (r >> 1), shh = 2 * r;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t lo = ((i < 4 ? ql.x : ql.y) >> (8 * (i & 3))) & 0xffu;
+            const uint32_t hi = ((i < 4 ? qh.x : qh.y) >> (8 * (i & 3))) & 0xffu;
+            const int n = (int)(((lo >> shl) & 15u) | (((hi >> shh) & 3u) << 4));
+            v[i] = __fmul_rn(ds, (float)(n - 32));
+        }
+        return (d & 0x7c00u) != 0x7c00u;
+    }
+};
+
+__device__ __forceinline__ uint32_t bf16x2_bits(__nv_bfloat162 h)
+{
+    return (uint32_t)__bfloat16_as_ushort(h.x) | ((uint32_t)__bfloat16_as_ushort(h.y) << 16);
+}
+
+// Split 8 floats into bf16 high and low planes (v ~= hi + lo, element 0 at
+// the lowest address) and store both 16-byte units.
+__device__ __forceinline__ void split_store(const float v[8], uint8_t *hi_plane, uint8_t *lo_plane, uint32_t off)
+{
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 hb = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        const float2 hf = __bfloat1622float2(hb);
+        h[j] = bf16x2_bits(hb);
+        l[j] = bf16x2_bits(__floats2bfloat162_rn(v[2 * j] - hf.x, v[2 * j + 1] - hf.y));
+    }
+    *(uint4 *)(hi_plane + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    *(uint4 *)(lo_plane + off) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// true when every x rounds to a finite bf16 (|x| below 0x7F7F8000 as bits)
+__device__ __forceinline__ bool x_in_range(const float4 &a, const float4 &b)
+{
+    uint32_t m = __float_as_uint(a.x) & 0x7fffffffu;
+    m = max(m, __float_as_uint(a.y) & 0x7fffffffu);
+    m = max(m, __float_as_uint(a.z) & 0x7fffffffu);
+    m = max(m, __float_as_uint(a.w) & 0x7fffffffu);
+    m = max(m, __float_as_uint(b.x) & 0x7fffffffu);
+    m = max(m, __float_as_uint(b.y) & 0x7fffffffu);
+    m = max(m, __float_as_uint(b.z) & 0x7fffffffu);
+    m = max(m, __float_as_uint(b.w) & 0x7fffffffu);
+    return m < 0x7f7f8000u;
+}
+
+// Shared-memory matrix descriptor, K-major, no swizzle: core matrices along
+// K 128 bytes apart (leading byte offset), 8-row groups 1024 bytes apart
+// (stride byte offset), descriptor version 1.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr)
+{
+    return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)(128u >> 4) << 16) | ((uint64_t)(1024u >> 4) << 32) |
+           (1ull << 46);
+}
+
+// Instruction descriptor: fp32 accumulator, bf16 A and B, both K-major,
+// N = tn, M = 128.
+__host__ __device__ constexpr uint32_t umma_idesc(int tn)
+{
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(tn >> 3) << 17) | ((uint32_t)(kTcM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 8 consecutive fp32 accumulator columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float v[8])
+{
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// fp32 recomputation of one tile (rows r0.., positions p0..) on the CUDA cores.
+template <uint32_t FMT>
+__device__ void tc_tile_fallback(const Layout &L, const uint8_t *__restrict__ w, const float *__restrict__ X,
+                                 int np, float *__restrict__ Y, int r0, int p0, int tn)
+{
+    for (int o = threadIdx.x; o < kTcM * tn; o += blockDim.x) {
+        const int row = r0 + (o % kTcM), pos = p0 + (o / kTcM);
+        if (row >= L.rows || pos >= np) continue;
+        const uint8_t *rp = w + (uint64_t)row * L.row_stride;
+        const float *xp = X + (size_t)pos * L.cols;
+        float acc = 0.f;
+        for (int k0 = 0; k0 < L.cols; k0 += 8) {
+            Raw8<FMT> raw;
+            raw.load(rp, L, k0);
+            float v[8];
+            raw.decode(k0, v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc += v[i] * xp[k0 + i];
+        }
+        Y[(size_t)pos * L.rows + row] = acc;
+    }
+}
+
+template <uint32_t FMT, int TN>
+__global__ void __launch_bounds__(kTcThreads, 1)
+matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ X, int np,
+                 float *__restrict__ Y)
+{
+    static_assert(TN % 64 == 0 && TN <= 256, "TN: 64, 128, 192 or 256 positions");
+    constexpr int kWUnits = kTcM * (kTcK / 8) / kTcThreads;  // 2
+    constexpr int kXUnits = TN * (kTcK / 8) / kTcThreads;    // 1 .. 4
+    constexpr uint32_t kPlaneW = kTcM * kTcK * 2, kPlaneX = TN * kTcK * 2;
+    constexpr uint32_t kStage = tc_stage_bytes(TN);
+    constexpr uint32_t kIdesc = umma_idesc(TN);
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) unsigned long long bars[kTcStages];
+    __shared__ uint32_t tmem_slot;
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int r0 = blockIdx.x * kTcM, p0 = blockIdx.y * TN;
+    const int nk = (L.cols + kTcK - 1) / kTcK;
+    const uint32_t smem0 = (uint32_t)__cvta_generic_to_shared(smem);
+    const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]);
+
+    if (tid == 0) {
+        for (int i = 0; i < kTcStages; ++i) mbar_init(bar0 + 8u * i, 1u);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         (uint32_t)__cvta_generic_to_shared(&tmem_slot)),
+                     "r"((uint32_t)TN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    // This thread's staging units: unit u of a plane holds 8 K values of
+    // tile row (u >> 6) * 8 + (u & 7), K offset ((u >> 3) & 7) * 8 in the
+    // stage, at byte u * 16.
+    const uint8_t *wrow[kWUnits];
+    int wk[kWUnits];
+    const float *xrow[kXUnits];
+    int xk[kXUnits];
+#pragma unroll
+    for (int i = 0; i < kWUnits; ++i) {
+        const int u = tid + i * kTcThreads;
+        const int row = r0 + (u >> 6) * 8 + (u & 7);
+        wrow[i] = row < L.rows ? w + (uint64_t)row * L.row_stride : nullptr;
+        wk[i] = ((u >> 3) & 7) * 8;
+    }
+#pragma unroll
+    for (int i = 0; i < kXUnits; ++i) {
+        const int u = tid + i * kTcThreads;
+        const int pos = p0 + (u >> 6) * 8 + (u & 7);
+        xrow[i] = pos < np ? X + (size_t)pos * L.cols : nullptr;
+        xk[i] = ((u >> 3) & 7) * 8;
+    }
+
+    Raw8<FMT> wr[kWUnits];
+    float4 xr[kXUnits][2];
+    auto load_stage = [&](int kc, Raw8<FMT> *w_out, float4 (*x_out)[2]) {
+#pragma unroll
+        for (int i = 0; i < kWUnits; ++i) {
+            const int k0 = kc * kTcK + wk[i];
+            if (wrow[i] != nullptr && k0 < L.cols) w_out[i].load(wrow[i], L, k0);
+        }
+#pragma unroll
+        for (int i = 0; i < kXUnits; ++i) {
+            const int k0 = kc * kTcK + xk[i];
+            if (xrow[i] != nullptr && k0 < L.cols) {
+                x_out[i][0] = __ldg((const float4 *)(xrow[i] + k0));
+                x_out[i][1] = __ldg((const float4 *)(xrow[i] + k0 + 4));
+            } else {
+                x_out[i][0] = x_out[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+    };
+    load_stage(0, wr, xr);
+
+    bool finite = true, ok = true;
+    for (int kc = 0; kc < nk; ++kc) {
+        const int s = kc % kTcStages;
+        Raw8<FMT> wn[kWUnits];
+        float4 xn[kXUnits][2];
+        if (kc + 1 < nk) load_stage(kc + 1, wn, xn);
+        // the MMAs that last read stage s (iteration kc - kTcStages) are done
+        if (kc >= kTcStages && !mbar_wait(bar0 + 8u * s, (uint32_t)((kc / kTcStages - 1) & 1))) ok = false;
+        if (__syncthreads_or(!ok)) {
+            ok = false;
+            break;
+        }
+        uint8_t *st = smem + (size_t)s * kStage;
+#pragma unroll
+        for (int i = 0; i < kWUnits; ++i) {
+            const int u = tid + i * kTcThreads;
+            const int k0 = kc * kTcK + wk[i];
+            float v[8];
+            if (wrow[i] != nullptr && k0 < L.cols) {
+                finite &= wr[i].decode(k0, v);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = 0.f;
+            }
+            split_store(v, st, st + kPlaneW, (uint32_t)u * 16u);
+        }
+#pragma unroll
+        for (int i = 0; i < kXUnits; ++i) {
+            const int u = tid + i * kTcThreads;
+            finite &= x_in_range(xr[i][0], xr[i][1]);
+            const float v[8] = {xr[i][0].x, xr[i][0].y, xr[i][0].z, xr[i][0].w,
+                                xr[i][1].x, xr[i][1].y, xr[i][1].z, xr[i][1].w};
+            split_store(v, st + 2 * kPlaneW, st + 2 * kPlaneW + kPlaneX, (uint32_t)u * 16u);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t a_h = smem0 + (uint32_t)s * kStage, a_l = a_h + kPlaneW;
+            const uint32_t b_h = a_h + 2 * kPlaneW, b_l = b_h + kPlaneX;
+#pragma unroll
+            for (int j = 0; j < kTcK / 16; ++j) {
+                const uint32_t o = 256u * j;  // two core matrices along K per slice
+                umma_bf16(tmem, umma_desc(a_h + o), umma_desc(b_h + o), kIdesc, (kc | j) != 0);
+                umma_bf16(tmem, umma_desc(a_l + o), umma_desc(b_h + o), kIdesc, 1u);
+                umma_bf16(tmem, umma_desc(a_h + o), umma_desc(b_l + o), kIdesc, 1u);
+            }
+            umma_commit(bar0 + 8u * s);
+        }
+#pragma unroll
+        for (int i = 0; i < kWUnits; ++i) wr[i] = wn[i];
+#pragma unroll
+        for (int i = 0; i < kXUnits; ++i) {
+            xr[i][0] = xn[i][0];
+            xr[i][1] = xn[i][1];
+        }
+    }
+
+    // every MMA has completed once the last stage's commit has arrived
+    if (ok) {
+        const int last = nk - 1;
+        if (!mbar_wait(bar0 + 8u * (last % kTcStages), (uint32_t)((last / kTcStages) & 1))) ok = false;
+    }
+    const bool failed = __syncthreads_or(!ok);
+    const bool fallback = __syncthreads_or(!finite);
+    tc_fence_after();
+    if (failed) {
+        if (tid == 0) atomicOr(&g_status, kStatusMmaTimeout);
+    } else if (fallback) {
+        tc_tile_fallback<FMT>(L, w, X, np, Y, r0, p0, TN);
+    } else {
+        const int q = warp & 3;
+        constexpr int kColsPerWarp = TN / 4;
+        const int c0 = (warp >> 2) * kColsPerWarp;
+        const int row = r0 + 32 * q + (tid & 31);
+#pragma unroll
+        for (int c = 0; c < kColsPerWarp; c += 8) {
+            float v[8];
+            tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(c0 + c), v);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            if (row < L.rows) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int pos = p0 + c0 + c + i;
+                    if (pos < np) Y[(size_t)pos * L.rows + row] = v[i];
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)TN));
+    }
+}
+
 // ------------------------------------------------------------- argmax
 
 __global__ void __launch_bounds__(kThreads)
@@ -1444,10 +1880,37 @@ cudaError_t matmul_go(const Layout &L, const uint8_t *w, const float *X, int bat
     return cudaSuccess;
 }
 
+int g_matmul_path = 0;  // 0 auto, 1 CUDA cores (dp4a), 2 tensor cores
+
+// Batches of at least this many positions take the tensor-core kernel.
+constexpr int kTcMinBatch = 32;
+
+template <uint32_t FMT, int TN>
+cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
+                         cudaStream_t s)
+{
+    auto kernel = matmul_tc_kernel<FMT, TN>;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = allow_max_smem((const void *)kernel, dev);
+    if (e != cudaSuccess) return e;
+    const dim3 grid((unsigned)((L.rows + kTcM - 1) / kTcM), (unsigned)((batch + TN - 1) / TN));
+    if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
+    kernel<<<grid, kTcThreads, (size_t)kTcStages * tc_stage_bytes(TN), s>>>(L, w, X, batch, Y);
+    return cudaGetLastError();
+}
+
 template <uint32_t FMT>
 cudaError_t matmul_fmt(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
                        cudaStream_t s)
 {
+    // the tensor-core kernel reads x with 16-byte loads
+    const bool tc_ok = ((uintptr_t)X & 15u) == 0;
+    if (g_matmul_path == 2 || (g_matmul_path == 0 && batch >= kTcMinBatch && tc_ok)) {
+        if (!tc_ok) return cudaErrorMisalignedAddress;
+        if (batch <= 64) return matmul_tc_go<FMT, 64>(L, w, X, batch, Y, s);
+        return matmul_tc_go<FMT, 128>(L, w, X, batch, Y, s);
+    }
     if (L.C <= 16) return matmul_go<FMT, 16>(L, w, X, batch, Y, s);
     return matmul_go<FMT, 32>(L, w, X, batch, Y, s);
 }
@@ -1575,6 +2038,7 @@ cudaError_t launch_matmul(const Layout &L, const uint8_t *w, const float *X, int
 }
 
 void set_gemv_path(int path) { g_gemv_path = path; }
+void set_matmul_path(int path) { g_matmul_path = path; }
 
 size_t exchange_parity_bytes(int world, int slot_rows)
 {

@@ -212,6 +212,104 @@ def test_matmul_parity(cuda, qmv, oracle, workloads, gtype, rows, cols, batch):
         assert bad.size == 0, (p, bad[:5])
 
 
+# ------------------------------------------------ matmul (tensor cores)
+
+@pytest.fixture
+def tensor_cores(qmv):
+    """Force the tcgen05 kernel (the automatic choice takes it from 32
+    positions up)."""
+    qmv.set_matmul_path(qmv.MATMUL_TENSOR_CORES)
+    yield
+    qmv.set_matmul_path(qmv.MATMUL_AUTO)
+
+
+def abs_dot_all(oracle, gtype, blocks, rows, cols, X):
+    """sum_k |w_k x_k| for every (position, row), from the oracle's dequantised
+    weights (bit-exact with the reference's), in float64."""
+    W = oracle.dequant(gtype, blocks, rows * cols // BE[gtype]).reshape(rows, cols)
+    return np.abs(np.asarray(X, np.float64)) @ np.abs(W.astype(np.float64)).T
+
+
+def device_matmul(torch, qmv, gtype, blocks, rows, cols, X):
+    w = qmv.Weight(gtype, blocks, rows, cols)
+    Xd = to_dev(torch, np.asarray(X, np.float32))
+    Yd = torch.full((X.shape[0], rows), float("nan"), dtype=torch.float32, device="cuda")
+    w.matmul(Xd.data_ptr(), X.shape[0], Yd.data_ptr())
+    torch.cuda.synchronize()
+    w.free()
+    return Yd.cpu().numpy()
+
+
+@pytest.mark.parametrize("gtype,rows,cols,batch", [
+    (Q5_0, 4864, 896, 512),   # the batched-prefill benchmark shape, every output checked
+    (Q8_0, 300, 896, 70), (Q5_0, 257, 96, 1), (Q4_K, 129, 3584, 33), (Q6_K, 129, 3584, 130),
+    (Q4_K, 40, 18944, 64), (Q6_K, 1000, 256, 200), (Q8_0, 128, 32, 13), (Q5_0, 131, 64, 257)])
+def test_matmul_tensor_cores(cuda, qmv, oracle, workloads, tensor_cores, gtype, rows, cols, batch):
+    """tcgen05 kernel (bf16 hi/lo operand splits, fp32 accumulation) against
+    the oracle over whole outputs: partial row tiles, partial position tiles,
+    a K tail shorter than one 64-wide stage, and long rows."""
+    torch = cuda
+    blocks = workloads.make_blocks(gtype, rows, cols, seed=3)
+    X = np.stack([workloads.make_activations(cols, seed=50 + p) for p in range(batch)])
+    Y = device_matmul(torch, qmv, gtype, blocks, rows, cols, X)
+    Y_ref = oracle.matmul(gtype, blocks, rows, cols, X, batch)
+    S = abs_dot_all(oracle, gtype, blocks, rows, cols, X)
+    bad, err, bound = tolerance_ok(Y.ravel(), Y_ref.ravel(), S.ravel(), REL_TOL)
+    assert bad.size == 0, (bad[:5], err[bad[:5]], bound[bad[:5]])
+    assert np.isfinite(Y).all()
+    assert qmv.device_status(clear=True) == 0
+
+
+def test_matmul_automatic_choice_is_tensor_cores(cuda, qmv, workloads):
+    """From 32 positions the automatic choice runs the tensor-core kernel: its
+    output equals the forced kernel's bit for bit (the kernel is
+    deterministic), and differs from the CUDA-core kernel's."""
+    torch = cuda
+    rows, cols, batch = 4864, 896, 64
+    blocks = workloads.make_blocks(Q5_0, rows, cols, seed=9)
+    X = np.stack([workloads.make_activations(cols, seed=90 + p) for p in range(batch)])
+    outs = {}
+    for path in (qmv.MATMUL_AUTO, qmv.MATMUL_TENSOR_CORES, qmv.MATMUL_CUDA_CORES):
+        qmv.set_matmul_path(path)
+        try:
+            outs[path] = device_matmul(torch, qmv, Q5_0, blocks, rows, cols, X)
+        finally:
+            qmv.set_matmul_path(qmv.MATMUL_AUTO)
+    assert np.array_equal(f32_bits(outs[qmv.MATMUL_AUTO]), f32_bits(outs[qmv.MATMUL_TENSOR_CORES]))
+    assert not np.array_equal(f32_bits(outs[qmv.MATMUL_AUTO]), f32_bits(outs[qmv.MATMUL_CUDA_CORES]))
+
+
+@pytest.mark.parametrize("gtype", [Q8_0, Q5_0, Q4_K, Q6_K])
+def test_matmul_tensor_cores_nonfinite(cuda, qmv, oracle, workloads, tensor_cores, gtype):
+    """Tiles holding an Inf/NaN scale, an Inf x, or an x beyond the bf16 range
+    are recomputed in fp32: Inf and NaN land where the reference's loop puts
+    them, every finite output stays inside the bound, and the other tiles
+    still take the tensor cores."""
+    torch = cuda
+    rows, cols, batch = 300, 512, 70
+    blocks = workloads.make_blocks(gtype, rows, cols, seed=5).copy()
+    nb = cols // BE[gtype]
+    off = 208 if gtype == Q6_K else 0
+    for row, blk, h in [(3, 0, 0x7C00), (140, nb - 1, 0x7E01), (141, 1, 0xFC00)]:
+        b = blocks.reshape(rows, nb, BB[gtype])[row, blk]
+        b[off:off + 2] = [h & 0xFF, h >> 8]
+    X = np.stack([workloads.make_activations(cols, seed=60 + p) for p in range(batch)])
+    X[2, 17] = np.inf
+    X[66, 300] = np.float32(3.3999e38)
+    Y = device_matmul(torch, qmv, gtype, blocks, rows, cols, X)
+    Y_ref = oracle.matmul(gtype, blocks, rows, cols, X, batch)
+    assert np.array_equal(np.isnan(Y), np.isnan(Y_ref))
+    assert np.array_equal(np.isposinf(Y), np.isposinf(Y_ref))
+    assert np.array_equal(np.isneginf(Y), np.isneginf(Y_ref))
+    assert not np.isfinite(Y_ref).all()
+    with np.errstate(invalid="ignore", over="ignore"):
+        S = abs_dot_all(oracle, gtype, blocks, rows, cols, X)
+    fin = np.isfinite(Y_ref) & np.isfinite(S)
+    bad, err, bound = tolerance_ok(Y[fin], Y_ref[fin], S[fin], REL_TOL)
+    assert bad.size == 0, (bad[:5], err[bad[:5]], bound[bad[:5]])
+    assert qmv.device_status(clear=True) == 0
+
+
 # -------------------------------------------------------------- argmax
 
 def test_argmax_known_answers(cuda, qmv):
