@@ -62,8 +62,9 @@ int qmv_set_gemv_path(int path);
  * (tensor cores, tcgen05 with bf16 hi/lo operand splits and fp32
  * accumulation, from 32 positions when X is 16-byte aligned; CUDA-core dp4a
  * kernel otherwise), 1 = CUDA cores only, 2 = tensor cores only (a misaligned
- * X then fails).  No counterpart in the reference; both paths compute the
- * same function within the parity bound. */
+ * X then fails), 64 / 128 / 176 / 256 = tensor cores with that many positions
+ * per tile (normally chosen from the shape).  No counterpart in the
+ * reference; all paths compute the same function within the parity bound. */
 int qmv_set_matmul_path(int path);
 
 /* ---- residency of packed tensors ----------------------------------------

@@ -265,7 +265,8 @@ MATMUL_AUTO, MATMUL_CUDA_CORES, MATMUL_TENSOR_CORES = 0, 1, 2
 
 
 def set_matmul_path(path: int):
-    """0 automatic, 1 CUDA-core (dp4a) kernel, 2 tensor-core (tcgen05) kernel."""
+    """0 automatic, 1 CUDA-core (dp4a) kernel, 2 tensor-core (tcgen05) kernel,
+    64/128/176/256 tensor-core kernel with that position-tile width."""
     _check(lib().qmv_set_matmul_path(path), "qmv_set_matmul_path")
 
 

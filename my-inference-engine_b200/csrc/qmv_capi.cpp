@@ -259,7 +259,8 @@ QMV_EXPORT int qmv_set_gemv_path(int path)
 
 QMV_EXPORT int qmv_set_matmul_path(int path)
 {
-    if (path < 0 || path > 2) return fail("matmul path must be 0, 1 or 2");
+    if (!(path == 0 || path == 1 || path == 2 || path == 64 || path == 128 || path == 176 || path == 256))
+        return fail("matmul path must be 0, 1, 2, 64, 128, 176 or 256");
     qmv::set_matmul_path(path);
     return 1;
 }

@@ -101,7 +101,8 @@ cudaError_t launch_matmul(const Layout &L, const uint8_t *w, const float *X, int
 // shared memory, direct loads otherwise), 1 direct loads, 2 TMA pipeline only.
 void set_gemv_path(int path);
 // Matmul kernel selection: 0 automatic (tensor cores from 32 positions when X
-// is 16-byte aligned), 1 CUDA cores (dp4a), 2 tensor cores only.
+// is 16-byte aligned), 1 CUDA cores (dp4a), 2 tensor cores only, 64 / 128 /
+// 176 / 256 tensor cores with that position-tile width.
 void set_matmul_path(int path);
 // Device status bits set by bounded waits that expired (0 = healthy).
 cudaError_t read_status(unsigned int *out, bool clear);

@@ -1042,7 +1042,7 @@ matmul_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__
 constexpr int kTcM = 128;         // rows per tile = accumulator lanes
 constexpr int kTcK = 64;          // K per stage
 constexpr int kTcThreads = 512;
-constexpr int kTcStages = 3;
+constexpr uint32_t kTcSmemBudget = 200u * 1024u;
 constexpr unsigned int kStatusMmaTimeout = 16u;
 
 __host__ __device__ constexpr uint32_t tc_stage_bytes(int tn)
@@ -1050,11 +1050,36 @@ __host__ __device__ constexpr uint32_t tc_stage_bytes(int tn)
     return 2u * kTcM * kTcK * 2u + 2u * (uint32_t)tn * kTcK * 2u;
 }
 
+// Stages that fit the shared-memory budget (2 .. 4).
+__host__ __device__ constexpr int tc_stages(int tn)
+{
+    return kTcSmemBudget / tc_stage_bytes(tn) > 4 ? 4 : (int)(kTcSmemBudget / tc_stage_bytes(tn));
+}
+
 __device__ __forceinline__ uint32_t ldg16(const uint8_t *p) { return __ldg((const unsigned short *)p); }
+
+// 2^23 + (byte I of w), exactly: the byte becomes the low mantissa bits of a
+// float whose exponent is that of 2^23.  Integer-to-float without the
+// conversion pipe; callers subtract 2^23 (plus any offset) exactly.
+template <int I>
+__device__ __forceinline__ float u8_magic(uint32_t w)
+{
+    return __uint_as_float(__byte_perm(w, 0x4b000000u, 0x7540u | I));
+}
+
+// v[4 j + i] = (2^23 + byte i of n[j]) - bias, exact for bias = 2^23 + offset
+__device__ __forceinline__ void bytes_to_float(uint32_t n0, uint32_t n1, float bias, float v[8])
+{
+    v[0] = u8_magic<0>(n0) - bias; v[1] = u8_magic<1>(n0) - bias;
+    v[2] = u8_magic<2>(n0) - bias; v[3] = u8_magic<3>(n0) - bias;
+    v[4] = u8_magic<0>(n1) - bias; v[5] = u8_magic<1>(n1) - bias;
+    v[6] = u8_magic<2>(n1) - bias; v[7] = u8_magic<3>(n1) - bias;
+}
 
 // Raw bytes of 8 consecutive weights (k0 .. k0 + 7, k0 a multiple of 8) of
 // one resident row, and their decoding to fp32 with the reference's
-// arithmetic (src/quantization.cpp:54-67, 161-184, 380-409, 588-615).
+// arithmetic (src/quantization.cpp:54-67, 161-184, 380-409, 588-615): every
+// product below is exact or rounds once, as there.
 template <uint32_t FMT> struct Raw8;
 
 template <> struct Raw8<kQ8_0> {
@@ -1068,11 +1093,11 @@ template <> struct Raw8<kQ8_0> {
     }
     __device__ __forceinline__ bool decode(int, float v[8]) const
     {
+        // signed bytes biased by 128 so that they read as unsigned
+        bytes_to_float(q.x ^ 0x80808080u, q.y ^ 0x80808080u, 8388736.0f, v);
         const float s = f16_fast(d);
-        v[0] = s * (float)sbyte<0>(q.x); v[1] = s * (float)sbyte<1>(q.x);
-        v[2] = s * (float)sbyte<2>(q.x); v[3] = s * (float)sbyte<3>(q.x);
-        v[4] = s * (float)sbyte<0>(q.y); v[5] = s * (float)sbyte<1>(q.y);
-        v[6] = s * (float)sbyte<2>(q.y); v[7] = s * (float)sbyte<3>(q.y);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(s, v[i]);
         return (d & 0x7c00u) != 0x7c00u;
     }
 };
@@ -1090,15 +1115,14 @@ template <> struct Raw8<kQ5_0> {
     __device__ __forceinline__ bool decode(int k0, float v[8]) const
     {
         // weight i of the block: low nibble of byte i (i < 16) or high nibble
-        // of byte i - 16, fifth bit = bit i of qh
+        // of byte i - 16, fifth bit = bit i of qh; value (n - 16) * d
         const int sh = (k0 & 16) ? 4 : 0;
+        const uint32_t n0 = ((q.x >> sh) & 0x0f0f0f0fu) | spread4(qh);
+        const uint32_t n1 = ((q.y >> sh) & 0x0f0f0f0fu) | spread4(qh >> 4);
+        bytes_to_float(n0, n1, 8388624.0f, v);
         const float s = f16_fast(d);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t byte = ((i < 4 ? q.x : q.y) >> (8 * (i & 3))) & 0xffu;
-            const int n = (int)(((byte >> sh) & 15u) | (((qh >> i) & 1u) << 4));
-            v[i] = s * (float)(n - 16);
-        }
+        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(s, v[i]);
         return (d & 0x7c00u) != 0x7c00u;
     }
 };
@@ -1129,11 +1153,11 @@ template <> struct Raw8<kQ4_K> {
         const float scale = __fmul_rn(f16_fast(hdr.x & 0xffffu), (float)sc);
         const float minimum = __fmul_rn(f16_fast(hdr.x >> 16), (float)mn);
         const int sh = 4 * (j & 1);
+        bytes_to_float((q.x >> sh) & 0x0f0f0f0fu, (q.y >> sh) & 0x0f0f0f0fu, 8388608.0f, v);
+        // scale * q is exact, so one fused rounding equals the reference's
+        // multiply-then-subtract
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t byte = ((i < 4 ? q.x : q.y) >> (8 * (i & 3))) & 0xffu;
-            v[i] = __fsub_rn(__fmul_rn(scale, (float)((byte >> sh) & 15u)), minimum);
-        }
+        for (int i = 0; i < 8; ++i) v[i] = __fmaf_rn(scale, v[i], -minimum);
         return (hdr.x & 0x7c00u) != 0x7c00u && (hdr.x & 0x7c000000u) != 0x7c000000u;
     }
 };
@@ -1158,39 +1182,44 @@ template <> struct Raw8<kQ6_K> {
         const int s = (int)(int8_t)((sc >> (8 * r)) & 0xffu);
         const float ds = __fmul_rn(f16_fast(d), (float)s);
         const int shl = 4 * (r >> 1), shh = 2 * r;
+        const uint32_t n0 = ((ql.x >> shl) & 0x0f0f0f0fu) | (((qh.x >> shh) & 0x03030303u) << 4);
+        const uint32_t n1 = ((ql.y >> shl) & 0x0f0f0f0fu) | (((qh.y >> shh) & 0x03030303u) << 4);
+        bytes_to_float(n0, n1, 8388640.0f, v);  // n - 32
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t lo = ((i < 4 ? ql.x : ql.y) >> (8 * (i & 3))) & 0xffu;
-            const uint32_t hi = ((i < 4 ? qh.x : qh.y) >> (8 * (i & 3))) & 0xffu;
-            const int n = (int)(((lo >> shl) & 15u) | (((hi >> shh) & 3u) << 4));
-            v[i] = __fmul_rn(ds, (float)(n - 32));
-        }
+        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(ds, v[i]);
         return (d & 0x7c00u) != 0x7c00u;
     }
 };
 
-__device__ __forceinline__ uint32_t bf16x2_bits(__nv_bfloat162 h)
+// x rounded to 8 significant bits (nearest), as an fp32 whose low 16 bits
+// are zero, i.e. an exact bf16: Veltkamp's splitting with 2^16 + 1.  The
+// explicitly rounded operations keep the compiler from contracting them.
+__device__ __forceinline__ float round8(float x)
 {
-    return (uint32_t)__bfloat16_as_ushort(h.x) | ((uint32_t)__bfloat16_as_ushort(h.y) << 16);
+    const float t = __fmul_rn(x, 65537.0f);
+    return __fsub_rn(t, __fsub_rn(t, x));
 }
 
-// Split 8 floats into bf16 high and low planes (v ~= hi + lo, element 0 at
-// the lowest address) and store both 16-byte units.
+// Split 8 floats into bf16 high and low planes, v = hi + lo + e with
+// |hi - v| <= 2^-8 |v| and |e| <= 2^-16 |v|, and store both 16-byte units
+// (element 0 at the lowest address).  FMA-pipe arithmetic and byte permutes
+// only.  |v| must stay below 2^111 (65537 v finite).
 __device__ __forceinline__ void split_store(const float v[8], uint8_t *hi_plane, uint8_t *lo_plane, uint32_t off)
 {
     uint32_t h[4], l[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const __nv_bfloat162 hb = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-        const float2 hf = __bfloat1622float2(hb);
-        h[j] = bf16x2_bits(hb);
-        l[j] = bf16x2_bits(__floats2bfloat162_rn(v[2 * j] - hf.x, v[2 * j + 1] - hf.y));
+        const float h0 = round8(v[2 * j]), h1 = round8(v[2 * j + 1]);
+        const float l0 = round8(__fsub_rn(v[2 * j], h0)), l1 = round8(__fsub_rn(v[2 * j + 1], h1));
+        h[j] = __byte_perm(__float_as_uint(h0), __float_as_uint(h1), 0x7632u);
+        l[j] = __byte_perm(__float_as_uint(l0), __float_as_uint(l1), 0x7632u);
     }
     *(uint4 *)(hi_plane + off) = make_uint4(h[0], h[1], h[2], h[3]);
     *(uint4 *)(lo_plane + off) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-// true when every x rounds to a finite bf16 (|x| below 0x7F7F8000 as bits)
+// true when every |x| < 2^111, the range split_store handles (NaN and Inf
+// fail)
 __device__ __forceinline__ bool x_in_range(const float4 &a, const float4 &b)
 {
     uint32_t m = __float_as_uint(a.x) & 0x7fffffffu;
@@ -1201,7 +1230,7 @@ __device__ __forceinline__ bool x_in_range(const float4 &a, const float4 &b)
     m = max(m, __float_as_uint(b.y) & 0x7fffffffu);
     m = max(m, __float_as_uint(b.z) & 0x7fffffffu);
     m = max(m, __float_as_uint(b.w) & 0x7fffffffu);
-    return m < 0x7f7f8000u;
+    return m < 0x77000000u;
 }
 
 // Shared-memory matrix descriptor, K-major, no swizzle: core matrices along
@@ -1277,15 +1306,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ X, int np,
                  float *__restrict__ Y)
 {
-    static_assert(TN % 64 == 0 && TN <= 256, "TN: 64, 128, 192 or 256 positions");
-    constexpr int kWUnits = kTcM * (kTcK / 8) / kTcThreads;  // 2
-    constexpr int kXUnits = TN * (kTcK / 8) / kTcThreads;    // 1 .. 4
+    static_assert(TN % 16 == 0 && TN >= 32 && TN <= 256, "N of one MMA: a multiple of 16 in 32..256");
+    constexpr int kStages = tc_stages(TN);
+    constexpr int kWUnits = kTcM * (kTcK / 8) / kTcThreads;                 // 2
+    constexpr int kXUnits = (TN * (kTcK / 8) + kTcThreads - 1) / kTcThreads;  // 1 .. 4
     constexpr uint32_t kPlaneW = kTcM * kTcK * 2, kPlaneX = TN * kTcK * 2;
     constexpr uint32_t kStage = tc_stage_bytes(TN);
     constexpr uint32_t kIdesc = umma_idesc(TN);
+    constexpr uint32_t kTmemCols = TN <= 32 ? 32u : TN <= 64 ? 64u : TN <= 128 ? 128u : 256u;
 
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) unsigned long long bars[kTcStages];
+    __shared__ __align__(8) unsigned long long bars[kStages];
     __shared__ uint32_t tmem_slot;
 
     const int tid = threadIdx.x, warp = tid >> 5;
@@ -1295,13 +1326,13 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
     const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]);
 
     if (tid == 0) {
-        for (int i = 0; i < kTcStages; ++i) mbar_init(bar0 + 8u * i, 1u);
+        for (int i = 0; i < kStages; ++i) mbar_init(bar0 + 8u * i, 1u);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          (uint32_t)__cvta_generic_to_shared(&tmem_slot)),
-                     "r"((uint32_t)TN));
+                     "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
@@ -1311,7 +1342,8 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
 
     // This thread's staging units: unit u of a plane holds 8 K values of
     // tile row (u >> 6) * 8 + (u & 7), K offset ((u >> 3) & 7) * 8 in the
-    // stage, at byte u * 16.
+    // stage, at byte u * 16 (core matrix (row / 8, K / 8) at 1024 (row / 8)
+    // + 128 (K / 8)).
     const uint8_t *wrow[kWUnits];
     int wk[kWUnits];
     const float *xrow[kXUnits];
@@ -1327,7 +1359,7 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
     for (int i = 0; i < kXUnits; ++i) {
         const int u = tid + i * kTcThreads;
         const int pos = p0 + (u >> 6) * 8 + (u & 7);
-        xrow[i] = pos < np ? X + (size_t)pos * L.cols : nullptr;
+        xrow[i] = (u < TN * (kTcK / 8) && pos < np) ? X + (size_t)pos * L.cols : nullptr;
         xk[i] = ((u >> 3) & 7) * 8;
     }
 
@@ -1354,12 +1386,12 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
 
     bool finite = true, ok = true;
     for (int kc = 0; kc < nk; ++kc) {
-        const int s = kc % kTcStages;
+        const int s = kc % kStages;
         Raw8<FMT> wn[kWUnits];
         float4 xn[kXUnits][2];
         if (kc + 1 < nk) load_stage(kc + 1, wn, xn);
-        // the MMAs that last read stage s (iteration kc - kTcStages) are done
-        if (kc >= kTcStages && !mbar_wait(bar0 + 8u * s, (uint32_t)((kc / kTcStages - 1) & 1))) ok = false;
+        // the MMAs that last read stage s (iteration kc - kStages) are done
+        if (kc >= kStages && !mbar_wait(bar0 + 8u * s, (uint32_t)((kc / kStages - 1) & 1))) ok = false;
         if (__syncthreads_or(!ok)) {
             ok = false;
             break;
@@ -1381,10 +1413,12 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
 #pragma unroll
         for (int i = 0; i < kXUnits; ++i) {
             const int u = tid + i * kTcThreads;
-            finite &= x_in_range(xr[i][0], xr[i][1]);
-            const float v[8] = {xr[i][0].x, xr[i][0].y, xr[i][0].z, xr[i][0].w,
-                                xr[i][1].x, xr[i][1].y, xr[i][1].z, xr[i][1].w};
-            split_store(v, st + 2 * kPlaneW, st + 2 * kPlaneW + kPlaneX, (uint32_t)u * 16u);
+            if (u < TN * (kTcK / 8)) {
+                finite &= x_in_range(xr[i][0], xr[i][1]);
+                const float v[8] = {xr[i][0].x, xr[i][0].y, xr[i][0].z, xr[i][0].w,
+                                    xr[i][1].x, xr[i][1].y, xr[i][1].z, xr[i][1].w};
+                split_store(v, st + 2 * kPlaneW, st + 2 * kPlaneW + kPlaneX, (uint32_t)u * 16u);
+            }
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
@@ -1413,7 +1447,7 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
     // every MMA has completed once the last stage's commit has arrived
     if (ok) {
         const int last = nk - 1;
-        if (!mbar_wait(bar0 + 8u * (last % kTcStages), (uint32_t)((last / kTcStages) & 1))) ok = false;
+        if (!mbar_wait(bar0 + 8u * (last % kStages), (uint32_t)((last / kStages) & 1))) ok = false;
     }
     const bool failed = __syncthreads_or(!ok);
     const bool fallback = __syncthreads_or(!finite);
@@ -1423,19 +1457,18 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
     } else if (fallback) {
         tc_tile_fallback<FMT>(L, w, X, np, Y, r0, p0, TN);
     } else {
+        // warp w reads lanes 32 (w % 4) .. + 31; the four warps sharing a lane
+        // quarter take 8-column chunks round-robin
         const int q = warp & 3;
-        constexpr int kColsPerWarp = TN / 4;
-        const int c0 = (warp >> 2) * kColsPerWarp;
         const int row = r0 + 32 * q + (tid & 31);
-#pragma unroll
-        for (int c = 0; c < kColsPerWarp; c += 8) {
+        for (int c = 8 * (warp >> 2); c < TN; c += 8 * (kTcThreads / 128)) {
             float v[8];
-            tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(c0 + c), v);
+            tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             if (row < L.rows) {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    const int pos = p0 + c0 + c + i;
+                    const int pos = p0 + c + i;
                     if (pos < np) Y[(size_t)pos * L.rows + row] = v[i];
                 }
             }
@@ -1445,7 +1478,7 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)TN));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
 }
 
@@ -1880,7 +1913,9 @@ cudaError_t matmul_go(const Layout &L, const uint8_t *w, const float *X, int bat
     return cudaSuccess;
 }
 
-int g_matmul_path = 0;  // 0 auto, 1 CUDA cores (dp4a), 2 tensor cores
+// 0 auto, 1 CUDA cores (dp4a), 2 tensor cores, 64/128/176/256 tensor cores
+// with that position-tile width
+int g_matmul_path = 0;
 
 // Batches of at least this many positions take the tensor-core kernel.
 constexpr int kTcMinBatch = 32;
@@ -1896,8 +1931,31 @@ cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const float *X, int 
     if (e != cudaSuccess) return e;
     const dim3 grid((unsigned)((L.rows + kTcM - 1) / kTcM), (unsigned)((batch + TN - 1) / TN));
     if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
-    kernel<<<grid, kTcThreads, (size_t)kTcStages * tc_stage_bytes(TN), s>>>(L, w, X, batch, Y);
+    kernel<<<grid, kTcThreads, (size_t)tc_stages(TN) * tc_stage_bytes(TN), s>>>(L, w, X, batch, Y);
     return cudaGetLastError();
+}
+
+// Position-tile width of the tensor-core kernel: the candidate with the
+// smallest (waves of one-CTA-per-SM tiles) x (per-stage cost), where a
+// stage costs max(decode of 128 x 64 weights + split of TN x 64 x values,
+// 3 x 4 MMAs of 128 x TN x 16), in SM cycles measured on B200.
+int tc_tile_width(int rows, int batch)
+{
+    static const int cand[] = {64, 128, 176, 256};
+    const long long row_tiles = (rows + kTcM - 1) / kTcM;
+    int best = 64;
+    double best_cost = 1e300;
+    for (int tn : cand) {
+        const long long tiles = row_tiles * ((batch + tn - 1) / tn);
+        const long long waves = (tiles + sm_count() - 1) / sm_count();
+        const double alu = 700.0 + 4.0 * tn, mma = 8.4 * tn;
+        const double cost = (double)waves * (alu > mma ? alu : mma);
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = tn;
+        }
+    }
+    return best;
 }
 
 template <uint32_t FMT>
@@ -1906,10 +1964,14 @@ cudaError_t matmul_fmt(const Layout &L, const uint8_t *w, const float *X, int ba
 {
     // the tensor-core kernel reads x with 16-byte loads
     const bool tc_ok = ((uintptr_t)X & 15u) == 0;
-    if (g_matmul_path == 2 || (g_matmul_path == 0 && batch >= kTcMinBatch && tc_ok)) {
+    if (g_matmul_path >= 2 || (g_matmul_path == 0 && batch >= kTcMinBatch && tc_ok)) {
         if (!tc_ok) return cudaErrorMisalignedAddress;
-        if (batch <= 64) return matmul_tc_go<FMT, 64>(L, w, X, batch, Y, s);
-        return matmul_tc_go<FMT, 128>(L, w, X, batch, Y, s);
+        switch (g_matmul_path > 2 ? g_matmul_path : tc_tile_width(L.rows, batch)) {
+        case 64: return matmul_tc_go<FMT, 64>(L, w, X, batch, Y, s);
+        case 128: return matmul_tc_go<FMT, 128>(L, w, X, batch, Y, s);
+        case 176: return matmul_tc_go<FMT, 176>(L, w, X, batch, Y, s);
+        default: return matmul_tc_go<FMT, 256>(L, w, X, batch, Y, s);
+        }
     }
     if (L.C <= 16) return matmul_go<FMT, 16>(L, w, X, batch, Y, s);
     return matmul_go<FMT, 32>(L, w, X, batch, Y, s);

@@ -260,6 +260,26 @@ def test_matmul_tensor_cores(cuda, qmv, oracle, workloads, tensor_cores, gtype, 
     assert qmv.device_status(clear=True) == 0
 
 
+@pytest.mark.parametrize("tile", [64, 128, 176, 256])
+def test_matmul_tensor_core_tile_widths(cuda, qmv, oracle, workloads, tile):
+    """Every position-tile width the kernel is built for, on a shape with a
+    partial last tile in both rows and positions and a K tail."""
+    torch = cuda
+    gtype, rows, cols, batch = Q6_K, 200, 768, 300
+    blocks = workloads.make_blocks(gtype, rows, cols, seed=11)
+    X = np.stack([workloads.make_activations(cols, seed=70 + p) for p in range(batch)])
+    qmv.set_matmul_path(tile)
+    try:
+        Y = device_matmul(torch, qmv, gtype, blocks, rows, cols, X)
+    finally:
+        qmv.set_matmul_path(qmv.MATMUL_AUTO)
+    Y_ref = oracle.matmul(gtype, blocks, rows, cols, X, batch)
+    S = abs_dot_all(oracle, gtype, blocks, rows, cols, X)
+    bad, err, bound = tolerance_ok(Y.ravel(), Y_ref.ravel(), S.ravel(), REL_TOL)
+    assert bad.size == 0, (bad[:5], err[bad[:5]], bound[bad[:5]])
+    assert qmv.device_status(clear=True) == 0
+
+
 def test_matmul_automatic_choice_is_tensor_cores(cuda, qmv, workloads):
     """From 32 positions the automatic choice runs the tensor-core kernel: its
     output equals the forced kernel's bit for bit (the kernel is
