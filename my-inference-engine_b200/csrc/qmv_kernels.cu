@@ -1018,43 +1018,56 @@ matmul_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__
 //
 // Batched projection of many positions on the 5th-generation tensor cores
 // (src/quantized_matvec.cpp:164-224 computes the same Y[p] = W X[p]).
-// A CTA owns a tile of 128 rows x TN positions and walks K in stages of 64.
-// All 512 threads stage one step: weights are decoded from the resident
-// layout to the reference's fp32 values and split into two bf16 planes
-// w = wh + wl, the positions' x likewise x = xh + xl, and both are written to
-// shared memory in the canonical K-major no-swizzle layout (8-row x 16-byte
-// core matrices; 16-byte unit u of a plane sits at u * 16).  Thread 0 then
-// issues, per 16-wide K slice, wh*xh + wl*xh + wh*xl as tcgen05.mma
-// (kind::f16, bf16 inputs, fp32 accumulator of 128 lanes x TN columns in
-// tensor memory) and commits the stage's MMAs to the mbarrier that frees the
-// stage.  wl and xl carry the next 8 bits, so every product is exact to
-// about 2^-16 of |w x| -- far inside the parity bound 1e-4 * sum|w x|.  Raw
-// bytes of the next stage are loaded into registers before the current one
-// is converted.  The epilogue reads the accumulator with tcgen05.ld (warp w
-// reads lanes 32 (w % 4) .. + 31, a quarter of the columns) and writes
-// Y[p][row], one 128-byte run per warp store.
+// Operands are split into bf16 pairs, w = wh + wl and x = xh + xl, and each
+// 16-wide K slice issues wh*xh + wl*xh + wh*xl as tcgen05.mma (kind::f16,
+// bf16 inputs, fp32 accumulator in tensor memory).  wl and xl carry the next
+// 8 bits, so every product is exact to about 2^-16 of |w x|, far inside the
+// parity bound 1e-4 * sum|w x|.
 //
-// A tile that holds a non-finite weight scale, or an x whose bf16 rounding
-// is not finite, is recomputed on the CUDA cores in fp32 so that Inf and NaN
+//  * split_x_kernel (once per call) writes x of every position tile as
+//    stage images: for each 32-wide K step the xh and xl planes of TN
+//    positions in the canonical K-major no-swizzle layout (8-row x 16-byte
+//    core matrices; 16-byte unit u of a plane at byte u * 16), so a stage is
+//    one contiguous bulk copy.  A word per position tile flags any x outside
+//    the range the split handles.
+//  * matmul_tc_kernel: a CTA owns 128 rows x TN positions.  Thread 0 keeps
+//    the x planes of the next stages in flight with cp.async.bulk (no
+//    multicast), completing on one mbarrier per stage.  All 512 threads
+//    decode the stage's 128 x 32 weights from the resident layout to the
+//    reference's fp32 values (raw bytes prefetched into registers a stage
+//    ahead), split them and store the planes; thread 0 then waits for the
+//    stage's x, issues its 6 MMAs and commits them to the mbarrier that frees
+//    the stage.  The epilogue reads the accumulator with tcgen05.ld (warp w
+//    reads lanes 32 (w % 4) .. + 31) and writes Y[p][row], one 128-byte run
+//    per warp store.
+//
+// A tile that holds a non-finite weight scale, or an x outside the split's
+// range, is recomputed on the CUDA cores in fp32 so that Inf and NaN
 // propagate as in the reference's loop; the split planes could otherwise
 // turn Inf * 0 into NaN.
 
 constexpr int kTcM = 128;         // rows per tile = accumulator lanes
-constexpr int kTcK = 64;          // K per stage
+constexpr int kTcK = 32;          // K per stage
 constexpr int kTcThreads = 512;
 constexpr uint32_t kTcSmemBudget = 200u * 1024u;
+constexpr int kTcMaxStages = 6;
 constexpr unsigned int kStatusMmaTimeout = 16u;
 
-__host__ __device__ constexpr uint32_t tc_stage_bytes(int tn)
-{
-    return 2u * kTcM * kTcK * 2u + 2u * (uint32_t)tn * kTcK * 2u;
-}
+// One stage: wh | wl (128 x 32 bf16 each) | xh | xl (TN x 32 bf16 each).
+__host__ __device__ constexpr uint32_t tc_plane_w() { return (uint32_t)kTcM * kTcK * 2u; }
+__host__ __device__ constexpr uint32_t tc_plane_x(int tn) { return (uint32_t)tn * kTcK * 2u; }
+__host__ __device__ constexpr uint32_t tc_stage_bytes(int tn) { return 2u * tc_plane_w() + 2u * tc_plane_x(tn); }
 
-// Stages that fit the shared-memory budget (2 .. 4).
+// Stages that fit the shared-memory budget (at most kTcMaxStages).
 __host__ __device__ constexpr int tc_stages(int tn)
 {
-    return kTcSmemBudget / tc_stage_bytes(tn) > 4 ? 4 : (int)(kTcSmemBudget / tc_stage_bytes(tn));
+    return kTcSmemBudget / tc_stage_bytes(tn) > (uint32_t)kTcMaxStages ? kTcMaxStages
+                                                                      : (int)(kTcSmemBudget / tc_stage_bytes(tn));
 }
+
+// Split-x scratch: a flag word per position tile (padded to 256 bytes), then
+// the stage images, position tile-major.
+__host__ __device__ constexpr size_t tc_x_header(int n_pt) { return ((size_t)n_pt * 4u + 255u) & ~(size_t)255u; }
 
 __device__ __forceinline__ uint32_t ldg16(const uint8_t *p) { return __ldg((const unsigned short *)p); }
 
@@ -1234,12 +1247,12 @@ __device__ __forceinline__ bool x_in_range(const float4 &a, const float4 &b)
 }
 
 // Shared-memory matrix descriptor, K-major, no swizzle: core matrices along
-// K 128 bytes apart (leading byte offset), 8-row groups 1024 bytes apart
+// K 128 bytes apart (leading byte offset), 8-row groups kTcK * 16 bytes apart
 // (stride byte offset), descriptor version 1.
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr)
 {
-    return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)(128u >> 4) << 16) | ((uint64_t)(1024u >> 4) << 32) |
-           (1ull << 46);
+    return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)(128u >> 4) << 16) |
+           ((uint64_t)((kTcK * 16u) >> 4) << 32) | (1ull << 46);
 }
 
 // Instruction descriptor: fp32 accumulator, bf16 A and B, both K-major,
@@ -1301,32 +1314,69 @@ __device__ void tc_tile_fallback(const Layout &L, const uint8_t *__restrict__ w,
     }
 }
 
+// x of every position tile -> bf16 stage images (see above).
+template <int TN>
+__global__ void __launch_bounds__(kThreads)
+split_x_kernel(const float *__restrict__ X, int np, int cols, int nk, uint8_t *__restrict__ xs)
+{
+    constexpr uint32_t kPlaneX = tc_plane_x(TN);
+    constexpr int kUnits = TN * (kTcK / 8);
+    const int n_pt = (np + TN - 1) / TN;
+    uint32_t *flags = (uint32_t *)xs;
+    uint8_t *images = xs + tc_x_header(n_pt);
+    const long long total = (long long)n_pt * nk * kUnits;
+    for (long long id = blockIdx.x * (long long)blockDim.x + threadIdx.x; id < total;
+         id += (long long)gridDim.x * blockDim.x) {
+        const int u = (int)(id % kUnits);
+        const long long img = id / kUnits;  // pt * nk + kc
+        const int kc = (int)(img % nk), pt = (int)(img / nk);
+        const int pos = pt * TN + (u >> 5) * 8 + (u & 7);
+        const int k0 = kc * kTcK + ((u >> 3) & 3) * 8;
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (pos < np && k0 < cols) {
+            const float4 a = __ldg((const float4 *)(X + (size_t)pos * cols + k0));
+            const float4 b = __ldg((const float4 *)(X + (size_t)pos * cols + k0 + 4));
+            if (!x_in_range(a, b)) atomicOr(&flags[pt], 1u);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        }
+        uint8_t *dst = images + (size_t)img * 2u * kPlaneX;
+        split_store(v, dst, dst + kPlaneX, (uint32_t)u * 16u);
+    }
+}
+
 template <uint32_t FMT, int TN>
-__global__ void __launch_bounds__(kTcThreads, 1)
-matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ X, int np,
-                 float *__restrict__ Y)
+__global__ void __launch_bounds__(kTcThreads + 32, 1)
+matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ X,
+                 const uint8_t *__restrict__ xs, int np, float *__restrict__ Y)
 {
     static_assert(TN % 16 == 0 && TN >= 32 && TN <= 256, "N of one MMA: a multiple of 16 in 32..256");
-    constexpr int kStages = tc_stages(TN);
-    constexpr int kWUnits = kTcM * (kTcK / 8) / kTcThreads;                 // 2
-    constexpr int kXUnits = (TN * (kTcK / 8) + kTcThreads - 1) / kTcThreads;  // 1 .. 4
-    constexpr uint32_t kPlaneW = kTcM * kTcK * 2, kPlaneX = TN * kTcK * 2;
+    static_assert(kTcM * (kTcK / 8) == kTcThreads, "one weight unit per decode thread and stage");
+    constexpr int S = tc_stages(TN);
+    constexpr int kDecodeWarps = kTcThreads / 32;  // warps 0..15; warp 16 issues copies and MMAs
+    constexpr uint32_t kPlaneW = tc_plane_w(), kPlaneX = tc_plane_x(TN);
     constexpr uint32_t kStage = tc_stage_bytes(TN);
     constexpr uint32_t kIdesc = umma_idesc(TN);
     constexpr uint32_t kTmemCols = TN <= 32 ? 32u : TN <= 64 ? 64u : TN <= 128 ? 128u : 256u;
 
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) unsigned long long bars[kStages];
+    // [0, S) weights stored, [S, 2S) x landed, [2S, 3S) MMAs done
+    __shared__ __align__(8) unsigned long long bars[3 * S];
     __shared__ uint32_t tmem_slot;
 
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int r0 = blockIdx.x * kTcM, p0 = blockIdx.y * TN;
+    const int r0 = blockIdx.x * kTcM, pt = blockIdx.y, p0 = pt * TN;
     const int nk = (L.cols + kTcK - 1) / kTcK;
     const uint32_t smem0 = (uint32_t)__cvta_generic_to_shared(smem);
-    const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]);
+    const uint32_t wbar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]);
+    const uint32_t xbar0 = wbar0 + 8u * S, ebar0 = wbar0 + 16u * S;
 
     if (tid == 0) {
-        for (int i = 0; i < kStages; ++i) mbar_init(bar0 + 8u * i, 1u);
+        for (int i = 0; i < S; ++i) {
+            mbar_init(wbar0 + 8u * i, (uint32_t)kDecodeWarps);
+            mbar_init(xbar0 + 8u * i, 1u);
+            mbar_init(ebar0 + 8u * i, 1u);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -1340,128 +1390,115 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
 
-    // This thread's staging units: unit u of a plane holds 8 K values of
-    // tile row (u >> 6) * 8 + (u & 7), K offset ((u >> 3) & 7) * 8 in the
-    // stage, at byte u * 16 (core matrix (row / 8, K / 8) at 1024 (row / 8)
-    // + 128 (K / 8)).
-    const uint8_t *wrow[kWUnits];
-    int wk[kWUnits];
-    const float *xrow[kXUnits];
-    int xk[kXUnits];
+    bool finite = true, ok = true;
+    int consumed = 0, issued = 0;  // x stages seen landed / copies issued (MMA thread)
+    if (warp == kDecodeWarps) {
+        // ------------------------------------------------ copies and MMAs
+        if ((tid & 31) == 0) {
+            const uint8_t *ximg = xs + tc_x_header((int)gridDim.y) + (size_t)pt * nk * 2u * kPlaneX;
+            auto issue_x = [&](int j) {
+                const uint32_t bar = xbar0 + 8u * (uint32_t)(j % S);
+                mbar_expect_tx(bar, 2u * kPlaneX);
+                bulk_g2s(smem0 + (uint32_t)(j % S) * kStage + 2u * kPlaneW, ximg + (size_t)j * 2u * kPlaneX,
+                         2u * kPlaneX, bar);
+                issued = j + 1;
+            };
+            for (int j = 0; j < S && j < nk; ++j) issue_x(j);
+            for (int kc = 0; kc < nk && ok; ++kc) {
+                const int s = kc % S;
+                const uint32_t par = (uint32_t)((kc / S) & 1);
+                if (!mbar_wait(wbar0 + 8u * s, par) || !mbar_wait(xbar0 + 8u * s, par)) {
+                    ok = false;
+                    break;
+                }
+                consumed = kc + 1;
+                tc_fence_after();
+                const uint32_t a_h = smem0 + (uint32_t)s * kStage, a_l = a_h + kPlaneW;
+                const uint32_t b_h = a_h + 2 * kPlaneW, b_l = b_h + kPlaneX;
 #pragma unroll
-    for (int i = 0; i < kWUnits; ++i) {
-        const int u = tid + i * kTcThreads;
-        const int row = r0 + (u >> 6) * 8 + (u & 7);
-        wrow[i] = row < L.rows ? w + (uint64_t)row * L.row_stride : nullptr;
-        wk[i] = ((u >> 3) & 7) * 8;
-    }
-#pragma unroll
-    for (int i = 0; i < kXUnits; ++i) {
-        const int u = tid + i * kTcThreads;
-        const int pos = p0 + (u >> 6) * 8 + (u & 7);
-        xrow[i] = (u < TN * (kTcK / 8) && pos < np) ? X + (size_t)pos * L.cols : nullptr;
-        xk[i] = ((u >> 3) & 7) * 8;
-    }
-
-    Raw8<FMT> wr[kWUnits];
-    float4 xr[kXUnits][2];
-    auto load_stage = [&](int kc, Raw8<FMT> *w_out, float4 (*x_out)[2]) {
-#pragma unroll
-        for (int i = 0; i < kWUnits; ++i) {
-            const int k0 = kc * kTcK + wk[i];
-            if (wrow[i] != nullptr && k0 < L.cols) w_out[i].load(wrow[i], L, k0);
-        }
-#pragma unroll
-        for (int i = 0; i < kXUnits; ++i) {
-            const int k0 = kc * kTcK + xk[i];
-            if (xrow[i] != nullptr && k0 < L.cols) {
-                x_out[i][0] = __ldg((const float4 *)(xrow[i] + k0));
-                x_out[i][1] = __ldg((const float4 *)(xrow[i] + k0 + 4));
-            } else {
-                x_out[i][0] = x_out[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int j = 0; j < kTcK / 16; ++j) {
+                    const uint32_t o = 256u * j;  // two core matrices along K per slice
+                    umma_bf16(tmem, umma_desc(a_h + o), umma_desc(b_h + o), kIdesc, (kc | j) != 0);
+                    umma_bf16(tmem, umma_desc(a_l + o), umma_desc(b_h + o), kIdesc, 1u);
+                    umma_bf16(tmem, umma_desc(a_h + o), umma_desc(b_l + o), kIdesc, 1u);
+                }
+                umma_commit(ebar0 + 8u * s);
+                // refill the buffer of stage kc - 1 with stage kc - 1 + S once
+                // its MMAs are done (stage kc's are queued behind them)
+                const int j = kc - 1 + S;
+                if (kc >= 1 && j < nk) {
+                    if (mbar_wait(ebar0 + 8u * ((kc - 1) % S), (uint32_t)(((kc - 1) / S) & 1)))
+                        issue_x(j);
+                    else
+                        ok = false;
+                }
             }
         }
-    };
-    load_stage(0, wr, xr);
-
-    bool finite = true, ok = true;
-    for (int kc = 0; kc < nk; ++kc) {
-        const int s = kc % kStages;
-        Raw8<FMT> wn[kWUnits];
-        float4 xn[kXUnits][2];
-        if (kc + 1 < nk) load_stage(kc + 1, wn, xn);
-        // the MMAs that last read stage s (iteration kc - kStages) are done
-        if (kc >= kStages && !mbar_wait(bar0 + 8u * s, (uint32_t)((kc / kStages - 1) & 1))) ok = false;
-        if (__syncthreads_or(!ok)) {
-            ok = false;
-            break;
-        }
-        uint8_t *st = smem + (size_t)s * kStage;
-#pragma unroll
-        for (int i = 0; i < kWUnits; ++i) {
-            const int u = tid + i * kTcThreads;
-            const int k0 = kc * kTcK + wk[i];
+    } else {
+        // ------------------------------------------------ weight decode
+        // This thread's unit: 8 K values of tile row (tid >> 5) * 8 +
+        // (tid & 7), K offset ((tid >> 3) & 3) * 8, at byte tid * 16 of a plane.
+        const int wrow_i = r0 + (tid >> 5) * 8 + (tid & 7);
+        const uint8_t *wrow = wrow_i < L.rows ? w + (uint64_t)wrow_i * L.row_stride : nullptr;
+        const int wk = ((tid >> 3) & 3) * 8;
+        Raw8<FMT> wr;
+        if (wrow != nullptr && wk < L.cols) wr.load(wrow, L, wk);
+        for (int kc = 0; kc < nk; ++kc) {
+            const int s = kc % S;
+            Raw8<FMT> wn;
+            const int kn = (kc + 1) * kTcK + wk;
+            if (wrow != nullptr && kn < L.cols) wn.load(wrow, L, kn);
+            // the MMAs that last read buffer s (stage kc - S) are done
+            if (kc >= S && !mbar_wait(ebar0 + 8u * s, (uint32_t)((kc / S - 1) & 1))) {
+                ok = false;
+                break;
+            }
+            uint8_t *st = smem + (size_t)s * kStage;
+            const int k0 = kc * kTcK + wk;
             float v[8];
-            if (wrow[i] != nullptr && k0 < L.cols) {
-                finite &= wr[i].decode(k0, v);
+            if (wrow != nullptr && k0 < L.cols) {
+                finite &= wr.decode(k0, v);
             } else {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) v[e] = 0.f;
             }
-            split_store(v, st, st + kPlaneW, (uint32_t)u * 16u);
-        }
-#pragma unroll
-        for (int i = 0; i < kXUnits; ++i) {
-            const int u = tid + i * kTcThreads;
-            if (u < TN * (kTcK / 8)) {
-                finite &= x_in_range(xr[i][0], xr[i][1]);
-                const float v[8] = {xr[i][0].x, xr[i][0].y, xr[i][0].z, xr[i][0].w,
-                                    xr[i][1].x, xr[i][1].y, xr[i][1].z, xr[i][1].w};
-                split_store(v, st + 2 * kPlaneW, st + 2 * kPlaneW + kPlaneX, (uint32_t)u * 16u);
-            }
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t a_h = smem0 + (uint32_t)s * kStage, a_l = a_h + kPlaneW;
-            const uint32_t b_h = a_h + 2 * kPlaneW, b_l = b_h + kPlaneX;
-#pragma unroll
-            for (int j = 0; j < kTcK / 16; ++j) {
-                const uint32_t o = 256u * j;  // two core matrices along K per slice
-                umma_bf16(tmem, umma_desc(a_h + o), umma_desc(b_h + o), kIdesc, (kc | j) != 0);
-                umma_bf16(tmem, umma_desc(a_l + o), umma_desc(b_h + o), kIdesc, 1u);
-                umma_bf16(tmem, umma_desc(a_h + o), umma_desc(b_l + o), kIdesc, 1u);
-            }
-            umma_commit(bar0 + 8u * s);
-        }
-#pragma unroll
-        for (int i = 0; i < kWUnits; ++i) wr[i] = wn[i];
-#pragma unroll
-        for (int i = 0; i < kXUnits; ++i) {
-            xr[i][0] = xn[i][0];
-            xr[i][1] = xn[i][1];
+            split_store(v, st, st + kPlaneW, (uint32_t)tid * 16u);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if ((tid & 31) == 0) mbar_arrive(wbar0 + 8u * s);
+            wr = wn;
         }
     }
 
     // every MMA has completed once the last stage's commit has arrived
-    if (ok) {
+    if (ok && (warp < kDecodeWarps || (tid & 31) == 0)) {
         const int last = nk - 1;
-        if (!mbar_wait(bar0 + 8u * (last % kStages), (uint32_t)((last / kStages) & 1))) ok = false;
+        if (!mbar_wait(ebar0 + 8u * (last % S), (uint32_t)((last / S) & 1))) ok = false;
     }
     const bool failed = __syncthreads_or(!ok);
-    const bool fallback = __syncthreads_or(!finite);
+    if (failed && warp == kDecodeWarps && (tid & 31) == 0) {
+        atomicOr(&g_status, kStatusMmaTimeout);
+        // x copies still in flight must land before the CTA exits
+        for (int j = consumed; j < issued; ++j) {
+            if (!mbar_wait(xbar0 + 8u * (j % S), (uint32_t)((j / S) & 1))) {
+                atomicOr(&g_status, kStatusDrainTimeout);
+                break;
+            }
+        }
+    }
+    const uint32_t x_flag = ((const uint32_t *)xs)[pt];
+    const bool fallback = __syncthreads_or(!finite || x_flag != 0u);
     tc_fence_after();
     if (failed) {
-        if (tid == 0) atomicOr(&g_status, kStatusMmaTimeout);
+        // nothing is written
     } else if (fallback) {
         tc_tile_fallback<FMT>(L, w, X, np, Y, r0, p0, TN);
-    } else {
+    } else if (warp < kDecodeWarps) {
         // warp w reads lanes 32 (w % 4) .. + 31; the four warps sharing a lane
         // quarter take 8-column chunks round-robin
         const int q = warp & 3;
         const int row = r0 + 32 * q + (tid & 31);
-        for (int c = 8 * (warp >> 2); c < TN; c += 8 * (kTcThreads / 128)) {
+        for (int c = 8 * (warp >> 2); c < TN; c += 8 * (kDecodeWarps / 4)) {
             float v[8];
             tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
@@ -1920,6 +1957,38 @@ int g_matmul_path = 0;
 // Batches of at least this many positions take the tensor-core kernel.
 constexpr int kTcMinBatch = 32;
 
+// Stream-ordered pool for the split-x scratch of the tensor-core matmul, one
+// per device, created on first use.  It keeps freed memory (release
+// threshold: unlimited), so steady-state calls allocate without the driver.
+cudaError_t tc_scratch_pool(cudaMemPool_t *out)
+{
+    static std::mutex mu;
+    static cudaMemPool_t pools[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (pools[dev] == nullptr) {
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t p = nullptr;
+        e = cudaMemPoolCreate(&p, &props);
+        if (e != cudaSuccess) return e;
+        uint64_t keep = ~0ull;
+        e = cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep);
+        if (e != cudaSuccess) {
+            cudaMemPoolDestroy(p);
+            return e;
+        }
+        pools[dev] = p;
+    }
+    *out = pools[dev];
+    return cudaSuccess;
+}
+
 template <uint32_t FMT, int TN>
 cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
                          cudaStream_t s)
@@ -1929,16 +1998,36 @@ cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const float *X, int 
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = allow_max_smem((const void *)kernel, dev);
     if (e != cudaSuccess) return e;
-    const dim3 grid((unsigned)((L.rows + kTcM - 1) / kTcM), (unsigned)((batch + TN - 1) / TN));
+    const int n_pt = (batch + TN - 1) / TN, nk = (L.cols + kTcK - 1) / kTcK;
+    const dim3 grid((unsigned)((L.rows + kTcM - 1) / kTcM), (unsigned)n_pt);
     if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
-    kernel<<<grid, kTcThreads, (size_t)tc_stages(TN) * tc_stage_bytes(TN), s>>>(L, w, X, batch, Y);
-    return cudaGetLastError();
+    const size_t header = tc_x_header(n_pt);
+    const size_t bytes = header + (size_t)n_pt * nk * 2u * tc_plane_x(TN);
+    cudaMemPool_t pool;
+    e = tc_scratch_pool(&pool);
+    if (e != cudaSuccess) return e;
+    void *xs = nullptr;
+    e = cudaMallocFromPoolAsync(&xs, bytes, pool, s);
+    if (e != cudaSuccess) return e;
+    e = cudaMemsetAsync(xs, 0, header, s);
+    if (e == cudaSuccess) {
+        const unsigned g = grid_for((uint64_t)n_pt * nk * TN * (kTcK / 8), kThreads);
+        split_x_kernel<TN><<<g, kThreads, 0, s>>>(X, batch, L.cols, nk, (uint8_t *)xs);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) {
+        kernel<<<grid, kTcThreads + 32, (size_t)tc_stages(TN) * tc_stage_bytes(TN), s>>>(
+            L, w, X, (const uint8_t *)xs, batch, Y);
+        e = cudaGetLastError();
+    }
+    const cudaError_t f = cudaFreeAsync(xs, s);
+    return e != cudaSuccess ? e : f;
 }
 
 // Position-tile width of the tensor-core kernel: the candidate with the
 // smallest (waves of one-CTA-per-SM tiles) x (per-stage cost), where a
-// stage costs max(decode of 128 x 64 weights + split of TN x 64 x values,
-// 3 x 4 MMAs of 128 x TN x 16), in SM cycles measured on B200.
+// 32-wide K stage costs max(decode of 128 x 32 weights, 6 MMAs of
+// 128 x TN x 16), in SM cycles.
 int tc_tile_width(int rows, int batch)
 {
     static const int cand[] = {64, 128, 176, 256};
@@ -1948,7 +2037,7 @@ int tc_tile_width(int rows, int batch)
     for (int tn : cand) {
         const long long tiles = row_tiles * ((batch + tn - 1) / tn);
         const long long waves = (tiles + sm_count() - 1) / sm_count();
-        const double alu = 700.0 + 4.0 * tn, mma = 8.4 * tn;
+        const double alu = 450.0, mma = 4.2 * tn;
         const double cost = (double)waves * (alu > mma ? alu : mma);
         if (cost < best_cost) {
             best_cost = cost;
