@@ -1048,15 +1048,16 @@ matmul_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__
 
 constexpr int kTcM = 128;         // rows per tile = accumulator lanes
 constexpr int kTcK = 32;          // K per stage
-constexpr int kTcThreads = 512;
+constexpr int kTcThreads = 512;   // weight-decode threads (16 warps)
 constexpr uint32_t kTcSmemBudget = 200u * 1024u;
-constexpr int kTcMaxStages = 6;
+constexpr int kTcMaxStages = 8;   // A ring: 8 stages x 32 columns after the 256 accumulator columns
+constexpr uint32_t kTcACol = 256u;
 constexpr unsigned int kStatusMmaTimeout = 16u;
 
-// One stage: wh | wl (128 x 32 bf16 each) | xh | xl (TN x 32 bf16 each).
-__host__ __device__ constexpr uint32_t tc_plane_w() { return (uint32_t)kTcM * kTcK * 2u; }
+// Shared memory of one stage: xh | xl (TN x 32 bf16 each).  The weights of a
+// stage (wh | wl, 16 columns each) live in tensor memory.
 __host__ __device__ constexpr uint32_t tc_plane_x(int tn) { return (uint32_t)tn * kTcK * 2u; }
-__host__ __device__ constexpr uint32_t tc_stage_bytes(int tn) { return 2u * tc_plane_w() + 2u * tc_plane_x(tn); }
+__host__ __device__ constexpr uint32_t tc_stage_bytes(int tn) { return 2u * tc_plane_x(tn); }
 
 // Stages that fit the shared-memory budget (at most kTcMaxStages).
 __host__ __device__ constexpr int tc_stages(int tn)
@@ -1065,10 +1066,7 @@ __host__ __device__ constexpr int tc_stages(int tn)
                                                                       : (int)(kTcSmemBudget / tc_stage_bytes(tn));
 }
 
-// Split-x scratch: a flag word per position tile (padded to 256 bytes), then
-// the stage images, position tile-major.
-__host__ __device__ constexpr size_t tc_x_header(int n_pt) { return ((size_t)n_pt * 4u + 255u) & ~(size_t)255u; }
-
+// Split-x scratch: the stage images, position tile-major.
 __device__ __forceinline__ uint32_t ldg16(const uint8_t *p) { return __ldg((const unsigned short *)p); }
 
 // 2^23 + (byte I of w), exactly: the byte becomes the low mantissa bits of a
@@ -1213,13 +1211,13 @@ __device__ __forceinline__ float round8(float x)
     return __fsub_rn(t, __fsub_rn(t, x));
 }
 
-// Split 8 floats into bf16 high and low planes, v = hi + lo + e with
-// |hi - v| <= 2^-8 |v| and |e| <= 2^-16 |v|, and store both 16-byte units
-// (element 0 at the lowest address).  FMA-pipe arithmetic and byte permutes
-// only.  |v| must stay below 2^111 (65537 v finite).
-__device__ __forceinline__ void split_store(const float v[8], uint8_t *hi_plane, uint8_t *lo_plane, uint32_t off)
+// Split 8 floats into bf16 high and low parts, v = hi + lo + e with
+// |hi - v| <= 2^-8 |v| and |e| <= 2^-16 |v|, as packed words (hi[j], lo[j]
+// hold elements 2j and 2j + 1, the even one in the low half).  FMA-pipe
+// arithmetic and byte permutes only.  |v| must stay below 2^111 (65537 v
+// finite).
+__device__ __forceinline__ void split_words(const float v[8], uint32_t h[4], uint32_t l[4])
 {
-    uint32_t h[4], l[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const float h0 = round8(v[2 * j]), h1 = round8(v[2 * j + 1]);
@@ -1227,23 +1225,15 @@ __device__ __forceinline__ void split_store(const float v[8], uint8_t *hi_plane,
         h[j] = __byte_perm(__float_as_uint(h0), __float_as_uint(h1), 0x7632u);
         l[j] = __byte_perm(__float_as_uint(l0), __float_as_uint(l1), 0x7632u);
     }
-    *(uint4 *)(hi_plane + off) = make_uint4(h[0], h[1], h[2], h[3]);
-    *(uint4 *)(lo_plane + off) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-// true when every |x| < 2^111, the range split_store handles (NaN and Inf
-// fail)
-__device__ __forceinline__ bool x_in_range(const float4 &a, const float4 &b)
+// The split stored as two 16-byte units (element 0 at the lowest address).
+__device__ __forceinline__ void split_store(const float v[8], uint8_t *hi_plane, uint8_t *lo_plane, uint32_t off)
 {
-    uint32_t m = __float_as_uint(a.x) & 0x7fffffffu;
-    m = max(m, __float_as_uint(a.y) & 0x7fffffffu);
-    m = max(m, __float_as_uint(a.z) & 0x7fffffffu);
-    m = max(m, __float_as_uint(a.w) & 0x7fffffffu);
-    m = max(m, __float_as_uint(b.x) & 0x7fffffffu);
-    m = max(m, __float_as_uint(b.y) & 0x7fffffffu);
-    m = max(m, __float_as_uint(b.z) & 0x7fffffffu);
-    m = max(m, __float_as_uint(b.w) & 0x7fffffffu);
-    return m < 0x77000000u;
+    uint32_t h[4], l[4];
+    split_words(v, h, l);
+    *(uint4 *)(hi_plane + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    *(uint4 *)(lo_plane + off) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
 // Shared-memory matrix descriptor, K-major, no swizzle: core matrices along
@@ -1269,6 +1259,25 @@ __device__ __forceinline__ void umma_bf16(uint32_t tmem, uint64_t a, uint64_t b,
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// Same, with A (128 x 16 bf16: lane = row, two K values per 32-bit column,
+// the even one in the low half) read from tensor memory.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// 4 consecutive 32-bit columns of this thread's lane.
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d)
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(a), "r"(b),
+                 "r"(c), "r"(d)
+                 : "memory");
 }
 
 __device__ __forceinline__ void umma_commit(uint32_t bar)
@@ -1314,7 +1323,9 @@ __device__ void tc_tile_fallback(const Layout &L, const uint8_t *__restrict__ w,
     }
 }
 
-// x of every position tile -> bf16 stage images (see above).
+// x of every position tile -> bf16 stage images (see above).  An x the split
+// cannot represent (non-finite, or |x| >= 2^111) becomes NaN in the planes,
+// so the tile's accumulator turns non-finite and the tile is recomputed.
 template <int TN>
 __global__ void __launch_bounds__(kThreads)
 split_x_kernel(const float *__restrict__ X, int np, int cols, int nk, uint8_t *__restrict__ xs)
@@ -1322,8 +1333,6 @@ split_x_kernel(const float *__restrict__ X, int np, int cols, int nk, uint8_t *_
     constexpr uint32_t kPlaneX = tc_plane_x(TN);
     constexpr int kUnits = TN * (kTcK / 8);
     const int n_pt = (np + TN - 1) / TN;
-    uint32_t *flags = (uint32_t *)xs;
-    uint8_t *images = xs + tc_x_header(n_pt);
     const long long total = (long long)n_pt * nk * kUnits;
     for (long long id = blockIdx.x * (long long)blockDim.x + threadIdx.x; id < total;
          id += (long long)gridDim.x * blockDim.x) {
@@ -1336,35 +1345,35 @@ split_x_kernel(const float *__restrict__ X, int np, int cols, int nk, uint8_t *_
         if (pos < np && k0 < cols) {
             const float4 a = __ldg((const float4 *)(X + (size_t)pos * cols + k0));
             const float4 b = __ldg((const float4 *)(X + (size_t)pos * cols + k0 + 4));
-            if (!x_in_range(a, b)) atomicOr(&flags[pt], 1u);
             v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
             v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
         }
-        uint8_t *dst = images + (size_t)img * 2u * kPlaneX;
+        uint8_t *dst = xs + (size_t)img * 2u * kPlaneX;
         split_store(v, dst, dst + kPlaneX, (uint32_t)u * 16u);
     }
 }
 
 template <uint32_t FMT, int TN>
-__global__ void __launch_bounds__(kTcThreads + 32, 1)
+__global__ void __launch_bounds__(kTcThreads + 64, 1)
 matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ X,
                  const uint8_t *__restrict__ xs, int np, float *__restrict__ Y)
 {
     static_assert(TN % 16 == 0 && TN >= 32 && TN <= 256, "N of one MMA: a multiple of 16 in 32..256");
     static_assert(kTcM * (kTcK / 8) == kTcThreads, "one weight unit per decode thread and stage");
     constexpr int S = tc_stages(TN);
-    constexpr int kDecodeWarps = kTcThreads / 32;  // warps 0..15; warp 16 issues copies and MMAs
-    constexpr uint32_t kPlaneW = tc_plane_w(), kPlaneX = tc_plane_x(TN);
+    static_assert(kTcACol + 32u * S <= 512u, "A ring must fit tensor memory");
+    // warps 0..15 decode weights, warp 16 issues MMAs, warp 17 copies x
+    constexpr int kDecodeWarps = kTcThreads / 32, kMmaWarp = kDecodeWarps, kCopyWarp = kDecodeWarps + 1;
+    constexpr uint32_t kPlaneX = tc_plane_x(TN);
     constexpr uint32_t kStage = tc_stage_bytes(TN);
     constexpr uint32_t kIdesc = umma_idesc(TN);
-    constexpr uint32_t kTmemCols = TN <= 32 ? 32u : TN <= 64 ? 64u : TN <= 128 ? 128u : 256u;
 
     extern __shared__ __align__(128) uint8_t smem[];
     // [0, S) weights stored, [S, 2S) x landed, [2S, 3S) MMAs done
     __shared__ __align__(8) unsigned long long bars[3 * S];
     __shared__ uint32_t tmem_slot;
 
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int r0 = blockIdx.x * kTcM, pt = blockIdx.y, p0 = pt * TN;
     const int nk = (L.cols + kTcK - 1) / kTcK;
     const uint32_t smem0 = (uint32_t)__cvta_generic_to_shared(smem);
@@ -1380,9 +1389,10 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
+        // all 512 columns: accumulator in [0, TN), weight stages from kTcACol
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          (uint32_t)__cvta_generic_to_shared(&tmem_slot)),
-                     "r"(kTmemCols));
+                     "r"(512u));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
@@ -1390,57 +1400,56 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
 
-    bool finite = true, ok = true;
-    int consumed = 0, issued = 0;  // x stages seen landed / copies issued (MMA thread)
-    if (warp == kDecodeWarps) {
-        // ------------------------------------------------ copies and MMAs
-        if ((tid & 31) == 0) {
-            const uint8_t *ximg = xs + tc_x_header((int)gridDim.y) + (size_t)pt * nk * 2u * kPlaneX;
-            auto issue_x = [&](int j) {
-                const uint32_t bar = xbar0 + 8u * (uint32_t)(j % S);
-                mbar_expect_tx(bar, 2u * kPlaneX);
-                bulk_g2s(smem0 + (uint32_t)(j % S) * kStage + 2u * kPlaneW, ximg + (size_t)j * 2u * kPlaneX,
-                         2u * kPlaneX, bar);
+    bool ok = true;
+    int issued = 0;  // x copies issued (copy thread)
+    if (warp == kCopyWarp) {
+        // ------------------------------------------------ x stage copies
+        if (lane == 0) {
+            const uint8_t *ximg = xs + (size_t)pt * nk * (size_t)kStage;
+            for (int j = 0; j < nk; ++j) {
+                const int s = j % S;
+                // buffer s is free once the MMAs of stage j - S are done
+                if (j >= S && !mbar_wait(ebar0 + 8u * s, (uint32_t)((j / S - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                mbar_expect_tx(xbar0 + 8u * s, kStage);
+                bulk_g2s(smem0 + (uint32_t)s * kStage, ximg + (size_t)j * kStage, kStage, xbar0 + 8u * s);
                 issued = j + 1;
-            };
-            for (int j = 0; j < S && j < nk; ++j) issue_x(j);
-            for (int kc = 0; kc < nk && ok; ++kc) {
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        // ------------------------------------------------ MMA issue
+        if (lane == 0) {
+            for (int kc = 0; kc < nk; ++kc) {
                 const int s = kc % S;
                 const uint32_t par = (uint32_t)((kc / S) & 1);
                 if (!mbar_wait(wbar0 + 8u * s, par) || !mbar_wait(xbar0 + 8u * s, par)) {
                     ok = false;
                     break;
                 }
-                consumed = kc + 1;
                 tc_fence_after();
-                const uint32_t a_h = smem0 + (uint32_t)s * kStage, a_l = a_h + kPlaneW;
-                const uint32_t b_h = a_h + 2 * kPlaneW, b_l = b_h + kPlaneX;
+                const uint32_t a_h = tmem + kTcACol + 32u * s, a_l = a_h + 16u;
+                const uint32_t b_h = smem0 + (uint32_t)s * kStage, b_l = b_h + kPlaneX;
 #pragma unroll
                 for (int j = 0; j < kTcK / 16; ++j) {
-                    const uint32_t o = 256u * j;  // two core matrices along K per slice
-                    umma_bf16(tmem, umma_desc(a_h + o), umma_desc(b_h + o), kIdesc, (kc | j) != 0);
-                    umma_bf16(tmem, umma_desc(a_l + o), umma_desc(b_h + o), kIdesc, 1u);
-                    umma_bf16(tmem, umma_desc(a_h + o), umma_desc(b_l + o), kIdesc, 1u);
+                    // K slice j: 8 columns of A, two core matrices along K of B
+                    umma_bf16_ts(tmem, a_h + 8u * j, umma_desc(b_h + 256u * j), kIdesc, (kc | j) != 0);
+                    umma_bf16_ts(tmem, a_l + 8u * j, umma_desc(b_h + 256u * j), kIdesc, 1u);
+                    umma_bf16_ts(tmem, a_h + 8u * j, umma_desc(b_l + 256u * j), kIdesc, 1u);
                 }
                 umma_commit(ebar0 + 8u * s);
-                // refill the buffer of stage kc - 1 with stage kc - 1 + S once
-                // its MMAs are done (stage kc's are queued behind them)
-                const int j = kc - 1 + S;
-                if (kc >= 1 && j < nk) {
-                    if (mbar_wait(ebar0 + 8u * ((kc - 1) % S), (uint32_t)(((kc - 1) / S) & 1)))
-                        issue_x(j);
-                    else
-                        ok = false;
-                }
             }
         }
     } else {
         // ------------------------------------------------ weight decode
-        // This thread's unit: 8 K values of tile row (tid >> 5) * 8 +
-        // (tid & 7), K offset ((tid >> 3) & 3) * 8, at byte tid * 16 of a plane.
-        const int wrow_i = r0 + (tid >> 5) * 8 + (tid & 7);
+        // Warp w owns tensor-memory lanes 32 (w % 4) .. + 31 (tile rows) and
+        // K group w / 4 of every stage: 8 K values = 4 columns per plane.
+        const int q = warp & 3, kg = warp >> 2;
+        const int wrow_i = r0 + 32 * q + lane;
         const uint8_t *wrow = wrow_i < L.rows ? w + (uint64_t)wrow_i * L.row_stride : nullptr;
-        const int wk = ((tid >> 3) & 3) * 8;
+        const int wk = kg * 8;
+        const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16) + kTcACol + 4u * kg;
         Raw8<FMT> wr;
         if (wrow != nullptr && wk < L.cols) wr.load(wrow, L, wk);
         for (int kc = 0; kc < nk; ++kc) {
@@ -1448,56 +1457,56 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
             Raw8<FMT> wn;
             const int kn = (kc + 1) * kTcK + wk;
             if (wrow != nullptr && kn < L.cols) wn.load(wrow, L, kn);
-            // the MMAs that last read buffer s (stage kc - S) are done
-            if (kc >= S && !mbar_wait(ebar0 + 8u * s, (uint32_t)((kc / S - 1) & 1))) {
-                ok = false;
-                break;
-            }
-            uint8_t *st = smem + (size_t)s * kStage;
             const int k0 = kc * kTcK + wk;
             float v[8];
             if (wrow != nullptr && k0 < L.cols) {
-                finite &= wr.decode(k0, v);
+                wr.decode(k0, v);
             } else {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) v[e] = 0.f;
             }
-            split_store(v, st, st + kPlaneW, (uint32_t)tid * 16u);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            uint32_t h[4], l[4];
+            split_words(v, h, l);
+            // the MMAs that last read stage buffer s (stage kc - S) are done
+            if (kc >= S && !mbar_wait(ebar0 + 8u * s, (uint32_t)((kc / S - 1) & 1))) ok = false;
+            if (!__all_sync(kFull, ok)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            tmem_st4(lane_addr + 32u * s, h[0], h[1], h[2], h[3]);
+            tmem_st4(lane_addr + 32u * s + 16u, l[0], l[1], l[2], l[3]);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
             __syncwarp();
-            if ((tid & 31) == 0) mbar_arrive(wbar0 + 8u * s);
+            if (lane == 0) mbar_arrive(wbar0 + 8u * s);
             wr = wn;
         }
     }
 
     // every MMA has completed once the last stage's commit has arrived
-    if (ok && (warp < kDecodeWarps || (tid & 31) == 0)) {
+    if (ok && (warp < kDecodeWarps || lane == 0)) {
         const int last = nk - 1;
         if (!mbar_wait(ebar0 + 8u * (last % S), (uint32_t)((last / S) & 1))) ok = false;
     }
     const bool failed = __syncthreads_or(!ok);
-    if (failed && warp == kDecodeWarps && (tid & 31) == 0) {
+    if (failed && warp == kCopyWarp && lane == 0) {
         atomicOr(&g_status, kStatusMmaTimeout);
         // x copies still in flight must land before the CTA exits
-        for (int j = consumed; j < issued; ++j) {
+        for (int j = issued - S > 0 ? issued - S : 0; j < issued; ++j) {
             if (!mbar_wait(xbar0 + 8u * (j % S), (uint32_t)((j / S) & 1))) {
                 atomicOr(&g_status, kStatusDrainTimeout);
                 break;
             }
         }
     }
-    const uint32_t x_flag = ((const uint32_t *)xs)[pt];
-    const bool fallback = __syncthreads_or(!finite || x_flag != 0u);
     tc_fence_after();
-    if (failed) {
-        // nothing is written
-    } else if (fallback) {
-        tc_tile_fallback<FMT>(L, w, X, np, Y, r0, p0, TN);
-    } else if (warp < kDecodeWarps) {
+    bool nonfinite = false;
+    if (!failed && warp < kDecodeWarps) {
         // warp w reads lanes 32 (w % 4) .. + 31; the four warps sharing a lane
         // quarter take 8-column chunks round-robin
         const int q = warp & 3;
-        const int row = r0 + 32 * q + (tid & 31);
+        const int row = r0 + 32 * q + lane;
         for (int c = 8 * (warp >> 2); c < TN; c += 8 * (kDecodeWarps / 4)) {
             float v[8];
             tmem_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
@@ -1506,16 +1515,22 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int pos = p0 + c + i;
-                    if (pos < np) Y[(size_t)pos * L.rows + row] = v[i];
+                    if (pos < np) {
+                        Y[(size_t)pos * L.rows + row] = v[i];
+                        nonfinite |= !isfinite(v[i]);
+                    }
                 }
             }
         }
     }
+    // A non-finite weight or x makes the split planes NaN: recompute the
+    // tile in fp32 (this overwrites every output the epilogue wrote).
+    if (__syncthreads_or(nonfinite) && !failed) tc_tile_fallback<FMT>(L, w, X, np, Y, r0, p0, TN);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u));
     }
 }
 
@@ -2001,23 +2016,24 @@ cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const float *X, int 
     const int n_pt = (batch + TN - 1) / TN, nk = (L.cols + kTcK - 1) / kTcK;
     const dim3 grid((unsigned)((L.rows + kTcM - 1) / kTcM), (unsigned)n_pt);
     if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
-    const size_t header = tc_x_header(n_pt);
-    const size_t bytes = header + (size_t)n_pt * nk * 2u * tc_plane_x(TN);
+    const size_t bytes = (size_t)n_pt * nk * tc_stage_bytes(TN);
     cudaMemPool_t pool;
     e = tc_scratch_pool(&pool);
     if (e != cudaSuccess) return e;
     void *xs = nullptr;
     e = cudaMallocFromPoolAsync(&xs, bytes, pool, s);
     if (e != cudaSuccess) return e;
-    e = cudaMemsetAsync(xs, 0, header, s);
-    if (e == cudaSuccess) {
+    {
         const unsigned g = grid_for((uint64_t)n_pt * nk * TN * (kTcK / 8), kThreads);
         split_x_kernel<TN><<<g, kThreads, 0, s>>>(X, batch, L.cols, nk, (uint8_t *)xs);
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) {
-        kernel<<<grid, kTcThreads + 32, (size_t)tc_stages(TN) * tc_stage_bytes(TN), s>>>(
-            L, w, X, (const uint8_t *)xs, batch, Y);
+        // at least 120 KiB so that one CTA holds an SM (and all of its
+        // tensor memory): a second CTA's allocation would wait for the first
+        size_t smem = (size_t)tc_stages(TN) * tc_stage_bytes(TN);
+        if (smem < 120u * 1024u) smem = 120u * 1024u;
+        kernel<<<grid, kTcThreads + 64, smem, s>>>(L, w, X, (const uint8_t *)xs, batch, Y);
         e = cudaGetLastError();
     }
     const cudaError_t f = cudaFreeAsync(xs, s);
