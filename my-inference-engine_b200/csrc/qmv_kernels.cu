@@ -328,26 +328,34 @@ __device__ __forceinline__ XS xs_view(const uint8_t *base, int cols)
 
 // Quantize x[0..cols) into shared memory (every thread of the CTA takes part;
 // 8 consecutive lanes own one 32-element block, 4 lanes one 16-element slice).
+// np > 1 quantizes the rows x[p * cols ..] of np positions in one pass (the
+// float4s of all positions form one contiguous range, and a 32-element block
+// never straddles two positions since cols is a multiple of 32), so the
+// global-load latency is paid once; position p goes to base + p * pos_bytes.
 template <uint32_t FMT, int NT = kThreads>
-__device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t *base)
+__device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t *base, int np = 1,
+                           size_t pos_bytes = 0)
 {
-    uint8_t *hi = base;
-    uint8_t *lo = base + cols;
-    float2 *rec = reinterpret_cast<float2 *>(base + 2 * cols);
     const int n4 = cols >> 2;
+    const int total = np * n4;
     constexpr int U = 8;
-    for (int it0 = 0; it0 * NT < n4; it0 += U) {
+    for (int it0 = 0; it0 * NT < total; it0 += U) {
         float4 v[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            int f = (it0 + u) * NT + threadIdx.x;
-            v[u] = f < n4 ? __ldg(reinterpret_cast<const float4 *>(x) + f)
-                          : make_float4(0.f, 0.f, 0.f, 0.f);
+            int g = (it0 + u) * NT + threadIdx.x;
+            v[u] = g < total ? __ldg(reinterpret_cast<const float4 *>(x) + g)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            if ((it0 + u) * NT >= n4) break;  // uniform across the CTA
-            const int f = (it0 + u) * NT + threadIdx.x;
+            if ((it0 + u) * NT >= total) break;  // uniform across the CTA
+            const int g = (it0 + u) * NT + threadIdx.x;
+            const int pos = (np == 1 || g >= total) ? 0 : g / n4;
+            const int f = g - pos * n4;
+            uint8_t *hi = base + pos * pos_bytes;
+            uint8_t *lo = hi + cols;
+            float2 *rec = reinterpret_cast<float2 *>(hi + 2 * cols);
             uint32_t a = max(max(__float_as_uint(fabsf(v[u].x)), __float_as_uint(fabsf(v[u].y))),
                              max(__float_as_uint(fabsf(v[u].z)), __float_as_uint(fabsf(v[u].w))));
             a = max(a, __shfl_xor_sync(kFull, a, 1));
@@ -375,7 +383,7 @@ __device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t
             int s4 = q0 + q1 + q2 + q3;
             s4 += __shfl_xor_sync(kFull, s4, 1);
             s4 += __shfl_xor_sync(kFull, s4, 2);
-            if (f < n4) {
+            if (g < total) {
                 const int p = (4 * f) & ~15;
                 const int si = Slices<FMT>::index(p, C);
                 const int off = (si << 4) + ((4 * f) & 15);
@@ -465,12 +473,20 @@ template <> struct W<kQ8_0> {
         b = lds128(row + ((L.C + c) << 4));
         d = lds16(row + L.off_a + 2 * c);
     }
-    __device__ __forceinline__ float dot(const XR<2> &x) const
+    // Unpacked chunk: what dot() needs, computed once per chunk and reused
+    // by every position of a batch.
+    struct U {
+        uint4 a, b;
+        float d;
+    };
+    __device__ __forceinline__ U unpack() const { return U{a, b, f16_fast(d)}; }
+    static __device__ __forceinline__ float dot_u(const U &u, const XR<2> &x)
     {
-        const int ah = dot4(b, x.h[1], dot4(a, x.h[0], 0));
-        const int al = dot4(b, x.l[1], dot4(a, x.l[0], 0));
-        return (f16_fast(d) * x.r[0].x) * (float)(ah * 256 + al);
+        const int ah = dot4(u.b, x.h[1], dot4(u.a, x.h[0], 0));
+        const int al = dot4(u.b, x.l[1], dot4(u.a, x.l[0], 0));
+        return (u.d * x.r[0].x) * (float)(ah * 256 + al);
     }
+    __device__ __forceinline__ float dot(const XR<2> &x) const { return dot_u(unpack(), x); }
 };
 
 // Spread bits 0..3 of v to bit 4 of bytes 0..3.
@@ -496,20 +512,29 @@ template <> struct W<kQ5_0> {
         qh = lds32(row + L.off_a + 4 * c);
         d = lds16(row + L.off_b + 2 * c);
     }
-    __device__ __forceinline__ float dot(const XR<2> &x) const
+    struct U {
+        uint4 lw, hw;
+        float d;
+    };
+    __device__ __forceinline__ U unpack() const
     {
         // weights 4k..4k+3 from low nibbles, 16+4k.. from high nibbles; the
         // fifth bit of weight i is bit i of qh
-        const uint4 lw = make_uint4((q.x & 0x0f0f0f0fu) | spread4(qh), (q.y & 0x0f0f0f0fu) | spread4(qh >> 4),
-                                    (q.z & 0x0f0f0f0fu) | spread4(qh >> 8), (q.w & 0x0f0f0f0fu) | spread4(qh >> 12));
-        const uint4 hw = make_uint4(((q.x >> 4) & 0x0f0f0f0fu) | spread4(qh >> 16),
-                                    ((q.y >> 4) & 0x0f0f0f0fu) | spread4(qh >> 20),
-                                    ((q.z >> 4) & 0x0f0f0f0fu) | spread4(qh >> 24),
-                                    ((q.w >> 4) & 0x0f0f0f0fu) | spread4(qh >> 28));
-        const int ah = dot4(hw, x.h[1], dot4(lw, x.h[0], 0));
-        const int al = dot4(hw, x.l[1], dot4(lw, x.l[0], 0));
-        return f16_fast(d) * (x.r[0].x * (float)(ah * 256 + al) - 16.f * (x.r[0].y + x.r[1].y));
+        U u;
+        u.lw = make_uint4((q.x & 0x0f0f0f0fu) | spread4(qh), (q.y & 0x0f0f0f0fu) | spread4(qh >> 4),
+                          (q.z & 0x0f0f0f0fu) | spread4(qh >> 8), (q.w & 0x0f0f0f0fu) | spread4(qh >> 12));
+        u.hw = make_uint4(((q.x >> 4) & 0x0f0f0f0fu) | spread4(qh >> 16), ((q.y >> 4) & 0x0f0f0f0fu) | spread4(qh >> 20),
+                          ((q.z >> 4) & 0x0f0f0f0fu) | spread4(qh >> 24), ((q.w >> 4) & 0x0f0f0f0fu) | spread4(qh >> 28));
+        u.d = f16_fast(d);
+        return u;
     }
+    static __device__ __forceinline__ float dot_u(const U &u, const XR<2> &x)
+    {
+        const int ah = dot4(u.hw, x.h[1], dot4(u.lw, x.h[0], 0));
+        const int al = dot4(u.hw, x.l[1], dot4(u.lw, x.l[0], 0));
+        return u.d * (x.r[0].x * (float)(ah * 256 + al) - 16.f * (x.r[0].y + x.r[1].y));
+    }
+    __device__ __forceinline__ float dot(const XR<2> &x) const { return dot_u(unpack(), x); }
 };
 
 template <> struct W<kQ4_K> {
@@ -531,20 +556,21 @@ template <> struct W<kQ4_K> {
         hdr = lds128(row + L.off_a + ((c >> 2) << 4));
         g = c & 3;
     }
-    __device__ __forceinline__ float dot(const XR<4> &x) const
+    struct U {
+        uint4 la, lb, ua, ub;
+        float s0, m0, s1, m1;  // d * sc and dmin * m of sub-blocks 2g and 2g+1
+    };
+    __device__ __forceinline__ U unpack() const
     {
         // slices 0/1: low nibbles of pieces a/b (sub-block 2g);
         // slices 2/3: high nibbles (sub-block 2g+1)
-        const uint4 la = make_uint4(a.x & 0x0f0f0f0fu, a.y & 0x0f0f0f0fu, a.z & 0x0f0f0f0fu, a.w & 0x0f0f0f0fu);
-        const uint4 lb = make_uint4(b.x & 0x0f0f0f0fu, b.y & 0x0f0f0f0fu, b.z & 0x0f0f0f0fu, b.w & 0x0f0f0f0fu);
-        const uint4 ua = make_uint4((a.x >> 4) & 0x0f0f0f0fu, (a.y >> 4) & 0x0f0f0f0fu,
-                                    (a.z >> 4) & 0x0f0f0f0fu, (a.w >> 4) & 0x0f0f0f0fu);
-        const uint4 ub = make_uint4((b.x >> 4) & 0x0f0f0f0fu, (b.y >> 4) & 0x0f0f0f0fu,
-                                    (b.z >> 4) & 0x0f0f0f0fu, (b.w >> 4) & 0x0f0f0f0fu);
-        const int ah0 = dot4(lb, x.h[1], dot4(la, x.h[0], 0));
-        const int al0 = dot4(lb, x.l[1], dot4(la, x.l[0], 0));
-        const int ah1 = dot4(ub, x.h[3], dot4(ua, x.h[2], 0));
-        const int al1 = dot4(ub, x.l[3], dot4(ua, x.l[2], 0));
+        U u;
+        u.la = make_uint4(a.x & 0x0f0f0f0fu, a.y & 0x0f0f0f0fu, a.z & 0x0f0f0f0fu, a.w & 0x0f0f0f0fu);
+        u.lb = make_uint4(b.x & 0x0f0f0f0fu, b.y & 0x0f0f0f0fu, b.z & 0x0f0f0f0fu, b.w & 0x0f0f0f0fu);
+        u.ua = make_uint4((a.x >> 4) & 0x0f0f0f0fu, (a.y >> 4) & 0x0f0f0f0fu, (a.z >> 4) & 0x0f0f0f0fu,
+                          (a.w >> 4) & 0x0f0f0f0fu);
+        u.ub = make_uint4((b.x >> 4) & 0x0f0f0f0fu, (b.y >> 4) & 0x0f0f0f0fu, (b.z >> 4) & 0x0f0f0f0fu,
+                          (b.w >> 4) & 0x0f0f0f0fu);
         // 6-bit scale / min of sub-blocks 2g and 2g+1 (src/quantization.cpp:351-378),
         // computed without a branch: lanes of one warp hold different g.
         // Sub-block j < 4: sc = b[j] & 63, m = b[j+4] & 63.  j >= 4:
@@ -560,10 +586,23 @@ template <> struct W<kQ4_K> {
         const uint32_t sc1 = ((lo_s >> t1) & lmask) | ((((hs >> t1) >> 6) & 3u) << 4);
         const uint32_t m1 = ((lo_m >> t1) & lmask) | ((((hm >> t1) >> 6) & 3u) << 4);
         const float d = f16_fast(hdr.x), dmin = f16_fast(hdr.x >> 16);
-        const float v0 = (d * (float)sc0) * (x.r[0].x * (float)(ah0 * 256 + al0)) - (dmin * (float)m0) * (x.r[0].y + x.r[1].y);
-        const float v1 = (d * (float)sc1) * (x.r[2].x * (float)(ah1 * 256 + al1)) - (dmin * (float)m1) * (x.r[2].y + x.r[3].y);
+        u.s0 = d * (float)sc0;
+        u.m0 = dmin * (float)m0;
+        u.s1 = d * (float)sc1;
+        u.m1 = dmin * (float)m1;
+        return u;
+    }
+    static __device__ __forceinline__ float dot_u(const U &u, const XR<4> &x)
+    {
+        const int ah0 = dot4(u.lb, x.h[1], dot4(u.la, x.h[0], 0));
+        const int al0 = dot4(u.lb, x.l[1], dot4(u.la, x.l[0], 0));
+        const int ah1 = dot4(u.ub, x.h[3], dot4(u.ua, x.h[2], 0));
+        const int al1 = dot4(u.ub, x.l[3], dot4(u.ua, x.l[2], 0));
+        const float v0 = u.s0 * (x.r[0].x * (float)(ah0 * 256 + al0)) - u.m0 * (x.r[0].y + x.r[1].y);
+        const float v1 = u.s1 * (x.r[2].x * (float)(ah1 * 256 + al1)) - u.m1 * (x.r[2].y + x.r[3].y);
         return v0 + v1;
     }
+    __device__ __forceinline__ float dot(const XR<4> &x) const { return dot_u(unpack(), x); }
 };
 
 // Signed byte B of v as an int, in one byte-permute (sign-replicating
@@ -597,37 +636,44 @@ template <> struct W<kQ6_K> {
         sc = lds32(row + L.off_a + 4 * c);
         d = lds16(row + L.off_b + 2 * (c >> 2));
     }
-    __device__ __forceinline__ float dot(const XR<4> &x) const
+    struct U {
+        uint4 w0, w1, w2, w3;
+        float s0, s1, s2, s3, d;
+    };
+    __device__ __forceinline__ U unpack() const
     {
         // 6-bit values 0..63 per region (src/quantization.cpp:559-586)
-        const uint4 w0 = make_uint4((a.x & 0x0f0f0f0fu) | ((u.x << 4) & 0x30303030u),
-                                    (a.y & 0x0f0f0f0fu) | ((u.y << 4) & 0x30303030u),
-                                    (a.z & 0x0f0f0f0fu) | ((u.z << 4) & 0x30303030u),
-                                    (a.w & 0x0f0f0f0fu) | ((u.w << 4) & 0x30303030u));
-        const uint4 w1 = make_uint4((b.x & 0x0f0f0f0fu) | ((u.x << 2) & 0x30303030u),
-                                    (b.y & 0x0f0f0f0fu) | ((u.y << 2) & 0x30303030u),
-                                    (b.z & 0x0f0f0f0fu) | ((u.z << 2) & 0x30303030u),
-                                    (b.w & 0x0f0f0f0fu) | ((u.w << 2) & 0x30303030u));
-        const uint4 w2 = make_uint4(((a.x >> 4) & 0x0f0f0f0fu) | (u.x & 0x30303030u),
-                                    ((a.y >> 4) & 0x0f0f0f0fu) | (u.y & 0x30303030u),
-                                    ((a.z >> 4) & 0x0f0f0f0fu) | (u.z & 0x30303030u),
-                                    ((a.w >> 4) & 0x0f0f0f0fu) | (u.w & 0x30303030u));
-        const uint4 w3 = make_uint4(((b.x >> 4) & 0x0f0f0f0fu) | ((u.x >> 2) & 0x30303030u),
-                                    ((b.y >> 4) & 0x0f0f0f0fu) | ((u.y >> 2) & 0x30303030u),
-                                    ((b.z >> 4) & 0x0f0f0f0fu) | ((u.z >> 2) & 0x30303030u),
-                                    ((b.w >> 4) & 0x0f0f0f0fu) | ((u.w >> 2) & 0x30303030u));
-        const int A0 = dot4(w0, x.h[0], 0) * 256 + dot4(w0, x.l[0], 0);
-        const int A1 = dot4(w1, x.h[1], 0) * 256 + dot4(w1, x.l[1], 0);
-        const int A2 = dot4(w2, x.h[2], 0) * 256 + dot4(w2, x.l[2], 0);
-        const int A3 = dot4(w3, x.h[3], 0) * 256 + dot4(w3, x.l[3], 0);
-        const float s0 = (float)sbyte<0>(sc), s1 = (float)sbyte<1>(sc);
-        const float s2 = (float)sbyte<2>(sc), s3 = (float)sbyte<3>(sc);
-        float acc = s0 * (x.r[0].x * (float)A0 - 32.f * x.r[0].y);
-        acc += s1 * (x.r[1].x * (float)A1 - 32.f * x.r[1].y);
-        acc += s2 * (x.r[2].x * (float)A2 - 32.f * x.r[2].y);
-        acc += s3 * (x.r[3].x * (float)A3 - 32.f * x.r[3].y);
-        return f16_fast(d) * acc;
+        U r;
+        r.w0 = make_uint4((a.x & 0x0f0f0f0fu) | ((u.x << 4) & 0x30303030u), (a.y & 0x0f0f0f0fu) | ((u.y << 4) & 0x30303030u),
+                          (a.z & 0x0f0f0f0fu) | ((u.z << 4) & 0x30303030u), (a.w & 0x0f0f0f0fu) | ((u.w << 4) & 0x30303030u));
+        r.w1 = make_uint4((b.x & 0x0f0f0f0fu) | ((u.x << 2) & 0x30303030u), (b.y & 0x0f0f0f0fu) | ((u.y << 2) & 0x30303030u),
+                          (b.z & 0x0f0f0f0fu) | ((u.z << 2) & 0x30303030u), (b.w & 0x0f0f0f0fu) | ((u.w << 2) & 0x30303030u));
+        r.w2 = make_uint4(((a.x >> 4) & 0x0f0f0f0fu) | (u.x & 0x30303030u), ((a.y >> 4) & 0x0f0f0f0fu) | (u.y & 0x30303030u),
+                          ((a.z >> 4) & 0x0f0f0f0fu) | (u.z & 0x30303030u), ((a.w >> 4) & 0x0f0f0f0fu) | (u.w & 0x30303030u));
+        r.w3 = make_uint4(((b.x >> 4) & 0x0f0f0f0fu) | ((u.x >> 2) & 0x30303030u),
+                          ((b.y >> 4) & 0x0f0f0f0fu) | ((u.y >> 2) & 0x30303030u),
+                          ((b.z >> 4) & 0x0f0f0f0fu) | ((u.z >> 2) & 0x30303030u),
+                          ((b.w >> 4) & 0x0f0f0f0fu) | ((u.w >> 2) & 0x30303030u));
+        r.s0 = (float)sbyte<0>(sc);
+        r.s1 = (float)sbyte<1>(sc);
+        r.s2 = (float)sbyte<2>(sc);
+        r.s3 = (float)sbyte<3>(sc);
+        r.d = f16_fast(d);
+        return r;
     }
+    static __device__ __forceinline__ float dot_u(const U &r, const XR<4> &x)
+    {
+        const int A0 = dot4(r.w0, x.h[0], 0) * 256 + dot4(r.w0, x.l[0], 0);
+        const int A1 = dot4(r.w1, x.h[1], 0) * 256 + dot4(r.w1, x.l[1], 0);
+        const int A2 = dot4(r.w2, x.h[2], 0) * 256 + dot4(r.w2, x.l[2], 0);
+        const int A3 = dot4(r.w3, x.h[3], 0) * 256 + dot4(r.w3, x.l[3], 0);
+        float acc = r.s0 * (x.r[0].x * (float)A0 - 32.f * x.r[0].y);
+        acc += r.s1 * (x.r[1].x * (float)A1 - 32.f * x.r[1].y);
+        acc += r.s2 * (x.r[2].x * (float)A2 - 32.f * x.r[2].y);
+        acc += r.s3 * (x.r[3].x * (float)A3 - 32.f * x.r[3].y);
+        return r.d * acc;
+    }
+    __device__ __forceinline__ float dot(const XR<4> &x) const { return dot_u(unpack(), x); }
 };
 
 // ------------------------------------------------------- GEMV (loads)
@@ -818,13 +864,18 @@ struct TmaPlan {
     int stages;            // NS
     int consumer_warps;    // CW
     int rows_per_warp;     // R
+    int np;                // positions (1: GEMV; up to the kernel's NP: batched)
 };
 
-template <uint32_t FMT, int CW, int R>
+// NP > 1: the batched form for up to NP positions (x holds P.np rows of
+// cols floats, y P.np rows of L.rows); each staged weight chunk is unpacked
+// once per row and applied to every position.  No argmax or exchange there.
+template <uint32_t FMT, int CW, int R, int NP = 1>
 __global__ void __launch_bounds__((CW + 1) * 32, 1)
 gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x,
                 float *__restrict__ y, ArgmaxOut am, int want_argmax, TmaPlan P, Exchange ex)
 {
+    static_assert(R * NP <= 32, "one lane per (row, position) output");
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) unsigned long long bars[2 * 8];
     __shared__ unsigned long long kscratch[kMaxConsumerWarps + 1];
@@ -898,7 +949,8 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
         asm volatile("griddepcontrol.wait;" ::: "memory");
         if (ex.world > 1)  // this rank's slot in this epoch's parity region
             y = ex.logits[exchange_epoch(ex) & 1u][ex.rank] + (size_t)ex.rank * ex.slot_rows;
-        quantize_x<FMT, CW * 32>(x, L.cols, C, smem);
+        const size_t xb = xs_bytes(L.cols);
+        quantize_x<FMT, CW * 32>(x, L.cols, C, smem, NP == 1 ? 1 : P.np, xb);
         asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
         const XS s = xs_view(smem, L.cols);
         const int NI = (C + 31) >> 5;
@@ -911,9 +963,12 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
             const int base_row = r0 + k * SR;
             const int rows_k = min(SR, r1 - base_row);
             const uint32_t sbase = stage0 + (uint32_t)sidx * P.stage_bytes;
-            float acc[R];
+            float acc[R][NP];
 #pragma unroll
-            for (int i = 0; i < R; ++i) acc[i] = 0.f;
+            for (int i = 0; i < R; ++i) {
+#pragma unroll
+                for (int p = 0; p < NP; ++p) acc[i][p] = 0.f;
+            }
             const int lr0 = warp * R;
             if (lr0 < rows_k) {
                 for (int it = 0; it < NI; ++it) {
@@ -926,9 +981,23 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
 #pragma unroll
                         for (int i = 0; i < R; ++i)
                             wv[i].load_smem(sbase + (uint32_t)(lr0 + i) * (uint32_t)L.row_stride, L, c);
-                        const XR<NSL> xr = load_xr<NSL>(s, C, c);
+                        if constexpr (NP == 1) {
+                            const XR<NSL> xr = load_xr<NSL>(s, C, c);
 #pragma unroll
-                        for (int i = 0; i < R; ++i) acc[i] += wv[i].dot(xr);
+                            for (int i = 0; i < R; ++i) acc[i][0] += wv[i].dot(xr);
+                        } else {
+                            typename W<FMT>::U u[R];
+#pragma unroll
+                            for (int i = 0; i < R; ++i) u[i] = wv[i].unpack();
+#pragma unroll
+                            for (int p = 0; p < NP; ++p) {
+                                if (p < P.np) {
+                                    const XR<NSL> xr = load_xr<NSL>(xs_view(smem + p * xb, L.cols), C, c);
+#pragma unroll
+                                    for (int i = 0; i < R; ++i) acc[i][p] += W<FMT>::dot_u(u[i], xr);
+                                }
+                            }
+                        }
                     }
                 }
             }
@@ -937,16 +1006,24 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
 #pragma unroll
             for (int i = 0; i < R; ++i) {
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(kFull, acc[i], o);
+                for (int p = 0; p < NP; ++p) {
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) acc[i][p] += __shfl_xor_sync(kFull, acc[i][p], o);
+                }
             }
+            // lane j writes row lr0 + j / NP, position j % NP
             float out = 0.f;
 #pragma unroll
-            for (int i = 0; i < R; ++i)
-                if (lane == i) out = acc[i];
-            if (lane < R && lr0 + lane < rows_k) {
-                const int row = base_row + lr0 + lane;
-                y[row] = out;
-                if (want_argmax) best = max_ull(best, make_key(out, am.index_base + row));
+            for (int i = 0; i < R; ++i) {
+#pragma unroll
+                for (int p = 0; p < NP; ++p)
+                    if (lane == i * NP + p) out = acc[i][p];
+            }
+            const int oi = lane / NP, op = lane % NP;
+            if (lane < R * NP && lr0 + oi < rows_k && op < P.np) {
+                const int row = base_row + lr0 + oi;
+                y[(size_t)op * L.rows + row] = out;
+                if (NP == 1 && want_argmax) best = max_ull(best, make_key(out, am.index_base + row));
             }
         }
     }
@@ -963,54 +1040,106 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
 
 // ------------------------------------------------------------- matmul
 //
-// Batched form for up to NP positions per launch: x of every position is
-// quantized into shared memory first, then each group of TPT lanes takes one
-// row at a time and applies every loaded weight chunk to all positions.
+// Batched form for up to NP positions per launch (the reference's chunk of
+// 8 positions).  quantize_x_kernel writes the quantized x of every position
+// once, as the shared-memory image the GEMV kernels build (hi | lo |
+// records, xs_bytes(cols) per position), and every matmul CTA copies that
+// image into shared memory.  The matmul kernel is launched with programmatic
+// dependent launch: its first weight loads are issued before
+// griddepcontrol.wait, so they overlap the quantization kernel.  Groups of
+// TPT lanes take rows with the same one-deep prefetch over (row, chunk)
+// items as gemv_kernel; each loaded chunk is unpacked once and applied to
+// every position.
+
+template <uint32_t FMT>
+__global__ void __launch_bounds__(kThreads)
+quantize_x_kernel(const float *__restrict__ X, int cols, int C, uint8_t *__restrict__ xq, size_t xb)
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    quantize_x<FMT>(X + (size_t)blockIdx.x * cols, cols, C, xq + (size_t)blockIdx.x * xb);
+}
 
 template <uint32_t FMT, int TPT, int NP>
 __global__ void __launch_bounds__(kThreads)
-matmul_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ X, int np,
+matmul_kernel(Layout L, const uint8_t *__restrict__ w, const uint8_t *__restrict__ xq, int np,
               float *__restrict__ Y)
 {
+    static_assert(TPT >= NP, "lane p of a row group writes position p");
     extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int NSL = W<FMT>::kSlices;
     const int C = L.C;
     const size_t xb = xs_bytes(L.cols);
-    for (int p = 0; p < np; ++p) quantize_x<FMT>(X + (size_t)p * L.cols, L.cols, C, smem + p * xb);
-    __syncthreads();
-
     constexpr int GPW = 32 / TPT;
     const int lane = threadIdx.x & 31;
     const int grp = lane / TPT, gl = lane % TPT;
     const int wg = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
     const int wtot = gridDim.x * (kThreads / 32);
+    const int NI = (C + TPT - 1) / TPT;
     const int tiles = (L.rows + GPW - 1) / GPW;
+    const int my_tiles = wg < tiles ? (tiles - 1 - wg) / wtot + 1 : 0;
+    const int n_items = my_tiles * NI;
 
-    for (int t = wg; t < tiles; t += wtot) {
-        const int row = t * GPW + grp;
-        float acc[NP];
+    // Item k = (tile t, chunk iteration it); both advance incrementally.
+    auto load_item = [&](int t, int it, W<FMT> &dst) {
+        const int c = it * TPT + gl, row = t * GPW + grp;
+        if (c < C && row < L.rows)
+            dst.load(w + (uint64_t)row * L.row_stride, L, c);
+        else
+            dst.zero();
+    };
+    W<FMT> bufa, bufb;
+    int t = wg, it = 0;
+    if (n_items > 0) load_item(t, it, bufa);
+
+    // x comes from quantize_x_kernel, the launch this one depends on
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(xq);
+        uint4 *dst = reinterpret_cast<uint4 *>(smem);
+        const int n16 = (int)((size_t)np * xb / 16);
+        for (int i = threadIdx.x; i < n16; i += kThreads) dst[i] = src[i];
+    }
+    __syncthreads();
+
+    float acc[NP];
 #pragma unroll
-        for (int p = 0; p < NP; ++p) acc[p] = 0.f;
-        if (row < L.rows) {
-            const uint8_t *rp = w + (uint64_t)row * L.row_stride;
-            for (int c = gl; c < C; c += TPT) {
-                W<FMT> ch;
-                ch.load(rp, L, c);
+    for (int p = 0; p < NP; ++p) acc[p] = 0.f;
+    // Compute item (t, it) from `use` while `pre` receives item k+1.
+    auto step = [&](int k, int &t, int &it, W<FMT> &use, W<FMT> &pre) {
+        int nt = t, nit = it + 1;
+        if (nit == NI) {
+            nit = 0;
+            nt += wtot;
+        }
+        if (k + 1 < n_items) load_item(nt, nit, pre);
+        const int c = it * TPT + gl;
+        if (c < C) {
+            const typename W<FMT>::U u = use.unpack();
 #pragma unroll
-                for (int p = 0; p < NP; ++p)
-                    if (p < np)
-                        acc[p] += ch.dot(load_xr<W<FMT>::kSlices>(xs_view(smem + p * xb, L.cols), C, c));
+            for (int p = 0; p < NP; ++p)
+                if (p < np) acc[p] += W<FMT>::dot_u(u, load_xr<NSL>(xs_view(smem + p * xb, L.cols), C, c));
+        }
+        if (it == NI - 1) {
+#pragma unroll
+            for (int p = 0; p < NP; ++p) {
+#pragma unroll
+                for (int o = TPT / 2; o > 0; o >>= 1) acc[p] += __shfl_xor_sync(kFull, acc[p], o);
             }
+            float out = 0.f;
+#pragma unroll
+            for (int p = 0; p < NP; ++p)
+                if (gl == p) out = acc[p];
+            const int row = t * GPW + grp;
+            if (gl < np && row < L.rows) Y[(size_t)gl * L.rows + row] = out;
+#pragma unroll
+            for (int p = 0; p < NP; ++p) acc[p] = 0.f;
         }
-#pragma unroll
-        for (int p = 0; p < NP; ++p) {
-#pragma unroll
-            for (int o = TPT / 2; o > 0; o >>= 1) acc[p] += __shfl_xor_sync(kFull, acc[p], o);
-        }
-        float out = 0.f;
-#pragma unroll
-        for (int p = 0; p < NP; ++p)
-            if (gl == p) out = acc[p];
-        if (gl < np && row < L.rows) Y[(size_t)gl * L.rows + row] = out;
+        t = nt;
+        it = nit;
+    };
+    for (int k = 0; k < n_items; k += 2) {
+        step(k, t, it, bufa, bufb);
+        if (k + 1 < n_items) step(k + 1, t, it, bufb, bufa);
     }
 }
 
@@ -1067,8 +1196,6 @@ __host__ __device__ constexpr int tc_stages(int tn)
 }
 
 // Split-x scratch: the stage images, position tile-major.
-__device__ __forceinline__ uint32_t ldg16(const uint8_t *p) { return __ldg((const unsigned short *)p); }
-
 // 2^23 + (byte I of w), exactly: the byte becomes the low mantissa bits of a
 // float whose exponent is that of 2^23.  Integer-to-float without the
 // conversion pipe; callers subtract 2^23 (plus any offset) exactly.
@@ -1091,16 +1218,26 @@ __device__ __forceinline__ void bytes_to_float(uint32_t n0, uint32_t n1, float b
 // one resident row, and their decoding to fp32 with the reference's
 // arithmetic (src/quantization.cpp:54-67, 161-184, 380-409, 588-615): every
 // product below is exact or rounds once, as there.
+// Loads of the raw bytes: read-only global loads, or plain loads when the
+// tile's rows have been copied to shared memory (same offsets).
+template <bool SMEM, typename T>
+__device__ __forceinline__ T ld_raw(const uint8_t *p)
+{
+    if constexpr (SMEM) return *(const T *)p;
+    else return __ldg((const T *)p);
+}
+
 template <uint32_t FMT> struct Raw8;
 
 template <> struct Raw8<kQ8_0> {
     uint2 q;
     uint32_t d;
+    template <bool SMEM = false>
     __device__ __forceinline__ void load(const uint8_t *row, const Layout &L, int k0)
     {
         const int b = k0 >> 5, i0 = k0 & 31;
-        q = __ldg((const uint2 *)(row + (((i0 < 16) ? b : L.C + b) << 4) + (i0 & 8)));
-        d = ldg16(row + L.off_a + 2 * b);
+        q = ld_raw<SMEM, uint2>(row + (((i0 < 16) ? b : L.C + b) << 4) + (i0 & 8));
+        d = ld_raw<SMEM, unsigned short>(row + L.off_a + 2 * b);
     }
     __device__ __forceinline__ bool decode(int, float v[8]) const
     {
@@ -1116,12 +1253,13 @@ template <> struct Raw8<kQ8_0> {
 template <> struct Raw8<kQ5_0> {
     uint2 q;
     uint32_t qh, d;
+    template <bool SMEM = false>
     __device__ __forceinline__ void load(const uint8_t *row, const Layout &L, int k0)
     {
         const int b = k0 >> 5, i0 = k0 & 31;
-        q = __ldg((const uint2 *)(row + (b << 4) + (i0 & 8)));
-        qh = __ldg((const uint32_t *)(row + L.off_a + 4 * b)) >> i0;
-        d = ldg16(row + L.off_b + 2 * b);
+        q = ld_raw<SMEM, uint2>(row + (b << 4) + (i0 & 8));
+        qh = ld_raw<SMEM, uint32_t>(row + L.off_a + 4 * b) >> i0;
+        d = ld_raw<SMEM, unsigned short>(row + L.off_b + 2 * b);
     }
     __device__ __forceinline__ bool decode(int k0, float v[8]) const
     {
@@ -1141,12 +1279,13 @@ template <> struct Raw8<kQ5_0> {
 template <> struct Raw8<kQ4_K> {
     uint2 q;
     uint4 hdr;
+    template <bool SMEM = false>
     __device__ __forceinline__ void load(const uint8_t *row, const Layout &L, int k0)
     {
         const int sb = k0 >> 8, j = (k0 >> 5) & 7, o0 = k0 & 31;
         const int c = 4 * sb + (j >> 1);
-        q = __ldg((const uint2 *)(row + (((o0 < 16) ? c : L.C + c) << 4) + (o0 & 8)));
-        hdr = __ldg((const uint4 *)(row + L.off_a + (sb << 4)));
+        q = ld_raw<SMEM, uint2>(row + (((o0 < 16) ? c : L.C + c) << 4) + (o0 & 8));
+        hdr = ld_raw<SMEM, uint4>(row + L.off_a + (sb << 4));
     }
     __device__ __forceinline__ bool decode(int k0, float v[8]) const
     {
@@ -1176,16 +1315,17 @@ template <> struct Raw8<kQ4_K> {
 template <> struct Raw8<kQ6_K> {
     uint2 ql, qh;
     uint32_t sc, d;
+    template <bool SMEM = false>
     __device__ __forceinline__ void load(const uint8_t *row, const Layout &L, int k0)
     {
         // weight 128 g + 32 r + o of the super-block lives in chunk
         // 4 sb + 2 g + (o >> 4)
         const int sb = k0 >> 8, g = (k0 >> 7) & 1, r = (k0 >> 5) & 3, o0 = k0 & 31;
         const int c = 4 * sb + 2 * g + (o0 >> 4);
-        ql = __ldg((const uint2 *)(row + ((((r & 1) ? L.C : 0) + c) << 4) + (o0 & 8)));
-        qh = __ldg((const uint2 *)(row + ((2 * L.C + c) << 4) + (o0 & 8)));
-        sc = __ldg((const uint32_t *)(row + L.off_a + 4 * c));
-        d = ldg16(row + L.off_b + 2 * sb);
+        ql = ld_raw<SMEM, uint2>(row + ((((r & 1) ? L.C : 0) + c) << 4) + (o0 & 8));
+        qh = ld_raw<SMEM, uint2>(row + ((2 * L.C + c) << 4) + (o0 & 8));
+        sc = ld_raw<SMEM, uint32_t>(row + L.off_a + 4 * c);
+        d = ld_raw<SMEM, unsigned short>(row + L.off_b + 2 * sb);
     }
     __device__ __forceinline__ bool decode(int k0, float v[8]) const
     {
@@ -1353,15 +1493,17 @@ split_x_kernel(const float *__restrict__ X, int np, int cols, int nk, uint8_t *_
     }
 }
 
-template <uint32_t FMT, int TN>
+// WSMEM: the tile's resident rows are copied to shared memory once (when
+// they fit) and decoded from there; otherwise each decode thread loads its
+// bytes from global memory one stage ahead.  S: x stages in the ring.
+template <uint32_t FMT, int TN, bool WSMEM>
 __global__ void __launch_bounds__(kTcThreads + 64, 1)
 matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ X,
-                 const uint8_t *__restrict__ xs, int np, float *__restrict__ Y)
+                 const uint8_t *__restrict__ xs, int np, float *__restrict__ Y, int S)
 {
     static_assert(TN % 16 == 0 && TN >= 32 && TN <= 256, "N of one MMA: a multiple of 16 in 32..256");
     static_assert(kTcM * (kTcK / 8) == kTcThreads, "one weight unit per decode thread and stage");
-    constexpr int S = tc_stages(TN);
-    static_assert(kTcACol + 32u * S <= 512u, "A ring must fit tensor memory");
+    static_assert(kTcACol + 32u * kTcMaxStages <= 512u, "A ring must fit tensor memory");
     // warps 0..15 decode weights, warp 16 issues MMAs, warp 17 copies x
     constexpr int kDecodeWarps = kTcThreads / 32, kMmaWarp = kDecodeWarps, kCopyWarp = kDecodeWarps + 1;
     constexpr uint32_t kPlaneX = tc_plane_x(TN);
@@ -1369,8 +1511,9 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
     constexpr uint32_t kIdesc = umma_idesc(TN);
 
     extern __shared__ __align__(128) uint8_t smem[];
-    // [0, S) weights stored, [S, 2S) x landed, [2S, 3S) MMAs done
-    __shared__ __align__(8) unsigned long long bars[3 * S];
+    // [0, S) weights stored, [S, 2S) x landed, [2S, 3S) MMAs done, then the
+    // weight tile's arrival
+    __shared__ __align__(8) unsigned long long bars[3 * kTcMaxStages + 1];
     __shared__ uint32_t tmem_slot;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1378,7 +1521,10 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
     const int nk = (L.cols + kTcK - 1) / kTcK;
     const uint32_t smem0 = (uint32_t)__cvta_generic_to_shared(smem);
     const uint32_t wbar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]);
-    const uint32_t xbar0 = wbar0 + 8u * S, ebar0 = wbar0 + 16u * S;
+    const uint32_t xbar0 = wbar0 + 8u * S, ebar0 = wbar0 + 16u * S, tbar = wbar0 + 24u * S;
+    const int tile_rows = L.rows - r0 < kTcM ? L.rows - r0 : kTcM;
+    const uint32_t tile_bytes = (uint32_t)tile_rows * (uint32_t)L.row_stride;
+    const uint8_t *wtile = smem + (size_t)S * kStage;  // WSMEM: resident rows r0 .. r0 + tile_rows
 
     if (tid == 0) {
         for (int i = 0; i < S; ++i) {
@@ -1386,6 +1532,7 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
             mbar_init(xbar0 + 8u * i, 1u);
             mbar_init(ebar0 + 8u * i, 1u);
         }
+        mbar_init(tbar, 1u);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -1405,6 +1552,14 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
     if (warp == kCopyWarp) {
         // ------------------------------------------------ x stage copies
         if (lane == 0) {
+            if (WSMEM) {
+                // the tile's rows are contiguous: one run of tile_bytes
+                mbar_expect_tx(tbar, tile_bytes);
+                const uint8_t *src = w + (uint64_t)r0 * L.row_stride;
+                const uint32_t dst = smem0 + (uint32_t)S * kStage;
+                for (uint32_t off = 0; off < tile_bytes; off += 32768u)
+                    bulk_g2s(dst + off, src + off, min(32768u, tile_bytes - off), tbar);
+            }
             const uint8_t *ximg = xs + (size_t)pt * nk * (size_t)kStage;
             for (int j = 0; j < nk; ++j) {
                 const int s = j % S;
@@ -1445,21 +1600,32 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
         // ------------------------------------------------ weight decode
         // Warp w owns tensor-memory lanes 32 (w % 4) .. + 31 (tile rows) and
         // K group w / 4 of every stage: 8 K values = 4 columns per plane.
+        // A stage's stores are published (wait::st, then the arrival) only
+        // after the next stage has been decoded, so their latency overlaps
+        // that work.
         const int q = warp & 3, kg = warp >> 2;
         const int wrow_i = r0 + 32 * q + lane;
-        const uint8_t *wrow = wrow_i < L.rows ? w + (uint64_t)wrow_i * L.row_stride : nullptr;
+        const bool have_row = wrow_i < L.rows;
+        const uint8_t *wrow = WSMEM ? wtile + (size_t)(32 * q + lane) * L.row_stride
+                                    : w + (uint64_t)(have_row ? wrow_i : 0) * L.row_stride;
         const int wk = kg * 8;
         const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16) + kTcACol + 4u * kg;
+        if (WSMEM && !mbar_wait(tbar, 0u)) ok = false;
         Raw8<FMT> wr;
-        if (wrow != nullptr && wk < L.cols) wr.load(wrow, L, wk);
+        if (!WSMEM && have_row && wk < L.cols) wr.load(wrow, L, wk);
+        int pending = -1;  // stage whose tensor-memory stores are not yet published
         for (int kc = 0; kc < nk; ++kc) {
             const int s = kc % S;
-            Raw8<FMT> wn;
-            const int kn = (kc + 1) * kTcK + wk;
-            if (wrow != nullptr && kn < L.cols) wn.load(wrow, L, kn);
             const int k0 = kc * kTcK + wk;
+            Raw8<FMT> wn;
+            if (WSMEM) {
+                if (have_row && k0 < L.cols) wr.template load<true>(wrow, L, k0);
+            } else {
+                const int kn = k0 + kTcK;
+                if (have_row && kn < L.cols) wn.load(wrow, L, kn);
+            }
             float v[8];
-            if (wrow != nullptr && k0 < L.cols) {
+            if (have_row && k0 < L.cols) {
                 wr.decode(k0, v);
             } else {
 #pragma unroll
@@ -1467,20 +1633,30 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
             }
             uint32_t h[4], l[4];
             split_words(v, h, l);
+            if (pending >= 0) {
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(wbar0 + 8u * (pending % S));
+            }
             // the MMAs that last read stage buffer s (stage kc - S) are done
             if (kc >= S && !mbar_wait(ebar0 + 8u * s, (uint32_t)((kc / S - 1) & 1))) ok = false;
             if (!__all_sync(kFull, ok)) {
                 ok = false;
+                pending = -1;
                 break;
             }
             tc_fence_after();
             tmem_st4(lane_addr + 32u * s, h[0], h[1], h[2], h[3]);
             tmem_st4(lane_addr + 32u * s + 16u, l[0], l[1], l[2], l[3]);
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            pending = kc;
+            if (!WSMEM) wr = wn;
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        if (pending >= 0) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(wbar0 + 8u * s);
-            wr = wn;
+            if (lane == 0) mbar_arrive(wbar0 + 8u * (pending % S));
         }
     }
 
@@ -1492,7 +1668,8 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
     const bool failed = __syncthreads_or(!ok);
     if (failed && warp == kCopyWarp && lane == 0) {
         atomicOr(&g_status, kStatusMmaTimeout);
-        // x copies still in flight must land before the CTA exits
+        // copies still in flight must land before the CTA exits
+        if (WSMEM && !mbar_wait(tbar, 0u)) atomicOr(&g_status, kStatusDrainTimeout);
         for (int j = issued - S > 0 ? issued - S : 0; j < issued; ++j) {
             if (!mbar_wait(xbar0 + 8u * (j % S), (uint32_t)((j / S) & 1))) {
                 atomicOr(&g_status, kStatusDrainTimeout);
@@ -1848,14 +2025,20 @@ int g_gemv_path = 0;  // 0 auto, 1 direct loads, 2 TMA pipeline
 // Shared-memory plan of the TMA kernel: the first of these (consumer warps,
 // rows per warp, minimum stages) whose stages fit.  Two rows per warp share
 // each x slice load, so they come first; 16 warps hide shared-memory latency
-// better than 8.  false when none fits (the direct-load kernel runs).
-bool tma_plan(const Layout &L, TmaPlan *P)
+// better than 8.  batched: the plan of the batched kernel (np positions of
+// x in shared memory, 8 consumer warps).  false when none fits (the
+// direct-load kernels run).
+bool tma_plan(const Layout &L, TmaPlan *P, int np = 1, bool batched = false)
 {
     constexpr uint32_t kBudget = 227u * 1024u - 1024u;  // dynamic bytes, leaving static room
     static const int kCandidates[][3] = {{16, 2, 2}, {8, 2, 3}, {16, 1, 3}, {8, 2, 2}, {16, 1, 2}, {8, 1, 2}};
-    const uint32_t xb = (uint32_t)((xs_bytes(L.cols) + 127) & ~(size_t)127);
+    // batched form: 8 consumer warps (its per-thread state is larger)
+    static const int kBatchCandidates[][3] = {{8, 2, 2}, {8, 1, 2}};
+    const uint32_t xb = (uint32_t)((xs_bytes(L.cols) * (size_t)np + 127) & ~(size_t)127);
     if (xb >= kBudget) return false;
-    for (const auto &cand : kCandidates) {
+    const int n_cand = batched ? 2 : 6;
+    for (int ci = 0; ci < n_cand; ++ci) {
+        const int *cand = batched ? kBatchCandidates[ci] : kCandidates[ci];
         const int cw = cand[0], r = cand[1], min_stages = cand[2];
         const uint64_t sb = ((uint64_t)cw * r * L.row_stride + 127) & ~127ull;
         const uint64_t ns = (kBudget - xb) / sb;
@@ -1866,16 +2049,17 @@ bool tma_plan(const Layout &L, TmaPlan *P)
         P->stages = (int)(ns > 8 ? 8 : ns);
         P->consumer_warps = cw;
         P->rows_per_warp = r;
+        P->np = np;
         return true;
     }
     return false;
 }
 
-template <uint32_t FMT, int CW, int R>
+template <uint32_t FMT, int CW, int R, int NP = 1>
 cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, const float *x, float *y,
                         const ArgmaxOut *am, cudaStream_t s, const Exchange &ex = Exchange{})
 {
-    auto kernel = gemv_tma_kernel<FMT, CW, R>;
+    auto kernel = gemv_tma_kernel<FMT, CW, R, NP>;
     const size_t smem = (size_t)P.x_bytes + (size_t)P.stages * P.stage_bytes;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -1935,47 +2119,10 @@ cudaError_t gemv_fmt(const Layout &L, const uint8_t *w, const float *x, float *y
     return gemv_go<FMT, 32, 2>(L, w, x, y, am, s);
 }
 
-template <uint32_t FMT, int TPT>
-cudaError_t matmul_go(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
-                      cudaStream_t s)
-{
-    constexpr int NP = 8;
-    auto kernel = matmul_kernel<FMT, TPT, NP>;
-    const size_t xb = xs_bytes(L.cols);
-    // positions per launch: up to 8, bounded by shared memory (<= 200 KiB)
-    int np_max = (int)((200u * 1024u) / xb);
-    if (np_max > NP) np_max = NP;
-    if (np_max < 1) return cudaErrorInvalidValue;
-    int occ = 0;
-    cudaError_t e = prepare(kernel, xb * np_max, &occ);
-    if (e != cudaSuccess) return e;
-    constexpr int GPW = 32 / TPT;
-    const long long tiles = ((long long)L.rows + GPW - 1) / GPW;
-    long long grid = (long long)sm_count() * occ;
-    const long long useful = (tiles + (kThreads / 32) - 1) / (kThreads / 32);
-    if (grid > useful) grid = useful;
-    if (grid < 1) grid = 1;
-    for (int p0 = 0; p0 < batch; p0 += np_max) {
-        const int np = batch - p0 < np_max ? batch - p0 : np_max;
-        kernel<<<(unsigned)grid, kThreads, xb * np, s>>>(L, w, X + (size_t)p0 * L.cols, np,
-                                                         Y + (size_t)p0 * L.rows);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) return e;
-    }
-    return cudaSuccess;
-}
-
-// 0 auto, 1 CUDA cores (dp4a), 2 tensor cores, 64/128/176/256 tensor cores
-// with that position-tile width
-int g_matmul_path = 0;
-
-// Batches of at least this many positions take the tensor-core kernel.
-constexpr int kTcMinBatch = 32;
-
-// Stream-ordered pool for the split-x scratch of the tensor-core matmul, one
-// per device, created on first use.  It keeps freed memory (release
+// Stream-ordered pool for the per-call scratch of the matmul paths (quantized
+// or split x), one per device, created on first use.  It keeps freed memory (release
 // threshold: unlimited), so steady-state calls allocate without the driver.
-cudaError_t tc_scratch_pool(cudaMemPool_t *out)
+cudaError_t scratch_pool(cudaMemPool_t *out)
 {
     static std::mutex mu;
     static cudaMemPool_t pools[64] = {};
@@ -2004,11 +2151,70 @@ cudaError_t tc_scratch_pool(cudaMemPool_t *out)
     return cudaSuccess;
 }
 
+template <uint32_t FMT, int TPT>
+cudaError_t matmul_go(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
+                      cudaStream_t s)
+{
+    constexpr int NP = 8;
+    auto kernel = matmul_kernel<FMT, TPT, NP>;
+    const size_t xb = xs_bytes(L.cols);
+    // positions per launch: up to 8, bounded by shared memory (<= 200 KiB)
+    int np_max = (int)((200u * 1024u) / xb);
+    if (np_max > NP) np_max = NP;
+    if (np_max < 1) return cudaErrorInvalidValue;
+    int occ = 0;
+    cudaError_t e = prepare(kernel, xb * np_max, &occ);
+    if (e != cudaSuccess) return e;
+    constexpr int GPW = 32 / TPT;
+    const long long tiles = ((long long)L.rows + GPW - 1) / GPW;
+    long long grid = (long long)sm_count() * occ;
+    const long long useful = (tiles + (kThreads / 32) - 1) / (kThreads / 32);
+    if (grid > useful) grid = useful;
+    if (grid < 1) grid = 1;
+    cudaMemPool_t pool;
+    e = scratch_pool(&pool);
+    if (e != cudaSuccess) return e;
+    void *xq = nullptr;
+    e = cudaMallocFromPoolAsync(&xq, (size_t)batch * xb, pool, s);
+    if (e != cudaSuccess) return e;
+    quantize_x_kernel<FMT><<<(unsigned)batch, kThreads, 0, s>>>(X, L.cols, L.C, (uint8_t *)xq, xb);
+    e = cudaGetLastError();
+    for (int p0 = 0; p0 < batch && e == cudaSuccess; p0 += np_max) {
+        const int np = batch - p0 < np_max ? batch - p0 : np_max;
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = xb * np;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, kernel, L, w, (const uint8_t *)xq + (size_t)p0 * xb, np,
+                               Y + (size_t)p0 * L.rows);
+    }
+    const cudaError_t f = cudaFreeAsync(xq, s);
+    return e != cudaSuccess ? e : f;
+}
+
+// 0 auto, 1 CUDA cores (dp4a), 2 tensor cores, 64/128/176/256 tensor cores
+// with that position-tile width
+int g_matmul_path = 0;
+
+// Batches of at least this many positions take the tensor-core kernel.
+constexpr int kTcMinBatch = 32;
+
 template <uint32_t FMT, int TN>
 cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
                          cudaStream_t s)
 {
-    auto kernel = matmul_tc_kernel<FMT, TN>;
+    // weight tile in shared memory when it leaves room for at least 4 x stages
+    const uint32_t tile_max = (uint32_t)kTcM * (uint32_t)L.row_stride;
+    const bool wsmem = (uint64_t)kTcM * L.row_stride + 4u * tc_stage_bytes(TN) <= kTcSmemBudget;
+    int S = wsmem ? (int)((kTcSmemBudget - tile_max) / tc_stage_bytes(TN)) : tc_stages(TN);
+    if (S > kTcMaxStages) S = kTcMaxStages;
+    auto kernel = wsmem ? matmul_tc_kernel<FMT, TN, true> : matmul_tc_kernel<FMT, TN, false>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = allow_max_smem((const void *)kernel, dev);
@@ -2018,7 +2224,7 @@ cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const float *X, int 
     if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
     const size_t bytes = (size_t)n_pt * nk * tc_stage_bytes(TN);
     cudaMemPool_t pool;
-    e = tc_scratch_pool(&pool);
+    e = scratch_pool(&pool);
     if (e != cudaSuccess) return e;
     void *xs = nullptr;
     e = cudaMallocFromPoolAsync(&xs, bytes, pool, s);
@@ -2031,9 +2237,9 @@ cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const float *X, int 
     if (e == cudaSuccess) {
         // at least 120 KiB so that one CTA holds an SM (and all of its
         // tensor memory): a second CTA's allocation would wait for the first
-        size_t smem = (size_t)tc_stages(TN) * tc_stage_bytes(TN);
+        size_t smem = (size_t)S * tc_stage_bytes(TN) + (wsmem ? tile_max : 0u);
         if (smem < 120u * 1024u) smem = 120u * 1024u;
-        kernel<<<grid, kTcThreads + 64, smem, s>>>(L, w, X, (const uint8_t *)xs, batch, Y);
+        kernel<<<grid, kTcThreads + 64, smem, s>>>(L, w, X, (const uint8_t *)xs, batch, Y, S);
         e = cudaGetLastError();
     }
     const cudaError_t f = cudaFreeAsync(xs, s);
@@ -2063,6 +2269,29 @@ int tc_tile_width(int rows, int batch)
     return best;
 }
 
+// Batched CUDA-core form on the TMA pipeline: chunks of up to 8 positions.
+// false in *done when no stage plan fits (very long rows).
+template <uint32_t FMT>
+cudaError_t matmul_tma_fmt(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
+                           cudaStream_t s, bool *done)
+{
+    constexpr int NP = 8;
+    *done = false;
+    TmaPlan P;
+    if (!tma_plan(L, &P, batch < NP ? batch : NP, true)) return cudaSuccess;
+    *done = true;
+    for (int p0 = 0; p0 < batch; p0 += NP) {
+        const int np = batch - p0 < NP ? batch - p0 : NP;
+        if (!tma_plan(L, &P, np, true) || P.consumer_warps != 8) return cudaErrorInvalidConfiguration;
+        const float *x = X + (size_t)p0 * L.cols;
+        float *y = Y + (size_t)p0 * L.rows;
+        const cudaError_t e = P.rows_per_warp == 2 ? gemv_tma_go<FMT, 8, 2, NP>(L, P, w, x, y, nullptr, s)
+                                                   : gemv_tma_go<FMT, 8, 1, NP>(L, P, w, x, y, nullptr, s);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
 template <uint32_t FMT>
 cudaError_t matmul_fmt(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
                        cudaStream_t s)
@@ -2078,6 +2307,9 @@ cudaError_t matmul_fmt(const Layout &L, const uint8_t *w, const float *X, int ba
         default: return matmul_tc_go<FMT, 256>(L, w, X, batch, Y, s);
         }
     }
+    bool done = false;
+    const cudaError_t e = matmul_tma_fmt<FMT>(L, w, X, batch, Y, s, &done);
+    if (done || e != cudaSuccess) return e;
     if (L.C <= 16) return matmul_go<FMT, 16>(L, w, X, batch, Y, s);
     return matmul_go<FMT, 32>(L, w, X, batch, Y, s);
 }
