@@ -832,6 +832,33 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity)
     }
 }
 
+// The same wait for threads that have nothing else to do: each try suspends
+// the thread (up to 0.5 us, or until the phase completes) instead of
+// re-issuing, so a waiting producer or MMA thread does not take issue slots
+// from the warps sharing its scheduler.
+__device__ __forceinline__ bool mbar_try_idle(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(500u)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_idle(uint32_t bar, uint32_t parity)
+{
+    if (mbar_try_idle(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    for (;;) {
+        if (mbar_try_idle(bar, parity)) return true;
+        if (globaltimer() - t0 > kWaitLimitNs) return false;
+    }
+}
+
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count)
 {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
@@ -1230,6 +1257,7 @@ __device__ __forceinline__ T ld_raw(const uint8_t *p)
 template <uint32_t FMT> struct Raw8;
 
 template <> struct Raw8<kQ8_0> {
+    static constexpr bool kExactLo = false;
     uint2 q;
     uint32_t d;
     template <bool SMEM = false>
@@ -1251,6 +1279,9 @@ template <> struct Raw8<kQ8_0> {
 };
 
 template <> struct Raw8<kQ5_0> {
+    // d (11 significant bits) times an integer in [-16, 15]: at most 16
+    // significant bits, so w - round8(w) is already an exact bf16
+    static constexpr bool kExactLo = true;
     uint2 q;
     uint32_t qh, d;
     template <bool SMEM = false>
@@ -1277,6 +1308,7 @@ template <> struct Raw8<kQ5_0> {
 };
 
 template <> struct Raw8<kQ4_K> {
+    static constexpr bool kExactLo = false;
     uint2 q;
     uint4 hdr;
     template <bool SMEM = false>
@@ -1313,6 +1345,7 @@ template <> struct Raw8<kQ4_K> {
 };
 
 template <> struct Raw8<kQ6_K> {
+    static constexpr bool kExactLo = false;
     uint2 ql, qh;
     uint32_t sc, d;
     template <bool SMEM = false>
@@ -1355,13 +1388,16 @@ __device__ __forceinline__ float round8(float x)
 // |hi - v| <= 2^-8 |v| and |e| <= 2^-16 |v|, as packed words (hi[j], lo[j]
 // hold elements 2j and 2j + 1, the even one in the low half).  FMA-pipe
 // arithmetic and byte permutes only.  |v| must stay below 2^111 (65537 v
-// finite).
+// finite).  EXACT_LO: every v has at most 16 significant bits, so v - hi is
+// an exact bf16 (e = 0) and needs no rounding.
+template <bool EXACT_LO = false>
 __device__ __forceinline__ void split_words(const float v[8], uint32_t h[4], uint32_t l[4])
 {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const float h0 = round8(v[2 * j]), h1 = round8(v[2 * j + 1]);
-        const float l0 = round8(__fsub_rn(v[2 * j], h0)), l1 = round8(__fsub_rn(v[2 * j + 1], h1));
+        const float r0 = __fsub_rn(v[2 * j], h0), r1 = __fsub_rn(v[2 * j + 1], h1);
+        const float l0 = EXACT_LO ? r0 : round8(r0), l1 = EXACT_LO ? r1 : round8(r1);
         h[j] = __byte_perm(__float_as_uint(h0), __float_as_uint(h1), 0x7632u);
         l[j] = __byte_perm(__float_as_uint(l0), __float_as_uint(l1), 0x7632u);
     }
@@ -1564,7 +1600,7 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
             for (int j = 0; j < nk; ++j) {
                 const int s = j % S;
                 // buffer s is free once the MMAs of stage j - S are done
-                if (j >= S && !mbar_wait(ebar0 + 8u * s, (uint32_t)((j / S - 1) & 1))) {
+                if (j >= S && !mbar_wait_idle(ebar0 + 8u * s, (uint32_t)((j / S - 1) & 1))) {
                     ok = false;
                     break;
                 }
@@ -1579,7 +1615,7 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
             for (int kc = 0; kc < nk; ++kc) {
                 const int s = kc % S;
                 const uint32_t par = (uint32_t)((kc / S) & 1);
-                if (!mbar_wait(wbar0 + 8u * s, par) || !mbar_wait(xbar0 + 8u * s, par)) {
+                if (!mbar_wait_idle(wbar0 + 8u * s, par) || !mbar_wait_idle(xbar0 + 8u * s, par)) {
                     ok = false;
                     break;
                 }
@@ -1613,9 +1649,9 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
         if (WSMEM && !mbar_wait(tbar, 0u)) ok = false;
         Raw8<FMT> wr;
         if (!WSMEM && have_row && wk < L.cols) wr.load(wrow, L, wk);
-        int pending = -1;  // stage whose tensor-memory stores are not yet published
-        for (int kc = 0; kc < nk; ++kc) {
-            const int s = kc % S;
+        int pending = -1;  // buffer whose tensor-memory stores are not yet published
+        int s = 0, round = 0;  // buffer and ring round of stage kc
+        for (int kc = 0; kc < nk; ++kc, s = (s + 1 == S ? 0 : s + 1), round += (s == 0)) {
             const int k0 = kc * kTcK + wk;
             Raw8<FMT> wn;
             if (WSMEM) {
@@ -1632,15 +1668,15 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
                 for (int e = 0; e < 8; ++e) v[e] = 0.f;
             }
             uint32_t h[4], l[4];
-            split_words(v, h, l);
+            split_words<Raw8<FMT>::kExactLo>(v, h, l);
             if (pending >= 0) {
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(wbar0 + 8u * (pending % S));
+                if (lane == 0) mbar_arrive(wbar0 + 8u * pending);
             }
             // the MMAs that last read stage buffer s (stage kc - S) are done
-            if (kc >= S && !mbar_wait(ebar0 + 8u * s, (uint32_t)((kc / S - 1) & 1))) ok = false;
+            if (round > 0 && !mbar_wait_idle(ebar0 + 8u * s, (uint32_t)((round - 1) & 1))) ok = false;
             if (!__all_sync(kFull, ok)) {
                 ok = false;
                 pending = -1;
@@ -1649,21 +1685,21 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
             tc_fence_after();
             tmem_st4(lane_addr + 32u * s, h[0], h[1], h[2], h[3]);
             tmem_st4(lane_addr + 32u * s + 16u, l[0], l[1], l[2], l[3]);
-            pending = kc;
+            pending = s;
             if (!WSMEM) wr = wn;
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         if (pending >= 0) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(wbar0 + 8u * (pending % S));
+            if (lane == 0) mbar_arrive(wbar0 + 8u * pending);
         }
     }
 
     // every MMA has completed once the last stage's commit has arrived
     if (ok && (warp < kDecodeWarps || lane == 0)) {
         const int last = nk - 1;
-        if (!mbar_wait(ebar0 + 8u * (last % S), (uint32_t)((last / S) & 1))) ok = false;
+        if (!mbar_wait_idle(ebar0 + 8u * (last % S), (uint32_t)((last / S) & 1))) ok = false;
     }
     const bool failed = __syncthreads_or(!ok);
     if (failed && warp == kCopyWarp && lane == 0) {
