@@ -892,20 +892,27 @@ struct TmaPlan {
     int consumer_warps;    // CW
     int rows_per_warp;     // R
     int np;                // positions (1: GEMV; up to the kernel's NP: batched)
+    int split;             // warps per row (2: long rows, see gemv_tma_kernel)
 };
 
 // NP > 1: the batched form for up to NP positions (x holds P.np rows of
 // cols floats, y P.np rows of L.rows); each staged weight chunk is unpacked
 // once per row and applied to every position.  No argmax or exchange there.
-template <uint32_t FMT, int CW, int R, int NP = 1>
+// SPLIT = 2 (long rows, where only a few rows fit a stage): two warps share
+// each row, taking alternate 32-chunk blocks; the second warp's sum reaches
+// the first through shared memory, handed over with a pair of mbarriers per
+// stage parity (bounded waits, like every other wait here).
+template <uint32_t FMT, int CW, int R, int NP = 1, int SPLIT = 1>
 __global__ void __launch_bounds__((CW + 1) * 32, 1)
 gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x,
                 float *__restrict__ y, ArgmaxOut am, int want_argmax, TmaPlan P, Exchange ex)
 {
     static_assert(R * NP <= 32, "one lane per (row, position) output");
+    static_assert(SPLIT == 1 || (SPLIT == 2 && R == 1 && NP == 1 && CW % 2 == 0), "split rows: one row per warp pair");
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) unsigned long long bars[2 * 8];
+    __shared__ __align__(8) unsigned long long bars[2 * 8 + 4];  // full[8] | empty[8] | pfull[2] | pfree[2]
     __shared__ unsigned long long kscratch[kMaxConsumerWarps + 1];
+    __shared__ float partial[2][kMaxConsumerWarps];
     constexpr int kConsumerWarps = CW;
     constexpr int NSL = W<FMT>::kSlices;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -914,6 +921,7 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
     const uint32_t stage0 = (uint32_t)__cvta_generic_to_shared(smem + P.x_bytes);
     const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(&bars[0]);
     const uint32_t empty0 = full0 + 8u * 8u;
+    const uint32_t pbar0 = full0 + 16u * 8u;
 
     const int r0 = (int)((long long)L.rows * blockIdx.x / gridDim.x);
     const int r1 = (int)((long long)L.rows * (blockIdx.x + 1) / gridDim.x);
@@ -930,6 +938,7 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
             mbar_init(full0 + 8u * i, 1u);
             mbar_init(empty0 + 8u * i, (uint32_t)kConsumerWarps);
         }
+        for (int i = 0; i < 4; ++i) mbar_init(pbar0 + 8u * i, (uint32_t)(kConsumerWarps / 2));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -980,7 +989,8 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
         quantize_x<FMT, CW * 32>(x, L.cols, C, smem, NP == 1 ? 1 : P.np, xb);
         asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
         const XS s = xs_view(smem, L.cols);
-        const int NI = (C + 31) >> 5;
+        const int NI = (C + 32 * SPLIT - 1) / (32 * SPLIT);
+        const int rw = warp % (CW / SPLIT), half = warp / (CW / SPLIT);  // row slot, chunk half
         for (int k = 0; k < n_stages; ++k) {
             const int sidx = k % NS;
             if (!mbar_wait(full0 + 8u * sidx, (uint32_t)((k / NS) & 1))) {
@@ -996,10 +1006,10 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
 #pragma unroll
                 for (int p = 0; p < NP; ++p) acc[i][p] = 0.f;
             }
-            const int lr0 = warp * R;
+            const int lr0 = rw * R;
             if (lr0 < rows_k) {
                 for (int it = 0; it < NI; ++it) {
-                    const int c = it * 32 + lane;
+                    const int c = (it * SPLIT + half) * 32 + lane;
                     if (c < C) {
                         // All R rows are loaded without a row guard: the stage
                         // buffer holds CW * R rows, so rows past rows_k read
@@ -1038,6 +1048,28 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
                     for (int o = 16; o > 0; o >>= 1) acc[i][p] += __shfl_xor_sync(kFull, acc[i][p], o);
                 }
             }
+            if constexpr (SPLIT == 2) {
+                // buffer pb of the partial sums carries stages k = pb (mod 2)
+                const int pb = k & 1;
+                const uint32_t pfull = pbar0 + 8u * pb, pfree = pbar0 + 8u * (2 + pb);
+                bool okp = true;
+                if (half == 1) {
+                    // free once the partners have read stage k - 2
+                    if (k >= 2) okp = mbar_wait(pfree, (uint32_t)(((k >> 1) - 1) & 1));
+                    if (okp && lane == 0) partial[pb][rw] = acc[0][0];
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(pfull);
+                } else {
+                    okp = mbar_wait(pfull, (uint32_t)((k >> 1) & 1));
+                    if (okp) acc[0][0] += partial[pb][rw];
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(pfree);
+                }
+                if (!__all_sync(kFull, okp)) {
+                    if (lane == 0) atomicOr(&g_status, kStatusConsumerTimeout);
+                    break;
+                }
+            }
             // lane j writes row lr0 + j / NP, position j % NP
             float out = 0.f;
 #pragma unroll
@@ -1047,7 +1079,7 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
                     if (lane == i * NP + p) out = acc[i][p];
             }
             const int oi = lane / NP, op = lane % NP;
-            if (lane < R * NP && lr0 + oi < rows_k && op < P.np) {
+            if (half == 0 && lane < R * NP && lr0 + oi < rows_k && op < P.np) {
                 const int row = base_row + lr0 + oi;
                 y[(size_t)op * L.rows + row] = out;
                 if (NP == 1 && want_argmax) best = max_ull(best, make_key(out, am.index_base + row));
@@ -2067,35 +2099,38 @@ int g_gemv_path = 0;  // 0 auto, 1 direct loads, 2 TMA pipeline
 bool tma_plan(const Layout &L, TmaPlan *P, int np = 1, bool batched = false)
 {
     constexpr uint32_t kBudget = 227u * 1024u - 1024u;  // dynamic bytes, leaving static room
-    static const int kCandidates[][3] = {{16, 2, 2}, {8, 2, 3}, {16, 1, 3}, {8, 2, 2}, {16, 1, 2}, {8, 1, 2}};
+    // {consumer warps, rows per warp, minimum stages, warps per row}
+    static const int kCandidates[][4] = {{16, 2, 2, 1}, {8, 2, 3, 1}, {16, 1, 3, 1}, {8, 2, 2, 1},
+                                         {16, 1, 2, 1}, {16, 1, 2, 2}, {8, 1, 2, 1}};
     // batched form: 8 consumer warps (its per-thread state is larger)
-    static const int kBatchCandidates[][3] = {{8, 2, 2}, {8, 1, 2}};
+    static const int kBatchCandidates[][4] = {{8, 2, 2, 1}, {8, 1, 2, 1}};
     const uint32_t xb = (uint32_t)((xs_bytes(L.cols) * (size_t)np + 127) & ~(size_t)127);
     if (xb >= kBudget) return false;
-    const int n_cand = batched ? 2 : 6;
+    const int n_cand = batched ? 2 : 7;
     for (int ci = 0; ci < n_cand; ++ci) {
         const int *cand = batched ? kBatchCandidates[ci] : kCandidates[ci];
-        const int cw = cand[0], r = cand[1], min_stages = cand[2];
-        const uint64_t sb = ((uint64_t)cw * r * L.row_stride + 127) & ~127ull;
+        const int cw = cand[0], r = cand[1], min_stages = cand[2], split = cand[3];
+        const uint64_t sb = ((uint64_t)cw * r / split * L.row_stride + 127) & ~127ull;
         const uint64_t ns = (kBudget - xb) / sb;
         if ((int)ns < min_stages) continue;
         P->x_bytes = xb;
         P->stage_bytes = (uint32_t)sb;
-        P->rows_per_stage = cw * r;
+        P->rows_per_stage = cw * r / split;
         P->stages = (int)(ns > 8 ? 8 : ns);
         P->consumer_warps = cw;
         P->rows_per_warp = r;
         P->np = np;
+        P->split = split;
         return true;
     }
     return false;
 }
 
-template <uint32_t FMT, int CW, int R, int NP = 1>
+template <uint32_t FMT, int CW, int R, int NP = 1, int SPLIT = 1>
 cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, const float *x, float *y,
                         const ArgmaxOut *am, cudaStream_t s, const Exchange &ex = Exchange{})
 {
-    auto kernel = gemv_tma_kernel<FMT, CW, R, NP>;
+    auto kernel = gemv_tma_kernel<FMT, CW, R, NP, SPLIT>;
     const size_t smem = (size_t)P.x_bytes + (size_t)P.stages * P.stage_bytes;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -2127,6 +2162,7 @@ cudaError_t gemv_exchange_fmt(const Layout &L, const uint8_t *w, const float *x,
 {
     TmaPlan P;
     if (!tma_plan(L, &P)) return cudaErrorNotSupported;
+    if (P.split == 2) return gemv_tma_go<FMT, 16, 1, 1, 2>(L, P, w, x, y, &am, s, ex);
     if (P.consumer_warps == 16) {
         if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 16, 2>(L, P, w, x, y, &am, s, ex);
         return gemv_tma_go<FMT, 16, 1>(L, P, w, x, y, &am, s, ex);
@@ -2141,6 +2177,7 @@ cudaError_t gemv_fmt(const Layout &L, const uint8_t *w, const float *x, float *y
 {
     TmaPlan P;
     if (g_gemv_path != 1 && tma_plan(L, &P)) {
+        if (P.split == 2) return gemv_tma_go<FMT, 16, 1, 1, 2>(L, P, w, x, y, am, s);
         if (P.consumer_warps == 16) {
             if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 16, 2>(L, P, w, x, y, am, s);
             return gemv_tma_go<FMT, 16, 1>(L, P, w, x, y, am, s);
