@@ -1264,13 +1264,32 @@ __device__ __forceinline__ float u8_magic(uint32_t w)
     return __uint_as_float(__byte_perm(w, 0x4b000000u, 0x7540u | I));
 }
 
+// Packed two-wide fp32 arithmetic (one instruction for both lanes of a
+// float2, each rounded exactly as the scalar operation).
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+
 // v[4 j + i] = (2^23 + byte i of n[j]) - bias, exact for bias = 2^23 + offset
 __device__ __forceinline__ void bytes_to_float(uint32_t n0, uint32_t n1, float bias, float v[8])
 {
-    v[0] = u8_magic<0>(n0) - bias; v[1] = u8_magic<1>(n0) - bias;
-    v[2] = u8_magic<2>(n0) - bias; v[3] = u8_magic<3>(n0) - bias;
-    v[4] = u8_magic<0>(n1) - bias; v[5] = u8_magic<1>(n1) - bias;
-    v[6] = u8_magic<2>(n1) - bias; v[7] = u8_magic<3>(n1) - bias;
+    const float2 nb = f2(-bias, -bias);
+    const float2 a = __fadd2_rn(f2(u8_magic<0>(n0), u8_magic<1>(n0)), nb);
+    const float2 b = __fadd2_rn(f2(u8_magic<2>(n0), u8_magic<3>(n0)), nb);
+    const float2 c = __fadd2_rn(f2(u8_magic<0>(n1), u8_magic<1>(n1)), nb);
+    const float2 d = __fadd2_rn(f2(u8_magic<2>(n1), u8_magic<3>(n1)), nb);
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
+
+// v[i] *= s, rounded once per element
+__device__ __forceinline__ void scale8(float s, float v[8])
+{
+    const float2 s2 = f2(s, s);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float2 r = __fmul2_rn(f2(v[2 * j], v[2 * j + 1]), s2);
+        v[2 * j] = r.x;
+        v[2 * j + 1] = r.y;
+    }
 }
 
 // Raw bytes of 8 consecutive weights (k0 .. k0 + 7, k0 a multiple of 8) of
@@ -1303,9 +1322,7 @@ template <> struct Raw8<kQ8_0> {
     {
         // signed bytes biased by 128 so that they read as unsigned
         bytes_to_float(q.x ^ 0x80808080u, q.y ^ 0x80808080u, 8388736.0f, v);
-        const float s = f16_fast(d);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(s, v[i]);
+        scale8(f16_fast(d), v);
         return (d & 0x7c00u) != 0x7c00u;
     }
 };
@@ -1332,9 +1349,7 @@ template <> struct Raw8<kQ5_0> {
         const uint32_t n0 = ((q.x >> sh) & 0x0f0f0f0fu) | spread4(qh);
         const uint32_t n1 = ((q.y >> sh) & 0x0f0f0f0fu) | spread4(qh >> 4);
         bytes_to_float(n0, n1, 8388624.0f, v);
-        const float s = f16_fast(d);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(s, v[i]);
+        scale8(f16_fast(d), v);
         return (d & 0x7c00u) != 0x7c00u;
     }
 };
@@ -1370,8 +1385,13 @@ template <> struct Raw8<kQ4_K> {
         bytes_to_float((q.x >> sh) & 0x0f0f0f0fu, (q.y >> sh) & 0x0f0f0f0fu, 8388608.0f, v);
         // scale * q is exact, so one fused rounding equals the reference's
         // multiply-then-subtract
+        const float2 sc2 = f2(scale, scale), mn2 = f2(-minimum, -minimum);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __fmaf_rn(scale, v[i], -minimum);
+        for (int j = 0; j < 4; ++j) {
+            const float2 r = __ffma2_rn(f2(v[2 * j], v[2 * j + 1]), sc2, mn2);
+            v[2 * j] = r.x;
+            v[2 * j + 1] = r.y;
+        }
         return (hdr.x & 0x7c00u) != 0x7c00u && (hdr.x & 0x7c000000u) != 0x7c000000u;
     }
 };
@@ -1401,19 +1421,19 @@ template <> struct Raw8<kQ6_K> {
         const uint32_t n0 = ((ql.x >> shl) & 0x0f0f0f0fu) | (((qh.x >> shh) & 0x03030303u) << 4);
         const uint32_t n1 = ((ql.y >> shl) & 0x0f0f0f0fu) | (((qh.y >> shh) & 0x03030303u) << 4);
         bytes_to_float(n0, n1, 8388640.0f, v);  // n - 32
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(ds, v[i]);
+        scale8(ds, v);
         return (d & 0x7c00u) != 0x7c00u;
     }
 };
 
-// x rounded to 8 significant bits (nearest), as an fp32 whose low 16 bits
+// x rounded to 8 significant bits (nearest), as fp32s whose low 16 bits
 // are zero, i.e. an exact bf16: Veltkamp's splitting with 2^16 + 1.  The
 // explicitly rounded operations keep the compiler from contracting them.
-__device__ __forceinline__ float round8(float x)
+__device__ __forceinline__ float2 round8x2(float2 x)
 {
-    const float t = __fmul_rn(x, 65537.0f);
-    return __fsub_rn(t, __fsub_rn(t, x));
+    const float2 m1 = f2(-1.f, -1.f);
+    const float2 t = __fmul2_rn(x, f2(65537.0f, 65537.0f));
+    return __ffma2_rn(__ffma2_rn(x, m1, t), m1, t);  // t - (t - x)
 }
 
 // Split 8 floats into bf16 high and low parts, v = hi + lo + e with
@@ -1427,11 +1447,12 @@ __device__ __forceinline__ void split_words(const float v[8], uint32_t h[4], uin
 {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const float h0 = round8(v[2 * j]), h1 = round8(v[2 * j + 1]);
-        const float r0 = __fsub_rn(v[2 * j], h0), r1 = __fsub_rn(v[2 * j + 1], h1);
-        const float l0 = EXACT_LO ? r0 : round8(r0), l1 = EXACT_LO ? r1 : round8(r1);
-        h[j] = __byte_perm(__float_as_uint(h0), __float_as_uint(h1), 0x7632u);
-        l[j] = __byte_perm(__float_as_uint(l0), __float_as_uint(l1), 0x7632u);
+        const float2 x = f2(v[2 * j], v[2 * j + 1]);
+        const float2 hi = round8x2(x);
+        float2 lo = __ffma2_rn(hi, f2(-1.f, -1.f), x);  // x - hi, exact
+        if (!EXACT_LO) lo = round8x2(lo);
+        h[j] = __byte_perm(__float_as_uint(hi.x), __float_as_uint(hi.y), 0x7632u);
+        l[j] = __byte_perm(__float_as_uint(lo.x), __float_as_uint(lo.y), 0x7632u);
     }
 }
 
