@@ -1235,15 +1235,16 @@ matmul_kernel(Layout L, const uint8_t *__restrict__ w, const uint8_t *__restrict
 // turn Inf * 0 into NaN.
 
 constexpr int kTcM = 128;         // rows per tile = accumulator lanes
-constexpr int kTcK = 32;          // K per stage
+constexpr int kTcK = 64;          // K per stage
 constexpr int kTcThreads = 512;   // weight-decode threads (16 warps)
-constexpr uint32_t kTcSmemBudget = 200u * 1024u;
-constexpr int kTcMaxStages = 8;   // A ring: 8 stages x 32 columns after the 256 accumulator columns
-constexpr uint32_t kTcACol = 256u;
+constexpr uint32_t kTcSmemBudget = 220u * 1024u;
+constexpr uint32_t kTcACol = 256u;  // weight ring after the 256 accumulator columns
+constexpr int kTcMaxStages = (512 - (int)kTcACol) / kTcK;  // a stage: wh | wl, kTcK / 2 columns each
+constexpr int kTcUnits = kTcK / 32;  // 8-weight units per decode thread and stage
 constexpr unsigned int kStatusMmaTimeout = 16u;
 
-// Shared memory of one stage: xh | xl (TN x 32 bf16 each).  The weights of a
-// stage (wh | wl, 16 columns each) live in tensor memory.
+// Shared memory of one stage: xh | xl (TN x kTcK bf16 each).  The weights of
+// a stage (wh | wl, kTcK / 2 columns each) live in tensor memory.
 __host__ __device__ constexpr uint32_t tc_plane_x(int tn) { return (uint32_t)tn * kTcK * 2u; }
 __host__ __device__ constexpr uint32_t tc_stage_bytes(int tn) { return 2u * tc_plane_x(tn); }
 
@@ -1509,6 +1510,14 @@ __device__ __forceinline__ void tmem_st4(uint32_t taddr, uint32_t a, uint32_t b,
                  : "memory");
 }
 
+// 8 consecutive 32-bit columns of this thread's lane.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t r[8])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+
 __device__ __forceinline__ void umma_commit(uint32_t bar)
 {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -1568,8 +1577,9 @@ split_x_kernel(const float *__restrict__ X, int np, int cols, int nk, uint8_t *_
         const int u = (int)(id % kUnits);
         const long long img = id / kUnits;  // pt * nk + kc
         const int kc = (int)(img % nk), pt = (int)(img / nk);
-        const int pos = pt * TN + (u >> 5) * 8 + (u & 7);
-        const int k0 = kc * kTcK + ((u >> 3) & 3) * 8;
+        constexpr int KG = kTcK / 8;  // 8-wide K groups per stage
+        const int pos = pt * TN + (u / (8 * KG)) * 8 + (u & 7);
+        const int k0 = kc * kTcK + ((u >> 3) % KG) * 8;
         float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         if (pos < np && k0 < cols) {
             const float4 a = __ldg((const float4 *)(X + (size_t)pos * cols + k0));
@@ -1591,8 +1601,8 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
                  const uint8_t *__restrict__ xs, int np, float *__restrict__ Y, int S)
 {
     static_assert(TN % 16 == 0 && TN >= 32 && TN <= 256, "N of one MMA: a multiple of 16 in 32..256");
-    static_assert(kTcM * (kTcK / 8) == kTcThreads, "one weight unit per decode thread and stage");
-    static_assert(kTcACol + 32u * kTcMaxStages <= 512u, "A ring must fit tensor memory");
+    static_assert(kTcM * (kTcK / 8) == kTcThreads * kTcUnits, "kTcUnits weight units per decode thread and stage");
+    static_assert(kTcACol + (uint32_t)kTcK * kTcMaxStages <= 512u, "A ring must fit tensor memory");
     // warps 0..15 decode weights, warp 16 issues MMAs, warp 17 copies x
     constexpr int kDecodeWarps = kTcThreads / 32, kMmaWarp = kDecodeWarps, kCopyWarp = kDecodeWarps + 1;
     constexpr uint32_t kPlaneX = tc_plane_x(TN);
@@ -1673,7 +1683,7 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a_h = tmem + kTcACol + 32u * s, a_l = a_h + 16u;
+                const uint32_t a_h = tmem + kTcACol + (uint32_t)kTcK * s, a_l = a_h + kTcK / 2;
                 const uint32_t b_h = smem0 + (uint32_t)s * kStage, b_l = b_h + kPlaneX;
 #pragma unroll
                 for (int j = 0; j < kTcK / 16; ++j) {
@@ -1688,40 +1698,47 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
     } else {
         // ------------------------------------------------ weight decode
         // Warp w owns tensor-memory lanes 32 (w % 4) .. + 31 (tile rows) and
-        // K group w / 4 of every stage: 8 K values = 4 columns per plane.
-        // A stage's stores are published (wait::st, then the arrival) only
-        // after the next stage has been decoded, so their latency overlaps
-        // that work.
-        const int q = warp & 3, kg = warp >> 2;
+        // K range w / 4 of every stage: kTcUnits 8-weight units, 4 columns
+        // each per plane.  A stage's stores are published (wait::st, then the
+        // arrival) only after the next stage has been decoded, so their
+        // latency overlaps that work.
+        const int q = warp & 3, kp = warp >> 2;
         const int wrow_i = r0 + 32 * q + lane;
         const bool have_row = wrow_i < L.rows;
         const uint8_t *wrow = WSMEM ? wtile + (size_t)(32 * q + lane) * L.row_stride
                                     : w + (uint64_t)(have_row ? wrow_i : 0) * L.row_stride;
-        const int wk = kg * 8;
-        const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16) + kTcACol + 4u * kg;
+        const int wk = kp * 8 * kTcUnits;
+        const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16) + kTcACol + 4u * kTcUnits * kp;
         if (WSMEM && !mbar_wait(tbar, 0u)) ok = false;
-        Raw8<FMT> wr;
-        if (!WSMEM && have_row && wk < L.cols) wr.load(wrow, L, wk);
+        Raw8<FMT> wr[kTcUnits];
+        if (!WSMEM) {
+#pragma unroll
+            for (int u = 0; u < kTcUnits; ++u)
+                if (have_row && wk + 8 * u < L.cols) wr[u].load(wrow, L, wk + 8 * u);
+        }
         int pending = -1;  // buffer whose tensor-memory stores are not yet published
         int s = 0, round = 0;  // buffer and ring round of stage kc
         for (int kc = 0; kc < nk; ++kc, s = (s + 1 == S ? 0 : s + 1), round += (s == 0)) {
             const int k0 = kc * kTcK + wk;
-            Raw8<FMT> wn;
-            if (WSMEM) {
-                if (have_row && k0 < L.cols) wr.template load<true>(wrow, L, k0);
-            } else {
-                const int kn = k0 + kTcK;
-                if (have_row && kn < L.cols) wn.load(wrow, L, kn);
-            }
-            float v[8];
-            if (have_row && k0 < L.cols) {
-                wr.decode(k0, v);
-            } else {
+            Raw8<FMT> wn[kTcUnits];
+            uint32_t h[4 * kTcUnits], l[4 * kTcUnits];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) v[e] = 0.f;
+            for (int u = 0; u < kTcUnits; ++u) {
+                const int ku = k0 + 8 * u;
+                if (WSMEM) {
+                    if (have_row && ku < L.cols) wr[u].template load<true>(wrow, L, ku);
+                } else {
+                    if (have_row && ku + kTcK < L.cols) wn[u].load(wrow, L, ku + kTcK);
+                }
+                float v[8];
+                if (have_row && ku < L.cols) {
+                    wr[u].decode(ku, v);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[e] = 0.f;
+                }
+                split_words<Raw8<FMT>::kExactLo>(v, h + 4 * u, l + 4 * u);
             }
-            uint32_t h[4], l[4];
-            split_words<Raw8<FMT>::kExactLo>(v, h, l);
             if (pending >= 0) {
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 tc_fence_before();
@@ -1736,10 +1753,14 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
                 break;
             }
             tc_fence_after();
-            tmem_st4(lane_addr + 32u * s, h[0], h[1], h[2], h[3]);
-            tmem_st4(lane_addr + 32u * s + 16u, l[0], l[1], l[2], l[3]);
+            static_assert(kTcUnits == 2, "stores are written for two units per thread");
+            tmem_st8(lane_addr + (uint32_t)kTcK * s, h);
+            tmem_st8(lane_addr + (uint32_t)kTcK * s + kTcK / 2, l);
             pending = s;
-            if (!WSMEM) wr = wn;
+            if (!WSMEM) {
+#pragma unroll
+                for (int u = 0; u < kTcUnits; ++u) wr[u] = wn[u];
+            }
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         if (pending >= 0) {
@@ -2303,9 +2324,9 @@ template <uint32_t FMT, int TN>
 cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
                          cudaStream_t s)
 {
-    // weight tile in shared memory when it leaves room for at least 4 x stages
+    // weight tile in shared memory when it leaves room for at least 3 x stages
     const uint32_t tile_max = (uint32_t)kTcM * (uint32_t)L.row_stride;
-    const bool wsmem = (uint64_t)kTcM * L.row_stride + 4u * tc_stage_bytes(TN) <= kTcSmemBudget;
+    const bool wsmem = (uint64_t)kTcM * L.row_stride + 3u * tc_stage_bytes(TN) <= kTcSmemBudget;
     int S = wsmem ? (int)((kTcSmemBudget - tile_max) / tc_stage_bytes(TN)) : tc_stages(TN);
     if (S > kTcMaxStages) S = kTcMaxStages;
     auto kernel = wsmem ? matmul_tc_kernel<FMT, TN, true> : matmul_tc_kernel<FMT, TN, false>;
@@ -2342,7 +2363,7 @@ cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const float *X, int 
 
 // Position-tile width of the tensor-core kernel: the candidate with the
 // smallest (waves of one-CTA-per-SM tiles) x (per-stage cost), where a
-// 32-wide K stage costs max(decode of 128 x 32 weights, 6 MMAs of
+// 64-wide K stage costs max(decode of 128 x 64 weights, 12 MMAs of
 // 128 x TN x 16), in SM cycles.
 int tc_tile_width(int rows, int batch)
 {
@@ -2353,7 +2374,7 @@ int tc_tile_width(int rows, int batch)
     for (int tn : cand) {
         const long long tiles = row_tiles * ((batch + tn - 1) / tn);
         const long long waves = (tiles + sm_count() - 1) / sm_count();
-        const double alu = 450.0, mma = 4.2 * tn;
+        const double alu = 900.0, mma = 8.4 * tn;
         const double cost = (double)waves * (alu > mma ? alu : mma);
         if (cost < best_cost) {
             best_cost = cost;
