@@ -1753,9 +1753,12 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
                 break;
             }
             tc_fence_after();
-            static_assert(kTcUnits == 2, "stores are written for two units per thread");
-            tmem_st8(lane_addr + (uint32_t)kTcK * s, h);
-            tmem_st8(lane_addr + (uint32_t)kTcK * s + kTcK / 2, l);
+            static_assert(kTcUnits % 2 == 0, "stores go 8 columns (two units) at a time");
+#pragma unroll
+            for (int g = 0; g < kTcUnits / 2; ++g) {
+                tmem_st8(lane_addr + (uint32_t)kTcK * s + 8u * g, h + 8 * g);
+                tmem_st8(lane_addr + (uint32_t)kTcK * s + kTcK / 2 + 8u * g, l + 8 * g);
+            }
             pending = s;
             if (!WSMEM) {
 #pragma unroll
