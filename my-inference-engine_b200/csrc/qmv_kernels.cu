@@ -1570,6 +1570,9 @@ split_x_kernel(const float *__restrict__ X, int np, int cols, int nk, uint8_t *_
 {
     constexpr uint32_t kPlaneX = tc_plane_x(TN);
     constexpr int kUnits = TN * (kTcK / 8);
+    // the matmul launched after this kernel may start its weight work now;
+    // it reads these images only after its griddepcontrol.wait
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int n_pt = (np + TN - 1) / TN;
     const long long total = (long long)n_pt * nk * kUnits;
     for (long long id = blockIdx.x * (long long)blockDim.x + threadIdx.x; id < total;
@@ -1660,6 +1663,9 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
                     bulk_g2s(dst + off, src + off, min(32768u, tile_bytes - off), tbar);
             }
             const uint8_t *ximg = xs + (size_t)pt * nk * (size_t)kStage;
+            // the x images come from split_x_kernel, the launch this one
+            // depends on (programmatic dependent launch)
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int j = 0; j < nk; ++j) {
                 const int s = j % S;
                 // buffer s is free once the MMAs of stage j - S are done
@@ -2357,8 +2363,17 @@ cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const float *X, int 
         // tensor memory): a second CTA's allocation would wait for the first
         size_t smem = (size_t)S * tc_stage_bytes(TN) + (wsmem ? tile_max : 0u);
         if (smem < 120u * 1024u) smem = 120u * 1024u;
-        kernel<<<grid, kTcThreads + 64, smem, s>>>(L, w, X, (const uint8_t *)xs, batch, Y, S);
-        e = cudaGetLastError();
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kTcThreads + 64);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, kernel, L, w, X, (const uint8_t *)xs, batch, Y, S);
     }
     const cudaError_t f = cudaFreeAsync(xs, s);
     return e != cudaSuccess ? e : f;
