@@ -152,3 +152,84 @@ def algorithmic_bytes(gtype: int, rows: int, cols: int, batch: int = 1) -> int:
     """Packed weight bytes + f32 input bytes + f32 output bytes for one call."""
     w = rows * (cols // BLOCK_ELEMENTS[gtype]) * BLOCK_BYTES[gtype]
     return w + 4 * cols * batch + 4 * rows * batch
+
+
+# --------------------------------------------------------------- Qwen2 decode
+#
+# Configuration 4: a Qwen2-0.5B-architecture model with random-init weights.
+# Projection formats: attn_q/k/v/output and ffn_gate Q8_0, ffn_up and
+# ffn_down Q5_0, token_embd Q8_0, output Q6_K (the same generators and
+# distributions as above, one stream per tensor).  F32 tensors: RMSNorm
+# weights 1 + N(0, 0.1), Q/K/V biases N(0, 0.02).  The KV cache is pre-filled
+# with N(0, 1) keys and values.
+
+QWEN2_CONFIGS = {
+    # dim, hidden, layers, heads, kv_heads, vocab, eps, rope_base
+    "cfg4_qwen2_0_5b": dict(dim=896, hidden=4864, layers=24, heads=14, kv_heads=2, vocab=151936,
+                            eps=1e-6, rope_base=1e6),
+    # small shape of the same architecture for parity tests
+    "qwen2_tiny": dict(dim=256, hidden=512, layers=2, heads=4, kv_heads=2, vocab=1000,
+                       eps=1e-6, rope_base=1e6),
+}
+
+QWEN2_TYPES = dict(q=Q8_0, k=Q8_0, v=Q8_0, o=Q8_0, gate=Q8_0, up=Q5_0, down=Q5_0, embd=Q8_0, out=Q6_K)
+
+
+def make_qwen2(name: str = "cfg4_qwen2_0_5b", seed: int = 0) -> dict:
+    """Synthetic model: config fields plus packed tensors as
+    (ggml_type, rows, cols, blocks) and F32 vectors, in the reference's
+    tensor names (src/qwen2_architecture.cpp)."""
+    c = dict(QWEN2_CONFIGS[name])
+    dim, hidden, kvd = c["dim"], c["hidden"], c["kv_heads"] * (c["dim"] // c["heads"])
+    stream = [100]
+
+    def packed(kind, rows, cols):
+        stream[0] += 1
+        t = QWEN2_TYPES[kind]
+        return (t, rows, cols, make_blocks(t, rows, cols, seed=seed, stream=stream[0]))
+
+    def vec(n, mean, std):
+        stream[0] += 1
+        return (mean + std * normal(seed, 16 * stream[0], n)).astype(np.float32)
+
+    m = dict(c)
+    m["embd"] = packed("embd", c["vocab"], dim)
+    layers = []
+    for _ in range(c["layers"]):
+        layers.append(dict(
+            attn_norm=vec(dim, 1.0, 0.1), q=packed("q", dim, dim), k=packed("k", kvd, dim),
+            v=packed("v", kvd, dim), q_bias=vec(dim, 0.0, 0.02), k_bias=vec(kvd, 0.0, 0.02),
+            v_bias=vec(kvd, 0.0, 0.02), o=packed("o", dim, dim), ffn_norm=vec(dim, 1.0, 0.1),
+            gate=packed("gate", hidden, dim), up=packed("up", hidden, dim), down=packed("down", dim, hidden)))
+    m["layer"] = layers
+    m["out_norm"] = vec(dim, 1.0, 0.1)
+    m["out"] = packed("out", c["vocab"], dim)
+    return m
+
+
+def make_kv_cache(m: dict, positions: int, seed: int = 0):
+    """Pre-filled keys and values, each [layers][positions][kv_dim] float32 N(0, 1)."""
+    kvd = m["kv_heads"] * (m["dim"] // m["heads"])
+    n = m["layers"] * positions * kvd
+    k = normal(seed, 16 * 900, n).astype(np.float32).reshape(m["layers"], positions, kvd)
+    v = normal(seed, 16 * 901, n).astype(np.float32).reshape(m["layers"], positions, kvd)
+    return k, v
+
+
+def qwen2_tensor_list(m: dict):
+    """(name, ggml_type, cols, rows, bytes-array) in the reference's tensor names;
+    rows 0 marks an F32 vector (type 0)."""
+    out = [("token_embd.weight", m["embd"][0], m["embd"][2], m["embd"][1], m["embd"][3])]
+    names = dict(q="attn_q.weight", k="attn_k.weight", v="attn_v.weight", o="attn_output.weight",
+                 gate="ffn_gate.weight", up="ffn_up.weight", down="ffn_down.weight")
+    vecs = dict(attn_norm="attn_norm.weight", ffn_norm="ffn_norm.weight", q_bias="attn_q.bias",
+                k_bias="attn_k.bias", v_bias="attn_v.bias")
+    for li, L in enumerate(m["layer"]):
+        for key, nm in vecs.items():
+            out.append((f"blk.{li}.{nm}", 0, L[key].size, 0, L[key]))
+        for key, nm in names.items():
+            t, rows, cols, blocks = L[key]
+            out.append((f"blk.{li}.{nm}", t, cols, rows, blocks))
+    out.append(("output_norm.weight", 0, m["out_norm"].size, 0, m["out_norm"]))
+    out.append(("output.weight", m["out"][0], m["out"][2], m["out"][1], m["out"][3]))
+    return out

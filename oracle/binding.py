@@ -58,6 +58,8 @@ class Oracle:
         L.or_matmul.argtypes = [ctypes.c_uint32, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P]
         L.or_row_abs_dot.argtypes = [ctypes.c_uint32, _P, ctypes.c_int, ctypes.c_int, _P, _P]
         L.or_argmax.argtypes = [_P, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+        L.or_qwen2_scratch_floats.argtypes = [_P]
+        L.or_qwen2_forward.argtypes = [_P, _P, _P, ctypes.c_int, ctypes.c_int, _P, _P]
         self.lib = L
 
     def f16(self, bits: int) -> float:
@@ -200,3 +202,93 @@ class Reference:
         logits = np.ascontiguousarray(logits, dtype=np.float32)
         ok = self.lib.ref_greedy(logits.ctypes.data, logits.size, ctypes.byref(tok), err, 128)
         return ok, tok.value, err.value.decode()
+
+
+# ------------------------------------------------------------ Qwen2 decode
+
+class OrTensorC(ctypes.Structure):
+    _fields_ = [("type", ctypes.c_uint32), ("data", ctypes.c_void_p)]
+
+
+class OrLayerC(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("attn_norm", "ffn_norm", "q_bias", "k_bias", "v_bias")] + \
+               [(n, OrTensorC) for n in ("q", "k", "v", "o", "gate", "up", "down")]
+
+
+class OrQwen2C(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("dim", "hidden", "layers", "heads", "kv_heads", "vocab", "max_ctx")] + \
+               [("eps", ctypes.c_float), ("rope_base", ctypes.c_float), ("embd", OrTensorC),
+                ("out_norm", ctypes.c_void_p), ("out", OrTensorC), ("layer", ctypes.c_void_p)]
+
+
+def _or_tensor(t):
+    return OrTensorC(t[0], t[3].ctypes.data)
+
+
+def qwen2_oracle_model(m: dict, max_ctx: int):
+    """ctypes model of a workloads.make_qwen2 dict (kept alive by the returned tuple)."""
+    layers = (OrLayerC * m["layers"])()
+    for i, L in enumerate(m["layer"]):
+        for n in ("attn_norm", "ffn_norm", "q_bias", "k_bias", "v_bias"):
+            setattr(layers[i], n, L[n].ctypes.data)
+        for n in ("q", "k", "v", "o", "gate", "up", "down"):
+            setattr(layers[i], n, _or_tensor(L[n]))
+    c = OrQwen2C(m["dim"], m["hidden"], m["layers"], m["heads"], m["kv_heads"], m["vocab"], max_ctx,
+                 m["eps"], m["rope_base"], _or_tensor(m["embd"]), m["out_norm"].ctypes.data,
+                 _or_tensor(m["out"]), ctypes.cast(layers, ctypes.c_void_p))
+    return c, layers
+
+
+def oracle_qwen2_forward(oracle, model_c, keys, values, pos, token):
+    """One decode step of the C restatement; keys/values [layers][max_ctx][kv_dim]
+    float32 (C-contiguous) are updated at position pos.  Returns (ok, logits)."""
+    scratch = np.empty(oracle.lib.or_qwen2_scratch_floats(ctypes.byref(model_c)), dtype=np.float32)
+    logits = np.empty(model_c.vocab, dtype=np.float32)
+    ok = oracle.lib.or_qwen2_forward(ctypes.byref(model_c), keys.ctypes.data, values.ctypes.data, pos, token,
+                                     logits.ctypes.data, scratch.ctypes.data)
+    return bool(ok), logits
+
+
+class RefTensorC(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("type", ctypes.c_uint32), ("cols", ctypes.c_uint64),
+                ("rows", ctypes.c_uint64), ("data", ctypes.c_void_p), ("bytes", ctypes.c_uint64)]
+
+
+class RefQwen2:
+    """The reference engine's own Qwen2 decode step (oracle/_ref) on an
+    in-memory model built from a workloads.make_qwen2 dict."""
+
+    def __init__(self, m: dict, tensors, max_ctx: int, path: str = REF_SCALAR_SO):
+        L = ctypes.CDLL(path)
+        L.ref_qwen2_create.restype = ctypes.c_void_p
+        L.ref_qwen2_create.argtypes = [_P, ctypes.c_float, ctypes.c_float, _P, ctypes.c_int, ctypes.c_int]
+        L.ref_qwen2_set_kv.argtypes = [ctypes.c_void_p, _P, _P, ctypes.c_int]
+        L.ref_qwen2_forward.argtypes = [ctypes.c_void_p, ctypes.c_int, _P]
+        L.ref_qwen2_get_kv.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, _P, _P]
+        L.ref_qwen2_destroy.argtypes = [ctypes.c_void_p]
+        self.lib, self.m = L, m
+        self._keep = [np.ascontiguousarray(t[4]) for t in tensors]
+        arr = (RefTensorC * len(tensors))()
+        for i, (name, t, cols, rows, data) in enumerate(tensors):
+            arr[i] = RefTensorC(name.encode(), t, cols, rows, self._keep[i].ctypes.data, self._keep[i].nbytes)
+        cfg = np.array([m["dim"], m["hidden"], m["layers"], m["heads"], m["kv_heads"], m["vocab"], max_ctx],
+                       dtype=np.int32)
+        self.h = L.ref_qwen2_create(cfg.ctypes.data, m["eps"], m["rope_base"], ctypes.cast(arr, ctypes.c_void_p),
+                                    len(tensors), max_ctx)
+        if not self.h:
+            raise RuntimeError("reference state_init failed")
+
+    def set_kv(self, keys: np.ndarray, values: np.ndarray) -> None:
+        keys = np.ascontiguousarray(keys, dtype=np.float32)
+        values = np.ascontiguousarray(values, dtype=np.float32)
+        assert self.lib.ref_qwen2_set_kv(self.h, keys.ctypes.data, values.ctypes.data, keys.shape[1])
+
+    def forward(self, token: int):
+        logits = np.empty(self.m["vocab"], dtype=np.float32)
+        ok = self.lib.ref_qwen2_forward(self.h, token, logits.ctypes.data)
+        return bool(ok), logits
+
+    def close(self):
+        if self.h:
+            self.lib.ref_qwen2_destroy(self.h)
+            self.h = None

@@ -7,8 +7,8 @@
  * cpu_baseline leg may load it; the product library never links or calls it.
  *
  * Parity pin: every function here is compared bit-for-bit with the reference's
- * own sources compiled from /root/reference by oracle/Makefile (the `_ref`
- * libraries), and with the known-answer blocks of the reference's tests
+ * own sources compiled from the reference checkout by oracle/Makefile (the
+ * `_ref` libraries), and with the known-answer blocks of the reference's tests
  * (tests/q8_0_reference_test.cpp, q5_0_..., q4_k_..., q6_k_...,
  * quantized_matvec_reference_test.cpp, sampler_greedy_test.cpp), see
  * tests/test_oracle.py.
@@ -332,5 +332,170 @@ int or_argmax(const float *logits, int n, int *id)
         if (logits[i] > logits[best]) best = i;
     }
     *id = best;
+    return 1;
+}
+
+/* ------------------------------------------------------------------------
+ * Qwen2 decode step (configuration 4): the reference's
+ * qwen2_forward_token_cached_impl (src/qwen2_architecture.cpp:1195-1531) with
+ * its helpers tensor_rms_norm_f32 (src/tensor.cpp:99-136), tensor_dot_f32
+ * (:25-45), tensor_add_f32 (:5-23), transformer_apply_rope_f32 and
+ * transformer_attention_f32 (src/transformer_ops.cpp:16-153) and
+ * transformer_swiglu_f32 (:155-178), restated in the same operation order.
+ * ---------------------------------------------------------------------- */
+
+/* type 0: F32 rows */
+typedef struct OrTensor {
+    uint32_t type;
+    const uint8_t *data;
+} OrTensor;
+
+typedef struct OrQwen2Layer {
+    const float *attn_norm, *ffn_norm, *q_bias, *k_bias, *v_bias;
+    OrTensor q, k, v, o, gate, up, down;
+} OrQwen2Layer;
+
+typedef struct OrQwen2 {
+    int dim, hidden, layers, heads, kv_heads, vocab, max_ctx;
+    float eps, rope_base;
+    OrTensor embd;
+    const float *out_norm;
+    OrTensor out;
+    const OrQwen2Layer *layer;
+} OrQwen2;
+
+static int or_tensor_matvec(OrTensor t, int rows, int cols, const float *x, float *y)
+{
+    if (t.type == 0) {
+        const float *w = (const float *)t.data;
+        for (int r = 0; r < rows; r++) {
+            float acc = 0.0f;
+            for (int c = 0; c < cols; c++) acc += w[(size_t)r * cols + c] * x[c];
+            y[r] = acc;
+        }
+        return 1;
+    }
+    return or_matvec(t.type, t.data, rows, cols, x, y);
+}
+
+/* tensor_rms_norm_f32: sum of squares in order, sqrtf(mean + eps), then
+ * (x / denom) * weight. */
+static void or_rms_norm(const float *x, const float *w, int n, float eps, float *out)
+{
+    float denom = 0.0f;
+    for (int j = 0; j < n; j++) denom += x[j] * x[j];
+    denom = sqrtf((denom / n) + eps);
+    for (int i = 0; i < n; i++) out[i] = (x[i] / denom) * w[i];
+}
+
+/* rotate_array_helper: pairs (i, i + d/2) of every head. */
+static void or_rope(float *v, int heads, int d, int pos, float base)
+{
+    for (int h = 0; h < heads; h++) {
+        int s = h * d;
+        for (int i = 0; i < d / 2; i++) {
+            float x = v[s + i];
+            float y = v[s + i + d / 2];
+            float angle = (float)pos / powf(base, (2.0f * (float)i / (float)d));
+            float rx = x * cosf(angle) - y * sinf(angle);
+            float ry = x * sinf(angle) + y * cosf(angle);
+            v[s + i] = rx;
+            v[s + i + d / 2] = ry;
+        }
+    }
+}
+
+/* transformer_attention_f32 over tokens [0, T) of one layer's cache. */
+static int or_attention(const float *q, int heads, int kv_heads, int d, const float *keys,
+                        const float *values, int T, float *prob, float *out)
+{
+    for (int h = 0; h < heads; h++) {
+        const float *qh = q + h * d;
+        int kvh = h / (heads / kv_heads);
+        for (int t = 0; t < T; t++) {
+            const float *k = keys + ((size_t)t * kv_heads + kvh) * d;
+            float score = 0.0f;
+            for (int i = 0; i < d; i++) score += qh[i] * k[i];
+            score /= sqrtf((float)d);
+            prob[h * T + t] = score;
+        }
+        float mx = prob[h * T];
+        for (int t = 1; t < T; t++)
+            if (prob[h * T + t] > mx) mx = prob[h * T + t];
+        float sum = 0.0f;
+        for (int t = 0; t < T; t++) {
+            prob[h * T + t] = expf(prob[h * T + t] - mx);
+            sum += prob[h * T + t];
+        }
+        if (!isfinite(sum) || sum <= 0.0f) return 0;
+        for (int t = 0; t < T; t++) prob[h * T + t] /= sum;
+        for (int i = 0; i < d; i++) out[h * d + i] = 0.0f;
+        for (int t = 0; t < T; t++) {
+            float p = prob[h * T + t];
+            const float *v = values + ((size_t)t * kv_heads + kvh) * d;
+            for (int i = 0; i < d; i++) out[h * d + i] += p * v[i];
+        }
+    }
+    return 1;
+}
+
+/* Workspace floats or_qwen2_forward needs. */
+int or_qwen2_scratch_floats(const OrQwen2 *m)
+{
+    int big = m->hidden > m->dim ? m->hidden : m->dim;
+    return 5 * m->dim + 2 * m->kv_heads * (m->dim / m->heads) + m->heads * m->max_ctx + 3 * big;
+}
+
+/* One decode step at position pos for token: keys/values are the caller's
+ * cache [layers][max_ctx][kv_heads * head_dim] (positions < pos filled; the
+ * step writes position pos), logits[vocab] out.  0 on a non-finite softmax
+ * sum or logit, as the reference fails. */
+int or_qwen2_forward(const OrQwen2 *m, float *keys, float *values, int pos, int token,
+                     float *logits, float *scratch)
+{
+    const int dim = m->dim, hd = dim / m->heads, kvd = m->kv_heads * hd;
+    const int big = m->hidden > dim ? m->hidden : dim;
+    float *h = scratch, *xn = h + dim, *q = xn + dim, *att = q + dim, *tmp = att + dim;
+    float *k = tmp + dim, *v = k + kvd, *prob = v + kvd;
+    float *gate = prob + m->heads * m->max_ctx, *up = gate + big, *mv = up + big;
+    if (pos < 0 || pos >= m->max_ctx || token < 0 || token >= m->vocab) return 0;
+
+    /* embedding row (qwen2_lookup_embedding, :477-528) */
+    if (m->embd.type == 0) {
+        memcpy(h, (const float *)m->embd.data + (size_t)token * dim, (size_t)dim * sizeof(float));
+    } else {
+        int be = or_block_elements(m->embd.type), bb = or_block_bytes(m->embd.type);
+        int nb = dim / be;
+        or_dequant_blocks(m->embd.type, m->embd.data + (size_t)token * nb * bb, (uint64_t)nb, h);
+    }
+    for (int l = 0; l < m->layers; l++) {
+        const OrQwen2Layer *L = &m->layer[l];
+        float *kc = keys + (size_t)l * m->max_ctx * kvd, *vc = values + (size_t)l * m->max_ctx * kvd;
+        or_rms_norm(h, L->attn_norm, dim, m->eps, xn);
+        /* qwen2_layer_project: matvec, then output + bias */
+        or_tensor_matvec(L->q, dim, dim, xn, q);
+        for (int i = 0; i < dim; i++) q[i] = q[i] + L->q_bias[i];
+        or_tensor_matvec(L->k, kvd, dim, xn, k);
+        for (int i = 0; i < kvd; i++) k[i] = k[i] + L->k_bias[i];
+        or_tensor_matvec(L->v, kvd, dim, xn, v);
+        for (int i = 0; i < kvd; i++) v[i] = v[i] + L->v_bias[i];
+        or_rope(q, m->heads, hd, pos, m->rope_base);
+        or_rope(k, m->kv_heads, hd, pos, m->rope_base);
+        memcpy(kc + (size_t)pos * kvd, k, (size_t)kvd * sizeof(float));
+        memcpy(vc + (size_t)pos * kvd, v, (size_t)kvd * sizeof(float));
+        if (!or_attention(q, m->heads, m->kv_heads, hd, kc, vc, pos + 1, prob, att)) return 0;
+        or_tensor_matvec(L->o, dim, dim, att, mv);
+        for (int i = 0; i < dim; i++) h[i] = mv[i] + h[i];
+        or_rms_norm(h, L->ffn_norm, dim, m->eps, xn);
+        or_tensor_matvec(L->gate, m->hidden, dim, xn, gate);
+        or_tensor_matvec(L->up, m->hidden, dim, xn, up);
+        for (int i = 0; i < m->hidden; i++) gate[i] = up[i] * (gate[i] / (1.0f + expf(-gate[i])));
+        or_tensor_matvec(L->down, dim, m->hidden, gate, mv);
+        for (int i = 0; i < dim; i++) h[i] = h[i] + mv[i];
+    }
+    or_rms_norm(h, m->out_norm, dim, m->eps, xn);
+    or_tensor_matvec(m->out, m->vocab, dim, xn, logits);
+    for (int j = 0; j < m->vocab; j++)
+        if (!isfinite(logits[j])) return 0;
     return 1;
 }

@@ -15,7 +15,7 @@ import struct
 import numpy as np
 import pytest
 
-from conftest import lcg_bytes
+from conftest import lcg_bytes, load_oracle_binding
 
 Q5_0, Q8_0, Q4_K, Q6_K = 6, 8, 12, 14
 
@@ -374,3 +374,39 @@ def test_golden_fixtures(oracle, workloads):
             X = np.stack([workloads.make_activations(cols, seed=seed + 100 + p) for p in range(P)])
             assert np.array_equal(f32_bits(oracle.matmul(gtype, blocks, rows, cols, X, P)),
                                   f32_bits(g[name + "__Y"])), name
+
+
+# ----------------------------------------------------- Qwen2 decode step
+
+def test_qwen2_decode_step_matches_reference(oracle, ref, workloads):
+    """The oracle's decode step (configuration 4's arithmetic) against the
+    reference's own qwen2_forward_token_cached_impl on an in-memory model:
+    logits and the KV entries each step writes are identical bit for bit,
+    over several steps from a pre-filled cache."""
+    ob = load_oracle_binding()
+    m = workloads.make_qwen2("qwen2_tiny", seed=1)
+    t0, max_ctx = 20, 40
+    keys, vals = workloads.make_kv_cache(m, t0, seed=1)
+    kvd = keys.shape[2]
+    K = np.zeros((m["layers"], max_ctx, kvd), np.float32)
+    V = np.zeros_like(K)
+    K[:, :t0], V[:, :t0] = keys, vals
+    model_c = ob.qwen2_oracle_model(m, max_ctx)
+    reference = ob.RefQwen2(m, workloads.qwen2_tensor_list(m), max_ctx)
+    try:
+        reference.set_kv(keys, vals)
+        token = 7
+        for step in range(4):
+            ok, logits = ob.oracle_qwen2_forward(oracle, model_c[0], K, V, t0 + step, token)
+            ok_ref, logits_ref = reference.forward(token)
+            assert ok and ok_ref
+            assert np.array_equal(logits.view(np.uint32), logits_ref.view(np.uint32))
+            for layer in range(m["layers"]):
+                k = np.empty(kvd, np.float32)
+                v = np.empty(kvd, np.float32)
+                reference.lib.ref_qwen2_get_kv(reference.h, layer, t0 + step, k.ctypes.data, v.ctypes.data)
+                assert np.array_equal(k.view(np.uint32), K[layer, t0 + step].view(np.uint32))
+                assert np.array_equal(v.view(np.uint32), V[layer, t0 + step].view(np.uint32))
+            token = int(np.argmax(logits_ref))
+    finally:
+        reference.close()
