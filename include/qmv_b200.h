@@ -219,6 +219,64 @@ int qmv_quantized_tensor_matmul_f32(const GgufQuantizedTensorView *matrix, const
                                     int input_count, int batch_count, float *outputs,
                                     int output_count);
 
+/* ---- device-resident Qwen2 decode step ------------------------------------
+ * Replaces the Qwen2 implementation of ArchitectureOps.forward_token
+ * (src/architecture.h:67-80, qwen2_forward_token_cached_impl
+ * src/qwen2_architecture.cpp:1195-1531) with one GPU-resident step: embedding,
+ * per layer RMSNorm + Q/K/V (+ biases) + RoPE + KV append + grouped-query
+ * attention + output projection + residual + RMSNorm + SwiGLU FFN + residual,
+ * then final RMSNorm, vocabulary projection and greedy argmax
+ * (src/sampler.cpp:14-36).  The step is captured once in a CUDA graph; the
+ * token and position live on the device, so generation replays the graph
+ * without host round trips.  Head dimension 64 and at most 16 query heads per
+ * KV head are supported.  Projections take the packed formats of this
+ * library; results follow the parity bound of the matvec path per projection.
+ * Calls on one decoder must not overlap. */
+typedef struct QmvQwen2Config {
+    int dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size; /* ModelConfig, include/engine.h:17-27 */
+    int max_context;                                                  /* KV-cache positions */
+    float rms_norm_epsilon, rope_frequency_base;
+} QmvQwen2Config;
+
+/* One tensor of the model under its GGUF name (token_embd.weight,
+ * blk.<l>.attn_norm.weight, blk.<l>.attn_q.weight / .bias, attn_k, attn_v,
+ * attn_output.weight, ffn_norm.weight, ffn_gate / ffn_up / ffn_down.weight,
+ * output_norm.weight, output.weight).  Matrices: packed type, cols (K), rows
+ * (N) and host bytes of rows x cols/block_elements blocks; vectors: type 0
+ * (F32), rows 0, cols floats. */
+typedef struct QmvQwen2Tensor {
+    const char *name;
+    uint32_t ggml_type;
+    uint64_t cols, rows;
+    const void *data;
+} QmvQwen2Tensor;
+
+typedef struct QmvQwen2 QmvQwen2;
+
+/* Upload every tensor to the current device and capture the step graph. */
+int qmv_qwen2_create(const QmvQwen2Config *config, const QmvQwen2Tensor *tensors, int count,
+                     QmvQwen2 **decoder);
+/* Pre-fill positions [0, token_count) of every layer's KV cache from host
+ * keys/values laid out [layer][token_count][n_kv_heads * head_dim]; the next
+ * step writes position token_count. */
+int qmv_qwen2_set_kv(QmvQwen2 *decoder, const float *keys, const float *values, int token_count);
+/* One step for `token`: logits[vocab_size] (host, may be NULL) and the greedy
+ * next token.  0 on a non-finite logit or a full context, as the reference. */
+int qmv_qwen2_forward(QmvQwen2 *decoder, int token, float *logits, int *next_token);
+/* `steps` greedy steps from first_token without host round trips;
+ * tokens[steps] receives the produced ids. */
+int qmv_qwen2_generate(QmvQwen2 *decoder, int first_token, int steps, int *tokens);
+/* Split form of qmv_qwen2_generate for timing: begin sets the first token,
+ * replay enqueues `steps` graph launches on `stream` (no synchronisation),
+ * read synchronises the device and copies the first `count` produced ids and
+ * the next position (may be NULL). */
+int qmv_qwen2_begin(QmvQwen2 *decoder, int first_token);
+int qmv_qwen2_replay(QmvQwen2 *decoder, int steps, void *stream);
+int qmv_qwen2_read(QmvQwen2 *decoder, int *tokens, int count, int *position);
+/* Host copy of one layer's cached key and value at `position`. */
+int qmv_qwen2_get_kv(QmvQwen2 *decoder, int layer, int position, float *key, float *value);
+int qmv_qwen2_destroy(QmvQwen2 *decoder);
+
 #ifdef __cplusplus
 }
 #endif

@@ -48,6 +48,8 @@ C_SYMBOLS = [
     "qmv_ipc_free", "qmv_memcpy", "qmv_exchange_logits", "qmv_matvec_argmax_exchange",
     "qmv_argmax_noalloc", "qmv_key_to_token", "qmv_greedy_sample",
     "qmv_quantized_tensor_matvec_f32", "qmv_quantized_tensor_matmul_f32",
+    "qmv_qwen2_create", "qmv_qwen2_set_kv", "qmv_qwen2_forward", "qmv_qwen2_generate", "qmv_qwen2_begin",
+    "qmv_qwen2_replay", "qmv_qwen2_read", "qmv_qwen2_get_kv", "qmv_qwen2_destroy",
 ]
 CXX_DROPIN_SYMBOLS = {
     "quantized_tensor_matvec_f32": "_Z27quantized_tensor_matvec_f32PK23GgufQuantizedTensorViewPKfiPfi",
@@ -138,6 +140,15 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "qmv_greedy_sample": (I, [P, I, IP, ctypes.c_char_p, I, P]),
         "qmv_quantized_tensor_matvec_f32": (I, [VP, P, I, P, I]),
         "qmv_quantized_tensor_matmul_f32": (I, [VP, P, I, I, P, I]),
+        "qmv_qwen2_create": (I, [P, P, I, ctypes.POINTER(P)]),
+        "qmv_qwen2_set_kv": (I, [P, P, P, I]),
+        "qmv_qwen2_forward": (I, [P, I, P, IP]),
+        "qmv_qwen2_generate": (I, [P, I, I, P]),
+        "qmv_qwen2_begin": (I, [P, I]),
+        "qmv_qwen2_replay": (I, [P, I, P]),
+        "qmv_qwen2_read": (I, [P, P, I, IP]),
+        "qmv_qwen2_get_kv": (I, [P, I, I, P, P]),
+        "qmv_qwen2_destroy": (I, [P]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
@@ -407,3 +418,83 @@ class Weight:
     def dequantize(self, out_dev, stream=None):
         _check(lib().qmv_dequantize(self.handle, _ptr(out_dev), self.rows * self.cols,
                                     _ptr(stream)), "qmv_dequantize")
+
+
+
+# ---------------------------------------------------------- Qwen2 decoder
+
+class QmvQwen2Config(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("dim", "hidden_dim", "n_layers", "n_heads", "n_kv_heads",
+                                            "vocab_size", "max_context")] + \
+               [("rms_norm_epsilon", ctypes.c_float), ("rope_frequency_base", ctypes.c_float)]
+
+
+class QmvQwen2Tensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("ggml_type", ctypes.c_uint32), ("cols", ctypes.c_uint64),
+                ("rows", ctypes.c_uint64), ("data", ctypes.c_void_p)]
+
+
+class Qwen2Decoder:
+    """Device-resident Qwen2 decode step (qmv_qwen2_*): the reference's
+    ArchitectureOps.forward_token for the Qwen2 architecture, on one GPU.
+
+    ``tensors``: (name, ggml_type, cols, rows, numpy bytes or float32 vector)
+    in GGUF names, e.g. ``workloads.qwen2_tensor_list(model)``."""
+
+    def __init__(self, config: dict, tensors, max_context: int):
+        c = QmvQwen2Config(config["dim"], config["hidden"], config["layers"], config["heads"],
+                           config["kv_heads"], config["vocab"], max_context, config["eps"], config["rope_base"])
+        self._keep = [np.ascontiguousarray(t[4]) for t in tensors]
+        arr = (QmvQwen2Tensor * len(tensors))()
+        for i, (name, t, cols, rows, _) in enumerate(tensors):
+            arr[i] = QmvQwen2Tensor(name.encode(), t, cols, rows, self._keep[i].ctypes.data)
+        h = ctypes.c_void_p()
+        _check(lib().qmv_qwen2_create(ctypes.byref(c), ctypes.cast(arr, ctypes.c_void_p), len(tensors),
+                                      ctypes.byref(h)), "qmv_qwen2_create")
+        self._keep = None  # uploaded
+        self.handle = h.value
+        self.vocab = config["vocab"]
+        self.kv_dim = config["kv_heads"] * (config["dim"] // config["heads"])
+
+    def set_kv(self, keys: np.ndarray, values: np.ndarray) -> None:
+        keys = np.ascontiguousarray(keys, dtype=np.float32)
+        values = np.ascontiguousarray(values, dtype=np.float32)
+        _check(lib().qmv_qwen2_set_kv(self.handle, keys.ctypes.data, values.ctypes.data, keys.shape[1]),
+               "qmv_qwen2_set_kv")
+
+    def forward(self, token: int):
+        """(logits float32[vocab], greedy next token) of one step."""
+        logits = np.empty(self.vocab, dtype=np.float32)
+        nxt = ctypes.c_int(-1)
+        _check(lib().qmv_qwen2_forward(self.handle, token, logits.ctypes.data, ctypes.byref(nxt)),
+               "qmv_qwen2_forward")
+        return logits, nxt.value
+
+    def generate(self, first_token: int, steps: int) -> np.ndarray:
+        out = np.empty(steps, dtype=np.int32)
+        _check(lib().qmv_qwen2_generate(self.handle, first_token, steps, out.ctypes.data), "qmv_qwen2_generate")
+        return out
+
+    def begin(self, first_token: int) -> None:
+        _check(lib().qmv_qwen2_begin(self.handle, first_token), "qmv_qwen2_begin")
+
+    def replay(self, steps: int, stream=None) -> None:
+        _check(lib().qmv_qwen2_replay(self.handle, steps, _ptr(stream)), "qmv_qwen2_replay")
+
+    def read(self, count: int):
+        out = np.empty(max(count, 1), dtype=np.int32)
+        pos = ctypes.c_int(-1)
+        _check(lib().qmv_qwen2_read(self.handle, out.ctypes.data, count, ctypes.byref(pos)), "qmv_qwen2_read")
+        return out[:count], pos.value
+
+    def get_kv(self, layer: int, position: int):
+        k = np.empty(self.kv_dim, dtype=np.float32)
+        v = np.empty(self.kv_dim, dtype=np.float32)
+        _check(lib().qmv_qwen2_get_kv(self.handle, layer, position, k.ctypes.data, v.ctypes.data),
+               "qmv_qwen2_get_kv")
+        return k, v
+
+    def close(self) -> None:
+        if self.handle:
+            _check(lib().qmv_qwen2_destroy(self.handle), "qmv_qwen2_destroy")
+            self.handle = None

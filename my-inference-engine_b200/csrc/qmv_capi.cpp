@@ -23,15 +23,6 @@
 
 #define QMV_EXPORT extern "C" __attribute__((visibility("default")))
 
-struct QmvWeight {
-    qmv::Layout L;
-    uint8_t *dev;
-    size_t bytes;
-    int device;
-    int row_begin;
-    bool registry_owned;
-};
-
 namespace {
 
 thread_local std::string g_error;
@@ -213,6 +204,11 @@ int decode_key(unsigned long long key, int *id)
 }
 
 }  // namespace
+
+namespace qmv {
+int set_error(const char *msg) { return fail("%s", msg); }
+int set_cuda_error(const char *what, cudaError_t e) { return cuda_fail(what, e); }
+}  // namespace qmv
 
 // ================================================================ exported
 

@@ -86,9 +86,25 @@ struct Exchange {
 };
 size_t exchange_parity_bytes(int world, int slot_rows);
 
+// Fused prologue / epilogue of a GEMV (the decode step's RMSNorm, SwiGLU,
+// bias and residual additions); device pointers.  Zero-initialised: none.
+enum : int { kPreNone = 0, kPreRmsNorm = 1, kPreSwiGlu = 2 };
+struct Fuse {
+    int pre;            // kPreRmsNorm: x <- (x / sqrt(mean(x^2) + eps)) * norm
+                        // kPreSwiGlu:  x <- up * x / (1 + exp(-x))   (x is the gate)
+    const float *norm;  // kPreRmsNorm: weight[cols]
+    float eps;
+    const float *up;    // kPreSwiGlu: up[cols]
+    const float *add;   // y[row] = (W x)[row] + add[row] when non-null (add == y: residual in place)
+};
+
 // y = W x (and optionally the argmax key of y).
 cudaError_t launch_gemv(const Layout &L, const uint8_t *w, const float *x, float *y,
                         const ArgmaxOut *am, cudaStream_t s);
+// The same with a fused prologue / epilogue; needs the TMA pipeline
+// (cudaErrorNotSupported when its stages do not fit).
+cudaError_t launch_gemv_fused(const Layout &L, const uint8_t *w, const float *x, float *y,
+                              const ArgmaxOut *am, const Fuse &fu, cudaStream_t s);
 // Fused projection + argmax + exchange: y is this rank's slot in its own
 // buffer; needs the TMA pipeline (cudaErrorNotSupported when its stages do
 // not fit).
@@ -106,6 +122,28 @@ void set_gemv_path(int path);
 void set_matmul_path(int path);
 // Device status bits set by bounded waits that expired (0 = healthy).
 cudaError_t read_status(unsigned int *out, bool clear);
+// ---- device-resident decode step (Qwen2 architecture)
+// Step state in device memory, so one step replays from a CUDA graph.
+struct DecodeState {
+    int pos;             // position the next step writes
+    int tok;             // token of the next step
+    int steps;           // tokens produced so far (index into the history)
+    unsigned int error;  // 1 token out of range, 2 context full, 4 no finite logit
+};
+// h = row st->tok of the resident embedding matrix (bit-exact dequant).
+cudaError_t launch_embed(const Layout &L, const uint8_t *w, DecodeState *st, float *h, cudaStream_t s);
+// RoPE, KV-cache append and grouped-query attention for one layer at
+// position st->pos.  qkv = [q (heads x hd) | k (kv_heads x hd) | v] after the
+// biases; kc / vc: this layer's cache [max_ctx][kv_heads x hd]; att: output
+// [heads x hd].  head_dim must be 64.
+size_t attention_workspace_floats(int heads, int kv_heads, int head_dim, int max_ctx);
+cudaError_t launch_attention(const float *qkv, int heads, int kv_heads, int head_dim, float *kc, float *vc,
+                             int max_ctx, float rope_base, DecodeState *st, float *part, unsigned int *counter,
+                             float *att, cudaStream_t s);
+// next token from the step's argmax key; history[st->steps] = token; pos += 1
+cudaError_t launch_advance(const unsigned long long *key, DecodeState *st, int *history, int max_steps,
+                           cudaStream_t s);
+
 // Argmax key of logits[0..n).
 cudaError_t launch_argmax(const float *logits, int n, const ArgmaxOut &am, cudaStream_t s);
 // Same, with the scratch in a static device array (no allocation, no caller
@@ -114,4 +152,19 @@ int noalloc_max_logits();
 cudaError_t launch_argmax_noalloc(const float *logits, int n, int index_base, unsigned long long *key,
                                   cudaStream_t s);
 
+// Per-thread error message of the C ABI (qmv_last_error); both return 0.
+int set_error(const char *msg);
+int set_cuda_error(const char *what, cudaError_t e);
+
 }  // namespace qmv
+
+// A resident packed tensor (rows [row_begin, row_begin + L.rows) of the
+// uploaded matrix), the opaque handle of the C ABI.
+struct QmvWeight {
+    qmv::Layout L;
+    uint8_t *dev;
+    size_t bytes;
+    int device;
+    int row_begin;
+    bool registry_owned;
+};

@@ -332,9 +332,12 @@ __device__ __forceinline__ XS xs_view(const uint8_t *base, int cols)
 // float4s of all positions form one contiguous range, and a 32-element block
 // never straddles two positions since cols is a multiple of 32), so the
 // global-load latency is paid once; position p goes to base + p * pos_bytes.
+// pre (kPreRmsNorm / kPreSwiGlu, one position): the x of a fused prologue,
+// formed element-wise as it is loaded (denom = sqrt(mean(x^2) + eps)).
 template <uint32_t FMT, int NT = kThreads>
 __device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t *base, int np = 1,
-                           size_t pos_bytes = 0)
+                           size_t pos_bytes = 0, int pre = kPreNone, float denom = 1.f,
+                           const float *__restrict__ aux = nullptr)
 {
     const int n4 = cols >> 2;
     const int total = np * n4;
@@ -346,6 +349,16 @@ __device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t
             int g = (it0 + u) * NT + threadIdx.x;
             v[u] = g < total ? __ldg(reinterpret_cast<const float4 *>(x) + g)
                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (pre != kPreNone && g < total) {
+                const float4 a = __ldg(reinterpret_cast<const float4 *>(aux) + g);
+                if (pre == kPreRmsNorm) {
+                    v[u] = make_float4((v[u].x / denom) * a.x, (v[u].y / denom) * a.y, (v[u].z / denom) * a.z,
+                                       (v[u].w / denom) * a.w);
+                } else {
+                    v[u] = make_float4(a.x * (v[u].x / (1.f + expf(-v[u].x))), a.y * (v[u].y / (1.f + expf(-v[u].y))),
+                                       a.z * (v[u].z / (1.f + expf(-v[u].z))), a.w * (v[u].w / (1.f + expf(-v[u].w))));
+                }
+            }
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -905,7 +918,7 @@ struct TmaPlan {
 template <uint32_t FMT, int CW, int R, int NP = 1, int SPLIT = 1>
 __global__ void __launch_bounds__((CW + 1) * 32, 1)
 gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x,
-                float *__restrict__ y, ArgmaxOut am, int want_argmax, TmaPlan P, Exchange ex)
+                float *__restrict__ y, ArgmaxOut am, int want_argmax, TmaPlan P, Exchange ex, Fuse fu)
 {
     static_assert(R * NP <= 32, "one lane per (row, position) output");
     static_assert(SPLIT == 1 || (SPLIT == 2 && R == 1 && NP == 1 && CW % 2 == 0), "split rows: one row per warp pair");
@@ -913,6 +926,7 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
     __shared__ __align__(8) unsigned long long bars[2 * 8 + 4];  // full[8] | empty[8] | pfull[2] | pfree[2]
     __shared__ unsigned long long kscratch[kMaxConsumerWarps + 1];
     __shared__ float partial[2][kMaxConsumerWarps];
+    __shared__ float sumsq[kMaxConsumerWarps];
     constexpr int kConsumerWarps = CW;
     constexpr int NSL = W<FMT>::kSlices;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -986,7 +1000,21 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
         if (ex.world > 1)  // this rank's slot in this epoch's parity region
             y = ex.logits[exchange_epoch(ex) & 1u][ex.rank] + (size_t)ex.rank * ex.slot_rows;
         const size_t xb = xs_bytes(L.cols);
-        quantize_x<FMT, CW * 32>(x, L.cols, C, smem, NP == 1 ? 1 : P.np, xb);
+        float denom = 1.f;
+        if (NP == 1 && fu.pre == kPreRmsNorm) {
+            // RMSNorm prologue: sum of squares over every consumer thread
+            float ss = 0.f;
+            for (int i = threadIdx.x; i < L.cols; i += CW * 32) ss += x[i] * x[i];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
+            if (lane == 0) sumsq[warp] = ss;
+            asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+            ss = 0.f;
+            for (int i = 0; i < CW; ++i) ss += sumsq[i];
+            denom = sqrtf(ss / (float)L.cols + fu.eps);
+        }
+        quantize_x<FMT, CW * 32>(x, L.cols, C, smem, NP == 1 ? 1 : P.np, xb, NP == 1 ? fu.pre : kPreNone, denom,
+                                 fu.pre == kPreRmsNorm ? fu.norm : fu.up);
         asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
         const XS s = xs_view(smem, L.cols);
         const int NI = (C + 32 * SPLIT - 1) / (32 * SPLIT);
@@ -1081,6 +1109,7 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
             const int oi = lane / NP, op = lane % NP;
             if (half == 0 && lane < R * NP && lr0 + oi < rows_k && op < P.np) {
                 const int row = base_row + lr0 + oi;
+                if (fu.add != nullptr) out += fu.add[(size_t)op * L.rows + row];
                 y[(size_t)op * L.rows + row] = out;
                 if (NP == 1 && want_argmax) best = max_ull(best, make_key(out, am.index_base + row));
             }
@@ -2040,6 +2069,174 @@ __global__ void dequant_raw_kernel(const uint8_t *__restrict__ raw, uint64_t nbl
         out[e] = dequant_value<FMT>(raw + (e / BE) * BB, (int)(e % BE));
 }
 
+// ------------------------------------------------- Qwen2 decode step
+//
+// Kernels of the device-resident decode step (the reference's
+// qwen2_forward_token_cached_impl, src/qwen2_architecture.cpp:1195-1531); the
+// projections are the fused GEMVs above.  Position and token live in device
+// memory (DecodeState), so one step replays from a CUDA graph: embed_kernel
+// reads the token, attention_kernel the position, and advance_kernel turns
+// the step's argmax key into the next token and moves the position on.  Every
+// device-side index is checked: a bad token or a full context sets a bit of
+// DecodeState::error and nothing is written out of bounds.
+
+constexpr int kAttnChunk = 32;  // cached tokens per attention CTA
+constexpr int kAttnThreads = 256;
+constexpr int kAttnMaxGroup = 16;  // query heads per KV head
+
+// One CTA: row st->tok of the resident embedding (src/qwen2_architecture.cpp:375-475
+// decodes the row with the block dequantiser; same bits here).
+template <uint32_t FMT>
+__global__ void embed_kernel(Layout L, const uint8_t *__restrict__ w, DecodeState *st, float *__restrict__ h)
+{
+    constexpr int BE = BlockShape<FMT>::E;
+    int tok = st->tok;
+    if (tok < 0 || tok >= L.rows) {
+        if (threadIdx.x == 0) atomicOr(&st->error, 1u);
+        tok = 0;
+    }
+    uint8_t raw[BlockShape<FMT>::B];
+    for (int b = threadIdx.x; b < L.nb; b += blockDim.x) {
+        gather_raw_block(L, w + (uint64_t)tok * L.row_stride, b, raw);
+        for (int i = 0; i < BE; ++i) h[b * BE + i] = dequant_value<FMT>(raw, i);
+    }
+}
+
+// Grid (kv head g, chunk c of kAttnChunk cached tokens).  Each CTA rotates the
+// query heads of group g (transformer_apply_rope_f32, src/transformer_ops.cpp:16-66:
+// pairs (i, i + hd/2), angle = pos / base^(2i/hd)), and, when its chunk holds
+// the new position, rotates that key and appends key and value to the cache.
+// It then forms its chunk's scores q.k / sqrt(hd), their maximum m, the sum l
+// of exp(score - m) and the weighted value sum o, and stores (m, l, o).  The
+// last CTA of group g to arrive merges the chunks: out = sum_c e^(m_c - M) o_c /
+// sum_c e^(m_c - M) l_c -- the softmax and weighted sum of
+// transformer_attention_f32 (src/transformer_ops.cpp:68-153), evaluated
+// chunk-wise.
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads)
+attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *__restrict__ kc,
+                 float *__restrict__ vc, int max_ctx, float rope_base, DecodeState *st, float *__restrict__ part,
+                 unsigned int *__restrict__ counter, float *__restrict__ att)
+{
+    __shared__ float cs[HD / 2], sn[HD / 2];
+    __shared__ float qs[kAttnMaxGroup][HD];
+    __shared__ float ks[kAttnChunk][HD + 1], vs[kAttnChunk][HD];
+    __shared__ float sc[kAttnMaxGroup][kAttnChunk];
+    __shared__ int last;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = blockIdx.x, c = blockIdx.y;
+    const int pos = st->pos;
+    if (pos < 0 || pos >= max_ctx) {
+        if (g == 0 && c == 0 && tid == 0) atomicOr(&st->error, 2u);
+        return;
+    }
+    const int T = pos + 1, nchunk = (T + kAttnChunk - 1) / kAttnChunk;
+    if (c >= nchunk) return;
+    const int G = heads / kv_heads, dim = heads * HD, kvd = kv_heads * HD;
+    const int t0 = c * kAttnChunk, tn = min(kAttnChunk, T - t0);
+
+    if (tid < HD / 2) {
+        const float angle = (float)pos / powf(rope_base, (2.0f * (float)tid / (float)HD));
+        cs[tid] = cosf(angle);
+        sn[tid] = sinf(angle);
+    }
+    __syncthreads();
+    for (int e = tid; e < G * HD; e += kAttnThreads) {
+        const int hh = e / HD, d = e % HD, i = d % (HD / 2);
+        const float *q = qkv + (g * G + hh) * HD;
+        const float x = q[i], y = q[i + HD / 2];
+        qs[hh][d] = d < HD / 2 ? x * cs[i] - y * sn[i] : x * sn[i] + y * cs[i];
+    }
+    for (int e = tid; e < tn * HD; e += kAttnThreads) {
+        const int t = e / HD, d = e % HD, tok = t0 + t;
+        const size_t slot = (size_t)tok * kvd + g * HD + d;
+        if (tok == pos) {
+            const int i = d % (HD / 2);
+            const float *k = qkv + dim + g * HD;
+            const float x = k[i], y = k[i + HD / 2];
+            const float kr = d < HD / 2 ? x * cs[i] - y * sn[i] : x * sn[i] + y * cs[i];
+            const float vv = qkv[dim + kvd + g * HD + d];
+            kc[slot] = kr;
+            vc[slot] = vv;
+            ks[t][d] = kr;
+            vs[t][d] = vv;
+        } else {
+            ks[t][d] = kc[slot];
+            vs[t][d] = vc[slot];
+        }
+    }
+    __syncthreads();
+    const float rs = sqrtf((float)HD);
+    for (int e = tid; e < G * tn; e += kAttnThreads) {
+        const int hh = e / tn, t = e % tn;
+        float acc = 0.f;
+#pragma unroll 16
+        for (int d = 0; d < HD; ++d) acc += qs[hh][d] * ks[t][d];
+        sc[hh][t] = acc / rs;
+    }
+    __syncthreads();
+    float *pc = part + ((size_t)(g * ((max_ctx + kAttnChunk - 1) / kAttnChunk) + c) * G) * (HD + 2);
+    for (int hh = warp; hh < G; hh += kAttnThreads / 32) {
+        float m = lane < tn ? sc[hh][lane] : -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
+        const float p = lane < tn ? expf(sc[hh][lane] - m) : 0.f;
+        float l = p;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(kFull, l, o);
+        if (lane < tn) sc[hh][lane] = p;
+        if (lane == 0) {
+            pc[hh * (HD + 2)] = m;
+            pc[hh * (HD + 2) + 1] = l;
+        }
+    }
+    __syncthreads();
+    for (int e = tid; e < G * HD; e += kAttnThreads) {
+        const int hh = e / HD, d = e % HD;
+        float o = 0.f;
+        for (int t = 0; t < tn; ++t) o += sc[hh][t] * vs[t][d];
+        pc[hh * (HD + 2) + 2 + d] = o;
+    }
+    // the last CTA of this group to finish merges every chunk
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(&counter[g], 1u) == (unsigned)(nchunk - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const float *pg = part + (size_t)g * ((max_ctx + kAttnChunk - 1) / kAttnChunk) * G * (HD + 2);
+    for (int e = tid; e < G * HD; e += kAttnThreads) {
+        const int hh = e / HD, d = e % HD;
+        float M = -INFINITY;
+        for (int k = 0; k < nchunk; ++k) M = fmaxf(M, pg[((size_t)k * G + hh) * (HD + 2)]);
+        float l = 0.f, o = 0.f;
+        for (int k = 0; k < nchunk; ++k) {
+            const float *pk = pg + ((size_t)k * G + hh) * (HD + 2);
+            const float f = expf(pk[0] - M);
+            l += f * pk[1];
+            o += f * pk[2 + d];
+        }
+        att[(g * G + hh) * HD + d] = o / l;
+    }
+    if (tid == 0) counter[g] = 0u;
+}
+
+// One thread: the step's greedy token (key of index_base 0) becomes the next
+// step's input; the position moves on.
+__global__ void advance_kernel(const unsigned long long *key, DecodeState *st, int *history, int max_steps)
+{
+    const unsigned long long k = *key;
+    int tok = 0;
+    if (k == 0ull || k == ~0ull)
+        atomicOr(&st->error, 4u);
+    else
+        tok = (int)(0xffffffffu - (unsigned int)(k & 0xffffffffull));
+    st->tok = tok;
+    if (st->steps >= 0 && st->steps < max_steps) history[st->steps] = tok;
+    st->steps += 1;
+    st->pos += 1;
+}
+
 // ------------------------------------------------------ launch helpers
 
 int sm_count()
@@ -2179,7 +2376,8 @@ bool tma_plan(const Layout &L, TmaPlan *P, int np = 1, bool batched = false)
 
 template <uint32_t FMT, int CW, int R, int NP = 1, int SPLIT = 1>
 cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, const float *x, float *y,
-                        const ArgmaxOut *am, cudaStream_t s, const Exchange &ex = Exchange{})
+                        const ArgmaxOut *am, cudaStream_t s, const Exchange &ex = Exchange{},
+                        const Fuse &fu = Fuse{})
 {
     auto kernel = gemv_tma_kernel<FMT, CW, R, NP, SPLIT>;
     const size_t smem = (size_t)P.x_bytes + (size_t)P.stages * P.stage_bytes;
@@ -2202,7 +2400,7 @@ cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, con
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     const int want = am ? 1 : 0;
-    e = cudaLaunchKernelEx(&cfg, kernel, L, w, x, y, a, want, P, ex);
+    e = cudaLaunchKernelEx(&cfg, kernel, L, w, x, y, a, want, P, ex, fu);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -2220,6 +2418,22 @@ cudaError_t gemv_exchange_fmt(const Layout &L, const uint8_t *w, const float *x,
     }
     if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 8, 2>(L, P, w, x, y, &am, s, ex);
     return gemv_tma_go<FMT, 8, 1>(L, P, w, x, y, &am, s, ex);
+}
+
+template <uint32_t FMT>
+cudaError_t gemv_fused_fmt(const Layout &L, const uint8_t *w, const float *x, float *y, const ArgmaxOut *am,
+                           const Fuse &fu, cudaStream_t s)
+{
+    TmaPlan P;
+    if (!tma_plan(L, &P)) return cudaErrorNotSupported;
+    const Exchange none{};
+    if (P.split == 2) return gemv_tma_go<FMT, 16, 1, 1, 2>(L, P, w, x, y, am, s, none, fu);
+    if (P.consumer_warps == 16) {
+        if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 16, 2>(L, P, w, x, y, am, s, none, fu);
+        return gemv_tma_go<FMT, 16, 1>(L, P, w, x, y, am, s, none, fu);
+    }
+    if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 8, 2>(L, P, w, x, y, am, s, none, fu);
+    return gemv_tma_go<FMT, 8, 1>(L, P, w, x, y, am, s, none, fu);
 }
 
 template <uint32_t FMT>
@@ -2545,6 +2759,45 @@ cudaError_t launch_dequant_raw(uint32_t type, const uint8_t *raw, uint64_t nbloc
     return cudaGetLastError();
 }
 
+cudaError_t launch_embed(const Layout &L, const uint8_t *w, DecodeState *st, float *h, cudaStream_t s)
+{
+    const unsigned t = (unsigned)(L.nb < 256 ? L.nb : 256);
+    switch (L.type) {
+    case kQ8_0: embed_kernel<kQ8_0><<<1, t, 0, s>>>(L, w, st, h); break;
+    case kQ5_0: embed_kernel<kQ5_0><<<1, t, 0, s>>>(L, w, st, h); break;
+    case kQ4_K: embed_kernel<kQ4_K><<<1, t, 0, s>>>(L, w, st, h); break;
+    case kQ6_K: embed_kernel<kQ6_K><<<1, t, 0, s>>>(L, w, st, h); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+size_t attention_workspace_floats(int heads, int kv_heads, int head_dim, int max_ctx)
+{
+    const size_t chunks = (size_t)(max_ctx + kAttnChunk - 1) / kAttnChunk;
+    return (size_t)kv_heads * chunks * (size_t)(heads / kv_heads) * (size_t)(head_dim + 2);
+}
+
+cudaError_t launch_attention(const float *qkv, int heads, int kv_heads, int head_dim, float *kc, float *vc,
+                             int max_ctx, float rope_base, DecodeState *st, float *part, unsigned int *counter,
+                             float *att, cudaStream_t s)
+{
+    if (head_dim != 64 || kv_heads <= 0 || heads % kv_heads != 0 || heads / kv_heads > kAttnMaxGroup ||
+        max_ctx <= 0)
+        return cudaErrorInvalidValue;
+    const dim3 grid((unsigned)kv_heads, (unsigned)((max_ctx + kAttnChunk - 1) / kAttnChunk));
+    attention_kernel<64><<<grid, kAttnThreads, 0, s>>>(qkv, heads, kv_heads, kc, vc, max_ctx, rope_base, st, part,
+                                                      counter, att);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_advance(const unsigned long long *key, DecodeState *st, int *history, int max_steps,
+                           cudaStream_t s)
+{
+    advance_kernel<<<1, 1, 0, s>>>(key, st, history, max_steps);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_gemv(const Layout &L, const uint8_t *w, const float *x, float *y,
                         const ArgmaxOut *am, cudaStream_t s)
 {
@@ -2553,6 +2806,18 @@ cudaError_t launch_gemv(const Layout &L, const uint8_t *w, const float *x, float
     case kQ5_0: return gemv_fmt<kQ5_0>(L, w, x, y, am, s);
     case kQ4_K: return gemv_fmt<kQ4_K>(L, w, x, y, am, s);
     case kQ6_K: return gemv_fmt<kQ6_K>(L, w, x, y, am, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_gemv_fused(const Layout &L, const uint8_t *w, const float *x, float *y,
+                              const ArgmaxOut *am, const Fuse &fu, cudaStream_t s)
+{
+    switch (L.type) {
+    case kQ8_0: return gemv_fused_fmt<kQ8_0>(L, w, x, y, am, fu, s);
+    case kQ5_0: return gemv_fused_fmt<kQ5_0>(L, w, x, y, am, fu, s);
+    case kQ4_K: return gemv_fused_fmt<kQ4_K>(L, w, x, y, am, fu, s);
+    case kQ6_K: return gemv_fused_fmt<kQ6_K>(L, w, x, y, am, fu, s);
     default: return cudaErrorInvalidValue;
     }
 }

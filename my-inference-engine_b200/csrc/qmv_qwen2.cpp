@@ -1,0 +1,418 @@
+// Device-resident Qwen2 decode step behind the C ABI (qmv_qwen2_*, declared
+// in include/qmv_b200.h).
+//
+// The reference runs one token through qwen2_forward_token_cached_impl
+// (src/qwen2_architecture.cpp:1195-1531) on the host, calling the packed
+// matvec once per projection and moving every activation through host
+// memory.  Here the whole step stays on one GPU:
+//
+//   embed_kernel                       token row of token_embd (bit-exact)
+//   per layer:
+//     GEMV [q; k; v]   RMSNorm(attn_norm) prologue, bias epilogue
+//     attention_kernel RoPE, KV-cache append, grouped-query attention
+//     GEMV o           residual epilogue (h += W_o att)
+//     GEMV gate, up    RMSNorm(ffn_norm) prologue
+//     GEMV down        SwiGLU prologue (up * silu(gate)), residual epilogue
+//   GEMV output        RMSNorm(output_norm) prologue, fused greedy argmax
+//   advance_kernel     argmax key -> next token, position + 1
+//
+// Token and position live in device memory, so the step is captured once into
+// a CUDA graph and replayed: generation runs token after token without the
+// host.  Weights are uploaded once (Q, K and V concatenated into one resident
+// tensor when they share a format); the KV cache is f32
+// [layer][max_context][n_kv_heads * head_dim] like the reference's
+// (src/qwen2_internal.h:33-39).
+#include <cuda_runtime.h>
+
+#include <stdint.h>
+#include <string.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "qmv_b200.h"
+#include "qmv_internal.h"
+
+#define QMV_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+struct Layer {
+    QmvWeight *qkv = nullptr;                            // [q; k; v] when they share a format
+    QmvWeight *q = nullptr, *k = nullptr, *v = nullptr;  // otherwise
+    QmvWeight *o = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
+    float *attn_norm = nullptr, *ffn_norm = nullptr, *bias_qkv = nullptr;
+};
+
+int cuda_err(const char *what, cudaError_t e) { return qmv::set_cuda_error(what, e); }
+
+#define QW_CUDA(call, what)                          \
+    do {                                             \
+        cudaError_t e_ = (call);                     \
+        if (e_ != cudaSuccess) return cuda_err(what, e_); \
+    } while (0)
+
+}  // namespace
+
+struct QmvQwen2 {
+    QmvQwen2Config cfg{};
+    int device = 0, head_dim = 0, kvd = 0;
+    QmvWeight *embd = nullptr, *out = nullptr;
+    std::vector<Layer> layers;
+    float *out_norm = nullptr;
+    float *h = nullptr, *qkv = nullptr, *att = nullptr, *gate = nullptr, *up = nullptr, *logits = nullptr;
+    float *kc = nullptr, *vc = nullptr;
+    float *attn_part = nullptr;
+    unsigned int *attn_cnt = nullptr;
+    unsigned long long *key = nullptr;
+    void *am_ws = nullptr;
+    qmv::DecodeState *st = nullptr;
+    int *history = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    std::vector<void *> allocs;
+    std::vector<QmvWeight *> weights;
+};
+
+namespace {
+
+int dalloc(QmvQwen2 *m, void **p, size_t bytes, const char *what)
+{
+    QW_CUDA(cudaMalloc(p, bytes), what);
+    m->allocs.push_back(*p);
+    QW_CUDA(cudaMemset(*p, 0, bytes), what);
+    return 1;
+}
+
+int upload_rows(QmvQwen2 *m, uint32_t type, uint64_t cols, uint64_t rows, const void *data, QmvWeight **out)
+{
+    const int be = qmv::block_elements(type), bb = qmv::block_bytes(type);
+    if (be == 0) return qmv::set_error("unsupported projection format");
+    GgufQuantizedTensorView v{};
+    v.data = (const unsigned char *)data;
+    v.ggml_type = type;
+    v.dimension_count = 2;
+    v.dimensions[0] = cols;
+    v.dimensions[1] = rows;
+    v.element_count = cols * rows;
+    v.block_elements = (uint64_t)be;
+    v.block_bytes = (uint64_t)bb;
+    v.block_count = v.element_count / (uint64_t)be;
+    if (!qmv_weight_upload(&v, 0, (int)rows, out)) return 0;
+    m->weights.push_back(*out);
+    return 1;
+}
+
+int upload_vector(QmvQwen2 *m, const float *host, size_t n, float **out, const char *what)
+{
+    if (!dalloc(m, (void **)out, n * sizeof(float), what)) return 0;
+    QW_CUDA(cudaMemcpy(*out, host, n * sizeof(float), cudaMemcpyHostToDevice), what);
+    return 1;
+}
+
+const QmvQwen2Tensor *find(const std::map<std::string, const QmvQwen2Tensor *> &by, const std::string &name,
+                           uint64_t cols, uint64_t rows)
+{
+    auto it = by.find(name);
+    if (it == by.end()) {
+        qmv::set_error(("missing tensor " + name).c_str());
+        return nullptr;
+    }
+    const QmvQwen2Tensor *t = it->second;
+    const bool vec = rows == 0;
+    if (t->cols != cols || t->rows != rows || t->data == nullptr || (vec && t->ggml_type != 0) ||
+        (!vec && qmv::block_elements(t->ggml_type) == 0) || (!vec && cols % qmv::block_elements(t->ggml_type))) {
+        qmv::set_error(("tensor " + name + " has the wrong shape or format").c_str());
+        return nullptr;
+    }
+    return t;
+}
+
+size_t tensor_bytes(const QmvQwen2Tensor *t)
+{
+    return (size_t)(t->cols / qmv::block_elements(t->ggml_type)) * t->rows * qmv::block_bytes(t->ggml_type);
+}
+
+cudaError_t gemv(QmvQwen2 *m, const QmvWeight *w, const float *x, float *y, const qmv::Fuse &fu,
+                 const qmv::ArgmaxOut *am = nullptr)
+{
+    return qmv::launch_gemv_fused(w->L, w->dev, x, y, am, fu, m->stream);
+}
+
+// One decode step, enqueued on m->stream.
+cudaError_t enqueue_step(QmvQwen2 *m)
+{
+    const QmvQwen2Config &c = m->cfg;
+    const int dim = c.dim, kvd = m->kvd;
+    cudaError_t e = qmv::launch_embed(m->embd->L, m->embd->dev, m->st, m->h, m->stream);
+    for (int l = 0; l < c.n_layers && e == cudaSuccess; ++l) {
+        const Layer &L = m->layers[(size_t)l];
+        qmv::Fuse pre_attn{qmv::kPreRmsNorm, L.attn_norm, c.rms_norm_epsilon, nullptr, L.bias_qkv};
+        if (L.qkv) {
+            e = gemv(m, L.qkv, m->h, m->qkv, pre_attn);
+        } else {
+            e = gemv(m, L.q, m->h, m->qkv, pre_attn);
+            pre_attn.add = L.bias_qkv + dim;
+            if (e == cudaSuccess) e = gemv(m, L.k, m->h, m->qkv + dim, pre_attn);
+            pre_attn.add = L.bias_qkv + dim + kvd;
+            if (e == cudaSuccess) e = gemv(m, L.v, m->h, m->qkv + dim + kvd, pre_attn);
+        }
+        const size_t layer_off = (size_t)l * (size_t)c.max_context * (size_t)kvd;
+        if (e == cudaSuccess)
+            e = qmv::launch_attention(m->qkv, c.n_heads, c.n_kv_heads, m->head_dim, m->kc + layer_off,
+                                      m->vc + layer_off, c.max_context, c.rope_frequency_base, m->st, m->attn_part,
+                                      m->attn_cnt, m->att, m->stream);
+        if (e == cudaSuccess) e = gemv(m, L.o, m->att, m->h, qmv::Fuse{qmv::kPreNone, nullptr, 0.f, nullptr, m->h});
+        const qmv::Fuse pre_ffn{qmv::kPreRmsNorm, L.ffn_norm, c.rms_norm_epsilon, nullptr, nullptr};
+        if (e == cudaSuccess) e = gemv(m, L.gate, m->h, m->gate, pre_ffn);
+        if (e == cudaSuccess) e = gemv(m, L.up, m->h, m->up, pre_ffn);
+        if (e == cudaSuccess)
+            e = gemv(m, L.down, m->gate, m->h, qmv::Fuse{qmv::kPreSwiGlu, nullptr, 0.f, m->up, m->h});
+    }
+    const qmv::ArgmaxOut am{m->key, m->am_ws, 0};
+    if (e == cudaSuccess)
+        e = gemv(m, m->out, m->h, m->logits,
+                 qmv::Fuse{qmv::kPreRmsNorm, m->out_norm, c.rms_norm_epsilon, nullptr, nullptr}, &am);
+    if (e == cudaSuccess) e = qmv::launch_advance(m->key, m->st, m->history, c.max_context, m->stream);
+    return e;
+}
+
+int set_token(QmvQwen2 *m, int token)
+{
+    if (token < 0 || token >= m->cfg.vocab_size) return qmv::set_error("token id is out of range");
+    const int tok_steps[2] = {token, 0};
+    QW_CUDA(cudaMemcpyAsync(&m->st->tok, tok_steps, sizeof tok_steps, cudaMemcpyHostToDevice, m->stream),
+            "set token");
+    QW_CUDA(cudaStreamSynchronize(m->stream), "set token");
+    return 1;
+}
+
+int check_state(QmvQwen2 *m, qmv::DecodeState *out)
+{
+    qmv::DecodeState s{};
+    QW_CUDA(cudaMemcpy(&s, m->st, sizeof s, cudaMemcpyDeviceToHost), "read decode state");
+    if (out) *out = s;
+    if (s.error & 1u) return qmv::set_error("decode step: token id out of range");
+    if (s.error & 2u) return qmv::set_error("decode step: context capacity is exhausted");
+    if (s.error & 4u) return qmv::set_error("decode step: output contains a non-finite logit");
+    return 1;
+}
+
+void release(QmvQwen2 *m)
+{
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    for (QmvWeight *w : m->weights) qmv_weight_free(w);
+    for (void *p : m->allocs) cudaFree(p);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+int build(QmvQwen2 *m, const QmvQwen2Tensor *tensors, int count)
+{
+    const QmvQwen2Config &c = m->cfg;
+    std::map<std::string, const QmvQwen2Tensor *> by;
+    for (int i = 0; i < count; ++i)
+        if (tensors[i].name) by[tensors[i].name] = &tensors[i];
+    const uint64_t dim = (uint64_t)c.dim, hid = (uint64_t)c.hidden_dim, kvd = (uint64_t)m->kvd;
+    const QmvQwen2Tensor *t = find(by, "token_embd.weight", dim, (uint64_t)c.vocab_size);
+    if (!t || !upload_rows(m, t->ggml_type, t->cols, t->rows, t->data, &m->embd)) return 0;
+    t = find(by, "output.weight", dim, (uint64_t)c.vocab_size);
+    if (!t || !upload_rows(m, t->ggml_type, t->cols, t->rows, t->data, &m->out)) return 0;
+    t = find(by, "output_norm.weight", dim, 0);
+    if (!t || !upload_vector(m, (const float *)t->data, dim, &m->out_norm, "output_norm")) return 0;
+    m->layers.resize((size_t)c.n_layers);
+    for (int l = 0; l < c.n_layers; ++l) {
+        Layer &L = m->layers[(size_t)l];
+        const std::string p = "blk." + std::to_string(l) + ".";
+        const QmvQwen2Tensor *q = find(by, p + "attn_q.weight", dim, dim);
+        const QmvQwen2Tensor *k = find(by, p + "attn_k.weight", dim, kvd);
+        const QmvQwen2Tensor *v = find(by, p + "attn_v.weight", dim, kvd);
+        const QmvQwen2Tensor *qb = find(by, p + "attn_q.bias", dim, 0);
+        const QmvQwen2Tensor *kb = find(by, p + "attn_k.bias", kvd, 0);
+        const QmvQwen2Tensor *vb = find(by, p + "attn_v.bias", kvd, 0);
+        if (!q || !k || !v || !qb || !kb || !vb) return 0;
+        if (q->ggml_type == k->ggml_type && k->ggml_type == v->ggml_type) {
+            const size_t bq = tensor_bytes(q), bk = tensor_bytes(k), bv = tensor_bytes(v);
+            std::vector<unsigned char> cat(bq + bk + bv);
+            memcpy(cat.data(), q->data, bq);
+            memcpy(cat.data() + bq, k->data, bk);
+            memcpy(cat.data() + bq + bk, v->data, bv);
+            if (!upload_rows(m, q->ggml_type, dim, dim + 2 * kvd, cat.data(), &L.qkv)) return 0;
+        } else if (!upload_rows(m, q->ggml_type, dim, dim, q->data, &L.q) ||
+                   !upload_rows(m, k->ggml_type, dim, kvd, k->data, &L.k) ||
+                   !upload_rows(m, v->ggml_type, dim, kvd, v->data, &L.v)) {
+            return 0;
+        }
+        std::vector<float> bias(dim + 2 * kvd);
+        memcpy(bias.data(), qb->data, dim * sizeof(float));
+        memcpy(bias.data() + dim, kb->data, kvd * sizeof(float));
+        memcpy(bias.data() + dim + kvd, vb->data, kvd * sizeof(float));
+        if (!upload_vector(m, bias.data(), bias.size(), &L.bias_qkv, "qkv bias")) return 0;
+        const QmvQwen2Tensor *o = find(by, p + "attn_output.weight", dim, dim);
+        const QmvQwen2Tensor *g = find(by, p + "ffn_gate.weight", dim, hid);
+        const QmvQwen2Tensor *u = find(by, p + "ffn_up.weight", dim, hid);
+        const QmvQwen2Tensor *d = find(by, p + "ffn_down.weight", hid, dim);
+        const QmvQwen2Tensor *an = find(by, p + "attn_norm.weight", dim, 0);
+        const QmvQwen2Tensor *fn = find(by, p + "ffn_norm.weight", dim, 0);
+        if (!o || !g || !u || !d || !an || !fn) return 0;
+        if (!upload_rows(m, o->ggml_type, dim, dim, o->data, &L.o) ||
+            !upload_rows(m, g->ggml_type, dim, hid, g->data, &L.gate) ||
+            !upload_rows(m, u->ggml_type, dim, hid, u->data, &L.up) ||
+            !upload_rows(m, d->ggml_type, hid, dim, d->data, &L.down) ||
+            !upload_vector(m, (const float *)an->data, dim, &L.attn_norm, "attn_norm") ||
+            !upload_vector(m, (const float *)fn->data, dim, &L.ffn_norm, "ffn_norm"))
+            return 0;
+    }
+    const size_t cache = (size_t)c.n_layers * (size_t)c.max_context * kvd * sizeof(float);
+    const size_t wide = (size_t)(hid > dim ? hid : dim);
+    if (!dalloc(m, (void **)&m->h, dim * sizeof(float), "activations") ||
+        !dalloc(m, (void **)&m->qkv, (dim + 2 * kvd) * sizeof(float), "activations") ||
+        !dalloc(m, (void **)&m->att, dim * sizeof(float), "activations") ||
+        !dalloc(m, (void **)&m->gate, wide * sizeof(float), "activations") ||
+        !dalloc(m, (void **)&m->up, wide * sizeof(float), "activations") ||
+        !dalloc(m, (void **)&m->logits, (size_t)c.vocab_size * sizeof(float), "logits") ||
+        !dalloc(m, (void **)&m->kc, cache, "key cache") || !dalloc(m, (void **)&m->vc, cache, "value cache") ||
+        !dalloc(m, (void **)&m->attn_part,
+                qmv::attention_workspace_floats(c.n_heads, c.n_kv_heads, m->head_dim, c.max_context) * sizeof(float),
+                "attention workspace") ||
+        !dalloc(m, (void **)&m->attn_cnt, (size_t)c.n_kv_heads * sizeof(unsigned int), "attention counters") ||
+        !dalloc(m, (void **)&m->key, sizeof(unsigned long long), "argmax key") ||
+        !dalloc(m, &m->am_ws, qmv::kArgmaxWorkspaceBytes, "argmax workspace") ||
+        !dalloc(m, (void **)&m->st, sizeof(qmv::DecodeState), "decode state") ||
+        !dalloc(m, (void **)&m->history, (size_t)c.max_context * sizeof(int), "token history"))
+        return 0;
+    QW_CUDA(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "decoder stream");
+    // One step outside capture sets every kernel's launch attributes, then the
+    // state and cache are cleared and the step is captured.
+    QW_CUDA(enqueue_step(m), "decode step");
+    QW_CUDA(cudaStreamSynchronize(m->stream), "decode step");
+    QW_CUDA(cudaMemset(m->st, 0, sizeof(qmv::DecodeState)), "decode state");
+    QW_CUDA(cudaMemset(m->kc, 0, cache), "key cache");
+    QW_CUDA(cudaMemset(m->vc, 0, cache), "value cache");
+    cudaGraph_t graph = nullptr;
+    QW_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "graph capture");
+    const cudaError_t e = enqueue_step(m);
+    const cudaError_t e2 = cudaStreamEndCapture(m->stream, &graph);
+    if (e != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        return cuda_err("graph capture", e);
+    }
+    QW_CUDA(e2, "graph capture");
+    const cudaError_t e3 = cudaGraphInstantiate(&m->exec, graph, 0);
+    cudaGraphDestroy(graph);
+    QW_CUDA(e3, "graph instantiate");
+    return 1;
+}
+
+}  // namespace
+
+QMV_EXPORT int qmv_qwen2_create(const QmvQwen2Config *cfg, const QmvQwen2Tensor *tensors, int count,
+                                QmvQwen2 **out)
+{
+    if (out == nullptr) return qmv::set_error("output handle pointer is null");
+    *out = nullptr;
+    if (cfg == nullptr || tensors == nullptr || count <= 0) return qmv::set_error("null configuration or tensors");
+    const QmvQwen2Config &c = *cfg;
+    if (c.dim <= 0 || c.hidden_dim <= 0 || c.n_layers <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 ||
+        c.vocab_size <= 0 || c.max_context <= 0 || c.dim % c.n_heads != 0 || c.n_heads % c.n_kv_heads != 0 ||
+        !(c.rms_norm_epsilon > 0.f) || !(c.rope_frequency_base > 0.f))
+        return qmv::set_error("invalid Qwen2 configuration");
+    if (c.dim / c.n_heads != 64 || c.n_heads / c.n_kv_heads > 16 || c.dim % 4 || c.hidden_dim % 4)
+        return qmv::set_error("unsupported shape: head dimension 64 and at most 16 query heads per KV head");
+    QmvQwen2 *m = new QmvQwen2();
+    m->cfg = c;
+    m->head_dim = c.dim / c.n_heads;
+    m->kvd = c.n_kv_heads * m->head_dim;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        delete m;
+        return qmv::set_error("no CUDA device");
+    }
+    m->device = dev;
+    if (!build(m, tensors, count)) {
+        release(m);
+        return 0;
+    }
+    *out = m;
+    return 1;
+}
+
+QMV_EXPORT int qmv_qwen2_set_kv(QmvQwen2 *m, const float *keys, const float *values, int token_count)
+{
+    if (m == nullptr || keys == nullptr || values == nullptr) return qmv::set_error("null argument");
+    if (token_count < 0 || token_count >= m->cfg.max_context) return qmv::set_error("token count out of range");
+    const size_t kvd = (size_t)m->kvd, T = (size_t)token_count;
+    for (int l = 0; l < m->cfg.n_layers; ++l) {
+        const size_t dst = (size_t)l * (size_t)m->cfg.max_context * kvd, src = (size_t)l * T * kvd;
+        QW_CUDA(cudaMemcpy(m->kc + dst, keys + src, T * kvd * sizeof(float), cudaMemcpyHostToDevice), "set kv");
+        QW_CUDA(cudaMemcpy(m->vc + dst, values + src, T * kvd * sizeof(float), cudaMemcpyHostToDevice), "set kv");
+    }
+    const qmv::DecodeState s{token_count, 0, 0, 0u};
+    QW_CUDA(cudaMemcpy(m->st, &s, sizeof s, cudaMemcpyHostToDevice), "set kv");
+    return 1;
+}
+
+QMV_EXPORT int qmv_qwen2_replay(QmvQwen2 *m, int steps, void *stream)
+{
+    if (m == nullptr || steps < 0) return qmv::set_error("bad replay request");
+    for (int i = 0; i < steps; ++i) QW_CUDA(cudaGraphLaunch(m->exec, (cudaStream_t)stream), "graph launch");
+    return 1;
+}
+
+QMV_EXPORT int qmv_qwen2_begin(QmvQwen2 *m, int token)
+{
+    if (m == nullptr) return qmv::set_error("null decoder");
+    return set_token(m, token);
+}
+
+QMV_EXPORT int qmv_qwen2_read(QmvQwen2 *m, int *tokens, int count, int *position)
+{
+    if (m == nullptr || count < 0 || (count > 0 && tokens == nullptr)) return qmv::set_error("bad read request");
+    QW_CUDA(cudaDeviceSynchronize(), "decode steps");
+    qmv::DecodeState s{};
+    if (!check_state(m, &s)) return 0;
+    if (count > s.steps || count > m->cfg.max_context) return qmv::set_error("fewer tokens were produced");
+    if (count > 0) QW_CUDA(cudaMemcpy(tokens, m->history, (size_t)count * sizeof(int), cudaMemcpyDeviceToHost), "read");
+    if (position) *position = s.pos;
+    return 1;
+}
+
+QMV_EXPORT int qmv_qwen2_forward(QmvQwen2 *m, int token, float *logits, int *next_token)
+{
+    if (m == nullptr) return qmv::set_error("null decoder");
+    if (!set_token(m, token) || !qmv_qwen2_replay(m, 1, m->stream)) return 0;
+    QW_CUDA(cudaStreamSynchronize(m->stream), "decode step");
+    if (!check_state(m, nullptr)) return 0;
+    if (logits)
+        QW_CUDA(cudaMemcpy(logits, m->logits, (size_t)m->cfg.vocab_size * sizeof(float), cudaMemcpyDeviceToHost),
+                "read logits");
+    if (next_token) QW_CUDA(cudaMemcpy(next_token, m->history, sizeof(int), cudaMemcpyDeviceToHost), "read token");
+    return 1;
+}
+
+QMV_EXPORT int qmv_qwen2_generate(QmvQwen2 *m, int first_token, int steps, int *tokens)
+{
+    if (m == nullptr || steps <= 0 || tokens == nullptr) return qmv::set_error("bad generate request");
+    if (!set_token(m, first_token) || !qmv_qwen2_replay(m, steps, m->stream)) return 0;
+    QW_CUDA(cudaStreamSynchronize(m->stream), "decode steps");
+    return qmv_qwen2_read(m, tokens, steps, nullptr);
+}
+
+QMV_EXPORT int qmv_qwen2_get_kv(QmvQwen2 *m, int layer, int position, float *key, float *value)
+{
+    if (m == nullptr || key == nullptr || value == nullptr || layer < 0 || layer >= m->cfg.n_layers || position < 0 ||
+        position >= m->cfg.max_context)
+        return qmv::set_error("bad KV request");
+    const size_t off = ((size_t)layer * (size_t)m->cfg.max_context + (size_t)position) * (size_t)m->kvd;
+    QW_CUDA(cudaMemcpy(key, m->kc + off, (size_t)m->kvd * sizeof(float), cudaMemcpyDeviceToHost), "read kv");
+    QW_CUDA(cudaMemcpy(value, m->vc + off, (size_t)m->kvd * sizeof(float), cudaMemcpyDeviceToHost), "read kv");
+    return 1;
+}
+
+QMV_EXPORT int qmv_qwen2_destroy(QmvQwen2 *m)
+{
+    if (m == nullptr) return qmv::set_error("null decoder");
+    release(m);
+    return 1;
+}

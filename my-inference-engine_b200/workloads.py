@@ -158,8 +158,9 @@ def algorithmic_bytes(gtype: int, rows: int, cols: int, batch: int = 1) -> int:
 #
 # Configuration 4: a Qwen2-0.5B-architecture model with random-init weights.
 # Projection formats: attn_q/k/v/output and ffn_gate Q8_0, ffn_up and
-# ffn_down Q5_0, token_embd Q8_0, output Q6_K (the same generators and
-# distributions as above, one stream per tensor).  F32 tensors: RMSNorm
+# ffn_down Q5_0, token_embd Q8_0, output Q6_K where its rows are whole
+# superblocks, else Q8_0 (the same generators and distributions as above, one
+# stream per tensor).  F32 tensors: RMSNorm
 # weights 1 + N(0, 0.1), Q/K/V biases N(0, 0.02).  The KV cache is pre-filled
 # with N(0, 1) keys and values.
 
@@ -175,6 +176,16 @@ QWEN2_CONFIGS = {
 QWEN2_TYPES = dict(q=Q8_0, k=Q8_0, v=Q8_0, o=Q8_0, gate=Q8_0, up=Q5_0, down=Q5_0, embd=Q8_0, out=Q6_K)
 
 
+def qwen2_type(kind: str, cols: int) -> int:
+    """The format of a projection; a K-quant whose rows are not whole 256-weight
+    superblocks (the 896-wide output projection of Qwen2-0.5B) is stored as
+    Q8_0 instead, as GGUF converters do."""
+    t = QWEN2_TYPES[kind]
+    if t in (Q4_K, Q6_K) and cols % 256:
+        return Q8_0
+    return t
+
+
 def make_qwen2(name: str = "cfg4_qwen2_0_5b", seed: int = 0) -> dict:
     """Synthetic model: config fields plus packed tensors as
     (ggml_type, rows, cols, blocks) and F32 vectors, in the reference's
@@ -185,7 +196,7 @@ def make_qwen2(name: str = "cfg4_qwen2_0_5b", seed: int = 0) -> dict:
 
     def packed(kind, rows, cols):
         stream[0] += 1
-        t = QWEN2_TYPES[kind]
+        t = qwen2_type(kind, cols)
         return (t, rows, cols, make_blocks(t, rows, cols, seed=seed, stream=stream[0]))
 
     def vec(n, mean, std):

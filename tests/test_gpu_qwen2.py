@@ -1,0 +1,116 @@
+"""GPU parity of the device-resident Qwen2 decode step (qmv_qwen2_*) against
+the C restatement of the reference's forward step (itself pinned bit-for-bit
+to the reference's qwen2_forward_token_cached_impl in test_oracle.py).
+
+Bars: teacher-forced (both sides fed the oracle's greedy token), every step
+yields the oracle's greedy token, logits within LOGIT_TOL of the logit scale,
+and the KV entries each step appends within KV_TOL; graph-replayed
+generation equals step-by-step decoding.
+"""
+import numpy as np
+import pytest
+
+from conftest import load_oracle_binding
+
+pytestmark = pytest.mark.gpu
+
+# The step chains ~7 quantized projections per layer (each within
+# 1e-4 * sum|w x| per output) through RMSNorm, attention and residuals; the
+# bars below are relative to max|logit| and to max|k|, |v| of the step.
+LOGIT_TOL = 2e-3
+KV_TOL = 2e-3
+
+
+def _oracle_setup(wl, m, t0, max_ctx, seed):
+    ob = load_oracle_binding()
+    keys, vals = wl.make_kv_cache(m, t0, seed=seed)
+    kvd = keys.shape[2]
+    K = np.zeros((m["layers"], max_ctx, kvd), np.float32)
+    V = np.zeros_like(K)
+    K[:, :t0], V[:, :t0] = keys, vals
+    return ob, keys, vals, K, V
+
+
+def _teacher_forced(qmv, oracle, wl, name, t0, max_ctx, steps, seed=0, first=7):
+    ob, keys, vals, K, V = _oracle_setup(wl, wl.make_qwen2(name, seed=seed), t0, max_ctx, seed)
+    m = wl.make_qwen2(name, seed=seed)
+    model_c = ob.qwen2_oracle_model(m, max_ctx)
+    dec = qmv.Qwen2Decoder(m, wl.qwen2_tensor_list(m), max_ctx)
+    worst = []
+    try:
+        dec.set_kv(keys, vals)
+        token = first
+        for step in range(steps):
+            pos = t0 + step
+            ok, ref_logits = ob.oracle_qwen2_forward(oracle, model_c[0], K, V, pos, token)
+            assert ok
+            logits, nxt = dec.forward(token)
+            ref_tok = int(np.argmax(ref_logits))
+            top2 = np.sort(ref_logits)[-2:]
+            scale = float(np.max(np.abs(ref_logits)))
+            err = float(np.max(np.abs(logits - ref_logits)))
+            worst.append((err / scale, float(top2[1] - top2[0]) / scale))
+            assert nxt == ref_tok, (step, nxt, ref_tok, worst[-1])
+            assert err <= LOGIT_TOL * scale, (step, err, scale)
+            for layer in range(m["layers"]):
+                k, v = dec.get_kv(layer, pos)
+                ks = float(np.max(np.abs(K[layer, pos]))) + 1e-6
+                vs = float(np.max(np.abs(V[layer, pos]))) + 1e-6
+                assert float(np.max(np.abs(k - K[layer, pos]))) <= KV_TOL * ks, (step, layer)
+                assert float(np.max(np.abs(v - V[layer, pos]))) <= KV_TOL * vs, (step, layer)
+            token = ref_tok
+    finally:
+        dec.close()
+    return worst
+
+
+def test_qwen2_decode_teacher_forced_small(cuda, qmv, oracle, workloads):
+    worst = _teacher_forced(qmv, oracle, workloads, "qwen2_tiny", t0=20, max_ctx=64, steps=6, seed=1)
+    print("relative logit error, relative top-2 gap per step:", worst)
+
+
+def test_qwen2_generate_equals_stepwise(cuda, qmv, workloads):
+    """Graph-replayed generation (token fed back on the device) produces the
+    same ids as one step at a time through the host."""
+    m = workloads.make_qwen2("qwen2_tiny", seed=2)
+    keys, vals = workloads.make_kv_cache(m, 10, seed=2)
+    dec = qmv.Qwen2Decoder(m, workloads.qwen2_tensor_list(m), 64)
+    try:
+        dec.set_kv(keys, vals)
+        gen = dec.generate(3, 12)
+        dec.set_kv(keys, vals)
+        tok, seq = 3, []
+        for _ in range(12):
+            _, tok = dec.forward(tok)
+            seq.append(tok)
+        assert list(gen) == seq
+        assert qmv.device_status(clear=True) == 0
+    finally:
+        dec.close()
+
+
+def test_qwen2_errors(cuda, qmv, workloads):
+    """A token outside the vocabulary and an exhausted context fail with a
+    message (as the reference's forward_token), and the decoder stays usable."""
+    m = workloads.make_qwen2("qwen2_tiny", seed=3)
+    keys, vals = workloads.make_kv_cache(m, 6, seed=3)
+    dec = qmv.Qwen2Decoder(m, workloads.qwen2_tensor_list(m), 8)
+    try:
+        dec.set_kv(keys, vals)
+        with pytest.raises(RuntimeError, match="out of range"):
+            dec.forward(m["vocab"])
+        dec.forward(1)
+        dec.forward(1)  # writes position 7, the last
+        with pytest.raises(RuntimeError, match="context capacity"):
+            dec.forward(1)
+        dec.set_kv(keys, vals)
+        dec.forward(2)
+    finally:
+        dec.close()
+
+
+def test_qwen2_config4_teacher_forced(cuda, qmv, oracle, workloads):
+    """Configuration 4 at full size: 24 layers, 1024 cached positions,
+    vocabulary 151936; three teacher-forced steps."""
+    worst = _teacher_forced(qmv, oracle, workloads, "cfg4_qwen2_0_5b", t0=1024, max_ctx=1280, steps=3, seed=0)
+    print("relative logit error, relative top-2 gap per step:", worst)
