@@ -583,6 +583,83 @@ def extras_single_gpu(qmv, steps, only=None):
     return out
 
 
+QWEN2_DECODE = "cfg4_qwen2_0_5b_decode"
+
+
+def bench_qwen2_decode(qmv, steps=256, prefill=1024, cpu_seconds=5.0, cpu=True):
+    """Configuration 4: greedy decode of `steps` tokens on the synthetic
+    Qwen2-0.5B model from a KV cache pre-filled to `prefill` positions.
+    value: device-timed tokens/s (CUDA events around `steps` replays of the
+    step graph on one stream; the token is fed back on the device).  e2e:
+    qmv_qwen2_generate through the C ABI (first token in, `steps` ids out),
+    wall clock.  Bytes per token: packed weights of every layer and of the
+    output projection, the embedding row, and the KV cache read by attention."""
+    import torch
+    wl = workloads()
+    m = wl.make_qwen2("cfg4_qwen2_0_5b", seed=0)
+    tensors = wl.qwen2_tensor_list(m)
+    keys, vals = wl.make_kv_cache(m, prefill, seed=0)
+    max_ctx = prefill + steps
+    dec = qmv.Qwen2Decoder(m, tensors, max_ctx)
+    try:
+        stream = torch.cuda.Stream()
+        dec.set_kv(keys, vals)
+        dec.generate(7, 8)  # warm-up
+        dec.set_kv(keys, vals)
+        dec.begin(7)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            torch.cuda.synchronize()
+            a.record(stream)
+            dec.replay(steps, stream.cuda_stream)
+            b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b)
+        toks, pos = dec.read(steps)
+        dec.set_kv(keys, vals)
+        t0 = time.perf_counter()
+        toks_e2e = dec.generate(7, steps)
+        e2e_s = time.perf_counter() - t0
+        status = qmv.device_status(clear=True)
+    finally:
+        dec.close()
+    packed = sum(t[4].nbytes for t in tensors if t[3] > 0 and t[0] != "token_embd.weight")
+    embd_row = m["embd"][3].shape[1]
+    kvd = m["kv_heads"] * (m["dim"] // m["heads"])
+    kv_read = sum(2 * m["layers"] * (prefill + i + 1) * kvd * 4 for i in range(steps)) / steps
+    per_token = packed + embd_row + kv_read
+    peak, _ = measured_peaks()
+    gbs = per_token * steps / (ms * 1e-3) / 1e9
+    rec = {"tokens_per_s": round(steps / (ms * 1e-3), 1), "us_per_token": round(ms * 1e3 / steps, 2),
+           "tokens": steps, "prefill": prefill, "bytes_per_token": int(per_token), "GB_s": round(gbs, 1),
+           "frac_hbm": round(gbs / peak, 3),
+           "gpu_launches_per_token": 1 + 6 * m["layers"] + 2,
+           "e2e": {"tokens_per_s": round(steps / e2e_s, 1), "h2d_bytes": 8, "d2h_bytes": 4 * steps},
+           "same_tokens_e2e": bool(np.array_equal(toks, toks_e2e)), "next_position": pos,
+           "timing": "CUDA events around graph replays (one stream)", "device_status": status,
+           "model": "Qwen2-0.5B architecture, random-init (Q8_0 attention/gate/embedding/output, Q5_0 up/down)"}
+    if cpu:
+        binding = _load("qmv_oracle_binding", os.path.join(REPO, "oracle", "binding.py"))
+        if os.path.exists(binding.REF_AVX2_SO):
+            ref = binding.RefQwen2(m, tensors, max_ctx, path=binding.REF_AVX2_SO)
+            try:
+                ref.set_kv(keys, vals)
+                n, tok, t0 = 0, 7, time.perf_counter()
+                while n < steps and (time.perf_counter() - t0) < cpu_seconds:
+                    ok, logits = ref.forward(tok)
+                    tok = int(np.argmax(logits))
+                    n += 1
+                el = time.perf_counter() - t0
+            finally:
+                ref.close()
+            rec["cpu_baseline"] = {"value": round(n / el, 2), "unit": "tokens/s", "cores": os.cpu_count(),
+                                   "kind": "reference",
+                                   "sample": f"{n} decode steps from {prefill} cached positions "
+                                             f"(reference forward_token, OpenMP AVX2 build, {el:.1f} s)"}
+    return rec
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -613,7 +690,11 @@ def main():
         torch.cuda.set_device(local_rank)
         qmv = load_qmv()
         qmv.set_device(local_rank)
-        print(json.dumps({"only": args.only, "result": extras_single_gpu(qmv, args.steps, args.only)}), flush=True)
+        if args.only == QWEN2_DECODE:
+            res = {QWEN2_DECODE: bench_qwen2_decode(qmv, steps=min(args.steps, 256), cpu=not args.no_cpu_baseline)}
+        else:
+            res = extras_single_gpu(qmv, args.steps, args.only)
+        print(json.dumps({"only": args.only, "result": res}), flush=True)
         return 0
 
     result = run_b200(args, rank, world, local_rank)
@@ -622,6 +703,7 @@ def main():
     if world == 1 and not args.no_extras:
         qmv = load_qmv()
         result["configs"] = extras_single_gpu(qmv, steps=200)
+        result["configs"][QWEN2_DECODE] = bench_qwen2_decode(qmv, cpu=not args.no_cpu_baseline)
     if world == 1 and not args.no_cpu_baseline:
         wl = workloads()
         blocks = wl.make_blocks(Q6_K, VOCAB_ROWS, HIDDEN, seed=0)
