@@ -2083,6 +2083,8 @@ __global__ void dequant_raw_kernel(const uint8_t *__restrict__ raw, uint64_t nbl
 constexpr int kAttnChunk = 32;  // cached tokens per attention CTA
 constexpr int kAttnThreads = 256;
 constexpr int kAttnMaxGroup = 16;  // query heads per KV head
+// chunks whose merge weights fit the score tile (kAttnMaxGroup x kAttnChunk)
+constexpr int kAttnMaxChunks = kAttnMaxGroup * kAttnChunk;
 
 // One CTA: row st->tok of the resident embedding (src/qwen2_architecture.cpp:375-475
 // decodes the row with the block dequantiser; same bits here).
@@ -2120,12 +2122,16 @@ attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *
 {
     __shared__ float cs[HD / 2], sn[HD / 2];
     __shared__ float qs[kAttnMaxGroup][HD];
-    __shared__ float ks[kAttnChunk][HD + 1], vs[kAttnChunk][HD];
+    __shared__ float ks[kAttnChunk][HD + 1];
+    __shared__ __align__(16) float vs[kAttnChunk][HD];
     __shared__ float sc[kAttnMaxGroup][kAttnChunk];
     __shared__ int last;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = blockIdx.x, c = blockIdx.y;
-    const int pos = st->pos;
+    // The next launch (the output projection) may start streaming its
+    // weights; it reads att only after its own griddepcontrol.wait.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int pos = st->pos;  // written by the previous step's advance_kernel
     if (pos < 0 || pos >= max_ctx) {
         if (g == 0 && c == 0 && tid == 0) atomicOr(&st->error, 2u);
         return;
@@ -2135,11 +2141,35 @@ attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *
     const int G = heads / kv_heads, dim = heads * HD, kvd = kv_heads * HD;
     const int t0 = c * kAttnChunk, tn = min(kAttnChunk, T - t0);
 
+    // Cached positions (< pos) do not depend on this layer's projections:
+    // load them before waiting for the Q/K/V GEMV, every load in flight at once.
+    constexpr int kV4 = kAttnChunk * HD / 4 / kAttnThreads;  // float4 per thread per matrix
+    static_assert(kAttnChunk * HD % (4 * kAttnThreads) == 0, "whole float4 per thread");
+    float4 kr4[kV4], vr4[kV4];
+#pragma unroll
+    for (int i = 0; i < kV4; ++i) {
+        const int e4 = tid + i * kAttnThreads, t = (4 * e4) / HD, d = (4 * e4) % HD, tok = t0 + t;
+        const size_t slot = (size_t)tok * kvd + g * HD + d;
+        if (t < tn && tok != pos) {
+            kr4[i] = __ldg(reinterpret_cast<const float4 *>(kc + slot));
+            vr4[i] = __ldg(reinterpret_cast<const float4 *>(vc + slot));
+        }
+    }
     if (tid < HD / 2) {
         const float angle = (float)pos / powf(rope_base, (2.0f * (float)tid / (float)HD));
         cs[tid] = cosf(angle);
         sn[tid] = sinf(angle);
     }
+#pragma unroll
+    for (int i = 0; i < kV4; ++i) {
+        const int e4 = tid + i * kAttnThreads, t = (4 * e4) / HD, d = (4 * e4) % HD, tok = t0 + t;
+        if (t < tn && tok != pos) {
+            ks[t][d] = kr4[i].x; ks[t][d + 1] = kr4[i].y; ks[t][d + 2] = kr4[i].z; ks[t][d + 3] = kr4[i].w;
+            *reinterpret_cast<float4 *>(&vs[t][d]) = vr4[i];
+        }
+    }
+    // q, k and v of this position come from the Q/K/V GEMV
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     __syncthreads();
     for (int e = tid; e < G * HD; e += kAttnThreads) {
         const int hh = e / HD, d = e % HD, i = d % (HD / 2);
@@ -2147,22 +2177,19 @@ attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *
         const float x = q[i], y = q[i + HD / 2];
         qs[hh][d] = d < HD / 2 ? x * cs[i] - y * sn[i] : x * sn[i] + y * cs[i];
     }
-    for (int e = tid; e < tn * HD; e += kAttnThreads) {
-        const int t = e / HD, d = e % HD, tok = t0 + t;
-        const size_t slot = (size_t)tok * kvd + g * HD + d;
-        if (tok == pos) {
+    if (pos >= t0 && pos < t0 + tn) {
+        const int t = pos - t0;
+        for (int d = tid; d < HD; d += kAttnThreads) {
             const int i = d % (HD / 2);
             const float *k = qkv + dim + g * HD;
             const float x = k[i], y = k[i + HD / 2];
             const float kr = d < HD / 2 ? x * cs[i] - y * sn[i] : x * sn[i] + y * cs[i];
             const float vv = qkv[dim + kvd + g * HD + d];
+            const size_t slot = (size_t)pos * kvd + g * HD + d;
             kc[slot] = kr;
             vc[slot] = vv;
             ks[t][d] = kr;
             vs[t][d] = vv;
-        } else {
-            ks[t][d] = kc[slot];
-            vs[t][d] = vc[slot];
         }
     }
     __syncthreads();
@@ -2204,19 +2231,34 @@ attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *
     __syncthreads();
     if (!last) return;
     __threadfence();
+    // Merge: every chunk's (m, l) of every head in one parallel load, the
+    // weights e^(m_c - M) / sum_c e^(m_c - M) l_c once per (chunk, head), then
+    // the weighted output sums with independent loads.
     const float *pg = part + (size_t)g * ((max_ctx + kAttnChunk - 1) / kAttnChunk) * G * (HD + 2);
+    float *wgt = &sc[0][0];  // reuses the score tile: nchunk x G weights (nchunk <= kAttnMaxChunks)
+    __shared__ float mx[kAttnMaxGroup], den[kAttnMaxGroup];
+    for (int e = tid; e < nchunk * G; e += kAttnThreads) wgt[e] = pg[(size_t)e * (HD + 2)];
+    __syncthreads();
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int k = 0; k < nchunk; ++k) M = fmaxf(M, wgt[k * G + tid]);
+        mx[tid] = M;
+    }
+    __syncthreads();
+    for (int e = tid; e < nchunk * G; e += kAttnThreads) wgt[e] = expf(wgt[e] - mx[e % G]);
+    __syncthreads();
+    if (tid < G) {
+        float l = 0.f;
+        for (int k = 0; k < nchunk; ++k) l += wgt[k * G + tid] * pg[((size_t)k * G + tid) * (HD + 2) + 1];
+        den[tid] = l;
+    }
+    __syncthreads();
     for (int e = tid; e < G * HD; e += kAttnThreads) {
         const int hh = e / HD, d = e % HD;
-        float M = -INFINITY;
-        for (int k = 0; k < nchunk; ++k) M = fmaxf(M, pg[((size_t)k * G + hh) * (HD + 2)]);
-        float l = 0.f, o = 0.f;
-        for (int k = 0; k < nchunk; ++k) {
-            const float *pk = pg + ((size_t)k * G + hh) * (HD + 2);
-            const float f = expf(pk[0] - M);
-            l += f * pk[1];
-            o += f * pk[2 + d];
-        }
-        att[(g * G + hh) * HD + d] = o / l;
+        float o = 0.f;
+#pragma unroll 8
+        for (int k = 0; k < nchunk; ++k) o += wgt[k * G + hh] * pg[((size_t)k * G + hh) * (HD + 2) + 2 + d];
+        att[(g * G + hh) * HD + d] = o / den[hh];
     }
     if (tid == 0) counter[g] = 0u;
 }
@@ -2783,12 +2825,21 @@ cudaError_t launch_attention(const float *qkv, int heads, int kv_heads, int head
                              float *att, cudaStream_t s)
 {
     if (head_dim != 64 || kv_heads <= 0 || heads % kv_heads != 0 || heads / kv_heads > kAttnMaxGroup ||
-        max_ctx <= 0)
+        max_ctx <= 0 ||
+        (long long)((max_ctx + kAttnChunk - 1) / kAttnChunk) * (heads / kv_heads) > kAttnMaxChunks)
         return cudaErrorInvalidValue;
     const dim3 grid((unsigned)kv_heads, (unsigned)((max_ctx + kAttnChunk - 1) / kAttnChunk));
-    attention_kernel<64><<<grid, kAttnThreads, 0, s>>>(qkv, heads, kv_heads, kc, vc, max_ctx, rope_base, st, part,
-                                                      counter, att);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, attention_kernel<64>, qkv, heads, kv_heads, kc, vc, max_ctx, rope_base, st, part,
+                              counter, att);
 }
 
 cudaError_t launch_advance(const unsigned long long *key, DecodeState *st, int *history, int max_steps,
