@@ -2406,7 +2406,15 @@ bool tma_plan(const Layout &L, TmaPlan *P, int np = 1, bool batched = false)
         P->x_bytes = xb;
         P->stage_bytes = (uint32_t)sb;
         P->rows_per_stage = cw * r / split;
-        P->stages = (int)(ns > 8 ? 8 : ns);
+        // no more stages than one CTA's rows fill (the grid has one CTA per
+        // SM), at least 2: small matrices then leave shared memory for the
+        // CTAs of the launches around them
+        const long long ctas = L.rows < sm_count() ? L.rows : sm_count();
+        const long long per_cta = ((long long)L.rows + ctas - 1) / ctas;
+        const long long need = (per_cta + P->rows_per_stage - 1) / P->rows_per_stage;
+        uint64_t cap = need < 2 ? 2 : (uint64_t)need;
+        if (cap > 8) cap = 8;
+        P->stages = (int)(ns > cap ? cap : ns);
         P->consumer_warps = cw;
         P->rows_per_warp = r;
         P->np = np;
