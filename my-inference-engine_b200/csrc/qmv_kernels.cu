@@ -2080,7 +2080,7 @@ __global__ void dequant_raw_kernel(const uint8_t *__restrict__ raw, uint64_t nbl
 // device-side index is checked: a bad token or a full context sets a bit of
 // DecodeState::error and nothing is written out of bounds.
 
-constexpr int kAttnChunk = 32;  // cached tokens per attention CTA
+constexpr int kAttnChunk = 64;  // cached tokens per attention CTA
 constexpr int kAttnThreads = 256;
 constexpr int kAttnMaxGroup = 16;  // query heads per KV head
 // chunks whose merge weights fit the score tile (kAttnMaxGroup x kAttnChunk)
@@ -2204,14 +2204,18 @@ attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *
     __syncthreads();
     float *pc = part + ((size_t)(g * ((max_ctx + kAttnChunk - 1) / kAttnChunk) + c) * G) * (HD + 2);
     for (int hh = warp; hh < G; hh += kAttnThreads / 32) {
-        float m = lane < tn ? sc[hh][lane] : -INFINITY;
+        float m = -INFINITY;
+        for (int t = lane; t < tn; t += 32) m = fmaxf(m, sc[hh][t]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
-        const float p = lane < tn ? expf(sc[hh][lane] - m) : 0.f;
-        float l = p;
+        float l = 0.f;
+        for (int t = lane; t < tn; t += 32) {
+            const float p = expf(sc[hh][t] - m);
+            sc[hh][t] = p;
+            l += p;
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(kFull, l, o);
-        if (lane < tn) sc[hh][lane] = p;
         if (lane == 0) {
             pc[hh * (HD + 2)] = m;
             pc[hh * (HD + 2) + 1] = l;
@@ -2247,10 +2251,12 @@ attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *
     __syncthreads();
     for (int e = tid; e < nchunk * G; e += kAttnThreads) wgt[e] = expf(wgt[e] - mx[e % G]);
     __syncthreads();
-    if (tid < G) {
+    for (int hh = warp; hh < G; hh += kAttnThreads / 32) {
         float l = 0.f;
-        for (int k = 0; k < nchunk; ++k) l += wgt[k * G + tid] * pg[((size_t)k * G + tid) * (HD + 2) + 1];
-        den[tid] = l;
+        for (int k = lane; k < nchunk; k += 32) l += wgt[k * G + hh] * pg[((size_t)k * G + hh) * (HD + 2) + 1];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(kFull, l, o);
+        if (lane == 0) den[hh] = l;
     }
     __syncthreads();
     for (int e = tid; e < G * HD; e += kAttnThreads) {
