@@ -622,6 +622,7 @@ def bench_qwen2_decode(qmv, steps=256, prefill=1024, cpu_seconds=5.0, cpu=True):
         toks_e2e = dec.generate(7, steps)
         e2e_s = time.perf_counter() - t0
         status = qmv.device_status(clear=True)
+        launches = dec.kernels_per_step
     finally:
         dec.close()
     packed = sum(t[4].nbytes for t in tensors if t[3] > 0 and t[0] != "token_embd.weight")
@@ -634,7 +635,7 @@ def bench_qwen2_decode(qmv, steps=256, prefill=1024, cpu_seconds=5.0, cpu=True):
     rec = {"tokens_per_s": round(steps / (ms * 1e-3), 1), "us_per_token": round(ms * 1e3 / steps, 2),
            "tokens": steps, "prefill": prefill, "bytes_per_token": int(per_token), "GB_s": round(gbs, 1),
            "frac_hbm": round(gbs / peak, 3),
-           "gpu_launches_per_token": 1 + 6 * m["layers"] + 2,
+           "gpu_launches_per_token": launches,
            "e2e": {"tokens_per_s": round(steps / e2e_s, 1), "h2d_bytes": 8, "d2h_bytes": 4 * steps},
            "same_tokens_e2e": bool(np.array_equal(toks, toks_e2e)), "next_position": pos,
            "timing": "CUDA events around graph replays (one stream)", "device_status": status,

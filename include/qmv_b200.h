@@ -275,6 +275,8 @@ int qmv_qwen2_replay(QmvQwen2 *decoder, int steps, void *stream);
 int qmv_qwen2_read(QmvQwen2 *decoder, int *tokens, int count, int *position);
 /* Host copy of one layer's cached key and value at `position`. */
 int qmv_qwen2_get_kv(QmvQwen2 *decoder, int layer, int position, float *key, float *value);
+/* Kernel launches in one captured step (0 on a null decoder). */
+int qmv_qwen2_kernels_per_step(const QmvQwen2 *decoder);
 int qmv_qwen2_destroy(QmvQwen2 *decoder);
 
 #ifdef __cplusplus

@@ -49,7 +49,8 @@ C_SYMBOLS = [
     "qmv_argmax_noalloc", "qmv_key_to_token", "qmv_greedy_sample",
     "qmv_quantized_tensor_matvec_f32", "qmv_quantized_tensor_matmul_f32",
     "qmv_qwen2_create", "qmv_qwen2_set_kv", "qmv_qwen2_forward", "qmv_qwen2_generate", "qmv_qwen2_begin",
-    "qmv_qwen2_replay", "qmv_qwen2_read", "qmv_qwen2_get_kv", "qmv_qwen2_destroy",
+    "qmv_qwen2_replay", "qmv_qwen2_read", "qmv_qwen2_get_kv", "qmv_qwen2_kernels_per_step",
+    "qmv_qwen2_destroy",
 ]
 CXX_DROPIN_SYMBOLS = {
     "quantized_tensor_matvec_f32": "_Z27quantized_tensor_matvec_f32PK23GgufQuantizedTensorViewPKfiPfi",
@@ -148,6 +149,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "qmv_qwen2_replay": (I, [P, I, P]),
         "qmv_qwen2_read": (I, [P, P, I, IP]),
         "qmv_qwen2_get_kv": (I, [P, I, I, P, P]),
+        "qmv_qwen2_kernels_per_step": (I, [P]),
         "qmv_qwen2_destroy": (I, [P]),
     }
     for name, (res, args) in sigs.items():
@@ -493,6 +495,14 @@ class Qwen2Decoder:
         _check(lib().qmv_qwen2_get_kv(self.handle, layer, position, k.ctypes.data, v.ctypes.data),
                "qmv_qwen2_get_kv")
         return k, v
+
+    @property
+    def kernels_per_step(self) -> int:
+        """Kernel launches in one captured decode step."""
+        n = lib().qmv_qwen2_kernels_per_step(self.handle)
+        if n <= 0:
+            raise RuntimeError(last_error())
+        return n
 
     def close(self) -> None:
         if self.handle:

@@ -105,6 +105,12 @@ cudaError_t launch_gemv(const Layout &L, const uint8_t *w, const float *x, float
 // (cudaErrorNotSupported when its stages do not fit).
 cudaError_t launch_gemv_fused(const Layout &L, const uint8_t *w, const float *x, float *y,
                               const ArgmaxOut *am, const Fuse &fu, cudaStream_t s);
+// Two matrices of different formats and equal columns over one x in one
+// launch (ya = Wa x', yb = Wb x', x' = x through fu's RMSNorm prologue, no
+// epilogue); the SMs are split between them by bytes.  cudaErrorNotSupported
+// when no common 16-warp plan fits (launch the two separately).
+cudaError_t launch_gemv_pair(const Layout &La, const uint8_t *wa, float *ya, const Layout &Lb, const uint8_t *wb,
+                             float *yb, const float *x, const Fuse &fu, cudaStream_t s);
 // Fused projection + argmax + exchange: y is this rank's slot in its own
 // buffer; needs the TMA pipeline (cudaErrorNotSupported when its stages do
 // not fit).

@@ -915,30 +915,37 @@ struct TmaPlan {
 // each row, taking alternate 32-chunk blocks; the second warp's sum reaches
 // the first through shared memory, handed over with a pair of mbarriers per
 // stage parity (bounded waits, like every other wait here).
+// The statically sized shared state of one GEMV CTA.
+struct TmaShared {
+    unsigned long long bars[2 * 8 + 4];  // full[8] | empty[8] | pfull[2] | pfree[2]
+    unsigned long long kscratch[kMaxConsumerWarps + 1];
+    float partial[2][kMaxConsumerWarps];
+    float sumsq[kMaxConsumerWarps];
+};
+
+// One CTA (number cta of ncta sharing the matrix) of the TMA GEMV; smem is
+// the dynamic shared memory (quantized x, then the stage ring).
 template <uint32_t FMT, int CW, int R, int NP = 1, int SPLIT = 1>
-__global__ void __launch_bounds__((CW + 1) * 32, 1)
-gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x,
-                float *__restrict__ y, ArgmaxOut am, int want_argmax, TmaPlan P, Exchange ex, Fuse fu)
+__device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int cta, int ncta, const Layout &L,
+                                              const uint8_t *__restrict__ w, const float *__restrict__ x,
+                                              float *__restrict__ y_, const ArgmaxOut &am, int want_argmax,
+                                              const TmaPlan &P, const Exchange &ex, const Fuse &fu)
 {
     static_assert(R * NP <= 32, "one lane per (row, position) output");
     static_assert(SPLIT == 1 || (SPLIT == 2 && R == 1 && NP == 1 && CW % 2 == 0), "split rows: one row per warp pair");
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) unsigned long long bars[2 * 8 + 4];  // full[8] | empty[8] | pfull[2] | pfree[2]
-    __shared__ unsigned long long kscratch[kMaxConsumerWarps + 1];
-    __shared__ float partial[2][kMaxConsumerWarps];
-    __shared__ float sumsq[kMaxConsumerWarps];
+    float *y = y_;
     constexpr int kConsumerWarps = CW;
     constexpr int NSL = W<FMT>::kSlices;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int C = L.C;
     const int NS = P.stages;
     const uint32_t stage0 = (uint32_t)__cvta_generic_to_shared(smem + P.x_bytes);
-    const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(&bars[0]);
+    const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(&sh.bars[0]);
     const uint32_t empty0 = full0 + 8u * 8u;
     const uint32_t pbar0 = full0 + 16u * 8u;
 
-    const int r0 = (int)((long long)L.rows * blockIdx.x / gridDim.x);
-    const int r1 = (int)((long long)L.rows * (blockIdx.x + 1) / gridDim.x);
+    const int r0 = (int)((long long)L.rows * cta / ncta);
+    const int r1 = (int)((long long)L.rows * (cta + 1) / ncta);
     const int SR = P.rows_per_stage;
     const int n_stages = (r1 - r0 + SR - 1) / SR;
     // Programmatic dependent launch: the next launch in the stream may start
@@ -1007,10 +1014,10 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
             for (int i = threadIdx.x; i < L.cols; i += CW * 32) ss += x[i] * x[i];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
-            if (lane == 0) sumsq[warp] = ss;
+            if (lane == 0) sh.sumsq[warp] = ss;
             asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
             ss = 0.f;
-            for (int i = 0; i < CW; ++i) ss += sumsq[i];
+            for (int i = 0; i < CW; ++i) ss += sh.sumsq[i];
             denom = sqrtf(ss / (float)L.cols + fu.eps);
         }
         quantize_x<FMT, CW * 32>(x, L.cols, C, smem, NP == 1 ? 1 : P.np, xb, NP == 1 ? fu.pre : kPreNone, denom,
@@ -1084,12 +1091,12 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
                 if (half == 1) {
                     // free once the partners have read stage k - 2
                     if (k >= 2) okp = mbar_wait(pfree, (uint32_t)(((k >> 1) - 1) & 1));
-                    if (okp && lane == 0) partial[pb][rw] = acc[0][0];
+                    if (okp && lane == 0) sh.partial[pb][rw] = acc[0][0];
                     __syncwarp();
                     if (lane == 0) mbar_arrive(pfull);
                 } else {
                     okp = mbar_wait(pfull, (uint32_t)((k >> 1) & 1));
-                    if (okp) acc[0][0] += partial[pb][rw];
+                    if (okp) acc[0][0] += sh.partial[pb][rw];
                     __syncwarp();
                     if (lane == 0) mbar_arrive(pfree);
                 }
@@ -1121,9 +1128,48 @@ gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict
         exchange_rows(ex, par, ex.logits[par][ex.rank] + (size_t)ex.rank * ex.slot_rows, r0, r1);
     }
     if (want_argmax) {
-        best = block_max_key(best, kscratch);
-        finish_argmax(best, am, kscratch, &ex);
+        best = block_max_key(best, sh.kscratch);
+        finish_argmax(best, am, sh.kscratch, &ex);
     }
+}
+
+template <uint32_t FMT, int CW, int R, int NP = 1, int SPLIT = 1>
+__global__ void __launch_bounds__((CW + 1) * 32, 1)
+gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x,
+                float *__restrict__ y, ArgmaxOut am, int want_argmax, TmaPlan P, Exchange ex, Fuse fu)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ TmaShared sh;
+    gemv_tma_body<FMT, CW, R, NP, SPLIT>(smem, sh, (int)blockIdx.x, (int)gridDim.x, L, w, x, y, am, want_argmax, P,
+                                         ex, fu);
+}
+
+// Two matrices with one input in one launch (the decode step's gate and up
+// projections when their formats differ): CTAs [0, ctas0) take matrix 0, the
+// rest matrix 1, each with its own plan; both read x through the same
+// prologue (fu) and write their own output.
+struct GemvPair {
+    Layout L[2];
+    const uint8_t *w[2];
+    float *y[2];
+    TmaPlan P[2];
+    int ctas0;
+};
+
+template <uint32_t FA, uint32_t FB, int CW, int R>
+__global__ void __launch_bounds__((CW + 1) * 32, 1)
+gemv_pair_kernel(GemvPair pr, const float *__restrict__ x, Fuse fu)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ TmaShared sh;
+    const ArgmaxOut none{nullptr, nullptr, 0};
+    const Exchange solo{};
+    const int cta = (int)blockIdx.x;
+    if (cta < pr.ctas0)
+        gemv_tma_body<FA, CW, R>(smem, sh, cta, pr.ctas0, pr.L[0], pr.w[0], x, pr.y[0], none, 0, pr.P[0], solo, fu);
+    else
+        gemv_tma_body<FB, CW, R>(smem, sh, cta - pr.ctas0, (int)gridDim.x - pr.ctas0, pr.L[1], pr.w[1], x, pr.y[1],
+                                 none, 0, pr.P[1], solo, fu);
 }
 
 // ------------------------------------------------------------- matmul
@@ -2392,41 +2438,46 @@ int g_gemv_path = 0;  // 0 auto, 1 direct loads, 2 TMA pipeline
 // better than 8.  batched: the plan of the batched kernel (np positions of
 // x in shared memory, 8 consumer warps).  false when none fits (the
 // direct-load kernels run).
+constexpr uint32_t kTmaBudget = 227u * 1024u - 1024u;  // dynamic bytes, leaving static room
+
+// One candidate {consumer warps, rows per warp, minimum stages, warps per
+// row} for a matrix whose rows spread over ctas CTAs; false when its stages
+// do not fit.
+bool tma_candidate(const Layout &L, const int *cand, int np, long long ctas, TmaPlan *P)
+{
+    const uint32_t xb = (uint32_t)((xs_bytes(L.cols) * (size_t)np + 127) & ~(size_t)127);
+    if (xb >= kTmaBudget || ctas < 1) return false;
+    const int cw = cand[0], r = cand[1], min_stages = cand[2], split = cand[3];
+    const uint64_t sb = ((uint64_t)cw * r / split * L.row_stride + 127) & ~127ull;
+    const uint64_t ns = (kTmaBudget - xb) / sb;
+    if ((int)ns < min_stages) return false;
+    P->x_bytes = xb;
+    P->stage_bytes = (uint32_t)sb;
+    P->rows_per_stage = cw * r / split;
+    // no more stages than one CTA's rows fill, at least 2: small matrices then
+    // leave shared memory for the CTAs of the launches around them
+    const long long per_cta = ((long long)L.rows + ctas - 1) / ctas;
+    const long long need = (per_cta + P->rows_per_stage - 1) / P->rows_per_stage;
+    uint64_t cap = need < 2 ? 2 : (uint64_t)need;
+    if (cap > 8) cap = 8;
+    P->stages = (int)(ns > cap ? cap : ns);
+    P->consumer_warps = cw;
+    P->rows_per_warp = r;
+    P->np = np;
+    P->split = split;
+    return true;
+}
+
 bool tma_plan(const Layout &L, TmaPlan *P, int np = 1, bool batched = false)
 {
-    constexpr uint32_t kBudget = 227u * 1024u - 1024u;  // dynamic bytes, leaving static room
-    // {consumer warps, rows per warp, minimum stages, warps per row}
     static const int kCandidates[][4] = {{16, 2, 2, 1}, {8, 2, 3, 1}, {16, 1, 3, 1}, {8, 2, 2, 1},
                                          {16, 1, 2, 1}, {16, 1, 2, 2}, {8, 1, 2, 1}};
     // batched form: 8 consumer warps (its per-thread state is larger)
     static const int kBatchCandidates[][4] = {{8, 2, 2, 1}, {8, 1, 2, 1}};
-    const uint32_t xb = (uint32_t)((xs_bytes(L.cols) * (size_t)np + 127) & ~(size_t)127);
-    if (xb >= kBudget) return false;
+    const long long ctas = L.rows < sm_count() ? L.rows : sm_count();  // one CTA per SM
     const int n_cand = batched ? 2 : 7;
-    for (int ci = 0; ci < n_cand; ++ci) {
-        const int *cand = batched ? kBatchCandidates[ci] : kCandidates[ci];
-        const int cw = cand[0], r = cand[1], min_stages = cand[2], split = cand[3];
-        const uint64_t sb = ((uint64_t)cw * r / split * L.row_stride + 127) & ~127ull;
-        const uint64_t ns = (kBudget - xb) / sb;
-        if ((int)ns < min_stages) continue;
-        P->x_bytes = xb;
-        P->stage_bytes = (uint32_t)sb;
-        P->rows_per_stage = cw * r / split;
-        // no more stages than one CTA's rows fill (the grid has one CTA per
-        // SM), at least 2: small matrices then leave shared memory for the
-        // CTAs of the launches around them
-        const long long ctas = L.rows < sm_count() ? L.rows : sm_count();
-        const long long per_cta = ((long long)L.rows + ctas - 1) / ctas;
-        const long long need = (per_cta + P->rows_per_stage - 1) / P->rows_per_stage;
-        uint64_t cap = need < 2 ? 2 : (uint64_t)need;
-        if (cap > 8) cap = 8;
-        P->stages = (int)(ns > cap ? cap : ns);
-        P->consumer_warps = cw;
-        P->rows_per_warp = r;
-        P->np = np;
-        P->split = split;
-        return true;
-    }
+    for (int ci = 0; ci < n_cand; ++ci)
+        if (tma_candidate(L, batched ? kBatchCandidates[ci] : kCandidates[ci], np, ctas, P)) return true;
     return false;
 }
 
@@ -2490,6 +2541,49 @@ cudaError_t gemv_fused_fmt(const Layout &L, const uint8_t *w, const float *x, fl
     }
     if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 8, 2>(L, P, w, x, y, am, s, none, fu);
     return gemv_tma_go<FMT, 8, 1>(L, P, w, x, y, am, s, none, fu);
+}
+
+template <uint32_t FA, uint32_t FB, int R>
+cudaError_t gemv_pair_go(const GemvPair &pr, int grid, const float *x, const Fuse &fu, cudaStream_t s)
+{
+    auto kernel = gemv_pair_kernel<FA, FB, 16, R>;
+    size_t smem = 0;
+    for (int i = 0; i < 2; ++i) {
+        const size_t b = (size_t)pr.P[i].x_bytes + (size_t)pr.P[i].stages * pr.P[i].stage_bytes;
+        if (b > smem) smem = b;
+    }
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    e = allow_max_smem((const void *)kernel, dev);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(17 * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kernel, pr, x, fu);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// Both matrices take the same 16-warp shape (one block size per launch).
+template <uint32_t FA, uint32_t FB>
+cudaError_t gemv_pair_fmt(GemvPair pr, int grid, const float *x, const Fuse &fu, cudaStream_t s)
+{
+    static const int kPairCandidates[][4] = {{16, 2, 2, 1}, {16, 1, 3, 1}, {16, 1, 2, 1}};
+    for (const int *cand : kPairCandidates) {
+        if (!tma_candidate(pr.L[0], cand, 1, pr.ctas0, &pr.P[0]) ||
+            !tma_candidate(pr.L[1], cand, 1, grid - pr.ctas0, &pr.P[1]))
+            continue;
+        return cand[1] == 2 ? gemv_pair_go<FA, FB, 2>(pr, grid, x, fu, s) : gemv_pair_go<FA, FB, 1>(pr, grid, x, fu, s);
+    }
+    return cudaErrorNotSupported;
 }
 
 template <uint32_t FMT>
@@ -2885,6 +2979,46 @@ cudaError_t launch_gemv_fused(const Layout &L, const uint8_t *w, const float *x,
     case kQ6_K: return gemv_fused_fmt<kQ6_K>(L, w, x, y, am, fu, s);
     default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t launch_gemv_pair(const Layout &La, const uint8_t *wa, float *ya, const Layout &Lb, const uint8_t *wb,
+                             float *yb, const float *x, const Fuse &fu, cudaStream_t s)
+{
+    if (La.cols != Lb.cols || La.type == Lb.type || fu.add != nullptr || fu.pre == kPreSwiGlu)
+        return cudaErrorInvalidValue;
+    GemvPair pr = {};
+    // ordered by format, so one instantiation serves both orders
+    const bool swap = La.type > Lb.type;
+    pr.L[0] = swap ? Lb : La;
+    pr.L[1] = swap ? La : Lb;
+    pr.w[0] = swap ? wb : wa;
+    pr.w[1] = swap ? wa : wb;
+    pr.y[0] = swap ? yb : ya;
+    pr.y[1] = swap ? ya : yb;
+    // one CTA per SM, split between the matrices by their bytes
+    const long long sms = sm_count();
+    if (sms < 2) return cudaErrorNotSupported;
+    const double b0 = (double)pr.L[0].rows * (double)pr.L[0].row_stride;
+    const double b1 = (double)pr.L[1].rows * (double)pr.L[1].row_stride;
+    long long c0 = (long long)(sms * b0 / (b0 + b1) + 0.5);
+    if (c0 < 1) c0 = 1;
+    if (c0 > sms - 1) c0 = sms - 1;
+    if (c0 > pr.L[0].rows) c0 = pr.L[0].rows;
+    long long c1 = sms - c0;
+    if (c1 > pr.L[1].rows) c1 = pr.L[1].rows;
+    pr.ctas0 = (int)c0;
+    const int grid = (int)(c0 + c1);
+    const uint32_t t0 = pr.L[0].type, t1 = pr.L[1].type;
+#define QMV_PAIR(A, B) \
+    if (t0 == A && t1 == B) return gemv_pair_fmt<A, B>(pr, grid, x, fu, s);
+    QMV_PAIR(kQ5_0, kQ8_0)
+    QMV_PAIR(kQ5_0, kQ4_K)
+    QMV_PAIR(kQ5_0, kQ6_K)
+    QMV_PAIR(kQ8_0, kQ4_K)
+    QMV_PAIR(kQ8_0, kQ6_K)
+    QMV_PAIR(kQ4_K, kQ6_K)
+#undef QMV_PAIR
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_matmul(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,

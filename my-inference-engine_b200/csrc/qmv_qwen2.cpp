@@ -11,15 +11,16 @@
 //     GEMV [q; k; v]   RMSNorm(attn_norm) prologue, bias epilogue
 //     attention_kernel RoPE, KV-cache append, grouped-query attention
 //     GEMV o           residual epilogue (h += W_o att)
-//     GEMV gate, up    RMSNorm(ffn_norm) prologue
+//     GEMV [gate; up]  RMSNorm(ffn_norm) prologue (one paired launch when
+//                      their formats differ)
 //     GEMV down        SwiGLU prologue (up * silu(gate)), residual epilogue
 //   GEMV output        RMSNorm(output_norm) prologue, fused greedy argmax
 //   advance_kernel     argmax key -> next token, position + 1
 //
 // Token and position live in device memory, so the step is captured once into
 // a CUDA graph and replayed: generation runs token after token without the
-// host.  Weights are uploaded once (Q, K and V concatenated into one resident
-// tensor when they share a format); the KV cache is f32
+// host.  Weights are uploaded once (Q, K and V, and gate and up, concatenated
+// into one resident tensor each when they share a format); the KV cache is f32
 // [layer][max_context][n_kv_heads * head_dim] like the reference's
 // (src/qwen2_internal.h:33-39).
 #include <cuda_runtime.h>
@@ -41,6 +42,7 @@ namespace {
 struct Layer {
     QmvWeight *qkv = nullptr;                            // [q; k; v] when they share a format
     QmvWeight *q = nullptr, *k = nullptr, *v = nullptr;  // otherwise
+    QmvWeight *gate_up = nullptr;                        // [gate; up] when they share a format
     QmvWeight *o = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
     float *attn_norm = nullptr, *ffn_norm = nullptr, *bias_qkv = nullptr;
 };
@@ -71,6 +73,7 @@ struct QmvQwen2 {
     int *history = nullptr;
     cudaStream_t stream = nullptr;
     cudaGraphExec_t exec = nullptr;
+    int kernels_per_step = 0;  // kernel nodes of the captured step
     std::vector<void *> allocs;
     std::vector<QmvWeight *> weights;
 };
@@ -165,10 +168,21 @@ cudaError_t enqueue_step(QmvQwen2 *m)
                                       m->attn_cnt, m->att, m->stream);
         if (e == cudaSuccess) e = gemv(m, L.o, m->att, m->h, qmv::Fuse{qmv::kPreNone, nullptr, 0.f, nullptr, m->h});
         const qmv::Fuse pre_ffn{qmv::kPreRmsNorm, L.ffn_norm, c.rms_norm_epsilon, nullptr, nullptr};
-        if (e == cudaSuccess) e = gemv(m, L.gate, m->h, m->gate, pre_ffn);
-        if (e == cudaSuccess) e = gemv(m, L.up, m->h, m->up, pre_ffn);
+        // With [gate; up] resident as one matrix, up lands right after gate.
+        float *up = L.gate_up ? m->gate + c.hidden_dim : m->up;
+        if (L.gate_up) {
+            if (e == cudaSuccess) e = gemv(m, L.gate_up, m->h, m->gate, pre_ffn);
+        } else if (e == cudaSuccess) {
+            // different formats: one paired launch, else two
+            e = qmv::launch_gemv_pair(L.gate->L, L.gate->dev, m->gate, L.up->L, L.up->dev, m->up, m->h, pre_ffn,
+                                      m->stream);
+            if (e == cudaErrorNotSupported) {
+                e = gemv(m, L.gate, m->h, m->gate, pre_ffn);
+                if (e == cudaSuccess) e = gemv(m, L.up, m->h, m->up, pre_ffn);
+            }
+        }
         if (e == cudaSuccess)
-            e = gemv(m, L.down, m->gate, m->h, qmv::Fuse{qmv::kPreSwiGlu, nullptr, 0.f, m->up, m->h});
+            e = gemv(m, L.down, m->gate, m->h, qmv::Fuse{qmv::kPreSwiGlu, nullptr, 0.f, up, m->h});
     }
     const qmv::ArgmaxOut am{m->key, m->am_ws, 0};
     if (e == cudaSuccess)
@@ -256,9 +270,17 @@ int build(QmvQwen2 *m, const QmvQwen2Tensor *tensors, int count)
         const QmvQwen2Tensor *an = find(by, p + "attn_norm.weight", dim, 0);
         const QmvQwen2Tensor *fn = find(by, p + "ffn_norm.weight", dim, 0);
         if (!o || !g || !u || !d || !an || !fn) return 0;
+        if (g->ggml_type == u->ggml_type) {
+            const size_t bg = tensor_bytes(g), bu = tensor_bytes(u);
+            std::vector<unsigned char> cat(bg + bu);
+            memcpy(cat.data(), g->data, bg);
+            memcpy(cat.data() + bg, u->data, bu);
+            if (!upload_rows(m, g->ggml_type, dim, 2 * hid, cat.data(), &L.gate_up)) return 0;
+        } else if (!upload_rows(m, g->ggml_type, dim, hid, g->data, &L.gate) ||
+                   !upload_rows(m, u->ggml_type, dim, hid, u->data, &L.up)) {
+            return 0;
+        }
         if (!upload_rows(m, o->ggml_type, dim, dim, o->data, &L.o) ||
-            !upload_rows(m, g->ggml_type, dim, hid, g->data, &L.gate) ||
-            !upload_rows(m, u->ggml_type, dim, hid, u->data, &L.up) ||
             !upload_rows(m, d->ggml_type, hid, dim, d->data, &L.down) ||
             !upload_vector(m, (const float *)an->data, dim, &L.attn_norm, "attn_norm") ||
             !upload_vector(m, (const float *)fn->data, dim, &L.ffn_norm, "ffn_norm"))
@@ -269,7 +291,7 @@ int build(QmvQwen2 *m, const QmvQwen2Tensor *tensors, int count)
     if (!dalloc(m, (void **)&m->h, dim * sizeof(float), "activations") ||
         !dalloc(m, (void **)&m->qkv, (dim + 2 * kvd) * sizeof(float), "activations") ||
         !dalloc(m, (void **)&m->att, dim * sizeof(float), "activations") ||
-        !dalloc(m, (void **)&m->gate, wide * sizeof(float), "activations") ||
+        !dalloc(m, (void **)&m->gate, 2 * wide * sizeof(float), "activations") ||
         !dalloc(m, (void **)&m->up, wide * sizeof(float), "activations") ||
         !dalloc(m, (void **)&m->logits, (size_t)c.vocab_size * sizeof(float), "logits") ||
         !dalloc(m, (void **)&m->kc, cache, "key cache") || !dalloc(m, (void **)&m->vc, cache, "value cache") ||
@@ -299,6 +321,19 @@ int build(QmvQwen2 *m, const QmvQwen2Tensor *tensors, int count)
         return cuda_err("graph capture", e);
     }
     QW_CUDA(e2, "graph capture");
+    size_t n_nodes = 0;
+    cudaError_t e4 = cudaGraphGetNodes(graph, nullptr, &n_nodes);
+    std::vector<cudaGraphNode_t> nodes(n_nodes);
+    if (e4 == cudaSuccess && n_nodes > 0) e4 = cudaGraphGetNodes(graph, nodes.data(), &n_nodes);
+    for (size_t i = 0; e4 == cudaSuccess && i < n_nodes; ++i) {
+        cudaGraphNodeType t;
+        e4 = cudaGraphNodeGetType(nodes[i], &t);
+        if (e4 == cudaSuccess && t == cudaGraphNodeTypeKernel) ++m->kernels_per_step;
+    }
+    if (e4 != cudaSuccess) {
+        cudaGraphDestroy(graph);
+        return cuda_err("graph nodes", e4);
+    }
     const cudaError_t e3 = cudaGraphInstantiate(&m->exec, graph, 0);
     cudaGraphDestroy(graph);
     QW_CUDA(e3, "graph instantiate");
@@ -408,6 +443,12 @@ QMV_EXPORT int qmv_qwen2_get_kv(QmvQwen2 *m, int layer, int position, float *key
     QW_CUDA(cudaMemcpy(key, m->kc + off, (size_t)m->kvd * sizeof(float), cudaMemcpyDeviceToHost), "read kv");
     QW_CUDA(cudaMemcpy(value, m->vc + off, (size_t)m->kvd * sizeof(float), cudaMemcpyDeviceToHost), "read kv");
     return 1;
+}
+
+QMV_EXPORT int qmv_qwen2_kernels_per_step(const QmvQwen2 *m)
+{
+    if (m == nullptr) return qmv::set_error("null decoder");
+    return m->kernels_per_step;
 }
 
 QMV_EXPORT int qmv_qwen2_destroy(QmvQwen2 *m)

@@ -176,27 +176,29 @@ QWEN2_CONFIGS = {
 QWEN2_TYPES = dict(q=Q8_0, k=Q8_0, v=Q8_0, o=Q8_0, gate=Q8_0, up=Q5_0, down=Q5_0, embd=Q8_0, out=Q6_K)
 
 
-def qwen2_type(kind: str, cols: int) -> int:
-    """The format of a projection; a K-quant whose rows are not whole 256-weight
-    superblocks (the 896-wide output projection of Qwen2-0.5B) is stored as
-    Q8_0 instead, as GGUF converters do."""
-    t = QWEN2_TYPES[kind]
+def qwen2_type(kind: str, cols: int, types: dict = None) -> int:
+    """The format of a projection (QWEN2_TYPES, entries of `types` taking
+    precedence); a K-quant whose rows are not whole 256-weight superblocks (the
+    896-wide output projection of Qwen2-0.5B) is stored as Q8_0 instead, as
+    GGUF converters do."""
+    t = (types or {}).get(kind, QWEN2_TYPES[kind])
     if t in (Q4_K, Q6_K) and cols % 256:
         return Q8_0
     return t
 
 
-def make_qwen2(name: str = "cfg4_qwen2_0_5b", seed: int = 0) -> dict:
+def make_qwen2(name: str = "cfg4_qwen2_0_5b", seed: int = 0, types: dict = None) -> dict:
     """Synthetic model: config fields plus packed tensors as
     (ggml_type, rows, cols, blocks) and F32 vectors, in the reference's
-    tensor names (src/qwen2_architecture.cpp)."""
+    tensor names (src/qwen2_architecture.cpp).  `types` overrides formats by
+    projection kind (q, k, v, o, gate, up, down, embd, out)."""
     c = dict(QWEN2_CONFIGS[name])
     dim, hidden, kvd = c["dim"], c["hidden"], c["kv_heads"] * (c["dim"] // c["heads"])
     stream = [100]
 
     def packed(kind, rows, cols):
         stream[0] += 1
-        t = qwen2_type(kind, cols)
+        t = qwen2_type(kind, cols, types)
         return (t, rows, cols, make_blocks(t, rows, cols, seed=seed, stream=stream[0]))
 
     def vec(n, mean, std):

@@ -31,9 +31,9 @@ def _oracle_setup(wl, m, t0, max_ctx, seed):
     return ob, keys, vals, K, V
 
 
-def _teacher_forced(qmv, oracle, wl, name, t0, max_ctx, steps, seed=0, first=7):
-    ob, keys, vals, K, V = _oracle_setup(wl, wl.make_qwen2(name, seed=seed), t0, max_ctx, seed)
-    m = wl.make_qwen2(name, seed=seed)
+def _teacher_forced(qmv, oracle, wl, name, t0, max_ctx, steps, seed=0, first=7, types=None):
+    m = wl.make_qwen2(name, seed=seed, types=types)
+    ob, keys, vals, K, V = _oracle_setup(wl, m, t0, max_ctx, seed)
     model_c = ob.qwen2_oracle_model(m, max_ctx)
     dec = qmv.Qwen2Decoder(m, wl.qwen2_tensor_list(m), max_ctx)
     worst = []
@@ -69,6 +69,16 @@ def test_qwen2_decode_teacher_forced_small(cuda, qmv, oracle, workloads):
     print("relative logit error, relative top-2 gap per step:", worst)
 
 
+@pytest.mark.parametrize("gate,up", [("Q5_0", "Q5_0"), ("Q8_0", "Q8_0"), ("Q4_K", "Q6_K"),
+                                     ("Q6_K", "Q8_0"), ("Q5_0", "Q4_K")])
+def test_qwen2_gate_up_formats(cuda, qmv, oracle, workloads, gate, up):
+    """Gate and up in one launch: concatenated rows when their formats match,
+    one paired launch (SMs split by bytes) when they differ, in either order
+    of the format codes."""
+    types = dict(gate=getattr(workloads, gate), up=getattr(workloads, up))
+    _teacher_forced(qmv, oracle, workloads, "qwen2_tiny", t0=12, max_ctx=32, steps=3, seed=4, types=types)
+
+
 def test_qwen2_generate_equals_stepwise(cuda, qmv, workloads):
     """Graph-replayed generation (token fed back on the device) produces the
     same ids as one step at a time through the host."""
@@ -77,6 +87,8 @@ def test_qwen2_generate_equals_stepwise(cuda, qmv, workloads):
     dec = qmv.Qwen2Decoder(m, workloads.qwen2_tensor_list(m), 64)
     try:
         dec.set_kv(keys, vals)
+        # embedding, 5 per layer (gate and up share one launch), output, advance
+        assert dec.kernels_per_step == 1 + 5 * m["layers"] + 2
         gen = dec.generate(3, 12)
         dec.set_kv(keys, vals)
         tok, seq = 3, []
