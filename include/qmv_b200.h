@@ -277,6 +277,60 @@ int qmv_qwen2_read(QmvQwen2 *decoder, int *tokens, int count, int *position);
 int qmv_qwen2_get_kv(QmvQwen2 *decoder, int layer, int position, float *key, float *value);
 /* Kernel launches in one captured step (0 on a null decoder). */
 int qmv_qwen2_kernels_per_step(const QmvQwen2 *decoder);
+
+/* ---- GGUF model images ---------------------------------------------------
+ * The reference opens a model with gguf_open (src/gguf_reader.h:71,
+ * src/gguf_reader.cpp:617-786) and derives a packed view per projection call
+ * (gguf_get_quantized_tensor_view, src/gguf_reader.h:136-140, called from
+ * src/qwen2_architecture.cpp:585-595).  These parse the same GGUF v3 image
+ * with the same acceptance rules, walk its tensor directory once to make
+ * every packed tensor resident, and configure the Qwen2 decoder from its
+ * metadata. */
+typedef struct QmvGguf QmvGguf;
+
+/* One directory entry; name and data point into the handle / the image. */
+typedef struct QmvGgufTensor {
+    const char *name;
+    uint32_t ggml_type;        /* 0 F32, 6 Q5_0, 8 Q8_0, 12 Q4_K, 14 Q6_K */
+    uint32_t dimension_count;  /* 1..4; dimensions[0] is the row length */
+    uint64_t dimensions[4];
+    uint64_t offset;           /* from the start of the data section */
+    uint64_t byte_size;
+    const void *data;
+} QmvGgufTensor;
+
+/* Parse an image the caller keeps mapped for the handle's lifetime
+ * (e.g. the reference's GgufFile::data / file_size). */
+int qmv_gguf_open(const void *data, uint64_t size, QmvGguf **gguf);
+/* Map `path` read-only and parse it; the handle owns the mapping. */
+int qmv_gguf_open_file(const char *path, QmvGguf **gguf);
+/* Also frees the resident weights keyed by addresses inside the image
+ * (made by qmv_gguf_upload or by drop-in calls on its views). */
+int qmv_gguf_close(QmvGguf *gguf);
+int qmv_gguf_info(const QmvGguf *gguf, uint64_t *tensor_count, uint64_t *metadata_count,
+                  uint64_t *data_offset, uint32_t *alignment);
+int qmv_gguf_tensor(const QmvGguf *gguf, uint64_t index, QmvGgufTensor *tensor);
+int qmv_gguf_find_tensor(const QmvGguf *gguf, const char *name, QmvGgufTensor *tensor);
+/* Metadata reads with the reference's rules (gguf_get_uint / _float /
+ * _string / _array_info, src/gguf_reader.h:73-90): 0 when the key is missing
+ * or of another type (no message; the output is left unchanged). */
+int qmv_gguf_get_uint(const QmvGguf *gguf, const char *key, uint64_t *value);
+int qmv_gguf_get_float(const QmvGguf *gguf, const char *key, double *value);
+int qmv_gguf_get_string(const QmvGguf *gguf, const char *key, const char **value, uint64_t *length);
+int qmv_gguf_get_array_info(const QmvGguf *gguf, const char *key, uint32_t *element_type, uint64_t *count);
+/* gguf_get_quantized_tensor_view (src/gguf_reader.h:136-140): the view is
+ * cleared on every failure (0, no message). */
+int qmv_gguf_quantized_view(const QmvGguf *gguf, const char *name, GgufQuantizedTensorView *view);
+/* Make every packed 2-D tensor resident on the calling thread's device,
+ * keyed by its mapped address (qmv_resident_weight); counts what is now
+ * resident.  For the reference: call after gguf_open in engine_load_model
+ * (src/engine.cpp:45-51) with the GgufFile's data and size. */
+int qmv_gguf_upload(const QmvGguf *gguf, int *tensors, uint64_t *device_bytes);
+/* A decoder configured from the image's qwen2.* metadata and vocabulary
+ * size (qwen2_configure_model, src/qwen2_architecture.cpp:105-257;
+ * engine_load_model, src/engine.cpp:64-72); 1 <= max_context <=
+ * qwen2.context_length (qwen2_state_init, :286-291). */
+int qmv_qwen2_create_from_gguf(const QmvGguf *gguf, int max_context, QmvQwen2 **decoder);
 int qmv_qwen2_destroy(QmvQwen2 *decoder);
 
 #ifdef __cplusplus

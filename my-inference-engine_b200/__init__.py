@@ -50,7 +50,9 @@ C_SYMBOLS = [
     "qmv_quantized_tensor_matvec_f32", "qmv_quantized_tensor_matmul_f32",
     "qmv_qwen2_create", "qmv_qwen2_set_kv", "qmv_qwen2_forward", "qmv_qwen2_generate", "qmv_qwen2_begin",
     "qmv_qwen2_replay", "qmv_qwen2_read", "qmv_qwen2_get_kv", "qmv_qwen2_kernels_per_step",
-    "qmv_qwen2_destroy",
+    "qmv_qwen2_destroy", "qmv_gguf_open", "qmv_gguf_open_file", "qmv_gguf_close", "qmv_gguf_info",
+    "qmv_gguf_tensor", "qmv_gguf_find_tensor", "qmv_gguf_get_uint", "qmv_gguf_get_float", "qmv_gguf_get_string",
+    "qmv_gguf_get_array_info", "qmv_gguf_quantized_view", "qmv_gguf_upload", "qmv_qwen2_create_from_gguf",
 ]
 CXX_DROPIN_SYMBOLS = {
     "quantized_tensor_matvec_f32": "_Z27quantized_tensor_matvec_f32PK23GgufQuantizedTensorViewPKfiPfi",
@@ -70,6 +72,20 @@ class GgufQuantizedTensorView(ctypes.Structure):
         ("block_elements", ctypes.c_uint64),
         ("block_bytes", ctypes.c_uint64),
         ("block_count", ctypes.c_uint64),
+    ]
+
+
+class QmvGgufTensor(ctypes.Structure):
+    """One tensor-directory entry of a GGUF image (include/qmv_b200.h)."""
+
+    _fields_ = [
+        ("name", ctypes.c_char_p),
+        ("ggml_type", ctypes.c_uint32),
+        ("dimension_count", ctypes.c_uint32),
+        ("dimensions", ctypes.c_uint64 * 4),
+        ("offset", ctypes.c_uint64),
+        ("byte_size", ctypes.c_uint64),
+        ("data", ctypes.c_void_p),
     ]
 
 
@@ -151,6 +167,20 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "qmv_qwen2_get_kv": (I, [P, I, I, P, P]),
         "qmv_qwen2_kernels_per_step": (I, [P]),
         "qmv_qwen2_destroy": (I, [P]),
+        "qmv_gguf_open": (I, [P, U64, ctypes.POINTER(P)]),
+        "qmv_gguf_open_file": (I, [ctypes.c_char_p, ctypes.POINTER(P)]),
+        "qmv_gguf_close": (I, [P]),
+        "qmv_gguf_info": (I, [P, ctypes.POINTER(U64), ctypes.POINTER(U64), ctypes.POINTER(U64),
+                              ctypes.POINTER(U32)]),
+        "qmv_gguf_tensor": (I, [P, U64, ctypes.POINTER(QmvGgufTensor)]),
+        "qmv_gguf_find_tensor": (I, [P, ctypes.c_char_p, ctypes.POINTER(QmvGgufTensor)]),
+        "qmv_gguf_get_uint": (I, [P, ctypes.c_char_p, ctypes.POINTER(U64)]),
+        "qmv_gguf_get_float": (I, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]),
+        "qmv_gguf_get_string": (I, [P, ctypes.c_char_p, ctypes.POINTER(P), ctypes.POINTER(U64)]),
+        "qmv_gguf_get_array_info": (I, [P, ctypes.c_char_p, ctypes.POINTER(U32), ctypes.POINTER(U64)]),
+        "qmv_gguf_quantized_view": (I, [P, ctypes.c_char_p, VP]),
+        "qmv_gguf_upload": (I, [P, IP, ctypes.POINTER(U64)]),
+        "qmv_qwen2_create_from_gguf": (I, [P, I, ctypes.POINTER(P)]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
@@ -504,7 +534,109 @@ class Qwen2Decoder:
             raise RuntimeError(last_error())
         return n
 
+    @classmethod
+    def from_gguf(cls, gguf: "GgufFile", max_context: int) -> "Qwen2Decoder":
+        """A decoder configured and filled from a GGUF image (qwen2.* metadata,
+        vocabulary size from tokenizer.ggml.tokens)."""
+        h = ctypes.c_void_p()
+        _check(lib().qmv_qwen2_create_from_gguf(gguf.handle, max_context, ctypes.byref(h)),
+               "qmv_qwen2_create_from_gguf")
+        self = cls.__new__(cls)
+        self.handle = h.value
+        self.vocab = gguf.get_array_info("tokenizer.ggml.tokens")[1]
+        dim = gguf.get_uint("qwen2.embedding_length")
+        self.kv_dim = gguf.get_uint("qwen2.attention.head_count_kv") * (dim // gguf.get_uint("qwen2.attention.head_count"))
+        return self
+
     def close(self) -> None:
         if self.handle:
             _check(lib().qmv_qwen2_destroy(self.handle), "qmv_qwen2_destroy")
             self.handle = None
+
+
+class GgufFile:
+    """A parsed GGUF v3 model image (qmv_gguf_*): the reference's gguf_open
+    acceptance rules, its metadata reads and packed views, and the walk that
+    makes every packed tensor resident on the current device.
+
+    ``GgufFile(path)`` maps the file; ``GgufFile(data=buffer)`` parses bytes
+    the object keeps alive."""
+
+    def __init__(self, path: str = None, data=None):
+        h = ctypes.c_void_p()
+        self._buf = None
+        if path is not None:
+            _check(lib().qmv_gguf_open_file(os.fsencode(path), ctypes.byref(h)), "qmv_gguf_open_file")
+        else:
+            self._buf = np.frombuffer(bytes(data), dtype=np.uint8) if not isinstance(data, np.ndarray) else data
+            _check(lib().qmv_gguf_open(self._buf.ctypes.data, self._buf.nbytes, ctypes.byref(h)), "qmv_gguf_open")
+        self.handle = h.value
+
+    def info(self) -> dict:
+        n_t, n_m, off = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+        align = ctypes.c_uint32()
+        _check(lib().qmv_gguf_info(self.handle, ctypes.byref(n_t), ctypes.byref(n_m), ctypes.byref(off),
+                                   ctypes.byref(align)), "qmv_gguf_info")
+        return dict(tensor_count=n_t.value, metadata_count=n_m.value, data_offset=off.value,
+                    alignment=align.value)
+
+    @staticmethod
+    def _tensor_dict(t: QmvGgufTensor) -> dict:
+        return dict(name=t.name.decode(), ggml_type=t.ggml_type,
+                    dimensions=[t.dimensions[i] for i in range(t.dimension_count)], offset=t.offset,
+                    byte_size=t.byte_size, data=t.data)
+
+    def tensors(self) -> list:
+        out = []
+        for i in range(self.info()["tensor_count"]):
+            t = QmvGgufTensor()
+            _check(lib().qmv_gguf_tensor(self.handle, i, ctypes.byref(t)), "qmv_gguf_tensor")
+            out.append(self._tensor_dict(t))
+        return out
+
+    def find_tensor(self, name: str) -> dict:
+        t = QmvGgufTensor()
+        _check(lib().qmv_gguf_find_tensor(self.handle, name.encode(), ctypes.byref(t)), "qmv_gguf_find_tensor")
+        return self._tensor_dict(t)
+
+    def get_uint(self, key: str):
+        v = ctypes.c_uint64()
+        return v.value if lib().qmv_gguf_get_uint(self.handle, key.encode(), ctypes.byref(v)) else None
+
+    def get_float(self, key: str):
+        v = ctypes.c_double()
+        return v.value if lib().qmv_gguf_get_float(self.handle, key.encode(), ctypes.byref(v)) else None
+
+    def get_string(self, key: str):
+        p, n = ctypes.c_void_p(), ctypes.c_uint64()
+        if not lib().qmv_gguf_get_string(self.handle, key.encode(), ctypes.byref(p), ctypes.byref(n)):
+            return None
+        return ctypes.string_at(p.value, n.value) if n.value else b""
+
+    def get_array_info(self, key: str):
+        t, n = ctypes.c_uint32(), ctypes.c_uint64()
+        if not lib().qmv_gguf_get_array_info(self.handle, key.encode(), ctypes.byref(t), ctypes.byref(n)):
+            return None
+        return t.value, n.value
+
+    def quantized_view(self, name: str):
+        """The packed view (GgufQuantizedTensorView) of a tensor, or None."""
+        v = GgufQuantizedTensorView()
+        return v if lib().qmv_gguf_quantized_view(self.handle, name.encode(), ctypes.byref(v)) else None
+
+    def upload(self):
+        """Make every packed 2-D tensor resident; (tensors, device bytes)."""
+        n, b = ctypes.c_int(), ctypes.c_uint64()
+        _check(lib().qmv_gguf_upload(self.handle, ctypes.byref(n), ctypes.byref(b)), "qmv_gguf_upload")
+        return n.value, b.value
+
+    def close(self) -> None:
+        if self.handle:
+            _check(lib().qmv_gguf_close(self.handle), "qmv_gguf_close")
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()

@@ -16,7 +16,7 @@ REPO_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_PATH = os.path.join(PKG_DIR, "libqmv_b200.so")
 
-SOURCES = ["qmv_kernels.cu", "qmv_capi.cpp", "qmv_qwen2.cpp", "quantized_matvec.cpp"]
+SOURCES = ["qmv_kernels.cu", "qmv_capi.cpp", "qmv_qwen2.cpp", "qmv_gguf.cpp", "quantized_matvec.cpp"]
 HEADERS = ["qmv_internal.h"]
 PUBLIC_HEADERS = ["qmv_b200.h", "quantized_matvec.h", "gguf_quantized_view.h"]
 

@@ -207,6 +207,27 @@ int decode_key(unsigned long long key, int *id)
 
 namespace qmv {
 int set_error(const char *msg) { return fail("%s", msg); }
+
+int release_resident_range(const void *begin, const void *end)
+{
+    std::lock_guard<std::mutex> lock(g_reg_mutex);
+    int n = 0, prev = -1;
+    for (auto it = g_registry.begin(); it != g_registry.end();) {
+        const char *p = (const char *)std::get<1>(it->first);
+        if (p < (const char *)begin || p >= (const char *)end) {
+            ++it;
+            continue;
+        }
+        if (prev < 0 && cudaGetDevice(&prev) != cudaSuccess) prev = 0;
+        cudaSetDevice(it->second->device);
+        cudaFree(it->second->dev);
+        delete it->second;
+        it = g_registry.erase(it);
+        ++n;
+    }
+    if (prev >= 0) cudaSetDevice(prev);
+    return n;
+}
 int set_cuda_error(const char *what, cudaError_t e) { return cuda_fail(what, e); }
 }  // namespace qmv
 

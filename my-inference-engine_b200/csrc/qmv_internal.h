@@ -161,6 +161,9 @@ cudaError_t launch_argmax_noalloc(const float *logits, int n, int index_base, un
 // Per-thread error message of the C ABI (qmv_last_error); both return 0.
 int set_error(const char *msg);
 int set_cuda_error(const char *what, cudaError_t e);
+// Free every registry-owned resident weight whose host key lies in
+// [begin, end) (an image that is being unmapped); returns how many.
+int release_resident_range(const void *begin, const void *end);
 
 }  // namespace qmv
 

@@ -246,3 +246,94 @@ def qwen2_tensor_list(m: dict):
     out.append(("output_norm.weight", 0, m["out_norm"].size, 0, m["out_norm"]))
     out.append(("output.weight", m["out"][0], m["out"][2], m["out"][1], m["out"][3]))
     return out
+
+
+# ------------------------------------------------------------- GGUF images
+#
+# GGUF v3 as the reference reads it (src/gguf_reader.cpp): "GGUF", u32
+# version, u64 tensor count, u64 metadata count; metadata entries (string key,
+# u32 value type, value); tensor entries (string name, u32 dimension count,
+# u64 dimensions, u32 type, u64 offset into the data section); the data
+# section at the directory's end rounded up to the alignment.  Little-endian;
+# strings are a u64 length and the bytes.
+
+GGUF_U8, GGUF_I8, GGUF_U16, GGUF_I16, GGUF_U32, GGUF_I32, GGUF_F32, GGUF_BOOL = range(8)
+GGUF_STRING, GGUF_ARRAY, GGUF_U64, GGUF_I64, GGUF_F64 = range(8, 13)
+_GGUF_PACK = {GGUF_U8: "<B", GGUF_I8: "<b", GGUF_U16: "<H", GGUF_I16: "<h", GGUF_U32: "<I", GGUF_I32: "<i",
+              GGUF_F32: "<f", GGUF_BOOL: "<B", GGUF_U64: "<Q", GGUF_I64: "<q", GGUF_F64: "<d"}
+
+
+def _gguf_string(s) -> bytes:
+    import struct
+    b = s.encode() if isinstance(s, str) else bytes(s)
+    return struct.pack("<Q", len(b)) + b
+
+
+def _gguf_value(vtype: int, value) -> bytes:
+    """One metadata value; arrays are (element type, [values])."""
+    import struct
+    if vtype == GGUF_STRING:
+        return _gguf_string(value)
+    if vtype == GGUF_ARRAY:
+        etype, items = value
+        return struct.pack("<IQ", etype, len(items)) + b"".join(_gguf_value(etype, v) for v in items)
+    if vtype in _GGUF_PACK:
+        return struct.pack(_GGUF_PACK[vtype], value)
+    return b""  # unknown type: no value bytes
+
+
+def gguf_image(metadata, tensors, alignment: int = 32, version: int = 3, magic: bytes = b"GGUF",
+               tensor_count: int = None, metadata_count: int = None, truncate: int = 0) -> bytes:
+    """A GGUF image.  metadata: [(key, value type, value)]; tensors:
+    [(name, ggml type, dimensions, data bytes)] or with a fifth element, an
+    explicit offset (otherwise each tensor starts at the next multiple of
+    `alignment` in the data section).  The counts, magic, version and a
+    truncation of the last `truncate` bytes may be overridden to make
+    malformed images."""
+    import struct
+    head = magic + struct.pack("<IQQ", version, len(tensors) if tensor_count is None else tensor_count,
+                               len(metadata) if metadata_count is None else metadata_count)
+    meta = b"".join(_gguf_string(k) + struct.pack("<I", t) + _gguf_value(t, v) for k, t, v in metadata)
+    entries, blobs, at = [], [], 0
+    for t in tensors:
+        name, gtype, dims, data = t[:4]
+        data = bytes(np.ascontiguousarray(data).view(np.uint8)) if isinstance(data, np.ndarray) else bytes(data)
+        at = (at + alignment - 1) // alignment * alignment
+        off = t[4] if len(t) > 4 else at
+        entries.append(_gguf_string(name) + struct.pack("<I", len(dims)) +
+                       b"".join(struct.pack("<Q", d) for d in dims) + struct.pack("<IQ", gtype, off))
+        blobs.append((off, data))
+        if len(t) <= 4:  # an explicit offset does not grow the data section
+            at = max(at, off + len(data))
+    directory = head + meta + b"".join(entries)
+    start = (len(directory) + alignment - 1) // alignment * alignment
+    body = bytearray(at)
+    for off, data in blobs:
+        end = min(off + len(data), len(body))
+        if off < end:
+            body[off:end] = data[:end - off]
+    img = directory + b"\0" * (start - len(directory)) + bytes(body)
+    return img[:len(img) - truncate] if truncate else img
+
+
+def qwen2_gguf(m: dict, context_length: int = 32768, alignment: int = 32, token_strings: bool = True) -> bytes:
+    """A GGUF image of a make_qwen2 model: the metadata the reference's
+    Qwen2 backend reads (src/qwen2_architecture.cpp:132-150; the vocabulary
+    size is the length of tokenizer.ggml.tokens, src/engine.cpp:64-72; the
+    token strings are placeholders) and every tensor in its GGUF name."""
+    meta = [("general.architecture", GGUF_STRING, "qwen2"),
+            ("general.alignment", GGUF_U32, alignment),
+            ("qwen2.embedding_length", GGUF_U32, m["dim"]),
+            ("qwen2.feed_forward_length", GGUF_U32, m["hidden"]),
+            ("qwen2.block_count", GGUF_U32, m["layers"]),
+            ("qwen2.attention.head_count", GGUF_U32, m["heads"]),
+            ("qwen2.attention.head_count_kv", GGUF_U32, m["kv_heads"]),
+            ("qwen2.context_length", GGUF_U32, context_length),
+            ("qwen2.attention.layer_norm_rms_epsilon", GGUF_F32, m["eps"]),
+            ("qwen2.rope.freq_base", GGUF_F32, m["rope_base"]),
+            ("tokenizer.ggml.tokens", GGUF_ARRAY,
+             (GGUF_STRING, [f"<t{i}>" for i in range(m["vocab"])] if token_strings else []))]
+    tensors = []
+    for name, gtype, cols, rows, data in qwen2_tensor_list(m):
+        tensors.append((name, gtype, [cols] if rows == 0 else [cols, rows], data))
+    return gguf_image(meta, tensors, alignment=alignment)

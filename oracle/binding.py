@@ -292,3 +292,84 @@ class RefQwen2:
         if self.h:
             self.lib.ref_qwen2_destroy(self.h)
             self.h = None
+
+
+class RefGguf:
+    """The reference engine's own GGUF reader (gguf_open and accessors,
+    oracle/_ref) on a file; ``ok`` False when gguf_open rejected it, with
+    its message in ``error``."""
+
+    def __init__(self, path: str, lib_path: str = REF_SCALAR_SO):
+        L = ctypes.CDLL(lib_path)
+        U32, U64 = ctypes.c_uint32, ctypes.c_uint64
+        L.ref_gguf_open.restype = ctypes.c_void_p
+        L.ref_gguf_open.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int]
+        L.ref_gguf_close.argtypes = [ctypes.c_void_p]
+        L.ref_gguf_info.argtypes = [ctypes.c_void_p, ctypes.POINTER(U64), ctypes.POINTER(U64), ctypes.POINTER(U64),
+                                    ctypes.POINTER(U32)]
+        L.ref_gguf_tensor.argtypes = [ctypes.c_void_p, U64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(U32),
+                                      ctypes.POINTER(U32), ctypes.POINTER(U64), ctypes.POINTER(U64),
+                                      ctypes.POINTER(U64)]
+        L.ref_gguf_get_uint.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(U64)]
+        L.ref_gguf_get_float.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]
+        L.ref_gguf_get_string.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p),
+                                          ctypes.POINTER(U64)]
+        L.ref_gguf_get_array_info.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(U32),
+                                              ctypes.POINTER(U64)]
+        L.ref_gguf_quantized_view.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_void_p,
+                                              ctypes.POINTER(U64)]
+        self.lib = L
+        err = ctypes.create_string_buffer(512)
+        self.h = L.ref_gguf_open(os.fsencode(path), err, 512)
+        self.ok = bool(self.h)
+        self.error = err.value.decode()
+
+    def info(self) -> dict:
+        n_t, n_m, off, al = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint32()
+        self.lib.ref_gguf_info(self.h, ctypes.byref(n_t), ctypes.byref(n_m), ctypes.byref(off), ctypes.byref(al))
+        return dict(tensor_count=n_t.value, metadata_count=n_m.value, data_offset=off.value, alignment=al.value)
+
+    def tensors(self) -> list:
+        out = []
+        for i in range(self.info()["tensor_count"]):
+            name, t, nd = ctypes.c_char_p(), ctypes.c_uint32(), ctypes.c_uint32()
+            dims, off, nb = (ctypes.c_uint64 * 4)(), ctypes.c_uint64(), ctypes.c_uint64()
+            self.lib.ref_gguf_tensor(self.h, i, ctypes.byref(name), ctypes.byref(t), ctypes.byref(nd), dims,
+                                     ctypes.byref(off), ctypes.byref(nb))
+            out.append(dict(name=name.value.decode(), ggml_type=t.value, dimensions=list(dims[:nd.value]),
+                            offset=off.value, byte_size=nb.value))
+        return out
+
+    def get_uint(self, key: str):
+        v = ctypes.c_uint64()
+        return v.value if self.lib.ref_gguf_get_uint(self.h, key.encode(), ctypes.byref(v)) else None
+
+    def get_float(self, key: str):
+        v = ctypes.c_double()
+        return v.value if self.lib.ref_gguf_get_float(self.h, key.encode(), ctypes.byref(v)) else None
+
+    def get_string(self, key: str):
+        p, n = ctypes.c_void_p(), ctypes.c_uint64()
+        if not self.lib.ref_gguf_get_string(self.h, key.encode(), ctypes.byref(p), ctypes.byref(n)):
+            return None
+        return ctypes.string_at(p.value, n.value) if n.value else b""
+
+    def get_array_info(self, key: str):
+        t, n = ctypes.c_uint32(), ctypes.c_uint64()
+        if not self.lib.ref_gguf_get_array_info(self.h, key.encode(), ctypes.byref(t), ctypes.byref(n)):
+            return None
+        return t.value, n.value
+
+    def quantized_view(self, name: str, view_type):
+        """(view fields as a dict with the data offset in the image), or None."""
+        v, at = view_type(), ctypes.c_uint64()
+        if not self.lib.ref_gguf_quantized_view(self.h, name.encode(), ctypes.byref(v), ctypes.byref(at)):
+            return None
+        return dict(data_at=at.value, ggml_type=v.ggml_type, dimensions=list(v.dimensions[:v.dimension_count]),
+                    element_count=v.element_count, block_elements=v.block_elements, block_bytes=v.block_bytes,
+                    block_count=v.block_count)
+
+    def close(self):
+        if self.h:
+            self.lib.ref_gguf_close(self.h)
+            self.h = None
