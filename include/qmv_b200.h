@@ -218,6 +218,14 @@ int qmv_quantized_tensor_matvec_f32(const GgufQuantizedTensorView *matrix, const
 int qmv_quantized_tensor_matmul_f32(const GgufQuantizedTensorView *matrix, const float *inputs,
                                     int input_count, int batch_count, float *outputs,
                                     int output_count);
+/* Kernel-only timing of the calling thread's drop-in calls above, for the
+ * reference's per-format weight profile (OperationProfile.weight_*_seconds,
+ * include/metrics.h:15-20, filled around quantized_tensor_matvec_f32 at
+ * src/qwen2_architecture.cpp:603-614): with profiling on, each call
+ * brackets its kernels (not its host<->device copies) with CUDA events, and
+ * qmv_last_kernel_seconds returns that device time of the latest call. */
+int qmv_set_profiling(int enabled);
+int qmv_last_kernel_seconds(double *seconds);
 
 /* ---- device-resident Qwen2 decode step ------------------------------------
  * Replaces the Qwen2 implementation of ArchitectureOps.forward_token
@@ -277,6 +285,37 @@ int qmv_qwen2_read(QmvQwen2 *decoder, int *tokens, int count, int *position);
 int qmv_qwen2_get_kv(QmvQwen2 *decoder, int layer, int position, float *key, float *value);
 /* Kernel launches in one captured step (0 on a null decoder). */
 int qmv_qwen2_kernels_per_step(const QmvQwen2 *decoder);
+
+/* The reference's per-request operation profile, field for field
+ * (OperationProfile, include/metrics.h:6-25; per-format arrays indexed
+ * F32, Q5_0, Q8_0, Q4_K, Q6_K), so a pointer to the reference's struct may
+ * be passed.  Seconds here are device time from CUDA events. */
+typedef struct QmvOperationProfile {
+    int enabled;
+    double matvec_seconds;
+    double attention_seconds;
+    double rmsnorm_seconds;
+    double rope_seconds;
+    double output_seconds;
+    double sampling_seconds;
+    double weight_layer_seconds[5];
+    double weight_output_seconds[5];
+    unsigned long long weight_layer_calls[5];
+    unsigned long long weight_output_calls[5];
+    double forward_seconds;
+    unsigned long long forward_calls;
+    unsigned long long sampling_calls;
+} QmvOperationProfile;
+
+/* qmv_qwen2_forward with the step's device time added to `profile` by stage
+ * and weight format when profile->enabled (the reference's --profile
+ * accounting, src/qwen2_architecture.cpp:1225-1525 and :603-614).  The step
+ * runs un-captured with an event after each launch.  RMSNorm and RoPE are
+ * fused into the projection and attention kernels (their rows stay 0); a
+ * launch covering two formats splits its time by weight bytes; calls count
+ * weight matrices as the reference's per-matrix matvec calls do. */
+int qmv_qwen2_forward_profiled(QmvQwen2 *decoder, int token, float *logits, int *next_token,
+                               QmvOperationProfile *profile);
 
 /* ---- GGUF model images ---------------------------------------------------
  * The reference opens a model with gguf_open (src/gguf_reader.h:71,

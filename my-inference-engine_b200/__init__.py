@@ -53,6 +53,7 @@ C_SYMBOLS = [
     "qmv_qwen2_destroy", "qmv_gguf_open", "qmv_gguf_open_file", "qmv_gguf_close", "qmv_gguf_info",
     "qmv_gguf_tensor", "qmv_gguf_find_tensor", "qmv_gguf_get_uint", "qmv_gguf_get_float", "qmv_gguf_get_string",
     "qmv_gguf_get_array_info", "qmv_gguf_quantized_view", "qmv_gguf_upload", "qmv_qwen2_create_from_gguf",
+    "qmv_set_profiling", "qmv_last_kernel_seconds", "qmv_qwen2_forward_profiled",
 ]
 CXX_DROPIN_SYMBOLS = {
     "quantized_tensor_matvec_f32": "_Z27quantized_tensor_matvec_f32PK23GgufQuantizedTensorViewPKfiPfi",
@@ -87,6 +88,31 @@ class QmvGgufTensor(ctypes.Structure):
         ("byte_size", ctypes.c_uint64),
         ("data", ctypes.c_void_p),
     ]
+
+
+class QmvOperationProfile(ctypes.Structure):
+    """The reference's OperationProfile (include/metrics.h:6-25), field for
+    field; per-format arrays are indexed F32, Q5_0, Q8_0, Q4_K, Q6_K."""
+
+    _fields_ = [
+        ("enabled", ctypes.c_int),
+        ("matvec_seconds", ctypes.c_double),
+        ("attention_seconds", ctypes.c_double),
+        ("rmsnorm_seconds", ctypes.c_double),
+        ("rope_seconds", ctypes.c_double),
+        ("output_seconds", ctypes.c_double),
+        ("sampling_seconds", ctypes.c_double),
+        ("weight_layer_seconds", ctypes.c_double * 5),
+        ("weight_output_seconds", ctypes.c_double * 5),
+        ("weight_layer_calls", ctypes.c_ulonglong * 5),
+        ("weight_output_calls", ctypes.c_ulonglong * 5),
+        ("forward_seconds", ctypes.c_double),
+        ("forward_calls", ctypes.c_ulonglong),
+        ("sampling_calls", ctypes.c_ulonglong),
+    ]
+
+
+PROFILE_FORMATS = {0: 0, 6: 1, 8: 2, 12: 3, 14: 4}  # ggml type -> per-format index
 
 
 def make_view(ggml_type: int, data, rows: int, cols: int) -> GgufQuantizedTensorView:
@@ -181,6 +207,9 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "qmv_gguf_quantized_view": (I, [P, ctypes.c_char_p, VP]),
         "qmv_gguf_upload": (I, [P, IP, ctypes.POINTER(U64)]),
         "qmv_qwen2_create_from_gguf": (I, [P, I, ctypes.POINTER(P)]),
+        "qmv_set_profiling": (I, [I]),
+        "qmv_last_kernel_seconds": (I, [ctypes.POINTER(ctypes.c_double)]),
+        "qmv_qwen2_forward_profiled": (I, [P, I, P, IP, ctypes.POINTER(QmvOperationProfile)]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
@@ -534,6 +563,15 @@ class Qwen2Decoder:
             raise RuntimeError(last_error())
         return n
 
+    def forward_profiled(self, token: int, profile: QmvOperationProfile):
+        """forward() with the step's device time added to ``profile`` by the
+        reference's stages and weight formats (when profile.enabled)."""
+        logits = np.empty(self.vocab, dtype=np.float32)
+        nxt = ctypes.c_int(-1)
+        _check(lib().qmv_qwen2_forward_profiled(self.handle, token, logits.ctypes.data, ctypes.byref(nxt),
+                                                ctypes.byref(profile)), "qmv_qwen2_forward_profiled")
+        return logits, nxt.value
+
     @classmethod
     def from_gguf(cls, gguf: "GgufFile", max_context: int) -> "Qwen2Decoder":
         """A decoder configured and filled from a GGUF image (qwen2.* metadata,
@@ -640,3 +678,15 @@ class GgufFile:
 
     def __exit__(self, *exc):
         self.close()
+
+
+def set_profiling(enabled: bool) -> None:
+    """Kernel-only event timing of this thread's drop-in calls."""
+    _check(lib().qmv_set_profiling(1 if enabled else 0), "qmv_set_profiling")
+
+
+def last_kernel_seconds() -> float:
+    """Device time of the kernels of this thread's latest drop-in call."""
+    v = ctypes.c_double()
+    _check(lib().qmv_last_kernel_seconds(ctypes.byref(v)), "qmv_last_kernel_seconds")
+    return v.value

@@ -145,6 +145,7 @@ struct Staging {
     void *ws = nullptr;
     unsigned long long *dkey = nullptr;
     unsigned long long *hkey = nullptr;
+    cudaEvent_t ev[2] = {nullptr, nullptr};  // around the kernels (profiling)
 };
 
 struct StagingSet {
@@ -159,12 +160,45 @@ struct StagingSet {
             cudaFree(st.ws);
             cudaFree(st.dkey);
             cudaFreeHost(st.hkey);
+            for (cudaEvent_t ev : st.ev)
+                if (ev) cudaEventDestroy(ev);
             if (st.stream) cudaStreamDestroy(st.stream);
         }
     }
 };
 
 thread_local StagingSet g_staging;
+
+// Per-thread kernel timing of the host-pointer drop-in calls: when on, each
+// call brackets its kernels (not its copies) with events on its stream.
+thread_local bool g_profiling = false;
+thread_local double g_last_kernel_seconds = -1.0;
+
+int kernels_begin(Staging *st)
+{
+    if (!g_profiling) return 1;
+    for (cudaEvent_t &ev : st->ev)
+        if (ev == nullptr) QMV_CUDA(cudaEventCreate(&ev), "cudaEventCreate");
+    QMV_CUDA(cudaEventRecord(st->ev[0], st->stream), "cudaEventRecord");
+    return 1;
+}
+
+int kernels_end(Staging *st)
+{
+    if (!g_profiling) return 1;
+    QMV_CUDA(cudaEventRecord(st->ev[1], st->stream), "cudaEventRecord");
+    return 1;
+}
+
+// After the call's synchronisation.
+int kernels_elapsed(Staging *st)
+{
+    if (!g_profiling) return 1;
+    float ms = 0.f;
+    QMV_CUDA(cudaEventElapsedTime(&ms, st->ev[0], st->ev[1]), "cudaEventElapsedTime");
+    g_last_kernel_seconds = (double)ms * 1e-3;
+    return 1;
+}
 
 int staging(Staging **out)
 {
@@ -271,6 +305,21 @@ QMV_EXPORT int qmv_set_gemv_path(int path)
 {
     if (path < 0 || path > 2) return fail("gemv path must be 0, 1 or 2");
     qmv::set_gemv_path(path);
+    return 1;
+}
+
+QMV_EXPORT int qmv_set_profiling(int enabled)
+{
+    g_profiling = enabled != 0;
+    g_last_kernel_seconds = -1.0;
+    return 1;
+}
+
+QMV_EXPORT int qmv_last_kernel_seconds(double *seconds)
+{
+    if (seconds == nullptr) return fail("null output");
+    if (g_last_kernel_seconds < 0.0) return fail("no profiled call on this thread (qmv_set_profiling(1) first)");
+    *seconds = g_last_kernel_seconds;
     return 1;
 }
 
@@ -605,10 +654,12 @@ QMV_EXPORT int qmv_quantized_tensor_matvec_f32(const GgufQuantizedTensorView *ma
     if (!grow(&st->dx, &st->dx_cap, (size_t)cols) || !grow(&st->dy, &st->dy_cap, (size_t)rows)) return 0;
     cudaStream_t s = st->stream;
     QMV_CUDA(cudaMemcpyAsync(st->dx, input, sizeof(float) * cols, cudaMemcpyHostToDevice, s), "copy input");
+    if (!kernels_begin(st)) return 0;
     QMV_CUDA(qmv::launch_gemv(w->L, w->dev, st->dx, st->dy, nullptr, s), "gemv launch");
+    if (!kernels_end(st)) return 0;
     QMV_CUDA(cudaMemcpyAsync(output, st->dy, sizeof(float) * rows, cudaMemcpyDeviceToHost, s), "copy output");
     QMV_CUDA(cudaStreamSynchronize(s), "matvec");
-    return 1;
+    return kernels_elapsed(st);
 }
 
 QMV_EXPORT int qmv_quantized_tensor_matmul_f32(const GgufQuantizedTensorView *matrix, const float *inputs,
@@ -633,8 +684,10 @@ QMV_EXPORT int qmv_quantized_tensor_matmul_f32(const GgufQuantizedTensorView *ma
     if (!grow(&st->dx, &st->dx_cap, nx) || !grow(&st->dy, &st->dy_cap, ny)) return 0;
     cudaStream_t s = st->stream;
     QMV_CUDA(cudaMemcpyAsync(st->dx, inputs, sizeof(float) * nx, cudaMemcpyHostToDevice, s), "copy inputs");
+    if (!kernels_begin(st)) return 0;
     QMV_CUDA(qmv::launch_matmul(w->L, w->dev, st->dx, batch_count, st->dy, s), "matmul launch");
+    if (!kernels_end(st)) return 0;
     QMV_CUDA(cudaMemcpyAsync(outputs, st->dy, sizeof(float) * ny, cudaMemcpyDeviceToHost, s), "copy outputs");
     QMV_CUDA(cudaStreamSynchronize(s), "matmul");
-    return 1;
+    return kernels_elapsed(st);
 }

@@ -74,6 +74,7 @@ struct QmvQwen2 {
     cudaStream_t stream = nullptr;
     cudaGraphExec_t exec = nullptr;
     int kernels_per_step = 0;  // kernel nodes of the captured step
+    std::vector<cudaEvent_t> prof_events;  // profiled steps (created on first use)
     std::vector<void *> allocs;
     std::vector<QmvWeight *> weights;
 };
@@ -143,52 +144,107 @@ cudaError_t gemv(QmvQwen2 *m, const QmvWeight *w, const float *x, float *y, cons
     return qmv::launch_gemv_fused(w->L, w->dev, x, y, am, fu, m->stream);
 }
 
-// One decode step, enqueued on m->stream.
-cudaError_t enqueue_step(QmvQwen2 *m)
+// Profiled steps (never captured): an event after each launch, tagged with
+// the reference's stage it belongs to (include/metrics.h:6-25).  A launch of
+// two formats (the gate/up pair) splits its time between them by weight
+// bytes; `calls` counts weight matrices, as the reference counts its
+// per-matrix matvec calls.
+enum Stage : int { kStageEmbed, kStageLayerGemv, kStageAttention, kStageOutput, kStageSampling };
+struct Mark {
+    int stage;
+    uint32_t type[2];
+    double share0;  // of the time, to type[0]
+    int calls[2];
+};
+struct Marks {
+    int used = 0;  // events recorded; event 0 precedes the first launch
+    std::vector<Mark> what;  // what[i] ends at event i + 1
+};
+
+cudaError_t record(QmvQwen2 *m, Marks *mk)
+{
+    if ((size_t)mk->used == m->prof_events.size()) {
+        cudaEvent_t ev = nullptr;
+        const cudaError_t e = cudaEventCreate(&ev);
+        if (e != cudaSuccess) return e;
+        m->prof_events.push_back(ev);
+    }
+    return cudaEventRecord(m->prof_events[(size_t)mk->used++], m->stream);
+}
+
+// After a successful launch, close its stage (no-op when not profiling).
+cudaError_t mark(QmvQwen2 *m, Marks *mk, cudaError_t launched, const Mark &w)
+{
+    if (mk == nullptr || launched != cudaSuccess) return launched;
+    mk->what.push_back(w);
+    return record(m, mk);
+}
+
+Mark layer_mark(const QmvWeight *w, int calls) { return Mark{kStageLayerGemv, {w->L.type, 0}, 1.0, {calls, 0}}; }
+
+// One decode step, enqueued on m->stream; mk != nullptr records the
+// profiling events of an un-captured step.
+cudaError_t enqueue_step(QmvQwen2 *m, Marks *mk = nullptr)
 {
     const QmvQwen2Config &c = m->cfg;
     const int dim = c.dim, kvd = m->kvd;
-    cudaError_t e = qmv::launch_embed(m->embd->L, m->embd->dev, m->st, m->h, m->stream);
+    cudaError_t e = mk ? record(m, mk) : cudaSuccess;
+    if (e == cudaSuccess)
+        e = mark(m, mk, qmv::launch_embed(m->embd->L, m->embd->dev, m->st, m->h, m->stream),
+                 Mark{kStageEmbed, {0, 0}, 1.0, {0, 0}});
     for (int l = 0; l < c.n_layers && e == cudaSuccess; ++l) {
         const Layer &L = m->layers[(size_t)l];
         qmv::Fuse pre_attn{qmv::kPreRmsNorm, L.attn_norm, c.rms_norm_epsilon, nullptr, L.bias_qkv};
         if (L.qkv) {
-            e = gemv(m, L.qkv, m->h, m->qkv, pre_attn);
+            e = mark(m, mk, gemv(m, L.qkv, m->h, m->qkv, pre_attn), layer_mark(L.qkv, 3));
         } else {
-            e = gemv(m, L.q, m->h, m->qkv, pre_attn);
+            e = mark(m, mk, gemv(m, L.q, m->h, m->qkv, pre_attn), layer_mark(L.q, 1));
             pre_attn.add = L.bias_qkv + dim;
-            if (e == cudaSuccess) e = gemv(m, L.k, m->h, m->qkv + dim, pre_attn);
+            if (e == cudaSuccess) e = mark(m, mk, gemv(m, L.k, m->h, m->qkv + dim, pre_attn), layer_mark(L.k, 1));
             pre_attn.add = L.bias_qkv + dim + kvd;
-            if (e == cudaSuccess) e = gemv(m, L.v, m->h, m->qkv + dim + kvd, pre_attn);
+            if (e == cudaSuccess)
+                e = mark(m, mk, gemv(m, L.v, m->h, m->qkv + dim + kvd, pre_attn), layer_mark(L.v, 1));
         }
         const size_t layer_off = (size_t)l * (size_t)c.max_context * (size_t)kvd;
         if (e == cudaSuccess)
-            e = qmv::launch_attention(m->qkv, c.n_heads, c.n_kv_heads, m->head_dim, m->kc + layer_off,
-                                      m->vc + layer_off, c.max_context, c.rope_frequency_base, m->st, m->attn_part,
-                                      m->attn_cnt, m->att, m->stream);
-        if (e == cudaSuccess) e = gemv(m, L.o, m->att, m->h, qmv::Fuse{qmv::kPreNone, nullptr, 0.f, nullptr, m->h});
+            e = mark(m, mk,
+                     qmv::launch_attention(m->qkv, c.n_heads, c.n_kv_heads, m->head_dim, m->kc + layer_off,
+                                           m->vc + layer_off, c.max_context, c.rope_frequency_base, m->st,
+                                           m->attn_part, m->attn_cnt, m->att, m->stream),
+                     Mark{kStageAttention, {0, 0}, 1.0, {0, 0}});
+        if (e == cudaSuccess)
+            e = mark(m, mk, gemv(m, L.o, m->att, m->h, qmv::Fuse{qmv::kPreNone, nullptr, 0.f, nullptr, m->h}),
+                     layer_mark(L.o, 1));
         const qmv::Fuse pre_ffn{qmv::kPreRmsNorm, L.ffn_norm, c.rms_norm_epsilon, nullptr, nullptr};
         // With [gate; up] resident as one matrix, up lands right after gate.
         float *up = L.gate_up ? m->gate + c.hidden_dim : m->up;
         if (L.gate_up) {
-            if (e == cudaSuccess) e = gemv(m, L.gate_up, m->h, m->gate, pre_ffn);
+            if (e == cudaSuccess) e = mark(m, mk, gemv(m, L.gate_up, m->h, m->gate, pre_ffn), layer_mark(L.gate_up, 2));
         } else if (e == cudaSuccess) {
             // different formats: one paired launch, else two
             e = qmv::launch_gemv_pair(L.gate->L, L.gate->dev, m->gate, L.up->L, L.up->dev, m->up, m->h, pre_ffn,
                                       m->stream);
             if (e == cudaErrorNotSupported) {
-                e = gemv(m, L.gate, m->h, m->gate, pre_ffn);
-                if (e == cudaSuccess) e = gemv(m, L.up, m->h, m->up, pre_ffn);
+                e = mark(m, mk, gemv(m, L.gate, m->h, m->gate, pre_ffn), layer_mark(L.gate, 1));
+                if (e == cudaSuccess) e = mark(m, mk, gemv(m, L.up, m->h, m->up, pre_ffn), layer_mark(L.up, 1));
+            } else {
+                const double bg = (double)L.gate->bytes, bu = (double)L.up->bytes;
+                e = mark(m, mk, e, Mark{kStageLayerGemv, {L.gate->L.type, L.up->L.type}, bg / (bg + bu), {1, 1}});
             }
         }
         if (e == cudaSuccess)
-            e = gemv(m, L.down, m->gate, m->h, qmv::Fuse{qmv::kPreSwiGlu, nullptr, 0.f, up, m->h});
+            e = mark(m, mk, gemv(m, L.down, m->gate, m->h, qmv::Fuse{qmv::kPreSwiGlu, nullptr, 0.f, up, m->h}),
+                     layer_mark(L.down, 1));
     }
     const qmv::ArgmaxOut am{m->key, m->am_ws, 0};
     if (e == cudaSuccess)
-        e = gemv(m, m->out, m->h, m->logits,
-                 qmv::Fuse{qmv::kPreRmsNorm, m->out_norm, c.rms_norm_epsilon, nullptr, nullptr}, &am);
-    if (e == cudaSuccess) e = qmv::launch_advance(m->key, m->st, m->history, c.max_context, m->stream);
+        e = mark(m, mk,
+                 gemv(m, m->out, m->h, m->logits,
+                      qmv::Fuse{qmv::kPreRmsNorm, m->out_norm, c.rms_norm_epsilon, nullptr, nullptr}, &am),
+                 Mark{kStageOutput, {m->out->L.type, 0}, 1.0, {1, 0}});
+    if (e == cudaSuccess)
+        e = mark(m, mk, qmv::launch_advance(m->key, m->st, m->history, c.max_context, m->stream),
+                 Mark{kStageSampling, {0, 0}, 1.0, {0, 0}});
     return e;
 }
 
@@ -215,6 +271,7 @@ int check_state(QmvQwen2 *m, qmv::DecodeState *out)
 
 void release(QmvQwen2 *m)
 {
+    for (cudaEvent_t ev : m->prof_events) cudaEventDestroy(ev);
     if (m->exec) cudaGraphExecDestroy(m->exec);
     for (QmvWeight *w : m->weights) qmv_weight_free(w);
     for (void *p : m->allocs) cudaFree(p);
@@ -419,6 +476,85 @@ QMV_EXPORT int qmv_qwen2_forward(QmvQwen2 *m, int token, float *logits, int *nex
     if (!set_token(m, token) || !qmv_qwen2_replay(m, 1, m->stream)) return 0;
     QW_CUDA(cudaStreamSynchronize(m->stream), "decode step");
     if (!check_state(m, nullptr)) return 0;
+    if (logits)
+        QW_CUDA(cudaMemcpy(logits, m->logits, (size_t)m->cfg.vocab_size * sizeof(float), cudaMemcpyDeviceToHost),
+                "read logits");
+    if (next_token) QW_CUDA(cudaMemcpy(next_token, m->history, sizeof(int), cudaMemcpyDeviceToHost), "read token");
+    return 1;
+}
+
+namespace {
+
+// Index of a weight format in the profile's per-format arrays
+// (PROFILE_F32 .. PROFILE_Q6_K, include/metrics.h:6-7); -1 otherwise.
+int profile_format(uint32_t type)
+{
+    switch (type) {
+    case 0: return 0;
+    case qmv::kQ5_0: return 1;
+    case qmv::kQ8_0: return 2;
+    case qmv::kQ4_K: return 3;
+    case qmv::kQ6_K: return 4;
+    default: return -1;
+    }
+}
+
+void add_weight(double *seconds, unsigned long long *calls, uint32_t type, double dt, int n)
+{
+    const int f = profile_format(type);
+    if (f < 0) return;
+    seconds[f] += dt;
+    calls[f] += (unsigned long long)n;
+}
+
+}  // namespace
+
+// One step like qmv_qwen2_forward, run un-captured with an event after each
+// launch; device times accumulate into `profile` by the reference's stages
+// when profile->enabled (otherwise a plain step).  RMSNorm and RoPE run inside
+// the projection and attention kernels, so their rows stay 0 and their time
+// is in matvec / attention; the fused greedy argmax is in output, and the
+// advance kernel that turns it into the next token is sampling.
+QMV_EXPORT int qmv_qwen2_forward_profiled(QmvQwen2 *m, int token, float *logits, int *next_token,
+                                          QmvOperationProfile *profile)
+{
+    if (m == nullptr) return qmv::set_error("null decoder");
+    if (profile == nullptr || !profile->enabled) return qmv_qwen2_forward(m, token, logits, next_token);
+    if (!set_token(m, token)) return 0;
+    Marks mk;
+    QW_CUDA(enqueue_step(m, &mk), "profiled decode step");
+    QW_CUDA(cudaStreamSynchronize(m->stream), "profiled decode step");
+    if (!check_state(m, nullptr)) return 0;
+    double forward = 0.0;
+    for (size_t i = 0; i < mk.what.size(); ++i) {
+        float ms = 0.f;
+        QW_CUDA(cudaEventElapsedTime(&ms, m->prof_events[i], m->prof_events[i + 1]), "profile events");
+        const double dt = (double)ms * 1e-3;
+        const Mark &w = mk.what[i];
+        switch (w.stage) {
+        case kStageLayerGemv:
+            profile->matvec_seconds += dt;
+            add_weight(profile->weight_layer_seconds, profile->weight_layer_calls, w.type[0], dt * w.share0,
+                       w.calls[0]);
+            if (w.calls[1] > 0)
+                add_weight(profile->weight_layer_seconds, profile->weight_layer_calls, w.type[1],
+                           dt * (1.0 - w.share0), w.calls[1]);
+            break;
+        case kStageAttention: profile->attention_seconds += dt; break;
+        case kStageOutput:
+            profile->output_seconds += dt;
+            add_weight(profile->weight_output_seconds, profile->weight_output_calls, w.type[0], dt, w.calls[0]);
+            break;
+        case kStageSampling:
+            profile->sampling_seconds += dt;
+            ++profile->sampling_calls;
+            break;
+        default: break;
+        }
+        if (w.stage != kStageSampling) forward += dt;  // forward stages exclude sampling
+    }
+    profile->forward_seconds += forward;
+    ++profile->forward_calls;
     if (logits)
         QW_CUDA(cudaMemcpy(logits, m->logits, (size_t)m->cfg.vocab_size * sizeof(float), cudaMemcpyDeviceToHost),
                 "read logits");

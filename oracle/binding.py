@@ -288,6 +288,17 @@ class RefQwen2:
         ok = self.lib.ref_qwen2_forward(self.h, token, logits.ctypes.data)
         return bool(ok), logits
 
+    def enable_profile(self) -> None:
+        self.lib.ref_qwen2_enable_profile.argtypes = [ctypes.c_void_p]
+        self.lib.ref_qwen2_enable_profile(self.h)
+
+    def read_profile(self, profile_type):
+        """The state's OperationProfile as a ctypes ``profile_type``."""
+        self.lib.ref_qwen2_read_profile.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        p = profile_type()
+        self.lib.ref_qwen2_read_profile(self.h, ctypes.byref(p))
+        return p
+
     def close(self):
         if self.h:
             self.lib.ref_qwen2_destroy(self.h)
@@ -373,3 +384,13 @@ class RefGguf:
         if self.h:
             self.lib.ref_gguf_close(self.h)
             self.h = None
+
+
+def reference_profile_layout(lib_path: str = REF_SCALAR_SO):
+    """sizeof(OperationProfile) and its field offsets, from the reference's
+    own header (include/metrics.h) as compiled in oracle/_ref."""
+    L = ctypes.CDLL(lib_path)
+    out = (ctypes.c_uint64 * 15)()
+    L.ref_operation_profile_layout.argtypes = [ctypes.c_void_p]
+    n_formats = L.ref_operation_profile_layout(out)
+    return list(out), n_formats

@@ -7,6 +7,7 @@
 // tests/forward_quantized_reference_test.cpp:26-117 assembles its fixture, with
 // the KV cache pre-filled through the private state
 // (src/qwen2_internal.h:21-52).  Nothing in the product links this file.
+#include <stddef.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -118,6 +119,22 @@ int ref_qwen2_forward(void *h, int token, float *logits)
     return 1;
 }
 
+// The reference's profile of this decoder state (enabled on first call):
+// its OperationProfile bytes are copied to `out` after the next
+// ref_qwen2_forward calls accumulate into it.
+void ref_qwen2_enable_profile(void *h)
+{
+    RefQwen2 *m = (RefQwen2 *)h;
+    memset(&m->state.profile, 0, sizeof(m->state.profile));
+    m->state.profile.enabled = 1;
+}
+
+void ref_qwen2_read_profile(void *h, void *out)
+{
+    RefQwen2 *m = (RefQwen2 *)h;
+    memcpy(out, &m->state.profile, sizeof(m->state.profile));
+}
+
 // KV entries of one layer and position (after a forward step wrote them).
 int ref_qwen2_get_kv(void *h, int layer, int position, float *key, float *value)
 {
@@ -128,6 +145,28 @@ int ref_qwen2_get_kv(void *h, int layer, int position, float *key, float *value)
     memcpy(key, s->keys + off, kvd * sizeof(float));
     memcpy(value, s->values + off, kvd * sizeof(float));
     return 1;
+}
+
+// sizeof(OperationProfile) and the offset of each field in declaration
+// order (include/metrics.h:8-25): 15 values.
+int ref_operation_profile_layout(uint64_t *out)
+{
+    out[0] = sizeof(OperationProfile);
+    out[1] = offsetof(OperationProfile, enabled);
+    out[2] = offsetof(OperationProfile, matvec_seconds);
+    out[3] = offsetof(OperationProfile, attention_seconds);
+    out[4] = offsetof(OperationProfile, rmsnorm_seconds);
+    out[5] = offsetof(OperationProfile, rope_seconds);
+    out[6] = offsetof(OperationProfile, output_seconds);
+    out[7] = offsetof(OperationProfile, sampling_seconds);
+    out[8] = offsetof(OperationProfile, weight_layer_seconds);
+    out[9] = offsetof(OperationProfile, weight_output_seconds);
+    out[10] = offsetof(OperationProfile, weight_layer_calls);
+    out[11] = offsetof(OperationProfile, weight_output_calls);
+    out[12] = offsetof(OperationProfile, forward_seconds);
+    out[13] = offsetof(OperationProfile, forward_calls);
+    out[14] = offsetof(OperationProfile, sampling_calls);
+    return PROFILE_WEIGHT_FORMAT_COUNT;
 }
 
 void ref_qwen2_destroy(void *h)
