@@ -661,6 +661,83 @@ def bench_qwen2_decode(qmv, steps=256, prefill=1024, cpu_seconds=5.0, cpu=True):
     return rec
 
 
+QWEN2_PREFILL = "cfg4_qwen2_0_5b_prefill1024"
+
+
+def bench_qwen2_prefill(qmv, prompt=1024, reps=5, cpu_seconds=5.0, cpu=True):
+    """Time to first token on the configuration-4 model: a `prompt`-token
+    prompt appended from position 0 through qmv_qwen2_prefill (every layer's
+    projections as batched matmuls over the 1024 positions, causal attention,
+    the last position's logits and greedy token).  value: prompt tokens per
+    second of device time (CUDA events on the decoder's stream around the
+    call); e2e: the same through the C ABI by wall clock, ids in and logits
+    out.  FLOPs: 2 x positions x layer weights, the output projection for the
+    last position, and 4 x heads x head_dim x visible keys per position and
+    layer for attention."""
+    import torch
+    wl = workloads()
+    m = wl.make_qwen2("cfg4_qwen2_0_5b", seed=0)
+    tensors = wl.qwen2_tensor_list(m)
+    ids = np.random.default_rng(0).integers(0, m["vocab"], prompt).astype(np.int32)
+    dec = qmv.Qwen2Decoder(m, tensors, prompt + 8)
+    dev_ms, wall_ms = [], []
+    try:
+        stream = torch.cuda.ExternalStream(dec.stream)
+        for _ in range(2):  # warm-up (buffers, dynamic shared memory limits, memory pool)
+            dec.reset()
+            dec.prefill(ids)
+        for _ in range(reps):
+            dec.reset()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            a.record(stream)
+            t0 = time.perf_counter()
+            _, tok = dec.prefill(ids)
+            wall_ms.append((time.perf_counter() - t0) * 1e3)
+            b.record(stream)
+            b.synchronize()
+            dev_ms.append(a.elapsed_time(b))
+        status = qmv.device_status(clear=True)
+    finally:
+        dec.close()
+    layer_w = sum(t[2] * t[3] for t in tensors if t[3] > 0 and t[0].startswith("blk."))
+    hd = m["dim"] // m["heads"]
+    attn = 4 * m["heads"] * hd * m["layers"] * prompt * (prompt + 1) / 2
+    flops = 2 * prompt * layer_w + 2 * m["vocab"] * m["dim"] + attn
+    ms = float(np.median(dev_ms))
+    peak, _ = measured_tensor_peak()
+    rec = {"tokens_per_s": round(prompt / (ms * 1e-3), 1), "ms_per_prompt": round(ms, 3),
+           "ms_min": round(min(dev_ms), 3), "prompt": prompt, "reps": reps,
+           "TFLOP_s": round(flops / (ms * 1e-3) / 1e12, 1), "GFLOP_per_prompt": round(flops / 1e9, 1),
+           "frac_tensor": round(flops / (ms * 1e-3) / 1e12 / peak, 3) if peak else None,
+           "e2e": {"tokens_per_s": round(prompt / (float(np.median(wall_ms)) * 1e-3), 1),
+                   "ms_per_prompt": round(float(np.median(wall_ms)), 3), "h2d_bytes": 4 * prompt,
+                   "d2h_bytes": 4 * m["vocab"]},
+           "next_token": tok, "device_status": status,
+           "timing": "CUDA events on the decoder stream around qmv_qwen2_prefill (median of reps)",
+           "model": "Qwen2-0.5B architecture, random-init (Q8_0 attention/gate/embedding/output, Q5_0 up/down)"}
+    if cpu:
+        binding = _load("qmv_oracle_binding", os.path.join(REPO, "oracle", "binding.py"))
+        if os.path.exists(binding.REF_AVX2_SO):
+            ref = binding.RefQwen2(m, tensors, prompt + 8, path=binding.REF_AVX2_SO)
+            try:
+                seg, n, t0 = 64, 0, time.perf_counter()
+                ref.reset()
+                while n + seg <= prompt and (time.perf_counter() - t0) < cpu_seconds:
+                    ok, _ = ref.prefill(ids[n:n + seg])
+                    assert ok
+                    n += seg
+                el = time.perf_counter() - t0
+            finally:
+                ref.close()
+            rec["cpu_baseline"] = {"value": round(n / el, 2), "unit": "tokens/s", "cores": os.cpu_count(),
+                                   "kind": "reference",
+                                   "sample": f"the first {n} prompt tokens in {seg}-token prefill_tokens calls "
+                                             f"(OpenMP AVX2 build, {el:.1f} s)"}
+    return rec
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -693,6 +770,8 @@ def main():
         qmv.set_device(local_rank)
         if args.only == QWEN2_DECODE:
             res = {QWEN2_DECODE: bench_qwen2_decode(qmv, steps=min(args.steps, 256), cpu=not args.no_cpu_baseline)}
+        elif args.only == QWEN2_PREFILL:
+            res = {QWEN2_PREFILL: bench_qwen2_prefill(qmv, cpu=not args.no_cpu_baseline)}
         else:
             res = extras_single_gpu(qmv, args.steps, args.only)
         print(json.dumps({"only": args.only, "result": res}), flush=True)
@@ -705,6 +784,7 @@ def main():
         qmv = load_qmv()
         result["configs"] = extras_single_gpu(qmv, steps=200)
         result["configs"][QWEN2_DECODE] = bench_qwen2_decode(qmv, cpu=not args.no_cpu_baseline)
+        result["configs"][QWEN2_PREFILL] = bench_qwen2_prefill(qmv, cpu=not args.no_cpu_baseline)
     if world == 1 and not args.no_cpu_baseline:
         wl = workloads()
         blocks = wl.make_blocks(Q6_K, VOCAB_ROWS, HIDDEN, seed=0)

@@ -283,6 +283,20 @@ int qmv_qwen2_replay(QmvQwen2 *decoder, int steps, void *stream);
 int qmv_qwen2_read(QmvQwen2 *decoder, int *tokens, int count, int *position);
 /* Host copy of one layer's cached key and value at `position`. */
 int qmv_qwen2_get_kv(QmvQwen2 *decoder, int layer, int position, float *key, float *value);
+/* The reference's prefill_tokens (src/architecture.h:78-79,
+ * qwen2_prefill_tokens, src/qwen2_architecture.cpp:1550-1729): append
+ * `count` prompt tokens at the current position -- their keys and values in
+ * every layer's cache -- and return the last position's logits (may be NULL)
+ * and greedy token.  Positions go through each layer in chunks of up to 1024,
+ * every projection one batched matmul (tensor cores from 32 positions).
+ * Same checks as the reference (ids, context capacity, non-finite logits);
+ * on failure the position is unchanged.  Continue with qmv_qwen2_generate /
+ * qmv_qwen2_forward from the returned token. */
+int qmv_qwen2_prefill(QmvQwen2 *decoder, const int *ids, int count, float *logits, int *next_token);
+/* The reference's state_reset (src/architecture.h:80-81): position 0. */
+int qmv_qwen2_reset(QmvQwen2 *decoder);
+/* The (non-blocking) stream the decoder's work runs on, as a cudaStream_t. */
+int qmv_qwen2_stream(const QmvQwen2 *decoder, void **stream);
 /* Kernel launches in one captured step (0 on a null decoder). */
 int qmv_qwen2_kernels_per_step(const QmvQwen2 *decoder);
 

@@ -53,7 +53,8 @@ C_SYMBOLS = [
     "qmv_qwen2_destroy", "qmv_gguf_open", "qmv_gguf_open_file", "qmv_gguf_close", "qmv_gguf_info",
     "qmv_gguf_tensor", "qmv_gguf_find_tensor", "qmv_gguf_get_uint", "qmv_gguf_get_float", "qmv_gguf_get_string",
     "qmv_gguf_get_array_info", "qmv_gguf_quantized_view", "qmv_gguf_upload", "qmv_qwen2_create_from_gguf",
-    "qmv_set_profiling", "qmv_last_kernel_seconds", "qmv_qwen2_forward_profiled",
+    "qmv_set_profiling", "qmv_last_kernel_seconds", "qmv_qwen2_forward_profiled", "qmv_qwen2_prefill",
+    "qmv_qwen2_reset", "qmv_qwen2_stream",
 ]
 CXX_DROPIN_SYMBOLS = {
     "quantized_tensor_matvec_f32": "_Z27quantized_tensor_matvec_f32PK23GgufQuantizedTensorViewPKfiPfi",
@@ -210,6 +211,9 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "qmv_set_profiling": (I, [I]),
         "qmv_last_kernel_seconds": (I, [ctypes.POINTER(ctypes.c_double)]),
         "qmv_qwen2_forward_profiled": (I, [P, I, P, IP, ctypes.POINTER(QmvOperationProfile)]),
+        "qmv_qwen2_prefill": (I, [P, P, I, P, IP]),
+        "qmv_qwen2_reset": (I, [P]),
+        "qmv_qwen2_stream": (I, [P, ctypes.POINTER(P)]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
@@ -562,6 +566,28 @@ class Qwen2Decoder:
         if n <= 0:
             raise RuntimeError(last_error())
         return n
+
+    def prefill(self, ids, want_logits: bool = True):
+        """Append prompt tokens (their KV entries in every layer); (logits of
+        the last position or None, its greedy token)."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        logits = np.empty(self.vocab, dtype=np.float32) if want_logits else None
+        nxt = ctypes.c_int(-1)
+        _check(lib().qmv_qwen2_prefill(self.handle, ids.ctypes.data, ids.size,
+                                       logits.ctypes.data if want_logits else None, ctypes.byref(nxt)),
+               "qmv_qwen2_prefill")
+        return logits, nxt.value
+
+    @property
+    def stream(self) -> int:
+        """The decoder's cudaStream_t (as an integer handle)."""
+        s = ctypes.c_void_p()
+        _check(lib().qmv_qwen2_stream(self.handle, ctypes.byref(s)), "qmv_qwen2_stream")
+        return s.value or 0
+
+    def reset(self) -> None:
+        """Back to position 0 (the reference's state_reset)."""
+        _check(lib().qmv_qwen2_reset(self.handle), "qmv_qwen2_reset")
 
     def forward_profiled(self, token: int, profile: QmvOperationProfile):
         """forward() with the step's device time added to ``profile`` by the

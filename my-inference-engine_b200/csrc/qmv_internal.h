@@ -149,6 +149,23 @@ cudaError_t launch_attention(const float *qkv, int heads, int kv_heads, int head
 // next token from the step's argmax key; history[st->steps] = token; pos += 1
 cudaError_t launch_advance(const unsigned long long *key, DecodeState *st, int *history, int max_steps,
                            cudaStream_t s);
+// Prefill steps (the reference's qwen2_prefill_tokens between its
+// projections), over n consecutive positions of one chunk; row-major
+// activations, device pointers.
+cudaError_t launch_embed_rows(const Layout &L, const uint8_t *w, const int *ids, int n, float *h,
+                              unsigned int *err, cudaStream_t s);
+cudaError_t launch_rmsnorm_rows(const float *x, const float *w, float eps, int cols, int rows, float *out,
+                                cudaStream_t s);
+// biases, RoPE (q in place) and the keys/values of positions pos0.. appended
+cudaError_t launch_rope_kv(float *q, int q_ld, const float *k, int k_ld, const float *v, int v_ld,
+                           const float *bias_q, const float *bias_k, const float *bias_v, int heads, int kv_heads,
+                           int head_dim, int pos0, int n, float rope_base, float *kc, float *vc, cudaStream_t s);
+// causal attention of positions pos0..pos0+n-1 over the cache; att [n][heads*hd]
+cudaError_t launch_prefill_attention(const float *q, int q_ld, const float *kc, const float *vc, int heads,
+                                     int kv_heads, int head_dim, int pos0, int n, float *att, cudaStream_t s);
+cudaError_t launch_add_rows(float *h, const float *y, size_t n, cudaStream_t s);
+cudaError_t launch_swiglu_rows(const float *gate, int g_ld, const float *up, int u_ld, int cols, int rows,
+                               float *out, cudaStream_t s);
 
 // Argmax key of logits[0..n).
 cudaError_t launch_argmax(const float *logits, int n, const ArgmaxOut &am, cudaStream_t s);

@@ -2331,6 +2331,248 @@ __global__ void advance_kernel(const unsigned long long *key, DecodeState *st, i
     st->pos += 1;
 }
 
+// ------------------------------------------------- Qwen2 prefill
+//
+// The reference's layer-first chunked prefill (qwen2_prefill_tokens,
+// src/qwen2_architecture.cpp:1550-1729) runs chunks of 8 positions through
+// every layer.  A query attends only to keys at or before its own position, so
+// the chunk length does not change what is computed: here a chunk is up to
+// 1024 positions and its projections are batched matmuls (tensor cores from 32
+// positions).  These kernels are the steps between the projections.
+
+// One CTA per position: the token's row of the resident embedding (bit-exact,
+// as embed_kernel).  A token outside the vocabulary sets error bit 1.
+template <uint32_t FMT>
+__global__ void embed_rows_kernel(Layout L, const uint8_t *__restrict__ w, const int *__restrict__ ids,
+                                  float *__restrict__ h, unsigned int *err)
+{
+    constexpr int BE = BlockShape<FMT>::E;
+    const int b = blockIdx.x;
+    int tok = ids[b];
+    if (tok < 0 || tok >= L.rows) {
+        if (threadIdx.x == 0) atomicOr(err, 1u);
+        tok = 0;
+    }
+    float *out = h + (size_t)b * L.cols;
+    uint8_t raw[BlockShape<FMT>::B];
+    for (int blk = threadIdx.x; blk < L.nb; blk += blockDim.x) {
+        gather_raw_block(L, w + (uint64_t)tok * L.row_stride, blk, raw);
+        for (int i = 0; i < BE; ++i) out[blk * BE + i] = dequant_value<FMT>(raw, i);
+    }
+}
+
+constexpr int kRowThreads = 256;
+
+// One CTA per row: out = (x / sqrt(mean(x^2) + eps)) * w
+// (tensor_rms_norm_f32, src/tensor.cpp:99-136).
+__global__ void __launch_bounds__(kRowThreads)
+rmsnorm_rows_kernel(const float *__restrict__ x, const float *__restrict__ w, float eps, int cols,
+                    float *__restrict__ out)
+{
+    __shared__ float part[kRowThreads / 32];
+    const float *xr = x + (size_t)blockIdx.x * cols;
+    float *orow = out + (size_t)blockIdx.x * cols;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < cols; i += kRowThreads) ss += xr[i] * xr[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kRowThreads / 32; ++i) ss += part[i];
+    const float denom = sqrtf(ss / (float)cols + eps);
+    for (int i = threadIdx.x; i < cols; i += kRowThreads) orow[i] = (xr[i] / denom) * w[i];
+}
+
+// One CTA per position b (absolute position pos0 + b): the projection biases
+// (qwen2_layer_project_batch, :763-807), RoPE on every query and key head
+// (transformer_apply_rope_f32, src/transformer_ops.cpp:43-69; q rotated in
+// place) and the key/value appended to the layer's cache.
+template <int HD>
+__global__ void rope_kv_kernel(float *__restrict__ q, int q_ld, const float *__restrict__ k, int k_ld,
+                               const float *__restrict__ v, int v_ld, const float *__restrict__ bias_q,
+                               const float *__restrict__ bias_k, const float *__restrict__ bias_v, int heads,
+                               int kv_heads, int pos0, float rope_base, float *__restrict__ kc,
+                               float *__restrict__ vc)
+{
+    __shared__ float cs[HD / 2], sn[HD / 2];
+    const int b = blockIdx.x, pos = pos0 + b, kvd = kv_heads * HD;
+    if (threadIdx.x < HD / 2) {
+        const float angle = (float)pos / powf(rope_base, (2.0f * (float)threadIdx.x / (float)HD));
+        cs[threadIdx.x] = cosf(angle);
+        sn[threadIdx.x] = sinf(angle);
+    }
+    __syncthreads();
+    float *qr = q + (size_t)b * q_ld;
+    for (int e = threadIdx.x; e < heads * (HD / 2); e += blockDim.x) {
+        const int o = (e / (HD / 2)) * HD, i = e % (HD / 2);
+        const float x = qr[o + i] + bias_q[o + i], y = qr[o + i + HD / 2] + bias_q[o + i + HD / 2];
+        qr[o + i] = x * cs[i] - y * sn[i];
+        qr[o + i + HD / 2] = x * sn[i] + y * cs[i];
+    }
+    const float *kr = k + (size_t)b * k_ld;
+    float *kdst = kc + (size_t)pos * kvd;
+    for (int e = threadIdx.x; e < kv_heads * (HD / 2); e += blockDim.x) {
+        const int o = (e / (HD / 2)) * HD, i = e % (HD / 2);
+        const float x = kr[o + i] + bias_k[o + i], y = kr[o + i + HD / 2] + bias_k[o + i + HD / 2];
+        kdst[o + i] = x * cs[i] - y * sn[i];
+        kdst[o + i + HD / 2] = x * sn[i] + y * cs[i];
+    }
+    const float *vr = v + (size_t)b * v_ld;
+    float *vdst = vc + (size_t)pos * kvd;
+    for (int e = threadIdx.x; e < kvd; e += blockDim.x) vdst[e] = vr[e] + bias_v[e];
+}
+
+constexpr int kPfKeys = 64;        // keys per shared-memory tile
+constexpr int kPfWarps = 8;
+constexpr int kPfRowsPerWarp = 8;  // (position, head) query rows per warp
+constexpr int kPfRows = kPfWarps * kPfRowsPerWarp;
+
+size_t prefill_attention_smem(int hd)
+{
+    return sizeof(float) * ((size_t)kPfRows * hd + (size_t)hd * (kPfKeys + 1) + (size_t)kPfKeys * hd +
+                            (size_t)kPfWarps * kPfRowsPerWarp * kPfKeys);
+}
+
+// Causal grouped-query attention for n consecutive positions pos0.. of one
+// chunk (transformer_attention_f32, src/transformer_ops.cpp:71-161, over the
+// position + 1 keys each query sees, :1640-1648).  Grid (KV head g, block of
+// qt positions); a CTA's rows are (position, query head of group g), 8 per
+// warp.  Keys and values stream through shared memory 64 at a time from the
+// layer's cache (which already holds this chunk's keys); each row keeps a
+// running maximum, sum of exp and weighted value sum (online softmax), so
+// scores never leave registers and shared memory.  fp32 throughout.
+template <int HD>
+__global__ void __launch_bounds__(kPfWarps * 32)
+prefill_attention_kernel(const float *__restrict__ q, int q_ld, const float *__restrict__ kc,
+                         const float *__restrict__ vc, int heads, int kv_heads, int pos0, int n, int qt,
+                         float *__restrict__ att)
+{
+    static_assert(HD == 64, "two output dimensions per lane");
+    constexpr int RW = kPfRowsPerWarp, KS = kPfKeys + 1;
+    extern __shared__ __align__(16) float sm[];
+    float *qs = sm;                     // [kPfRows][HD]
+    float *kt = qs + kPfRows * HD;      // [HD][KS]   keys, transposed
+    float *vs = kt + HD * KS;           // [kPfKeys][HD]
+    float *ps = vs + kPfKeys * HD;      // [warp][RW][kPfKeys] probabilities
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = blockIdx.x, G = heads / kv_heads, kvd = kv_heads * HD, dim = heads * HD;
+    const int b0 = blockIdx.y * qt, nq = min(qt, n - b0), rows = nq * G;
+    for (int e = tid; e < rows * HD; e += kPfWarps * 32) {
+        const int r = e / HD, d = e % HD;
+        qs[e] = q[(size_t)(b0 + r / G) * q_ld + (g * G + r % G) * HD + d];
+    }
+    float m[RW], l[RW], a0[RW], a1[RW];
+    int qpos[RW];
+#pragma unroll
+    for (int j = 0; j < RW; ++j) {
+        const int r = warp * RW + j;
+        m[j] = -INFINITY;
+        l[j] = a0[j] = a1[j] = 0.f;
+        qpos[j] = r < rows ? pos0 + b0 + r / G : -1;
+    }
+    const float rs = sqrtf((float)HD);
+    const int last = pos0 + b0 + nq - 1;  // keys [0, last]
+    float *pw = ps + warp * RW * kPfKeys;
+    for (int t0 = 0; t0 <= last; t0 += kPfKeys) {
+        const int tn = min(kPfKeys, last + 1 - t0);
+        __syncthreads();  // the previous tile is consumed (and qs written)
+        for (int e = tid; e < kPfKeys * HD; e += kPfWarps * 32) {
+            const int t = e / HD, d = e % HD;
+            float kv = 0.f, vv = 0.f;
+            if (t < tn) {
+                const size_t slot = (size_t)(t0 + t) * kvd + g * HD + d;
+                kv = kc[slot];
+                vv = vc[slot];
+            }
+            kt[d * KS + t] = kv;
+            vs[e] = vv;
+        }
+        __syncthreads();
+        float s0[RW], s1[RW];
+#pragma unroll
+        for (int j = 0; j < RW; ++j) s0[j] = s1[j] = 0.f;
+        const float *qw = qs + warp * RW * HD;
+#pragma unroll 4
+        for (int d = 0; d < HD; ++d) {
+            const float k0 = kt[d * KS + lane], k1 = kt[d * KS + lane + 32];
+#pragma unroll
+            for (int j = 0; j < RW; ++j) {
+                const float qv = qw[j * HD + d];
+                s0[j] += qv * k0;
+                s1[j] += qv * k1;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < RW; ++j) {
+            const float v0 = (lane < tn && t0 + lane <= qpos[j]) ? s0[j] / rs : -INFINITY;
+            const float v1 = (lane + 32 < tn && t0 + lane + 32 <= qpos[j]) ? s1[j] / rs : -INFINITY;
+            float mx = fmaxf(v0, v1);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+            const float mn = fmaxf(m[j], mx);
+            float p0 = 0.f, p1 = 0.f, corr = 1.f;
+            if (mn != -INFINITY) {  // a row with no visible key yet (padding rows) stays empty
+                corr = expf(m[j] - mn);
+                p0 = expf(v0 - mn);
+                p1 = expf(v1 - mn);
+            }
+            l[j] = l[j] * corr + p0 + p1;
+            a0[j] *= corr;
+            a1[j] *= corr;
+            m[j] = mn;
+            pw[j * kPfKeys + lane] = p0;
+            pw[j * kPfKeys + lane + 32] = p1;
+        }
+        __syncwarp();
+#pragma unroll 4
+        for (int t = 0; t < tn; ++t) {
+            const float vlo = vs[t * HD + lane], vhi = vs[t * HD + lane + 32];
+#pragma unroll
+            for (int j = 0; j < RW; ++j) {
+                const float p = pw[j * kPfKeys + t];
+                a0[j] += p * vlo;
+                a1[j] += p * vhi;
+            }
+        }
+        __syncwarp();
+    }
+#pragma unroll
+    for (int j = 0; j < RW; ++j) {
+        float lt = l[j];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lt += __shfl_xor_sync(kFull, lt, o);
+        const int r = warp * RW + j;
+        if (r < rows) {
+            float *o = att + (size_t)(b0 + r / G) * dim + (g * G + r % G) * HD;
+            o[lane] = a0[j] / lt;
+            o[lane + 32] = a1[j] / lt;
+        }
+    }
+}
+
+// h += y over n floats (the residual additions, :1653-1655, :1684-1686).
+__global__ void add_rows_kernel(float *__restrict__ h, const float *__restrict__ y, size_t n)
+{
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        h[i] += y[i];
+}
+
+// out = up * silu(gate) row by row (transformer_swiglu_f32,
+// src/transformer_ops.cpp:163-178); gate and up may be the halves of one
+// [gate | up] row.
+__global__ void swiglu_rows_kernel(const float *__restrict__ gate, int g_ld, const float *__restrict__ up, int u_ld,
+                                   int cols, int rows, float *__restrict__ out)
+{
+    const size_t n = (size_t)rows * cols;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = e / cols, c = e % cols;
+        const float x = gate[r * g_ld + c];
+        out[e] = up[r * u_ld + c] * (x / (1.0f + expf(-x)));
+    }
+}
+
 // ------------------------------------------------------ launch helpers
 
 int sm_count()
@@ -2954,6 +3196,71 @@ cudaError_t launch_advance(const unsigned long long *key, DecodeState *st, int *
                            cudaStream_t s)
 {
     advance_kernel<<<1, 1, 0, s>>>(key, st, history, max_steps);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_embed_rows(const Layout &L, const uint8_t *w, const int *ids, int n, float *h,
+                              unsigned int *err, cudaStream_t s)
+{
+    if (n <= 0) return cudaErrorInvalidValue;
+    const int t = 128;
+    switch (L.type) {
+    case kQ8_0: embed_rows_kernel<kQ8_0><<<n, t, 0, s>>>(L, w, ids, h, err); break;
+    case kQ5_0: embed_rows_kernel<kQ5_0><<<n, t, 0, s>>>(L, w, ids, h, err); break;
+    case kQ4_K: embed_rows_kernel<kQ4_K><<<n, t, 0, s>>>(L, w, ids, h, err); break;
+    case kQ6_K: embed_rows_kernel<kQ6_K><<<n, t, 0, s>>>(L, w, ids, h, err); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm_rows(const float *x, const float *w, float eps, int cols, int rows, float *out,
+                                cudaStream_t s)
+{
+    if (rows <= 0 || cols <= 0) return cudaErrorInvalidValue;
+    rmsnorm_rows_kernel<<<rows, kRowThreads, 0, s>>>(x, w, eps, cols, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rope_kv(float *q, int q_ld, const float *k, int k_ld, const float *v, int v_ld,
+                           const float *bias_q, const float *bias_k, const float *bias_v, int heads, int kv_heads,
+                           int head_dim, int pos0, int n, float rope_base, float *kc, float *vc, cudaStream_t s)
+{
+    if (head_dim != 64 || n <= 0) return cudaErrorInvalidValue;
+    rope_kv_kernel<64><<<n, 128, 0, s>>>(q, q_ld, k, k_ld, v, v_ld, bias_q, bias_k, bias_v, heads, kv_heads, pos0,
+                                         rope_base, kc, vc);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_attention(const float *q, int q_ld, const float *kc, const float *vc, int heads,
+                                     int kv_heads, int head_dim, int pos0, int n, float *att, cudaStream_t s)
+{
+    const int G = heads / kv_heads;
+    if (head_dim != 64 || n <= 0 || G < 1 || G > kPfRows) return cudaErrorInvalidValue;
+    auto kernel = prefill_attention_kernel<64>;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    e = allow_max_smem((const void *)kernel, dev);
+    if (e != cudaSuccess) return e;
+    const int qt = kPfRows / G;  // positions per CTA: qt * G rows <= kPfRows
+    const dim3 grid((unsigned)kv_heads, (unsigned)((n + qt - 1) / qt));
+    kernel<<<grid, kPfWarps * 32, prefill_attention_smem(64), s>>>(q, q_ld, kc, vc, heads, kv_heads, pos0, n, qt,
+                                                                   att);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_add_rows(float *h, const float *y, size_t n, cudaStream_t s)
+{
+    add_rows_kernel<<<grid_for(n, kThreads), kThreads, 0, s>>>(h, y, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_rows(const float *gate, int g_ld, const float *up, int u_ld, int cols, int rows,
+                               float *out, cudaStream_t s)
+{
+    swiglu_rows_kernel<<<grid_for((uint64_t)rows * cols, kThreads), kThreads, 0, s>>>(gate, g_ld, up, u_ld, cols,
+                                                                                       rows, out);
     return cudaGetLastError();
 }
 

@@ -74,6 +74,11 @@ struct QmvQwen2 {
     cudaStream_t stream = nullptr;
     cudaGraphExec_t exec = nullptr;
     int kernels_per_step = 0;  // kernel nodes of the captured step
+    // prefill chunk buffers (allocated on first use), pf_cap positions each
+    int pf_cap = 0;
+    int *pf_ids = nullptr;
+    float *pf_h = nullptr, *pf_xn = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_y = nullptr;
+    float *pf_gu = nullptr, *pf_g = nullptr;
     std::vector<cudaEvent_t> prof_events;  // profiled steps (created on first use)
     std::vector<void *> allocs;
     std::vector<QmvWeight *> weights;
@@ -445,6 +450,25 @@ QMV_EXPORT int qmv_qwen2_set_kv(QmvQwen2 *m, const float *keys, const float *val
     return 1;
 }
 
+// The stream every call of this decoder runs on (for callers timing it with
+// their own events).
+QMV_EXPORT int qmv_qwen2_stream(const QmvQwen2 *m, void **stream)
+{
+    if (m == nullptr || stream == nullptr) return qmv::set_error("null argument");
+    *stream = (void *)m->stream;
+    return 1;
+}
+
+// The reference's state_reset (src/architecture.h:80-81): back to position
+// zero; the cache is overwritten as positions are written again.
+QMV_EXPORT int qmv_qwen2_reset(QmvQwen2 *m)
+{
+    if (m == nullptr) return qmv::set_error("null decoder");
+    const qmv::DecodeState s{0, 0, 0, 0u};
+    QW_CUDA(cudaMemcpy(m->st, &s, sizeof s, cudaMemcpyHostToDevice), "reset");
+    return 1;
+}
+
 QMV_EXPORT int qmv_qwen2_replay(QmvQwen2 *m, int steps, void *stream)
 {
     if (m == nullptr || steps < 0) return qmv::set_error("bad replay request");
@@ -559,6 +583,137 @@ QMV_EXPORT int qmv_qwen2_forward_profiled(QmvQwen2 *m, int token, float *logits,
         QW_CUDA(cudaMemcpy(logits, m->logits, (size_t)m->cfg.vocab_size * sizeof(float), cudaMemcpyDeviceToHost),
                 "read logits");
     if (next_token) QW_CUDA(cudaMemcpy(next_token, m->history, sizeof(int), cudaMemcpyDeviceToHost), "read token");
+    return 1;
+}
+
+namespace {
+
+constexpr int kPrefillChunk = 1024;  // positions per chunk (activation buffers scale with it)
+
+int prefill_buffers(QmvQwen2 *m)
+{
+    if (m->pf_cap > 0) return 1;
+    const QmvQwen2Config &c = m->cfg;
+    const size_t C = (size_t)(c.max_context < kPrefillChunk ? c.max_context : kPrefillChunk);
+    const size_t dim = (size_t)c.dim, hid = (size_t)c.hidden_dim, kvd = (size_t)m->kvd;
+    if (!dalloc(m, (void **)&m->pf_ids, C * sizeof(int), "prefill ids") ||
+        !dalloc(m, (void **)&m->pf_h, C * dim * sizeof(float), "prefill activations") ||
+        !dalloc(m, (void **)&m->pf_xn, C * dim * sizeof(float), "prefill activations") ||
+        !dalloc(m, (void **)&m->pf_qkv, C * (dim + 2 * kvd) * sizeof(float), "prefill activations") ||
+        !dalloc(m, (void **)&m->pf_att, C * dim * sizeof(float), "prefill activations") ||
+        !dalloc(m, (void **)&m->pf_y, C * dim * sizeof(float), "prefill activations") ||
+        !dalloc(m, (void **)&m->pf_gu, C * 2 * hid * sizeof(float), "prefill activations") ||
+        !dalloc(m, (void **)&m->pf_g, C * hid * sizeof(float), "prefill activations"))
+        return 0;
+    m->pf_cap = (int)C;
+    return 1;
+}
+
+cudaError_t matmul(QmvQwen2 *m, const QmvWeight *w, const float *X, int n, float *Y)
+{
+    return qmv::launch_matmul(w->L, w->dev, X, n, Y, m->stream);
+}
+
+// Positions pos0 .. pos0 + n - 1 (ids already on the device) through every
+// layer: the reference's per-chunk schedule (src/qwen2_architecture.cpp:
+// 1586-1690) with the chunk's positions batched in every projection.
+cudaError_t enqueue_prefill_chunk(QmvQwen2 *m, int pos0, int n)
+{
+    const QmvQwen2Config &c = m->cfg;
+    const int dim = c.dim, hid = c.hidden_dim, kvd = m->kvd;
+    cudaError_t e = qmv::launch_embed_rows(m->embd->L, m->embd->dev, m->pf_ids, n, m->pf_h, &m->st->error, m->stream);
+    for (int l = 0; l < c.n_layers && e == cudaSuccess; ++l) {
+        const Layer &L = m->layers[(size_t)l];
+        e = qmv::launch_rmsnorm_rows(m->pf_h, L.attn_norm, c.rms_norm_epsilon, dim, n, m->pf_xn, m->stream);
+        float *q = m->pf_qkv, *k, *v;
+        int q_ld, k_ld, v_ld;
+        if (L.qkv) {
+            if (e == cudaSuccess) e = matmul(m, L.qkv, m->pf_xn, n, m->pf_qkv);
+            k = q + dim;
+            v = k + kvd;
+            q_ld = k_ld = v_ld = dim + 2 * kvd;
+        } else {
+            k = q + (size_t)n * dim;
+            v = k + (size_t)n * kvd;
+            q_ld = dim;
+            k_ld = v_ld = kvd;
+            if (e == cudaSuccess) e = matmul(m, L.q, m->pf_xn, n, q);
+            if (e == cudaSuccess) e = matmul(m, L.k, m->pf_xn, n, k);
+            if (e == cudaSuccess) e = matmul(m, L.v, m->pf_xn, n, v);
+        }
+        const size_t off = (size_t)l * (size_t)c.max_context * (size_t)kvd;
+        if (e == cudaSuccess)
+            e = qmv::launch_rope_kv(q, q_ld, k, k_ld, v, v_ld, L.bias_qkv, L.bias_qkv + dim, L.bias_qkv + dim + kvd,
+                                    c.n_heads, c.n_kv_heads, m->head_dim, pos0, n, c.rope_frequency_base, m->kc + off,
+                                    m->vc + off, m->stream);
+        if (e == cudaSuccess)
+            e = qmv::launch_prefill_attention(q, q_ld, m->kc + off, m->vc + off, c.n_heads, c.n_kv_heads, m->head_dim,
+                                              pos0, n, m->pf_att, m->stream);
+        if (e == cudaSuccess) e = matmul(m, L.o, m->pf_att, n, m->pf_y);
+        if (e == cudaSuccess) e = qmv::launch_add_rows(m->pf_h, m->pf_y, (size_t)n * dim, m->stream);
+        if (e == cudaSuccess)
+            e = qmv::launch_rmsnorm_rows(m->pf_h, L.ffn_norm, c.rms_norm_epsilon, dim, n, m->pf_xn, m->stream);
+        if (L.gate_up) {  // [gate | up] rows of 2 * hid
+            if (e == cudaSuccess) e = matmul(m, L.gate_up, m->pf_xn, n, m->pf_gu);
+            if (e == cudaSuccess)
+                e = qmv::launch_swiglu_rows(m->pf_gu, 2 * hid, m->pf_gu + hid, 2 * hid, hid, n, m->pf_g, m->stream);
+        } else {
+            float *up = m->pf_gu + (size_t)n * hid;
+            if (e == cudaSuccess) e = matmul(m, L.gate, m->pf_xn, n, m->pf_gu);
+            if (e == cudaSuccess) e = matmul(m, L.up, m->pf_xn, n, up);
+            if (e == cudaSuccess) e = qmv::launch_swiglu_rows(m->pf_gu, hid, up, hid, hid, n, m->pf_g, m->stream);
+        }
+        if (e == cudaSuccess) e = matmul(m, L.down, m->pf_g, n, m->pf_y);
+        if (e == cudaSuccess) e = qmv::launch_add_rows(m->pf_h, m->pf_y, (size_t)n * dim, m->stream);
+    }
+    return e;
+}
+
+}  // namespace
+
+// The reference's prefill_tokens (qwen2_prefill_tokens,
+// src/qwen2_architecture.cpp:1550-1729): append `count` tokens at the current
+// position, writing their keys and values into every layer's cache, and
+// publish the logits of the last one (plus its greedy token).  Same checks and
+// messages; on failure the position is unchanged.  One token is one decode
+// step, as in the reference.
+QMV_EXPORT int qmv_qwen2_prefill(QmvQwen2 *m, const int *ids, int count, float *logits, int *next_token)
+{
+    if (m == nullptr || ids == nullptr || count <= 0) return qmv::set_error("Qwen2 prefill arguments are invalid.");
+    const QmvQwen2Config &c = m->cfg;
+    qmv::DecodeState st{};
+    if (!check_state(m, &st)) return 0;
+    const int pos0 = st.pos;
+    if (pos0 < 0 || pos0 > c.max_context || count > c.max_context - pos0)
+        return qmv::set_error("Qwen2 prefill context capacity is exhausted.");
+    for (int i = 0; i < count; ++i)
+        if (ids[i] < 0 || ids[i] >= c.vocab_size) return qmv::set_error("Qwen2 prefill token ID is out of range.");
+    if (count == 1) return qmv_qwen2_forward(m, ids[0], logits, next_token);
+    if (!prefill_buffers(m)) return 0;
+    int last_n = 0;
+    for (int start = 0; start < count; start += m->pf_cap) {
+        const int n = count - start < m->pf_cap ? count - start : m->pf_cap;
+        QW_CUDA(cudaMemcpyAsync(m->pf_ids, ids + start, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, m->stream),
+                "prefill ids");
+        QW_CUDA(enqueue_prefill_chunk(m, pos0 + start, n), "prefill");
+        last_n = n;
+    }
+    // the last position's logits: output_norm, output projection, greedy argmax
+    const qmv::ArgmaxOut am{m->key, m->am_ws, 0};
+    QW_CUDA(gemv(m, m->out, m->pf_h + (size_t)(last_n - 1) * c.dim, m->logits,
+                 qmv::Fuse{qmv::kPreRmsNorm, m->out_norm, c.rms_norm_epsilon, nullptr, nullptr}, &am),
+            "prefill output");
+    unsigned long long key = 0;
+    QW_CUDA(cudaMemcpyAsync(&key, m->key, sizeof key, cudaMemcpyDeviceToHost, m->stream), "prefill output");
+    QW_CUDA(cudaStreamSynchronize(m->stream), "prefill");
+    if (!check_state(m, nullptr)) return 0;
+    if (key == 0ull || key == ~0ull) return qmv::set_error("Output contains a non-finite logit.");
+    const int pos = pos0 + count;
+    QW_CUDA(cudaMemcpy(&m->st->pos, &pos, sizeof pos, cudaMemcpyHostToDevice), "prefill position");
+    if (logits)
+        QW_CUDA(cudaMemcpy(logits, m->logits, (size_t)c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost),
+                "read logits");
+    if (next_token) *next_token = (int)(0xffffffffu - (unsigned int)(key & 0xffffffffull));
     return 1;
 }
 

@@ -288,6 +288,25 @@ class RefQwen2:
         ok = self.lib.ref_qwen2_forward(self.h, token, logits.ctypes.data)
         return bool(ok), logits
 
+    def prefill(self, ids):
+        """(ok, last position's logits) of the reference's prefill_tokens."""
+        self.lib.ref_qwen2_prefill.argtypes = [ctypes.c_void_p, _P, ctypes.c_int, _P]
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        logits = np.empty(self.m["vocab"], dtype=np.float32)
+        ok = self.lib.ref_qwen2_prefill(self.h, ids.ctypes.data, ids.size, logits.ctypes.data)
+        return bool(ok), logits
+
+    def reset(self) -> None:
+        self.lib.ref_qwen2_reset.argtypes = [ctypes.c_void_p]
+        self.lib.ref_qwen2_reset(self.h)
+
+    def get_kv(self, layer: int, position: int):
+        kvd = self.m["kv_heads"] * (self.m["dim"] // self.m["heads"])
+        k = np.empty(kvd, dtype=np.float32)
+        v = np.empty(kvd, dtype=np.float32)
+        self.lib.ref_qwen2_get_kv(self.h, layer, position, k.ctypes.data, v.ctypes.data)
+        return k, v
+
     def enable_profile(self) -> None:
         self.lib.ref_qwen2_enable_profile.argtypes = [ctypes.c_void_p]
         self.lib.ref_qwen2_enable_profile(self.h)

@@ -135,6 +135,24 @@ void ref_qwen2_read_profile(void *h, void *out)
     memcpy(out, &m->state.profile, sizeof(m->state.profile));
 }
 
+// The reference's prefill_tokens (qwen2_prefill_tokens) on `count` ids at the
+// state's position; the last position's logits on success.
+int ref_qwen2_prefill(void *h, const int *ids, int count, float *logits)
+{
+    RefQwen2 *m = (RefQwen2 *)h;
+    char error[512] = {};
+    if (!qwen2_architecture_ops()->prefill_tokens(&m->model, &m->state, ids, count, error, sizeof(error))) return 0;
+    memcpy(logits, m->state.logits, (size_t)m->model.config.vocab_size * sizeof(float));
+    return 1;
+}
+
+// The reference's state_reset: back to position zero.
+void ref_qwen2_reset(void *h)
+{
+    RefQwen2 *m = (RefQwen2 *)h;
+    qwen2_architecture_ops()->state_reset(&m->state);
+}
+
 // KV entries of one layer and position (after a forward step wrote them).
 int ref_qwen2_get_kv(void *h, int layer, int position, float *key, float *value)
 {
