@@ -160,9 +160,13 @@ cudaError_t launch_rmsnorm_rows(const float *x, const float *w, float eps, int c
 cudaError_t launch_rope_kv(float *q, int q_ld, const float *k, int k_ld, const float *v, int v_ld,
                            const float *bias_q, const float *bias_k, const float *bias_v, int heads, int kv_heads,
                            int head_dim, int pos0, int n, float rope_base, float *kc, float *vc, cudaStream_t s);
-// causal attention of positions pos0..pos0+n-1 over the cache; att [n][heads*hd]
+// causal attention of positions pos0..pos0+n-1 over the cache; att [n][heads*hd];
+// part: prefill_attention_part_floats(heads, head_dim, n) floats of scratch
+// (partials of rows whose keys are split across CTAs)
+size_t prefill_attention_part_floats(int heads, int head_dim, int positions);
 cudaError_t launch_prefill_attention(const float *q, int q_ld, const float *kc, const float *vc, int heads,
-                                     int kv_heads, int head_dim, int pos0, int n, float *att, cudaStream_t s);
+                                     int kv_heads, int head_dim, int pos0, int n, float *att, float *part,
+                                     cudaStream_t s);
 cudaError_t launch_add_rows(float *h, const float *y, size_t n, cudaStream_t s);
 cudaError_t launch_swiglu_rows(const float *gate, int g_ld, const float *up, int u_ld, int cols, int rows,
                                float *out, cudaStream_t s);

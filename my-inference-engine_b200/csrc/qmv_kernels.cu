@@ -2424,131 +2424,267 @@ __global__ void rope_kv_kernel(float *__restrict__ q, int q_ld, const float *__r
     for (int e = threadIdx.x; e < kvd; e += blockDim.x) vdst[e] = vr[e] + bias_v[e];
 }
 
-constexpr int kPfKeys = 64;        // keys per shared-memory tile
-constexpr int kPfWarps = 8;
-constexpr int kPfRowsPerWarp = 8;  // (position, head) query rows per warp
-constexpr int kPfRows = kPfWarps * kPfRowsPerWarp;
+constexpr int kPfKeys = 64;   // keys per shared-memory tile
+constexpr int kPfWarps = 4;   // 16 query rows each (one m16 tile)
+constexpr int kPfRows = 16 * kPfWarps;
+constexpr int kPfPairs = kPfKeys / 2 + 4;  // 32-bit words per smem row: 64 bf16 + 8 of padding
+// dynamic shared memory: the raw fp32 K and V rows of the next tile (filled by
+// cp.async while the current tile's MMAs run), then the split bf16 planes of
+// the current tile
+constexpr int kPfRawFloats = kPfKeys * 64;
+constexpr size_t kPfSmem = sizeof(float) * 2 * kPfRawFloats + sizeof(uint32_t) * 4 * 64 * kPfPairs;
+constexpr int kPfMaxSplits = 8;  // key-range splits per query block (partials per row)
 
-size_t prefill_attention_smem(int hd)
+// 16-byte global -> shared copy, L2 only; src_bytes 0 fills zeros (the source
+// is then not read).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes)
 {
-    return sizeof(float) * ((size_t)kPfRows * hd + (size_t)hd * (kPfKeys + 1) + (size_t)kPfKeys * hd +
-                            (size_t)kPfWarps * kPfRowsPerWarp * kPfKeys);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Packed bf16 hi/lo parts of (a, b): hi = each rounded to 8 significant bits,
+// lo = the remainder rounded likewise; a = hi + lo to about 2^-16 relative.
+// The element with the lower index sits in the lower half (MMA fragment order).
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t &h, uint32_t &l)
+{
+    const float2 x = f2(a, b);
+    const float2 hi = round8x2(x);
+    const float2 lo = round8x2(__ffma2_rn(hi, f2(-1.f, -1.f), x));
+    h = __byte_perm(__float_as_uint(hi.x), __float_as_uint(hi.y), 0x7632u);
+    l = __byte_perm(__float_as_uint(lo.x), __float_as_uint(lo.y), 0x7632u);
+}
+
+// d += a b for one 16x8x16 bf16 tile (fp32 accumulate), fragments in the
+// mma.sync register layout.
+__device__ __forceinline__ void mma_bf16_16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// x y to fp32 accuracy from the split parts: xh yh + xl yh + xh yl.
+__device__ __forceinline__ void mma_split(float d[4], const uint32_t ah[4], const uint32_t al[4], uint32_t bh0,
+                                          uint32_t bh1, uint32_t bl0, uint32_t bl1)
+{
+    mma_bf16_16816(d, ah, bh0, bh1);
+    mma_bf16_16816(d, al, bh0, bh1);
+    mma_bf16_16816(d, ah, bl0, bl1);
+}
+
+// Key tiles of query block y (positions b0 .. b0 + nq - 1 of the chunk) and
+// the number of key-range splits its rows take.
+__device__ __forceinline__ int pf_tiles(int pos0, int b0, int nq) { return (pos0 + b0 + nq - 1) / kPfKeys + 1; }
 
 // Causal grouped-query attention for n consecutive positions pos0.. of one
 // chunk (transformer_attention_f32, src/transformer_ops.cpp:71-161, over the
 // position + 1 keys each query sees, :1640-1648).  Grid (KV head g, block of
-// qt positions); a CTA's rows are (position, query head of group g), 8 per
-// warp.  Keys and values stream through shared memory 64 at a time from the
-// layer's cache (which already holds this chunk's keys); each row keeps a
-// running maximum, sum of exp and weighted value sum (online softmax), so
-// scores never leave registers and shared memory.  fp32 throughout.
+// qt positions, key-range split z of tps tiles); a CTA's rows are (position,
+// query head of group g), 16 per warp.  A block whose keys span one split
+// writes its rows normalised to att; otherwise each split stores its rows'
+// (running max, sum of exp, unnormalised output) in part and
+// prefill_merge_kernel combines them.  Keys and values stream through shared memory 64 at a time from the
+// layer's cache (which already holds this chunk's keys) as bf16 hi/lo parts;
+// Q K^T and P V run on the tensor cores (mma.sync m16n8k16) with three
+// products per split pair (dropping only lo x lo, ~2^-16 relative), fp32
+// accumulation, and an online softmax in registers: the score tile's
+// accumulator layout is the A-fragment layout of P, so scores never leave
+// registers.  Scores are divided by sqrt(head_dim) as the reference does.
 template <int HD>
 __global__ void __launch_bounds__(kPfWarps * 32)
 prefill_attention_kernel(const float *__restrict__ q, int q_ld, const float *__restrict__ kc,
-                         const float *__restrict__ vc, int heads, int kv_heads, int pos0, int n, int qt,
-                         float *__restrict__ att)
+                         const float *__restrict__ vc, int heads, int kv_heads, int pos0, int n, int qt, int tps,
+                         float *__restrict__ att, float *__restrict__ part)
 {
-    static_assert(HD == 64, "two output dimensions per lane");
-    constexpr int RW = kPfRowsPerWarp, KS = kPfKeys + 1;
-    extern __shared__ __align__(16) float sm[];
-    float *qs = sm;                     // [kPfRows][HD]
-    float *kt = qs + kPfRows * HD;      // [HD][KS]   keys, transposed
-    float *vs = kt + HD * KS;           // [kPfKeys][HD]
-    float *ps = vs + kPfKeys * HD;      // [warp][RW][kPfKeys] probabilities
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = blockIdx.x, G = heads / kv_heads, kvd = kv_heads * HD, dim = heads * HD;
+    static_assert(HD == 64, "four 16-wide K steps, eight 8-wide output tiles");
+    extern __shared__ __align__(16) float pf_sm[];
+    float *raw = pf_sm;  // [K | V][key][d]
+    uint32_t(*kh)[kPfPairs] = reinterpret_cast<uint32_t(*)[kPfPairs]>(pf_sm + 2 * kPfRawFloats);  // [key][d pair]
+    uint32_t(*kl)[kPfPairs] = kh + kPfKeys;
+    uint32_t(*vh)[kPfPairs] = kl + kPfKeys;  // [d][key pair]
+    uint32_t(*vl)[kPfPairs] = vh + HD;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gr = lane >> 2, tg = lane & 3;
+    const int kvh = blockIdx.x, G = heads / kv_heads, kvd = kv_heads * HD, dim = heads * HD;
     const int b0 = blockIdx.y * qt, nq = min(qt, n - b0), rows = nq * G;
-    for (int e = tid; e < rows * HD; e += kPfWarps * 32) {
-        const int r = e / HD, d = e % HD;
-        qs[e] = q[(size_t)(b0 + r / G) * q_ld + (g * G + r % G) * HD + d];
-    }
-    float m[RW], l[RW], a0[RW], a1[RW];
-    int qpos[RW];
+    const int ntiles = pf_tiles(pos0, b0, nq), splits = (ntiles + tps - 1) / tps, z = blockIdx.z;
+    if (z >= splits) return;
+    const int ra = warp * 16 + gr, rb = ra + 8;  // this thread's two rows
+    const int pa = ra < rows ? pos0 + b0 + ra / G : -1, pb = rb < rows ? pos0 + b0 + rb / G : -1;
+    // Q fragments of both rows for the four 16-wide d steps, split once
+    uint32_t qh[4][4], ql[4][4];
+    {
+        const float *qa = ra < rows ? q + (size_t)(b0 + ra / G) * q_ld + (kvh * G + ra % G) * HD : nullptr;
+        const float *qb = rb < rows ? q + (size_t)(b0 + rb / G) * q_ld + (kvh * G + rb % G) * HD : nullptr;
 #pragma unroll
-    for (int j = 0; j < RW; ++j) {
-        const int r = warp * RW + j;
-        m[j] = -INFINITY;
-        l[j] = a0[j] = a1[j] = 0.f;
-        qpos[j] = r < rows ? pos0 + b0 + r / G : -1;
+        for (int st = 0; st < 4; ++st) {
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {  // d = 16 st + 8 half + 2 tg
+                const int d = 16 * st + 8 * half + 2 * tg;
+                const float2 xa = qa ? *reinterpret_cast<const float2 *>(qa + d) : f2(0.f, 0.f);
+                const float2 xb = qb ? *reinterpret_cast<const float2 *>(qb + d) : f2(0.f, 0.f);
+                split_pair(xa.x, xa.y, qh[st][2 * half], ql[st][2 * half]);
+                split_pair(xb.x, xb.y, qh[st][2 * half + 1], ql[st][2 * half + 1]);
+            }
+        }
     }
+    float o[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float ma = -INFINITY, mb = -INFINITY, la = 0.f, lb = 0.f;
     const float rs = sqrtf((float)HD);
-    const int last = pos0 + b0 + nq - 1;  // keys [0, last]
-    float *pw = ps + warp * RW * kPfKeys;
-    for (int t0 = 0; t0 <= last; t0 += kPfKeys) {
+    const int last = pos0 + b0 + nq - 1;  // keys [0, last] are visible to some row
+    const int tb = z * tps * kPfKeys, te = min((z + 1) * tps * kPfKeys, last + 1);  // this split's keys
+    const uint32_t raw_s = (uint32_t)__cvta_generic_to_shared(raw);
+    // raw K and V rows of the tile at t0 (keys past `last` are zero-filled,
+    // never read)
+    auto fetch = [&](int t0) {
+        for (int e = tid; e < kPfKeys * (HD / 4); e += kPfWarps * 32) {
+            const int key = e / (HD / 4), c4 = e % (HD / 4);
+            const bool ok = t0 + key <= last;
+            const size_t src = ok ? (size_t)(t0 + key) * kvd + kvh * HD + 4 * c4 : 0;
+            const uint32_t dst = raw_s + 4u * (uint32_t)(key * HD + 4 * c4);
+            cp_async16(dst, kc + src, ok ? 16u : 0u);
+            cp_async16(dst + 4u * kPfRawFloats, vc + src, ok ? 16u : 0u);
+        }
+        cp_async_commit();
+    };
+    fetch(tb);
+    for (int t0 = tb; t0 < te; t0 += kPfKeys) {
         const int tn = min(kPfKeys, last + 1 - t0);
-        __syncthreads();  // the previous tile is consumed (and qs written)
-        for (int e = tid; e < kPfKeys * HD; e += kPfWarps * 32) {
-            const int t = e / HD, d = e % HD;
-            float kv = 0.f, vv = 0.f;
-            if (t < tn) {
-                const size_t slot = (size_t)(t0 + t) * kvd + g * HD + d;
-                kv = kc[slot];
-                vv = vc[slot];
-            }
-            kt[d * KS + t] = kv;
-            vs[e] = vv;
+        cp_async_wait<0>();
+        __syncthreads();  // this tile's raw rows are visible; the previous tile's planes are consumed
+        const float *kr = raw, *vr = raw + kPfRawFloats;
+        for (int e = tid; e < kPfKeys * (HD / 2); e += kPfWarps * 32) {
+            const int key = e / (HD / 2), dp = e % (HD / 2);
+            const float2 kk = *reinterpret_cast<const float2 *>(kr + key * HD + 2 * dp);
+            split_pair(kk.x, kk.y, kh[key][dp], kl[key][dp]);
         }
-        __syncthreads();
-        float s0[RW], s1[RW];
-#pragma unroll
-        for (int j = 0; j < RW; ++j) s0[j] = s1[j] = 0.f;
-        const float *qw = qs + warp * RW * HD;
-#pragma unroll 4
-        for (int d = 0; d < HD; ++d) {
-            const float k0 = kt[d * KS + lane], k1 = kt[d * KS + lane + 32];
-#pragma unroll
-            for (int j = 0; j < RW; ++j) {
-                const float qv = qw[j * HD + d];
-                s0[j] += qv * k0;
-                s1[j] += qv * k1;
-            }
+        for (int e = tid; e < (kPfKeys / 2) * HD; e += kPfWarps * 32) {
+            const int kp = e / HD, d = e % HD;
+            split_pair(vr[2 * kp * HD + d], vr[(2 * kp + 1) * HD + d], vh[d][kp], vl[d][kp]);
         }
+        __syncthreads();                               // planes ready, raw buffer free
+        if (t0 + kPfKeys < te) fetch(t0 + kPfKeys);  // in flight during this tile's MMAs
+        // S = Q K^T: tile j holds keys t0 + 8 j + 2 tg + {0, 1} of rows ra (0, 1) and rb (2, 3)
+        float sc[8][4];
 #pragma unroll
-        for (int j = 0; j < RW; ++j) {
-            const float v0 = (lane < tn && t0 + lane <= qpos[j]) ? s0[j] / rs : -INFINITY;
-            const float v1 = (lane + 32 < tn && t0 + lane + 32 <= qpos[j]) ? s1[j] / rs : -INFINITY;
-            float mx = fmaxf(v0, v1);
+        for (int j = 0; j < 8; ++j) {
+            sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
-            const float mn = fmaxf(m[j], mx);
-            float p0 = 0.f, p1 = 0.f, corr = 1.f;
-            if (mn != -INFINITY) {  // a row with no visible key yet (padding rows) stays empty
-                corr = expf(m[j] - mn);
-                p0 = expf(v0 - mn);
-                p1 = expf(v1 - mn);
-            }
-            l[j] = l[j] * corr + p0 + p1;
-            a0[j] *= corr;
-            a1[j] *= corr;
-            m[j] = mn;
-            pw[j * kPfKeys + lane] = p0;
-            pw[j * kPfKeys + lane + 32] = p1;
+            for (int st = 0; st < 4; ++st)
+                mma_split(sc[j], qh[st], ql[st], kh[8 * j + gr][8 * st + tg], kh[8 * j + gr][8 * st + 4 + tg],
+                          kl[8 * j + gr][8 * st + tg], kl[8 * j + gr][8 * st + 4 + tg]);
         }
-        __syncwarp();
-#pragma unroll 4
-        for (int t = 0; t < tn; ++t) {
-            const float vlo = vs[t * HD + lane], vhi = vs[t * HD + lane + 32];
+        float mxa = -INFINITY, mxb = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < RW; ++j) {
-                const float p = pw[j * kPfKeys + t];
-                a0[j] += p * vlo;
-                a1[j] += p * vhi;
+        for (int j = 0; j < 8; ++j) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const int key = t0 + 8 * j + 2 * tg + c;
+                sc[j][c] = key - t0 < tn && key <= pa ? sc[j][c] / rs : -INFINITY;
+                sc[j][2 + c] = key - t0 < tn && key <= pb ? sc[j][2 + c] / rs : -INFINITY;
+                mxa = fmaxf(mxa, sc[j][c]);
+                mxb = fmaxf(mxb, sc[j][2 + c]);
             }
         }
-        __syncwarp();
+#pragma unroll
+        for (int off = 1; off < 4; off <<= 1) {  // the four lanes of a row
+            mxa = fmaxf(mxa, __shfl_xor_sync(kFull, mxa, off));
+            mxb = fmaxf(mxb, __shfl_xor_sync(kFull, mxb, off));
+        }
+        const float na = fmaxf(ma, mxa), nb = fmaxf(mb, mxb);
+        // a row with no visible key yet (a padding row) keeps zero weights
+        const float ca = na == -INFINITY ? 1.f : expf(ma - na), cb = nb == -INFINITY ? 1.f : expf(mb - nb);
+        la *= ca;
+        lb *= cb;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            o[j][0] *= ca;
+            o[j][1] *= ca;
+            o[j][2] *= cb;
+            o[j][3] *= cb;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                sc[j][c] = na == -INFINITY ? 0.f : expf(sc[j][c] - na);
+                sc[j][2 + c] = nb == -INFINITY ? 0.f : expf(sc[j][2 + c] - nb);
+                la += sc[j][c];
+                lb += sc[j][2 + c];
+            }
+        }
+        ma = na;
+        mb = nb;
+        // O += P V: the k-step st (keys 16 st ..) takes P from score tiles 2 st, 2 st + 1
+#pragma unroll
+        for (int st = 0; st < 4; ++st) {
+            uint32_t ph[4], pl[4];
+            split_pair(sc[2 * st][0], sc[2 * st][1], ph[0], pl[0]);
+            split_pair(sc[2 * st][2], sc[2 * st][3], ph[1], pl[1]);
+            split_pair(sc[2 * st + 1][0], sc[2 * st + 1][1], ph[2], pl[2]);
+            split_pair(sc[2 * st + 1][2], sc[2 * st + 1][3], ph[3], pl[3]);
+#pragma unroll
+            for (int jd = 0; jd < 8; ++jd)
+                mma_split(o[jd], ph, pl, vh[8 * jd + gr][8 * st + tg], vh[8 * jd + gr][8 * st + 4 + tg],
+                          vl[8 * jd + gr][8 * st + tg], vl[8 * jd + gr][8 * st + 4 + tg]);
+        }
     }
 #pragma unroll
-    for (int j = 0; j < RW; ++j) {
-        float lt = l[j];
+    for (int off = 1; off < 4; off <<= 1) {
+        la += __shfl_xor_sync(kFull, la, off);
+        lb += __shfl_xor_sync(kFull, lb, off);
+    }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) lt += __shfl_xor_sync(kFull, lt, o);
-        const int r = warp * RW + j;
-        if (r < rows) {
-            float *o = att + (size_t)(b0 + r / G) * dim + (g * G + r % G) * HD;
-            o[lane] = a0[j] / lt;
-            o[lane + 32] = a1[j] / lt;
+    for (int h2 = 0; h2 < 2; ++h2) {
+        const int r = h2 ? rb : ra;
+        if (r >= rows) continue;
+        const float l = h2 ? lb : la, mm = h2 ? mb : ma;
+        const int b = b0 + r / G, head = kvh * G + r % G;
+        if (splits == 1) {
+            float *out = att + (size_t)b * dim + head * HD;
+#pragma unroll
+            for (int jd = 0; jd < 8; ++jd)
+                *reinterpret_cast<float2 *>(out + 8 * jd + 2 * tg) = f2(o[jd][2 * h2] / l, o[jd][2 * h2 + 1] / l);
+        } else {
+            float *pp = part + ((size_t)(b * heads + head) * kPfMaxSplits + z) * (HD + 2);
+            if (tg == 0) {
+                pp[0] = mm;
+                pp[1] = l;
+            }
+#pragma unroll
+            for (int jd = 0; jd < 8; ++jd) {
+                pp[2 + 8 * jd + 2 * tg] = o[jd][2 * h2];
+                pp[3 + 8 * jd + 2 * tg] = o[jd][2 * h2 + 1];
+            }
         }
+    }
+}
+
+// Rows whose keys were split: out = sum_z e^(m_z - M) o_z / sum_z e^(m_z - M) l_z
+// (the softmax over all their keys).  One CTA per position.
+template <int HD>
+__global__ void prefill_merge_kernel(const float *__restrict__ part, int heads, int kv_heads, int pos0, int n,
+                                     int qt, int tps, float *__restrict__ att)
+{
+    const int b = blockIdx.x, y = b / qt, b0 = y * qt, nq = min(qt, n - b0);
+    const int splits = (pf_tiles(pos0, b0, nq) + tps - 1) / tps;
+    if (splits == 1) return;
+    (void)kv_heads;
+    for (int e = threadIdx.x; e < heads * HD; e += blockDim.x) {
+        const int head = e / HD, d = e % HD;
+        const float *pp = part + (size_t)(b * heads + head) * kPfMaxSplits * (HD + 2);
+        float M = -INFINITY;
+        for (int z = 0; z < splits; ++z) M = fmaxf(M, pp[z * (HD + 2)]);
+        float den = 0.f, num = 0.f;
+        for (int z = 0; z < splits; ++z) {
+            const float mz = pp[z * (HD + 2)];
+            const float w = mz == -INFINITY ? 0.f : expf(mz - M);
+            den += w * pp[z * (HD + 2) + 1];
+            num += w * pp[z * (HD + 2) + 2 + d];
+        }
+        att[(size_t)b * heads * HD + e] = num / den;
     }
 }
 
@@ -3232,11 +3368,20 @@ cudaError_t launch_rope_kv(float *q, int q_ld, const float *k, int k_ld, const f
     return cudaGetLastError();
 }
 
+size_t prefill_attention_part_floats(int heads, int head_dim, int positions)
+{
+    return (size_t)positions * heads * kPfMaxSplits * (head_dim + 2);
+}
+
 cudaError_t launch_prefill_attention(const float *q, int q_ld, const float *kc, const float *vc, int heads,
-                                     int kv_heads, int head_dim, int pos0, int n, float *att, cudaStream_t s)
+                                     int kv_heads, int head_dim, int pos0, int n, float *att, float *part,
+                                     cudaStream_t s)
 {
     const int G = heads / kv_heads;
-    if (head_dim != 64 || n <= 0 || G < 1 || G > kPfRows) return cudaErrorInvalidValue;
+    if (head_dim != 64 || n <= 0 || G < 1 || G > kPfRows || (q_ld & 1) || ((uintptr_t)q & 7u) ||
+        ((uintptr_t)kc & 7u))
+        return cudaErrorInvalidValue;
+    if ((kv_heads * head_dim) % 4 || ((uintptr_t)kc & 15u) || ((uintptr_t)vc & 15u)) return cudaErrorInvalidValue;
     auto kernel = prefill_attention_kernel<64>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -3244,9 +3389,18 @@ cudaError_t launch_prefill_attention(const float *q, int q_ld, const float *kc, 
     e = allow_max_smem((const void *)kernel, dev);
     if (e != cudaSuccess) return e;
     const int qt = kPfRows / G;  // positions per CTA: qt * G rows <= kPfRows
-    const dim3 grid((unsigned)kv_heads, (unsigned)((n + qt - 1) / qt));
-    kernel<<<grid, kPfWarps * 32, prefill_attention_smem(64), s>>>(q, q_ld, kc, vc, heads, kv_heads, pos0, n, qt,
-                                                                   att);
+    // at most 4 key tiles per CTA (a short causal critical path), at most
+    // kPfMaxSplits splits per query block
+    const int max_tiles = (pos0 + n - 1) / kPfKeys + 1;
+    int tps = 4;
+    if ((max_tiles + tps - 1) / tps > kPfMaxSplits) tps = (max_tiles + kPfMaxSplits - 1) / kPfMaxSplits;
+    const int zs = (max_tiles + tps - 1) / tps;
+    if (zs > 1 && part == nullptr) return cudaErrorInvalidValue;
+    const dim3 grid((unsigned)kv_heads, (unsigned)((n + qt - 1) / qt), (unsigned)zs);
+    kernel<<<grid, kPfWarps * 32, kPfSmem, s>>>(q, q_ld, kc, vc, heads, kv_heads, pos0, n, qt, tps, att, part);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || zs == 1) return e;
+    prefill_merge_kernel<64><<<n, kThreads, 0, s>>>(part, heads, kv_heads, pos0, n, qt, tps, att);
     return cudaGetLastError();
 }
 

@@ -78,7 +78,7 @@ struct QmvQwen2 {
     int pf_cap = 0;
     int *pf_ids = nullptr;
     float *pf_h = nullptr, *pf_xn = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_y = nullptr;
-    float *pf_gu = nullptr, *pf_g = nullptr;
+    float *pf_gu = nullptr, *pf_g = nullptr, *pf_part = nullptr;
     std::vector<cudaEvent_t> prof_events;  // profiled steps (created on first use)
     std::vector<void *> allocs;
     std::vector<QmvWeight *> weights;
@@ -603,7 +603,10 @@ int prefill_buffers(QmvQwen2 *m)
         !dalloc(m, (void **)&m->pf_att, C * dim * sizeof(float), "prefill activations") ||
         !dalloc(m, (void **)&m->pf_y, C * dim * sizeof(float), "prefill activations") ||
         !dalloc(m, (void **)&m->pf_gu, C * 2 * hid * sizeof(float), "prefill activations") ||
-        !dalloc(m, (void **)&m->pf_g, C * hid * sizeof(float), "prefill activations"))
+        !dalloc(m, (void **)&m->pf_g, C * hid * sizeof(float), "prefill activations") ||
+        !dalloc(m, (void **)&m->pf_part,
+                qmv::prefill_attention_part_floats(c.n_heads, m->head_dim, (int)C) * sizeof(float),
+                "prefill attention partials"))
         return 0;
     m->pf_cap = (int)C;
     return 1;
@@ -648,7 +651,7 @@ cudaError_t enqueue_prefill_chunk(QmvQwen2 *m, int pos0, int n)
                                     m->vc + off, m->stream);
         if (e == cudaSuccess)
             e = qmv::launch_prefill_attention(q, q_ld, m->kc + off, m->vc + off, c.n_heads, c.n_kv_heads, m->head_dim,
-                                              pos0, n, m->pf_att, m->stream);
+                                              pos0, n, m->pf_att, m->pf_part, m->stream);
         if (e == cudaSuccess) e = matmul(m, L.o, m->pf_att, n, m->pf_y);
         if (e == cudaSuccess) e = qmv::launch_add_rows(m->pf_h, m->pf_y, (size_t)n * dim, m->stream);
         if (e == cudaSuccess)
