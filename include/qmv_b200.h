@@ -107,6 +107,13 @@ int qmv_matvec(const QmvWeight *weight, const float *x, int x_count, float *y, i
 int qmv_matmul(const QmvWeight *weight, const float *X, int x_count, int batch, float *Y,
                int y_count, void *stream);
 
+/* H[p, :] += W X[p, :] (the residual projections of the reference's prefill,
+ * src/qwen2_architecture.cpp:1650-1655, :1679-1686): on the tensor cores from
+ * 32 positions, with K split across CTAs when that fills more SMs and the
+ * partial products summed into H in split order.  Device pointers. */
+int qmv_matmul_residual(const QmvWeight *weight, const float *X, int x_count, int batch, float *H,
+                        int h_count, void *stream);
+
 /* Bit-exact dequantisation of a resident weight into out[rows * cols]
  * (row-major).  Same bits as the reference's *_dequantize_block
  * (src/quantization.cpp:54-67, 161-184, 380-409, 588-615). */

@@ -54,7 +54,7 @@ C_SYMBOLS = [
     "qmv_gguf_tensor", "qmv_gguf_find_tensor", "qmv_gguf_get_uint", "qmv_gguf_get_float", "qmv_gguf_get_string",
     "qmv_gguf_get_array_info", "qmv_gguf_quantized_view", "qmv_gguf_upload", "qmv_qwen2_create_from_gguf",
     "qmv_set_profiling", "qmv_last_kernel_seconds", "qmv_qwen2_forward_profiled", "qmv_qwen2_prefill",
-    "qmv_qwen2_reset", "qmv_qwen2_stream",
+    "qmv_qwen2_reset", "qmv_qwen2_stream", "qmv_matmul_residual",
 ]
 CXX_DROPIN_SYMBOLS = {
     "quantized_tensor_matvec_f32": "_Z27quantized_tensor_matvec_f32PK23GgufQuantizedTensorViewPKfiPfi",
@@ -166,6 +166,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "qmv_resident_release_all": (I, []),
         "qmv_matvec": (I, [P, P, I, P, I, P]),
         "qmv_matmul": (I, [P, P, I, I, P, I, P]),
+        "qmv_matmul_residual": (I, [P, P, I, I, P, I, P]),
         "qmv_dequantize": (I, [P, P, U64, P]),
         "qmv_dequantize_raw": (I, [U32, P, U64, P, P]),
         "qmv_argmax_workspace_bytes": (SZ, []),
@@ -464,6 +465,11 @@ class Weight:
     def matmul(self, X_dev, batch: int, Y_dev, stream=None):
         _check(lib().qmv_matmul(self.handle, _ptr(X_dev), self.cols, batch, _ptr(Y_dev), self.rows,
                                 _ptr(stream)), "qmv_matmul")
+
+    def matmul_residual(self, X_dev, batch: int, H_dev, stream=None):
+        """H += W X over `batch` positions (device pointers)."""
+        _check(lib().qmv_matmul_residual(self.handle, _ptr(X_dev), self.cols, batch, _ptr(H_dev), self.rows,
+                                         _ptr(stream)), "qmv_matmul_residual")
 
     def matvec_argmax(self, x_dev, logits_dev, key_dev, workspace_dev, stream=None):
         _check(lib().qmv_matvec_argmax(self.handle, _ptr(x_dev), self.cols, _ptr(logits_dev),

@@ -425,6 +425,19 @@ QMV_EXPORT int qmv_matmul(const QmvWeight *w, const float *X, int x_count, int b
     return 1;
 }
 
+QMV_EXPORT int qmv_matmul_residual(const QmvWeight *w, const float *X, int x_count, int batch, float *H,
+                                   int h_count, void *stream)
+{
+    if (!check_weight(w)) return 0;
+    if (X == nullptr || H == nullptr) return fail("X or H is null");
+    if (batch <= 0) return fail("batch must be positive");
+    if (x_count != w->L.cols || h_count != w->L.rows)
+        return fail("counts (%d, %d) do not match the %d x %d weight", x_count, h_count, w->L.rows, w->L.cols);
+    if (!aligned16(X)) return fail("X must be 16-byte aligned");
+    QMV_CUDA(qmv::launch_matmul_residual(w->L, w->dev, X, batch, H, (cudaStream_t)stream), "matmul launch");
+    return 1;
+}
+
 QMV_EXPORT int qmv_dequantize(const QmvWeight *w, float *out, uint64_t out_count, void *stream)
 {
     if (!check_weight(w)) return 0;

@@ -117,6 +117,11 @@ cudaError_t launch_gemv_pair(const Layout &La, const uint8_t *wa, float *ya, con
 cudaError_t launch_gemv_exchange(const Layout &L, const uint8_t *w, const float *x, float *y,
                                  const ArgmaxOut &am, const Exchange &ex, cudaStream_t s);
 // Y[p] = W X[p], p < batch.
+// H [batch][rows] += W X (the prefill's residual projections): on the tensor
+// cores with K split across CTAs when that fills more SMs, the partial
+// products summed into H in split order; scratch from the stream-ordered pool.
+cudaError_t launch_matmul_residual(const Layout &L, const uint8_t *w, const float *X, int batch, float *H,
+                                   cudaStream_t s);
 cudaError_t launch_matmul(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
                           cudaStream_t s);
 // GEMV kernel selection: 0 automatic (TMA pipeline when its stages fit in

@@ -1613,10 +1613,11 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float v[8])
     for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// fp32 recomputation of one tile (rows r0.., positions p0..) on the CUDA cores.
+// fp32 recomputation of one tile (rows r0.., positions p0..) over columns
+// [kb, ke) on the CUDA cores.
 template <uint32_t FMT>
 __device__ void tc_tile_fallback(const Layout &L, const uint8_t *__restrict__ w, const float *__restrict__ X,
-                                 int np, float *__restrict__ Y, int r0, int p0, int tn)
+                                 int np, float *__restrict__ Y, int r0, int p0, int tn, int kb, int ke)
 {
     for (int o = threadIdx.x; o < kTcM * tn; o += blockDim.x) {
         const int row = r0 + (o % kTcM), pos = p0 + (o / kTcM);
@@ -1624,7 +1625,7 @@ __device__ void tc_tile_fallback(const Layout &L, const uint8_t *__restrict__ w,
         const uint8_t *rp = w + (uint64_t)row * L.row_stride;
         const float *xp = X + (size_t)pos * L.cols;
         float acc = 0.f;
-        for (int k0 = 0; k0 < L.cols; k0 += 8) {
+        for (int k0 = kb; k0 < ke; k0 += 8) {
             Raw8<FMT> raw;
             raw.load(rp, L, k0);
             float v[8];
@@ -1673,6 +1674,8 @@ split_x_kernel(const float *__restrict__ X, int np, int cols, int nk, uint8_t *_
 // WSMEM: the tile's resident rows are copied to shared memory once (when
 // they fit) and decoded from there; otherwise each decode thread loads its
 // bytes from global memory one stage ahead.  S: x stages in the ring.
+// Split K (gridDim.z > 1): CTA z takes stages [z nk / Z, (z + 1) nk / Z) and
+// writes its partial products to slice z of Y (np x rows floats each).
 template <uint32_t FMT, int TN, bool WSMEM>
 __global__ void __launch_bounds__(kTcThreads + 64, 1)
 matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ X,
@@ -1696,6 +1699,9 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int r0 = blockIdx.x * kTcM, pt = blockIdx.y, p0 = pt * TN;
     const int nk = (L.cols + kTcK - 1) / kTcK;
+    const int kc0 = (int)((long long)nk * blockIdx.z / gridDim.z), kc1 = (int)((long long)nk * (blockIdx.z + 1) / gridDim.z);
+    const int nloc = kc1 - kc0;  // this CTA's stages (>= 1: the host keeps splits <= nk)
+    Y += (size_t)blockIdx.z * (size_t)np * (size_t)L.rows;
     const uint32_t smem0 = (uint32_t)__cvta_generic_to_shared(smem);
     const uint32_t wbar0 = (uint32_t)__cvta_generic_to_shared(&bars[0]);
     const uint32_t xbar0 = wbar0 + 8u * S, ebar0 = wbar0 + 16u * S, tbar = wbar0 + 24u * S;
@@ -1741,7 +1747,7 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
             // the x images come from split_x_kernel, the launch this one
             // depends on (programmatic dependent launch)
             asm volatile("griddepcontrol.wait;" ::: "memory");
-            for (int j = 0; j < nk; ++j) {
+            for (int j = 0; j < nloc; ++j) {
                 const int s = j % S;
                 // buffer s is free once the MMAs of stage j - S are done
                 if (j >= S && !mbar_wait_idle(ebar0 + 8u * s, (uint32_t)((j / S - 1) & 1))) {
@@ -1749,14 +1755,14 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
                     break;
                 }
                 mbar_expect_tx(xbar0 + 8u * s, kStage);
-                bulk_g2s(smem0 + (uint32_t)s * kStage, ximg + (size_t)j * kStage, kStage, xbar0 + 8u * s);
+                bulk_g2s(smem0 + (uint32_t)s * kStage, ximg + (size_t)(kc0 + j) * kStage, kStage, xbar0 + 8u * s);
                 issued = j + 1;
             }
         }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------ MMA issue
         if (lane == 0) {
-            for (int kc = 0; kc < nk; ++kc) {
+            for (int kc = 0; kc < nloc; ++kc) {  // local stage index
                 const int s = kc % S;
                 const uint32_t par = (uint32_t)((kc / S) & 1);
                 if (!mbar_wait_idle(wbar0 + 8u * s, par) || !mbar_wait_idle(xbar0 + 8u * s, par)) {
@@ -1788,7 +1794,7 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
         const bool have_row = wrow_i < L.rows;
         const uint8_t *wrow = WSMEM ? wtile + (size_t)(32 * q + lane) * L.row_stride
                                     : w + (uint64_t)(have_row ? wrow_i : 0) * L.row_stride;
-        const int wk = kp * 8 * kTcUnits;
+        const int wk = kc0 * kTcK + kp * 8 * kTcUnits;  // first column of this thread's range
         const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16) + kTcACol + 4u * kTcUnits * kp;
         if (WSMEM && !mbar_wait(tbar, 0u)) ok = false;
         Raw8<FMT> wr[kTcUnits];
@@ -1799,7 +1805,7 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
         }
         int pending = -1;  // buffer whose tensor-memory stores are not yet published
         int s = 0, round = 0;  // buffer and ring round of stage kc
-        for (int kc = 0; kc < nk; ++kc, s = (s + 1 == S ? 0 : s + 1), round += (s == 0)) {
+        for (int kc = 0; kc < nloc; ++kc, s = (s + 1 == S ? 0 : s + 1), round += (s == 0)) {
             const int k0 = kc * kTcK + wk;
             Raw8<FMT> wn[kTcUnits];
             uint32_t h[4 * kTcUnits], l[4 * kTcUnits];
@@ -1856,7 +1862,7 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
 
     // every MMA has completed once the last stage's commit has arrived
     if (ok && (warp < kDecodeWarps || lane == 0)) {
-        const int last = nk - 1;
+        const int last = nloc - 1;
         if (!mbar_wait_idle(ebar0 + 8u * (last % S), (uint32_t)((last / S) & 1))) ok = false;
     }
     const bool failed = __syncthreads_or(!ok);
@@ -1896,7 +1902,8 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restric
     }
     // A non-finite weight or x makes the split planes NaN: recompute the
     // tile in fp32 (this overwrites every output the epilogue wrote).
-    if (__syncthreads_or(nonfinite) && !failed) tc_tile_fallback<FMT>(L, w, X, np, Y, r0, p0, TN);
+    if (__syncthreads_or(nonfinite) && !failed)
+        tc_tile_fallback<FMT>(L, w, X, np, Y, r0, p0, TN, kc0 * kTcK, min(kc1 * kTcK, L.cols));
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -3073,11 +3080,12 @@ constexpr int kTcMinBatch = 32;
 
 template <uint32_t FMT, int TN>
 cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
-                         cudaStream_t s)
+                         cudaStream_t s, int ksplit = 1)
 {
     // weight tile in shared memory when it leaves room for at least 3 x stages
     const uint32_t tile_max = (uint32_t)kTcM * (uint32_t)L.row_stride;
-    const bool wsmem = (uint64_t)kTcM * L.row_stride + 3u * tc_stage_bytes(TN) <= kTcSmemBudget;
+    // (a split CTA reads only its columns: it decodes from global memory)
+    const bool wsmem = ksplit == 1 && (uint64_t)kTcM * L.row_stride + 3u * tc_stage_bytes(TN) <= kTcSmemBudget;
     int S = wsmem ? (int)((kTcSmemBudget - tile_max) / tc_stage_bytes(TN)) : tc_stages(TN);
     if (S > kTcMaxStages) S = kTcMaxStages;
     auto kernel = wsmem ? matmul_tc_kernel<FMT, TN, true> : matmul_tc_kernel<FMT, TN, false>;
@@ -3086,7 +3094,8 @@ cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const float *X, int 
     if (e == cudaSuccess) e = allow_max_smem((const void *)kernel, dev);
     if (e != cudaSuccess) return e;
     const int n_pt = (batch + TN - 1) / TN, nk = (L.cols + kTcK - 1) / kTcK;
-    const dim3 grid((unsigned)((L.rows + kTcM - 1) / kTcM), (unsigned)n_pt);
+    if (ksplit < 1 || ksplit > nk) return cudaErrorInvalidValue;
+    const dim3 grid((unsigned)((L.rows + kTcM - 1) / kTcM), (unsigned)n_pt, (unsigned)ksplit);
     if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
     const size_t bytes = (size_t)n_pt * nk * tc_stage_bytes(TN);
     cudaMemPool_t pool;
@@ -3187,6 +3196,73 @@ cudaError_t matmul_fmt(const Layout &L, const uint8_t *w, const float *X, int ba
     if (done || e != cudaSuccess) return e;
     if (L.C <= 16) return matmul_go<FMT, 16>(L, w, X, batch, Y, s);
     return matmul_go<FMT, 32>(L, w, X, batch, Y, s);
+}
+
+// out += sum of ks partial slices of n floats (in slice order)
+__global__ void add_partials_kernel(float *__restrict__ out, const float *__restrict__ part, size_t n, int ks)
+{
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float acc = part[i];
+        for (int z = 1; z < ks; ++z) acc += part[(size_t)z * n + i];
+        out[i] += acc;
+    }
+}
+
+constexpr int kTcMaxSplit = 8;
+
+// Tile width and K split of the tensor-core kernel for a residual product:
+// the smallest (waves) x ((stages per CTA) x (per-stage cost) + a CTA's
+// prologue and epilogue) over the tile widths and splits (one CTA per SM),
+// fewer splits on ties.
+void tc_split_plan(int rows, int batch, int nk, int *tn_out, int *ks_out)
+{
+    static const int cand[] = {64, 128, 176, 256};
+    const long long row_tiles = (rows + kTcM - 1) / kTcM;
+    double best = 1e300;
+    for (int tn : cand) {
+        for (int ks = 1; ks <= kTcMaxSplit && ks <= nk; ++ks) {
+            const long long ctas = row_tiles * ((batch + tn - 1) / tn) * ks;
+            const long long waves = (ctas + sm_count() - 1) / sm_count();
+            const double alu = 900.0, mma = 8.4 * tn;
+            const double cost = (double)waves * ((double)((nk + ks - 1) / ks) * (alu > mma ? alu : mma) + 3000.0);
+            if (cost < best * 0.999) {
+                best = cost;
+                *tn_out = tn;
+                *ks_out = ks;
+            }
+        }
+    }
+}
+
+template <uint32_t FMT>
+cudaError_t matmul_residual_fmt(const Layout &L, const uint8_t *w, const float *X, int batch, float *H,
+                                cudaStream_t s)
+{
+    const bool tc_ok = ((uintptr_t)X & 15u) == 0;
+    const int nk = (L.cols + kTcK - 1) / kTcK;
+    int tn = 0, ks = 1;
+    if (g_matmul_path == 0 && batch >= kTcMinBatch && tc_ok) tc_split_plan(L.rows, batch, nk, &tn, &ks);
+    cudaMemPool_t pool;
+    cudaError_t e = scratch_pool(&pool);
+    if (e != cudaSuccess) return e;
+    const size_t n = (size_t)batch * (size_t)L.rows;
+    void *part = nullptr;
+    e = cudaMallocFromPoolAsync(&part, n * (size_t)ks * sizeof(float), pool, s);
+    if (e != cudaSuccess) return e;
+    float *P = (float *)part;
+    switch (tn) {
+    case 0: e = matmul_fmt<FMT>(L, w, X, batch, P, s); break;
+    case 64: e = matmul_tc_go<FMT, 64>(L, w, X, batch, P, s, ks); break;
+    case 128: e = matmul_tc_go<FMT, 128>(L, w, X, batch, P, s, ks); break;
+    case 176: e = matmul_tc_go<FMT, 176>(L, w, X, batch, P, s, ks); break;
+    default: e = matmul_tc_go<FMT, 256>(L, w, X, batch, P, s, ks); break;
+    }
+    if (e == cudaSuccess) {
+        add_partials_kernel<<<grid_for(n, kThreads), kThreads, 0, s>>>(H, P, n, ks);
+        e = cudaGetLastError();
+    }
+    const cudaError_t f = cudaFreeAsync(part, s);
+    return e != cudaSuccess ? e : f;
 }
 
 }  // namespace
@@ -3480,6 +3556,19 @@ cudaError_t launch_gemv_pair(const Layout &La, const uint8_t *wa, float *ya, con
     QMV_PAIR(kQ4_K, kQ6_K)
 #undef QMV_PAIR
     return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_matmul_residual(const Layout &L, const uint8_t *w, const float *X, int batch, float *H,
+                                   cudaStream_t s)
+{
+    if (batch <= 0) return cudaErrorInvalidValue;
+    switch (L.type) {
+    case kQ8_0: return matmul_residual_fmt<kQ8_0>(L, w, X, batch, H, s);
+    case kQ5_0: return matmul_residual_fmt<kQ5_0>(L, w, X, batch, H, s);
+    case kQ4_K: return matmul_residual_fmt<kQ4_K>(L, w, X, batch, H, s);
+    case kQ6_K: return matmul_residual_fmt<kQ6_K>(L, w, X, batch, H, s);
+    default: return cudaErrorInvalidValue;
+    }
 }
 
 cudaError_t launch_matmul(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,

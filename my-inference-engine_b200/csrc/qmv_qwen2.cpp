@@ -652,8 +652,7 @@ cudaError_t enqueue_prefill_chunk(QmvQwen2 *m, int pos0, int n)
         if (e == cudaSuccess)
             e = qmv::launch_prefill_attention(q, q_ld, m->kc + off, m->vc + off, c.n_heads, c.n_kv_heads, m->head_dim,
                                               pos0, n, m->pf_att, m->pf_part, m->stream);
-        if (e == cudaSuccess) e = matmul(m, L.o, m->pf_att, n, m->pf_y);
-        if (e == cudaSuccess) e = qmv::launch_add_rows(m->pf_h, m->pf_y, (size_t)n * dim, m->stream);
+        if (e == cudaSuccess) e = qmv::launch_matmul_residual(L.o->L, L.o->dev, m->pf_att, n, m->pf_h, m->stream);
         if (e == cudaSuccess)
             e = qmv::launch_rmsnorm_rows(m->pf_h, L.ffn_norm, c.rms_norm_epsilon, dim, n, m->pf_xn, m->stream);
         if (L.gate_up) {  // [gate | up] rows of 2 * hid
@@ -666,8 +665,8 @@ cudaError_t enqueue_prefill_chunk(QmvQwen2 *m, int pos0, int n)
             if (e == cudaSuccess) e = matmul(m, L.up, m->pf_xn, n, up);
             if (e == cudaSuccess) e = qmv::launch_swiglu_rows(m->pf_gu, hid, up, hid, hid, n, m->pf_g, m->stream);
         }
-        if (e == cudaSuccess) e = matmul(m, L.down, m->pf_g, n, m->pf_y);
-        if (e == cudaSuccess) e = qmv::launch_add_rows(m->pf_h, m->pf_y, (size_t)n * dim, m->stream);
+        if (e == cudaSuccess)
+            e = qmv::launch_matmul_residual(L.down->L, L.down->dev, m->pf_g, n, m->pf_h, m->stream);
     }
     return e;
 }

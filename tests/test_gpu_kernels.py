@@ -241,6 +241,30 @@ def device_matmul(torch, qmv, gtype, blocks, rows, cols, X):
 
 
 @pytest.mark.parametrize("gtype,rows,cols,batch", [
+    (Q5_0, 896, 4864, 1024),  # the prefill's down projection: K split across CTAs
+    (Q8_0, 896, 896, 1024), (Q4_K, 129, 3584, 70), (Q6_K, 300, 512, 33), (Q5_0, 257, 96, 5)])
+def test_matmul_residual(cuda, qmv, oracle, workloads, gtype, rows, cols, batch):
+    """H += W X (qmv_matmul_residual: split-K partial products on the tensor
+    cores, summed into H) against H0 + the oracle's matmul."""
+    torch = cuda
+    blocks = workloads.make_blocks(gtype, rows, cols, seed=9)
+    X = np.stack([workloads.make_activations(cols, seed=70 + p) for p in range(batch)])
+    H0 = np.stack([workloads.make_activations(rows, seed=900 + p) for p in range(batch)])
+    w = qmv.Weight(gtype, blocks, rows, cols)
+    Xd = to_dev(torch, X.astype(np.float32))
+    Hd = to_dev(torch, H0.astype(np.float32))
+    w.matmul_residual(Xd.data_ptr(), batch, Hd.data_ptr())
+    torch.cuda.synchronize()
+    w.free()
+    H = Hd.cpu().numpy()
+    Y_ref = oracle.matmul(gtype, blocks, rows, cols, X, batch)
+    S = abs_dot_all(oracle, gtype, blocks, rows, cols, X) + np.abs(H0)
+    bad, err, bound = tolerance_ok((H - H0).ravel(), Y_ref.ravel(), S.ravel(), REL_TOL)
+    assert bad.size == 0, (bad[:5], err[bad[:5]], bound[bad[:5]])
+    assert qmv.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("gtype,rows,cols,batch", [
     (Q5_0, 4864, 896, 512),   # the batched-prefill benchmark shape, every output checked
     (Q8_0, 300, 896, 70), (Q5_0, 257, 96, 1), (Q4_K, 129, 3584, 33), (Q6_K, 129, 3584, 130),
     (Q4_K, 40, 18944, 64), (Q6_K, 1000, 256, 200), (Q8_0, 128, 32, 13), (Q5_0, 131, 64, 257)])
