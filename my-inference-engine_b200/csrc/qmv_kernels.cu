@@ -2432,7 +2432,7 @@ __global__ void rope_kv_kernel(float *__restrict__ q, int q_ld, const float *__r
 }
 
 constexpr int kPfKeys = 64;   // keys per shared-memory tile
-constexpr int kPfWarps = 4;   // 16 query rows each (one m16 tile)
+constexpr int kPfWarps = 8;   // 16 query rows each (one m16 tile)
 constexpr int kPfRows = 16 * kPfWarps;
 constexpr int kPfPairs = kPfKeys / 2 + 4;  // 32-bit words per smem row: 64 bf16 + 8 of padding
 // dynamic shared memory: the raw fp32 K and V rows of the next tile (filled by
