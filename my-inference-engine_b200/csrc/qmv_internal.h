@@ -122,6 +122,15 @@ cudaError_t launch_gemv_exchange(const Layout &L, const uint8_t *w, const float 
 // products summed into H in split order; scratch from the stream-ordered pool.
 cudaError_t launch_matmul_residual(const Layout &L, const uint8_t *w, const float *X, int batch, float *H,
                                    cudaStream_t s);
+// The same product left as *ks partial slices of batch x rows floats in
+// stream-ordered scratch (free with cudaFreeAsync on s after summing them):
+// launch_rmsnorm_residual folds them into the residual stream and normalises
+// it in one pass; launch_add_partials only adds them.
+cudaError_t launch_matmul_partials(const Layout &L, const uint8_t *w, const float *X, int batch, float **part,
+                                   int *ks, cudaStream_t s);
+cudaError_t launch_rmsnorm_residual(float *h, const float *part, int ks, const float *w, float eps, int cols,
+                                    int rows, float *out, cudaStream_t s);
+cudaError_t launch_add_partials(float *h, const float *part, size_t n, int ks, cudaStream_t s);
 cudaError_t launch_matmul(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
                           cudaStream_t s);
 // GEMV kernel selection: 0 automatic (TMA pipeline when its stages fit in
@@ -169,9 +178,11 @@ cudaError_t launch_rope_kv(float *q, int q_ld, const float *k, int k_ld, const f
 // part: prefill_attention_part_floats(heads, head_dim, n) floats of scratch
 // (partials of rows whose keys are split across CTAs)
 size_t prefill_attention_part_floats(int heads, int head_dim, int positions);
+// counter: kv_heads x n zeroed words (arrivals of a block's split CTAs;
+// each block's merging CTA re-arms its own)
 cudaError_t launch_prefill_attention(const float *q, int q_ld, const float *kc, const float *vc, int heads,
                                      int kv_heads, int head_dim, int pos0, int n, float *att, float *part,
-                                     cudaStream_t s);
+                                     unsigned int *counter, cudaStream_t s);
 cudaError_t launch_add_rows(float *h, const float *y, size_t n, cudaStream_t s);
 cudaError_t launch_swiglu_rows(const float *gate, int g_ld, const float *up, int u_ld, int cols, int rows,
                                float *out, cudaStream_t s);

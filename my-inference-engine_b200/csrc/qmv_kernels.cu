@@ -2493,8 +2493,10 @@ __device__ __forceinline__ int pf_tiles(int pos0, int b0, int nq) { return (pos0
 // qt positions, key-range split z of tps tiles); a CTA's rows are (position,
 // query head of group g), 16 per warp.  A block whose keys span one split
 // writes its rows normalised to att; otherwise each split stores its rows'
-// (running max, sum of exp, unnormalised output) in part and
-// prefill_merge_kernel combines them.  Keys and values stream through shared memory 64 at a time from the
+// (running max, sum of exp, unnormalised output) in part, and the block's
+// last split CTA to finish (an arrival counter, re-armed by it) combines them:
+// out = sum_z e^(m_z - M) o_z / sum_z e^(m_z - M) l_z, the softmax over all
+// of a row's keys.  Keys and values stream through shared memory 64 at a time from the
 // layer's cache (which already holds this chunk's keys) as bf16 hi/lo parts;
 // Q K^T and P V run on the tensor cores (mma.sync m16n8k16) with three
 // products per split pair (dropping only lo x lo, ~2^-16 relative), fp32
@@ -2502,10 +2504,10 @@ __device__ __forceinline__ int pf_tiles(int pos0, int b0, int nq) { return (pos0
 // accumulator layout is the A-fragment layout of P, so scores never leave
 // registers.  Scores are divided by sqrt(head_dim) as the reference does.
 template <int HD>
-__global__ void __launch_bounds__(kPfWarps * 32)
+__global__ void __launch_bounds__(kPfWarps * 32, 2)
 prefill_attention_kernel(const float *__restrict__ q, int q_ld, const float *__restrict__ kc,
                          const float *__restrict__ vc, int heads, int kv_heads, int pos0, int n, int qt, int tps,
-                         float *__restrict__ att, float *__restrict__ part)
+                         float *__restrict__ att, float *__restrict__ part, unsigned int *__restrict__ counter)
 {
     static_assert(HD == 64, "four 16-wide K steps, eight 8-wide output tiles");
     extern __shared__ __align__(16) float pf_sm[];
@@ -2667,32 +2669,51 @@ prefill_attention_kernel(const float *__restrict__ q, int q_ld, const float *__r
             }
         }
     }
-}
-
-// Rows whose keys were split: out = sum_z e^(m_z - M) o_z / sum_z e^(m_z - M) l_z
-// (the softmax over all their keys).  One CTA per position.
-template <int HD>
-__global__ void prefill_merge_kernel(const float *__restrict__ part, int heads, int kv_heads, int pos0, int n,
-                                     int qt, int tps, float *__restrict__ att)
-{
-    const int b = blockIdx.x, y = b / qt, b0 = y * qt, nq = min(qt, n - b0);
-    const int splits = (pf_tiles(pos0, b0, nq) + tps - 1) / tps;
     if (splits == 1) return;
-    (void)kv_heads;
-    for (int e = threadIdx.x; e < heads * HD; e += blockDim.x) {
-        const int head = e / HD, d = e % HD;
-        const float *pp = part + (size_t)(b * heads + head) * kPfMaxSplits * (HD + 2);
+    // the last split CTA of this block merges every split's rows
+    __shared__ int last_cta;
+    __threadfence();
+    __syncthreads();
+    unsigned int *cnt = counter + (size_t)kvh * gridDim.y + blockIdx.y;
+    if (tid == 0) last_cta = atomicAdd(cnt, 1u) == (unsigned)(splits - 1);
+    __syncthreads();
+    if (!last_cta) return;
+    __threadfence();
+    float *wgt = reinterpret_cast<float *>(&kh[0][0]);  // [row][split] weights, then 1 / denominator per row
+    float *inv = wgt + kPfRows * kPfMaxSplits;
+    for (int r = tid; r < rows; r += kPfWarps * 32) {
+        const float *pp = part + (size_t)((b0 + r / G) * heads + kvh * G + r % G) * kPfMaxSplits * (HD + 2);
         float M = -INFINITY;
-        for (int z = 0; z < splits; ++z) M = fmaxf(M, pp[z * (HD + 2)]);
-        float den = 0.f, num = 0.f;
-        for (int z = 0; z < splits; ++z) {
-            const float mz = pp[z * (HD + 2)];
-            const float w = mz == -INFINITY ? 0.f : expf(mz - M);
-            den += w * pp[z * (HD + 2) + 1];
-            num += w * pp[z * (HD + 2) + 2 + d];
+        for (int zz = 0; zz < splits; ++zz) M = fmaxf(M, pp[zz * (HD + 2)]);
+        float den = 0.f;
+        for (int zz = 0; zz < splits; ++zz) {
+            const float mz = pp[zz * (HD + 2)];
+            const float wz = mz == -INFINITY ? 0.f : expf(mz - M);
+            wgt[r * kPfMaxSplits + zz] = wz;
+            den += wz * pp[zz * (HD + 2) + 1];
         }
-        att[(size_t)b * heads * HD + e] = num / den;
+        inv[r] = den;
     }
+    __syncthreads();
+    // two output columns per thread and step, every split's loads issued together
+#pragma unroll 2
+    for (int e = tid; e < rows * (HD / 2); e += kPfWarps * 32) {
+        const int r = e / (HD / 2), d = 2 * (e % (HD / 2)), b = b0 + r / G, head = kvh * G + r % G;
+        const float *pp = part + (size_t)(b * heads + head) * kPfMaxSplits * (HD + 2) + 2 + d;
+        float2 v[kPfMaxSplits];
+#pragma unroll
+        for (int zz = 0; zz < kPfMaxSplits; ++zz)
+            v[zz] = zz < splits ? *reinterpret_cast<const float2 *>(pp + zz * (HD + 2)) : f2(0.f, 0.f);
+        float n0 = 0.f, n1 = 0.f;
+#pragma unroll
+        for (int zz = 0; zz < kPfMaxSplits; ++zz) {
+            const float wz = zz < splits ? wgt[r * kPfMaxSplits + zz] : 0.f;
+            n0 += wz * v[zz].x;
+            n1 += wz * v[zz].y;
+        }
+        *reinterpret_cast<float2 *>(att + (size_t)b * dim + head * HD + d) = f2(n0 / inv[r], n1 / inv[r]);
+    }
+    if (tid == 0) *cnt = 0u;
 }
 
 // h += y over n floats (the residual additions, :1653-1655, :1684-1686).
@@ -3234,9 +3255,11 @@ void tc_split_plan(int rows, int batch, int nk, int *tn_out, int *ks_out)
     }
 }
 
+// W X as ks partial slices in scratch from the stream-ordered pool (the
+// caller sums them and frees the scratch on the same stream).
 template <uint32_t FMT>
-cudaError_t matmul_residual_fmt(const Layout &L, const uint8_t *w, const float *X, int batch, float *H,
-                                cudaStream_t s)
+cudaError_t matmul_partials_fmt(const Layout &L, const uint8_t *w, const float *X, int batch, float **part_out,
+                                int *ks_out, cudaStream_t s)
 {
     const bool tc_ok = ((uintptr_t)X & 15u) == 0;
     const int nk = (L.cols + kTcK - 1) / kTcK;
@@ -3257,11 +3280,57 @@ cudaError_t matmul_residual_fmt(const Layout &L, const uint8_t *w, const float *
     case 176: e = matmul_tc_go<FMT, 176>(L, w, X, batch, P, s, ks); break;
     default: e = matmul_tc_go<FMT, 256>(L, w, X, batch, P, s, ks); break;
     }
-    if (e == cudaSuccess) {
-        add_partials_kernel<<<grid_for(n, kThreads), kThreads, 0, s>>>(H, P, n, ks);
-        e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        cudaFreeAsync(part, s);
+        return e;
     }
-    const cudaError_t f = cudaFreeAsync(part, s);
+    *part_out = P;
+    *ks_out = ks;
+    return cudaSuccess;
+}
+
+// One CTA per row: h += the ks partial slices (in slice order), then
+// out = (h / sqrt(mean(h^2) + eps)) * w (tensor_rms_norm_f32 of the updated
+// residual stream).
+__global__ void __launch_bounds__(kRowThreads)
+rmsnorm_residual_kernel(float *__restrict__ h, const float *__restrict__ part, size_t slice, int ks,
+                        const float *__restrict__ w, float eps, int cols, float *__restrict__ out)
+{
+    __shared__ float red[kRowThreads / 32];
+    float *hr = h + (size_t)blockIdx.x * cols;
+    const float *pr = part + (size_t)blockIdx.x * cols;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < cols; i += kRowThreads) {
+        float acc = pr[i];
+        for (int z = 1; z < ks; ++z) acc += pr[(size_t)z * slice + i];
+        const float v = hr[i] + acc;
+        hr[i] = v;
+        ss += v * v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kRowThreads / 32; ++i) ss += red[i];
+    const float denom = sqrtf(ss / (float)cols + eps);
+    float *orow = out + (size_t)blockIdx.x * cols;
+    for (int i = threadIdx.x; i < cols; i += kRowThreads) orow[i] = (hr[i] / denom) * w[i];
+}
+
+template <uint32_t FMT>
+cudaError_t matmul_residual_fmt(const Layout &L, const uint8_t *w, const float *X, int batch, float *H,
+                                cudaStream_t s)
+{
+    float *P = nullptr;
+    int ks = 1;
+    cudaError_t e = matmul_partials_fmt<FMT>(L, w, X, batch, &P, &ks, s);
+    if (e != cudaSuccess) return e;
+    const size_t n = (size_t)batch * (size_t)L.rows;
+    add_partials_kernel<<<grid_for(n, kThreads), kThreads, 0, s>>>(H, P, n, ks);
+    e = cudaGetLastError();
+    const cudaError_t f = cudaFreeAsync(P, s);
     return e != cudaSuccess ? e : f;
 }
 
@@ -3451,7 +3520,7 @@ size_t prefill_attention_part_floats(int heads, int head_dim, int positions)
 
 cudaError_t launch_prefill_attention(const float *q, int q_ld, const float *kc, const float *vc, int heads,
                                      int kv_heads, int head_dim, int pos0, int n, float *att, float *part,
-                                     cudaStream_t s)
+                                     unsigned int *counter, cudaStream_t s)
 {
     const int G = heads / kv_heads;
     if (head_dim != 64 || n <= 0 || G < 1 || G > kPfRows || (q_ld & 1) || ((uintptr_t)q & 7u) ||
@@ -3472,11 +3541,10 @@ cudaError_t launch_prefill_attention(const float *q, int q_ld, const float *kc, 
     if ((max_tiles + tps - 1) / tps > kPfMaxSplits) tps = (max_tiles + kPfMaxSplits - 1) / kPfMaxSplits;
     const int zs = (max_tiles + tps - 1) / tps;
     if (zs > 1 && part == nullptr) return cudaErrorInvalidValue;
+    if (zs > 1 && counter == nullptr) return cudaErrorInvalidValue;
     const dim3 grid((unsigned)kv_heads, (unsigned)((n + qt - 1) / qt), (unsigned)zs);
-    kernel<<<grid, kPfWarps * 32, kPfSmem, s>>>(q, q_ld, kc, vc, heads, kv_heads, pos0, n, qt, tps, att, part);
-    e = cudaGetLastError();
-    if (e != cudaSuccess || zs == 1) return e;
-    prefill_merge_kernel<64><<<n, kThreads, 0, s>>>(part, heads, kv_heads, pos0, n, qt, tps, att);
+    kernel<<<grid, kPfWarps * 32, kPfSmem, s>>>(q, q_ld, kc, vc, heads, kv_heads, pos0, n, qt, tps, att, part,
+                                                counter);
     return cudaGetLastError();
 }
 
@@ -3556,6 +3624,33 @@ cudaError_t launch_gemv_pair(const Layout &La, const uint8_t *wa, float *ya, con
     QMV_PAIR(kQ4_K, kQ6_K)
 #undef QMV_PAIR
     return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_matmul_partials(const Layout &L, const uint8_t *w, const float *X, int batch, float **part,
+                                   int *ks, cudaStream_t s)
+{
+    if (batch <= 0) return cudaErrorInvalidValue;
+    switch (L.type) {
+    case kQ8_0: return matmul_partials_fmt<kQ8_0>(L, w, X, batch, part, ks, s);
+    case kQ5_0: return matmul_partials_fmt<kQ5_0>(L, w, X, batch, part, ks, s);
+    case kQ4_K: return matmul_partials_fmt<kQ4_K>(L, w, X, batch, part, ks, s);
+    case kQ6_K: return matmul_partials_fmt<kQ6_K>(L, w, X, batch, part, ks, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_rmsnorm_residual(float *h, const float *part, int ks, const float *w, float eps, int cols,
+                                    int rows, float *out, cudaStream_t s)
+{
+    if (rows <= 0 || cols <= 0 || ks < 1) return cudaErrorInvalidValue;
+    rmsnorm_residual_kernel<<<rows, kRowThreads, 0, s>>>(h, part, (size_t)rows * cols, ks, w, eps, cols, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_add_partials(float *h, const float *part, size_t n, int ks, cudaStream_t s)
+{
+    add_partials_kernel<<<grid_for(n, kThreads), kThreads, 0, s>>>(h, part, n, ks);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_matmul_residual(const Layout &L, const uint8_t *w, const float *X, int batch, float *H,

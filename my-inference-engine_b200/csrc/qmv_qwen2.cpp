@@ -79,6 +79,9 @@ struct QmvQwen2 {
     int *pf_ids = nullptr;
     float *pf_h = nullptr, *pf_xn = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_y = nullptr;
     float *pf_gu = nullptr, *pf_g = nullptr, *pf_part = nullptr;
+    unsigned int *pf_cnt = nullptr;
+    cudaStream_t pf_side = nullptr;  // up projection beside gate (different formats)
+    cudaEvent_t pf_fork = nullptr, pf_join = nullptr;
     std::vector<cudaEvent_t> prof_events;  // profiled steps (created on first use)
     std::vector<void *> allocs;
     std::vector<QmvWeight *> weights;
@@ -277,6 +280,9 @@ int check_state(QmvQwen2 *m, qmv::DecodeState *out)
 void release(QmvQwen2 *m)
 {
     for (cudaEvent_t ev : m->prof_events) cudaEventDestroy(ev);
+    if (m->pf_fork) cudaEventDestroy(m->pf_fork);
+    if (m->pf_join) cudaEventDestroy(m->pf_join);
+    if (m->pf_side) cudaStreamDestroy(m->pf_side);
     if (m->exec) cudaGraphExecDestroy(m->exec);
     for (QmvWeight *w : m->weights) qmv_weight_free(w);
     for (void *p : m->allocs) cudaFree(p);
@@ -606,8 +612,12 @@ int prefill_buffers(QmvQwen2 *m)
         !dalloc(m, (void **)&m->pf_g, C * hid * sizeof(float), "prefill activations") ||
         !dalloc(m, (void **)&m->pf_part,
                 qmv::prefill_attention_part_floats(c.n_heads, m->head_dim, (int)C) * sizeof(float),
-                "prefill attention partials"))
+                "prefill attention partials") ||
+        !dalloc(m, (void **)&m->pf_cnt, (size_t)c.n_kv_heads * C * sizeof(unsigned int), "prefill counters"))
         return 0;
+    QW_CUDA(cudaStreamCreateWithFlags(&m->pf_side, cudaStreamNonBlocking), "prefill stream");
+    QW_CUDA(cudaEventCreateWithFlags(&m->pf_fork, cudaEventDisableTiming), "prefill event");
+    QW_CUDA(cudaEventCreateWithFlags(&m->pf_join, cudaEventDisableTiming), "prefill event");
     m->pf_cap = (int)C;
     return 1;
 }
@@ -619,15 +629,32 @@ cudaError_t matmul(QmvQwen2 *m, const QmvWeight *w, const float *X, int n, float
 
 // Positions pos0 .. pos0 + n - 1 (ids already on the device) through every
 // layer: the reference's per-chunk schedule (src/qwen2_architecture.cpp:
-// 1586-1690) with the chunk's positions batched in every projection.
+// 1586-1690) with the chunk's positions batched in every projection.  The
+// residual projections (o, down) leave split-K partial products that the next
+// RMSNorm folds into the residual stream; gate and up of different formats
+// run on two streams so their CTAs share the SMs.
 cudaError_t enqueue_prefill_chunk(QmvQwen2 *m, int pos0, int n)
 {
     const QmvQwen2Config &c = m->cfg;
     const int dim = c.dim, hid = c.hidden_dim, kvd = m->kvd;
-    cudaError_t e = qmv::launch_embed_rows(m->embd->L, m->embd->dev, m->pf_ids, n, m->pf_h, &m->st->error, m->stream);
+    cudaStream_t st = m->stream;
+    float *pend = nullptr;  // the previous down projection's partials, not yet in h
+    int pend_ks = 0;
+    auto fold = [&](const float *norm) {  // h += pending partials; xn = rmsnorm(h)
+        cudaError_t e = pend ? qmv::launch_rmsnorm_residual(m->pf_h, pend, pend_ks, norm, c.rms_norm_epsilon, dim, n,
+                                                            m->pf_xn, st)
+                             : qmv::launch_rmsnorm_rows(m->pf_h, norm, c.rms_norm_epsilon, dim, n, m->pf_xn, st);
+        if (pend) {
+            const cudaError_t f = cudaFreeAsync(pend, st);
+            if (e == cudaSuccess) e = f;
+            pend = nullptr;
+        }
+        return e;
+    };
+    cudaError_t e = qmv::launch_embed_rows(m->embd->L, m->embd->dev, m->pf_ids, n, m->pf_h, &m->st->error, st);
     for (int l = 0; l < c.n_layers && e == cudaSuccess; ++l) {
         const Layer &L = m->layers[(size_t)l];
-        e = qmv::launch_rmsnorm_rows(m->pf_h, L.attn_norm, c.rms_norm_epsilon, dim, n, m->pf_xn, m->stream);
+        e = fold(L.attn_norm);
         float *q = m->pf_qkv, *k, *v;
         int q_ld, k_ld, v_ld;
         if (L.qkv) {
@@ -648,25 +675,33 @@ cudaError_t enqueue_prefill_chunk(QmvQwen2 *m, int pos0, int n)
         if (e == cudaSuccess)
             e = qmv::launch_rope_kv(q, q_ld, k, k_ld, v, v_ld, L.bias_qkv, L.bias_qkv + dim, L.bias_qkv + dim + kvd,
                                     c.n_heads, c.n_kv_heads, m->head_dim, pos0, n, c.rope_frequency_base, m->kc + off,
-                                    m->vc + off, m->stream);
+                                    m->vc + off, st);
         if (e == cudaSuccess)
             e = qmv::launch_prefill_attention(q, q_ld, m->kc + off, m->vc + off, c.n_heads, c.n_kv_heads, m->head_dim,
-                                              pos0, n, m->pf_att, m->pf_part, m->stream);
-        if (e == cudaSuccess) e = qmv::launch_matmul_residual(L.o->L, L.o->dev, m->pf_att, n, m->pf_h, m->stream);
-        if (e == cudaSuccess)
-            e = qmv::launch_rmsnorm_rows(m->pf_h, L.ffn_norm, c.rms_norm_epsilon, dim, n, m->pf_xn, m->stream);
+                                              pos0, n, m->pf_att, m->pf_part, m->pf_cnt, st);
+        if (e == cudaSuccess) e = qmv::launch_matmul_partials(L.o->L, L.o->dev, m->pf_att, n, &pend, &pend_ks, st);
+        if (e == cudaSuccess) e = fold(L.ffn_norm);
         if (L.gate_up) {  // [gate | up] rows of 2 * hid
             if (e == cudaSuccess) e = matmul(m, L.gate_up, m->pf_xn, n, m->pf_gu);
             if (e == cudaSuccess)
-                e = qmv::launch_swiglu_rows(m->pf_gu, 2 * hid, m->pf_gu + hid, 2 * hid, hid, n, m->pf_g, m->stream);
+                e = qmv::launch_swiglu_rows(m->pf_gu, 2 * hid, m->pf_gu + hid, 2 * hid, hid, n, m->pf_g, st);
         } else {
             float *up = m->pf_gu + (size_t)n * hid;
+            if (e == cudaSuccess) e = cudaEventRecord(m->pf_fork, st);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(m->pf_side, m->pf_fork, 0);
+            if (e == cudaSuccess) e = qmv::launch_matmul(L.up->L, L.up->dev, m->pf_xn, n, up, m->pf_side);
             if (e == cudaSuccess) e = matmul(m, L.gate, m->pf_xn, n, m->pf_gu);
-            if (e == cudaSuccess) e = matmul(m, L.up, m->pf_xn, n, up);
-            if (e == cudaSuccess) e = qmv::launch_swiglu_rows(m->pf_gu, hid, up, hid, hid, n, m->pf_g, m->stream);
+            if (e == cudaSuccess) e = cudaEventRecord(m->pf_join, m->pf_side);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(st, m->pf_join, 0);
+            if (e == cudaSuccess) e = qmv::launch_swiglu_rows(m->pf_gu, hid, up, hid, hid, n, m->pf_g, st);
         }
         if (e == cudaSuccess)
-            e = qmv::launch_matmul_residual(L.down->L, L.down->dev, m->pf_g, n, m->pf_h, m->stream);
+            e = qmv::launch_matmul_partials(L.down->L, L.down->dev, m->pf_g, n, &pend, &pend_ks, st);
+    }
+    if (pend) {  // the last layer's down projection
+        if (e == cudaSuccess) e = qmv::launch_add_partials(m->pf_h, pend, (size_t)n * dim, pend_ks, st);
+        const cudaError_t f = cudaFreeAsync(pend, st);
+        if (e == cudaSuccess) e = f;
     }
     return e;
 }
