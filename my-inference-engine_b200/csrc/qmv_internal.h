@@ -86,6 +86,15 @@ struct Exchange {
 };
 size_t exchange_parity_bytes(int world, int slot_rows);
 
+// x of a batched matmul: x[p][k] = x[p * ldx + k], or, with up set,
+// up[p * ldu + k] * silu(x[p * ldx + k]) (a SwiGLU formed as x is read).
+struct XSource {
+    const float *x;
+    const float *up;
+    int ldx;
+    int ldu;
+};
+
 // Fused prologue / epilogue of a GEMV (the decode step's RMSNorm, SwiGLU,
 // bias and residual additions); device pointers.  Zero-initialised: none.
 enum : int { kPreNone = 0, kPreRmsNorm = 1, kPreSwiGlu = 2 };
@@ -128,6 +137,10 @@ cudaError_t launch_matmul_residual(const Layout &L, const uint8_t *w, const floa
 // it in one pass; launch_add_partials only adds them.
 cudaError_t launch_matmul_partials(const Layout &L, const uint8_t *w, const float *X, int batch, float **part,
                                    int *ks, cudaStream_t s);
+// The same with x = up * silu(gate) formed as x is read (the prefill's down
+// projection): gate and up rows g_ld / u_ld floats apart.
+cudaError_t launch_matmul_partials_swiglu(const Layout &L, const uint8_t *w, const float *gate, int g_ld,
+                                          const float *up, int u_ld, int batch, float **part, int *ks, cudaStream_t s);
 cudaError_t launch_rmsnorm_residual(float *h, const float *part, int ks, const float *w, float eps, int cols,
                                     int rows, float *out, cudaStream_t s);
 cudaError_t launch_add_partials(float *h, const float *part, size_t n, int ks, cudaStream_t s);

@@ -1613,17 +1613,25 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float v[8])
     for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// x of position pos, column k: X[pos][k], or up[pos][k] * silu(X[pos][k])
+// when the source carries the SwiGLU of a [gate | up] pair
+// (transformer_swiglu_f32, src/transformer_ops.cpp:163-178).
+__device__ __forceinline__ float x_at(const XSource &src, int pos, int k)
+{
+    const float g = src.x[(size_t)pos * src.ldx + k];
+    return src.up ? src.up[(size_t)pos * src.ldu + k] * (g / (1.0f + expf(-g))) : g;
+}
+
 // fp32 recomputation of one tile (rows r0.., positions p0..) over columns
 // [kb, ke) on the CUDA cores.
 template <uint32_t FMT>
-__device__ void tc_tile_fallback(const Layout &L, const uint8_t *__restrict__ w, const float *__restrict__ X,
-                                 int np, float *__restrict__ Y, int r0, int p0, int tn, int kb, int ke)
+__device__ void tc_tile_fallback(const Layout &L, const uint8_t *__restrict__ w, const XSource &src, int np,
+                                 float *__restrict__ Y, int r0, int p0, int tn, int kb, int ke)
 {
     for (int o = threadIdx.x; o < kTcM * tn; o += blockDim.x) {
         const int row = r0 + (o % kTcM), pos = p0 + (o / kTcM);
         if (row >= L.rows || pos >= np) continue;
         const uint8_t *rp = w + (uint64_t)row * L.row_stride;
-        const float *xp = X + (size_t)pos * L.cols;
         float acc = 0.f;
         for (int k0 = kb; k0 < ke; k0 += 8) {
             Raw8<FMT> raw;
@@ -1631,7 +1639,7 @@ __device__ void tc_tile_fallback(const Layout &L, const uint8_t *__restrict__ w,
             float v[8];
             raw.decode(k0, v);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc += v[i] * xp[k0 + i];
+            for (int i = 0; i < 8; ++i) acc += v[i] * x_at(src, pos, k0 + i);
         }
         Y[(size_t)pos * L.rows + row] = acc;
     }
@@ -1642,7 +1650,7 @@ __device__ void tc_tile_fallback(const Layout &L, const uint8_t *__restrict__ w,
 // so the tile's accumulator turns non-finite and the tile is recomputed.
 template <int TN>
 __global__ void __launch_bounds__(kThreads)
-split_x_kernel(const float *__restrict__ X, int np, int cols, int nk, uint8_t *__restrict__ xs)
+split_x_kernel(XSource src, int np, int cols, int nk, uint8_t *__restrict__ xs)
 {
     constexpr uint32_t kPlaneX = tc_plane_x(TN);
     constexpr int kUnits = TN * (kTcK / 8);
@@ -1661,10 +1669,19 @@ split_x_kernel(const float *__restrict__ X, int np, int cols, int nk, uint8_t *_
         const int k0 = kc * kTcK + ((u >> 3) % KG) * 8;
         float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         if (pos < np && k0 < cols) {
-            const float4 a = __ldg((const float4 *)(X + (size_t)pos * cols + k0));
-            const float4 b = __ldg((const float4 *)(X + (size_t)pos * cols + k0 + 4));
+            const float *xp = src.x + (size_t)pos * src.ldx + k0;
+            const float4 a = __ldg((const float4 *)xp);
+            const float4 b = __ldg((const float4 *)(xp + 4));
             v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
             v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+            if (src.up) {  // x = up * silu(gate)
+                const float *up = src.up + (size_t)pos * src.ldu + k0;
+                const float4 c = __ldg((const float4 *)up);
+                const float4 d = __ldg((const float4 *)(up + 4));
+                const float u[8] = {c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = u[i] * (v[i] / (1.0f + expf(-v[i])));
+            }
         }
         uint8_t *dst = xs + (size_t)img * 2u * kPlaneX;
         split_store(v, dst, dst + kPlaneX, (uint32_t)u * 16u);
@@ -1678,8 +1695,8 @@ split_x_kernel(const float *__restrict__ X, int np, int cols, int nk, uint8_t *_
 // writes its partial products to slice z of Y (np x rows floats each).
 template <uint32_t FMT, int TN, bool WSMEM>
 __global__ void __launch_bounds__(kTcThreads + 64, 1)
-matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ X,
-                 const uint8_t *__restrict__ xs, int np, float *__restrict__ Y, int S)
+matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, XSource X, const uint8_t *__restrict__ xs, int np,
+                 float *__restrict__ Y, int S)
 {
     static_assert(TN % 16 == 0 && TN >= 32 && TN <= 256, "N of one MMA: a multiple of 16 in 32..256");
     static_assert(kTcM * (kTcK / 8) == kTcThreads * kTcUnits, "kTcUnits weight units per decode thread and stage");
@@ -3100,7 +3117,7 @@ int g_matmul_path = 0;
 constexpr int kTcMinBatch = 32;
 
 template <uint32_t FMT, int TN>
-cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
+cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const XSource &X, int batch, float *Y,
                          cudaStream_t s, int ksplit = 1)
 {
     // weight tile in shared memory when it leaves room for at least 3 x stages
@@ -3206,10 +3223,10 @@ cudaError_t matmul_fmt(const Layout &L, const uint8_t *w, const float *X, int ba
     if (g_matmul_path >= 2 || (g_matmul_path == 0 && batch >= kTcMinBatch && tc_ok)) {
         if (!tc_ok) return cudaErrorMisalignedAddress;
         switch (g_matmul_path > 2 ? g_matmul_path : tc_tile_width(L.rows, batch)) {
-        case 64: return matmul_tc_go<FMT, 64>(L, w, X, batch, Y, s);
-        case 128: return matmul_tc_go<FMT, 128>(L, w, X, batch, Y, s);
-        case 176: return matmul_tc_go<FMT, 176>(L, w, X, batch, Y, s);
-        default: return matmul_tc_go<FMT, 256>(L, w, X, batch, Y, s);
+        case 64: return matmul_tc_go<FMT, 64>(L, w, XSource{X, nullptr, L.cols, 0}, batch, Y, s);
+        case 128: return matmul_tc_go<FMT, 128>(L, w, XSource{X, nullptr, L.cols, 0}, batch, Y, s);
+        case 176: return matmul_tc_go<FMT, 176>(L, w, XSource{X, nullptr, L.cols, 0}, batch, Y, s);
+        default: return matmul_tc_go<FMT, 256>(L, w, XSource{X, nullptr, L.cols, 0}, batch, Y, s);
         }
     }
     bool done = false;
@@ -3257,11 +3274,13 @@ void tc_split_plan(int rows, int batch, int nk, int *tn_out, int *ks_out)
 
 // W X as ks partial slices in scratch from the stream-ordered pool (the
 // caller sums them and frees the scratch on the same stream).
+// up != nullptr: x = up * silu(X) (row strides ldx, ldu), formed as x is read.
 template <uint32_t FMT>
 cudaError_t matmul_partials_fmt(const Layout &L, const uint8_t *w, const float *X, int batch, float **part_out,
-                                int *ks_out, cudaStream_t s)
+                                int *ks_out, cudaStream_t s, const float *up = nullptr, int ldx = 0, int ldu = 0)
 {
-    const bool tc_ok = ((uintptr_t)X & 15u) == 0;
+    const bool tc_ok = ((uintptr_t)X & 15u) == 0 &&
+                       (up == nullptr || (((uintptr_t)up & 15u) == 0 && ldx % 4 == 0 && ldu % 4 == 0));
     const int nk = (L.cols + kTcK - 1) / kTcK;
     int tn = 0, ks = 1;
     if (g_matmul_path == 0 && batch >= kTcMinBatch && tc_ok) tc_split_plan(L.rows, batch, nk, &tn, &ks);
@@ -3273,13 +3292,26 @@ cudaError_t matmul_partials_fmt(const Layout &L, const uint8_t *w, const float *
     e = cudaMallocFromPoolAsync(&part, n * (size_t)ks * sizeof(float), pool, s);
     if (e != cudaSuccess) return e;
     float *P = (float *)part;
-    switch (tn) {
-    case 0: e = matmul_fmt<FMT>(L, w, X, batch, P, s); break;
-    case 64: e = matmul_tc_go<FMT, 64>(L, w, X, batch, P, s, ks); break;
-    case 128: e = matmul_tc_go<FMT, 128>(L, w, X, batch, P, s, ks); break;
-    case 176: e = matmul_tc_go<FMT, 176>(L, w, X, batch, P, s, ks); break;
-    default: e = matmul_tc_go<FMT, 256>(L, w, X, batch, P, s, ks); break;
+    const XSource src{X, up, up ? ldx : L.cols, ldu};
+    void *xbuf = nullptr;
+    if (tn == 0 && up) {  // the CUDA-core paths read a plain x: materialise up * silu(gate)
+        e = cudaMallocFromPoolAsync(&xbuf, (size_t)batch * L.cols * sizeof(float), pool, s);
+        if (e == cudaSuccess) {
+            swiglu_rows_kernel<<<grid_for((uint64_t)batch * L.cols, kThreads), kThreads, 0, s>>>(
+                X, ldx, up, ldu, L.cols, batch, (float *)xbuf);
+            e = cudaGetLastError();
+        }
     }
+    if (e == cudaSuccess) {
+        switch (tn) {
+        case 0: e = matmul_fmt<FMT>(L, w, xbuf ? (const float *)xbuf : X, batch, P, s); break;
+        case 64: e = matmul_tc_go<FMT, 64>(L, w, src, batch, P, s, ks); break;
+        case 128: e = matmul_tc_go<FMT, 128>(L, w, src, batch, P, s, ks); break;
+        case 176: e = matmul_tc_go<FMT, 176>(L, w, src, batch, P, s, ks); break;
+        default: e = matmul_tc_go<FMT, 256>(L, w, src, batch, P, s, ks); break;
+        }
+    }
+    if (xbuf) cudaFreeAsync(xbuf, s);
     if (e != cudaSuccess) {
         cudaFreeAsync(part, s);
         return e;
@@ -3635,6 +3667,19 @@ cudaError_t launch_matmul_partials(const Layout &L, const uint8_t *w, const floa
     case kQ5_0: return matmul_partials_fmt<kQ5_0>(L, w, X, batch, part, ks, s);
     case kQ4_K: return matmul_partials_fmt<kQ4_K>(L, w, X, batch, part, ks, s);
     case kQ6_K: return matmul_partials_fmt<kQ6_K>(L, w, X, batch, part, ks, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_matmul_partials_swiglu(const Layout &L, const uint8_t *w, const float *gate, int g_ld,
+                                          const float *up, int u_ld, int batch, float **part, int *ks, cudaStream_t s)
+{
+    if (batch <= 0 || gate == nullptr || up == nullptr) return cudaErrorInvalidValue;
+    switch (L.type) {
+    case kQ8_0: return matmul_partials_fmt<kQ8_0>(L, w, gate, batch, part, ks, s, up, g_ld, u_ld);
+    case kQ5_0: return matmul_partials_fmt<kQ5_0>(L, w, gate, batch, part, ks, s, up, g_ld, u_ld);
+    case kQ4_K: return matmul_partials_fmt<kQ4_K>(L, w, gate, batch, part, ks, s, up, g_ld, u_ld);
+    case kQ6_K: return matmul_partials_fmt<kQ6_K>(L, w, gate, batch, part, ks, s, up, g_ld, u_ld);
     default: return cudaErrorInvalidValue;
     }
 }

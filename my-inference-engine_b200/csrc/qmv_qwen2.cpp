@@ -78,7 +78,7 @@ struct QmvQwen2 {
     int pf_cap = 0;
     int *pf_ids = nullptr;
     float *pf_h = nullptr, *pf_xn = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_y = nullptr;
-    float *pf_gu = nullptr, *pf_g = nullptr, *pf_part = nullptr;
+    float *pf_gu = nullptr, *pf_part = nullptr;
     unsigned int *pf_cnt = nullptr;
     cudaStream_t pf_side = nullptr;  // up projection beside gate (different formats)
     cudaEvent_t pf_fork = nullptr, pf_join = nullptr;
@@ -609,7 +609,6 @@ int prefill_buffers(QmvQwen2 *m)
         !dalloc(m, (void **)&m->pf_att, C * dim * sizeof(float), "prefill activations") ||
         !dalloc(m, (void **)&m->pf_y, C * dim * sizeof(float), "prefill activations") ||
         !dalloc(m, (void **)&m->pf_gu, C * 2 * hid * sizeof(float), "prefill activations") ||
-        !dalloc(m, (void **)&m->pf_g, C * hid * sizeof(float), "prefill activations") ||
         !dalloc(m, (void **)&m->pf_part,
                 qmv::prefill_attention_part_floats(c.n_heads, m->head_dim, (int)C) * sizeof(float),
                 "prefill attention partials") ||
@@ -681,10 +680,12 @@ cudaError_t enqueue_prefill_chunk(QmvQwen2 *m, int pos0, int n)
                                               pos0, n, m->pf_att, m->pf_part, m->pf_cnt, st);
         if (e == cudaSuccess) e = qmv::launch_matmul_partials(L.o->L, L.o->dev, m->pf_att, n, &pend, &pend_ks, st);
         if (e == cudaSuccess) e = fold(L.ffn_norm);
+        // the down projection reads x = up * silu(gate) straight from the
+        // gate / up outputs (the SwiGLU is formed as its x is split)
+        const float *gate = m->pf_gu, *upv = m->pf_gu + hid;
+        int g_ld = 2 * hid, u_ld = 2 * hid;
         if (L.gate_up) {  // [gate | up] rows of 2 * hid
             if (e == cudaSuccess) e = matmul(m, L.gate_up, m->pf_xn, n, m->pf_gu);
-            if (e == cudaSuccess)
-                e = qmv::launch_swiglu_rows(m->pf_gu, 2 * hid, m->pf_gu + hid, 2 * hid, hid, n, m->pf_g, st);
         } else {
             float *up = m->pf_gu + (size_t)n * hid;
             if (e == cudaSuccess) e = cudaEventRecord(m->pf_fork, st);
@@ -693,10 +694,12 @@ cudaError_t enqueue_prefill_chunk(QmvQwen2 *m, int pos0, int n)
             if (e == cudaSuccess) e = matmul(m, L.gate, m->pf_xn, n, m->pf_gu);
             if (e == cudaSuccess) e = cudaEventRecord(m->pf_join, m->pf_side);
             if (e == cudaSuccess) e = cudaStreamWaitEvent(st, m->pf_join, 0);
-            if (e == cudaSuccess) e = qmv::launch_swiglu_rows(m->pf_gu, hid, up, hid, hid, n, m->pf_g, st);
+            upv = up;
+            g_ld = u_ld = hid;
         }
         if (e == cudaSuccess)
-            e = qmv::launch_matmul_partials(L.down->L, L.down->dev, m->pf_g, n, &pend, &pend_ks, st);
+            e = qmv::launch_matmul_partials_swiglu(L.down->L, L.down->dev, gate, g_ld, upv, u_ld, n, &pend, &pend_ks,
+                                                   st);
     }
     if (pend) {  // the last layer's down projection
         if (e == cudaSuccess) e = qmv::launch_add_partials(m->pf_h, pend, (size_t)n * dim, pend_ks, st);
