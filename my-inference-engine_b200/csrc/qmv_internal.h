@@ -196,9 +196,7 @@ size_t prefill_attention_part_floats(int heads, int head_dim, int positions);
 cudaError_t launch_prefill_attention(const float *q, int q_ld, const float *kc, const float *vc, int heads,
                                      int kv_heads, int head_dim, int pos0, int n, float *att, float *part,
                                      unsigned int *counter, cudaStream_t s);
-cudaError_t launch_add_rows(float *h, const float *y, size_t n, cudaStream_t s);
-cudaError_t launch_swiglu_rows(const float *gate, int g_ld, const float *up, int u_ld, int cols, int rows,
-                               float *out, cudaStream_t s);
+
 
 // Argmax key of logits[0..n).
 cudaError_t launch_argmax(const float *logits, int n, const ArgmaxOut &am, cudaStream_t s);

@@ -2733,13 +2733,6 @@ prefill_attention_kernel(const float *__restrict__ q, int q_ld, const float *__r
     if (tid == 0) *cnt = 0u;
 }
 
-// h += y over n floats (the residual additions, :1653-1655, :1684-1686).
-__global__ void add_rows_kernel(float *__restrict__ h, const float *__restrict__ y, size_t n)
-{
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        h[i] += y[i];
-}
-
 // out = up * silu(gate) row by row (transformer_swiglu_f32,
 // src/transformer_ops.cpp:163-178); gate and up may be the halves of one
 // [gate | up] row.
@@ -3577,20 +3570,6 @@ cudaError_t launch_prefill_attention(const float *q, int q_ld, const float *kc, 
     const dim3 grid((unsigned)kv_heads, (unsigned)((n + qt - 1) / qt), (unsigned)zs);
     kernel<<<grid, kPfWarps * 32, kPfSmem, s>>>(q, q_ld, kc, vc, heads, kv_heads, pos0, n, qt, tps, att, part,
                                                 counter);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_add_rows(float *h, const float *y, size_t n, cudaStream_t s)
-{
-    add_rows_kernel<<<grid_for(n, kThreads), kThreads, 0, s>>>(h, y, n);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_swiglu_rows(const float *gate, int g_ld, const float *up, int u_ld, int cols, int rows,
-                               float *out, cudaStream_t s)
-{
-    swiglu_rows_kernel<<<grid_for((uint64_t)rows * cols, kThreads), kThreads, 0, s>>>(gate, g_ld, up, u_ld, cols,
-                                                                                       rows, out);
     return cudaGetLastError();
 }
 
