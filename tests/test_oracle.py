@@ -410,3 +410,36 @@ def test_qwen2_decode_step_matches_reference(oracle, ref, workloads):
             token = int(np.argmax(logits_ref))
     finally:
         reference.close()
+
+
+def test_reference_prefill_equals_stepwise_oracle(oracle, ref, workloads):
+    """The reference's chunked prefill (qwen2_prefill_tokens, chunks of 8
+    positions, batched projections) computes exactly what the oracle's
+    one-token steps compute: the last position's logits and every key/value
+    written are identical bit for bit.  So the prefill oracle is the decode
+    oracle, and chunking (1024-position chunks on the device) changes no
+    arithmetic the reference defines."""
+    ob = load_oracle_binding()
+    m = workloads.make_qwen2("qwen2_tiny", seed=1)
+    ids = (np.arange(29) * 53 + 5) % m["vocab"]
+    max_ctx = 40
+    kvd = m["kv_heads"] * (m["dim"] // m["heads"])
+    K = np.zeros((m["layers"], max_ctx, kvd), np.float32)
+    V = np.zeros_like(K)
+    model_c = ob.qwen2_oracle_model(m, max_ctx)
+    for pos, t in enumerate(ids):
+        ok, logits = ob.oracle_qwen2_forward(oracle, model_c[0], K, V, pos, int(t))
+        assert ok
+    reference = ob.RefQwen2(m, workloads.qwen2_tensor_list(m), max_ctx)
+    try:
+        reference.reset()
+        ok, ref_logits = reference.prefill(ids)
+        assert ok
+        assert np.array_equal(ref_logits.view(np.uint32), logits.view(np.uint32))
+        for layer in range(m["layers"]):
+            for pos in range(len(ids)):
+                k, v = reference.get_kv(layer, pos)
+                assert np.array_equal(k.view(np.uint32), K[layer, pos].view(np.uint32)), (layer, pos)
+                assert np.array_equal(v.view(np.uint32), V[layer, pos].view(np.uint32)), (layer, pos)
+    finally:
+        reference.close()
