@@ -652,7 +652,7 @@ class GgufFile:
 
     @staticmethod
     def _tensor_dict(t: QmvGgufTensor) -> dict:
-        return dict(name=t.name.decode(), ggml_type=t.ggml_type,
+        return dict(name=t.name.decode("utf-8", "surrogateescape"), ggml_type=t.ggml_type,
                     dimensions=[t.dimensions[i] for i in range(t.dimension_count)], offset=t.offset,
                     byte_size=t.byte_size, data=t.data)
 
@@ -666,7 +666,7 @@ class GgufFile:
 
     def find_tensor(self, name: str) -> dict:
         t = QmvGgufTensor()
-        _check(lib().qmv_gguf_find_tensor(self.handle, name.encode(), ctypes.byref(t)), "qmv_gguf_find_tensor")
+        _check(lib().qmv_gguf_find_tensor(self.handle, name.encode("utf-8", "surrogateescape"), ctypes.byref(t)), "qmv_gguf_find_tensor")
         return self._tensor_dict(t)
 
     def get_uint(self, key: str):
@@ -692,7 +692,7 @@ class GgufFile:
     def quantized_view(self, name: str):
         """The packed view (GgufQuantizedTensorView) of a tensor, or None."""
         v = GgufQuantizedTensorView()
-        return v if lib().qmv_gguf_quantized_view(self.handle, name.encode(), ctypes.byref(v)) else None
+        return v if lib().qmv_gguf_quantized_view(self.handle, name.encode("utf-8", "surrogateescape"), ctypes.byref(v)) else None
 
     def upload(self):
         """Make every packed 2-D tensor resident; (tensors, device bytes)."""

@@ -182,8 +182,10 @@ bool element_count(const QmvGguf::Tensor &t, uint64_t *n)
 const QmvGguf::Meta *find_meta(const QmvGguf *g, const char *key)
 {
     if (g == nullptr || key == nullptr) return nullptr;
+    // C-string comparison, as the reference's (a key holding a NUL byte
+    // matches up to it)
     for (const QmvGguf::Meta &m : g->meta)
-        if (m.key == key) return &m;  // the first entry of that name
+        if (strcmp(m.key.c_str(), key) == 0) return &m;  // the first entry of that name
     return nullptr;
 }
 
@@ -191,7 +193,7 @@ const QmvGguf::Tensor *find_tensor(const QmvGguf *g, const char *name)
 {
     if (g == nullptr || name == nullptr) return nullptr;
     for (const QmvGguf::Tensor &t : g->tensors)
-        if (t.name == name) return &t;
+        if (strcmp(t.name.c_str(), name) == 0) return &t;
     return nullptr;
 }
 
@@ -248,7 +250,7 @@ int parse(QmvGguf *g)
     }
     for (size_t i = 0; i < g->tensors.size(); ++i)
         for (size_t j = 0; j < i; ++j)
-            if (g->tensors[i].name == g->tensors[j].name)
+            if (strcmp(g->tensors[i].name.c_str(), g->tensors[j].name.c_str()) == 0)
                 return qmv::set_error("GGUF tensor directory has duplicate names");
     const uint64_t end = c.at;
     if (end > UINT64_MAX - (g->alignment - 1)) return qmv::set_error("GGUF tensor directory size overflows");

@@ -366,7 +366,8 @@ class RefGguf:
             dims, off, nb = (ctypes.c_uint64 * 4)(), ctypes.c_uint64(), ctypes.c_uint64()
             self.lib.ref_gguf_tensor(self.h, i, ctypes.byref(name), ctypes.byref(t), ctypes.byref(nd), dims,
                                      ctypes.byref(off), ctypes.byref(nb))
-            out.append(dict(name=name.value.decode(), ggml_type=t.value, dimensions=list(dims[:nd.value]),
+            out.append(dict(name=name.value.decode("utf-8", "surrogateescape"), ggml_type=t.value,
+                            dimensions=list(dims[:nd.value]),
                             offset=off.value, byte_size=nb.value))
         return out
 
@@ -393,7 +394,7 @@ class RefGguf:
     def quantized_view(self, name: str, view_type):
         """(view fields as a dict with the data offset in the image), or None."""
         v, at = view_type(), ctypes.c_uint64()
-        if not self.lib.ref_gguf_quantized_view(self.h, name.encode(), ctypes.byref(v), ctypes.byref(at)):
+        if not self.lib.ref_gguf_quantized_view(self.h, name.encode("utf-8", "surrogateescape"), ctypes.byref(v), ctypes.byref(at)):
             return None
         return dict(data_at=at.value, ggml_type=v.ggml_type, dimensions=list(v.dimensions[:v.dimension_count]),
                     element_count=v.element_count, block_elements=v.block_elements, block_bytes=v.block_bytes,

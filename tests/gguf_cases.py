@@ -102,6 +102,10 @@ def cases(wl):
         ("tensor_offset_misaligned", G.gguf_image([arch], [q8[:4] + (8,)])),
         ("tensor_offset_past_end", G.gguf_image([arch], [q8[:4] + (1 << 40,)])),
         ("tensor_duplicate_names", G.gguf_image([arch], [q8, ("w.q8",) + q8[1:]])),
+        # names and keys compare as C strings: equal up to a NUL byte is equal
+        ("tensor_names_equal_up_to_nul", G.gguf_image([arch], [("w\0a",) + q8[1:], ("w\0b",) + q8[1:]])),
+        ("architecture_key_with_nul_suffix", G.gguf_image([("general.architecture\0x", G.GGUF_STRING, "qwen2")],
+                                                           [q8])),
         ("tensor_data_truncated", G.gguf_image([arch], [q8], truncate=1)),
         ("tensor_data_exact_end", G.gguf_image([arch], [f32, q8])),
         # the image ends with the directory (no data section at all)
