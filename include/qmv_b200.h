@@ -378,6 +378,31 @@ int qmv_gguf_get_uint(const QmvGguf *gguf, const char *key, uint64_t *value);
 int qmv_gguf_get_float(const QmvGguf *gguf, const char *key, double *value);
 int qmv_gguf_get_string(const QmvGguf *gguf, const char *key, const char **value, uint64_t *length);
 int qmv_gguf_get_array_info(const QmvGguf *gguf, const char *key, uint32_t *element_type, uint64_t *count);
+/* gguf_get_bool (src/gguf_reader.h:89). */
+int qmv_gguf_get_bool(const QmvGguf *gguf, const char *key, int *value);
+/* Sequential reads of one top-level array (GgufArrayCursor and
+ * gguf_array_cursor_init / gguf_array_next_string / _uint / _int,
+ * src/gguf_reader.h:64-69, :89-94): each read checks the element type and
+ * the image bounds; strings point into the image. */
+typedef struct QmvGgufArrayCursor {
+    const QmvGguf *gguf;
+    uint64_t position;
+    uint64_t remaining;
+    uint32_t element_type;
+} QmvGgufArrayCursor;
+int qmv_gguf_array_cursor_init(const QmvGguf *gguf, const char *key, QmvGgufArrayCursor *cursor);
+int qmv_gguf_array_next_string(QmvGgufArrayCursor *cursor, const char **value, uint64_t *length);
+int qmv_gguf_array_next_uint(QmvGgufArrayCursor *cursor, uint64_t *value);
+int qmv_gguf_array_next_int(QmvGgufArrayCursor *cursor, int64_t *value);
+/* gguf_get_f32_tensor_view (src/gguf_reader.h:99-118; same fields as its
+ * GgufF32TensorView): F32 tensors only, cleared on every failure. */
+typedef struct QmvGgufF32View {
+    const float *data;
+    uint32_t dimension_count;
+    uint64_t dimensions[4];
+    uint64_t element_count;
+} QmvGgufF32View;
+int qmv_gguf_f32_view(const QmvGguf *gguf, const char *name, QmvGgufF32View *view);
 /* gguf_get_quantized_tensor_view (src/gguf_reader.h:136-140): the view is
  * cleared on every failure (0, no message). */
 int qmv_gguf_quantized_view(const QmvGguf *gguf, const char *name, GgufQuantizedTensorView *view);

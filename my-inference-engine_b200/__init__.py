@@ -54,7 +54,9 @@ C_SYMBOLS = [
     "qmv_gguf_tensor", "qmv_gguf_find_tensor", "qmv_gguf_get_uint", "qmv_gguf_get_float", "qmv_gguf_get_string",
     "qmv_gguf_get_array_info", "qmv_gguf_quantized_view", "qmv_gguf_upload", "qmv_qwen2_create_from_gguf",
     "qmv_set_profiling", "qmv_last_kernel_seconds", "qmv_qwen2_forward_profiled", "qmv_qwen2_prefill",
-    "qmv_qwen2_reset", "qmv_qwen2_stream", "qmv_matmul_residual",
+    "qmv_qwen2_reset", "qmv_qwen2_stream", "qmv_matmul_residual", "qmv_gguf_get_bool",
+    "qmv_gguf_array_cursor_init", "qmv_gguf_array_next_string", "qmv_gguf_array_next_uint",
+    "qmv_gguf_array_next_int", "qmv_gguf_f32_view",
 ]
 CXX_DROPIN_SYMBOLS = {
     "quantized_tensor_matvec_f32": "_Z27quantized_tensor_matvec_f32PK23GgufQuantizedTensorViewPKfiPfi",
@@ -89,6 +91,20 @@ class QmvGgufTensor(ctypes.Structure):
         ("byte_size", ctypes.c_uint64),
         ("data", ctypes.c_void_p),
     ]
+
+
+class QmvGgufArrayCursor(ctypes.Structure):
+    """Position in one top-level GGUF array (include/qmv_b200.h)."""
+
+    _fields_ = [("gguf", ctypes.c_void_p), ("position", ctypes.c_uint64), ("remaining", ctypes.c_uint64),
+                ("element_type", ctypes.c_uint32)]
+
+
+class QmvGgufF32View(ctypes.Structure):
+    """An F32 tensor of a GGUF image (the reference's GgufF32TensorView fields)."""
+
+    _fields_ = [("data", ctypes.c_void_p), ("dimension_count", ctypes.c_uint32),
+                ("dimensions", ctypes.c_uint64 * 4), ("element_count", ctypes.c_uint64)]
 
 
 class QmvOperationProfile(ctypes.Structure):
@@ -207,6 +223,13 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "qmv_gguf_get_string": (I, [P, ctypes.c_char_p, ctypes.POINTER(P), ctypes.POINTER(U64)]),
         "qmv_gguf_get_array_info": (I, [P, ctypes.c_char_p, ctypes.POINTER(U32), ctypes.POINTER(U64)]),
         "qmv_gguf_quantized_view": (I, [P, ctypes.c_char_p, VP]),
+        "qmv_gguf_get_bool": (I, [P, ctypes.c_char_p, ctypes.POINTER(I)]),
+        "qmv_gguf_array_cursor_init": (I, [P, ctypes.c_char_p, ctypes.POINTER(QmvGgufArrayCursor)]),
+        "qmv_gguf_array_next_string": (I, [ctypes.POINTER(QmvGgufArrayCursor), ctypes.POINTER(P),
+                                           ctypes.POINTER(U64)]),
+        "qmv_gguf_array_next_uint": (I, [ctypes.POINTER(QmvGgufArrayCursor), ctypes.POINTER(U64)]),
+        "qmv_gguf_array_next_int": (I, [ctypes.POINTER(QmvGgufArrayCursor), ctypes.POINTER(ctypes.c_int64)]),
+        "qmv_gguf_f32_view": (I, [P, ctypes.c_char_p, ctypes.POINTER(QmvGgufF32View)]),
         "qmv_gguf_upload": (I, [P, IP, ctypes.POINTER(U64)]),
         "qmv_qwen2_create_from_gguf": (I, [P, I, ctypes.POINTER(P)]),
         "qmv_set_profiling": (I, [I]),
@@ -688,6 +711,42 @@ class GgufFile:
         if not lib().qmv_gguf_get_array_info(self.handle, key.encode(), ctypes.byref(t), ctypes.byref(n)):
             return None
         return t.value, n.value
+
+    def get_bool(self, key: str):
+        v = ctypes.c_int()
+        return v.value if lib().qmv_gguf_get_bool(self.handle, key.encode(), ctypes.byref(v)) else None
+
+    def array_read(self, key: str, kind: int, max_items: int = 64):
+        """Elements of a top-level array through the cursor readers (kind 0
+        strings as bytes, 1 unsigned, 2 signed), up to the first failed read
+        or max_items; None when the cursor does not open."""
+        cur = QmvGgufArrayCursor()
+        if not lib().qmv_gguf_array_cursor_init(self.handle, key.encode(), ctypes.byref(cur)):
+            return None
+        out = []
+        for _ in range(max_items):
+            if kind == 0:
+                p, n = ctypes.c_void_p(), ctypes.c_uint64()
+                if not lib().qmv_gguf_array_next_string(ctypes.byref(cur), ctypes.byref(p), ctypes.byref(n)):
+                    break
+                out.append(ctypes.string_at(p.value, n.value) if n.value else b"")
+            elif kind == 1:
+                v = ctypes.c_uint64()
+                if not lib().qmv_gguf_array_next_uint(ctypes.byref(cur), ctypes.byref(v)):
+                    break
+                out.append(v.value)
+            else:
+                v = ctypes.c_int64()
+                if not lib().qmv_gguf_array_next_int(ctypes.byref(cur), ctypes.byref(v)):
+                    break
+                out.append(v.value)
+        return out
+
+    def f32_view(self, name: str):
+        """The F32 view of a tensor (QmvGgufF32View), or None."""
+        v = QmvGgufF32View()
+        ok = lib().qmv_gguf_f32_view(self.handle, name.encode("utf-8", "surrogateescape"), ctypes.byref(v))
+        return v if ok else None
 
     def quantized_view(self, name: str):
         """The packed view (GgufQuantizedTensorView) of a tensor, or None."""

@@ -407,6 +407,98 @@ QMV_EXPORT int qmv_gguf_get_array_info(const QmvGguf *g, const char *key, uint32
     return 1;
 }
 
+// gguf_get_bool (src/gguf_reader.cpp:375-388): a bool entry's byte != 0.
+QMV_EXPORT int qmv_gguf_get_bool(const QmvGguf *g, const char *key, int *value)
+{
+    const QmvGguf::Meta *m = find_meta(g, key);
+    if (m == nullptr || value == nullptr || m->type != 7 || m->value_at >= g->size) return 0;
+    *value = g->data[m->value_at] != 0;
+    return 1;
+}
+
+// Sequential reads of one top-level array (gguf_array_cursor_init and the
+// next_* readers, src/gguf_reader.cpp:390-489): the cursor sits on the next
+// element; each read checks the element type and the image bounds.
+QMV_EXPORT int qmv_gguf_array_cursor_init(const QmvGguf *g, const char *key, QmvGgufArrayCursor *cursor)
+{
+    const QmvGguf::Meta *m = find_meta(g, key);
+    if (m == nullptr || cursor == nullptr || m->type != 9) return 0;
+    Cursor c{g->data, g->size, m->value_at};
+    uint32_t et = 0;
+    uint64_t count = 0;
+    if (!c.u32(&et) || !c.u64(&count) || et != m->array_type || count != m->array_count) return 0;
+    cursor->gguf = g;
+    cursor->position = c.at;
+    cursor->remaining = count;
+    cursor->element_type = et;
+    return 1;
+}
+
+QMV_EXPORT int qmv_gguf_array_next_string(QmvGgufArrayCursor *cursor, const char **value, uint64_t *length)
+{
+    if (cursor == nullptr || value == nullptr || length == nullptr || cursor->gguf == nullptr ||
+        cursor->remaining == 0 || cursor->element_type != 8)
+        return 0;
+    Cursor c{cursor->gguf->data, cursor->gguf->size, cursor->position};
+    uint64_t n = 0;
+    if (!c.u64(&n) || !c.has(n)) return 0;
+    *value = (const char *)(c.p + c.at);
+    *length = n;
+    cursor->position = c.at + n;
+    --cursor->remaining;
+    return 1;
+}
+
+QMV_EXPORT int qmv_gguf_array_next_uint(QmvGgufArrayCursor *cursor, uint64_t *value)
+{
+    if (cursor == nullptr || value == nullptr || cursor->gguf == nullptr || cursor->remaining == 0 ||
+        !is_unsigned(cursor->element_type))
+        return 0;
+    Cursor c{cursor->gguf->data, cursor->gguf->size, cursor->position};
+    uint64_t v = 0;
+    if (!c.le(value_width(cursor->element_type), &v)) return 0;
+    cursor->position = c.at;
+    --cursor->remaining;
+    *value = v;
+    return 1;
+}
+
+QMV_EXPORT int qmv_gguf_array_next_int(QmvGgufArrayCursor *cursor, int64_t *value)
+{
+    const uint32_t t = cursor ? cursor->element_type : 0u;
+    if (cursor == nullptr || value == nullptr || cursor->gguf == nullptr || cursor->remaining == 0 ||
+        !(t == 1 || t == 3 || t == 5 || t == 11))
+        return 0;
+    const int w = value_width(t);
+    Cursor c{cursor->gguf->data, cursor->gguf->size, cursor->position};
+    uint64_t bits = 0;
+    if (!c.le(w, &bits)) return 0;
+    if (w < 8 && (bits >> (8 * w - 1)) & 1u) bits |= ~((1ull << (8 * w)) - 1ull);  // sign-extend
+    cursor->position = c.at;
+    --cursor->remaining;
+    *value = (int64_t)bits;
+    return 1;
+}
+
+// gguf_get_f32_tensor_view (src/gguf_reader.cpp:514-571): F32 tensors only;
+// the view is cleared on every failure.
+QMV_EXPORT int qmv_gguf_f32_view(const QmvGguf *g, const char *name, QmvGgufF32View *view)
+{
+    if (view == nullptr) return 0;
+    memset(view, 0, sizeof(*view));
+    if (g == nullptr || name == nullptr || g->tensors.empty()) return 0;
+    const QmvGguf::Tensor *t = find_tensor(g, name);
+    uint64_t elems = 0;
+    if (t == nullptr || t->type != 0 || t->n_dims == 0 || t->n_dims > 4 || !element_count(*t, &elems)) return 0;
+    if (elems > UINT64_MAX / sizeof(float) || t->bytes != elems * sizeof(float)) return 0;
+    if (t->offset > g->size - g->data_offset) return 0;
+    view->data = (const float *)(g->data + g->data_offset + t->offset);
+    view->element_count = elems;
+    view->dimension_count = t->n_dims;
+    for (uint32_t d = 0; d < t->n_dims; ++d) view->dimensions[d] = t->dims[d];
+    return 1;
+}
+
 // The reference's gguf_get_quantized_tensor_view (src/gguf_reader.cpp:690-741):
 // a cleared view on every failure; packed types only; whole blocks whose
 // byte count matches the directory; data inside the image.

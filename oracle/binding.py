@@ -391,6 +391,48 @@ class RefGguf:
             return None
         return t.value, n.value
 
+    def get_bool(self, key: str):
+        v = ctypes.c_int()
+        self.lib.ref_gguf_get_bool.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int)]
+        return v.value if self.lib.ref_gguf_get_bool(self.h, key.encode(), ctypes.byref(v)) else None
+
+    def array_read(self, key: str, kind: int, max_items: int = 64):
+        """Elements of a top-level array read through the reference's cursor
+        (kind 0 strings as bytes, 1 unsigned, 2 signed) up to the first failed
+        read; None when the cursor does not open."""
+        L = self.lib
+        L.ref_gguf_array_read.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_int, _P, _P,
+                                          ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]
+        ints = np.zeros(max_items, np.uint64)
+        buf = np.zeros(1 << 16, np.uint8)
+        used = ctypes.c_uint64()
+        n = L.ref_gguf_array_read(self.h, key.encode(), kind, max_items, ints.ctypes.data, buf.ctypes.data,
+                                  buf.nbytes, ctypes.byref(used))
+        if n < 0:
+            return None
+        if kind != 0:
+            vals = [int(v) for v in ints[:n]]
+            return vals if kind == 1 else [v - (1 << 64) if v >= 1 << 63 else v for v in vals]
+        out, at, raw = [], 0, buf[:used.value].tobytes()
+        while at < len(raw):
+            ln = int.from_bytes(raw[at:at + 8], "little")
+            out.append(raw[at + 8:at + 8 + ln])
+            at += 8 + ln
+        return out
+
+    def f32_view(self, name: str):
+        class V(ctypes.Structure):
+            _fields_ = [("data", ctypes.c_void_p), ("dimension_count", ctypes.c_uint32),
+                        ("dimensions", ctypes.c_uint64 * 4), ("element_count", ctypes.c_uint64)]
+        v, at = V(), ctypes.c_uint64()
+        self.lib.ref_gguf_f32_view.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_void_p,
+                                               ctypes.POINTER(ctypes.c_uint64)]
+        if not self.lib.ref_gguf_f32_view(self.h, name.encode("utf-8", "surrogateescape"), ctypes.byref(v),
+                                          ctypes.byref(at)):
+            return None
+        return dict(data_at=at.value, dimensions=list(v.dimensions[:v.dimension_count]),
+                    element_count=v.element_count)
+
     def quantized_view(self, name: str, view_type):
         """(view fields as a dict with the data offset in the image), or None."""
         v, at = view_type(), ctypes.c_uint64()

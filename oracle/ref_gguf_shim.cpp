@@ -83,4 +83,46 @@ int ref_gguf_quantized_view(void *h, const char *name, GgufQuantizedTensorView *
     return ok;
 }
 
+int ref_gguf_get_bool(void *h, const char *key, int *value) { return gguf_get_bool((GgufFile *)h, key, value); }
+
+// Every element of a top-level array through the reference's cursor readers:
+// kind 0 strings (each as length then bytes into `bytes`), 1 unsigned, 2
+// signed (into `ints`).  Returns the elements read before the first failure
+// (-1 when the cursor does not open).
+int ref_gguf_array_read(void *h, const char *key, int kind, int max, uint64_t *ints, uint8_t *bytes,
+                        uint64_t bytes_cap, uint64_t *bytes_used)
+{
+    GgufArrayCursor cur;
+    if (!gguf_array_cursor_init((GgufFile *)h, key, &cur)) return -1;
+    int n = 0;
+    uint64_t used = 0;
+    for (; n < max; ++n) {
+        if (kind == 0) {
+            const char *v = nullptr;
+            uint64_t len = 0;
+            if (!gguf_array_next_string(&cur, &v, &len) || used + 8 + len > bytes_cap) break;
+            memcpy(bytes + used, &len, 8);
+            memcpy(bytes + used + 8, v, (size_t)len);
+            used += 8 + len;
+        } else if (kind == 1) {
+            if (!gguf_array_next_uint(&cur, &ints[n])) break;
+        } else {
+            int64_t v = 0;
+            if (!gguf_array_next_int(&cur, &v)) break;
+            ints[n] = (uint64_t)v;
+        }
+    }
+    *bytes_used = used;
+    return n;
+}
+
+// The reference's F32 view, its data as an offset into the mapped image.
+int ref_gguf_f32_view(void *h, const char *name, GgufF32TensorView *view, uint64_t *data_at)
+{
+    const GgufFile *f = (const GgufFile *)h;
+    const int ok = gguf_get_f32_tensor_view(f, name, view);
+    *data_at = ok ? (uint64_t)((const unsigned char *)view->data - f->data) : 0;
+    return ok;
+}
+
 }  // extern "C"

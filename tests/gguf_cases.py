@@ -7,6 +7,7 @@ import numpy as np
 KEYS = ["general.architecture", "general.alignment", "fixture.f32", "fixture.f64", "fixture.f32_inf",
         "fixture.f32_nan", "fixture.f64_inf", "fixture.f64_nan", "fixture.u8", "fixture.u16", "fixture.u64",
         "fixture.i32", "fixture.bool", "fixture.strings", "fixture.nested", "fixture.empty", "missing.key",
+        "fixture.u16s", "fixture.i8s", "fixture.i64s", "fixture.u64s", "fixture.bools",
         "qwen2.embedding_length", "qwen2.attention.layer_norm_rms_epsilon", "qwen2.rope.freq_base",
         "tokenizer.ggml.tokens"]
 
@@ -47,6 +48,12 @@ def cases(wl):
             ("fixture.strings", G.GGUF_ARRAY, (G.GGUF_STRING, ["a", "bc", ""])),
             ("fixture.nested", G.GGUF_ARRAY, (G.GGUF_ARRAY, [(G.GGUF_U16, [1, 2]), (G.GGUF_U16, [])])),
             ("fixture.empty", G.GGUF_STRING, ""),
+            # arrays for the cursor readers (signed ones sign-extend)
+            ("fixture.u16s", G.GGUF_ARRAY, (G.GGUF_U16, [0, 1, 65535])),
+            ("fixture.i8s", G.GGUF_ARRAY, (G.GGUF_I8, [-128, -1, 0, 127])),
+            ("fixture.i64s", G.GGUF_ARRAY, (G.GGUF_I64, [-(2 ** 63), -2, 2 ** 63 - 1])),
+            ("fixture.u64s", G.GGUF_ARRAY, (G.GGUF_U64, [2 ** 64 - 1, 7])),
+            ("fixture.bools", G.GGUF_ARRAY, (G.GGUF_BOOL, [1, 0])),
             ("fixture.f32", G.GGUF_U32, 9)]  # a second entry of one key: the first wins
     all_types = [("t.q5_0", G.Q5_0, [32, 2], blocks(G.Q5_0, 64)), ("t.q8_0", G.Q8_0, [32], blocks(G.Q8_0, 32)),
                  ("t.q4_k", G.Q4_K, [256, 2], blocks(G.Q4_K, 512)),

@@ -2,7 +2,8 @@
 GGUF reader (src/gguf_reader.cpp, compiled into oracle/_ref by oracle/Makefile)
 reports for every image of tests/gguf_cases.py — accepted or not, and for
 accepted images the header fields, the tensor directory, the metadata reads
-of gguf_cases.KEYS and the packed view of every tensor.
+of gguf_cases.KEYS (scalars, bools, array elements through the cursor readers)
+and the packed and F32 views of every tensor.
 
     python tests/golden/make_gguf_golden.py
 
@@ -36,6 +37,13 @@ def view_type():
     return V
 
 
+def hexed(items):
+    """Array elements in a JSON-friendly form (strings as hex)."""
+    if items is None:
+        return None
+    return [v.hex() if isinstance(v, bytes) else v for v in items]
+
+
 def describe_reference(path: str) -> dict:
     r = binding.RefGguf(path)
     try:
@@ -49,7 +57,10 @@ def describe_reference(path: str) -> dict:
                 "string": {k: (None if r.get_string(k) is None else r.get_string(k).hex()) for k in gguf_cases.KEYS},
                 "array": {k: (None if r.get_array_info(k) is None else list(r.get_array_info(k)))
                           for k in gguf_cases.KEYS},
-                "views": {t["name"]: r.quantized_view(t["name"], V) for t in tensors + [{"name": "missing"}]}}
+                "views": {t["name"]: r.quantized_view(t["name"], V) for t in tensors + [{"name": "missing"}]},
+                "bool": {k: r.get_bool(k) for k in gguf_cases.KEYS},
+                "arrays": {k: [hexed(r.array_read(k, kind)) for kind in (0, 1, 2)] for k in gguf_cases.KEYS},
+                "f32": {t["name"]: r.f32_view(t["name"]) for t in tensors + [{"name": "missing"}]}}
     finally:
         r.close()
 

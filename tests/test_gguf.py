@@ -3,8 +3,8 @@
 Each image of gguf_cases.py is parsed by the product and compared field by
 field with tests/golden/gguf_reference.json, which holds what the reference's
 gguf_open and accessors (src/gguf_reader.cpp, compiled in oracle/_ref) report
-for it: acceptance, header fields, tensor directory, metadata reads and
-packed views.  test_golden_is_the_reference re-derives the fixture from the
+for it: acceptance, header fields, tensor directory, metadata reads (scalars,
+bools, array elements through the cursor readers), packed and F32 views.  test_golden_is_the_reference re-derives the fixture from the
 live reference where oracle/_ref exists.  Host-only: no GPU call."""
 import ctypes
 import json
@@ -51,12 +51,24 @@ def describe(qmv, img: bytes) -> dict:
         for t in tensors + [{"name": "missing"}]:
             v = g.quantized_view(t["name"])
             views[t["name"]] = None if v is None else _view_dict(v, base)
+        f32 = {}
+        for t in tensors + [{"name": "missing"}]:
+            v = g.f32_view(t["name"])
+            f32[t["name"]] = None if v is None else dict(
+                data_at=v.data - base, dimensions=list(v.dimensions[:v.dimension_count]),
+                element_count=v.element_count)
+
+        def hexed(items):
+            return None if items is None else [x.hex() if isinstance(x, bytes) else x for x in items]
+
         K = gguf_cases.KEYS
         return {"ok": True, "info": info, "tensors": tensors, "uint": {k: g.get_uint(k) for k in K},
                 "float": {k: g.get_float(k) for k in K},
                 "string": {k: (None if g.get_string(k) is None else g.get_string(k).hex()) for k in K},
                 "array": {k: (None if g.get_array_info(k) is None else list(g.get_array_info(k))) for k in K},
-                "views": views}
+                "views": views, "bool": {k: g.get_bool(k) for k in K},
+                "arrays": {k: [hexed(g.array_read(k, kind)) for kind in (0, 1, 2)] for k in K},
+                "f32": f32}
     finally:
         g.close()
 
