@@ -6,7 +6,10 @@
   quantized_tensor_matvec_f32 / _matmul_f32 do (both are called with the same
   views; validation runs before any device work);
 * the greedy sampler's argument contract (src/sampler.cpp:14-24);
-* argmax key encoding and decoding.
+* argmax key encoding and decoding;
+* the decoder, prefill, profiling, residual-matmul and GGUF entry points
+  reject null handles and arguments before any device work, and the GGUF
+  array cursor reads exactly its array's elements.
 """
 import ctypes
 import os
@@ -141,3 +144,66 @@ def test_key_order_and_decode(qmv, oracle):
     assert qmv.key_to_token(0xFFFFFFFFFFFFFFFF) == -1
     assert qmv.key_to_token(0) == -1
     assert qmv.key_to_token(py_key(1.5, 123456)) == 123456
+
+
+def test_whole_model_entry_points_reject_bad_arguments(qmv):
+    """The decoder, prefill, profiling, residual-matmul and GGUF entry points
+    fail with a 0 return (and, where the reference has one, its message)
+    before any device work when handed null handles or arguments."""
+    lib = qmv.lib()
+    P = ctypes.c_void_p
+    assert lib.qmv_qwen2_prefill(None, None, 3, None, None) == 0
+    assert qmv.last_error() == "Qwen2 prefill arguments are invalid."
+    assert lib.qmv_qwen2_reset(None) == 0 and "null decoder" in qmv.last_error()
+    assert lib.qmv_qwen2_stream(None, ctypes.byref(P())) == 0
+    assert lib.qmv_qwen2_kernels_per_step(None) == 0
+    prof = qmv.QmvOperationProfile()
+    prof.enabled = 1
+    assert lib.qmv_qwen2_forward_profiled(None, 1, None, None, ctypes.byref(prof)) == 0
+    assert bytes(prof)[8:] == bytes(qmv.QmvOperationProfile())[8:]  # nothing accumulated
+    assert lib.qmv_matmul_residual(None, None, 4, 1, None, 4, None) == 0
+    # kernel timing of the drop-in calls: nothing to report before a profiled call
+    assert lib.qmv_set_profiling(1) == 1
+    assert lib.qmv_last_kernel_seconds(ctypes.byref(ctypes.c_double())) == 0
+    assert "no profiled call" in qmv.last_error()
+    assert lib.qmv_last_kernel_seconds(None) == 0
+    assert lib.qmv_set_profiling(0) == 1
+    # GGUF handle and accessors
+    h = P()
+    assert lib.qmv_gguf_open(None, 100, ctypes.byref(h)) == 0 and h.value is None
+    assert lib.qmv_gguf_open_file(b"", ctypes.byref(h)) == 0
+    assert lib.qmv_gguf_close(None) == 0
+    assert lib.qmv_gguf_upload(None, None, None) == 0
+    assert lib.qmv_gguf_get_bool(None, b"k", ctypes.byref(ctypes.c_int())) == 0
+    cur = qmv.QmvGgufArrayCursor()
+    assert lib.qmv_gguf_array_cursor_init(None, b"k", ctypes.byref(cur)) == 0
+    assert lib.qmv_gguf_array_next_uint(ctypes.byref(cur), ctypes.byref(ctypes.c_uint64())) == 0
+    assert lib.qmv_gguf_array_next_int(None, ctypes.byref(ctypes.c_int64())) == 0
+    v = qmv.QmvGgufF32View()
+    v.data, v.dimension_count, v.element_count = 1234, 3, 9
+    assert lib.qmv_gguf_f32_view(None, b"x", ctypes.byref(v)) == 0
+    assert (v.data or 0) == 0 and v.dimension_count == 0 and v.element_count == 0
+    assert lib.qmv_qwen2_create_from_gguf(None, 8, ctypes.byref(h)) == 0 and h.value is None
+
+
+def test_gguf_cursor_reads_stop_at_the_end(qmv, workloads):
+    """A cursor reads exactly the array's elements, of its own element type
+    only (gguf_array_next_*, src/gguf_reader.cpp:419-489)."""
+    import gguf_cases
+    g = qmv.GgufFile(data=dict(gguf_cases.cases(workloads))["metadata_all_types"])
+    try:
+        lib = qmv.lib()
+        cur = qmv.QmvGgufArrayCursor()
+        assert lib.qmv_gguf_array_cursor_init(g.handle, b"fixture.u16s", ctypes.byref(cur)) == 1
+        got, v = [], ctypes.c_uint64()
+        while lib.qmv_gguf_array_next_uint(ctypes.byref(cur), ctypes.byref(v)):
+            got.append(v.value)
+        assert got == [0, 1, 65535] and cur.remaining == 0
+        assert lib.qmv_gguf_array_cursor_init(g.handle, b"fixture.u16s", ctypes.byref(cur)) == 1
+        assert lib.qmv_gguf_array_next_int(ctypes.byref(cur), ctypes.byref(ctypes.c_int64())) == 0  # unsigned
+        assert g.array_read("fixture.i64s", 2) == [-(2 ** 63), -2, 2 ** 63 - 1]
+        assert g.array_read("fixture.strings", 0) == [b"a", b"bc", b""]
+        assert g.array_read("fixture.u8", 1) is None  # not an array
+        assert g.get_bool("fixture.bool") == 1 and g.get_bool("fixture.u8") is None
+    finally:
+        g.close()
