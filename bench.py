@@ -204,6 +204,69 @@ def cpu_vocab_step(lib, kind, blocks, x, threads):
     return tok
 
 
+def reference_vocab_logits(x, cores):
+    """Configuration 2 on the host, as the parity gate's reference: the
+    reference's own scalar build (oracle/_ref, its src/quantized_matvec.cpp
+    projection and src/sampler.cpp greedy sampler; the C restatement when that
+    build is absent) on the full seeded 152064 x 3584 matrix.  Returns
+    (logits f32, per-row tolerance 1e-4 * sum|w x| f64, token, source)."""
+    binding = _load("qmv_oracle_binding", os.path.join(REPO, "oracle", "binding.py"))
+    wl = workloads()
+    blocks = wl.make_blocks(Q6_K, VOCAB_ROWS, HIDDEN, seed=0)
+    oracle = binding.Oracle()
+    if os.path.exists(binding.REF_SCALAR_SO):
+        ref = binding.Reference(binding.REF_SCALAR_SO)
+        ref.set_threads(cores)
+        y_ref = ref.matvec(Q6_K, blocks, VOCAB_ROWS, HIDDEN, x)
+        ok, tok, _ = ref.greedy(y_ref)
+        source = "reference scalar build (oracle/_ref: src/quantized_matvec.cpp + src/sampler.cpp)"
+    else:
+        y_ref = oracle.matvec(Q6_K, blocks, VOCAB_ROWS, HIDDEN, x, threads=cores)
+        ok, tok = oracle.argmax(y_ref)
+        source = "C restatement of the reference's scalar path (oracle/qmv_oracle.c)"
+    bound = 1e-4 * oracle.row_abs_dot(Q6_K, blocks, VOCAB_ROWS, HIDDEN, x, threads=cores)
+    return y_ref, bound, (tok if ok else -1), source
+
+
+def check_vocab_parity(logits, token, x, dev, rank, world):
+    """Every rank compares its full gathered logits and its global token with
+    the reference's (computed once on rank 0 and broadcast).  Returns the
+    parity record (rank 0: the worst rank's figures) and whether it passed."""
+    import torch
+    import torch.distributed as dist
+    if rank == 0:
+        y_ref, bound, ref_tok, source = reference_vocab_logits(x, os.cpu_count() or 1)
+        t_ref = torch.from_numpy(y_ref).to(dev)
+        t_bound = torch.from_numpy(bound).to(dev)
+        t_tok = torch.tensor([ref_tok], dtype=torch.int64, device=dev)
+    else:
+        t_ref = torch.empty(VOCAB_ROWS, dtype=torch.float32, device=dev)
+        t_bound = torch.empty(VOCAB_ROWS, dtype=torch.float64, device=dev)
+        t_tok = torch.empty(1, dtype=torch.int64, device=dev)
+        source = None
+    if world > 1:
+        for t in (t_ref, t_bound, t_tok):
+            dist.broadcast(t, 0)
+    y_ref = t_ref.cpu().numpy()
+    bound = t_bound.cpu().numpy()
+    ref_tok = int(t_tok.item())
+    err = np.abs(logits.astype(np.float64) - y_ref.astype(np.float64))
+    ratio = float(np.max(err / np.maximum(bound, 1e-300)))
+    rows_out = int(np.count_nonzero(err > bound))
+    match = 1.0 if (token == ref_tok and ref_tok >= 0) else 0.0
+    agg = torch.tensor([ratio, float(rows_out), -match], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(agg, op=dist.ReduceOp.MAX)
+    ratio, rows_out, match = float(agg[0]), int(agg[1]), -float(agg[2])
+    top2 = np.sort(y_ref)[-2:]
+    rec = {"token": token, "reference_token": ref_tok, "token_match": match == 1.0,
+           "max_err_over_bound": round(ratio, 5), "rows_out_of_bound": rows_out,
+           "rows_checked": VOCAB_ROWS, "ranks_checked": world, "seed": 0,
+           "reference_top2_gap": float(top2[1] - top2[0]), "reference": source,
+           "bound": "|y - y_ref| <= 1e-4 * sum|w x| per row; identical greedy token"}
+    return rec, (match == 1.0 and ratio <= 1.0)
+
+
 def time_cpu_reference(blocks, x, min_seconds, max_steps=None):
     lib, kind = cpu_reference_lib()
     cores = os.cpu_count() or 1
@@ -224,6 +287,15 @@ def time_cpu_reference(blocks, x, min_seconds, max_steps=None):
 
 def vocab_bytes(rows):
     return rows * (HIDDEN // 256) * 210
+
+
+def bench_config(world):
+    """The workload both arms report (identical keys and values for one N)."""
+    return {"workload": "cfg2_q6_k_vocab_projection_argmax", "rows": VOCAB_ROWS, "cols": HIDDEN,
+            "ggml_type": "Q6_K", "parallelism": f"row-shard x{world}",
+            "rows_per_rank": -(-VOCAB_ROWS // world),
+            "l2_defeat": "inputs larger than L2: 447 MB of weights per step at N=1; at N>1 each rank "
+                         "rotates over weight copies of its shard totalling >= 2.5x L2"}
 
 
 def shard(rank, world):
@@ -264,8 +336,9 @@ def run_reference_arm(args, rank, world):
         "ms_per_step": round(1e3 * el / args.steps, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "tokens_per_s": round(args.steps / el, 3),
-        "config": {"workload": "cfg2_q6_k_vocab_projection_argmax", "rows": VOCAB_ROWS, "cols": HIDDEN,
-                   "ggml_type": "Q6_K", "parallelism": "host OpenMP"},
+        "config": bench_config(world),
+        "implementation": {"step": "the reference's quantized_tensor_matvec_f32 + sampler_greedy_sample "
+                                   "(OpenMP over rows on the host cores)"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": kind,
                          "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -344,9 +417,35 @@ def run_b200(args, rank, world, local_rank):
         if world > 1 and not p2p:
             dist.all_gather_into_tensor(gathered, sendbuf)
 
-    # correctness gate before timing: the token of this input
+    def gathered_logits():
+        """This rank's copy of all VOCAB_ROWS logits of the latest step."""
+        if world == 1:
+            return sendbuf[:rows].cpu().numpy()
+        if p2p:
+            host = np.empty(world * per, np.float32)
+            qmv.memcpy(host, qmv.exchange_logits(group.own, world, per, group.epoch), host.nbytes, sptr)
+        else:
+            host = gathered.view(world, stride)[:, :per].contiguous().view(-1).cpu().numpy()
+        return np.concatenate([host[s0:s1] for s0, s1 in sh.gathered_rows(VOCAB_ROWS, world)])
+
+    # correctness gate before timing (seed 0): every rank's full logits and
+    # its global token against the reference's own scalar build
     step(0, False)
+    torch.cuda.synchronize()
     token = qmv.key_to_token(global_key())
+    parity, parity_ok = check_vocab_parity(gathered_logits(), token, x_host, dev, rank, world)
+    if not parity_ok:
+        for wobj in weights:
+            wobj.free()
+        if world > 1:
+            dist.barrier()
+            if group is not None:
+                group.close()
+            dist.destroy_process_group()
+        if rank == 0:
+            return {"metric": METRIC, "error": "parity gate failed on configuration 2", "parity": parity,
+                    "n_gpus": world, "config": bench_config(world)}, False
+        return None, False
 
     for i in range(args.warmup):
         step(i, False)
@@ -410,6 +509,46 @@ def run_b200(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, kms_max = float(t[0]), float(t[1])
     clock_info = clocks.stop() if clocks else None
+
+    # N > 1: the same shard projection + argmax without any exchange (each
+    # rank alone, graph-replayed), so the step splits into shard compute and
+    # the cost of joining the ranks (exchange stores, flags, waiting for the
+    # slowest rank; in NCCL mode the all-gather)
+    breakdown = None
+    if world > 1:
+        g2 = torch.cuda.CUDAGraph()
+        gs2 = torch.cuda.Stream(dev)
+        with torch.cuda.graph(g2, stream=gs2):
+            for i in range(args.steps):
+                weights[i % copies].matvec_argmax(x_dev.data_ptr(), sendbuf.data_ptr(), keyview.data_ptr(),
+                                                  ws.data_ptr(), gs2.cuda_stream)
+        with torch.cuda.stream(gs2):
+            g2.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        a2, b2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(gs2):
+            a2.record(gs2)
+            g2.replay()
+            b2.record(gs2)
+        torch.cuda.synchronize()
+        del g2
+        tb = torch.tensor([a2.elapsed_time(b2) / args.steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(tb, op=dist.ReduceOp.MAX)
+        shard_us = float(tb[0]) * 1e3
+        step_us = ms / args.steps * 1e3
+        breakdown = {
+            "step_us": round(step_us, 2),
+            "shard_projection_argmax_us": round(shard_us, 2),
+            "join_us": round(step_us - shard_us, 2),
+            "join": ("fused exchange: logit stores to peers, flags, the wait for the slowest rank"
+                     if p2p else "NCCL all-gather of logit slices and keys, launched after each kernel"),
+            "nvlink_bytes_per_step_per_rank": (4 * per + 8 + 4) * (world - 1),
+            "shard_bytes_per_step": vocab_bytes(rows) + 4 * HIDDEN + 4 * rows,
+            "shard_roofline_us": round((vocab_bytes(rows) + 4 * HIDDEN + 4 * rows) / (measured_peaks()[0] * 1e3), 2),
+        }
+        if not p2p:
+            breakdown["kernel_us_events"] = round(kms_max * 1e3, 2)
 
     # ---- end to end through the C ABI with host buffers (pinned)
     x_pin = torch.from_numpy(x_host).pin_memory()
@@ -483,17 +622,19 @@ def run_b200(args, rank, world, local_rank):
             "data": "synthetic (seeded splitmix64; Q6_K blocks per the configuration)",
             "tokens_per_s": round(args.steps / (ms * 1e-3), 1),
             "token": token,
-            "config": {"workload": "cfg2_q6_k_vocab_projection_argmax", "rows": VOCAB_ROWS, "cols": HIDDEN,
-                       "ggml_type": "Q6_K", "parallelism": par, "rows_per_rank": per,
-                       "l2_defeat": f"{copies} rotating weight copies per rank (>= 2.5x L2)"},
+            "parity": parity,
+            "config": bench_config(world),
+            "implementation": {"step": par, "weight_copies_per_rank": copies},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": "gemv_tma_kernel<Q6_K> fused argmax" + (" + exchange" if p2p else ""),
                          "kernel_ms": round(kms_max, 5), "peak_source": peak_kind},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * HIDDEN,
                     "d2h_bytes_per_step": 4 * out_floats + (8 if p2p else 0), "steps": e2e_steps,
-                    "tokens_per_s": round(e2e_steps / (e2e_ms * 1e-3), 1), "token": e2e_tok},
+                    "tokens_per_s": round(e2e_steps / (e2e_ms * 1e-3), 1), "token": e2e_tok,
+                    "token_matches_reference": e2e_tok == parity["reference_token"]},
             "gpu_launches": args.steps,
+            "breakdown": breakdown,
             "clocks": clock_info,
             "device_status": status,
         }
@@ -505,7 +646,7 @@ def run_b200(args, rank, world, local_rank):
         if group is not None:
             group.close()
         dist.destroy_process_group()
-    return result
+    return result, True
 
 
 SECONDARY = (("cfg0_q8_0_4864x896", 0), ("cfg1a_q4_k_18944x3584", 0), ("cfg1b_q4_k_3584x18944", 0),
@@ -586,7 +727,45 @@ def extras_single_gpu(qmv, steps, only=None):
 QWEN2_DECODE = "cfg4_qwen2_0_5b_decode"
 
 
-def bench_qwen2_decode(qmv, steps=256, prefill=1024, cpu_seconds=5.0, cpu=True):
+def qwen2_free_run(binding, m, tensors, max_ctx, keys, vals, gpu_tokens, seconds):
+    """Free-run token identity of configuration 4: the reference's own scalar
+    build (oracle/_ref: forward_token, src/qwen2_architecture.cpp:1195-1531,
+    then sampler_greedy_sample, src/sampler.cpp:14-36) decodes greedily from
+    the same cache and start token, feeding back its own tokens, until its
+    token differs from the GPU's, all GPU tokens are compared, or `seconds`
+    pass.  At a divergence the reference's logit gap between its token and the
+    GPU's says whether the two were a near tie."""
+    ref = binding.RefQwen2(m, tensors, max_ctx, path=binding.REF_SCALAR_SO)
+    sampler = binding.Reference(binding.REF_SCALAR_SO)
+    first, n, tok = None, 0, 7
+    t0 = time.perf_counter()
+    try:
+        ref.set_kv(keys, vals)
+        for i in range(len(gpu_tokens)):
+            ok, logits = ref.forward(tok)
+            ok2, rtok, _ = sampler.greedy(logits)
+            if not (ok and ok2):
+                first = {"step": i, "reference_failed": True}
+                break
+            g = int(gpu_tokens[i])
+            if rtok != g:
+                gap = float(logits[rtok]) - float(logits[g]) if 0 <= g < logits.size else None
+                first = {"step": i, "gpu_token": g, "reference_token": int(rtok), "reference_logit_gap": gap,
+                         "gap_over_max_abs_logit": (gap / float(np.max(np.abs(logits)))) if gap is not None else None}
+                break
+            n += 1
+            tok = rtok
+            if time.perf_counter() - t0 > seconds:
+                break
+    finally:
+        ref.close()
+    return {"gpu_tokens": len(gpu_tokens), "compared": n + (1 if first else 0), "identical": n,
+            "first_divergence": first, "seconds": round(time.perf_counter() - t0, 1),
+            "reference": "the reference's scalar build (forward_token + sampler_greedy_sample), "
+                         "feeding back its own tokens from the same 1024-position cache and start token 7"}
+
+
+def bench_qwen2_decode(qmv, steps=256, prefill=1024, cpu_seconds=5.0, cpu=True, free_seconds=45.0):
     """Configuration 4: greedy decode of `steps` tokens on the synthetic
     Qwen2-0.5B model from a KV cache pre-filled to `prefill` positions.
     value: device-timed tokens/s (CUDA events around `steps` replays of the
@@ -642,6 +821,8 @@ def bench_qwen2_decode(qmv, steps=256, prefill=1024, cpu_seconds=5.0, cpu=True):
            "model": "Qwen2-0.5B architecture, random-init (Q8_0 attention/gate/embedding/output, Q5_0 up/down)"}
     if cpu:
         binding = _load("qmv_oracle_binding", os.path.join(REPO, "oracle", "binding.py"))
+        if os.path.exists(binding.REF_SCALAR_SO):
+            rec["free_run"] = qwen2_free_run(binding, m, tensors, max_ctx, keys, vals, toks, free_seconds)
         if os.path.exists(binding.REF_AVX2_SO):
             ref = binding.RefQwen2(m, tensors, max_ctx, path=binding.REF_AVX2_SO)
             try:
@@ -777,7 +958,11 @@ def main():
         print(json.dumps({"only": args.only, "result": res}), flush=True)
         return 0
 
-    result = run_b200(args, rank, world, local_rank)
+    result, ok = run_b200(args, rank, world, local_rank)
+    if not ok:
+        if rank == 0:
+            print(json.dumps(result), flush=True)
+        return 3
     if rank != 0:
         return 0
     if world == 1 and not args.no_extras:

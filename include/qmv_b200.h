@@ -53,9 +53,14 @@ int qmv_set_device(int device);
 int qmv_device_status(uint32_t *flags, int clear);
 
 /* GEMV kernel selection for the calling process: 0 = automatic (TMA bulk-copy
- * pipeline when its shared-memory stages fit, direct loads otherwise),
- * 1 = direct loads, 2 = TMA pipeline only (shapes it cannot stage fail).
- * No counterpart in the reference; both paths compute the same function. */
+ * pipeline with the exclusive plan when its shared-memory stages fit, direct
+ * loads otherwise),
+ * 1 = direct loads, 2 = TMA pipeline only (shapes it cannot stage fail),
+ * 3 = the exclusive TMA plan (one CTA per SM using all of its shared
+ * memory; direct loads where no stages fit), 4 = the shared TMA plan where
+ * its stages fit in half an SM (a CTA that leaves half of the SM to the next
+ * launch, so consecutive launches overlap), else as 0.  No counterpart in
+ * the reference; every path computes the same function. */
 int qmv_set_gemv_path(int path);
 
 /* Batched-matmul kernel selection for the calling process: 0 = automatic
@@ -201,7 +206,10 @@ int qmv_matvec_argmax_exchange(const QmvWeight *weight, const float *x, int x_co
  * 16 + 8 * 2048 bytes, held on every GPU that loads this library until the
  * process exits, so n is limited to QMV_ARGMAX_NOALLOC_MAX_LOGITS; larger n
  * is rejected with an error.  The first call on a device looks up the array's
- * device address; make that first call before any stream capture.  All calls
+ * device address in that device's primary context (the CUDA runtime's) and
+ * keeps it for the life of the process: make that first call before any
+ * stream capture, and do not use this entry point after a cudaDeviceReset or
+ * from a context other than the primary one.  All calls
  * on a device share the array: each call clears its counter first, and calls
  * that overlap on the GPU (e.g. on concurrent streams) race. */
 #define QMV_ARGMAX_NOALLOC_MAX_LOGITS (2048 * 4096)

@@ -303,7 +303,7 @@ QMV_EXPORT int qmv_device_status(uint32_t *flags, int clear)
 
 QMV_EXPORT int qmv_set_gemv_path(int path)
 {
-    if (path < 0 || path > 2) return fail("gemv path must be 0, 1 or 2");
+    if (path < 0 || path > 4) return fail("gemv path must be 0, 1, 2, 3 or 4");
     qmv::set_gemv_path(path);
     return 1;
 }

@@ -1133,8 +1133,12 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
     }
 }
 
-template <uint32_t FMT, int CW, int R, int NP = 1, int SPLIT = 1>
-__global__ void __launch_bounds__((CW + 1) * 32, 1)
+// MINB = 2: the register-capped instance of the shared plan, whose CTA
+// leaves registers and shared memory for one CTA of the next launch on the
+// same SM (programmatic dependent launch then streams that launch's first
+// stages while this one finishes).
+template <uint32_t FMT, int CW, int R, int NP = 1, int SPLIT = 1, int MINB = 1>
+__global__ void __launch_bounds__((CW + 1) * 32, MINB)
 gemv_tma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x,
                 float *__restrict__ y, ArgmaxOut am, int want_argmax, TmaPlan P, Exchange ex, Fuse fu)
 {
@@ -2846,7 +2850,10 @@ cudaError_t gemv_go(const Layout &L, const uint8_t *w, const float *x, float *y,
     return cudaGetLastError();
 }
 
-int g_gemv_path = 0;  // 0 auto, 1 direct loads, 2 TMA pipeline
+// 0 auto (exclusive TMA plan, else direct loads), 1 direct loads, 2 TMA
+// pipeline only, 3 exclusive TMA plan (else direct loads), 4 the shared TMA
+// plan where it fits (else as 0)
+int g_gemv_path = 0;
 
 // Shared-memory plan of the TMA kernel: the first of these (consumer warps,
 // rows per warp, minimum stages) whose stages fit.  Two rows per warp share
@@ -2855,17 +2862,20 @@ int g_gemv_path = 0;  // 0 auto, 1 direct loads, 2 TMA pipeline
 // x in shared memory, 8 consumer warps).  false when none fits (the
 // direct-load kernels run).
 constexpr uint32_t kTmaBudget = 227u * 1024u - 1024u;  // dynamic bytes, leaving static room
+// Two CTAs per SM: each takes at most half of the SM's 228 KiB, less its
+// static shared memory and the 1 KiB the system reserves per CTA.
+constexpr uint32_t kTmaBudgetShared = 112u * 1024u;
 
 // One candidate {consumer warps, rows per warp, minimum stages, warps per
 // row} for a matrix whose rows spread over ctas CTAs; false when its stages
 // do not fit.
-bool tma_candidate(const Layout &L, const int *cand, int np, long long ctas, TmaPlan *P)
+bool tma_candidate(const Layout &L, const int *cand, int np, long long ctas, TmaPlan *P, uint32_t budget)
 {
     const uint32_t xb = (uint32_t)((xs_bytes(L.cols) * (size_t)np + 127) & ~(size_t)127);
-    if (xb >= kTmaBudget || ctas < 1) return false;
+    if (xb >= budget || ctas < 1) return false;
     const int cw = cand[0], r = cand[1], min_stages = cand[2], split = cand[3];
     const uint64_t sb = ((uint64_t)cw * r / split * L.row_stride + 127) & ~127ull;
-    const uint64_t ns = (kTmaBudget - xb) / sb;
+    const uint64_t ns = (budget - xb) / sb;
     if ((int)ns < min_stages) return false;
     P->x_bytes = xb;
     P->stage_bytes = (uint32_t)sb;
@@ -2893,16 +2903,46 @@ bool tma_plan(const Layout &L, TmaPlan *P, int np = 1, bool batched = false)
     const long long ctas = L.rows < sm_count() ? L.rows : sm_count();  // one CTA per SM
     const int n_cand = batched ? 2 : 7;
     for (int ci = 0; ci < n_cand; ++ci)
-        if (tma_candidate(L, batched ? kBatchCandidates[ci] : kCandidates[ci], np, ctas, P)) return true;
+        if (tma_candidate(L, batched ? kBatchCandidates[ci] : kCandidates[ci], np, ctas, P, kTmaBudget))
+            return true;
     return false;
 }
 
-template <uint32_t FMT, int CW, int R, int NP = 1, int SPLIT = 1>
+// The shared plan: one CTA per SM whose stages fit in half of the SM's shared
+// memory (and whose kernel instance is capped to half the registers), so the
+// CTA of the next launch in the stream can be resident beside it and stream
+// its first stages while this one computes its last.  Single position, no
+// split rows.
+bool tma_plan_shared(const Layout &L, TmaPlan *P)
+{
+    static const int kShared[][4] = {{16, 2, 2, 1}, {16, 1, 3, 1}, {8, 2, 3, 1}, {16, 1, 2, 1}, {8, 2, 2, 1}};
+    const long long ctas = L.rows < sm_count() ? L.rows : sm_count();
+    for (const int *cand : kShared)
+        if (tma_candidate(L, cand, 1, ctas, P, kTmaBudgetShared)) return true;
+    return false;
+}
+
+// Plan of a single-position GEMV under the current path setting; *shared
+// tells which kernel instance the plan is for.  The exclusive plan is the
+// default: measured on B200, the shared plan (register-capped, half the
+// stages) cost more in the consumers than the overlap of neighbouring
+// launches saved, except on the smallest matrices.
+bool gemv_plan(const Layout &L, TmaPlan *P, bool *shared)
+{
+    *shared = false;
+    if (g_gemv_path == 4 && tma_plan_shared(L, P)) {
+        *shared = true;
+        return true;
+    }
+    return tma_plan(L, P);
+}
+
+template <uint32_t FMT, int CW, int R, int NP = 1, int SPLIT = 1, int MINB = 1>
 cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, const float *x, float *y,
                         const ArgmaxOut *am, cudaStream_t s, const Exchange &ex = Exchange{},
                         const Fuse &fu = Fuse{})
 {
-    auto kernel = gemv_tma_kernel<FMT, CW, R, NP, SPLIT>;
+    auto kernel = gemv_tma_kernel<FMT, CW, R, NP, SPLIT, MINB>;
     const size_t smem = (size_t)P.x_bytes + (size_t)P.stages * P.stage_bytes;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -2928,19 +2968,33 @@ cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, con
     return cudaGetLastError();
 }
 
+// Launch the single-position TMA GEMV instance that plan P was made for
+// (shared: the register-capped instance; 8-warp CTAs fit twice per SM
+// without a cap).
+template <uint32_t FMT>
+cudaError_t gemv_tma_dispatch(const Layout &L, const TmaPlan &P, bool shared, const uint8_t *w, const float *x,
+                              float *y, const ArgmaxOut *am, cudaStream_t s, const Exchange &ex = Exchange{},
+                              const Fuse &fu = Fuse{})
+{
+    if (P.split == 2) return gemv_tma_go<FMT, 16, 1, 1, 2>(L, P, w, x, y, am, s, ex, fu);
+    if (P.consumer_warps == 16) {
+        if (shared)
+            return P.rows_per_warp == 2 ? gemv_tma_go<FMT, 16, 2, 1, 1, 2>(L, P, w, x, y, am, s, ex, fu)
+                                        : gemv_tma_go<FMT, 16, 1, 1, 1, 2>(L, P, w, x, y, am, s, ex, fu);
+        return P.rows_per_warp == 2 ? gemv_tma_go<FMT, 16, 2>(L, P, w, x, y, am, s, ex, fu)
+                                    : gemv_tma_go<FMT, 16, 1>(L, P, w, x, y, am, s, ex, fu);
+    }
+    return P.rows_per_warp == 2 ? gemv_tma_go<FMT, 8, 2>(L, P, w, x, y, am, s, ex, fu)
+                                : gemv_tma_go<FMT, 8, 1>(L, P, w, x, y, am, s, ex, fu);
+}
+
 template <uint32_t FMT>
 cudaError_t gemv_exchange_fmt(const Layout &L, const uint8_t *w, const float *x, float *y, const ArgmaxOut &am,
                               const Exchange &ex, cudaStream_t s)
 {
     TmaPlan P;
     if (!tma_plan(L, &P)) return cudaErrorNotSupported;
-    if (P.split == 2) return gemv_tma_go<FMT, 16, 1, 1, 2>(L, P, w, x, y, &am, s, ex);
-    if (P.consumer_warps == 16) {
-        if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 16, 2>(L, P, w, x, y, &am, s, ex);
-        return gemv_tma_go<FMT, 16, 1>(L, P, w, x, y, &am, s, ex);
-    }
-    if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 8, 2>(L, P, w, x, y, &am, s, ex);
-    return gemv_tma_go<FMT, 8, 1>(L, P, w, x, y, &am, s, ex);
+    return gemv_tma_dispatch<FMT>(L, P, false, w, x, y, &am, s, ex);
 }
 
 template <uint32_t FMT>
@@ -2948,15 +3002,9 @@ cudaError_t gemv_fused_fmt(const Layout &L, const uint8_t *w, const float *x, fl
                            const Fuse &fu, cudaStream_t s)
 {
     TmaPlan P;
-    if (!tma_plan(L, &P)) return cudaErrorNotSupported;
-    const Exchange none{};
-    if (P.split == 2) return gemv_tma_go<FMT, 16, 1, 1, 2>(L, P, w, x, y, am, s, none, fu);
-    if (P.consumer_warps == 16) {
-        if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 16, 2>(L, P, w, x, y, am, s, none, fu);
-        return gemv_tma_go<FMT, 16, 1>(L, P, w, x, y, am, s, none, fu);
-    }
-    if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 8, 2>(L, P, w, x, y, am, s, none, fu);
-    return gemv_tma_go<FMT, 8, 1>(L, P, w, x, y, am, s, none, fu);
+    bool shared = false;
+    if (!gemv_plan(L, &P, &shared)) return cudaErrorNotSupported;
+    return gemv_tma_dispatch<FMT>(L, P, shared, w, x, y, am, s, Exchange{}, fu);
 }
 
 template <uint32_t FA, uint32_t FB, int R>
@@ -2994,8 +3042,8 @@ cudaError_t gemv_pair_fmt(GemvPair pr, int grid, const float *x, const Fuse &fu,
 {
     static const int kPairCandidates[][4] = {{16, 2, 2, 1}, {16, 1, 3, 1}, {16, 1, 2, 1}};
     for (const int *cand : kPairCandidates) {
-        if (!tma_candidate(pr.L[0], cand, 1, pr.ctas0, &pr.P[0]) ||
-            !tma_candidate(pr.L[1], cand, 1, grid - pr.ctas0, &pr.P[1]))
+        if (!tma_candidate(pr.L[0], cand, 1, pr.ctas0, &pr.P[0], kTmaBudget) ||
+            !tma_candidate(pr.L[1], cand, 1, grid - pr.ctas0, &pr.P[1], kTmaBudget))
             continue;
         return cand[1] == 2 ? gemv_pair_go<FA, FB, 2>(pr, grid, x, fu, s) : gemv_pair_go<FA, FB, 1>(pr, grid, x, fu, s);
     }
@@ -3007,15 +3055,8 @@ cudaError_t gemv_fmt(const Layout &L, const uint8_t *w, const float *x, float *y
                      cudaStream_t s)
 {
     TmaPlan P;
-    if (g_gemv_path != 1 && tma_plan(L, &P)) {
-        if (P.split == 2) return gemv_tma_go<FMT, 16, 1, 1, 2>(L, P, w, x, y, am, s);
-        if (P.consumer_warps == 16) {
-            if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 16, 2>(L, P, w, x, y, am, s);
-            return gemv_tma_go<FMT, 16, 1>(L, P, w, x, y, am, s);
-        }
-        if (P.rows_per_warp == 2) return gemv_tma_go<FMT, 8, 2>(L, P, w, x, y, am, s);
-        return gemv_tma_go<FMT, 8, 1>(L, P, w, x, y, am, s);
-    }
+    bool shared = false;
+    if (g_gemv_path != 1 && gemv_plan(L, &P, &shared)) return gemv_tma_dispatch<FMT>(L, P, shared, w, x, y, am, s);
     if (g_gemv_path == 2) return cudaErrorInvalidConfiguration;
     // 16-lane groups for short rows, whole warps otherwise; two rows per group
     // share each x slice load.
@@ -3772,7 +3813,11 @@ int noalloc_max_logits() { return kNoAllocMaxCtas * kNoAllocLogitsPerCta; }
 
 // Device address of the scratch array on the current device.  Host code only
 // knows a host-side stand-in for the symbol, so the address is looked up once
-// per device (with that device current) and cached.
+// per device (with that device current) and cached.  The address belongs to
+// the CUDA runtime's primary context of that device, the one every runtime
+// call of this library uses; it does not survive a cudaDeviceReset, and a
+// host driving the library from a context of its own must not use this entry
+// point.
 static cudaError_t noalloc_scratch(void **out)
 {
     int dev = 0;

@@ -19,7 +19,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "libqmv_oracle.so")
 REF_SCALAR_SO = os.path.join(HERE, "_ref", "libqmvref_scalar.so")
 REF_AVX2_SO = os.path.join(HERE, "_ref", "libqmvref_avx2.so")
-REFERENCE_SRC = "/root/reference"
+# The reference checkout: $QMV_REFERENCE_SRC, else a directory named
+# "reference" beside this repository.
+REFERENCE_SRC = os.environ.get("QMV_REFERENCE_SRC") or os.path.join(
+    os.path.dirname(os.path.dirname(HERE)), "reference")
 
 _P = ctypes.c_void_p
 
@@ -113,10 +116,25 @@ class Oracle:
         return Y
 
     def row_abs_dot(self, gtype: int, blocks: np.ndarray, rows: int, cols: int,
-                    x: np.ndarray) -> np.ndarray:
+                    x: np.ndarray, threads: int = 1) -> np.ndarray:
+        """S[r] = sum_k |w_rk x_k| (double); threads > 1 splits the rows
+        (ctypes releases the GIL during each call)."""
         s = np.empty(rows, dtype=np.float64)
         x = np.ascontiguousarray(x, dtype=np.float32)
-        assert self.lib.or_row_abs_dot(gtype, _addr(blocks), rows, cols, x.ctypes.data, s.ctypes.data)
+        if threads <= 1 or rows < 2 * threads:
+            assert self.lib.or_row_abs_dot(gtype, _addr(blocks), rows, cols, x.ctypes.data, s.ctypes.data)
+            return s
+        blocks = np.ascontiguousarray(blocks)
+        row_bytes = (cols // (32 if gtype in (6, 8) else 256)) * {6: 22, 8: 34, 12: 144, 14: 210}[gtype]
+        edges = np.linspace(0, rows, threads + 1).astype(int)
+
+        def part(i):
+            r0, r1 = int(edges[i]), int(edges[i + 1])
+            return self.lib.or_row_abs_dot(gtype, blocks.ctypes.data + r0 * row_bytes, r1 - r0, cols,
+                                           x.ctypes.data, s.ctypes.data + 8 * r0)
+
+        with cf.ThreadPoolExecutor(threads) as ex:
+            assert all(ex.map(part, range(threads)))
         return s
 
     def argmax(self, logits: np.ndarray):

@@ -31,10 +31,13 @@ def to_dev(torch, a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-@pytest.fixture(params=[0, 1], ids=["auto", "loads"])
+@pytest.fixture(params=[0, 1, 4], ids=["auto", "loads", "shared"])
 def gemv_path(request, qmv):
-    """Run a test with the automatic kernel choice (TMA pipeline where its
-    stages fit) and with the direct-load kernel forced."""
+    """Run a test with the automatic kernel choice (the TMA pipeline's
+    exclusive plan where its stages fit, else direct loads), with the
+    direct-load kernel forced, and with the shared TMA plan (half an SM per
+    CTA, register-capped kernel) where its stages fit (else the automatic
+    choice)."""
     qmv.set_gemv_path(request.param)
     yield request.param
     qmv.set_gemv_path(0)

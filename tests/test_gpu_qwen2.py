@@ -126,3 +126,41 @@ def test_qwen2_config4_teacher_forced(cuda, qmv, oracle, workloads):
     vocabulary 151936; three teacher-forced steps."""
     worst = _teacher_forced(qmv, oracle, workloads, "cfg4_qwen2_0_5b", t0=1024, max_ctx=1280, steps=3, seed=0)
     print("relative logit error, relative top-2 gap per step:", worst)
+
+
+def test_qwen2_config4_free_run(cuda, qmv, workloads, ref):
+    """Configuration 4, free run: 40 greedy tokens generated on the device
+    (graph replay, each token fed back on the GPU) against the reference's own
+    scalar build decoding from the same 1024-position cache and start token,
+    each side feeding back its own tokens (forward_token,
+    src/qwen2_architecture.cpp:1195-1531, then sampler_greedy_sample,
+    src/sampler.cpp:14-36).  The sequences must be identical; a divergence is
+    only tolerated at a step whose two candidate logits the reference itself
+    separates by less than the logit bar (a tie within tolerance)."""
+    ob = load_oracle_binding()
+    steps, t0 = 40, 1024
+    m = workloads.make_qwen2("cfg4_qwen2_0_5b", seed=0)
+    tensors = workloads.qwen2_tensor_list(m)
+    keys, vals = workloads.make_kv_cache(m, t0, seed=0)
+    dec = qmv.Qwen2Decoder(m, tensors, t0 + steps)
+    try:
+        dec.set_kv(keys, vals)
+        gpu = [int(t) for t in dec.generate(7, steps)]
+    finally:
+        dec.close()
+    rq = ob.RefQwen2(m, tensors, t0 + steps, path=ob.REF_SCALAR_SO)
+    try:
+        rq.set_kv(keys, vals)
+        tok = 7
+        for i in range(steps):
+            ok, logits = rq.forward(tok)
+            ok2, rtok, _ = ref.greedy(logits)
+            assert ok and ok2
+            if rtok != gpu[i]:
+                gap = float(logits[rtok] - logits[gpu[i]])
+                assert gap <= LOGIT_TOL * float(np.max(np.abs(logits))), (i, rtok, gpu[i], gap)
+                break
+            tok = rtok
+    finally:
+        rq.close()
+    assert qmv.device_status(clear=True) == 0

@@ -36,6 +36,30 @@ def test_argmax_noalloc_matches_workspace_entry_point(cuda, qmv):
         assert qmv.key_to_token(_key(key_na)) == base + n // 2
 
 
+def test_argmax_noalloc_limit_and_ragged_sizes(cuda, qmv):
+    """The largest accepted call (every key slot of the static array in use,
+    the winner inside the last CTA's range) and a size one past a whole number
+    of CTAs (the last CTA holds a single logit, which wins), each twice in a
+    row, against the workspace entry point."""
+    torch = cuda
+    rng = np.random.default_rng(99)
+    ws = torch.zeros(qmv.argmax_workspace_bytes(), dtype=torch.uint8, device="cuda")
+    n_max = qmv.ARGMAX_NOALLOC_MAX_LOGITS
+    for n, win in ((n_max, n_max - 5), (4096 * 37 + 1, 4096 * 37)):
+        a = rng.standard_normal(n).astype(np.float32)
+        a[win] = 100.0
+        d = torch.from_numpy(a).cuda()
+        for _ in range(2):
+            key_ws = torch.zeros(1, dtype=torch.int64, device="cuda")
+            key_na = torch.full((1,), -1, dtype=torch.int64, device="cuda")
+            qmv.argmax(d.data_ptr(), n, key_ws.data_ptr(), ws.data_ptr())
+            qmv.argmax_noalloc(d.data_ptr(), n, key_na.data_ptr())
+            torch.cuda.synchronize()
+            assert _key(key_na) == _key(key_ws)
+            assert qmv.key_to_token(_key(key_na)) == win
+        del d
+
+
 def test_argmax_noalloc_rejects_oversize_and_bad_args(cuda, qmv):
     torch = cuda
     d = torch.zeros(8, dtype=torch.float32, device="cuda")
