@@ -314,6 +314,16 @@ int qmv_qwen2_reset(QmvQwen2 *decoder);
 int qmv_qwen2_stream(const QmvQwen2 *decoder, void **stream);
 /* Kernel launches in one captured step (0 on a null decoder). */
 int qmv_qwen2_kernels_per_step(const QmvQwen2 *decoder);
+/* How decoders created afterwards in this process run a step: 0 (default) =
+ * one launch per projection and attention, captured in a CUDA graph;
+ * 1 = the layer stack as one persistent cooperative launch (one CTA per SM,
+ * grid barriers between the phases of each layer, each CTA copying its rows
+ * of the next two projections into shared memory ahead of use), then the
+ * output projection with its fused argmax and the advance kernel: 3 launches
+ * per token; falls back to 0 where the device cannot keep every CTA
+ * resident.  Same results within the parity bound (mode 1 adds a row's
+ * partial sums in another order).  No counterpart in the reference. */
+int qmv_set_decode_mode(int mode);
 
 /* The reference's per-request operation profile, field for field
  * (OperationProfile, include/metrics.h:6-25; per-format arrays indexed

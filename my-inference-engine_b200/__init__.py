@@ -49,7 +49,7 @@ C_SYMBOLS = [
     "qmv_argmax_noalloc", "qmv_key_to_token", "qmv_greedy_sample",
     "qmv_quantized_tensor_matvec_f32", "qmv_quantized_tensor_matmul_f32",
     "qmv_qwen2_create", "qmv_qwen2_set_kv", "qmv_qwen2_forward", "qmv_qwen2_generate", "qmv_qwen2_begin",
-    "qmv_qwen2_replay", "qmv_qwen2_read", "qmv_qwen2_get_kv", "qmv_qwen2_kernels_per_step",
+    "qmv_qwen2_replay", "qmv_qwen2_read", "qmv_qwen2_get_kv", "qmv_qwen2_kernels_per_step", "qmv_set_decode_mode",
     "qmv_qwen2_destroy", "qmv_gguf_open", "qmv_gguf_open_file", "qmv_gguf_close", "qmv_gguf_info",
     "qmv_gguf_tensor", "qmv_gguf_find_tensor", "qmv_gguf_get_uint", "qmv_gguf_get_float", "qmv_gguf_get_string",
     "qmv_gguf_get_array_info", "qmv_gguf_quantized_view", "qmv_gguf_upload", "qmv_qwen2_create_from_gguf",
@@ -174,6 +174,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "qmv_set_device": (I, [I]),
         "qmv_device_status": (I, [ctypes.POINTER(U32), I]),
         "qmv_set_gemv_path": (I, [I]),
+        "qmv_set_decode_mode": (I, [I]),
         "qmv_set_matmul_path": (I, [I]),
         "qmv_weight_upload": (I, [VP, I, I, ctypes.POINTER(P)]),
         "qmv_weight_free": (I, [P]),
@@ -285,6 +286,19 @@ def _f32(a) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=np.float32)
 
 
+def resident_weight_handle(view: GgufQuantizedTensorView) -> int:
+    """Address of the registry's resident weight for ``view`` on the current
+    device (uploaded on first use; the same handle for every later caller)."""
+    h = ctypes.c_void_p()
+    _check(lib().qmv_resident_weight(ctypes.byref(view), ctypes.byref(h)), "qmv_resident_weight")
+    return int(h.value or 0)
+
+
+def resident_release_all() -> None:
+    """Free every registry-owned resident weight (no call may be using them)."""
+    _check(lib().qmv_resident_release_all(), "qmv_resident_release_all")
+
+
 # ------------------------------------------------ reference-shaped entry points
 
 def quantized_tensor_matvec_f32(matrix: GgufQuantizedTensorView, input, input_count: int,
@@ -354,6 +368,12 @@ def device_status(clear: bool = False) -> int:
 
 
 GEMV_AUTO, GEMV_LOADS, GEMV_TMA = 0, 1, 2
+
+
+def set_decode_mode(mode: int):
+    """0 (default): one launch per projection; 1: persistent layer stack
+    (3 launches per token).  Read when a decoder is created."""
+    _check(lib().qmv_set_decode_mode(mode), "qmv_set_decode_mode")
 
 
 def set_gemv_path(path: int):

@@ -145,6 +145,8 @@ struct Staging {
     void *ws = nullptr;
     unsigned long long *dkey = nullptr;
     unsigned long long *hkey = nullptr;
+    unsigned int *hstatus = nullptr;  // mapped pinned word: this thread's expired-wait bits
+    unsigned int *dstatus = nullptr;  // its device address
     cudaEvent_t ev[2] = {nullptr, nullptr};  // around the kernels (profiling)
 };
 
@@ -155,11 +157,15 @@ struct StagingSet {
         for (auto &kv : per_device) {
             Staging &st = kv.second;
             if (cudaSetDevice(kv.first) != cudaSuccess) continue;
-            cudaFree(st.dx);
-            cudaFree(st.dy);
+            if (st.stream) {
+                qmv::stream_free(st.dx, st.stream);
+                qmv::stream_free(st.dy, st.stream);
+                cudaStreamSynchronize(st.stream);
+            }
             cudaFree(st.ws);
             cudaFree(st.dkey);
             cudaFreeHost(st.hkey);
+            cudaFreeHost(st.hstatus);
             for (cudaEvent_t ev : st.ev)
                 if (ev) cudaEventDestroy(ev);
             if (st.stream) cudaStreamDestroy(st.stream);
@@ -211,21 +217,45 @@ int staging(Staging **out)
         QMV_CUDA(cudaMemset(st.ws, 0, qmv::kArgmaxWorkspaceBytes), "cudaMemset(workspace)");
         QMV_CUDA(cudaMalloc(&st.dkey, sizeof(unsigned long long)), "cudaMalloc(key)");
         QMV_CUDA(cudaMallocHost(&st.hkey, sizeof(unsigned long long)), "cudaMallocHost(key)");
+        QMV_CUDA(cudaHostAlloc(&st.hstatus, 16, cudaHostAllocMapped), "cudaHostAlloc(status)");
+        QMV_CUDA(cudaHostGetDevicePointer((void **)&st.dstatus, st.hstatus, 0), "cudaHostGetDevicePointer");
     }
     *out = &st;
     return 1;
 }
 
-int grow(float **buf, size_t *cap, size_t count)
+// Grow a per-thread staging buffer on its own stream from the library's
+// stream-ordered pool: no cudaFree (and so no device-wide synchronisation)
+// on the call path when a larger shape arrives.
+int grow(float **buf, size_t *cap, size_t count, cudaStream_t s)
 {
     if (*cap >= count) return 1;
-    if (*buf) cudaFree(*buf);
+    QMV_CUDA(qmv::stream_free(*buf, s), "free staging");
     *buf = nullptr;
     *cap = 0;
-    QMV_CUDA(cudaMalloc(buf, count * sizeof(float)), "cudaMalloc(staging)");
+    QMV_CUDA(qmv::stream_alloc((void **)buf, count * sizeof(float), s), "allocate staging");
     *cap = count;
     return 1;
 }
+
+// For the duration of one drop-in call, the kernels this thread launches also
+// report expired bounded waits in the thread's own status word.
+struct CallStatus {
+    Staging *st;
+    explicit CallStatus(Staging *s) : st(s)
+    {
+        *st->hstatus = 0u;
+        qmv::set_call_status(st->dstatus);
+    }
+    ~CallStatus() { qmv::set_call_status(nullptr); }
+    // after the call's synchronisation
+    int check(const char *what) const
+    {
+        const unsigned int v = *(volatile unsigned int *)st->hstatus;
+        if (v != 0u) return fail("%s: a bounded wait of this call's kernel expired (status 0x%x)", what, v);
+        return 1;
+    }
+};
 
 int decode_key(unsigned long long key, int *id)
 {
@@ -664,14 +694,16 @@ QMV_EXPORT int qmv_quantized_tensor_matvec_f32(const GgufQuantizedTensorView *ma
     if (!qmv_resident_weight(matrix, &w)) return 0;
     Staging *st = nullptr;
     if (!staging(&st)) return 0;
-    if (!grow(&st->dx, &st->dx_cap, (size_t)cols) || !grow(&st->dy, &st->dy_cap, (size_t)rows)) return 0;
     cudaStream_t s = st->stream;
+    if (!grow(&st->dx, &st->dx_cap, (size_t)cols, s) || !grow(&st->dy, &st->dy_cap, (size_t)rows, s)) return 0;
+    const CallStatus cs(st);
     QMV_CUDA(cudaMemcpyAsync(st->dx, input, sizeof(float) * cols, cudaMemcpyHostToDevice, s), "copy input");
     if (!kernels_begin(st)) return 0;
     QMV_CUDA(qmv::launch_gemv(w->L, w->dev, st->dx, st->dy, nullptr, s), "gemv launch");
     if (!kernels_end(st)) return 0;
     QMV_CUDA(cudaMemcpyAsync(output, st->dy, sizeof(float) * rows, cudaMemcpyDeviceToHost, s), "copy output");
     QMV_CUDA(cudaStreamSynchronize(s), "matvec");
+    if (!cs.check("matvec")) return 0;
     return kernels_elapsed(st);
 }
 
@@ -694,13 +726,15 @@ QMV_EXPORT int qmv_quantized_tensor_matmul_f32(const GgufQuantizedTensorView *ma
     Staging *st = nullptr;
     if (!staging(&st)) return 0;
     const size_t nx = (size_t)batch_count * cols, ny = (size_t)batch_count * rows;
-    if (!grow(&st->dx, &st->dx_cap, nx) || !grow(&st->dy, &st->dy_cap, ny)) return 0;
     cudaStream_t s = st->stream;
+    if (!grow(&st->dx, &st->dx_cap, nx, s) || !grow(&st->dy, &st->dy_cap, ny, s)) return 0;
+    const CallStatus cs(st);
     QMV_CUDA(cudaMemcpyAsync(st->dx, inputs, sizeof(float) * nx, cudaMemcpyHostToDevice, s), "copy inputs");
     if (!kernels_begin(st)) return 0;
     QMV_CUDA(qmv::launch_matmul(w->L, w->dev, st->dx, batch_count, st->dy, s), "matmul launch");
     if (!kernels_end(st)) return 0;
     QMV_CUDA(cudaMemcpyAsync(outputs, st->dy, sizeof(float) * ny, cudaMemcpyDeviceToHost, s), "copy outputs");
     QMV_CUDA(cudaStreamSynchronize(s), "matmul");
+    if (!cs.check("matmul")) return 0;
     return kernels_elapsed(st);
 }

@@ -97,10 +97,12 @@ struct XSource {
 
 // Fused prologue / epilogue of a GEMV (the decode step's RMSNorm, SwiGLU,
 // bias and residual additions); device pointers.  Zero-initialised: none.
-enum : int { kPreNone = 0, kPreRmsNorm = 1, kPreSwiGlu = 2 };
+enum : int { kPreNone = 0, kPreRmsNorm = 1, kPreSwiGlu = 2, kPreScale = 3 };
 struct Fuse {
     int pre;            // kPreRmsNorm: x <- (x / sqrt(mean(x^2) + eps)) * norm
                         // kPreSwiGlu:  x <- up * x / (1 + exp(-x))   (x is the gate)
+                        // kPreScale:   x <- x * norm (the persistent step's RMSNorm,
+                        //              whose 1 / sqrt(mean(x^2) + eps) scales the dot)
     const float *norm;  // kPreRmsNorm: weight[cols]
     float eps;
     const float *up;    // kPreSwiGlu: up[cols]
@@ -155,13 +157,20 @@ void set_gemv_path(int path);
 void set_matmul_path(int path);
 // Device status bits set by bounded waits that expired (0 = healthy).
 cudaError_t read_status(unsigned int *out, bool clear);
+// A device-visible word that the calling thread's later launches also set
+// their expired-wait bits in (null: the device-wide word only).
+void set_call_status(unsigned int *word);
+// Stream-ordered scratch from the library's per-device pool (no device-wide
+// synchronisation; steady-state allocations do not reach the driver).
+cudaError_t stream_alloc(void **ptr, size_t bytes, cudaStream_t s);
+cudaError_t stream_free(void *ptr, cudaStream_t s);
 // ---- device-resident decode step (Qwen2 architecture)
 // Step state in device memory, so one step replays from a CUDA graph.
 struct DecodeState {
     int pos;             // position the next step writes
     int tok;             // token of the next step
     int steps;           // tokens produced so far (index into the history)
-    unsigned int error;  // 1 token out of range, 2 context full, 4 no finite logit
+    unsigned int error;  // 1 token out of range, 2 context full, 4 no finite logit, 8 barrier expired
 };
 // h = row st->tok of the resident embedding matrix (bit-exact dequant).
 cudaError_t launch_embed(const Layout &L, const uint8_t *w, DecodeState *st, float *h, cudaStream_t s);
@@ -173,9 +182,49 @@ size_t attention_workspace_floats(int heads, int kv_heads, int head_dim, int max
 cudaError_t launch_attention(const float *qkv, int heads, int kv_heads, int head_dim, float *kc, float *vc,
                              int max_ctx, float rope_base, DecodeState *st, float *part, unsigned int *counter,
                              float *att, cudaStream_t s);
+// The layer stack of one decode step as one cooperative launch (one CTA per
+// SM, grid barriers between the phases of each layer): embedding, then per
+// layer [q; k; v] (RMSNorm prologue, biases), attention, o (residual),
+// [gate; up] (RMSNorm prologue), down (SwiGLU prologue, residual).  Leaves h
+// for the output projection.  head_dim must be 64.
+struct PGemv {
+    Layout L;
+    const uint8_t *w;  // resident rows (null: absent)
+};
+struct PLayer {
+    PGemv qkv[3];  // [q; k; v] as one matrix (n_qkv = 1) or q, k, v (3)
+    int n_qkv;
+    PGemv o;
+    PGemv gu[2];  // [gate; up] as one matrix (n_gu = 1) or gate, up (2)
+    int n_gu;
+    PGemv down;
+    const float *attn_norm, *ffn_norm, *bias_qkv;
+    float *kc, *vc;  // this layer's cache [max_ctx][kv_heads * 64]
+};
+struct GridBar {  // zeroed before the first launch
+    unsigned int count;  // arrivals of the current step
+    unsigned int abort;  // a barrier expired: every later one returns at once
+    unsigned int pad[2];
+};
+struct PStep {
+    const PLayer *layers;  // device array of n_layers
+    int n_layers;
+    int dim, hid, heads, kv_heads, max_ctx;
+    float eps, rope_base;
+    PGemv embd;
+    float *h, *qkv, *att, *gate, *up;  // up: the up output of layers with n_gu == 2
+    float *part;                       // attention_workspace_floats
+    unsigned int *attn_cnt;            // kv_heads zeroed words
+    DecodeState *st;                   // error bit 8: a grid barrier expired
+    GridBar *bar;                      // count re-armed by launch_advance
+    uint32_t slot_bytes;               // decode_layers_slot_bytes
+};
+uint32_t decode_layers_slot_bytes(int dim, int hid);
+size_t decode_layers_smem(int dim, int hid, uint32_t slot_bytes);
+cudaError_t launch_decode_layers(const PStep &P, cudaStream_t s);
 // next token from the step's argmax key; history[st->steps] = token; pos += 1
 cudaError_t launch_advance(const unsigned long long *key, DecodeState *st, int *history, int max_steps,
-                           cudaStream_t s);
+                           cudaStream_t s, unsigned int *bar_count = nullptr);
 // Prefill steps (the reference's qwen2_prefill_tokens between its
 // projections), over n consecutive positions of one chunk; row-major
 // activations, device pointers.

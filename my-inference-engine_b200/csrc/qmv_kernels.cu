@@ -334,10 +334,16 @@ __device__ __forceinline__ XS xs_view(const uint8_t *base, int cols)
 // global-load latency is paid once; position p goes to base + p * pos_bytes.
 // pre (kPreRmsNorm / kPreSwiGlu, one position): the x of a fused prologue,
 // formed element-wise as it is loaded (denom = sqrt(mean(x^2) + eps)).
-template <uint32_t FMT, int NT = kThreads>
+// special (shared, optional): set to 1 when a block holds a NaN/Inf or is
+// nonzero with every magnitude below 2^-100 (the blocks the integer path would
+// turn into NaN or flush); the kernel then computes its rows in fp32.
+// LIVE: x and aux were written earlier in the same launch (the persistent
+// decode step), so they are read through L2 rather than the read-only path.
+// ss (kPreScale): this thread's sum of x^2 is added to *ss.
+template <uint32_t FMT, int NT = kThreads, bool LIVE = false>
 __device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t *base, int np = 1,
                            size_t pos_bytes = 0, int pre = kPreNone, float denom = 1.f,
-                           const float *__restrict__ aux = nullptr)
+                           const float *__restrict__ aux = nullptr, int *special = nullptr, float *ss = nullptr)
 {
     const int n4 = cols >> 2;
     const int total = np * n4;
@@ -347,13 +353,18 @@ __device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             int g = (it0 + u) * NT + threadIdx.x;
-            v[u] = g < total ? __ldg(reinterpret_cast<const float4 *>(x) + g)
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[u] = g >= total ? make_float4(0.f, 0.f, 0.f, 0.f)
+                   : LIVE     ? __ldcg(reinterpret_cast<const float4 *>(x) + g)
+                              : __ldg(reinterpret_cast<const float4 *>(x) + g);
             if (pre != kPreNone && g < total) {
-                const float4 a = __ldg(reinterpret_cast<const float4 *>(aux) + g);
+                const float4 a = LIVE ? __ldcg(reinterpret_cast<const float4 *>(aux) + g)
+                                      : __ldg(reinterpret_cast<const float4 *>(aux) + g);
                 if (pre == kPreRmsNorm) {
                     v[u] = make_float4((v[u].x / denom) * a.x, (v[u].y / denom) * a.y, (v[u].z / denom) * a.z,
                                        (v[u].w / denom) * a.w);
+                } else if (pre == kPreScale) {
+                    *ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+                    v[u] = make_float4(v[u].x * a.x, v[u].y * a.y, v[u].z * a.z, v[u].w * a.w);
                 } else {
                     v[u] = make_float4(a.x * (v[u].x / (1.f + expf(-v[u].x))), a.y * (v[u].y / (1.f + expf(-v[u].y))),
                                        a.z * (v[u].z / (1.f + expf(-v[u].z))), a.w * (v[u].w / (1.f + expf(-v[u].w))));
@@ -377,6 +388,7 @@ __device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t
             // Power-of-two scale s = 2^e with |x| / s <= 32639: x * 2^-e is
             // exact, so dyadic inputs (small integers, k/2^n) stay exact.
             const bool bad = a >= 0x7f800000u;
+            if (special != nullptr && g < total && (bad || (a != 0u && (a >> 23) < 27u))) *special = 1;
             const int ea = max((int)(a >> 23), 27);  // blocks below 2^-100 share 2^-114
             int e = ea - 127 - 14;
             float inv = __uint_as_float((uint32_t)(127 - e) << 23);
@@ -499,6 +511,13 @@ template <> struct W<kQ8_0> {
         const int al = dot4(u.b, x.l[1], dot4(u.a, x.l[0], 0));
         return (u.d * x.r[0].x) * (float)(ah * 256 + al);
     }
+    // weights 32c.. of chunk (block) c: d * q
+    template <typename XF>
+    static __device__ __forceinline__ float dot_f32(const U &u, int c, const XF &xv)
+    {
+        const auto f = [&](uint32_t q) { return u.d * (float)(int8_t)q; };
+        return dot16_f32(u.b, 32 * c + 16, f, xv, dot16_f32(u.a, 32 * c, f, xv, 0.f));
+    }
     __device__ __forceinline__ float dot(const XR<2> &x) const { return dot_u(unpack(), x); }
 };
 
@@ -546,6 +565,13 @@ template <> struct W<kQ5_0> {
         const int ah = dot4(u.hw, x.h[1], dot4(u.lw, x.h[0], 0));
         const int al = dot4(u.hw, x.l[1], dot4(u.lw, x.l[0], 0));
         return u.d * (x.r[0].x * (float)(ah * 256 + al) - 16.f * (x.r[0].y + x.r[1].y));
+    }
+    // weights 32c.. of block c: d * (v - 16)
+    template <typename XF>
+    static __device__ __forceinline__ float dot_f32(const U &u, int c, const XF &xv)
+    {
+        const auto f = [&](uint32_t v) { return u.d * (float)((int)v - 16); };
+        return dot16_f32(u.hw, 32 * c + 16, f, xv, dot16_f32(u.lw, 32 * c, f, xv, 0.f));
     }
     __device__ __forceinline__ float dot(const XR<2> &x) const { return dot_u(unpack(), x); }
 };
@@ -614,6 +640,17 @@ template <> struct W<kQ4_K> {
         const float v0 = u.s0 * (x.r[0].x * (float)(ah0 * 256 + al0)) - u.m0 * (x.r[0].y + x.r[1].y);
         const float v1 = u.s1 * (x.r[2].x * (float)(ah1 * 256 + al1)) - u.m1 * (x.r[2].y + x.r[3].y);
         return v0 + v1;
+    }
+    // weights 64c.. of chunk c (sub-blocks 2g, 2g+1): d sc q - dmin m
+    template <typename XF>
+    static __device__ __forceinline__ float dot_f32(const U &u, int c, const XF &xv)
+    {
+        const auto f0 = [&](uint32_t q) { return u.s0 * (float)q - u.m0; };
+        const auto f1 = [&](uint32_t q) { return u.s1 * (float)q - u.m1; };
+        float acc = dot16_f32(u.la, 64 * c, f0, xv, 0.f);
+        acc = dot16_f32(u.lb, 64 * c + 16, f0, xv, acc);
+        acc = dot16_f32(u.ua, 64 * c + 32, f1, xv, acc);
+        return dot16_f32(u.ub, 64 * c + 48, f1, xv, acc);
     }
     __device__ __forceinline__ float dot(const XR<4> &x) const { return dot_u(unpack(), x); }
 };
@@ -686,8 +723,95 @@ template <> struct W<kQ6_K> {
         acc += r.s3 * (x.r[3].x * (float)A3 - 32.f * x.r[3].y);
         return r.d * acc;
     }
+    // chunk c = 4 sb + 2 g + h holds weights 256 sb + 128 g + 32 r + 16 h + o:
+    // d * sc_r * (q - 32)
+    template <typename XF>
+    static __device__ __forceinline__ float dot_f32(const U &r, int c, const XF &xv)
+    {
+        const int base = 256 * (c >> 2) + 128 * ((c >> 1) & 1) + 16 * (c & 1);
+        const auto f0 = [&](uint32_t q) { return r.d * r.s0 * (float)((int)q - 32); };
+        const auto f1 = [&](uint32_t q) { return r.d * r.s1 * (float)((int)q - 32); };
+        const auto f2 = [&](uint32_t q) { return r.d * r.s2 * (float)((int)q - 32); };
+        const auto f3 = [&](uint32_t q) { return r.d * r.s3 * (float)((int)q - 32); };
+        float acc = dot16_f32(r.w0, base, f0, xv, 0.f);
+        acc = dot16_f32(r.w1, base + 32, f1, xv, acc);
+        acc = dot16_f32(r.w2, base + 64, f2, xv, acc);
+        return dot16_f32(r.w3, base + 96, f3, xv, acc);
+    }
     __device__ __forceinline__ float dot(const XR<4> &x) const { return dot_u(unpack(), x); }
 };
+
+// ------------------------------------------------ fp32 rows (rare path)
+//
+// When x holds a NaN/Inf or a tiny block, a CTA computes its rows in fp32:
+// each weight dequantized as the reference does (src/quantization.cpp:54-67,
+// 161-184, 380-409, 588-615) times the float x, so Inf and NaN propagate as in
+// the reference's loops and tiny magnitudes keep their bits.  xv(k) returns
+// element k of the (prologue-transformed) x.
+
+template <int K>
+__device__ __forceinline__ uint32_t byte_at(const uint4 &v)
+{
+    const uint32_t w = K < 4 ? v.x : K < 8 ? v.y : K < 12 ? v.z : v.w;
+    return (w >> (8 * (K & 3))) & 0xffu;
+}
+
+// Element k of position p's x as the fused prologue forms it (the fp32 rows).
+struct XVal {
+    const float *x;
+    int pre;
+    float denom;
+    const float *aux;
+    __device__ __forceinline__ float operator()(int k) const
+    {
+        const float v = __ldg(x + k);
+        if (pre == kPreRmsNorm) return (v / denom) * __ldg(aux + k);
+        if (pre == kPreSwiGlu) return __ldg(aux + k) * (v / (1.f + expf(-v)));
+        return v;
+    }
+};
+
+// sum over the 16 bytes of v of f(byte, k) * x[base + k]
+template <typename F, typename XF>
+__device__ __forceinline__ float dot16_f32(const uint4 &v, int base, const F &f, const XF &xv, float acc)
+{
+#define QMV_DOT16_STEP(K) acc = fmaf(f(byte_at<K>(v)), xv(base + (K)), acc);
+    QMV_DOT16_STEP(0) QMV_DOT16_STEP(1) QMV_DOT16_STEP(2) QMV_DOT16_STEP(3)
+    QMV_DOT16_STEP(4) QMV_DOT16_STEP(5) QMV_DOT16_STEP(6) QMV_DOT16_STEP(7)
+    QMV_DOT16_STEP(8) QMV_DOT16_STEP(9) QMV_DOT16_STEP(10) QMV_DOT16_STEP(11)
+    QMV_DOT16_STEP(12) QMV_DOT16_STEP(13) QMV_DOT16_STEP(14) QMV_DOT16_STEP(15)
+#undef QMV_DOT16_STEP
+    return acc;
+}
+
+// fp32 rows [r0, r1) of y (the rare path): a warp per row, lanes over its
+// chunks read from global memory; y[row] = dot (+ add[row]).  Returns the
+// calling thread's best argmax key of the rows it wrote.  Not inlined: kept
+// out of the GEMV kernels' code it would otherwise slow down (measured).
+template <uint32_t FMT>
+__device__ __noinline__ unsigned long long fp32_rows(const Layout &L, const uint8_t *__restrict__ w, int r0, int r1, int warp,
+                                        int nwarps, const XVal &xv, float *y, const float *add, bool want_key,
+                                        int index_base)
+{
+    const int lane = threadIdx.x & 31;
+    unsigned long long best = 0ull;
+    for (int row = r0 + warp; row < r1; row += nwarps) {
+        float acc = 0.f;
+        for (int c = lane; c < L.C; c += 32) {
+            W<FMT> wv;
+            wv.load(w + (uint64_t)row * L.row_stride, L, c);
+            acc += W<FMT>::dot_f32(wv.unpack(), c, xv);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
+        if (lane == 0) {
+            const float out = add != nullptr ? acc + add[row] : acc;
+            y[row] = out;
+            if (want_key) best = max_ull(best, make_key(out, index_base + row));
+        }
+    }
+    return best;
+}
 
 // ------------------------------------------------------- GEMV (loads)
 //
@@ -708,11 +832,15 @@ gemv_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x
 {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ unsigned long long kscratch[kThreads / 32];
+    __shared__ int special;
     constexpr int NSL = W<FMT>::kSlices;
 
     const int C = L.C;
-    quantize_x<FMT>(x, L.cols, C, smem);
+    if (threadIdx.x == 0) special = 0;
     __syncthreads();
+    quantize_x<FMT>(x, L.cols, C, smem, 1, 0, kPreNone, 1.f, nullptr, &special);
+    __syncthreads();
+    const bool f32 = *(volatile int *)&special != 0;
     const XS s = xs_view(smem, L.cols);
 
     constexpr int GPW = 32 / TPT;
@@ -780,11 +908,17 @@ gemv_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ x
         it = nit;
     };
 
-    int t = wg, it = 0;
-    if (n_items > 0) load_item(t, it, bufa);
-    for (int k = 0; k < n_items; k += 2) {
-        step(k, t, it, bufa, bufb);
-        if (k + 1 < n_items) step(k + 1, t, it, bufb, bufa);
+    if (f32) {
+        // special x: every row of the grid in fp32, a warp per row
+        best = fp32_rows<FMT>(L, w, 0, L.rows, wg, wtot, XVal{x, kPreNone, 1.f, nullptr}, y, nullptr,
+                              want_argmax != 0, am.index_base);
+    } else {
+        int t = wg, it = 0;
+        if (n_items > 0) load_item(t, it, bufa);
+        for (int k = 0; k < n_items; k += 2) {
+            step(k, t, it, bufa, bufb);
+            if (k + 1 < n_items) step(k + 1, t, it, bufb, bufa);
+        }
     }
     if (want_argmax) {
         best = block_max_key(best, kscratch);
@@ -813,6 +947,17 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ unsigned int g_status;
 enum : unsigned int { kStatusConsumerTimeout = 1u, kStatusProducerTimeout = 2u, kStatusDrainTimeout = 4u };
+
+// An expired wait sets its bit in the device-wide word and, when the launch
+// carries one, in the calling thread's own word (a mapped host word of the
+// drop-in calls, written with a plain store: host memory need not support
+// device atomics), so a concurrent caller's clean call is not failed by
+// another's timeout.
+__device__ __forceinline__ void report_status(unsigned int *call_status, unsigned int bit)
+{
+    atomicOr(&g_status, bit);
+    if (call_status != nullptr) *(volatile unsigned int *)call_status = *(volatile unsigned int *)call_status | bit;
+}
 
 __device__ __forceinline__ unsigned long long globaltimer()
 {
@@ -906,6 +1051,7 @@ struct TmaPlan {
     int rows_per_warp;     // R
     int np;                // positions (1: GEMV; up to the kernel's NP: batched)
     int split;             // warps per row (2: long rows, see gemv_tma_kernel)
+    unsigned int *status;  // the calling thread's status word, or null
 };
 
 // NP > 1: the batched form for up to NP positions (x holds P.np rows of
@@ -921,11 +1067,15 @@ struct TmaShared {
     unsigned long long kscratch[kMaxConsumerWarps + 1];
     float partial[2][kMaxConsumerWarps];
     float sumsq[kMaxConsumerWarps];
+    int special;  // x holds a NaN/Inf or tiny block: rows in fp32
 };
+
 
 // One CTA (number cta of ncta sharing the matrix) of the TMA GEMV; smem is
 // the dynamic shared memory (quantized x, then the stage ring).
-template <uint32_t FMT, int CW, int R, int NP = 1, int SPLIT = 1>
+// RARE: compile the fp32 rows of a special x (the paired gate/up launch of
+// the decode step leaves them out: there any non-finite value fails the step).
+template <uint32_t FMT, int CW, int R, int NP = 1, int SPLIT = 1, bool RARE = true>
 __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int cta, int ncta, const Layout &L,
                                               const uint8_t *__restrict__ w, const float *__restrict__ x,
                                               float *__restrict__ y_, const ArgmaxOut &am, int want_argmax,
@@ -961,6 +1111,7 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
         }
         for (int i = 0; i < 4; ++i) mbar_init(pbar0 + 8u * i, (uint32_t)(kConsumerWarps / 2));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        sh.special = 0;
     }
     __syncthreads();
 
@@ -973,7 +1124,7 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
             for (int k = 0; k < n_stages; ++k) {
                 const int sidx = k % NS;
                 if (k >= NS && !mbar_wait(empty0 + 8u * sidx, (uint32_t)((k / NS - 1) & 1))) {
-                    atomicOr(&g_status, kStatusProducerTimeout);
+                    report_status(P.status, kStatusProducerTimeout);
                     ok = false;
                     break;
                 }
@@ -993,7 +1144,7 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
                 // drain: every issued copy must land before the CTA exits
                 for (int k = max(0, issued - NS); k < issued; ++k) {
                     if (!mbar_wait(full0 + 8u * (k % NS), (uint32_t)((k / NS) & 1))) {
-                        atomicOr(&g_status, kStatusDrainTimeout);
+                        report_status(P.status, kStatusDrainTimeout);
                         break;
                     }
                 }
@@ -1020,16 +1171,33 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
             for (int i = 0; i < CW; ++i) ss += sh.sumsq[i];
             denom = sqrtf(ss / (float)L.cols + fu.eps);
         }
-        quantize_x<FMT, CW * 32>(x, L.cols, C, smem, NP == 1 ? 1 : P.np, xb, NP == 1 ? fu.pre : kPreNone, denom,
-                                 fu.pre == kPreRmsNorm ? fu.norm : fu.up);
+        const int pre = NP == 1 ? fu.pre : kPreNone;
+        const float *aux = fu.pre == kPreRmsNorm ? fu.norm : fu.up;
+        quantize_x<FMT, CW * 32>(x, L.cols, C, smem, NP == 1 ? 1 : P.np, xb, pre, denom, aux,
+                                 NP == 1 && RARE ? &sh.special : nullptr);
         asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+        const bool f32 = *(volatile int *)&sh.special != 0;  // uniform over the CTA
         const XS s = xs_view(smem, L.cols);
         const int NI = (C + 32 * SPLIT - 1) / (32 * SPLIT);
         const int rw = warp % (CW / SPLIT), half = warp / (CW / SPLIT);  // row slot, chunk half
+        if (RARE && NP == 1 && f32) {
+            // special x: consume the stages (the producer must finish), then
+            // this CTA's rows in fp32 from global memory
+            for (int k = 0; k < n_stages; ++k) {
+                if (!mbar_wait(full0 + 8u * (k % NS), (uint32_t)((k / NS) & 1))) {
+                    report_status(P.status, kStatusConsumerTimeout);
+                    break;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty0 + 8u * (k % NS));
+            }
+            best = fp32_rows<FMT>(L, w, r0, r1, warp, CW, XVal{x, pre, denom, aux}, y, fu.add, want_argmax != 0,
+                                  am.index_base);
+        } else
         for (int k = 0; k < n_stages; ++k) {
             const int sidx = k % NS;
             if (!mbar_wait(full0 + 8u * sidx, (uint32_t)((k / NS) & 1))) {
-                atomicOr(&g_status, kStatusConsumerTimeout);
+                report_status(P.status, kStatusConsumerTimeout);
                 break;
             }
             const int base_row = r0 + k * SR;
@@ -1101,7 +1269,7 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
                     if (lane == 0) mbar_arrive(pfree);
                 }
                 if (!__all_sync(kFull, okp)) {
-                    if (lane == 0) atomicOr(&g_status, kStatusConsumerTimeout);
+                    if (lane == 0) report_status(P.status, kStatusConsumerTimeout);
                     break;
                 }
             }
@@ -1170,10 +1338,11 @@ gemv_pair_kernel(GemvPair pr, const float *__restrict__ x, Fuse fu)
     const Exchange solo{};
     const int cta = (int)blockIdx.x;
     if (cta < pr.ctas0)
-        gemv_tma_body<FA, CW, R>(smem, sh, cta, pr.ctas0, pr.L[0], pr.w[0], x, pr.y[0], none, 0, pr.P[0], solo, fu);
+        gemv_tma_body<FA, CW, R, 1, 1, false>(smem, sh, cta, pr.ctas0, pr.L[0], pr.w[0], x, pr.y[0], none, 0, pr.P[0],
+                                              solo, fu);
     else
-        gemv_tma_body<FB, CW, R>(smem, sh, cta - pr.ctas0, (int)gridDim.x - pr.ctas0, pr.L[1], pr.w[1], x, pr.y[1],
-                                 none, 0, pr.P[1], solo, fu);
+        gemv_tma_body<FB, CW, R, 1, 1, false>(smem, sh, cta - pr.ctas0, (int)gridDim.x - pr.ctas0, pr.L[1], pr.w[1],
+                                              x, pr.y[1], none, 0, pr.P[1], solo, fu);
 }
 
 // ------------------------------------------------------------- matmul
@@ -1700,7 +1869,7 @@ split_x_kernel(XSource src, int np, int cols, int nk, uint8_t *__restrict__ xs)
 template <uint32_t FMT, int TN, bool WSMEM>
 __global__ void __launch_bounds__(kTcThreads + 64, 1)
 matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, XSource X, const uint8_t *__restrict__ xs, int np,
-                 float *__restrict__ Y, int S)
+                 float *__restrict__ Y, int S, unsigned int *call_status)
 {
     static_assert(TN % 16 == 0 && TN >= 32 && TN <= 256, "N of one MMA: a multiple of 16 in 32..256");
     static_assert(kTcM * (kTcK / 8) == kTcThreads * kTcUnits, "kTcUnits weight units per decode thread and stage");
@@ -1888,12 +2057,12 @@ matmul_tc_kernel(Layout L, const uint8_t *__restrict__ w, XSource X, const uint8
     }
     const bool failed = __syncthreads_or(!ok);
     if (failed && warp == kCopyWarp && lane == 0) {
-        atomicOr(&g_status, kStatusMmaTimeout);
+        report_status(call_status, kStatusMmaTimeout);
         // copies still in flight must land before the CTA exits
-        if (WSMEM && !mbar_wait(tbar, 0u)) atomicOr(&g_status, kStatusDrainTimeout);
+        if (WSMEM && !mbar_wait(tbar, 0u)) report_status(call_status, kStatusDrainTimeout);
         for (int j = issued - S > 0 ? issued - S : 0; j < issued; ++j) {
             if (!mbar_wait(xbar0 + 8u * (j % S), (uint32_t)((j / S) & 1))) {
-                atomicOr(&g_status, kStatusDrainTimeout);
+                report_status(call_status, kStatusDrainTimeout);
                 break;
             }
         }
@@ -2157,7 +2326,7 @@ __global__ void dequant_raw_kernel(const uint8_t *__restrict__ raw, uint64_t nbl
 constexpr int kAttnChunk = 64;  // cached tokens per attention CTA
 constexpr int kAttnThreads = 256;
 constexpr int kAttnMaxGroup = 16;  // query heads per KV head
-// chunks whose merge weights fit the score tile (kAttnMaxGroup x kAttnChunk)
+// merge weights (chunk, head) that fit the score tile: one merge tile
 constexpr int kAttnMaxChunks = kAttnMaxGroup * kAttnChunk;
 
 // One CTA: row st->tok of the resident embedding (src/qwen2_architecture.cpp:375-475
@@ -2188,41 +2357,49 @@ __global__ void embed_kernel(Layout L, const uint8_t *__restrict__ w, DecodeStat
 // sum_c e^(m_c - M) l_c -- the softmax and weighted sum of
 // transformer_attention_f32 (src/transformer_ops.cpp:68-153), evaluated
 // chunk-wise.
+// Shared tiles of one attention work item.
 template <int HD>
-__global__ void __launch_bounds__(kAttnThreads)
-attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *__restrict__ kc,
-                 float *__restrict__ vc, int max_ctx, float rope_base, DecodeState *st, float *__restrict__ part,
-                 unsigned int *__restrict__ counter, float *__restrict__ att)
+struct AttnShared {
+    float cs[HD / 2], sn[HD / 2];
+    float qs[kAttnMaxGroup][HD];
+    float ks[kAttnChunk][HD + 1];
+    __align__(16) float vs[kAttnChunk][HD];
+    float sc[kAttnMaxGroup][kAttnChunk];
+    float mx[kAttnMaxGroup], den[kAttnMaxGroup];
+    int last;
+};
+
+// One work item (kv head g, chunk c) of the decode attention, run by all NT
+// threads of the CTA.  PDL: the
+// standalone kernel's programmatic-launch handshake around the loads that do
+// not depend on the Q/K/V projection.
+template <int HD, bool PDL, int NT = kAttnThreads>
+__device__ void attention_item(AttnShared<HD> &sm, int g, int c, const float *__restrict__ qkv, int heads,
+                               int kv_heads, float *__restrict__ kc, float *__restrict__ vc, int max_ctx,
+                               float rope_base, const DecodeState *st, float *__restrict__ part,
+                               unsigned int *__restrict__ counter, float *__restrict__ att)
 {
-    __shared__ float cs[HD / 2], sn[HD / 2];
-    __shared__ float qs[kAttnMaxGroup][HD];
-    __shared__ float ks[kAttnChunk][HD + 1];
-    __shared__ __align__(16) float vs[kAttnChunk][HD];
-    __shared__ float sc[kAttnMaxGroup][kAttnChunk];
-    __shared__ int last;
+    auto &cs = sm.cs;
+    auto &sn = sm.sn;
+    auto &qs = sm.qs;
+    auto &ks = sm.ks;
+    auto &vs = sm.vs;
+    auto &sc = sm.sc;
+    auto &last = sm.last;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = blockIdx.x, c = blockIdx.y;
-    // The next launch (the output projection) may start streaming its
-    // weights; it reads att only after its own griddepcontrol.wait.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const int pos = st->pos;  // written by the previous step's advance_kernel
-    if (pos < 0 || pos >= max_ctx) {
-        if (g == 0 && c == 0 && tid == 0) atomicOr(&st->error, 2u);
-        return;
-    }
+    const int pos = st->pos;
     const int T = pos + 1, nchunk = (T + kAttnChunk - 1) / kAttnChunk;
-    if (c >= nchunk) return;
     const int G = heads / kv_heads, dim = heads * HD, kvd = kv_heads * HD;
     const int t0 = c * kAttnChunk, tn = min(kAttnChunk, T - t0);
 
     // Cached positions (< pos) do not depend on this layer's projections:
     // load them before waiting for the Q/K/V GEMV, every load in flight at once.
-    constexpr int kV4 = kAttnChunk * HD / 4 / kAttnThreads;  // float4 per thread per matrix
-    static_assert(kAttnChunk * HD % (4 * kAttnThreads) == 0, "whole float4 per thread");
+    constexpr int kV4 = kAttnChunk * HD / 4 / NT;  // float4 per thread per matrix
+    static_assert(kAttnChunk * HD % (4 * NT) == 0, "whole float4 per thread");
     float4 kr4[kV4], vr4[kV4];
 #pragma unroll
     for (int i = 0; i < kV4; ++i) {
-        const int e4 = tid + i * kAttnThreads, t = (4 * e4) / HD, d = (4 * e4) % HD, tok = t0 + t;
+        const int e4 = tid + i * NT, t = (4 * e4) / HD, d = (4 * e4) % HD, tok = t0 + t;
         const size_t slot = (size_t)tok * kvd + g * HD + d;
         if (t < tn && tok != pos) {
             kr4[i] = __ldg(reinterpret_cast<const float4 *>(kc + slot));
@@ -2236,29 +2413,29 @@ attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *
     }
 #pragma unroll
     for (int i = 0; i < kV4; ++i) {
-        const int e4 = tid + i * kAttnThreads, t = (4 * e4) / HD, d = (4 * e4) % HD, tok = t0 + t;
+        const int e4 = tid + i * NT, t = (4 * e4) / HD, d = (4 * e4) % HD, tok = t0 + t;
         if (t < tn && tok != pos) {
             ks[t][d] = kr4[i].x; ks[t][d + 1] = kr4[i].y; ks[t][d + 2] = kr4[i].z; ks[t][d + 3] = kr4[i].w;
             *reinterpret_cast<float4 *>(&vs[t][d]) = vr4[i];
         }
     }
     // q, k and v of this position come from the Q/K/V GEMV
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if constexpr (PDL) asm volatile("griddepcontrol.wait;" ::: "memory");
     __syncthreads();
-    for (int e = tid; e < G * HD; e += kAttnThreads) {
+    for (int e = tid; e < G * HD; e += NT) {
         const int hh = e / HD, d = e % HD, i = d % (HD / 2);
         const float *q = qkv + (g * G + hh) * HD;
-        const float x = q[i], y = q[i + HD / 2];
+        const float x = __ldcg(q + i), y = __ldcg(q + i + HD / 2);
         qs[hh][d] = d < HD / 2 ? x * cs[i] - y * sn[i] : x * sn[i] + y * cs[i];
     }
     if (pos >= t0 && pos < t0 + tn) {
         const int t = pos - t0;
-        for (int d = tid; d < HD; d += kAttnThreads) {
+        for (int d = tid; d < HD; d += NT) {
             const int i = d % (HD / 2);
             const float *k = qkv + dim + g * HD;
-            const float x = k[i], y = k[i + HD / 2];
+            const float x = __ldcg(k + i), y = __ldcg(k + i + HD / 2);
             const float kr = d < HD / 2 ? x * cs[i] - y * sn[i] : x * sn[i] + y * cs[i];
-            const float vv = qkv[dim + kvd + g * HD + d];
+            const float vv = __ldcg(qkv + dim + kvd + g * HD + d);
             const size_t slot = (size_t)pos * kvd + g * HD + d;
             kc[slot] = kr;
             vc[slot] = vv;
@@ -2268,7 +2445,7 @@ attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *
     }
     __syncthreads();
     const float rs = sqrtf((float)HD);
-    for (int e = tid; e < G * tn; e += kAttnThreads) {
+    for (int e = tid; e < G * tn; e += NT) {
         const int hh = e / tn, t = e % tn;
         float acc = 0.f;
 #pragma unroll 16
@@ -2277,7 +2454,7 @@ attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *
     }
     __syncthreads();
     float *pc = part + ((size_t)(g * ((max_ctx + kAttnChunk - 1) / kAttnChunk) + c) * G) * (HD + 2);
-    for (int hh = warp; hh < G; hh += kAttnThreads / 32) {
+    for (int hh = warp; hh < G; hh += NT / 32) {
         float m = -INFINITY;
         for (int t = lane; t < tn; t += 32) m = fmaxf(m, sc[hh][t]);
 #pragma unroll
@@ -2296,7 +2473,7 @@ attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *
         }
     }
     __syncthreads();
-    for (int e = tid; e < G * HD; e += kAttnThreads) {
+    for (int e = tid; e < G * HD; e += NT) {
         const int hh = e / HD, d = e % HD;
         float o = 0.f;
         for (int t = 0; t < tn; ++t) o += sc[hh][t] * vs[t][d];
@@ -2309,44 +2486,96 @@ attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *
     __syncthreads();
     if (!last) return;
     __threadfence();
-    // Merge: every chunk's (m, l) of every head in one parallel load, the
-    // weights e^(m_c - M) / sum_c e^(m_c - M) l_c once per (chunk, head), then
-    // the weighted output sums with independent loads.
+    // Merge: the weights e^(m_c - M) once per (chunk, head), the denominators
+    // sum_c e^(m_c - M) l_c, then the weighted output sums with independent
+    // loads.
     const float *pg = part + (size_t)g * ((max_ctx + kAttnChunk - 1) / kAttnChunk) * G * (HD + 2);
-    float *wgt = &sc[0][0];  // reuses the score tile: nchunk x G weights (nchunk <= kAttnMaxChunks)
-    __shared__ float mx[kAttnMaxGroup], den[kAttnMaxGroup];
-    for (int e = tid; e < nchunk * G; e += kAttnThreads) wgt[e] = pg[(size_t)e * (HD + 2)];
-    __syncthreads();
-    if (tid < G) {
-        float M = -INFINITY;
-        for (int k = 0; k < nchunk; ++k) M = fmaxf(M, wgt[k * G + tid]);
-        mx[tid] = M;
+    // The chunks are merged in tiles whose G weights each fit the score tile,
+    // so any context length merges (one tile up to kAttnMaxChunks / G chunks).
+    float *wgt = &sc[0][0];
+    auto &mx = sm.mx;
+    auto &den = sm.den;
+    const int tile = kAttnMaxChunks / G;
+    // pass 1: the maximum of every head's chunk maxima
+    if (tid < G) mx[tid] = -INFINITY;
+    for (int k0 = 0; k0 < nchunk; k0 += tile) {
+        const int nk = min(tile, nchunk - k0);
+        __syncthreads();
+        for (int e = tid; e < nk * G; e += NT) wgt[e] = __ldcg(pg + ((size_t)k0 * G + e) * (HD + 2));
+        __syncthreads();
+        if (tid < G) {
+            float M = mx[tid];
+            for (int k = 0; k < nk; ++k) M = fmaxf(M, wgt[k * G + tid]);
+            mx[tid] = M;
+        }
     }
-    __syncthreads();
-    for (int e = tid; e < nchunk * G; e += kAttnThreads) wgt[e] = expf(wgt[e] - mx[e % G]);
-    __syncthreads();
-    for (int hh = warp; hh < G; hh += kAttnThreads / 32) {
-        float l = 0.f;
-        for (int k = lane; k < nchunk; k += 32) l += wgt[k * G + hh] * pg[((size_t)k * G + hh) * (HD + 2) + 1];
+    // pass 2: weights e^(m_c - M), the denominators and the weighted sums
+    constexpr int kOut = (kAttnMaxGroup * HD + NT - 1) / NT;  // outputs per thread
+    float o[kOut];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(kFull, l, o);
-        if (lane == 0) den[hh] = l;
+    for (int j = 0; j < kOut; ++j) o[j] = 0.f;
+    if (tid < G) den[tid] = 0.f;
+    for (int k0 = 0; k0 < nchunk; k0 += tile) {
+        const int nk = min(tile, nchunk - k0);
+        __syncthreads();
+        for (int e = tid; e < nk * G; e += NT)
+            wgt[e] = expf(__ldcg(pg + ((size_t)k0 * G + e) * (HD + 2)) - mx[e % G]);
+        __syncthreads();
+        for (int hh = warp; hh < G; hh += NT / 32) {
+            float l = 0.f;
+            for (int k = lane; k < nk; k += 32)
+                l += wgt[k * G + hh] * __ldcg(pg + ((size_t)(k0 + k) * G + hh) * (HD + 2) + 1);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(kFull, l, off);
+            if (lane == 0) den[hh] += l;
+        }
+#pragma unroll
+        for (int j = 0; j < kOut; ++j) {
+            const int e = tid + j * NT;
+            if (e < G * HD) {
+                const int hh = e / HD, d = e % HD;
+#pragma unroll 8
+                for (int k = 0; k < nk; ++k)
+                    o[j] += wgt[k * G + hh] * __ldcg(pg + ((size_t)(k0 + k) * G + hh) * (HD + 2) + 2 + d);
+            }
+        }
     }
     __syncthreads();
-    for (int e = tid; e < G * HD; e += kAttnThreads) {
-        const int hh = e / HD, d = e % HD;
-        float o = 0.f;
-#pragma unroll 8
-        for (int k = 0; k < nchunk; ++k) o += wgt[k * G + hh] * pg[((size_t)k * G + hh) * (HD + 2) + 2 + d];
-        att[(g * G + hh) * HD + d] = o / den[hh];
+#pragma unroll
+    for (int j = 0; j < kOut; ++j) {
+        const int e = tid + j * NT;
+        if (e < G * HD) att[(g * G + e / HD) * HD + e % HD] = o[j] / den[e / HD];
     }
     if (tid == 0) counter[g] = 0u;
 }
 
+// Grid (kv head g, chunk c of kAttnChunk cached tokens): one work item per CTA.
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads)
+attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *__restrict__ kc,
+                 float *__restrict__ vc, int max_ctx, float rope_base, DecodeState *st, float *__restrict__ part,
+                 unsigned int *__restrict__ counter, float *__restrict__ att)
+{
+    __shared__ AttnShared<HD> sm;
+    const int g = blockIdx.x, c = blockIdx.y;
+    // The next launch (the output projection) may start streaming its
+    // weights; it reads att only after its own griddepcontrol.wait.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int pos = st->pos;  // written by the previous step's advance_kernel
+    if (pos < 0 || pos >= max_ctx) {
+        if (g == 0 && c == 0 && threadIdx.x == 0) atomicOr(&st->error, 2u);
+        return;
+    }
+    if (c >= (pos + kAttnChunk) / kAttnChunk) return;  // chunk beyond the position
+    attention_item<HD, true>(sm, g, c, qkv, heads, kv_heads, kc, vc, max_ctx, rope_base, st, part, counter, att);
+}
+
 // One thread: the step's greedy token (key of index_base 0) becomes the next
 // step's input; the position moves on.
-__global__ void advance_kernel(const unsigned long long *key, DecodeState *st, int *history, int max_steps)
+__global__ void advance_kernel(const unsigned long long *key, DecodeState *st, int *history, int max_steps,
+                               unsigned int *bar_count)
 {
+    if (bar_count != nullptr) *bar_count = 0u;  // re-arm the persistent step's grid barrier
     const unsigned long long k = *key;
     int tok = 0;
     if (k == 0ull || k == ~0ull)
@@ -2357,6 +2586,374 @@ __global__ void advance_kernel(const unsigned long long *key, DecodeState *st, i
     if (st->steps >= 0 && st->steps < max_steps) history[st->steps] = tok;
     st->steps += 1;
     st->pos += 1;
+}
+
+// ------------------------------------------- persistent decode layers
+//
+// The whole layer stack of one decode step in one cooperative launch: one CTA
+// per SM runs the embedding and, per layer, five phases separated by grid
+// barriers --
+//   1  [q; k; v] rows of this CTA, RMSNorm(attn_norm) prologue, biases
+//   2  attention work items (kv head, 64-token chunk), as attention_kernel
+//   3  o rows, residual (h += W_o att)
+//   4  [gate; up] rows, RMSNorm(ffn_norm) prologue
+//   5  down rows, SwiGLU prologue (up * silu(gate)), residual
+// -- instead of five launches whose boundaries each cost a drain, a launch and
+// a pipeline fill.  Every CTA owns a fixed row range of every matrix.  The
+// projections of the step form one sequence of units (q, k, v or [q; k; v],
+// o, gate and up or [gate; up], down, layer after layer); a CTA keeps its rows
+// of the next two units in flight into two shared-memory slots (bulk copies
+// completing on an mbarrier per slot), so a phase's weights are on chip
+// before its barrier opens.  (Bulk L2 prefetches of the layer after were
+// tried and dropped: issuing them stalled the issuing thread ~3 us a layer.)
+// Rows that do not fit a slot are read from global memory.  The current and
+// next layer's descriptors sit in shared memory.  Activations written in the
+// launch are read through L2 (ld.global.cg) in one pass: the RMSNorm prologue
+// quantizes x * norm and scales the row sums by 1 / sqrt(mean(x^2) + eps),
+// and a unit whose x has the slice layout of the previous unit of its phase
+// (gate then up, q then k then v) reuses it.  The x quantization and
+// block dots are the GEMV kernels'; a row's 32-chunk blocks may sit in
+// different warps and are summed in block order.  Barriers count arrivals
+// (the advance kernel re-arms the counter after each step) and are bounded:
+// one that does not complete within 2 s raises an abort flag that every
+// later barrier honours, sets error bit 8 of the decode state and ends the
+// launch.
+
+constexpr int kPsThreads = 512;
+constexpr int kPsParts = 4096;  // per-CTA partial sums of (row, 32-chunk block) items
+
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int *p)
+{
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(unsigned int *p, unsigned int v)
+{
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Grid barrier number k of the launch (k = 1, 2, ...): wait until k arrivals
+// per CTA have been counted.  false once any CTA's wait has expired.
+__device__ bool grid_sync(GridBar *b, unsigned int k, DecodeState *st)
+{
+    __shared__ int ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        ok = 1;
+        const unsigned int target = k * gridDim.x;
+        red_release_gpu_add(&b->count, 1u);
+        if (ld_acquire_gpu(&b->count) < target) {
+            const unsigned long long t0 = globaltimer();
+            for (uint32_t n = 1; ld_acquire_gpu(&b->count) < target; ++n) {
+                if ((n & 63u) != 0u) continue;
+                if (*(volatile unsigned int *)&b->abort) {
+                    ok = 0;
+                    break;
+                }
+                if (globaltimer() - t0 > kWaitLimitNs) {
+                    atomicExch(&b->abort, 1u);
+                    atomicOr(&st->error, 8u);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    return ok != 0;
+}
+
+__device__ __forceinline__ void cta_rows(int rows, int *r0, int *r1)
+{
+    *r0 = (int)((long long)rows * blockIdx.x / gridDim.x);
+    *r1 = (int)((long long)rows * (blockIdx.x + 1) / gridDim.x);
+}
+
+// The step's projections as one sequence of units: per layer q, k, v (or
+// [q; k; v]), o, gate, up (or [gate; up]), down.
+struct PsUnits {
+    const PLayer *ring;  // shared-memory copies of layers l (slot l & 1) and l + 1
+    __device__ int per_layer(int l) const { return ring[l & 1].n_qkv + ring[l & 1].n_gu + 2; }
+    // unit u of layer l (null past the layer)
+    __device__ const PGemv *at(int l, int u) const
+    {
+        const PLayer &ly = ring[l & 1];
+        if (u < ly.n_qkv) return &ly.qkv[u];
+        u -= ly.n_qkv;
+        if (u == 0) return &ly.o;
+        u -= 1;
+        if (u < ly.n_gu) return &ly.gu[u];
+        u -= ly.n_gu;
+        return u == 0 ? &ly.down : nullptr;
+    }
+};
+
+// Position of the unit that the slots load next (every thread keeps the same
+// copy; thread 0 issues).
+struct PsCursor {
+    int l = 0, u = 0, seq = 0;
+};
+
+__device__ __forceinline__ uint64_t unit_bytes(const PGemv &g)
+{
+    int r0, r1;
+    cta_rows(g.L.rows, &r0, &r1);
+    return (uint64_t)(r1 - r0) * g.L.row_stride;
+}
+
+// Start loading the unit at the cursor into slot seq & 1 and advance the
+// cursor.  The slot's mbarrier completes one phase per unit: with the bytes
+// of a bulk copy, or at once for a unit that does not fit (read from global).
+__device__ void ps_issue(const PStep &P, const PLayer *ring, PsCursor &cur, uint32_t slots, uint32_t slot_bytes,
+                         uint32_t bars)
+{
+    const PsUnits U{ring};
+    if (cur.l >= P.n_layers) return;
+    const PGemv &g = *U.at(cur.l, cur.u);
+    if (threadIdx.x == 0) {
+        const uint32_t bar = bars + 8u * (uint32_t)(cur.seq & 1);
+        const uint64_t bytes = unit_bytes(g);
+        if (bytes > 0 && bytes <= slot_bytes) {
+            int r0, r1;
+            cta_rows(g.L.rows, &r0, &r1);
+            const uint8_t *src = g.w + (uint64_t)r0 * g.L.row_stride;
+            const uint32_t dst = slots + (uint32_t)(cur.seq & 1) * slot_bytes;
+            mbar_expect_tx(bar, (uint32_t)bytes);
+            for (uint32_t off = 0; off < (uint32_t)bytes; off += 32768u)
+                bulk_g2s(dst + off, src + off, min(32768u, (uint32_t)bytes - off), bar);
+        } else {
+            mbar_arrive(bar);
+        }
+    }
+    cur.seq += 1;
+    if (++cur.u == U.per_layer(cur.l)) {
+        cur.u = 0;
+        cur.l += 1;
+    }
+}
+
+// This CTA's rows of y = W x' (+ add) for the unit of sequence number seq;
+// x and add may have been written earlier in the launch.
+// reuse: the quantized x in shared memory (and red[], which holds the sum of
+// squares) came from the previous unit of this phase, with the same x,
+// prologue and slice layout.
+template <uint32_t FMT>
+__device__ bool ps_gemv(const PGemv &g, int seq, uint32_t slots, uint32_t slot_bytes, uint32_t bars, const float *x,
+                        int pre, const float *aux, float eps, float *y, const float *add, uint8_t *smem, float *parts,
+                        float *red, GridBar *b, DecodeState *st, bool reuse)
+{
+    const Layout &L = g.L;
+    const int C = L.C, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr int NSL = W<FMT>::kSlices;
+    float scale = 1.f, ss = 0.f;
+    if (!reuse) {
+        quantize_x<FMT, kPsThreads, true>(x, L.cols, C, smem, 1, 0, pre == kPreRmsNorm ? kPreScale : pre, 1.f, aux,
+                                          nullptr, &ss);
+        if (pre == kPreRmsNorm) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
+            if (lane == 0) red[warp] = ss;
+        }
+        __syncthreads();
+    }
+    if (pre == kPreRmsNorm) {
+        ss = 0.f;
+        for (int i = 0; i < kPsThreads / 32; ++i) ss += red[i];
+        scale = 1.f / sqrtf(ss / (float)L.cols + eps);
+    }
+    const XS s = xs_view(smem, L.cols);
+    const uint64_t bytes = unit_bytes(g);
+    const bool in_smem = bytes > 0 && bytes <= slot_bytes;
+    const uint32_t slot = slots + (uint32_t)(seq & 1) * slot_bytes;
+    // every thread waits for the slot (its phase completes even when the
+    // unit is read from global memory)
+    if (!mbar_wait(bars + 8u * (uint32_t)(seq & 1), (uint32_t)((seq >> 1) & 1))) {
+        if (tid == 0) {
+            atomicExch(&b->abort, 1u);
+            atomicOr(&st->error, 8u);
+        }
+        return false;
+    }
+    int r0, r1;
+    cta_rows(L.rows, &r0, &r1);
+    const int NB = (C + 31) / 32;
+    const int RB = max(1, kPsParts / NB);
+    for (int rb = r0; rb < r1; rb += RB) {
+        const int nr = min(RB, r1 - rb), items = nr * NB;
+        for (int it = warp; it < items; it += kPsThreads / 32) {
+            const int r = it / NB, bk = it - r * NB, c = bk * 32 + lane;
+            float acc = 0.f;
+            if (c < C) {
+                W<FMT> wv;
+                if (in_smem)
+                    wv.load_smem(slot + (uint32_t)(rb + r - r0) * (uint32_t)L.row_stride, L, c);
+                else
+                    wv.load(g.w + (uint64_t)(rb + r) * L.row_stride, L, c);
+                const XR<NSL> xr = load_xr<NSL>(s, C, c);
+                acc = wv.dot(xr);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
+            if (lane == 0) parts[it] = acc;
+        }
+        __syncthreads();
+        for (int r = tid; r < nr; r += kPsThreads) {
+            float v = 0.f;
+            for (int bk = 0; bk < NB; ++bk) v += parts[r * NB + bk];
+            v *= scale;
+            const int row = rb + r;
+            if (add != nullptr) v += __ldcg(add + row);
+            y[row] = v;
+        }
+        __syncthreads();
+    }
+    // every thread is past the slot's wait before thread 0 re-arms the slot
+    __syncthreads();
+    return true;
+}
+
+__device__ bool ps_gemv_any(const PGemv &g, int seq, uint32_t slots, uint32_t slot_bytes, uint32_t bars,
+                            const float *x, int pre, const float *aux, float eps, float *y, const float *add,
+                            uint8_t *smem, float *parts, float *red, GridBar *b, DecodeState *st, bool reuse)
+{
+    switch (g.L.type) {
+    case kQ8_0:
+        return ps_gemv<kQ8_0>(g, seq, slots, slot_bytes, bars, x, pre, aux, eps, y, add, smem, parts, red, b, st, reuse);
+    case kQ5_0:
+        return ps_gemv<kQ5_0>(g, seq, slots, slot_bytes, bars, x, pre, aux, eps, y, add, smem, parts, red, b, st, reuse);
+    case kQ4_K:
+        return ps_gemv<kQ4_K>(g, seq, slots, slot_bytes, bars, x, pre, aux, eps, y, add, smem, parts, red, b, st, reuse);
+    default:
+        return ps_gemv<kQ6_K>(g, seq, slots, slot_bytes, bars, x, pre, aux, eps, y, add, smem, parts, red, b, st, reuse);
+    }
+}
+
+// Formats whose quantized x has the same slice layout (Q8_0 and Q5_0: 16-element
+// halves of 32-blocks; Q4_K; Q6_K).
+__device__ __forceinline__ int slice_family(uint32_t type) { return type == kQ5_0 ? (int)kQ8_0 : (int)type; }
+
+template <uint32_t FMT>
+__device__ void ps_embed(const PGemv &e, int tok, float *h)
+{
+    constexpr int BE = BlockShape<FMT>::E;
+    uint8_t raw[BlockShape<FMT>::B];
+    for (int bk = blockIdx.x * blockDim.x + threadIdx.x; bk < e.L.nb; bk += gridDim.x * blockDim.x) {
+        gather_raw_block(e.L, e.w + (uint64_t)tok * e.L.row_stride, bk, raw);
+        for (int i = 0; i < BE; ++i) h[bk * BE + i] = dequant_value<FMT>(raw, i);
+    }
+}
+
+// Dynamic shared memory: quantized x | partial sums | two weight slots.
+__host__ __device__ constexpr uint32_t ps_x_bytes(int dim, int hid)
+{
+    return (uint32_t)((xs_bytes(dim > hid ? dim : hid) + 127) / 128 * 128);
+}
+
+__global__ void __launch_bounds__(kPsThreads, 1) decode_layers_kernel(PStep P)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ AttnShared<64> attn;
+    __shared__ float red[kPsThreads / 32];
+    __shared__ __align__(8) unsigned long long slot_bars[2];
+    __shared__ __align__(16) PLayer ring[2];  // layers l (slot l & 1) and l + 1
+    float *parts = reinterpret_cast<float *>(smem + ps_x_bytes(P.dim, P.hid));
+    const uint32_t slots = (uint32_t)__cvta_generic_to_shared(smem + ps_x_bytes(P.dim, P.hid) + 4u * kPsParts);
+    const uint32_t bars = (uint32_t)__cvta_generic_to_shared(&slot_bars[0]);
+    const int pos = P.st->pos, tok = P.st->tok;
+    if (pos < 0 || pos >= P.max_ctx) {  // uniform over the grid: no barrier is reached
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(&P.st->error, 2u);
+        return;
+    }
+    // copy layer l's descriptor into ring slot l & 1 (all threads, then a barrier)
+    auto load_layer = [&](int l) {
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(P.layers + l);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(&ring[l & 1]);
+        for (int i = threadIdx.x; i < (int)(sizeof(PLayer) / 4); i += kPsThreads) dst[i] = src[i];
+    };
+    if (threadIdx.x == 0) {
+        mbar_init(bars, 1u);
+        mbar_init(bars + 8u, 1u);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    load_layer(0);
+    if (P.n_layers > 1) load_layer(1);
+    __syncthreads();
+    PsCursor cur;
+    ps_issue(P, ring, cur, slots, P.slot_bytes, bars);
+    ps_issue(P, ring, cur, slots, P.slot_bytes, bars);
+    // embedding row (bit-exact block dequant), spread over the grid
+    {
+        int t = tok;
+        if (t < 0 || t >= P.embd.L.rows) {
+            if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(&P.st->error, 1u);
+            t = 0;
+        }
+        switch (P.embd.L.type) {
+        case kQ8_0: ps_embed<kQ8_0>(P.embd, t, P.h); break;
+        case kQ5_0: ps_embed<kQ5_0>(P.embd, t, P.h); break;
+        case kQ4_K: ps_embed<kQ4_K>(P.embd, t, P.h); break;
+        default: ps_embed<kQ6_K>(P.embd, t, P.h); break;
+        }
+    }
+    unsigned int nbar = 0;
+    bool ok = grid_sync(P.bar, ++nbar, P.st);
+    const int hd = 64, dim = P.dim, kvd = P.kv_heads * hd;
+    const int nchunk = (pos + kAttnChunk) / kAttnChunk;
+    int seq = 0;  // sequence number of the next unit to compute
+    // one unit: compute from its slot, then reuse the slot for the unit two ahead
+    auto unit = [&](const PGemv &g, const float *x, int pre, const float *aux, float *y, const float *add,
+                    bool reuse) {
+        if (!ok) return;
+        ok = ps_gemv_any(g, seq, slots, P.slot_bytes, bars, x, pre, aux, P.eps, y, add, smem, parts, red, P.bar,
+                         P.st, reuse);
+        ++seq;
+        ps_issue(P, ring, cur, slots, P.slot_bytes, bars);
+    };
+    for (int l = 0; l < P.n_layers && ok; ++l) {
+        const PLayer &ly = ring[l & 1];
+        // 1: [q; k; v] with the RMSNorm prologue and the biases
+        if (ly.n_qkv == 1) {
+            unit(ly.qkv[0], P.h, kPreRmsNorm, ly.attn_norm, P.qkv, ly.bias_qkv, false);
+        } else {
+            const int f0 = slice_family(ly.qkv[0].L.type), f1 = slice_family(ly.qkv[1].L.type);
+            unit(ly.qkv[0], P.h, kPreRmsNorm, ly.attn_norm, P.qkv, ly.bias_qkv, false);
+            unit(ly.qkv[1], P.h, kPreRmsNorm, ly.attn_norm, P.qkv + dim, ly.bias_qkv + dim, f1 == f0);
+            unit(ly.qkv[2], P.h, kPreRmsNorm, ly.attn_norm, P.qkv + dim + kvd, ly.bias_qkv + dim + kvd,
+                 slice_family(ly.qkv[2].L.type) == f1);
+        }
+        ok = ok && grid_sync(P.bar, ++nbar, P.st);
+        if (!ok) break;
+        // 2: attention items; the last CTA of each kv head merges its chunks
+        for (int item = blockIdx.x; item < P.kv_heads * nchunk; item += gridDim.x)
+            attention_item<64, false, kPsThreads>(attn, item / nchunk, item % nchunk, P.qkv, P.heads, P.kv_heads,
+                                                  ly.kc, ly.vc, P.max_ctx, P.rope_base, P.st, P.part, P.attn_cnt,
+                                                  P.att);
+        ok = grid_sync(P.bar, ++nbar, P.st);
+        // 3: o, residual
+        unit(ly.o, P.att, kPreNone, nullptr, P.h, P.h, false);
+        ok = ok && grid_sync(P.bar, ++nbar, P.st);
+        // 4: [gate; up] with the RMSNorm prologue (one matrix: up lands after gate)
+        float *up = ly.n_gu == 1 ? P.gate + P.hid : P.up;
+        unit(ly.gu[0], P.h, kPreRmsNorm, ly.ffn_norm, P.gate, nullptr, false);
+        if (ly.n_gu == 2)
+            unit(ly.gu[1], P.h, kPreRmsNorm, ly.ffn_norm, up, nullptr,
+                 slice_family(ly.gu[1].L.type) == slice_family(ly.gu[0].L.type));
+        ok = ok && grid_sync(P.bar, ++nbar, P.st);
+        // 5: down with the SwiGLU prologue, residual; then the descriptor of
+        // layer l + 2 takes ring slot l & 1 (the issue cursor is past layer l)
+        if (l + 1 == P.n_layers) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+        unit(ly.down, P.gate, kPreSwiGlu, up, P.h, P.h, false);
+        if (l + 2 < P.n_layers) load_layer(l + 2);
+        if (l + 1 < P.n_layers) ok = ok && grid_sync(P.bar, ++nbar, P.st);
+    }
+    // Copies still in flight into the slots must land before the CTA exits
+    // (bounded waits: after an abort a slot may hold an issued unit).
+    while (seq < cur.seq) {
+        if (!mbar_wait(bars + 8u * (uint32_t)(seq & 1), (uint32_t)((seq >> 1) & 1))) break;
+        ++seq;
+    }
 }
 
 // ------------------------------------------------- Qwen2 prefill
@@ -2753,6 +3350,10 @@ __global__ void swiglu_rows_kernel(const float *__restrict__ gate, int g_ld, con
 
 // ------------------------------------------------------ launch helpers
 
+// The calling thread's own status word for the launches it makes (set around
+// the drop-in calls; null otherwise).
+thread_local unsigned int *t_call_status = nullptr;
+
 int sm_count()
 {
     static int count = 0;
@@ -2891,6 +3492,7 @@ bool tma_candidate(const Layout &L, const int *cand, int np, long long ctas, Tma
     P->rows_per_warp = r;
     P->np = np;
     P->split = split;
+    P->status = nullptr;
     return true;
 }
 
@@ -2943,6 +3545,8 @@ cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, con
                         const Fuse &fu = Fuse{})
 {
     auto kernel = gemv_tma_kernel<FMT, CW, R, NP, SPLIT, MINB>;
+    TmaPlan Pc = P;
+    Pc.status = t_call_status;
     const size_t smem = (size_t)P.x_bytes + (size_t)P.stages * P.stage_bytes;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -2963,7 +3567,7 @@ cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, con
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     const int want = am ? 1 : 0;
-    e = cudaLaunchKernelEx(&cfg, kernel, L, w, x, y, a, want, P, ex, fu);
+    e = cudaLaunchKernelEx(&cfg, kernel, L, w, x, y, a, want, Pc, ex, fu);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -3021,6 +3625,8 @@ cudaError_t gemv_pair_go(const GemvPair &pr, int grid, const float *x, const Fus
     if (e != cudaSuccess) return e;
     e = allow_max_smem((const void *)kernel, dev);
     if (e != cudaSuccess) return e;
+    GemvPair pc = pr;
+    pc.P[0].status = pc.P[1].status = t_call_status;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(17 * 32);
@@ -3031,7 +3637,7 @@ cudaError_t gemv_pair_go(const GemvPair &pr, int grid, const float *x, const Fus
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kernel, pr, x, fu);
+    e = cudaLaunchKernelEx(&cfg, kernel, pc, x, fu);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -3095,6 +3701,20 @@ cudaError_t scratch_pool(cudaMemPool_t *out)
     *out = pools[dev];
     return cudaSuccess;
 }
+
+}  // namespace
+
+cudaError_t stream_alloc(void **ptr, size_t bytes, cudaStream_t s)
+{
+    cudaMemPool_t pool;
+    const cudaError_t e = scratch_pool(&pool);
+    if (e != cudaSuccess) return e;
+    return cudaMallocFromPoolAsync(ptr, bytes, pool, s);
+}
+
+cudaError_t stream_free(void *ptr, cudaStream_t s) { return ptr ? cudaFreeAsync(ptr, s) : cudaSuccess; }
+
+namespace {
 
 template <uint32_t FMT, int TPT>
 cudaError_t matmul_go(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y,
@@ -3196,7 +3816,7 @@ cudaError_t matmul_tc_go(const Layout &L, const uint8_t *w, const XSource &X, in
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, kernel, L, w, X, (const uint8_t *)xs, batch, Y, S);
+        e = cudaLaunchKernelEx(&cfg, kernel, L, w, X, (const uint8_t *)xs, batch, Y, S, t_call_status);
     }
     const cudaError_t f = cudaFreeAsync(xs, s);
     return e != cudaSuccess ? e : f;
@@ -3522,8 +4142,7 @@ cudaError_t launch_attention(const float *qkv, int heads, int kv_heads, int head
                              float *att, cudaStream_t s)
 {
     if (head_dim != 64 || kv_heads <= 0 || heads % kv_heads != 0 || heads / kv_heads > kAttnMaxGroup ||
-        max_ctx <= 0 ||
-        (long long)((max_ctx + kAttnChunk - 1) / kAttnChunk) * (heads / kv_heads) > kAttnMaxChunks)
+        max_ctx <= 0)
         return cudaErrorInvalidValue;
     const dim3 grid((unsigned)kv_heads, (unsigned)((max_ctx + kAttnChunk - 1) / kAttnChunk));
     cudaLaunchConfig_t cfg{};
@@ -3540,9 +4159,9 @@ cudaError_t launch_attention(const float *qkv, int heads, int kv_heads, int head
 }
 
 cudaError_t launch_advance(const unsigned long long *key, DecodeState *st, int *history, int max_steps,
-                           cudaStream_t s)
+                           cudaStream_t s, unsigned int *bar_count)
 {
-    advance_kernel<<<1, 1, 0, s>>>(key, st, history, max_steps);
+    advance_kernel<<<1, 1, 0, s>>>(key, st, history, max_steps, bar_count);
     return cudaGetLastError();
 }
 
@@ -3744,6 +4363,7 @@ cudaError_t launch_matmul(const Layout &L, const uint8_t *w, const float *X, int
 }
 
 void set_gemv_path(int path) { g_gemv_path = path; }
+void set_call_status(unsigned int *word) { t_call_status = word; }
 void set_matmul_path(int path) { g_matmul_path = path; }
 
 size_t exchange_parity_bytes(int world, int slot_rows)
@@ -3785,6 +4405,61 @@ cudaError_t launch_argmax(const float *logits, int n, const ArgmaxOut &am, cudaS
     unsigned g = grid_for((uint64_t)n, kThreads * 4);
     if (g > (unsigned)kMaxArgmaxCtas) g = kMaxArgmaxCtas;
     argmax_kernel<<<g, kThreads, 0, s>>>(logits, n, am);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------- persistent decode step
+
+size_t decode_layers_smem(int dim, int hid, uint32_t slot_bytes)
+{
+    return (size_t)ps_x_bytes(dim, hid) + sizeof(float) * (size_t)kPsParts + 2u * (size_t)slot_bytes;
+}
+
+// Weight slot size: two slots in what the x area, the partial sums and the
+// static tiles leave of the opt-in shared memory, at most 64 KiB each, a
+// multiple of 128 bytes.
+uint32_t decode_layers_slot_bytes(int dim, int hid)
+{
+    int dev = 0, optin = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+        return 0;
+    cudaFuncAttributes attr;
+    if (cudaFuncGetAttributes(&attr, decode_layers_kernel) != cudaSuccess) return 0;
+    const long long left =
+        (long long)optin - (long long)attr.sharedSizeBytes - (long long)ps_x_bytes(dim, hid) - 4ll * kPsParts;
+    long long slot = left / 2;
+    if (slot > 64 * 1024) slot = 64 * 1024;
+    return slot > 0 ? (uint32_t)(slot / 128 * 128) : 0u;
+}
+
+cudaError_t launch_decode_layers(const PStep &P, cudaStream_t s)
+{
+    if (P.heads <= 0 || P.kv_heads <= 0 || P.heads % P.kv_heads != 0 || P.heads / P.kv_heads > kAttnMaxGroup ||
+        P.max_ctx <= 0 || P.dim != P.heads * 64)
+        return cudaErrorInvalidValue;
+    const size_t smem = decode_layers_smem(P.dim, P.hid, P.slot_bytes);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    e = allow_max_smem((const void *)decode_layers_kernel, dev);
+    if (e != cudaSuccess) return e;
+    int occ = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_layers_kernel, kPsThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (occ < 1) return cudaErrorCooperativeLaunchTooLarge;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)sm_count());  // one CTA per SM, all resident (cooperative)
+    cfg.blockDim = dim3(kPsThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, decode_layers_kernel, P);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

@@ -82,12 +82,21 @@ struct QmvQwen2 {
     unsigned int *pf_cnt = nullptr;
     cudaStream_t pf_side = nullptr;  // up projection beside gate (different formats)
     cudaEvent_t pf_fork = nullptr, pf_join = nullptr;
+    // persistent step (decode_layers_kernel): descriptors and grid barrier
+    bool persistent = false;
+    qmv::PStep ps{};
+    qmv::GridBar *bar = nullptr;
     std::vector<cudaEvent_t> prof_events;  // profiled steps (created on first use)
     std::vector<void *> allocs;
     std::vector<QmvWeight *> weights;
 };
 
 namespace {
+
+// 0: one launch per projection and attention; 1: the layer stack as one
+// persistent cooperative launch where the device allows it (process-wide,
+// read when a decoder is created).
+int g_decode_mode = 0;
 
 int dalloc(QmvQwen2 *m, void **p, size_t bytes, const char *what)
 {
@@ -190,10 +199,27 @@ cudaError_t mark(QmvQwen2 *m, Marks *mk, cudaError_t launched, const Mark &w)
 
 Mark layer_mark(const QmvWeight *w, int calls) { return Mark{kStageLayerGemv, {w->L.type, 0}, 1.0, {calls, 0}}; }
 
+// One decode step as three launches: the persistent layer stack, the output
+// projection with its fused greedy argmax, and the advance kernel.
+cudaError_t enqueue_step_persistent(QmvQwen2 *m)
+{
+    const QmvQwen2Config &c = m->cfg;
+    cudaError_t e = qmv::launch_decode_layers(m->ps, m->stream);
+    const qmv::ArgmaxOut am{m->key, m->am_ws, 0};
+    if (e == cudaSuccess)
+        e = gemv(m, m->out, m->h, m->logits,
+                 qmv::Fuse{qmv::kPreRmsNorm, m->out_norm, c.rms_norm_epsilon, nullptr, nullptr}, &am);
+    if (e == cudaSuccess)
+        e = qmv::launch_advance(m->key, m->st, m->history, c.max_context, m->stream, &m->bar->count);
+    return e;
+}
+
 // One decode step, enqueued on m->stream; mk != nullptr records the
-// profiling events of an un-captured step.
+// profiling events of an un-captured step (always one launch per projection,
+// so each stage has its own events).
 cudaError_t enqueue_step(QmvQwen2 *m, Marks *mk = nullptr)
 {
+    if (m->persistent && mk == nullptr) return enqueue_step_persistent(m);
     const QmvQwen2Config &c = m->cfg;
     const int dim = c.dim, kvd = m->kvd;
     cudaError_t e = mk ? record(m, mk) : cudaSuccess;
@@ -259,6 +285,7 @@ cudaError_t enqueue_step(QmvQwen2 *m, Marks *mk = nullptr)
 int set_token(QmvQwen2 *m, int token)
 {
     if (token < 0 || token >= m->cfg.vocab_size) return qmv::set_error("token id is out of range");
+    if (m->bar) QW_CUDA(cudaMemsetAsync(m->bar, 0, sizeof(qmv::GridBar), m->stream), "set token");
     const int tok_steps[2] = {token, 0};
     QW_CUDA(cudaMemcpyAsync(&m->st->tok, tok_steps, sizeof tok_steps, cudaMemcpyHostToDevice, m->stream),
             "set token");
@@ -274,6 +301,7 @@ int check_state(QmvQwen2 *m, qmv::DecodeState *out)
     if (s.error & 1u) return qmv::set_error("decode step: token id out of range");
     if (s.error & 2u) return qmv::set_error("decode step: context capacity is exhausted");
     if (s.error & 4u) return qmv::set_error("decode step: output contains a non-finite logit");
+    if (s.error & 8u) return qmv::set_error("decode step: a grid barrier of the persistent step expired");
     return 1;
 }
 
@@ -288,6 +316,76 @@ void release(QmvQwen2 *m)
     for (void *p : m->allocs) cudaFree(p);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
+}
+
+qmv::PGemv pg(const QmvWeight *w) { return w ? qmv::PGemv{w->L, w->dev} : qmv::PGemv{qmv::Layout{}, nullptr}; }
+
+// Descriptors of the persistent step (decode_layers_kernel) in device memory.
+int build_persistent(QmvQwen2 *m)
+{
+    const QmvQwen2Config &c = m->cfg;
+    std::vector<qmv::PLayer> host((size_t)c.n_layers);
+    const size_t kvd = (size_t)m->kvd;
+    for (int l = 0; l < c.n_layers; ++l) {
+        const Layer &L = m->layers[(size_t)l];
+        qmv::PLayer &p = host[(size_t)l];
+        p = qmv::PLayer{};
+        if (L.qkv) {
+            p.qkv[0] = pg(L.qkv);
+            p.n_qkv = 1;
+        } else {
+            p.qkv[0] = pg(L.q);
+            p.qkv[1] = pg(L.k);
+            p.qkv[2] = pg(L.v);
+            p.n_qkv = 3;
+        }
+        p.o = pg(L.o);
+        if (L.gate_up) {
+            p.gu[0] = pg(L.gate_up);
+            p.n_gu = 1;
+        } else {
+            p.gu[0] = pg(L.gate);
+            p.gu[1] = pg(L.up);
+            p.n_gu = 2;
+        }
+        p.down = pg(L.down);
+        p.attn_norm = L.attn_norm;
+        p.ffn_norm = L.ffn_norm;
+        p.bias_qkv = L.bias_qkv;
+        const size_t off = (size_t)l * (size_t)c.max_context * kvd;
+        p.kc = m->kc + off;
+        p.vc = m->vc + off;
+    }
+    qmv::PLayer *dev_layers = nullptr;
+    if (!dalloc(m, (void **)&dev_layers, host.size() * sizeof(qmv::PLayer), "persistent step") ||
+        !dalloc(m, (void **)&m->bar, sizeof(qmv::GridBar), "grid barrier"))
+        return 0;
+    QW_CUDA(cudaMemcpy(dev_layers, host.data(), host.size() * sizeof(qmv::PLayer), cudaMemcpyHostToDevice),
+            "persistent step");
+    qmv::PStep &P = m->ps;
+    P.slot_bytes = qmv::decode_layers_slot_bytes(c.dim, c.hidden_dim);
+    if (P.slot_bytes < 16u) return 1;  // no room for the weight slots: one launch per projection
+    P.layers = dev_layers;
+    P.n_layers = c.n_layers;
+    P.dim = c.dim;
+    P.hid = c.hidden_dim;
+    P.heads = c.n_heads;
+    P.kv_heads = c.n_kv_heads;
+    P.max_ctx = c.max_context;
+    P.eps = c.rms_norm_epsilon;
+    P.rope_base = c.rope_frequency_base;
+    P.embd = pg(m->embd);
+    P.h = m->h;
+    P.qkv = m->qkv;
+    P.att = m->att;
+    P.gate = m->gate;
+    P.up = m->up;
+    P.part = m->attn_part;
+    P.attn_cnt = m->attn_cnt;
+    P.st = m->st;
+    P.bar = m->bar;
+    m->persistent = true;
+    return 1;
 }
 
 int build(QmvQwen2 *m, const QmvQwen2Tensor *tensors, int count)
@@ -373,17 +471,35 @@ int build(QmvQwen2 *m, const QmvQwen2Tensor *tensors, int count)
         !dalloc(m, (void **)&m->history, (size_t)c.max_context * sizeof(int), "token history"))
         return 0;
     QW_CUDA(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "decoder stream");
+    if (g_decode_mode == 1 && m->head_dim == 64 && !build_persistent(m)) return 0;
     // One step outside capture sets every kernel's launch attributes, then the
-    // state and cache are cleared and the step is captured.
-    QW_CUDA(enqueue_step(m), "decode step");
+    // state and cache are cleared and the step is captured.  A persistent step
+    // the device refuses (its CTAs cannot all be resident) or that cannot be
+    // captured falls back to one launch per projection.
+    cudaError_t e0 = enqueue_step(m);
+    if (e0 != cudaSuccess && m->persistent) {
+        cudaGetLastError();
+        m->persistent = false;
+        e0 = enqueue_step(m);
+    }
+    QW_CUDA(e0, "decode step");
     QW_CUDA(cudaStreamSynchronize(m->stream), "decode step");
     QW_CUDA(cudaMemset(m->st, 0, sizeof(qmv::DecodeState)), "decode state");
     QW_CUDA(cudaMemset(m->kc, 0, cache), "key cache");
     QW_CUDA(cudaMemset(m->vc, 0, cache), "value cache");
     cudaGraph_t graph = nullptr;
     QW_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "graph capture");
-    const cudaError_t e = enqueue_step(m);
-    const cudaError_t e2 = cudaStreamEndCapture(m->stream, &graph);
+    cudaError_t e = enqueue_step(m);
+    cudaError_t e2 = cudaStreamEndCapture(m->stream, &graph);
+    if ((e != cudaSuccess || e2 != cudaSuccess) && m->persistent) {
+        if (graph) cudaGraphDestroy(graph);
+        graph = nullptr;
+        cudaGetLastError();
+        m->persistent = false;
+        QW_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "graph capture");
+        e = enqueue_step(m);
+        e2 = cudaStreamEndCapture(m->stream, &graph);
+    }
     if (e != cudaSuccess) {
         if (graph) cudaGraphDestroy(graph);
         return cuda_err("graph capture", e);
@@ -773,6 +889,13 @@ QMV_EXPORT int qmv_qwen2_get_kv(QmvQwen2 *m, int layer, int position, float *key
     const size_t off = ((size_t)layer * (size_t)m->cfg.max_context + (size_t)position) * (size_t)m->kvd;
     QW_CUDA(cudaMemcpy(key, m->kc + off, (size_t)m->kvd * sizeof(float), cudaMemcpyDeviceToHost), "read kv");
     QW_CUDA(cudaMemcpy(value, m->vc + off, (size_t)m->kvd * sizeof(float), cudaMemcpyDeviceToHost), "read kv");
+    return 1;
+}
+
+QMV_EXPORT int qmv_set_decode_mode(int mode)
+{
+    if (mode < 0 || mode > 1) return qmv::set_error("decode mode must be 0 or 1");
+    g_decode_mode = mode;
     return 1;
 }
 

@@ -171,6 +171,9 @@ QWEN2_CONFIGS = {
     # small shape of the same architecture for parity tests
     "qwen2_tiny": dict(dim=256, hidden=512, layers=2, heads=4, kv_heads=2, vocab=1000,
                        eps=1e-6, rope_base=1e6),
+    # configuration 4's head grouping (7 query heads per KV head), two layers
+    "qwen2_g7_small": dict(dim=896, hidden=1024, layers=2, heads=14, kv_heads=2, vocab=2000,
+                           eps=1e-6, rope_base=1e6),
 }
 
 QWEN2_TYPES = dict(q=Q8_0, k=Q8_0, v=Q8_0, o=Q8_0, gate=Q8_0, up=Q5_0, down=Q5_0, embd=Q8_0, out=Q6_K)

@@ -193,6 +193,47 @@ def test_dropin_host_entry_unaligned(cuda, qmv, oracle, gtype, cxx):
         assert tolerance_ok(Y[p], yp, 2 * s)[0].size == 0
 
 
+@pytest.mark.parametrize("gtype,rows,cols", [(Q8_0, 300, 896), (Q5_0, 300, 896), (Q4_K, 129, 3584),
+                                             (Q6_K, 129, 3584), (Q4_K, 64, 18944)])
+def test_matvec_nonfinite_and_tiny_x(cuda, qmv, oracle, workloads, gemv_path, gtype, rows, cols):
+    """x holding +Inf, -Inf or NaN, an all-tiny x (every magnitude below
+    2^-100) and one tiny block among normal ones.  The reference's float loops
+    (src/quantization.cpp:140-159, 319-349, 521-557, 721-756) give +-Inf where
+    one infinite x meets nonzero weights of one sign and NaN where it meets a
+    zero weight or both signs; the kernels must give the same class and sign
+    on every row, and finite rows must stay within the parity bound."""
+    torch = cuda
+    blocks = workloads.make_blocks(gtype, rows, cols, seed=31)
+    base = workloads.make_activations(cols, seed=31)
+    cases = []
+    for v in (np.inf, -np.inf, np.nan):
+        x = base.copy()
+        x[cols // 3] = v
+        cases.append(x)
+    cases.append((base * np.float32(2.0 ** -110)).astype(np.float32))
+    x = base.copy()
+    x[64:96] *= np.float32(2.0 ** -120)
+    cases.append(x)
+    w = qmv.Weight(gtype, blocks, rows, cols)
+    for x in cases:
+        xd = to_dev(torch, x)
+        yd = torch.full((rows,), 7.0, dtype=torch.float32, device="cuda")
+        w.matvec(xd.data_ptr(), yd.data_ptr())
+        torch.cuda.synchronize()
+        y = yd.cpu().numpy()
+        y_ref = oracle.matvec(gtype, blocks, rows, cols, x)
+        assert np.array_equal(np.isnan(y), np.isnan(y_ref))
+        assert np.array_equal(np.isposinf(y), np.isposinf(y_ref))
+        assert np.array_equal(np.isneginf(y), np.isneginf(y_ref))
+        fin = np.isfinite(y_ref)
+        if fin.any():
+            s = oracle.row_abs_dot(gtype, blocks, rows, cols, x)
+            bad, err, bound = tolerance_ok(y[fin], y_ref[fin], s[fin], REL_TOL)
+            assert bad.size == 0, (bad[:5], err[bad[:5]], bound[bad[:5]])
+    w.free()
+    assert qmv.device_status(clear=True) == 0
+
+
 # -------------------------------------------------------------- matmul
 
 @pytest.mark.parametrize("gtype,rows,cols", [(Q5_0, 4864, 896), (Q8_0, 300, 896), (Q4_K, 129, 3584),

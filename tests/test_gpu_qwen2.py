@@ -64,14 +64,36 @@ def _teacher_forced(qmv, oracle, wl, name, t0, max_ctx, steps, seed=0, first=7, 
     return worst
 
 
-def test_qwen2_decode_teacher_forced_small(cuda, qmv, oracle, workloads):
+@pytest.fixture(params=[0, 1], ids=["per-launch", "persistent"])
+def decode_mode(request, qmv):
+    """Decoders created inside the test run their step as one launch per
+    projection (mode 0) or as the persistent layer stack (mode 1)."""
+    qmv.set_decode_mode(request.param)
+    yield request.param
+    qmv.set_decode_mode(0)
+
+
+def test_qwen2_decode_teacher_forced_small(cuda, qmv, oracle, workloads, decode_mode):
     worst = _teacher_forced(qmv, oracle, workloads, "qwen2_tiny", t0=20, max_ctx=64, steps=6, seed=1)
     print("relative logit error, relative top-2 gap per step:", worst)
 
 
+def test_qwen2_decode_long_context(cuda, qmv, oracle, workloads, decode_mode):
+    """More attention work items than SMs (a 9500-position cache: 2 kv heads x
+    149 chunks), so CTAs of the persistent step take several items."""
+    _teacher_forced(qmv, oracle, workloads, "qwen2_tiny", t0=9500, max_ctx=9504, steps=2, seed=5)
+
+
+def test_qwen2_decode_merge_tiles(cuda, qmv, oracle, workloads, decode_mode):
+    """Configuration 4's grouping (7 query heads per KV head) over a
+    10,000-position cache: 157 chunks x 7 heads of merge weights exceed one
+    shared-memory tile, so the merge runs in two tiles (no context limit)."""
+    _teacher_forced(qmv, oracle, workloads, "qwen2_g7_small", t0=9995, max_ctx=10000, steps=2, seed=6)
+
+
 @pytest.mark.parametrize("gate,up", [("Q5_0", "Q5_0"), ("Q8_0", "Q8_0"), ("Q4_K", "Q6_K"),
                                      ("Q6_K", "Q8_0"), ("Q5_0", "Q4_K")])
-def test_qwen2_gate_up_formats(cuda, qmv, oracle, workloads, gate, up):
+def test_qwen2_gate_up_formats(cuda, qmv, oracle, workloads, gate, up, decode_mode):
     """Gate and up in one launch: concatenated rows when their formats match,
     one paired launch (SMs split by bytes) when they differ, in either order
     of the format codes."""
@@ -79,7 +101,7 @@ def test_qwen2_gate_up_formats(cuda, qmv, oracle, workloads, gate, up):
     _teacher_forced(qmv, oracle, workloads, "qwen2_tiny", t0=12, max_ctx=32, steps=3, seed=4, types=types)
 
 
-def test_qwen2_generate_equals_stepwise(cuda, qmv, workloads):
+def test_qwen2_generate_equals_stepwise(cuda, qmv, workloads, decode_mode):
     """Graph-replayed generation (token fed back on the device) produces the
     same ids as one step at a time through the host."""
     m = workloads.make_qwen2("qwen2_tiny", seed=2)
@@ -87,8 +109,9 @@ def test_qwen2_generate_equals_stepwise(cuda, qmv, workloads):
     dec = qmv.Qwen2Decoder(m, workloads.qwen2_tensor_list(m), 64)
     try:
         dec.set_kv(keys, vals)
-        # embedding, 5 per layer (gate and up share one launch), output, advance
-        assert dec.kernels_per_step == 1 + 5 * m["layers"] + 2
+        # persistent: layer stack, output, advance; per launch: embedding,
+        # 5 per layer (gate and up share one launch), output, advance
+        assert dec.kernels_per_step == (3 if decode_mode == 1 else 1 + 5 * m["layers"] + 2)
         gen = dec.generate(3, 12)
         dec.set_kv(keys, vals)
         tok, seq = 3, []
@@ -101,7 +124,7 @@ def test_qwen2_generate_equals_stepwise(cuda, qmv, workloads):
         dec.close()
 
 
-def test_qwen2_errors(cuda, qmv, workloads):
+def test_qwen2_errors(cuda, qmv, workloads, decode_mode):
     """A token outside the vocabulary and an exhausted context fail with a
     message (as the reference's forward_token), and the decoder stays usable."""
     m = workloads.make_qwen2("qwen2_tiny", seed=3)
@@ -121,7 +144,7 @@ def test_qwen2_errors(cuda, qmv, workloads):
         dec.close()
 
 
-def test_qwen2_config4_teacher_forced(cuda, qmv, oracle, workloads):
+def test_qwen2_config4_teacher_forced(cuda, qmv, oracle, workloads, decode_mode):
     """Configuration 4 at full size: 24 layers, 1024 cached positions,
     vocabulary 151936; three teacher-forced steps."""
     worst = _teacher_forced(qmv, oracle, workloads, "cfg4_qwen2_0_5b", t0=1024, max_ctx=1280, steps=3, seed=0)

@@ -75,7 +75,11 @@ def test_reference_step_call_counts(qmv, workloads):
 @pytest.mark.parametrize("types", [None, dict(gate="Q5_0"), dict(q="Q5_0", k="Q8_0", v="Q5_0")])
 def test_decode_profile_matches_reference_accounting(cuda, qmv, workloads, types):
     """Per-format call counts equal the reference's; time lands in the same
-    format slots; the profiled step computes what the plain step does."""
+    format slots; the profiled step computes what the plain step does: the
+    same token, and logits equal to within 1e-4 of max|logit| (the profiled
+    step runs one launch per projection; the plain step may run the
+    persistent layer stack, which adds a row's partial sums in another
+    order)."""
     types = {k: getattr(workloads, v) for k, v in (types or {}).items()}
     m = workloads.make_qwen2("qwen2_tiny", seed=1, types=types)
     t0, steps = 6, 3
@@ -94,7 +98,8 @@ def test_decode_profile_matches_reference_accounting(cuda, qmv, workloads, types
         prof.enabled = 1
         for i in range(steps):
             lg, nxt = dec.forward_profiled(tok, prof)
-            assert nxt == plain[i][1] and np.array_equal(lg, plain[i][0])
+            assert nxt == plain[i][1]
+            assert np.max(np.abs(lg - plain[i][0])) <= 1e-4 * np.max(np.abs(plain[i][0]))
             tok = nxt
     finally:
         dec.close()
