@@ -161,8 +161,9 @@ int qmv_matvec_argmax(const QmvWeight *weight, const float *x, int x_count, floa
  * src/sampler.cpp:14-36).  Each rank owns an exchange buffer of
  * qmv_exchange_bytes() allocated with qmv_ipc_alloc: a 256-byte control block
  * (the rank's device-side step counter) and two parity regions
- * (logits[world * slot_rows] f32 | keys[world] u64 | flags[world] u32).  The
- * ranks share their IPC handles and open each other's with qmv_ipc_open. */
+ * (logits[world * slot_rows] f32 | one argmax key and one flag per source
+ * CTA).  The ranks share their IPC handles and open each other's with
+ * qmv_ipc_open.  All ranks run the same GPU model. */
 
 /* Bytes of one rank's exchange buffer. */
 int qmv_exchange_bytes(int world, int slot_rows, size_t *bytes);
@@ -185,15 +186,17 @@ int qmv_memcpy(void *dst, const void *src, size_t bytes, void *stream);
 int qmv_exchange_logits(void *buffer, int world, int slot_rows, uint32_t epoch, float **logits);
 
 /* One kernel per rank: this rank's rows of W x (the weight must hold rows
- * [rank * slot_rows, ...)), its argmax key, stores of its logits and key into
- * every rank's buffer over NVLink, and a bounded wait for every peer's flag of
- * this step.  The step counter lives in the buffer (device side), so the
- * call can be captured in a CUDA graph and replayed.  On completion *key
- * (device) is the global argmax key on every rank and every rank's buffer
- * holds all logits of the step.  `buffers` is a host array of world device
- * pointers (own + opened peers).  Read a step's gathered logits on the same
- * stream before the call after next.  A peer that never arrives within 2 s
- * leaves key 0 (no token) and sets bit 3 of qmv_device_status. */
+ * [rank * slot_rows, ...)) and its argmax key.  Every CTA stores its logits
+ * and its key into every rank's buffer over NVLink and release-stores its
+ * flag there; the rank's last CTA waits (bounded) until every rank's CTAs of
+ * this step have delivered and folds their keys.  The step counter lives in the
+ * buffer (device side), so the call can be captured in a CUDA graph and
+ * replayed.  On completion *key (device) is the global argmax key on every
+ * rank and every rank's buffer holds all logits of the step.  `buffers` is a
+ * host array of world device pointers (own + opened peers).  Read a step's
+ * gathered logits on the same stream before the call after next.  A rank that
+ * never arrives within 2 s leaves key 0 (no token) and sets bit 3 of
+ * qmv_device_status. */
 int qmv_matvec_argmax_exchange(const QmvWeight *weight, const float *x, int x_count, int rank, int world,
                                void *const *buffers, int slot_rows, uint64_t *key, void *workspace,
                                void *stream);

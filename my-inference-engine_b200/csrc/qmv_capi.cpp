@@ -611,13 +611,13 @@ QMV_EXPORT int qmv_matvec_argmax_exchange(const QmvWeight *w, const float *x, in
     if (!aligned16(x)) return fail("x must be 16-byte aligned");
     const size_t pb = qmv::exchange_parity_bytes(world, slot_rows);
     const size_t keys_off = ((size_t)world * slot_rows * 4 + 255) & ~(size_t)255;
-    const size_t flags_off = keys_off + (((size_t)world * 8 + 255) & ~(size_t)255);
     qmv::Exchange ex{};
     ex.world = world;
     ex.rank = rank;
     ex.slot_rows = slot_rows;
     if (buffers[rank] == nullptr) return fail("buffer of rank %d is null", rank);
     ex.epoch = (unsigned int *)buffers[rank];
+    const size_t flags_off = keys_off + (size_t)world * qmv::kMaxExCtas * 8;
     for (int p = 0; p < world; ++p) {
         if (buffers[p] == nullptr) return fail("buffer of rank %d is null", p);
         for (int par = 0; par < 2; ++par) {

@@ -69,20 +69,24 @@ struct ArgmaxOut {
 // Row-sharded exchange over peer memory (one node, up to kMaxPeers GPUs).
 // Each rank's exchange buffer starts with a 256-byte control block whose
 // first word is the rank's step counter (epoch, device-side), followed by two
-// parity regions: logits[world * slot_rows] f32 | keys[world] u64 |
-// flags[world] u32.  A kernel runs epoch = counter + 1, uses parity region
-// epoch & 1 and stores the counter back when its exchange completed, so
-// repeated launches (including CUDA-graph replays) need no host epoch.
+// parity regions: logits[world * slot_rows] f32 | keys[world][kMaxExCtas] u64
+// | flags[world][kMaxExCtas] u32 (one key and one flag per source CTA).  A
+// kernel runs epoch = counter + 1, uses parity region epoch & 1 and stores
+// the counter back when its exchange completed, so repeated launches
+// (including CUDA-graph replays) need no host epoch.  Every rank launches
+// ncta = min(SMs, slot_rows) CTAs (the GPUs of a node are one model).
 constexpr int kMaxPeers = 8;
+constexpr int kMaxExCtas = 256;
 constexpr size_t kExchangeHeader = 256;
 struct Exchange {
     int world;  // <= 1: no exchange
     int rank;
     int slot_rows;
+    int ncta;             // CTAs per rank (set by the launcher)
     unsigned int *epoch;  // this rank's counter
     float *logits[2][kMaxPeers];
-    unsigned long long *keys[2][kMaxPeers];
-    unsigned int *flags[2][kMaxPeers];
+    unsigned long long *keys[2][kMaxPeers];  // rank p's keys: [source rank][CTA]
+    unsigned int *flags[2][kMaxPeers];       // rank p's flags: [source rank][CTA], = epoch when delivered
 };
 size_t exchange_parity_bytes(int world, int slot_rows);
 

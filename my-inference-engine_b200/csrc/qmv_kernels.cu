@@ -141,10 +141,7 @@ __device__ unsigned long long block_max_key(unsigned long long k, unsigned long 
 
 // Publish this CTA's key; the last CTA to arrive folds all of them into
 // *am.key and re-arms the counter.  No CTA waits on another.
-__device__ void exchange_finish(const Exchange &ex, unsigned long long rank_key, unsigned long long *out_key);
-
-__device__ void finish_argmax(unsigned long long cta_key, const ArgmaxOut &am,
-                              unsigned long long *scratch, const Exchange *ex = nullptr)
+__device__ void finish_argmax(unsigned long long cta_key, const ArgmaxOut &am, unsigned long long *scratch)
 {
     unsigned int *counter = reinterpret_cast<unsigned int *>(am.workspace);
     unsigned long long *keys =
@@ -163,16 +160,6 @@ __device__ void finish_argmax(unsigned long long cta_key, const ArgmaxOut &am,
     for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x)
         k = max_ull(k, __ldcg(keys + i));
     k = block_max_key(k, scratch);
-    if (ex != nullptr && ex->world > 1) {
-        __shared__ unsigned long long rank_key;
-        if (threadIdx.x == 0) {
-            rank_key = k;
-            *counter = 0u;
-        }
-        __syncthreads();
-        exchange_finish(*ex, rank_key, am.key);
-        return;
-    }
     if (threadIdx.x == 0) {
         *am.key = k;
         *counter = 0u;
@@ -183,25 +170,27 @@ __device__ void finish_argmax(unsigned long long cta_key, const ArgmaxOut &am,
 //
 // Row-sharded projection across the GPUs of one node.  Every CTA copies the
 // logits of its own contiguous rows into each peer's slot for this rank
-// (coalesced NVLink stores) and fences at system scope before it counts
-// itself done.  The last CTA of the rank then stores the rank's argmax key
-// into every peer, publishes the step's epoch in every peer's flag for this
-// rank with a release store, waits (bounded) until all peers' flags for this
-// rank carry the epoch, and folds the keys.  After the kernel every rank holds
-// all logits and the same global key.
+// (coalesced NVLink stores), writes its argmax key into every rank's key
+// table, fences at system scope and release-stores the epoch into its own
+// flag in every rank's buffer (plain stores and loads over NVLink, no remote
+// atomics).  No CTA waits for the others of its rank before signalling.  The
+// rank's last CTA to finish (a local counter) waits until every source CTA's
+// flag of every rank shows this epoch, folds the world * ncta keys and
+// advances the epoch.  After the kernel every rank holds all logits and the
+// same global key.
 
 __device__ unsigned int g_peer_status;
-
-__device__ __forceinline__ void st_release_sys(unsigned int *p, unsigned int v)
-{
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
 __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int *p)
 {
     unsigned int v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned int *p, unsigned int v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long globaltimer_ns()
@@ -218,57 +207,60 @@ __device__ __forceinline__ unsigned int exchange_epoch(const Exchange &ex)
     return *((volatile unsigned int *)ex.epoch) + 1u;
 }
 
-// Copy rows [r0, r1) of this rank's slot to every peer (all threads of the CTA).
-__device__ void exchange_rows(const Exchange &ex, int par, const float *y_local, int r0, int r1)
+// This CTA's part of the exchange (all threads): its rows [r0, r1) of this
+// rank's slot to every peer, its key into every rank's table, then the
+// release of its flag.  cta_key is valid in thread 0.
+__device__ void exchange_send(const Exchange &ex, int par, unsigned int epoch, const float *y_local, int r0, int r1,
+                              unsigned long long cta_key)
 {
     for (int p = 0; p < ex.world; ++p) {
         if (p == ex.rank) continue;
         float *dst = ex.logits[par][p] + (size_t)ex.rank * ex.slot_rows;
         for (int i = r0 + (int)threadIdx.x; i < r1; i += blockDim.x) dst[i] = y_local[i];
     }
-    // One system-scope fence per CTA: the barrier orders every thread's peer
-    // stores before thread 0's fence, which orders them before the CTA's
-    // arrival on the counter (and so before the rank's release flag).
-    __syncthreads();
-    if (threadIdx.x == 0) __threadfence_system();
-}
-
-// Last CTA of the rank: publish key + flag, wait for all peers, fold keys,
-// advance the rank's epoch counter.
-__device__ void exchange_finish(const Exchange &ex, unsigned long long rank_key, unsigned long long *out_key)
-{
-    __shared__ int ok;
-    const unsigned int epoch = exchange_epoch(ex);
-    const int par = (int)(epoch & 1u);
-    if (threadIdx.x == 0) ok = 1;
-    __syncthreads();
-    const int p = threadIdx.x;
-    if (p < ex.world) ex.keys[par][p][ex.rank] = rank_key;
-    __threadfence_system();
-    __syncthreads();
-    if (p < ex.world) st_release_sys(ex.flags[par][p] + ex.rank, epoch);
-    if (p < ex.world) {
-        const unsigned int *flag = ex.flags[par][ex.rank] + p;
-        if (ld_acquire_sys(flag) != epoch) {
-            const unsigned long long t0 = globaltimer_ns();
-            for (uint32_t n = 1;; ++n) {
-                if (ld_acquire_sys(flag) == epoch) break;
-                if ((n & 63u) == 0u && globaltimer_ns() - t0 > 2000000000ull) {
-                    atomicOr(&g_peer_status, 1u);
-                    ok = 0;
-                    break;
-                }
-            }
-        }
-    }
+    if (threadIdx.x == 0)
+        for (int p = 0; p < ex.world; ++p) ex.keys[par][p][ex.rank * kMaxExCtas + blockIdx.x] = cta_key;
+    // The barrier orders every thread's peer stores before thread 0's
+    // system-scope fence and the release of the flags.
     __syncthreads();
     if (threadIdx.x == 0) {
-        unsigned long long k = 0ull;
-        if (ok) {
-            for (int q = 0; q < ex.world; ++q)
-                k = max_ull(k, ((volatile unsigned long long *)ex.keys[par][ex.rank])[q]);
+        __threadfence_system();
+        for (int p = 0; p < ex.world; ++p) st_release_sys(ex.flags[par][p] + ex.rank * kMaxExCtas + blockIdx.x, epoch);
+    }
+}
+
+// The rank's last CTA: wait (bounded) for every rank's CTAs of this epoch,
+// fold all keys, advance the epoch.  A CTA whose flag never arrives leaves
+// key 0 (no token) and sets g_peer_status.
+__device__ void exchange_collect(const Exchange &ex, int par, unsigned int epoch, unsigned long long *out_key,
+                                 unsigned long long *scratch)
+{
+    __shared__ int ok;
+    if (threadIdx.x == 0) ok = 1;
+    __syncthreads();
+    const unsigned int *flags = ex.flags[par][ex.rank];
+    const unsigned long long t0 = globaltimer_ns();
+    for (int e = threadIdx.x; e < ex.world * ex.ncta; e += blockDim.x) {
+        const unsigned int *f = flags + (e / ex.ncta) * kMaxExCtas + e % ex.ncta;
+        for (uint32_t n = 1; ld_acquire_sys(f) != epoch; ++n) {
+            if ((n & 63u) == 0u && globaltimer_ns() - t0 > 2000000000ull) {
+                atomicOr(&g_peer_status, 1u);
+                ok = 0;
+                break;
+            }
         }
-        *out_key = k;  // 0 decodes as "no token" when a peer never arrived
+        if (!*(volatile int *)&ok) break;
+    }
+    __syncthreads();
+    unsigned long long k = 0ull;
+    if (ok) {
+        const unsigned long long *keys = ex.keys[par][ex.rank];
+        for (int e = threadIdx.x; e < ex.world * ex.ncta; e += blockDim.x)
+            k = max_ull(k, __ldcg(keys + (e / ex.ncta) * kMaxExCtas + e % ex.ncta));
+    }
+    k = block_max_key(k, scratch);
+    if (threadIdx.x == 0) {
+        *out_key = ok ? k : 0ull;  // 0 decodes as "no token"
         *ex.epoch = epoch;
     }
 }
@@ -576,6 +568,29 @@ template <> struct W<kQ5_0> {
     __device__ __forceinline__ float dot(const XR<2> &x) const { return dot_u(unpack(), x); }
 };
 
+// Unsigned bytes of a times signed bytes of b, summed into c.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c)
+{
+    int r;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+__device__ __forceinline__ int dot4_us(const uint4 &w, const uint4 &x, int acc)
+{
+    acc = dp4a_us(w.x, x.x, acc);
+    acc = dp4a_us(w.y, x.y, acc);
+    acc = dp4a_us(w.z, x.z, acc);
+    return dp4a_us(w.w, x.w, acc);
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel)
+{
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
 template <> struct W<kQ4_K> {
     static constexpr int kSlices = 4;
     uint4 a, b, hdr;
@@ -595,64 +610,63 @@ template <> struct W<kQ4_K> {
         hdr = lds128(row + L.off_a + ((c >> 2) << 4));
         g = c & 3;
     }
+    // Weights of sub-block 2g (low nibbles, la/lb) and of sub-block 2g+1
+    // (high nibbles left in place, ua/ub: 16 times the value, which the
+    // unsigned-by-signed dp4a sums exactly; s1 carries the 1/16).
     struct U {
         uint4 la, lb, ua, ub;
-        float s0, m0, s1, m1;  // d * sc and dmin * m of sub-blocks 2g and 2g+1
+        float s0, m0, s1, m1;  // d * sc and dmin * m of sub-blocks 2g and 2g+1 (s1 over 16)
     };
     __device__ __forceinline__ U unpack() const
     {
-        // slices 0/1: low nibbles of pieces a/b (sub-block 2g);
-        // slices 2/3: high nibbles (sub-block 2g+1)
         U u;
         u.la = make_uint4(a.x & 0x0f0f0f0fu, a.y & 0x0f0f0f0fu, a.z & 0x0f0f0f0fu, a.w & 0x0f0f0f0fu);
         u.lb = make_uint4(b.x & 0x0f0f0f0fu, b.y & 0x0f0f0f0fu, b.z & 0x0f0f0f0fu, b.w & 0x0f0f0f0fu);
-        u.ua = make_uint4((a.x >> 4) & 0x0f0f0f0fu, (a.y >> 4) & 0x0f0f0f0fu, (a.z >> 4) & 0x0f0f0f0fu,
-                          (a.w >> 4) & 0x0f0f0f0fu);
-        u.ub = make_uint4((b.x >> 4) & 0x0f0f0f0fu, (b.y >> 4) & 0x0f0f0f0fu, (b.z >> 4) & 0x0f0f0f0fu,
-                          (b.w >> 4) & 0x0f0f0f0fu);
-        // 6-bit scale / min of sub-blocks 2g and 2g+1 (src/quantization.cpp:351-378),
-        // computed without a branch: lanes of one warp hold different g.
-        // Sub-block j < 4: sc = b[j] & 63, m = b[j+4] & 63.  j >= 4:
-        // sc = (b[j+4] & 15) | (b[j-4] >> 6) << 4, m = (b[j+4] >> 4) | (b[j] >> 6) << 4.
-        const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
-        const int t0 = 16 * (g & 1), t1 = t0 + 8;  // byte offset of j and j+1 within a word
-        const uint32_t lo_s = g < 2 ? s0 : s2;     // word holding the low bits of sc
-        const uint32_t lo_m = g < 2 ? s1 : (s2 >> 4);
-        const uint32_t lmask = g < 2 ? 63u : 15u;
-        const uint32_t hs = g < 2 ? 0u : s0, hm = g < 2 ? 0u : s1;  // top-2-bit sources
-        const uint32_t sc0 = ((lo_s >> t0) & lmask) | ((((hs >> t0) >> 6) & 3u) << 4);
-        const uint32_t m0 = ((lo_m >> t0) & lmask) | ((((hm >> t0) >> 6) & 3u) << 4);
-        const uint32_t sc1 = ((lo_s >> t1) & lmask) | ((((hs >> t1) >> 6) & 3u) << 4);
-        const uint32_t m1 = ((lo_m >> t1) & lmask) | ((((hm >> t1) >> 6) & 3u) << 4);
+        u.ua = make_uint4(a.x & 0xf0f0f0f0u, a.y & 0xf0f0f0f0u, a.z & 0xf0f0f0f0u, a.w & 0xf0f0f0f0u);
+        u.ub = make_uint4(b.x & 0xf0f0f0f0u, b.y & 0xf0f0f0f0u, b.z & 0xf0f0f0f0u, b.w & 0xf0f0f0f0u);
+        // 6-bit scale / min of sub-blocks j = 2g, 2g+1 from the 12 bytes
+        // b[0..11] = hdr.y, hdr.z, hdr.w (src/quantization.cpp:351-378).
+        // j < 4: sc = b[j] & 63, m = b[j+4] & 63.  j >= 4: sc = (b[j+4] & 15) |
+        // (b[j-4] >> 6) << 4, m = (b[j+4] >> 4) | (b[j] >> 6) << 4.  With
+        // h = g & 1, P gathers bytes (y[2h], y[2h+1], z[2h], z[2h+1]) and Q
+        // (w[2h], w[2h+1], w[2h], w[2h+1]); the result's bytes are
+        // (sc_2g, sc_2g+1, m_2g, m_2g+1).  The selectors and masks depend only
+        // on the lane's g.
+        const bool lo = g < 2;
+        const uint32_t P = prmt(hdr.y, hdr.z, (g & 1) ? 0x7632u : 0x5410u);
+        const uint32_t Q = prmt(hdr.w, hdr.w, (g & 1) ? 0x3232u : 0x1010u);
+        const uint32_t v = (P & (lo ? 0x3f3f3f3fu : 0u)) | ((P >> 2) & (lo ? 0u : 0x30303030u)) |
+                           (Q & (lo ? 0u : 0x00000f0fu)) | ((Q >> 4) & (lo ? 0u : 0x0f0f0000u));
         const float d = f16_fast(hdr.x), dmin = f16_fast(hdr.x >> 16);
-        u.s0 = d * (float)sc0;
-        u.m0 = dmin * (float)m0;
-        u.s1 = d * (float)sc1;
-        u.m1 = dmin * (float)m1;
+        u.s0 = d * (float)(v & 0xffu);
+        u.s1 = (d * (float)((v >> 8) & 0xffu)) * 0.0625f;
+        u.m0 = dmin * (float)((v >> 16) & 0xffu);
+        u.m1 = dmin * (float)(v >> 24);
         return u;
     }
     static __device__ __forceinline__ float dot_u(const U &u, const XR<4> &x)
     {
-        const int ah0 = dot4(u.lb, x.h[1], dot4(u.la, x.h[0], 0));
-        const int al0 = dot4(u.lb, x.l[1], dot4(u.la, x.l[0], 0));
-        const int ah1 = dot4(u.ub, x.h[3], dot4(u.ua, x.h[2], 0));
-        const int al1 = dot4(u.ub, x.l[3], dot4(u.ua, x.l[2], 0));
+        const int ah0 = dot4_us(u.lb, x.h[1], dot4_us(u.la, x.h[0], 0));
+        const int al0 = dot4_us(u.lb, x.l[1], dot4_us(u.la, x.l[0], 0));
+        const int ah1 = dot4_us(u.ub, x.h[3], dot4_us(u.ua, x.h[2], 0));
+        const int al1 = dot4_us(u.ub, x.l[3], dot4_us(u.ua, x.l[2], 0));
         const float v0 = u.s0 * (x.r[0].x * (float)(ah0 * 256 + al0)) - u.m0 * (x.r[0].y + x.r[1].y);
         const float v1 = u.s1 * (x.r[2].x * (float)(ah1 * 256 + al1)) - u.m1 * (x.r[2].y + x.r[3].y);
         return v0 + v1;
     }
+    __device__ __forceinline__ float dot(const XR<4> &x) const { return dot_u(unpack(), x); }
     // weights 64c.. of chunk c (sub-blocks 2g, 2g+1): d sc q - dmin m
     template <typename XF>
     static __device__ __forceinline__ float dot_f32(const U &u, int c, const XF &xv)
     {
+        const float s1 = u.s1 * 16.f;  // the high-nibble bytes hold 16 q
         const auto f0 = [&](uint32_t q) { return u.s0 * (float)q - u.m0; };
-        const auto f1 = [&](uint32_t q) { return u.s1 * (float)q - u.m1; };
+        const auto f1 = [&](uint32_t q) { return s1 * (float)(q >> 4) - u.m1; };
         float acc = dot16_f32(u.la, 64 * c, f0, xv, 0.f);
         acc = dot16_f32(u.lb, 64 * c + 16, f0, xv, acc);
         acc = dot16_f32(u.ua, 64 * c + 32, f1, xv, acc);
         return dot16_f32(u.ub, 64 * c + 48, f1, xv, acc);
     }
-    __device__ __forceinline__ float dot(const XR<4> &x) const { return dot_u(unpack(), x); }
 };
 
 // Signed byte B of v as an int, in one byte-permute (sign-replicating
@@ -1291,13 +1305,28 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
         }
     }
     if (ex.world > 1) {
-        __syncthreads();  // this CTA's rows of y are written
-        const int par = (int)(exchange_epoch(ex) & 1u);
-        exchange_rows(ex, par, ex.logits[par][ex.rank] + (size_t)ex.rank * ex.slot_rows, r0, r1);
+        // this CTA's rows of y are written (block_max_key synchronizes first)
+        best = block_max_key(best, sh.kscratch);
+        const unsigned int epoch = exchange_epoch(ex);
+        const int par = (int)(epoch & 1u);
+        exchange_send(ex, par, epoch, ex.logits[par][ex.rank] + (size_t)ex.rank * ex.slot_rows, r0, r1, best);
+        // the rank's last CTA collects
+        __shared__ int is_last;
+        unsigned int *counter = reinterpret_cast<unsigned int *>(am.workspace);
+        if (threadIdx.x == 0) {
+            __threadfence();
+            is_last = atomicAdd(counter, 1u) == gridDim.x - 1u;
+        }
+        __syncthreads();
+        if (!is_last) return;
+        __threadfence();
+        if (threadIdx.x == 0) *counter = 0u;
+        exchange_collect(ex, par, epoch, am.key, sh.kscratch);
+        return;
     }
     if (want_argmax) {
         best = block_max_key(best, sh.kscratch);
-        finish_argmax(best, am, sh.kscratch, &ex);
+        finish_argmax(best, am, sh.kscratch);
     }
 }
 
@@ -3554,7 +3583,13 @@ cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, con
     e = allow_max_smem((const void *)kernel, dev);
     if (e != cudaSuccess) return e;
     long long grid = sm_count();
-    if (grid > L.rows) grid = L.rows;
+    // the exchange: every rank launches the same number of CTAs (min(SMs,
+    // slot rows)); ranks with fewer rows have CTAs without rows
+    const long long rows_for_grid = ex.world > 1 ? ex.slot_rows : L.rows;
+    if (grid > rows_for_grid) grid = rows_for_grid;
+    if (ex.world > 1 && grid > kMaxExCtas) grid = kMaxExCtas;
+    Exchange exc = ex;
+    exc.ncta = (int)grid;
     ArgmaxOut a = am ? *am : ArgmaxOut{nullptr, nullptr, 0};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
@@ -3567,7 +3602,7 @@ cudaError_t gemv_tma_go(const Layout &L, const TmaPlan &P, const uint8_t *w, con
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     const int want = am ? 1 : 0;
-    e = cudaLaunchKernelEx(&cfg, kernel, L, w, x, y, a, want, Pc, ex, fu);
+    e = cudaLaunchKernelEx(&cfg, kernel, L, w, x, y, a, want, Pc, exc, fu);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -4369,9 +4404,7 @@ void set_matmul_path(int path) { g_matmul_path = path; }
 size_t exchange_parity_bytes(int world, int slot_rows)
 {
     const size_t logits = ((size_t)world * slot_rows * 4 + 255) & ~(size_t)255;
-    const size_t keys = ((size_t)world * 8 + 255) & ~(size_t)255;
-    const size_t flags = ((size_t)world * 4 + 255) & ~(size_t)255;
-    return logits + keys + flags;
+    return logits + (size_t)world * kMaxExCtas * (8 + 4);
 }
 
 cudaError_t launch_gemv_exchange(const Layout &L, const uint8_t *w, const float *x, float *y,

@@ -115,7 +115,7 @@ def test_dequant_reference_known_blocks(cuda, qmv, oracle):
     (Q5_0, 1, 32), (Q5_0, 17, 96), (Q5_0, 300, 896), (Q5_0, 77, 3584),
     (Q4_K, 1, 256), (Q4_K, 17, 768), (Q4_K, 301, 3584), (Q4_K, 64, 18944),
     (Q6_K, 1, 256), (Q6_K, 17, 768), (Q6_K, 301, 3584), (Q6_K, 33, 18944),
-    (Q8_0, 5, 65536),
+    (Q8_0, 5, 65536), (Q8_0, 200, 16384), (Q5_0, 150, 16384 + 96),
 ])
 def test_matvec_shapes(cuda, qmv, oracle, workloads, gemv_path, gtype, rows, cols):
     blocks = workloads.make_blocks(gtype, rows, cols, seed=rows + cols)
