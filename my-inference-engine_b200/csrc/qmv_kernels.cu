@@ -1077,7 +1077,12 @@ struct TmaPlan {
 // stage parity (bounded waits, like every other wait here).
 // The statically sized shared state of one GEMV CTA.
 struct TmaShared {
-    unsigned long long bars[2 * 8 + 4];  // full[8] | empty[8] | pfull[2] | pfree[2]
+    // full: per stage and row slot (the R rows of one consumer warp, or of a
+    // warp pair in the split-row plan), so a warp starts as soon as its own
+    // rows have landed; empty: per stage; pbar: pfull[2] | pfree[2]
+    unsigned long long full[8][kMaxConsumerWarps];
+    unsigned long long empty[8];
+    unsigned long long pbar[4];
     unsigned long long kscratch[kMaxConsumerWarps + 1];
     float partial[2][kMaxConsumerWarps];
     float sumsq[kMaxConsumerWarps];
@@ -1104,9 +1109,12 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
     const int C = L.C;
     const int NS = P.stages;
     const uint32_t stage0 = (uint32_t)__cvta_generic_to_shared(smem + P.x_bytes);
-    const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(&sh.bars[0]);
-    const uint32_t empty0 = full0 + 8u * 8u;
-    const uint32_t pbar0 = full0 + 16u * 8u;
+    const uint32_t full0 = (uint32_t)__cvta_generic_to_shared(&sh.full[0][0]);
+    const uint32_t empty0 = (uint32_t)__cvta_generic_to_shared(&sh.empty[0]);
+    const uint32_t pbar0 = (uint32_t)__cvta_generic_to_shared(&sh.pbar[0]);
+    constexpr int NSLOT = CW / SPLIT;  // row slots per stage, R rows each
+    // the full barrier of stage sidx, row slot j
+    auto full = [&](int sidx, int j) { return full0 + 8u * (uint32_t)(sidx * kMaxConsumerWarps + j); };
 
     const int r0 = (int)((long long)L.rows * cta / ncta);
     const int r1 = (int)((long long)L.rows * (cta + 1) / ncta);
@@ -1120,7 +1128,7 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NS; ++i) {
-            mbar_init(full0 + 8u * i, 1u);
+            for (int j = 0; j < NSLOT; ++j) mbar_init(full(i, j), 1u);
             mbar_init(empty0 + 8u * i, (uint32_t)kConsumerWarps);
         }
         for (int i = 0; i < 4; ++i) mbar_init(pbar0 + 8u * i, (uint32_t)(kConsumerWarps / 2));
@@ -1131,36 +1139,42 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
 
     unsigned long long best = 0ull;
     if (warp == kConsumerWarps) {
-        // ---------------- producer
-        if (lane == 0) {
-            int issued = 0;
-            bool ok = true;
-            for (int k = 0; k < n_stages; ++k) {
-                const int sidx = k % NS;
-                if (k >= NS && !mbar_wait(empty0 + 8u * sidx, (uint32_t)((k / NS - 1) & 1))) {
-                    report_status(P.status, kStatusProducerTimeout);
+        // ---------------- producer: lane j copies row slot j of each stage
+        int issued = 0;
+        bool ok = true;
+        for (int k = 0; k < n_stages; ++k) {
+            const int sidx = k % NS;
+            if (k >= NS) {
+                const bool freed = mbar_wait(empty0 + 8u * sidx, (uint32_t)((k / NS - 1) & 1));
+                if (!__all_sync(kFull, freed)) {
+                    if (lane == 0) report_status(P.status, kStatusProducerTimeout);
                     ok = false;
                     break;
                 }
-                const int rows_k = min(SR, r1 - (r0 + k * SR));
-                const uint32_t bytes = (uint32_t)rows_k * (uint32_t)L.row_stride;
-                const uint32_t bar = full0 + 8u * sidx;
-                mbar_expect_tx(bar, bytes);
-                const uint8_t *src = w + (uint64_t)(r0 + k * SR) * L.row_stride;
-                const uint32_t dst = stage0 + (uint32_t)sidx * P.stage_bytes;
-                for (uint32_t off = 0; off < bytes; off += 32768u) {
-                    const uint32_t n = min(32768u, bytes - off);
-                    bulk_g2s(dst + off, src + off, n, bar);
-                }
-                ++issued;
             }
-            if (!ok) {
-                // drain: every issued copy must land before the CTA exits
-                for (int k = max(0, issued - NS); k < issued; ++k) {
-                    if (!mbar_wait(full0 + 8u * (k % NS), (uint32_t)((k / NS) & 1))) {
-                        report_status(P.status, kStatusDrainTimeout);
-                        break;
-                    }
+            if (lane < NSLOT) {
+                const int rows_k = min(SR, r1 - (r0 + k * SR));
+                const int lr = lane * R, nr = min(R, rows_k - lr);
+                const uint32_t bar = full(sidx, lane);
+                if (nr > 0) {
+                    const uint32_t bytes = (uint32_t)nr * (uint32_t)L.row_stride;
+                    mbar_expect_tx(bar, bytes);
+                    const uint8_t *src = w + (uint64_t)(r0 + k * SR + lr) * L.row_stride;
+                    const uint32_t dst = stage0 + (uint32_t)sidx * P.stage_bytes + (uint32_t)lr * (uint32_t)L.row_stride;
+                    for (uint32_t off = 0; off < bytes; off += 32768u)
+                        bulk_g2s(dst + off, src + off, min(32768u, bytes - off), bar);
+                } else {
+                    mbar_arrive(bar);  // a slot past the last row: its phase completes at once
+                }
+            }
+            ++issued;
+        }
+        if (!ok && lane < NSLOT) {
+            // drain: every issued copy must land before the CTA exits
+            for (int k = max(0, issued - NS); k < issued; ++k) {
+                if (!mbar_wait(full(k % NS, lane), (uint32_t)((k / NS) & 1))) {
+                    report_status(P.status, kStatusDrainTimeout);
+                    break;
                 }
             }
         }
@@ -1198,7 +1212,7 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
             // special x: consume the stages (the producer must finish), then
             // this CTA's rows in fp32 from global memory
             for (int k = 0; k < n_stages; ++k) {
-                if (!mbar_wait(full0 + 8u * (k % NS), (uint32_t)((k / NS) & 1))) {
+                if (!mbar_wait(full(k % NS, rw), (uint32_t)((k / NS) & 1))) {
                     report_status(P.status, kStatusConsumerTimeout);
                     break;
                 }
@@ -1210,7 +1224,7 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
         } else
         for (int k = 0; k < n_stages; ++k) {
             const int sidx = k % NS;
-            if (!mbar_wait(full0 + 8u * sidx, (uint32_t)((k / NS) & 1))) {
+            if (!mbar_wait(full(sidx, rw), (uint32_t)((k / NS) & 1))) {
                 report_status(P.status, kStatusConsumerTimeout);
                 break;
             }
@@ -3491,10 +3505,10 @@ int g_gemv_path = 0;
 // better than 8.  batched: the plan of the batched kernel (np positions of
 // x in shared memory, 8 consumer warps).  false when none fits (the
 // direct-load kernels run).
-constexpr uint32_t kTmaBudget = 227u * 1024u - 1024u;  // dynamic bytes, leaving static room
+constexpr uint32_t kTmaBudget = 227u * 1024u - 2048u;  // dynamic bytes, leaving room for the static ~1.6 KB
 // Two CTAs per SM: each takes at most half of the SM's 228 KiB, less its
-// static shared memory and the 1 KiB the system reserves per CTA.
-constexpr uint32_t kTmaBudgetShared = 112u * 1024u;
+// static shared memory (~1.6 KB) and the 1 KiB the system reserves per CTA.
+constexpr uint32_t kTmaBudgetShared = 111u * 1024u;
 
 // One candidate {consumer warps, rows per warp, minimum stages, warps per
 // row} for a matrix whose rows spread over ctas CTAs; false when its stages
