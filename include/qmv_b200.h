@@ -52,15 +52,19 @@ int qmv_set_device(int device);
  * wait completed.  clear != 0 resets the word.  No counterpart in the reference (its kernels never wait). */
 int qmv_device_status(uint32_t *flags, int clear);
 
-/* GEMV kernel selection for the calling process: 0 = automatic (TMA bulk-copy
- * pipeline with the exclusive plan when its shared-memory stages fit, direct
- * loads otherwise),
+/* GEMV kernel selection for the calling process: 0 = automatic (the
+ * resident-row-range kernel when one CTA's rows fit in its shared memory
+ * whole -- a small CTA, so the CTAs of the next launches of a stream are
+ * resident beside it and copy their weights while it computes -- else the
+ * TMA bulk-copy pipeline with the exclusive plan when its shared-memory
+ * stages fit, direct loads otherwise),
  * 1 = direct loads, 2 = TMA pipeline only (shapes it cannot stage fail),
  * 3 = the exclusive TMA plan (one CTA per SM using all of its shared
  * memory; direct loads where no stages fit), 4 = the shared TMA plan where
  * its stages fit in half an SM (a CTA that leaves half of the SM to the next
- * launch, so consecutive launches overlap), else as 0.  No counterpart in
- * the reference; every path computes the same function. */
+ * launch, so consecutive launches overlap), else as 3, 5 = the
+ * resident-row-range kernel only (shapes it cannot hold fail).  No
+ * counterpart in the reference; every path computes the same function. */
 int qmv_set_gemv_path(int path);
 
 /* Batched-matmul kernel selection for the calling process: 0 = automatic
@@ -327,6 +331,15 @@ int qmv_qwen2_kernels_per_step(const QmvQwen2 *decoder);
  * resident.  Same results within the parity bound (mode 1 adds a row's
  * partial sums in another order).  No counterpart in the reference. */
 int qmv_set_decode_mode(int mode);
+/* Decode attention kernel for steps captured afterwards in this process
+ * (one launch per layer, decode mode 0): 0 (default) = one cluster of 16
+ * CTAs per KV head, each CTA a range of the cached positions, the ranges'
+ * softmax partials merged in the leader CTA's shared memory (groups of up to
+ * 8 query heads, where the device places 16-CTA clusters; else as 1);
+ * 1 = KV head x 64-position chunks merged through global memory by the last
+ * CTA of each head.  Same function within the parity bound.  No counterpart
+ * in the reference. */
+int qmv_set_attention_path(int path);
 
 /* The reference's per-request operation profile, field for field
  * (OperationProfile, include/metrics.h:6-25; per-format arrays indexed

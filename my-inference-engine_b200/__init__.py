@@ -50,6 +50,7 @@ C_SYMBOLS = [
     "qmv_quantized_tensor_matvec_f32", "qmv_quantized_tensor_matmul_f32",
     "qmv_qwen2_create", "qmv_qwen2_set_kv", "qmv_qwen2_forward", "qmv_qwen2_generate", "qmv_qwen2_begin",
     "qmv_qwen2_replay", "qmv_qwen2_read", "qmv_qwen2_get_kv", "qmv_qwen2_kernels_per_step", "qmv_set_decode_mode",
+    "qmv_set_attention_path",
     "qmv_qwen2_destroy", "qmv_gguf_open", "qmv_gguf_open_file", "qmv_gguf_close", "qmv_gguf_info",
     "qmv_gguf_tensor", "qmv_gguf_find_tensor", "qmv_gguf_get_uint", "qmv_gguf_get_float", "qmv_gguf_get_string",
     "qmv_gguf_get_array_info", "qmv_gguf_quantized_view", "qmv_gguf_upload", "qmv_qwen2_create_from_gguf",
@@ -175,6 +176,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "qmv_device_status": (I, [ctypes.POINTER(U32), I]),
         "qmv_set_gemv_path": (I, [I]),
         "qmv_set_decode_mode": (I, [I]),
+        "qmv_set_attention_path": (I, [I]),
         "qmv_set_matmul_path": (I, [I]),
         "qmv_weight_upload": (I, [VP, I, I, ctypes.POINTER(P)]),
         "qmv_weight_free": (I, [P]),
@@ -374,6 +376,12 @@ def set_decode_mode(mode: int):
     """0 (default): one launch per projection; 1: persistent layer stack
     (3 launches per token).  Read when a decoder is created."""
     _check(lib().qmv_set_decode_mode(mode), "qmv_set_decode_mode")
+
+
+def set_attention_path(path: int):
+    """0 (default): decode attention on one 16-CTA cluster per KV head;
+    1: the chunked kernel.  Read when a decode step is captured."""
+    _check(lib().qmv_set_attention_path(path), "qmv_set_attention_path")
 
 
 def set_gemv_path(path: int):

@@ -333,7 +333,7 @@ QMV_EXPORT int qmv_device_status(uint32_t *flags, int clear)
 
 QMV_EXPORT int qmv_set_gemv_path(int path)
 {
-    if (path < 0 || path > 4) return fail("gemv path must be 0, 1, 2, 3 or 4");
+    if (path < 0 || path > 5) return fail("gemv path must be 0, 1, 2, 3, 4 or 5");
     qmv::set_gemv_path(path);
     return 1;
 }

@@ -174,7 +174,8 @@ struct DecodeState {
     int pos;             // position the next step writes
     int tok;             // token of the next step
     int steps;           // tokens produced so far (index into the history)
-    unsigned int error;  // 1 token out of range, 2 context full, 4 no finite logit, 8 barrier expired
+    unsigned int error;  // 1 token out of range, 2 context full, 4 no finite logit, 8 barrier expired,
+                         // 16 the attention cluster's wait for its partials expired
 };
 // h = row st->tok of the resident embedding matrix (bit-exact dequant).
 cudaError_t launch_embed(const Layout &L, const uint8_t *w, DecodeState *st, float *h, cudaStream_t s);
@@ -186,6 +187,11 @@ size_t attention_workspace_floats(int heads, int kv_heads, int head_dim, int max
 cudaError_t launch_attention(const float *qkv, int heads, int kv_heads, int head_dim, float *kc, float *vc,
                              int max_ctx, float rope_base, DecodeState *st, float *part, unsigned int *counter,
                              float *att, cudaStream_t s);
+// Decode attention kernel: 0 automatic (one 16-CTA cluster per KV head,
+// merged in distributed shared memory, where the group has at most 8 query
+// heads and the device places such clusters), 1 the chunked kernel (KV head
+// x 64-position chunks, merged by the last CTA through global memory).
+void set_attention_path(int path);
 // The layer stack of one decode step as one cooperative launch (one CTA per
 // SM, grid barriers between the phases of each layer): embedding, then per
 // layer [q; k; v] (RMSNorm prologue, biases), attention, o (residual),

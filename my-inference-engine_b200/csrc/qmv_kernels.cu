@@ -1388,6 +1388,201 @@ gemv_pair_kernel(GemvPair pr, const float *__restrict__ x, Fuse fu)
                                               x, pr.y[1], none, 0, pr.P[1], solo, fu);
 }
 
+// ---------------------------------------------- GEMV (resident row range)
+//
+// Small matrices (the decode step's projections, configuration 0): every CTA
+// owns a contiguous row range small enough to sit in shared memory whole
+// (of one matrix, or of two matrices that share x -- the decode step's gate
+// and up of different formats).  Thread 0 issues the bulk copies of all of
+// the CTA's rows on one mbarrier before griddepcontrol.wait.  Exactly two
+// such CTAs fit on an SM (each reserves at least kLiteSmemFloor bytes), one
+// per SM per launch: under programmatic dependent launch the CTA of the next
+// launch of a stream is resident beside the current one and copies its
+// weights while the current one computes, so a chain of launches costs about
+// one activation hand-off per launch instead of a pipeline fill, and no SM
+// ever holds two CTAs of one launch.
+constexpr int kLiteWarps = 8;
+constexpr uint32_t kLiteRowBudget = 72u * 1024u;   // one CTA's rows of both matrices
+constexpr uint32_t kLiteXBudget = 16u * 1024u;     // quantized x (up to 6,553 columns)
+constexpr uint32_t kLiteSmemFloor = 77u * 1024u;   // three CTAs never fit in an SM's 228 KB
+
+struct LiteMat {
+    Layout L;
+    const uint8_t *w;
+    float *y;
+    const float *add;  // y[row] = (W x)[row] + add[row] when non-null (may alias y)
+    uint32_t soff;     // offset of the CTA's rows in the dynamic shared memory
+};
+struct LitePlan {
+    LiteMat m[2];
+    int nmat;              // 1 or 2 (two: equal columns and x slice layout)
+    uint32_t x_bytes;      // quantized x, rounded to 128
+    uint32_t smem;         // dynamic shared memory of a CTA
+    unsigned int *status;  // the calling thread's status word, or null
+};
+
+__device__ __forceinline__ void lite_rows_of(int rows, int *r0, int *r1)
+{
+    *r0 = (int)((long long)rows * blockIdx.x / gridDim.x);
+    *r1 = (int)((long long)rows * (blockIdx.x + 1) / gridDim.x);
+}
+
+// This CTA's rows of one matrix from its shared-memory copy at srow, times
+// scale (the RMSNorm prologue's 1 / sqrt(mean(x^2) + eps), else 1), plus the
+// epilogue's add.  Row groups of R go to the warps round robin, starting at
+// warp `first` (the second matrix of a pair starts where the first one's
+// last group went, so their tails land on different warps); lanes stride over
+// chunks.
+template <uint32_t FMT, int R>
+__device__ __forceinline__ unsigned long long lite_rows(const LiteMat &M, uint32_t srow, const XS &s, float scale,
+                                                        int first, bool want_key, int index_base)
+{
+    constexpr int NSL = W<FMT>::kSlices;
+    const Layout &L = M.L;
+    const int lane = threadIdx.x & 31, C = L.C;
+    const int warp = ((threadIdx.x >> 5) + kLiteWarps - first) % kLiteWarps;
+    int r0, r1;
+    lite_rows_of(L.rows, &r0, &r1);
+    const int nr = r1 - r0;
+    unsigned long long best = 0ull;
+    for (int lr0 = warp * R; lr0 < nr; lr0 += kLiteWarps * R) {
+        float acc[R];
+#pragma unroll
+        for (int i = 0; i < R; ++i) acc[i] = 0.f;
+        for (int c = lane; c < C; c += 32) {
+            W<FMT> wv[R];
+#pragma unroll
+            for (int i = 0; i < R; ++i)  // rows past the range re-read the last row (in bounds, never written)
+                wv[i].load_smem(srow + (uint32_t)min(lr0 + i, nr - 1) * (uint32_t)L.row_stride, L, c);
+            const XR<NSL> xr = load_xr<NSL>(s, C, c);
+#pragma unroll
+            for (int i = 0; i < R; ++i) acc[i] += wv[i].dot(xr);
+        }
+        float out = 0.f;
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(kFull, acc[i], o);
+            if (lane == i) out = acc[i];
+        }
+        if (lane < R && lr0 + lane < nr) {
+            const int row = r0 + lr0 + lane;
+            out *= scale;
+            if (M.add != nullptr) out += __ldcg(M.add + row);
+            M.y[row] = out;
+            if (want_key) best = max_ull(best, make_key(out, index_base + row));
+        }
+    }
+    return best;
+}
+
+// Warp that takes the row group after matrix M's last one.
+__device__ __forceinline__ int lite_next_warp(const LiteMat &M, int R)
+{
+    int r0, r1;
+    lite_rows_of(M.L.rows, &r0, &r1);
+    return ((r1 - r0 + R - 1) / R) % kLiteWarps;
+}
+
+template <uint32_t FA, uint32_t FB, int R>
+__global__ void __launch_bounds__(kLiteWarps * 32, 2)
+gemv_lite_kernel(LitePlan P, const float *__restrict__ x, ArgmaxOut am, int want_argmax, Fuse fu)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) unsigned long long bar;
+    __shared__ float sumsq[kLiteWarps];
+    __shared__ unsigned long long kscratch[kLiteWarps + 1];
+    __shared__ int special;
+    constexpr int NT = kLiteWarps * 32;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t bar_a = (uint32_t)__cvta_generic_to_shared(&bar);
+    const uint32_t rows_a = (uint32_t)__cvta_generic_to_shared(smem + P.x_bytes);
+    // The next launch of the stream may start now: it only copies its own
+    // weights until its griddepcontrol.wait.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (tid == 0) {
+        mbar_init(bar_a, 1u);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        special = 0;
+        uint32_t total = 0;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            if (i >= P.nmat) break;
+            int r0, r1;
+            lite_rows_of(P.m[i].L.rows, &r0, &r1);
+            total += (uint32_t)(r1 - r0) * (uint32_t)P.m[i].L.row_stride;
+        }
+        mbar_expect_tx(bar_a, total);  // with no bytes the arrival alone completes the phase
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            if (i >= P.nmat) break;
+            int r0, r1;
+            lite_rows_of(P.m[i].L.rows, &r0, &r1);
+            const uint32_t bytes = (uint32_t)(r1 - r0) * (uint32_t)P.m[i].L.row_stride;
+            const uint8_t *src = P.m[i].w + (uint64_t)r0 * P.m[i].L.row_stride;
+            for (uint32_t off = 0; off < bytes; off += 32768u)
+                bulk_g2s(rows_a + P.m[i].soff + off, src + off, min(32768u, bytes - off), bar_a);
+        }
+    }
+    // x (and add) may be written by the previous launch: read through L2
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const Layout &L0 = P.m[0].L;
+    // One pass over x: the RMSNorm prologue quantizes x * norm and scales the
+    // row sums by 1 / sqrt(mean(x^2) + eps), whose sum of squares is gathered
+    // in the same pass.
+    const int pre = fu.pre == kPreRmsNorm ? kPreScale : fu.pre;
+    const float *aux = fu.pre == kPreRmsNorm ? fu.norm : fu.up;
+    float ss = 0.f;
+    quantize_x<FA, NT, true>(x, L0.cols, L0.C, smem, 1, 0, pre, 1.f, aux, &special, &ss);
+    if (fu.pre == kPreRmsNorm) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
+        if (lane == 0) sumsq[warp] = ss;
+    }
+    __syncthreads();
+    float denom = 1.f, scale = 1.f;
+    if (fu.pre == kPreRmsNorm) {
+        ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < kLiteWarps; ++i) ss += sumsq[i];
+        denom = sqrtf(ss / (float)L0.cols + fu.eps);
+        scale = 1.f / denom;
+    }
+    // every thread waits for the rows (bounded); the phase completes once
+    bool landed = mbar_wait(bar_a, 0u);
+    if (!__syncthreads_and(landed)) {
+        if (tid == 0) {
+            report_status(P.status, kStatusConsumerTimeout);
+            // copies still in flight must land before the CTA exits
+            if (!landed && !mbar_wait(bar_a, 0u)) report_status(P.status, kStatusDrainTimeout);
+        }
+        return;
+    }
+    unsigned long long best = 0ull;
+    const bool key = want_argmax != 0 && P.nmat == 1;
+    if (*(volatile int *)&special != 0) {
+        // x holds a NaN/Inf or tiny block: these rows in fp32 from global memory
+        const XVal xv{x, fu.pre, denom, aux};
+        int r0, r1;
+        lite_rows_of(P.m[0].L.rows, &r0, &r1);
+        best = fp32_rows<FA>(P.m[0].L, P.m[0].w, r0, r1, warp, kLiteWarps, xv, P.m[0].y, P.m[0].add, key,
+                             am.index_base);
+        if constexpr (FB != 0) {
+            lite_rows_of(P.m[1].L.rows, &r0, &r1);
+            fp32_rows<FB>(P.m[1].L, P.m[1].w, r0, r1, warp, kLiteWarps, xv, P.m[1].y, P.m[1].add, false, 0);
+        }
+    } else {
+        const XS s = xs_view(smem, L0.cols);
+        best = lite_rows<FA, R>(P.m[0], rows_a + P.m[0].soff, s, scale, 0, key, am.index_base);
+        if constexpr (FB != 0)
+            lite_rows<FB, R>(P.m[1], rows_a + P.m[1].soff, s, scale, lite_next_warp(P.m[0], R), false, 0);
+    }
+    if (key) {
+        best = block_max_key(best, kscratch);
+        finish_argmax(best, am, kscratch);
+    }
+}
+
 // ------------------------------------------------------------- matmul
 //
 // Batched form for up to NP positions per launch (the reference's chunk of
@@ -2613,6 +2808,276 @@ attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *
     attention_item<HD, true>(sm, g, c, qkv, heads, kv_heads, kc, vc, max_ctx, rope_base, st, part, counter, att);
 }
 
+// ------------------------------------- decode attention on a CTA cluster
+//
+// One cluster of kDaSplit CTAs per KV head.  CTA r of the cluster owns the
+// positions [r*T/S, (r+1)*T/S) of the T = pos + 1 positions and every query
+// head of the group (G <= 8): it stages its cached keys and values in shared
+// memory with 16-byte cp.async copies before griddepcontrol.wait (they do not
+// depend on this layer's projections, so the copies overlap the Q/K/V GEMV),
+// then rotates the group's queries, computes its scores, softmax and weighted
+// value sums over tiles of kDaTile positions (online softmax across tiles:
+// running maximum m, sum of exponentials l, weighted sum o), and sends
+// {m, l, o[64]} per head to the leader CTA with asynchronous remote stores
+// (st.async into the leader's shared memory, completing on the leader's
+// mbarrier).  The leader merges the S partials per head as
+// sum_r e^(m_r - M) o_r / sum_r e^(m_r - M) l_r -- the softmax and weighted
+// sum of transformer_attention_f32 (src/transformer_ops.cpp:68-153)
+// evaluated over position ranges.  The CTA whose range ends at pos rotates
+// this position's key, appends key and value to the cache, and patches them
+// into its staged tile.  The only cluster barrier (it orders the leader's
+// mbarrier initialisation before the remote stores) is arrived at before
+// griddepcontrol.wait, so it is off the critical path; the leader's wait is
+// bounded (2 s, then decode-state error bit 16).
+constexpr int kDaSplit = 16;
+constexpr int kDaTile = 128;       // positions per staged tile
+constexpr int kDaThreads = 256;    // 8 warps: warp h runs head h's softmax and weighted sums
+constexpr int kDaMaxGroup = 8;
+constexpr int kDaKStride = 68;     // floats per staged key row: conflict-free 128-bit reads
+constexpr int kDaPart = 68;        // floats per received partial: m, l, 2 pad, o[64] (16-byte aligned o)
+constexpr uint32_t kDaKBytes = kDaTile * kDaKStride * 4;
+constexpr uint32_t kDaVBytes = kDaTile * 64 * 4;
+constexpr uint32_t kDaPartBytes = kDaSplit * kDaMaxGroup * kDaPart * 4;
+constexpr uint32_t kDaSmem =
+    kDaKBytes + kDaVBytes + kDaMaxGroup * 64 * 4 + kDaMaxGroup * kDaTile * 4 + 2 * 64 * 4 + kDaPartBytes;
+
+__device__ __forceinline__ void da_cp16(uint32_t dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// Stage keys/values of positions [a, b) (b - a <= kDaTile) of KV head g,
+// skipping position `skip` (not yet written).
+__device__ __forceinline__ void da_stage(float *ks, float *vs, const float *kc, const float *vc, int kvd, int g, int a,
+                                         int b, int skip)
+{
+    const uint32_t ks_a = (uint32_t)__cvta_generic_to_shared(ks), vs_a = (uint32_t)__cvta_generic_to_shared(vs);
+    const int n16 = (b - a) * 16;  // 16-byte pieces per matrix
+    for (int e = threadIdx.x; e < 2 * n16; e += kDaThreads) {
+        const int m = e >= n16, f = e - m * n16, t = f >> 4, q = f & 15;
+        if (a + t == skip) continue;
+        const size_t src = (size_t)(a + t) * kvd + g * 64 + q * 4;
+        if (m == 0)
+            da_cp16(ks_a + (uint32_t)(t * kDaKStride + q * 4) * 4u, kc + src);
+        else
+            da_cp16(vs_a + (uint32_t)(t * 64 + q * 4) * 4u, vc + src);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kDaThreads, 1)
+attention_cluster_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *__restrict__ kc,
+                         float *__restrict__ vc, int max_ctx, float rope_base, DecodeState *st,
+                         float *__restrict__ att)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    float *ks = reinterpret_cast<float *>(smem);                          // [kDaTile][kDaKStride]
+    float *vs = reinterpret_cast<float *>(smem + kDaKBytes);              // [kDaTile][64]
+    float *qs = reinterpret_cast<float *>(smem + kDaKBytes + kDaVBytes);  // [G][64]
+    float *ps = qs + kDaMaxGroup * 64;                                    // [G][kDaTile]
+    float *knew = ps + kDaMaxGroup * kDaTile;                             // rotated key of pos [64], value [64]
+    float *part = knew + 128;                                             // leader: [S][kDaMaxGroup][kDaPart]
+    __shared__ float cs[32], sn[32], mh[kDaMaxGroup], lh[kDaMaxGroup];
+    __shared__ float wr[kDaSplit][kDaMaxGroup];
+    __shared__ __align__(8) unsigned long long bar;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint32_t rank;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    const int g = (int)(blockIdx.x / kDaSplit);
+    const int G = heads / kv_heads, dim = heads * 64, kvd = kv_heads * 64;
+    const uint32_t bar_a = (uint32_t)__cvta_generic_to_shared(&bar);
+    // The output projection may start copying its weights; it reads att only
+    // after its own griddepcontrol.wait.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int pos = st->pos;  // written by the previous step's advance kernel
+    if (pos < 0 || pos >= max_ctx) {  // the same for every CTA: no cluster barrier is reached
+        if (blockIdx.x == 0 && tid == 0) atomicOr(&st->error, 2u);
+        return;
+    }
+    if (rank == 0 && tid == 0) {
+        // the leader's mbarrier expects the other CTAs' partials
+        mbar_init(bar_a, 1u);
+        mbar_expect_tx(bar_a, (uint32_t)((kDaSplit - 1) * G * (64 + 2) * 4));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+    const int T = pos + 1;
+    const int a0 = (int)((long long)T * rank / kDaSplit), b0 = (int)((long long)T * (rank + 1) / kDaSplit);
+    const int ntiles = (b0 - a0 + kDaTile - 1) / kDaTile;
+    if (ntiles > 0) da_stage(ks, vs, kc, vc, kvd, g, a0, min(b0, a0 + kDaTile), pos);
+    if (tid < 32) {
+        const float angle = (float)pos / powf(rope_base, (2.0f * (float)tid / 64.f));
+        cs[tid] = cosf(angle);
+        sn[tid] = sinf(angle);
+    }
+    if (tid < kDaMaxGroup) {
+        mh[tid] = -INFINITY;
+        lh[tid] = 0.f;
+    }
+    // q, k and v of this position come from the Q/K/V GEMV
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    __syncthreads();
+    for (int e = tid; e < G * 64; e += kDaThreads) {
+        const int hh = e >> 6, d = e & 63, i = d & 31;
+        const float *q = qkv + (g * G + hh) * 64;
+        const float x = __ldcg(q + i), y = __ldcg(q + i + 32);
+        qs[hh * 64 + d] = d < 32 ? x * cs[i] - y * sn[i] : x * sn[i] + y * cs[i];
+    }
+    const bool owns_pos = pos >= a0 && pos < b0;
+    if (owns_pos && tid < 64) {
+        const int d = tid, i = d & 31;
+        const float *k = qkv + dim + g * 64;
+        const float x = __ldcg(k + i), y = __ldcg(k + i + 32);
+        const float kr = d < 32 ? x * cs[i] - y * sn[i] : x * sn[i] + y * cs[i];
+        const float vv = __ldcg(qkv + dim + kvd + g * 64 + d);
+        const size_t slot = (size_t)pos * kvd + g * 64 + d;
+        kc[slot] = kr;
+        vc[slot] = vv;
+        knew[d] = kr;
+        knew[64 + d] = vv;
+    }
+    // per thread: the weighted sums of head `warp`, dimensions 4*(lane & 15)..,
+    // over the tile positions of half (lane >> 4)
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    const int dq = lane & 15, half = lane >> 4;
+    const float rs = sqrtf(64.f);
+    for (int ti = 0; ti < ntiles; ++ti) {
+        const int a = a0 + ti * kDaTile, b = min(b0, a + kDaTile), tn = b - a;
+        if (ti > 0) {
+            __syncthreads();  // every thread is done with the previous tile
+            da_stage(ks, vs, kc, vc, kvd, g, a, b, pos);
+        }
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();
+        if (pos >= a && pos < b && tid < 64) {  // this position's key and value
+            ks[(pos - a) * kDaKStride + tid] = knew[tid];
+            vs[(pos - a) * 64 + tid] = knew[64 + tid];
+        }
+        __syncthreads();
+        // scores: thread (position t, heads hg, hg + NG, ...): NG = 4 groups
+        // of 64 positions when the tile has at most 64, else 2 of 128
+        {
+            const int P = tn <= 64 ? 64 : kDaTile, NG = kDaThreads / P;
+            const int t = tid % P, hg = tid / P;
+            if (t < tn) {
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
+                const float4 *kr = reinterpret_cast<const float4 *>(ks + t * kDaKStride);
+#pragma unroll 4
+                for (int d4 = 0; d4 < 16; ++d4) {
+                    const float4 k4 = kr[d4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int hh = hg + NG * j;
+                        if (hh < G) {
+                            const float4 q4 = reinterpret_cast<const float4 *>(qs + hh * 64)[d4];
+                            acc[j] += q4.x * k4.x;
+                            acc[j] += q4.y * k4.y;
+                            acc[j] += q4.z * k4.z;
+                            acc[j] += q4.w * k4.w;
+                        }
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (hg + NG * j < G) ps[(hg + NG * j) * kDaTile + t] = acc[j] / rs;
+            }
+        }
+        __syncthreads();
+        // softmax update of head `warp`: running maximum and sum, tile weights
+        if (warp < G) {
+            float *pr = ps + warp * kDaTile;
+            float mt = -INFINITY;
+            for (int t = lane; t < tn; t += 32) mt = fmaxf(mt, pr[t]);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(kFull, mt, off));
+            const float m_old = mh[warp], m_new = fmaxf(m_old, mt);
+            float l = 0.f;
+            for (int t = lane; t < tn; t += 32) {
+                const float p = expf(pr[t] - m_new);
+                pr[t] = p;
+                l += p;
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(kFull, l, off);
+            const float alpha = expf(m_old - m_new);  // 0 on the first tile
+            __syncwarp();
+            if (lane == 0) {
+                mh[warp] = m_new;
+                lh[warp] = lh[warp] * alpha + l;
+            }
+            // weighted value sums of this head (the warp owns it)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[j] *= alpha;
+            const int t_end = min(tn, (half + 1) * (kDaTile / 2));
+#pragma unroll 8
+            for (int t = half * (kDaTile / 2); t < t_end; ++t) {
+                const float p = pr[t];
+                const float4 v4 = reinterpret_cast<const float4 *>(vs + t * 64)[dq];
+                o[0] += p * v4.x;
+                o[1] += p * v4.y;
+                o[2] += p * v4.z;
+                o[3] += p * v4.w;
+            }
+            __syncwarp();
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] += __shfl_xor_sync(kFull, o[j], 16);
+    __syncthreads();  // mh / lh final
+    // the leader's mbarrier is initialised (cluster barrier arrived at above)
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+    if (warp < G) {
+        float *mine = part + (rank * kDaMaxGroup + warp) * kDaPart;
+        if (rank == 0) {
+            if (lane < 16) *reinterpret_cast<float4 *>(mine + 4 + 4 * dq) = make_float4(o[0], o[1], o[2], o[3]);
+            if (lane == 0) *reinterpret_cast<float2 *>(mine) = make_float2(mh[warp], lh[warp]);
+        } else {
+            uint32_t remote, rbar;
+            const uint32_t local = (uint32_t)__cvta_generic_to_shared(mine);
+            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(remote) : "r"(local));
+            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(rbar) : "r"(bar_a));
+            if (lane < 16)
+                asm volatile(
+                    "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                        remote + 16u + 16u * (uint32_t)dq),
+                    "f"(o[0]), "f"(o[1]), "f"(o[2]), "f"(o[3]), "r"(rbar)
+                    : "memory");
+            if (lane == 0)
+                asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+                                 remote),
+                             "f"(mh[warp]), "f"(lh[warp]), "r"(rbar)
+                             : "memory");
+        }
+    }
+    if (rank != 0) return;
+    // leader: every partial has landed (bounded wait; the barrier also
+    // publishes the leader's own partials), then the merge
+    const bool landed = mbar_wait(bar_a, 0u);
+    if (!__syncthreads_and(landed)) {
+        if (tid == 0) atomicOr(&st->error, 16u);
+        return;
+    }
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int r = 0; r < kDaSplit; ++r) M = fmaxf(M, part[(r * kDaMaxGroup + tid) * kDaPart]);
+        float den = 0.f;
+        for (int r = 0; r < kDaSplit; ++r) {
+            const float w = expf(part[(r * kDaMaxGroup + tid) * kDaPart] - M);
+            wr[r][tid] = w;
+            den += w * part[(r * kDaMaxGroup + tid) * kDaPart + 1];
+        }
+        lh[tid] = den;
+    }
+    __syncthreads();
+    for (int e = tid; e < G * 64; e += kDaThreads) {
+        const int hh = e >> 6, d = e & 63;
+        float num = 0.f;
+#pragma unroll 4
+        for (int r = 0; r < kDaSplit; ++r) num += wr[r][hh] * part[(r * kDaMaxGroup + hh) * kDaPart + 4 + d];
+        att[(g * G + hh) * 64 + d] = num / lh[hh];
+    }
+}
+
 // One thread: the step's greedy token (key of index_base 0) becomes the next
 // step's input; the position moves on.
 __global__ void advance_kernel(const unsigned long long *key, DecodeState *st, int *history, int max_steps,
@@ -3494,10 +3959,51 @@ cudaError_t gemv_go(const Layout &L, const uint8_t *w, const float *x, float *y,
     return cudaGetLastError();
 }
 
-// 0 auto (exclusive TMA plan, else direct loads), 1 direct loads, 2 TMA
-// pipeline only, 3 exclusive TMA plan (else direct loads), 4 the shared TMA
-// plan where it fits (else as 0)
+// 0 auto (resident-row-range kernel, else exclusive TMA plan, else direct
+// loads), 1 direct loads, 2 TMA pipeline only, 3 exclusive TMA plan (else
+// direct loads), 4 the shared TMA plan where it fits (else as 3), 5 the
+// resident-row-range kernel only
 int g_gemv_path = 0;
+
+// Decode attention: 0 the cluster kernel where the group has at most 8 query
+// heads and the device can place a 16-CTA cluster, 1 the chunked kernel.
+int g_attn_path = 0;
+
+// Whether a 16-CTA cluster of attention_cluster_kernel fits on the current
+// device (non-portable cluster size; checked once per device).
+bool attention_cluster_ok()
+{
+    static std::mutex mu;
+    static int state[64] = {};  // 0 unknown, 1 yes, 2 no
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    std::lock_guard<std::mutex> lock(mu);
+    if (state[dev] == 0) {
+        bool ok = cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+                      cudaSuccess &&
+                  cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kDaSmem) == cudaSuccess;
+        if (ok) {
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(kDaSplit);
+            cfg.blockDim = dim3(kDaThreads);
+            cfg.dynamicSmemBytes = kDaSmem;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = kDaSplit;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int clusters = 0;
+            ok = cudaOccupancyMaxActiveClusters(&clusters, attention_cluster_kernel, &cfg) == cudaSuccess &&
+                 clusters > 0;
+        }
+        cudaGetLastError();  // a refused attribute is not an error of a later call
+        state[dev] = ok ? 1 : 2;
+    }
+    return state[dev] == 1;
+}
 
 // Shared-memory plan of the TMA kernel: the first of these (consumer warps,
 // rows per warp, minimum stages) whose stages fit.  Two rows per warp share
@@ -3565,6 +4071,88 @@ bool tma_plan_shared(const Layout &L, TmaPlan *P)
     for (const int *cand : kShared)
         if (tma_candidate(L, cand, 1, ctas, P, kTmaBudgetShared)) return true;
     return false;
+}
+
+// Plan of the resident-row-range kernel for one matrix, or two with equal
+// columns sharing x: one CTA per SM (fewer for fewer rows); false when a
+// CTA's rows or the quantized x exceed their budgets.
+bool lite_plan(const LiteMat *mats, int n, LitePlan *P, unsigned *grid_out)
+{
+    long long grid = sm_count();
+    for (int i = 0; i < n; ++i)
+        if (grid > mats[i].L.rows) grid = mats[i].L.rows;
+    if (grid < 1) return false;
+    const uint32_t xb = (uint32_t)((xs_bytes(mats[0].L.cols) + 127) & ~(size_t)127);
+    if (xb > kLiteXBudget) return false;
+    uint64_t off = 0;
+    for (int i = 0; i < n; ++i) {
+        const uint64_t max_rows = ((uint64_t)mats[i].L.rows + (uint64_t)grid - 1) / (uint64_t)grid;
+        P->m[i] = mats[i];
+        P->m[i].soff = (uint32_t)off;
+        off += (max_rows * mats[i].L.row_stride + 127) & ~127ull;
+        if (off > kLiteRowBudget) return false;
+    }
+    P->nmat = n;
+    P->x_bytes = xb;
+    P->smem = xb + (uint32_t)off;
+    if (P->smem < kLiteSmemFloor) P->smem = kLiteSmemFloor;  // at most two CTAs per SM
+    P->status = nullptr;
+    *grid_out = (unsigned)grid;
+    return true;
+}
+
+template <uint32_t FA, uint32_t FB, int R>
+cudaError_t gemv_lite_go_r(const LitePlan &P, unsigned grid, const float *x, const ArgmaxOut *am, const Fuse &fu,
+                           cudaStream_t s)
+{
+    auto kernel = gemv_lite_kernel<FA, FB, R>;
+    LitePlan Pc = P;
+    Pc.status = t_call_status;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    e = allow_max_smem((const void *)kernel, dev);
+    if (e != cudaSuccess) return e;
+    const ArgmaxOut a = am ? *am : ArgmaxOut{nullptr, nullptr, 0};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kLiteWarps * 32);
+    cfg.dynamicSmemBytes = P.smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kernel, Pc, x, a, am ? 1 : 0, fu);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// One row per warp pass when a CTA holds at most one row per warp (all warps
+// busy), else two (each x slice load serves two rows).
+template <uint32_t FA, uint32_t FB>
+cudaError_t gemv_lite_go(const LitePlan &P, unsigned grid, const float *x, const ArgmaxOut *am, const Fuse &fu,
+                         cudaStream_t s)
+{
+    const int per_cta = (P.m[0].L.rows + (int)grid - 1) / (int)grid;
+    if (per_cta <= kLiteWarps) return gemv_lite_go_r<FA, FB, 1>(P, grid, x, am, fu, s);
+    return gemv_lite_go_r<FA, FB, 2>(P, grid, x, am, fu, s);
+}
+
+// One matrix on the resident-row-range kernel under the current path
+// setting (automatic or forced); cudaErrorNotSupported when it does not
+// apply.
+template <uint32_t FMT>
+cudaError_t gemv_lite_single(const Layout &L, const uint8_t *w, const float *x, float *y, const ArgmaxOut *am,
+                             const Fuse &fu, cudaStream_t s)
+{
+    if (g_gemv_path != 0 && g_gemv_path != 5) return cudaErrorNotSupported;
+    const LiteMat m{L, w, y, fu.add, 0};
+    LitePlan P;
+    unsigned grid = 0;
+    if (!lite_plan(&m, 1, &P, &grid)) return g_gemv_path == 5 ? cudaErrorInvalidConfiguration : cudaErrorNotSupported;
+    return gemv_lite_go<FMT, 0>(P, grid, x, am, fu, s);
 }
 
 // Plan of a single-position GEMV under the current path setting; *shared
@@ -3654,6 +4242,14 @@ template <uint32_t FMT>
 cudaError_t gemv_fused_fmt(const Layout &L, const uint8_t *w, const float *x, float *y, const ArgmaxOut *am,
                            const Fuse &fu, cudaStream_t s)
 {
+    // The decode step's fused projections keep the TMA pipeline unless the
+    // resident-row-range kernel is forced: in that chain its launches follow
+    // attention CTAs that leave some SMs empty early, the next launch then
+    // doubles up on those SMs, and the step measured slower (822 vs 683 us
+    // per configuration-4 token on B200).
+    const cudaError_t el =
+        g_gemv_path == 5 ? gemv_lite_single<FMT>(L, w, x, y, am, fu, s) : cudaErrorNotSupported;
+    if (el != cudaErrorNotSupported) return el;
     TmaPlan P;
     bool shared = false;
     if (!gemv_plan(L, &P, &shared)) return cudaErrorNotSupported;
@@ -3709,6 +4305,8 @@ template <uint32_t FMT>
 cudaError_t gemv_fmt(const Layout &L, const uint8_t *w, const float *x, float *y, const ArgmaxOut *am,
                      cudaStream_t s)
 {
+    const cudaError_t el = gemv_lite_single<FMT>(L, w, x, y, am, Fuse{}, s);
+    if (el != cudaErrorNotSupported) return el;
     TmaPlan P;
     bool shared = false;
     if (g_gemv_path != 1 && gemv_plan(L, &P, &shared)) return gemv_tma_dispatch<FMT>(L, P, shared, w, x, y, am, s);
@@ -4193,6 +4791,24 @@ cudaError_t launch_attention(const float *qkv, int heads, int kv_heads, int head
     if (head_dim != 64 || kv_heads <= 0 || heads % kv_heads != 0 || heads / kv_heads > kAttnMaxGroup ||
         max_ctx <= 0)
         return cudaErrorInvalidValue;
+    if (g_attn_path == 0 && heads / kv_heads <= kDaMaxGroup && attention_cluster_ok()) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3((unsigned)(kv_heads * kDaSplit));
+        cfg.blockDim = dim3(kDaThreads);
+        cfg.dynamicSmemBytes = kDaSmem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = kDaSplit;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 2;
+        return cudaLaunchKernelEx(&cfg, attention_cluster_kernel, qkv, heads, kv_heads, kc, vc, max_ctx, rope_base, st,
+                                  att);
+    }
     const dim3 grid((unsigned)kv_heads, (unsigned)((max_ctx + kAttnChunk - 1) / kAttnChunk));
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
@@ -4206,6 +4822,8 @@ cudaError_t launch_attention(const float *qkv, int heads, int kv_heads, int head
     return cudaLaunchKernelEx(&cfg, attention_kernel<64>, qkv, heads, kv_heads, kc, vc, max_ctx, rope_base, st, part,
                               counter, att);
 }
+
+void set_attention_path(int path) { g_attn_path = path; }
 
 cudaError_t launch_advance(const unsigned long long *key, DecodeState *st, int *history, int max_steps,
                            cudaStream_t s, unsigned int *bar_count)
@@ -4320,6 +4938,14 @@ cudaError_t launch_gemv_pair(const Layout &La, const uint8_t *wa, float *ya, con
     pr.w[1] = swap ? wa : wb;
     pr.y[0] = swap ? yb : ya;
     pr.y[1] = swap ? ya : yb;
+    // Q5_0 and Q8_0 share the quantized x's slice layout: both matrices in
+    // every CTA of one resident-row-range launch when their rows fit
+    if (g_gemv_path == 5 && pr.L[0].type == kQ5_0 && pr.L[1].type == kQ8_0) {
+        const LiteMat mats[2] = {{pr.L[0], pr.w[0], pr.y[0], nullptr, 0}, {pr.L[1], pr.w[1], pr.y[1], nullptr, 0}};
+        LitePlan P;
+        unsigned lgrid = 0;
+        if (lite_plan(mats, 2, &P, &lgrid)) return gemv_lite_go<kQ5_0, kQ8_0>(P, lgrid, x, nullptr, fu, s);
+    }
     // one CTA per SM, split between the matrices by their bytes
     const long long sms = sm_count();
     if (sms < 2) return cudaErrorNotSupported;

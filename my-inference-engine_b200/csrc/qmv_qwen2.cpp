@@ -302,6 +302,7 @@ int check_state(QmvQwen2 *m, qmv::DecodeState *out)
     if (s.error & 2u) return qmv::set_error("decode step: context capacity is exhausted");
     if (s.error & 4u) return qmv::set_error("decode step: output contains a non-finite logit");
     if (s.error & 8u) return qmv::set_error("decode step: a grid barrier of the persistent step expired");
+    if (s.error & 16u) return qmv::set_error("decode step: the attention cluster's wait for its partials expired");
     return 1;
 }
 
@@ -896,6 +897,13 @@ QMV_EXPORT int qmv_set_decode_mode(int mode)
 {
     if (mode < 0 || mode > 1) return qmv::set_error("decode mode must be 0 or 1");
     g_decode_mode = mode;
+    return 1;
+}
+
+QMV_EXPORT int qmv_set_attention_path(int path)
+{
+    if (path < 0 || path > 1) return qmv::set_error("attention path must be 0 or 1");
+    qmv::set_attention_path(path);
     return 1;
 }
 

@@ -31,13 +31,14 @@ def to_dev(torch, a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-@pytest.fixture(params=[0, 1, 4], ids=["auto", "loads", "shared"])
+@pytest.fixture(params=[0, 1, 3, 4], ids=["auto", "loads", "tma", "shared"])
 def gemv_path(request, qmv):
-    """Run a test with the automatic kernel choice (the TMA pipeline's
-    exclusive plan where its stages fit, else direct loads), with the
-    direct-load kernel forced, and with the shared TMA plan (half an SM per
-    CTA, register-capped kernel) where its stages fit (else the automatic
-    choice)."""
+    """Run a test with the automatic kernel choice (the resident-row-range
+    kernel where a CTA's rows fit in its shared memory, else the TMA
+    pipeline's exclusive plan where its stages fit, else direct loads), with
+    the direct-load kernel forced, with the TMA pipeline's exclusive plan
+    (else direct loads), and with the shared TMA plan (half an SM per CTA,
+    register-capped kernel) where its stages fit (else the exclusive plan)."""
     qmv.set_gemv_path(request.param)
     yield request.param
     qmv.set_gemv_path(0)

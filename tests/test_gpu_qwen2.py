@@ -64,13 +64,18 @@ def _teacher_forced(qmv, oracle, wl, name, t0, max_ctx, steps, seed=0, first=7, 
     return worst
 
 
-@pytest.fixture(params=[0, 1], ids=["per-launch", "persistent"])
+@pytest.fixture(params=[(0, 0), (0, 1), (1, 0)], ids=["per-launch", "per-launch-chunked-attention", "persistent"])
 def decode_mode(request, qmv):
     """Decoders created inside the test run their step as one launch per
-    projection (mode 0) or as the persistent layer stack (mode 1)."""
-    qmv.set_decode_mode(request.param)
-    yield request.param
+    projection (mode 0), with the cluster attention kernel (one 16-CTA
+    cluster per KV head) or the chunked one, or as the persistent layer stack
+    (mode 1)."""
+    mode, attention = request.param
+    qmv.set_decode_mode(mode)
+    qmv.set_attention_path(attention)
+    yield mode
     qmv.set_decode_mode(0)
+    qmv.set_attention_path(0)
 
 
 def test_qwen2_decode_teacher_forced_small(cuda, qmv, oracle, workloads, decode_mode):
@@ -186,4 +191,18 @@ def test_qwen2_config4_free_run(cuda, qmv, workloads, ref):
             tok = rtok
     finally:
         rq.close()
+    assert qmv.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("gate,up", [("Q8_0", "Q5_0"), ("Q8_0", "Q8_0")])
+def test_qwen2_decode_resident_row_kernel(cuda, qmv, oracle, workloads, gate, up):
+    """The decode step with every projection that fits on the
+    resident-row-range GEMV kernel (gemv path 5), including its paired
+    gate/up launch for Q8_0 and Q5_0 in one CTA."""
+    types = dict(gate=getattr(workloads, gate), up=getattr(workloads, up))
+    qmv.set_gemv_path(5)
+    try:
+        _teacher_forced(qmv, oracle, workloads, "qwen2_g7_small", t0=40, max_ctx=64, steps=3, seed=8, types=types)
+    finally:
+        qmv.set_gemv_path(0)
     assert qmv.device_status(clear=True) == 0
