@@ -111,6 +111,11 @@ struct Fuse {
     float eps;
     const float *up;    // kPreSwiGlu: up[cols]
     const float *add;   // y[row] = (W x)[row] + add[row] when non-null (add == y: residual in place)
+    // L2 prefetch of the launch that follows in the stream (the decode step's
+    // next projection): each CTA prefetches its share of these byte ranges
+    // once its own copies are issued.  Null: none.
+    const uint8_t *pf[2];
+    uint64_t pf_bytes[2];
 };
 
 // y = W x (and optionally the argmax key of y).

@@ -358,8 +358,13 @@ __device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t
                     *ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
                     v[u] = make_float4(v[u].x * a.x, v[u].y * a.y, v[u].z * a.z, v[u].w * a.w);
                 } else {
-                    v[u] = make_float4(a.x * (v[u].x / (1.f + expf(-v[u].x))), a.y * (v[u].y / (1.f + expf(-v[u].y))),
-                                       a.z * (v[u].z / (1.f + expf(-v[u].z))), a.w * (v[u].w / (1.f + expf(-v[u].w))));
+                    // SwiGLU: the x that is quantized next (to 2^-15 of its
+                    // block maximum), so the fast exponential's few-ulp error
+                    // is far below what the quantization keeps
+                    v[u] = make_float4(a.x * (v[u].x / (1.f + __expf(-v[u].x))),
+                                       a.y * (v[u].y / (1.f + __expf(-v[u].y))),
+                                       a.z * (v[u].z / (1.f + __expf(-v[u].z))),
+                                       a.w * (v[u].w / (1.f + __expf(-v[u].w))));
                 }
             }
         }
@@ -1056,6 +1061,32 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
                  : "memory");
 }
 
+// Prefetch of the L2 line holding p (a valid address).
+__device__ __forceinline__ void prefetch_line_l2(const void *p)
+{
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+// Bulk prefetch of [p, p + bytes) into L2 (16-byte aligned, multiple of 16).
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// This CTA's share (of ncta) of the fused prefetch ranges.
+__device__ __forceinline__ void prefetch_share(const Fuse &fu, int cta, int ncta)
+{
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        if (fu.pf[i] == nullptr || fu.pf_bytes[i] == 0) continue;
+        const uint64_t B = fu.pf_bytes[i];
+        const uint64_t b0 = (B * (uint64_t)cta / (uint64_t)ncta) & ~15ull;
+        const uint64_t b1 = cta + 1 == ncta ? (B & ~15ull) : ((B * (uint64_t)(cta + 1) / (uint64_t)ncta) & ~15ull);
+        for (uint64_t off = b0; off < b1; off += 65536u)
+            prefetch_l2(fu.pf[i] + off, (uint32_t)(b1 - off < 65536u ? b1 - off : 65536u));
+    }
+}
+
 struct TmaPlan {
     uint32_t x_bytes;      // quantized x, rounded to 128
     uint32_t stage_bytes;  // rows_per_stage * row_stride, rounded to 128
@@ -1178,39 +1209,55 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
                 }
             }
         }
+        if (ok && lane == 0) prefetch_share(fu, (int)blockIdx.x, (int)gridDim.x);
         __syncwarp();
         asm volatile("griddepcontrol.wait;" ::: "memory");
     } else {
         // ---------------- consumers
+        // The RMSNorm weights and the epilogue's addend rows of this CTA do
+        // not depend on the previous launch (the addend is a bias, or the
+        // residual stream, whose lines are then simply in L2 already): bring
+        // their lines into L2 while the previous launch finishes.
+        if (NP == 1) {
+            if (fu.pre == kPreRmsNorm)
+                for (int i = threadIdx.x * 32; i < L.cols; i += CW * 32 * 32) prefetch_line_l2(fu.norm + i);
+            if (fu.add != nullptr)
+                for (int i = r0 + threadIdx.x * 32; i < r1; i += CW * 32 * 32) prefetch_line_l2(fu.add + i);
+        }
         asm volatile("griddepcontrol.wait;" ::: "memory");
         if (ex.world > 1)  // this rank's slot in this epoch's parity region
             y = ex.logits[exchange_epoch(ex) & 1u][ex.rank] + (size_t)ex.rank * ex.slot_rows;
         const size_t xb = xs_bytes(L.cols);
-        float denom = 1.f;
-        if (NP == 1 && fu.pre == kPreRmsNorm) {
-            // RMSNorm prologue: sum of squares over every consumer thread
-            float ss = 0.f;
-            for (int i = threadIdx.x; i < L.cols; i += CW * 32) ss += x[i] * x[i];
+        // One pass over x: the RMSNorm prologue quantizes x * norm and scales
+        // the row sums by 1 / sqrt(mean(x^2) + eps), whose sum of squares is
+        // gathered in the same pass.
+        const bool rms = NP == 1 && fu.pre == kPreRmsNorm;
+        const int pre = NP == 1 ? (rms ? kPreScale : fu.pre) : kPreNone;
+        const float *aux = fu.pre == kPreRmsNorm ? fu.norm : fu.up;
+        float ss = 0.f;
+        quantize_x<FMT, CW * 32>(x, L.cols, C, smem, NP == 1 ? 1 : P.np, xb, pre, 1.f, aux,
+                                 RARE ? &sh.special : nullptr, &ss);
+        if (rms) {
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
             if (lane == 0) sh.sumsq[warp] = ss;
-            asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+        float denom = 1.f, rscale = 1.f;
+        if (rms) {
             ss = 0.f;
             for (int i = 0; i < CW; ++i) ss += sh.sumsq[i];
             denom = sqrtf(ss / (float)L.cols + fu.eps);
+            rscale = 1.f / denom;
         }
-        const int pre = NP == 1 ? fu.pre : kPreNone;
-        const float *aux = fu.pre == kPreRmsNorm ? fu.norm : fu.up;
-        quantize_x<FMT, CW * 32>(x, L.cols, C, smem, NP == 1 ? 1 : P.np, xb, pre, denom, aux,
-                                 NP == 1 && RARE ? &sh.special : nullptr);
-        asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
         const bool f32 = *(volatile int *)&sh.special != 0;  // uniform over the CTA
         const XS s = xs_view(smem, L.cols);
         const int NI = (C + 32 * SPLIT - 1) / (32 * SPLIT);
         const int rw = warp % (CW / SPLIT), half = warp / (CW / SPLIT);  // row slot, chunk half
-        if (RARE && NP == 1 && f32) {
+        if (RARE && f32) {
             // special x: consume the stages (the producer must finish), then
-            // this CTA's rows in fp32 from global memory
+            // this CTA's rows in fp32 from global memory (every position of a
+            // batch)
             for (int k = 0; k < n_stages; ++k) {
                 if (!mbar_wait(full(k % NS, rw), (uint32_t)((k / NS) & 1))) {
                     report_status(P.status, kStatusConsumerTimeout);
@@ -1219,8 +1266,14 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
                 __syncwarp();
                 if (lane == 0) mbar_arrive(empty0 + 8u * (k % NS));
             }
-            best = fp32_rows<FMT>(L, w, r0, r1, warp, CW, XVal{x, pre, denom, aux}, y, fu.add, want_argmax != 0,
-                                  am.index_base);
+            if constexpr (NP == 1) {
+                best = fp32_rows<FMT>(L, w, r0, r1, warp, CW, XVal{x, fu.pre, denom, aux}, y, fu.add,
+                                      want_argmax != 0, am.index_base);
+            } else {
+                for (int p = 0; p < P.np; ++p)
+                    fp32_rows<FMT>(L, w, r0, r1, warp, CW, XVal{x + (size_t)p * L.cols, kPreNone, 1.f, nullptr},
+                                   y + (size_t)p * L.rows, nullptr, false, 0);
+            }
         } else
         for (int k = 0; k < n_stages; ++k) {
             const int sidx = k % NS;
@@ -1312,6 +1365,7 @@ __device__ __forceinline__ void gemv_tma_body(uint8_t *smem, TmaShared &sh, int 
             const int oi = lane / NP, op = lane % NP;
             if (half == 0 && lane < R * NP && lr0 + oi < rows_k && op < P.np) {
                 const int row = base_row + lr0 + oi;
+                out *= rscale;
                 if (fu.add != nullptr) out += fu.add[(size_t)op * L.rows + row];
                 y[(size_t)op * L.rows + row] = out;
                 if (NP == 1 && want_argmax) best = max_ull(best, make_key(out, am.index_base + row));
@@ -1523,6 +1577,7 @@ gemv_lite_kernel(LitePlan P, const float *__restrict__ x, ArgmaxOut am, int want
             for (uint32_t off = 0; off < bytes; off += 32768u)
                 bulk_g2s(rows_a + P.m[i].soff + off, src + off, min(32768u, bytes - off), bar_a);
         }
+        prefetch_share(fu, (int)blockIdx.x, (int)gridDim.x);
     }
     // x (and add) may be written by the previous launch: read through L2
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -4049,7 +4104,9 @@ bool tma_plan(const Layout &L, TmaPlan *P, int np = 1, bool batched = false)
 {
     static const int kCandidates[][4] = {{16, 2, 2, 1}, {8, 2, 3, 1}, {16, 1, 3, 1}, {8, 2, 2, 1},
                                          {16, 1, 2, 1}, {16, 1, 2, 2}, {8, 1, 2, 1}};
-    // batched form: 8 consumer warps (its per-thread state is larger)
+    // batched form: 8 warps of two rows (each x slice load serves two rows;
+    // 16 warps of one row measured slower on configuration 3 at 8 positions,
+    // 9.2 vs 8.3 us)
     static const int kBatchCandidates[][4] = {{8, 2, 2, 1}, {8, 1, 2, 1}};
     const long long ctas = L.rows < sm_count() ? L.rows : sm_count();  // one CTA per SM
     const int n_cand = batched ? 2 : 7;
@@ -4505,11 +4562,12 @@ cudaError_t matmul_tma_fmt(const Layout &L, const uint8_t *w, const float *X, in
     *done = true;
     for (int p0 = 0; p0 < batch; p0 += NP) {
         const int np = batch - p0 < NP ? batch - p0 : NP;
-        if (!tma_plan(L, &P, np, true) || P.consumer_warps != 8) return cudaErrorInvalidConfiguration;
+        if (!tma_plan(L, &P, np, true)) return cudaErrorInvalidConfiguration;
         const float *x = X + (size_t)p0 * L.cols;
         float *y = Y + (size_t)p0 * L.rows;
-        const cudaError_t e = P.rows_per_warp == 2 ? gemv_tma_go<FMT, 8, 2, NP>(L, P, w, x, y, nullptr, s)
-                                                   : gemv_tma_go<FMT, 8, 1, NP>(L, P, w, x, y, nullptr, s);
+        const cudaError_t e = P.consumer_warps == 16 ? gemv_tma_go<FMT, 16, 1, NP>(L, P, w, x, y, nullptr, s)
+                              : P.rows_per_warp == 2 ? gemv_tma_go<FMT, 8, 2, NP>(L, P, w, x, y, nullptr, s)
+                                                     : gemv_tma_go<FMT, 8, 1, NP>(L, P, w, x, y, nullptr, s);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

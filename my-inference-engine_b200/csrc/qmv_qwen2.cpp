@@ -217,11 +217,53 @@ cudaError_t enqueue_step_persistent(QmvQwen2 *m)
 // One decode step, enqueued on m->stream; mk != nullptr records the
 // profiling events of an un-captured step (always one launch per projection,
 // so each stage has its own events).
+// The step's projections in launch order (gate and up of a paired launch
+// as one entry each), for the L2 prefetch of the ones ahead.
+std::vector<const QmvWeight *> step_weights(const QmvQwen2 *m)
+{
+    std::vector<const QmvWeight *> seq;
+    for (const Layer &L : m->layers) {
+        if (L.qkv) {
+            seq.push_back(L.qkv);
+        } else {
+            seq.push_back(L.q);
+            seq.push_back(L.k);
+            seq.push_back(L.v);
+        }
+        seq.push_back(L.o);
+        if (L.gate_up) {
+            seq.push_back(L.gate_up);
+        } else {
+            seq.push_back(L.gate);
+            seq.push_back(L.up);
+        }
+        seq.push_back(L.down);
+    }
+    return seq;
+}
+
+// Prefetch ranges of a launch whose last weight matrix is seq[i]: the next
+// two matrices (the output projection, hundreds of MB, is never prefetched).
+qmv::Fuse with_prefetch(qmv::Fuse fu, const std::vector<const QmvWeight *> &seq, size_t i)
+{
+    constexpr size_t kMaxPrefetch = 16u << 20;
+    for (int j = 0; j < 2; ++j) {
+        const size_t n = i + 1 + (size_t)j;
+        if (n < seq.size() && seq[n]->bytes <= kMaxPrefetch) {
+            fu.pf[j] = seq[n]->dev;
+            fu.pf_bytes[j] = seq[n]->bytes;
+        }
+    }
+    return fu;
+}
+
 cudaError_t enqueue_step(QmvQwen2 *m, Marks *mk = nullptr)
 {
     if (m->persistent && mk == nullptr) return enqueue_step_persistent(m);
     const QmvQwen2Config &c = m->cfg;
     const int dim = c.dim, kvd = m->kvd;
+    const std::vector<const QmvWeight *> seq = step_weights(m);
+    size_t si = 0;  // index in seq of the next launch's first matrix
     cudaError_t e = mk ? record(m, mk) : cudaSuccess;
     if (e == cudaSuccess)
         e = mark(m, mk, qmv::launch_embed(m->embd->L, m->embd->dev, m->st, m->h, m->stream),
@@ -230,14 +272,19 @@ cudaError_t enqueue_step(QmvQwen2 *m, Marks *mk = nullptr)
         const Layer &L = m->layers[(size_t)l];
         qmv::Fuse pre_attn{qmv::kPreRmsNorm, L.attn_norm, c.rms_norm_epsilon, nullptr, L.bias_qkv};
         if (L.qkv) {
-            e = mark(m, mk, gemv(m, L.qkv, m->h, m->qkv, pre_attn), layer_mark(L.qkv, 3));
+            e = mark(m, mk, gemv(m, L.qkv, m->h, m->qkv, with_prefetch(pre_attn, seq, si)), layer_mark(L.qkv, 3));
+            si += 1;
         } else {
-            e = mark(m, mk, gemv(m, L.q, m->h, m->qkv, pre_attn), layer_mark(L.q, 1));
+            e = mark(m, mk, gemv(m, L.q, m->h, m->qkv, with_prefetch(pre_attn, seq, si)), layer_mark(L.q, 1));
             pre_attn.add = L.bias_qkv + dim;
-            if (e == cudaSuccess) e = mark(m, mk, gemv(m, L.k, m->h, m->qkv + dim, pre_attn), layer_mark(L.k, 1));
+            if (e == cudaSuccess)
+                e = mark(m, mk, gemv(m, L.k, m->h, m->qkv + dim, with_prefetch(pre_attn, seq, si + 1)),
+                         layer_mark(L.k, 1));
             pre_attn.add = L.bias_qkv + dim + kvd;
             if (e == cudaSuccess)
-                e = mark(m, mk, gemv(m, L.v, m->h, m->qkv + dim + kvd, pre_attn), layer_mark(L.v, 1));
+                e = mark(m, mk, gemv(m, L.v, m->h, m->qkv + dim + kvd, with_prefetch(pre_attn, seq, si + 2)),
+                         layer_mark(L.v, 1));
+            si += 3;
         }
         const size_t layer_off = (size_t)l * (size_t)c.max_context * (size_t)kvd;
         if (e == cudaSuccess)
@@ -247,28 +294,44 @@ cudaError_t enqueue_step(QmvQwen2 *m, Marks *mk = nullptr)
                                            m->attn_part, m->attn_cnt, m->att, m->stream),
                      Mark{kStageAttention, {0, 0}, 1.0, {0, 0}});
         if (e == cudaSuccess)
-            e = mark(m, mk, gemv(m, L.o, m->att, m->h, qmv::Fuse{qmv::kPreNone, nullptr, 0.f, nullptr, m->h}),
+            e = mark(m, mk,
+                     gemv(m, L.o, m->att, m->h,
+                          with_prefetch(qmv::Fuse{qmv::kPreNone, nullptr, 0.f, nullptr, m->h}, seq, si)),
                      layer_mark(L.o, 1));
+        si += 1;
         const qmv::Fuse pre_ffn{qmv::kPreRmsNorm, L.ffn_norm, c.rms_norm_epsilon, nullptr, nullptr};
         // With [gate; up] resident as one matrix, up lands right after gate.
         float *up = L.gate_up ? m->gate + c.hidden_dim : m->up;
         if (L.gate_up) {
-            if (e == cudaSuccess) e = mark(m, mk, gemv(m, L.gate_up, m->h, m->gate, pre_ffn), layer_mark(L.gate_up, 2));
-        } else if (e == cudaSuccess) {
-            // different formats: one paired launch, else two
-            e = qmv::launch_gemv_pair(L.gate->L, L.gate->dev, m->gate, L.up->L, L.up->dev, m->up, m->h, pre_ffn,
-                                      m->stream);
-            if (e == cudaErrorNotSupported) {
-                e = mark(m, mk, gemv(m, L.gate, m->h, m->gate, pre_ffn), layer_mark(L.gate, 1));
-                if (e == cudaSuccess) e = mark(m, mk, gemv(m, L.up, m->h, m->up, pre_ffn), layer_mark(L.up, 1));
-            } else {
-                const double bg = (double)L.gate->bytes, bu = (double)L.up->bytes;
-                e = mark(m, mk, e, Mark{kStageLayerGemv, {L.gate->L.type, L.up->L.type}, bg / (bg + bu), {1, 1}});
+            if (e == cudaSuccess)
+                e = mark(m, mk, gemv(m, L.gate_up, m->h, m->gate, with_prefetch(pre_ffn, seq, si)),
+                         layer_mark(L.gate_up, 2));
+            si += 1;
+        } else {
+            if (e == cudaSuccess) {
+                // different formats: one paired launch, else two
+                e = qmv::launch_gemv_pair(L.gate->L, L.gate->dev, m->gate, L.up->L, L.up->dev, m->up, m->h,
+                                          with_prefetch(pre_ffn, seq, si + 1), m->stream);
+                if (e == cudaErrorNotSupported) {
+                    e = mark(m, mk, gemv(m, L.gate, m->h, m->gate, with_prefetch(pre_ffn, seq, si)),
+                             layer_mark(L.gate, 1));
+                    if (e == cudaSuccess)
+                        e = mark(m, mk, gemv(m, L.up, m->h, m->up, with_prefetch(pre_ffn, seq, si + 1)),
+                                 layer_mark(L.up, 1));
+                } else {
+                    const double bg = (double)L.gate->bytes, bu = (double)L.up->bytes;
+                    e = mark(m, mk, e,
+                             Mark{kStageLayerGemv, {L.gate->L.type, L.up->L.type}, bg / (bg + bu), {1, 1}});
+                }
             }
+            si += 2;
         }
         if (e == cudaSuccess)
-            e = mark(m, mk, gemv(m, L.down, m->gate, m->h, qmv::Fuse{qmv::kPreSwiGlu, nullptr, 0.f, up, m->h}),
+            e = mark(m, mk,
+                     gemv(m, L.down, m->gate, m->h,
+                          with_prefetch(qmv::Fuse{qmv::kPreSwiGlu, nullptr, 0.f, up, m->h}, seq, si)),
                      layer_mark(L.down, 1));
+        si += 1;
     }
     const qmv::ArgmaxOut am{m->key, m->am_ws, 0};
     if (e == cudaSuccess)

@@ -240,8 +240,19 @@ def test_matvec_nonfinite_and_tiny_x(cuda, qmv, oracle, workloads, gemv_path, gt
 @pytest.mark.parametrize("gtype,rows,cols", [(Q5_0, 4864, 896), (Q8_0, 300, 896), (Q4_K, 129, 3584),
                                              (Q6_K, 129, 3584), (Q4_K, 40, 18944)])
 @pytest.mark.parametrize("batch", [1, 3, 8, 13])
-def test_matmul_parity(cuda, qmv, oracle, workloads, gtype, rows, cols, batch):
+@pytest.mark.parametrize("path", [0, 3], ids=["auto", "tma"])
+def test_matmul_parity(cuda, qmv, oracle, workloads, gtype, rows, cols, batch, path):
+    """Batched CUDA-core projections (chunks of up to 8 positions on the TMA
+    pipeline), with the automatic GEMV choice and the exclusive TMA plan."""
     torch = cuda
+    qmv.set_gemv_path(path)
+    try:
+        _matmul_parity(torch, qmv, oracle, workloads, gtype, rows, cols, batch)
+    finally:
+        qmv.set_gemv_path(0)
+
+
+def _matmul_parity(torch, qmv, oracle, workloads, gtype, rows, cols, batch):
     blocks = workloads.make_blocks(gtype, rows, cols, seed=3)
     X = np.stack([workloads.make_activations(cols, seed=50 + p) for p in range(batch)])
     w = qmv.Weight(gtype, blocks, rows, cols)
@@ -255,6 +266,39 @@ def test_matmul_parity(cuda, qmv, oracle, workloads, gtype, rows, cols, batch):
         s = oracle.row_abs_dot(gtype, blocks, rows, cols, X[p])
         bad, err, bound = tolerance_ok(Y[p], Y_ref[p], s, REL_TOL)
         assert bad.size == 0, (p, bad[:5])
+
+
+@pytest.mark.parametrize("path", [0, 3], ids=["auto", "tma"])
+def test_matmul_nonfinite_x_small_batch(cuda, qmv, oracle, workloads, path):
+    """An Inf in one position's x (CUDA-core batched form): the batch's rows
+    are computed in fp32, so that position's rows follow the reference's float
+    loop (Inf/NaN where it has them) and the others stay within the bound."""
+    torch = cuda
+    gtype, rows, cols, batch = Q8_0, 300, 896, 3
+    blocks = workloads.make_blocks(gtype, rows, cols, seed=11)
+    X = np.stack([workloads.make_activations(cols, seed=70 + p) for p in range(batch)])
+    X[1, 5] = np.inf
+    qmv.set_gemv_path(path)
+    try:
+        w = qmv.Weight(gtype, blocks, rows, cols)
+        Xd = to_dev(torch, X)
+        Yd = torch.full((batch, rows), 0.0, dtype=torch.float32, device="cuda")
+        w.matmul(Xd.data_ptr(), batch, Yd.data_ptr())
+        torch.cuda.synchronize()
+        Y = Yd.cpu().numpy()
+        w.free()
+    finally:
+        qmv.set_gemv_path(0)
+    Y_ref = oracle.matmul(gtype, blocks, rows, cols, X, batch)
+    for p in (0, 2):
+        s = oracle.row_abs_dot(gtype, blocks, rows, cols, X[p])
+        bad, err, bound = tolerance_ok(Y[p], Y_ref[p], s, REL_TOL)
+        assert bad.size == 0, (p, bad[:5])
+    # that position's rows in fp32, as the reference's loop
+    assert np.array_equal(np.isnan(Y[1]), np.isnan(Y_ref[1]))
+    assert np.array_equal(np.isposinf(Y[1]), np.isposinf(Y_ref[1]))
+    assert np.array_equal(np.isneginf(Y[1]), np.isneginf(Y_ref[1]))
+    assert qmv.device_status(clear=True) == 0
 
 
 # ------------------------------------------------ matmul (tensor cores)
