@@ -1638,6 +1638,178 @@ gemv_lite_kernel(LitePlan P, const float *__restrict__ x, ArgmaxOut am, int want
     }
 }
 
+// ------------------------------------ batched projection on int8 tensor cores
+//
+// Up to 8 positions (the reference's prefill chunk, configuration 3 at
+// P = 8) for the 32-weight block formats, on mma.sync m16n8k32 integer tensor
+// cores: A = 16 rows x 32 weights of one block (Q8_0 signed, Q5_0 unsigned
+// 0..31), B = 32 x values x 8 positions of one plane of the quantized x (hi
+// and lo int8 planes, two MMAs), exact int32 sums; each (row, position, block)
+// then takes the block's scales exactly as the CUDA-core dot does
+// ((d s) (256 hi + lo), Q5_0 minus 16 d s-weighted slice sums).  A CTA's rows
+// sit in shared memory whole (bulk copies before griddepcontrol.wait, as the
+// resident-row-range GEMV); warp w takes blocks [w C / 8, (w + 1) C / 8) of
+// every 16-row tile, and the warps' partial tiles are added in warp order.
+// A special x computes every position's rows in fp32.
+constexpr int kMmaWarps = 8;
+constexpr int kMmaMaxTiles = 4;  // 64 rows per CTA
+
+template <uint32_t FMT>
+__device__ __forceinline__ void mma_blk(int d[4], const uint32_t a[4], uint32_t b0, uint32_t b1)
+{
+    if constexpr (FMT == kQ8_0)
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%0,%1,%2,%3};"
+                     : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    else
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%0,%1,%2,%3};"
+                     : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Weights k = 4t..4t+3 (lo) and 16+4t..16+4t+3 (hi) of block c of the row
+// staged at srow, as A-fragment words; *d the block's scale.
+template <uint32_t FMT>
+__device__ __forceinline__ void mma_row_words(uint32_t srow, const Layout &L, int c, int t, uint32_t *lo,
+                                              uint32_t *hi, float *d)
+{
+    if constexpr (FMT == kQ8_0) {
+        *lo = lds32(srow + (uint32_t)(c << 4) + 4u * t);
+        *hi = lds32(srow + (uint32_t)((L.C + c) << 4) + 4u * t);
+        *d = f16_fast(lds16(srow + L.off_a + 2u * c));
+    } else {
+        // byte i of qs: weight i (low nibble), weight i + 16 (high nibble);
+        // bit i of qh: the fifth bit of weight i
+        const uint32_t q = lds32(srow + (uint32_t)(c << 4) + 4u * t);
+        const uint32_t qh = lds32(srow + L.off_a + 4u * c);
+        *lo = (q & 0x0f0f0f0fu) | spread4(qh >> (4 * t));
+        *hi = ((q >> 4) & 0x0f0f0f0fu) | spread4(qh >> (16 + 4 * t));
+        *d = f16_fast(lds16(srow + L.off_b + 2u * c));
+    }
+}
+
+template <uint32_t FMT>
+__global__ void __launch_bounds__(kMmaWarps * 32, 1)
+matmul_mma_kernel(Layout L, const uint8_t *__restrict__ w, const float *__restrict__ X, int np, float *__restrict__ Y,
+                  uint32_t x_bytes, unsigned int *status)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) unsigned long long bar;
+    __shared__ int special;
+    __shared__ float part[kMmaWarps][kMmaMaxTiles][16 * 8];
+    constexpr int NT = kMmaWarps * 32;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t bar_a = (uint32_t)__cvta_generic_to_shared(&bar);
+    const uint32_t rows_a = (uint32_t)__cvta_generic_to_shared(smem + x_bytes);
+    const int r0 = (int)((long long)L.rows * blockIdx.x / gridDim.x);
+    const int r1 = (int)((long long)L.rows * (blockIdx.x + 1) / gridDim.x);
+    const int nr = r1 - r0, ntiles = (nr + 15) / 16;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (tid == 0) {
+        mbar_init(bar_a, 1u);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        special = 0;
+        const uint32_t bytes = (uint32_t)nr * (uint32_t)L.row_stride;
+        mbar_expect_tx(bar_a, bytes);
+        const uint8_t *src = w + (uint64_t)r0 * L.row_stride;
+        for (uint32_t off = 0; off < bytes; off += 32768u)
+            bulk_g2s(rows_a + off, src + off, min(32768u, bytes - off), bar_a);
+    }
+    // X may be written by the previous launch: read through L2
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const size_t xb = xs_bytes(L.cols);
+    quantize_x<FMT, NT, true>(X, L.cols, L.C, smem, np, xb, kPreNone, 1.f, nullptr, &special);
+    __syncthreads();
+    const bool landed = mbar_wait(bar_a, 0u);
+    if (!__syncthreads_and(landed)) {
+        if (tid == 0) {
+            report_status(status, kStatusConsumerTimeout);
+            if (!landed && !mbar_wait(bar_a, 0u)) report_status(status, kStatusDrainTimeout);
+        }
+        return;
+    }
+    if (*(volatile int *)&special != 0) {
+        for (int p = 0; p < np; ++p)
+            fp32_rows<FMT>(L, w, r0, r1, warp, kMmaWarps, XVal{X + (size_t)p * L.cols, kPreNone, 1.f, nullptr},
+                           Y + (size_t)p * L.rows, nullptr, false, 0);
+        return;
+    }
+    const int C = L.C;
+    const int k0 = C * warp / kMmaWarps, k1 = C * (warp + 1) / kMmaWarps;
+    float acc[kMmaMaxTiles][4];
+#pragma unroll
+    for (int ti = 0; ti < kMmaMaxTiles; ++ti) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[ti][j] = 0.f;
+    }
+    // B column g: position g (positions past np re-read the last one, never written)
+    const uint32_t xh = (uint32_t)__cvta_generic_to_shared(smem + (size_t)min(g, np - 1) * xb);
+    const uint32_t xl = xh + (uint32_t)L.cols;
+    // C columns 2t, 2t + 1: the scales of those positions' slices
+    const float2 *reca = reinterpret_cast<const float2 *>(smem + (size_t)min(2 * t, np - 1) * xb + 2 * (size_t)L.cols);
+    const float2 *recb =
+        reinterpret_cast<const float2 *>(smem + (size_t)min(2 * t + 1, np - 1) * xb + 2 * (size_t)L.cols);
+    for (int c = k0; c < k1; ++c) {
+        const uint32_t bh0 = lds32(xh + (uint32_t)(c << 4) + 4u * t);
+        const uint32_t bh1 = lds32(xh + (uint32_t)((C + c) << 4) + 4u * t);
+        const uint32_t bl0 = lds32(xl + (uint32_t)(c << 4) + 4u * t);
+        const uint32_t bl1 = lds32(xl + (uint32_t)((C + c) << 4) + 4u * t);
+        const float2 sa = reca[c], sb = recb[c];
+        float ma = 0.f, mb = 0.f;  // Q5_0: 16 (s sum of slice c + s sum of slice C + c)
+        if constexpr (FMT == kQ5_0) {
+            ma = 16.f * (sa.y + reca[C + c].y);
+            mb = 16.f * (sb.y + recb[C + c].y);
+        }
+#pragma unroll
+        for (int ti = 0; ti < kMmaMaxTiles; ++ti) {
+            if (ti >= ntiles) break;  // uniform over the warp
+            const int ra = min(ti * 16 + g, nr - 1), rb = min(ti * 16 + g + 8, nr - 1);
+            uint32_t a[4];
+            float da, db;
+            mma_row_words<FMT>(rows_a + (uint32_t)ra * (uint32_t)L.row_stride, L, c, t, &a[0], &a[2], &da);
+            mma_row_words<FMT>(rows_a + (uint32_t)rb * (uint32_t)L.row_stride, L, c, t, &a[1], &a[3], &db);
+            int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0};
+            mma_blk<FMT>(dh, a, bh0, bh1);
+            mma_blk<FMT>(dl, a, bl0, bl1);
+            // D: (ra, 2t), (ra, 2t + 1), (rb, 2t), (rb, 2t + 1); the block's
+            // scales in the order of the CUDA-core dot (W<FMT>::dot_u)
+            if constexpr (FMT == kQ8_0) {
+                acc[ti][0] += (da * sa.x) * (float)(dh[0] * 256 + dl[0]);
+                acc[ti][1] += (da * sb.x) * (float)(dh[1] * 256 + dl[1]);
+                acc[ti][2] += (db * sa.x) * (float)(dh[2] * 256 + dl[2]);
+                acc[ti][3] += (db * sb.x) * (float)(dh[3] * 256 + dl[3]);
+            } else {
+                acc[ti][0] += da * (sa.x * (float)(dh[0] * 256 + dl[0]) - ma);
+                acc[ti][1] += da * (sb.x * (float)(dh[1] * 256 + dl[1]) - mb);
+                acc[ti][2] += db * (sa.x * (float)(dh[2] * 256 + dl[2]) - ma);
+                acc[ti][3] += db * (sb.x * (float)(dh[3] * 256 + dl[3]) - mb);
+            }
+        }
+    }
+#pragma unroll
+    for (int ti = 0; ti < kMmaMaxTiles; ++ti) {
+        if (ti >= ntiles) break;
+        part[warp][ti][g * 8 + 2 * t] = acc[ti][0];
+        part[warp][ti][g * 8 + 2 * t + 1] = acc[ti][1];
+        part[warp][ti][(g + 8) * 8 + 2 * t] = acc[ti][2];
+        part[warp][ti][(g + 8) * 8 + 2 * t + 1] = acc[ti][3];
+    }
+    __syncthreads();
+    // the warps' K ranges added in warp order
+    for (int e = tid; e < ntiles * 128; e += NT) {
+        const int ti = e >> 7, rr = (e >> 3) & 15, n = e & 7, row = ti * 16 + rr;
+        if (row < nr && n < np) {
+            float v = part[0][ti][rr * 8 + n];
+#pragma unroll
+            for (int q = 1; q < kMmaWarps; ++q) v += part[q][ti][rr * 8 + n];
+            Y[(size_t)n * L.rows + r0 + row] = v;
+        }
+    }
+}
+
 // ------------------------------------------------------------- matmul
 //
 // Batched form for up to NP positions per launch (the reference's chunk of
@@ -4549,6 +4721,54 @@ int tc_tile_width(int rows, int batch)
     return best;
 }
 
+// Batched form on the int8 tensor cores (Q8_0, Q5_0; chunks of up to 8
+// positions) where a CTA's rows (at most 64) and the positions' quantized x
+// fit in shared memory; false in *done when it does not apply.
+template <uint32_t FMT>
+cudaError_t matmul_mma_fmt(const Layout &L, const uint8_t *w, const float *X, int batch, float *Y, cudaStream_t s,
+                           bool *done)
+{
+    constexpr int NP = 8;
+    *done = false;
+    if constexpr (FMT != kQ8_0 && FMT != kQ5_0) {
+        return cudaSuccess;
+    } else {
+        const long long sms = sm_count();
+        const long long grid = L.rows < sms ? L.rows : sms;
+        const long long per_cta = (L.rows + grid - 1) / grid;
+        if (grid < 1 || per_cta > 16 * kMmaMaxTiles) return cudaSuccess;
+        const int np0 = batch < NP ? batch : NP;
+        const uint32_t xb = (uint32_t)((xs_bytes(L.cols) * (size_t)np0 + 127) & ~(size_t)127);
+        const uint64_t rows_bytes = (uint64_t)per_cta * L.row_stride;
+        if (xb > 64u * 1024u || rows_bytes > 96u * 1024u) return cudaSuccess;
+        const size_t smem = (size_t)xb + rows_bytes;
+        auto kernel = matmul_mma_kernel<FMT>;
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        e = allow_max_smem((const void *)kernel, dev);
+        if (e != cudaSuccess) return e;
+        *done = true;
+        for (int p0 = 0; p0 < batch; p0 += NP) {
+            const int np = batch - p0 < NP ? batch - p0 : NP;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)grid);
+            cfg.blockDim = dim3(kMmaWarps * 32);
+            cfg.dynamicSmemBytes = smem;
+            cfg.stream = s;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            e = cudaLaunchKernelEx(&cfg, kernel, L, w, X + (size_t)p0 * L.cols, np, Y + (size_t)p0 * L.rows, xb,
+                                   t_call_status);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaGetLastError();
+    }
+}
+
 // Batched CUDA-core form on the TMA pipeline: chunks of up to 8 positions.
 // false in *done when no stage plan fits (very long rows).
 template <uint32_t FMT>
@@ -4589,6 +4809,10 @@ cudaError_t matmul_fmt(const Layout &L, const uint8_t *w, const float *X, int ba
         }
     }
     bool done = false;
+    if (g_matmul_path == 0) {
+        const cudaError_t em = matmul_mma_fmt<FMT>(L, w, X, batch, Y, s, &done);
+        if (done || em != cudaSuccess) return em;
+    }
     const cudaError_t e = matmul_tma_fmt<FMT>(L, w, X, batch, Y, s, &done);
     if (done || e != cudaSuccess) return e;
     if (L.C <= 16) return matmul_go<FMT, 16>(L, w, X, batch, Y, s);

@@ -238,18 +238,21 @@ def test_matvec_nonfinite_and_tiny_x(cuda, qmv, oracle, workloads, gemv_path, gt
 # -------------------------------------------------------------- matmul
 
 @pytest.mark.parametrize("gtype,rows,cols", [(Q5_0, 4864, 896), (Q8_0, 300, 896), (Q4_K, 129, 3584),
-                                             (Q6_K, 129, 3584), (Q4_K, 40, 18944)])
+                                             (Q6_K, 129, 3584), (Q4_K, 40, 18944), (Q8_0, 9472, 896),
+                                             (Q5_0, 1000, 4864), (Q8_0, 7, 32)])
 @pytest.mark.parametrize("batch", [1, 3, 8, 13])
-@pytest.mark.parametrize("path", [0, 3], ids=["auto", "tma"])
+@pytest.mark.parametrize("path", [0, 1], ids=["auto", "cuda-cores"])
 def test_matmul_parity(cuda, qmv, oracle, workloads, gtype, rows, cols, batch, path):
-    """Batched CUDA-core projections (chunks of up to 8 positions on the TMA
-    pipeline), with the automatic GEMV choice and the exclusive TMA plan."""
+    """Batched projections below 32 positions: the automatic choice (int8
+    mma.sync tensor cores for Q8_0/Q5_0 where a CTA's rows and the x of a
+    chunk of 8 positions fit in shared memory, else the CUDA-core TMA kernel)
+    and the CUDA-core kernel forced."""
     torch = cuda
-    qmv.set_gemv_path(path)
+    qmv.set_matmul_path(path)
     try:
         _matmul_parity(torch, qmv, oracle, workloads, gtype, rows, cols, batch)
     finally:
-        qmv.set_gemv_path(0)
+        qmv.set_matmul_path(0)
 
 
 def _matmul_parity(torch, qmv, oracle, workloads, gtype, rows, cols, batch):
@@ -268,7 +271,7 @@ def _matmul_parity(torch, qmv, oracle, workloads, gtype, rows, cols, batch):
         assert bad.size == 0, (p, bad[:5])
 
 
-@pytest.mark.parametrize("path", [0, 3], ids=["auto", "tma"])
+@pytest.mark.parametrize("path", [0, 1], ids=["auto", "cuda-cores"])
 def test_matmul_nonfinite_x_small_batch(cuda, qmv, oracle, workloads, path):
     """An Inf in one position's x (CUDA-core batched form): the batch's rows
     are computed in fp32, so that position's rows follow the reference's float
@@ -278,7 +281,7 @@ def test_matmul_nonfinite_x_small_batch(cuda, qmv, oracle, workloads, path):
     blocks = workloads.make_blocks(gtype, rows, cols, seed=11)
     X = np.stack([workloads.make_activations(cols, seed=70 + p) for p in range(batch)])
     X[1, 5] = np.inf
-    qmv.set_gemv_path(path)
+    qmv.set_matmul_path(path)
     try:
         w = qmv.Weight(gtype, blocks, rows, cols)
         Xd = to_dev(torch, X)
@@ -288,7 +291,7 @@ def test_matmul_nonfinite_x_small_batch(cuda, qmv, oracle, workloads, path):
         Y = Yd.cpu().numpy()
         w.free()
     finally:
-        qmv.set_gemv_path(0)
+        qmv.set_matmul_path(0)
     Y_ref = oracle.matmul(gtype, blocks, rows, cols, X, batch)
     for p in (0, 2):
         s = oracle.row_abs_dot(gtype, blocks, rows, cols, X[p])
