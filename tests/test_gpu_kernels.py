@@ -81,6 +81,34 @@ def test_dequant_resident_bitexact(cuda, qmv, oracle, workloads, gtype, rows, co
     assert np.array_equal(f32_bits(out.cpu().numpy()), f32_bits(want))
 
 
+def test_dequant_every_f16_scale_encoding(cuda, qmv, oracle):
+    """All 65,536 fp16 encodings as Q8_0 scales (tests/q8_0_reference_test.cpp:48-64
+    pins every encoding of the reference's decode): one block per encoding,
+    quants covering sign, zero and both extremes, dequantized on the device
+    through the raw and the resident layouts, bit for bit against the oracle
+    (NaN payloads included)."""
+    torch = cuda
+    n = 65536
+    q = np.array([1, -1, 0, 127, -128, 2, -3, 64] * 4, dtype=np.int8)
+    blocks = np.zeros((n, 34), np.uint8)
+    blocks[:, 0] = np.arange(n, dtype=np.uint32) & 0xFF
+    blocks[:, 1] = (np.arange(n, dtype=np.uint32) >> 8) & 0xFF
+    blocks[:, 2:] = q.view(np.uint8)
+    want = oracle.dequant(Q8_0, blocks, n)
+    d = to_dev(torch, blocks)
+    out = torch.empty(n * 32, dtype=torch.float32, device="cuda")
+    qmv.dequantize_raw(Q8_0, d.data_ptr(), n, out.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(f32_bits(out.cpu().numpy()), f32_bits(want))
+    # the same blocks resident (chunk-major) as a 256-row x 8192-column matrix
+    w = qmv.Weight(Q8_0, blocks.reshape(256, -1), 256, 8192)
+    out2 = torch.empty(n * 32, dtype=torch.float32, device="cuda")
+    w.dequantize(out2.data_ptr())
+    torch.cuda.synchronize()
+    w.free()
+    assert np.array_equal(f32_bits(out2.cpu().numpy()), f32_bits(want))
+
+
 @pytest.mark.parametrize("gtype", [Q8_0, Q5_0, Q4_K, Q6_K])
 def test_dequant_raw_unaligned_and_special_scales(cuda, qmv, oracle, gtype):
     """Raw blocks at an odd device address; fp16 scales cover subnormals, both
