@@ -145,6 +145,8 @@ def test_dequant_reference_known_blocks(cuda, qmv, oracle):
     (Q4_K, 1, 256), (Q4_K, 17, 768), (Q4_K, 301, 3584), (Q4_K, 64, 18944),
     (Q6_K, 1, 256), (Q6_K, 17, 768), (Q6_K, 301, 3584), (Q6_K, 33, 18944),
     (Q8_0, 5, 65536), (Q8_0, 200, 16384), (Q5_0, 150, 16384 + 96),
+    # short rows, many rows per CTA: the 8-warp x 4-row plan
+    (Q8_0, 20000, 896), (Q5_0, 9600, 1024), (Q4_K, 10000, 2048), (Q6_K, 9600, 512),
 ])
 def test_matvec_shapes(cuda, qmv, oracle, workloads, gemv_path, gtype, rows, cols):
     blocks = workloads.make_blocks(gtype, rows, cols, seed=rows + cols)
@@ -541,6 +543,29 @@ def test_matvec_argmax_fused_and_sharded(cuda, qmv, oracle, workloads, gemv_path
         assert qmv.key_to_token(max(keys)) == want
         s = oracle.row_abs_dot(Q6_K, blocks, rows, cols, x)
         assert tolerance_ok(logits.cpu().numpy(), y_ref, s, REL_TOL)[0].size == 0
+
+
+def test_matvec_argmax_short_rows(cuda, qmv, oracle, workloads, gemv_path):
+    """Fused projection + argmax on the shape of a Qwen2 output projection
+    slice (Q8_0, 896 columns, 160 rows per SM: the 8-warp x 4-row plan)."""
+    torch = cuda
+    rows, cols = 23680, 896
+    blocks = workloads.make_blocks(Q8_0, rows, cols, seed=12)
+    x = workloads.make_activations(cols, seed=12)
+    y_ref = oracle.matvec(Q8_0, blocks, rows, cols, x, threads=8)
+    ok, want = oracle.argmax(y_ref)
+    assert ok
+    w = qmv.Weight(Q8_0, blocks, rows, cols)
+    xd = to_dev(torch, x)
+    ws = torch.zeros(qmv.argmax_workspace_bytes(), dtype=torch.uint8, device="cuda")
+    logits = torch.empty(rows, dtype=torch.float32, device="cuda")
+    key = torch.zeros(1, dtype=torch.int64, device="cuda")
+    w.matvec_argmax(xd.data_ptr(), logits.data_ptr(), key.data_ptr(), ws.data_ptr())
+    torch.cuda.synchronize()
+    w.free()
+    assert qmv.key_to_token(int(key.cpu().numpy().view(np.uint64)[0])) == want
+    s = oracle.row_abs_dot(Q8_0, blocks, rows, cols, x)
+    assert tolerance_ok(logits.cpu().numpy(), y_ref, s, REL_TOL)[0].size == 0
 
 
 def test_tma_path_covers_benchmark_shapes(cuda, qmv, workloads):
