@@ -3037,9 +3037,11 @@ attention_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *
 
 // ------------------------------------- decode attention on a CTA cluster
 //
-// One cluster of kDaSplit CTAs per KV head.  CTA r of the cluster owns the
-// positions [r*T/S, (r+1)*T/S) of the T = pos + 1 positions and every query
-// head of the group (G <= 8): it stages its cached keys and values in shared
+// One cluster of kDaSplit CTAs per KV head and part of its query-head group
+// (groups of 4 or more query heads are split in two parts, so each CTA scores
+// half the heads).  CTA r of the cluster owns the positions [r*T/S,
+// (r+1)*T/S) of the T = pos + 1 positions and the part's query heads (a
+// group of G <= 8): it stages its cached keys and values in shared
 // memory with 16-byte cp.async copies before griddepcontrol.wait (they do not
 // depend on this layer's projections, so the copies overlap the Q/K/V GEMV),
 // then rotates the group's queries, computes its scores, softmax and weighted
@@ -3095,13 +3097,13 @@ __device__ __forceinline__ void da_stage(float *ks, float *vs, const float *kc, 
 __global__ void __launch_bounds__(kDaThreads, 1)
 attention_cluster_kernel(const float *__restrict__ qkv, int heads, int kv_heads, float *__restrict__ kc,
                          float *__restrict__ vc, int max_ctx, float rope_base, DecodeState *st,
-                         float *__restrict__ att)
+                         float *__restrict__ att, int hsplit)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     float *ks = reinterpret_cast<float *>(smem);                          // [kDaTile][kDaKStride]
     float *vs = reinterpret_cast<float *>(smem + kDaKBytes);              // [kDaTile][64]
-    float *qs = reinterpret_cast<float *>(smem + kDaKBytes + kDaVBytes);  // [G][64]
-    float *ps = qs + kDaMaxGroup * 64;                                    // [G][kDaTile]
+    float *qs = reinterpret_cast<float *>(smem + kDaKBytes + kDaVBytes);  // [Gs][64]
+    float *ps = qs + kDaMaxGroup * 64;                                    // [Gs][kDaTile]
     float *knew = ps + kDaMaxGroup * kDaTile;                             // rotated key of pos [64], value [64]
     float *part = knew + 128;                                             // leader: [S][kDaMaxGroup][kDaPart]
     __shared__ float cs[32], sn[32], mh[kDaMaxGroup], lh[kDaMaxGroup];
@@ -3110,8 +3112,10 @@ attention_cluster_kernel(const float *__restrict__ qkv, int heads, int kv_heads,
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint32_t rank;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
-    const int g = (int)(blockIdx.x / kDaSplit);
+    // cluster (KV head g, head part hs): query heads [h0, h0 + Gs) of the group
+    const int cid = (int)(blockIdx.x / kDaSplit), g = cid / hsplit, hs = cid % hsplit;
     const int G = heads / kv_heads, dim = heads * 64, kvd = kv_heads * 64;
+    const int h0 = hs * G / hsplit, Gs = (hs + 1) * G / hsplit - h0;
     const uint32_t bar_a = (uint32_t)__cvta_generic_to_shared(&bar);
     // The output projection may start copying its weights; it reads att only
     // after its own griddepcontrol.wait.
@@ -3124,7 +3128,7 @@ attention_cluster_kernel(const float *__restrict__ qkv, int heads, int kv_heads,
     if (rank == 0 && tid == 0) {
         // the leader's mbarrier expects the other CTAs' partials
         mbar_init(bar_a, 1u);
-        mbar_expect_tx(bar_a, (uint32_t)((kDaSplit - 1) * G * (64 + 2) * 4));
+        mbar_expect_tx(bar_a, (uint32_t)((kDaSplit - 1) * Gs * (64 + 2) * 4));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
@@ -3144,9 +3148,9 @@ attention_cluster_kernel(const float *__restrict__ qkv, int heads, int kv_heads,
     // q, k and v of this position come from the Q/K/V GEMV
     asm volatile("griddepcontrol.wait;" ::: "memory");
     __syncthreads();
-    for (int e = tid; e < G * 64; e += kDaThreads) {
+    for (int e = tid; e < Gs * 64; e += kDaThreads) {
         const int hh = e >> 6, d = e & 63, i = d & 31;
-        const float *q = qkv + (g * G + hh) * 64;
+        const float *q = qkv + (g * G + h0 + hh) * 64;
         const float x = __ldcg(q + i), y = __ldcg(q + i + 32);
         qs[hh * 64 + d] = d < 32 ? x * cs[i] - y * sn[i] : x * sn[i] + y * cs[i];
     }
@@ -3158,8 +3162,10 @@ attention_cluster_kernel(const float *__restrict__ qkv, int heads, int kv_heads,
         const float kr = d < 32 ? x * cs[i] - y * sn[i] : x * sn[i] + y * cs[i];
         const float vv = __ldcg(qkv + dim + kvd + g * 64 + d);
         const size_t slot = (size_t)pos * kvd + g * 64 + d;
-        kc[slot] = kr;
-        vc[slot] = vv;
+        if (hs == 0) {  // one cluster of the KV head appends to the cache
+            kc[slot] = kr;
+            vc[slot] = vv;
+        }
         knew[d] = kr;
         knew[64 + d] = vv;
     }
@@ -3195,7 +3201,7 @@ attention_cluster_kernel(const float *__restrict__ qkv, int heads, int kv_heads,
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const int hh = hg + NG * j;
-                        if (hh < G) {
+                        if (hh < Gs) {
                             const float4 q4 = reinterpret_cast<const float4 *>(qs + hh * 64)[d4];
                             acc[j] += q4.x * k4.x;
                             acc[j] += q4.y * k4.y;
@@ -3206,12 +3212,12 @@ attention_cluster_kernel(const float *__restrict__ qkv, int heads, int kv_heads,
                 }
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
-                    if (hg + NG * j < G) ps[(hg + NG * j) * kDaTile + t] = acc[j] / rs;
+                    if (hg + NG * j < Gs) ps[(hg + NG * j) * kDaTile + t] = acc[j] / rs;
             }
         }
         __syncthreads();
         // softmax update of head `warp`: running maximum and sum, tile weights
-        if (warp < G) {
+        if (warp < Gs) {
             float *pr = ps + warp * kDaTile;
             float mt = -INFINITY;
             for (int t = lane; t < tn; t += 32) mt = fmaxf(mt, pr[t]);
@@ -3253,7 +3259,7 @@ attention_cluster_kernel(const float *__restrict__ qkv, int heads, int kv_heads,
     __syncthreads();  // mh / lh final
     // the leader's mbarrier is initialised (cluster barrier arrived at above)
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
-    if (warp < G) {
+    if (warp < Gs) {
         float *mine = part + (rank * kDaMaxGroup + warp) * kDaPart;
         if (rank == 0) {
             if (lane < 16) *reinterpret_cast<float4 *>(mine + 4 + 4 * dq) = make_float4(o[0], o[1], o[2], o[3]);
@@ -3284,7 +3290,7 @@ attention_cluster_kernel(const float *__restrict__ qkv, int heads, int kv_heads,
         if (tid == 0) atomicOr(&st->error, 16u);
         return;
     }
-    if (tid < G) {
+    if (tid < Gs) {
         float M = -INFINITY;
         for (int r = 0; r < kDaSplit; ++r) M = fmaxf(M, part[(r * kDaMaxGroup + tid) * kDaPart]);
         float den = 0.f;
@@ -3296,12 +3302,12 @@ attention_cluster_kernel(const float *__restrict__ qkv, int heads, int kv_heads,
         lh[tid] = den;
     }
     __syncthreads();
-    for (int e = tid; e < G * 64; e += kDaThreads) {
+    for (int e = tid; e < Gs * 64; e += kDaThreads) {
         const int hh = e >> 6, d = e & 63;
         float num = 0.f;
 #pragma unroll 4
         for (int r = 0; r < kDaSplit; ++r) num += wr[r][hh] * part[(r * kDaMaxGroup + hh) * kDaPart + 4 + d];
-        att[(g * G + hh) * 64 + d] = num / lh[hh];
+        att[(g * G + h0 + hh) * 64 + d] = num / lh[hh];
     }
 }
 
@@ -5083,7 +5089,9 @@ cudaError_t launch_attention(const float *qkv, int heads, int kv_heads, int head
         return cudaErrorInvalidValue;
     if (g_attn_path == 0 && heads / kv_heads <= kDaMaxGroup && attention_cluster_ok()) {
         cudaLaunchConfig_t cfg{};
-        cfg.gridDim = dim3((unsigned)(kv_heads * kDaSplit));
+        // two clusters per KV head (each half of the query heads) from 4 heads per group
+        const int hsplit = heads / kv_heads >= 4 ? 2 : 1;
+        cfg.gridDim = dim3((unsigned)(kv_heads * hsplit * kDaSplit));
         cfg.blockDim = dim3(kDaThreads);
         cfg.dynamicSmemBytes = kDaSmem;
         cfg.stream = s;
@@ -5097,7 +5105,7 @@ cudaError_t launch_attention(const float *qkv, int heads, int kv_heads, int head
         cfg.attrs = attr;
         cfg.numAttrs = 2;
         return cudaLaunchKernelEx(&cfg, attention_cluster_kernel, qkv, heads, kv_heads, kc, vc, max_ctx, rope_base, st,
-                                  att);
+                                  att, hsplit);
     }
     const dim3 grid((unsigned)kv_heads, (unsigned)((max_ctx + kAttnChunk - 1) / kAttnChunk));
     cudaLaunchConfig_t cfg{};
