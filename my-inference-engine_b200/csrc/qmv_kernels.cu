@@ -139,31 +139,28 @@ __device__ unsigned long long block_max_key(unsigned long long k, unsigned long 
     return k;
 }
 
-// Publish this CTA's key; the last CTA to arrive folds all of them into
-// *am.key and re-arms the counter.  No CTA waits on another.
+// Fold this CTA's key (valid in thread 0) into the workspace's running
+// maximum (an atomic max, then an arrival counted with release semantics);
+// the last CTA to arrive (acquire) copies the maximum to *am.key and re-arms
+// the slot and the counter.  No CTA waits on another, and no CTA but the last
+// reads anything back beyond its own arrival.  Workspace: u32 counter at 0,
+// u64 running maximum at 8 (both zero between launches).
 __device__ void finish_argmax(unsigned long long cta_key, const ArgmaxOut &am, unsigned long long *scratch)
 {
+    (void)scratch;
+    if (threadIdx.x != 0) return;
     unsigned int *counter = reinterpret_cast<unsigned int *>(am.workspace);
-    unsigned long long *keys =
-        reinterpret_cast<unsigned long long *>(reinterpret_cast<uint8_t *>(am.workspace) + 16);
-    __shared__ int is_last;
-    if (threadIdx.x == 0) {
-        keys[blockIdx.x] = cta_key;
-        __threadfence();
-        unsigned int prev = atomicAdd(counter, 1u);
-        is_last = (prev == gridDim.x - 1u);
-    }
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    unsigned long long k = 0ull;
-    for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x)
-        k = max_ull(k, __ldcg(keys + i));
-    k = block_max_key(k, scratch);
-    if (threadIdx.x == 0) {
-        *am.key = k;
-        *counter = 0u;
-    }
+    unsigned long long *slot =
+        reinterpret_cast<unsigned long long *>(reinterpret_cast<uint8_t *>(am.workspace) + 8);
+    atomicMax(slot, cta_key);
+    unsigned int prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(counter) : "memory");
+    if (prev != gridDim.x - 1u) return;
+    unsigned long long k;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(k) : "l"(slot) : "memory");
+    *am.key = k;
+    *slot = 0ull;
+    *counter = 0u;
 }
 
 // ------------------------------------------------------ peer exchange
@@ -5438,10 +5435,11 @@ cudaError_t launch_decode_layers(const PStep &P, cudaStream_t s)
 //
 // For callers that cannot call cudaMalloc (a host that owns every device
 // allocation through its own pool and hands a plugin only input and output
-// buffers): the argmax scratch -- the arrival counter and one key slot per CTA
-// -- lives in this file-scope device array instead of a caller workspace.
-// One CTA covers kNoAllocLogitsPerCta logits, so the array bounds a call at
-// kNoAllocMaxLogits logits.  Every GPU that loads the library holds the array
+// buffers): the argmax scratch -- the arrival counter and the running maximum
+// key in its first 16 bytes, then room for one key per CTA (the layout of the
+// caller workspace of qmv_argmax) -- lives in this file-scope device array
+// instead of a caller workspace.  One CTA covers kNoAllocLogitsPerCta logits,
+// and a call is bounded at kNoAllocMaxCtas CTAs (kNoAllocMaxLogits logits).  Every GPU that loads the library holds the array
 // until the process exits.  All calls on a device share it and it keeps the
 // last call's contents: each call clears the counter first, and calls that
 // overlap on the GPU (concurrent streams) race on it.
@@ -5488,7 +5486,7 @@ cudaError_t launch_argmax_noalloc(const float *logits, int n, int index_base, un
     void *scratch = nullptr;
     cudaError_t e = noalloc_scratch(&scratch);
     if (e != cudaSuccess) return e;
-    e = cudaMemsetAsync(scratch, 0, 16, s);  // arrival counter starts at zero
+    e = cudaMemsetAsync(scratch, 0, 16, s);  // arrival counter and running maximum start at zero
     if (e != cudaSuccess) return e;
     const unsigned g = (unsigned)((n + kNoAllocLogitsPerCta - 1) / kNoAllocLogitsPerCta);
     argmax_kernel<<<g, kThreads, 0, s>>>(logits, n, ArgmaxOut{key, scratch, index_base});
