@@ -338,30 +338,41 @@ __device__ void quantize_x(const float *__restrict__ x, int cols, int C, uint8_t
     const int total = np * n4;
     constexpr int U = 8;
     for (int it0 = 0; it0 * NT < total; it0 += U) {
-        float4 v[U];
+        // every load of the batch is issued at once (predicated past the
+        // end); the prologue arithmetic then runs only for the valid part
+        float4 v[U], w4[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            int g = (it0 + u) * NT + threadIdx.x;
+            const int g = (it0 + u) * NT + threadIdx.x;
             v[u] = g >= total ? make_float4(0.f, 0.f, 0.f, 0.f)
                    : LIVE     ? __ldcg(reinterpret_cast<const float4 *>(x) + g)
                               : __ldg(reinterpret_cast<const float4 *>(x) + g);
-            if (pre != kPreNone && g < total) {
-                const float4 a = LIVE ? __ldcg(reinterpret_cast<const float4 *>(aux) + g)
-                                      : __ldg(reinterpret_cast<const float4 *>(aux) + g);
+            if (pre != kPreNone)
+                w4[u] = g >= total ? make_float4(0.f, 0.f, 0.f, 0.f)
+                        : LIVE     ? __ldcg(reinterpret_cast<const float4 *>(aux) + g)
+                                   : __ldg(reinterpret_cast<const float4 *>(aux) + g);
+        }
+        if (pre != kPreNone) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                if ((it0 + u) * NT >= total) break;  // uniform across the CTA
+                const int g = (it0 + u) * NT + threadIdx.x;
+                if (g >= total) continue;
+                const float4 b = w4[u];
                 if (pre == kPreRmsNorm) {
-                    v[u] = make_float4((v[u].x / denom) * a.x, (v[u].y / denom) * a.y, (v[u].z / denom) * a.z,
-                                       (v[u].w / denom) * a.w);
+                    v[u] = make_float4((v[u].x / denom) * b.x, (v[u].y / denom) * b.y, (v[u].z / denom) * b.z,
+                                       (v[u].w / denom) * b.w);
                 } else if (pre == kPreScale) {
                     *ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
-                    v[u] = make_float4(v[u].x * a.x, v[u].y * a.y, v[u].z * a.z, v[u].w * a.w);
+                    v[u] = make_float4(v[u].x * b.x, v[u].y * b.y, v[u].z * b.z, v[u].w * b.w);
                 } else {
                     // SwiGLU: the x that is quantized next (to 2^-15 of its
                     // block maximum), so the fast exponential's few-ulp error
                     // is far below what the quantization keeps
-                    v[u] = make_float4(a.x * (v[u].x / (1.f + __expf(-v[u].x))),
-                                       a.y * (v[u].y / (1.f + __expf(-v[u].y))),
-                                       a.z * (v[u].z / (1.f + __expf(-v[u].z))),
-                                       a.w * (v[u].w / (1.f + __expf(-v[u].w))));
+                    v[u] = make_float4(b.x * (v[u].x / (1.f + __expf(-v[u].x))),
+                                       b.y * (v[u].y / (1.f + __expf(-v[u].y))),
+                                       b.z * (v[u].z / (1.f + __expf(-v[u].z))),
+                                       b.w * (v[u].w / (1.f + __expf(-v[u].w))));
                 }
             }
         }
