@@ -783,7 +783,7 @@ def bench_qwen2_decode(qmv, steps=256, prefill=1024, cpu_seconds=5.0, cpu=True, 
     try:
         stream = torch.cuda.Stream()
         dec.set_kv(keys, vals)
-        dec.generate(7, 8)  # warm-up
+        dec.generate(7, min(8, steps))  # warm-up (within the steps the context holds)
         dec.set_kv(keys, vals)
         dec.begin(7)
         a = torch.cuda.Event(enable_timing=True)
