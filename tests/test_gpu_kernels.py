@@ -63,6 +63,9 @@ def check_matvec(torch, qmv, oracle, gtype, blocks, rows, cols, x, rows_to_check
         bad, err, bound = tolerance_ok(y[sel], y_ref, s, REL_TOL)
     assert bad.size == 0, f"{bad.size} rows out of tolerance, worst ratio {np.max(err / np.maximum(bound, 1e-30))}"
     w.free()
+    # no bounded wait ran out (a timeout falls back to correct fp32 rows, so
+    # the values alone would not show it)
+    assert qmv.device_status(clear=True) == 0
     return y
 
 
